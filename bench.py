@@ -1,0 +1,298 @@
+#!/usr/bin/env python
+"""Benchmark of the per-frame dual-AR decode path (frames/s).
+
+Workload (one "step"): one utterance through the full dual-AR frame loop on
+the S2 Pro shape with Q8_0 weights at batch 1: a 64-token seeded text prompt
+is prefilled, then 200 frames are decoded greedily (each frame = 9 Fast-AR
+passes + samples + one Slow-AR step + sample).  Weights are seeded synthetic
+N(0, 0.02) quantized to Q8_0 (no checkpoints offline).  min_tokens_before_end
+is set to the frame count so every step yields exactly 200 frames.
+
+Multi-GPU: one process per GPU (torchrun); each rank decodes its own
+utterance with no collective on the data path (request-level sharding,
+"weak" scaling).  Timing: CUDA events on the library's stream, barrier +
+synchronize on both sides, max over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "s2.cpp_b200"))
+
+import synthetic  # noqa: E402
+
+PROMPT = 64
+FRAMES = 200
+SEED = 1234
+METRIC = "codec frames/s (dual-AR frame loop, Q8_0, bs=1 per GPU)"
+WORKLOAD = ("dual-AR frame loop, S2 Pro shape (36+4 layers, d2560, GQA 32/8, ff 9728, vocab 155648), "
+            "Q8_0, bs=1: 64-token text prompt prefill + 200 greedy frames")
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+def frame_bytes(hp, ctx0: int, frames: int) -> float:
+    """Algorithmic bytes of one step: weights streamed per frame (Slow step +
+    9 Fast-AR passes) + f16 KV read by the Slow step, + the prefill's weights."""
+    q8 = 34 / 32
+    d, ff = hp.embedding_length, hp.feed_forward_length
+    qkv = (hp.head_count + 2 * hp.head_count_kv) * hp.head_dim
+    layer = d * qkv + hp.head_count * hp.head_dim * d + 3 * d * ff
+    slow = (hp.block_count * layer + hp.vocab_size * d) * q8
+    fast = (hp.fast_block_count * layer + hp.codebook_size * d) * q8
+    kv_per_pos = hp.block_count * 2 * hp.head_count_kv * hp.head_dim * 2
+    total = 0.0
+    for f in range(frames):
+        total += slow + (hp.num_codebooks - 1) * fast + kv_per_pos * (ctx0 + f + 1)
+    return total
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, dev: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(dev), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 7:
+                rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def build_weights(hp, threads: int):
+    synthetic._lib().s2synth_set_threads(threads)
+    return list(synthetic.make_model(hp, seed=SEED, norm_std=0.0))
+
+
+def cpu_sample(hp, tensors, frames_sample: int) -> dict:
+    """The CPU oracle (C restatement of the reference path) on a bounded sample:
+    the 64-token prefill + `frames_sample` frames, scaled to the 200-frame step."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # noqa: E402  (cpu_baseline leg only)
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    om = oracle.OracleModel(hp)
+    om.load_tensors(tensors)
+    prompt = synthetic.text_prompt(hp, PROMPT, seed=7)
+    _, pre_ms, loop_ms = om.generate_timed(prompt, frames_sample, temperature=0.0, seed=SEED,
+                                           min_tokens_before_end=frames_sample)
+    om.close()
+    per_frame = loop_ms / frames_sample
+    step_s = (pre_ms + FRAMES * per_frame) / 1e3
+    return {"value": FRAMES / step_s, "unit": "frames/s", "cores": cores, "kind": "port",
+            "sample": f"oracle generate: {PROMPT}-token prefill ({pre_ms / 1e3:.1f} s) + {frames_sample} frames "
+                      f"({per_frame / 1e3:.2f} s/frame), scaled to {FRAMES} frames",
+            "prefill_s": pre_ms / 1e3, "s_per_frame": per_frame / 1e3}
+
+
+def run_reference(args, rank: int) -> None:
+    """--impl reference: the reference's CPU path on the host cores.  ggml is an
+    un-vendored submodule of s2.cpp (absent), so the reference cannot be built;
+    its restatement in oracle/ is timed instead."""
+    if rank != 0:
+        return
+    hp = synthetic.preset("s2pro")
+    tensors = build_weights(hp, os.cpu_count() or 1)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_sample(hp, tensors, args.cpu_frames)
+        if i >= args.warmup:
+            vals.append(r)
+    v = float(np.mean([r["value"] for r in vals]))
+    ms = 1e3 * FRAMES / v
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "frames/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q8_0", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "prompt_tokens": PROMPT, "frames": FRAMES},
+        "cpu_baseline": {k: vals[-1][k] for k in ("unit", "cores", "kind", "sample")} | {"value": v},
+        "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "ggml (s2.cpp's compute backend) is an absent submodule; the C restatement in oracle/ is timed",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--frames", type=int, default=FRAMES)
+    ap.add_argument("--cpu-frames", type=int, default=2, help="frames in the CPU oracle sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    import s2k  # noqa: E402
+
+    dist_on = world > 1
+    if dist_on:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    hp = synthetic.preset("s2pro")
+    threads = max(1, (os.cpu_count() or 8) // max(world, 1))
+    t0 = time.time()
+    tensors = build_weights(hp, threads)
+    t_synth = time.time() - t0
+    m = s2k.SlowARModel(hp, device=local)
+    m.load_tensors(tensors)
+    if not (rank == 0 and world == 1 and not args.no_cpu_baseline):
+        del tensors
+        tensors = None
+    frames = args.frames
+    prompt = synthetic.text_prompt(hp, PROMPT, seed=7 + rank)  # this rank's utterance
+    m.init_kv_cache(PROMPT + frames)
+    d_prompt = torch.from_numpy(np.ascontiguousarray(prompt.T)).to(f"cuda:{local}")
+    d_codes = torch.zeros((hp.num_codebooks, frames), dtype=torch.int32, device=f"cuda:{local}")
+    stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
+    kw = dict(temperature=0.0, top_p=0.8, top_k=30, min_tokens_before_end=frames, im_end_id=-1, seed=SEED,
+              seq_id=rank)
+
+    def step():
+        n = m.generate_device(d_prompt.data_ptr(), PROMPT, d_codes.data_ptr(), frames, **kw)
+        assert n == frames, n
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist_on:
+        dist.barrier()
+    clocks = Clocks(local)
+    torch.cuda.synchronize()
+    s2k.launch_count(reset=True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = s2k.launch_count()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist_on:
+        dist.barrier()
+        t = torch.tensor([ms], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * args.steps * frames / (ms / 1e3)
+
+    # end to end through the host API: host prompt in, host codes out
+    e2e_times = []
+    for _ in range(args.steps):
+        torch.cuda.synchronize()
+        a = time.perf_counter()
+        out = m.generate(prompt, frames, **kw)
+        e2e_times.append(time.perf_counter() - a)
+        assert out.shape == (hp.num_codebooks, frames)
+    e2e_s = float(np.sum(e2e_times))
+    if dist_on:
+        t = torch.tensor([e2e_s], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * args.steps * frames / e2e_s
+
+    # dominant kernel: the Slow-step GEMV chain (every weight GEMV of a step), events on its stream
+    gb, gms, glaunch = m.profile_gemv(reps=5)
+    pk = peaks()
+    achieved = gb / (gms / 1e3) / 1e9
+    fb = frame_bytes(hp, PROMPT, frames)
+    step_bytes = fb  # + prefill weights, counted separately below
+    frame_achieved = step_bytes / (ms_per_step / 1e3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and tensors is not None:
+        try:
+            cpu = cpu_sample(hp, tensors, args.cpu_frames)
+        except Exception as e:  # reported, never fatal
+            cpu = {"value": None, "error": str(e)}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q8_0", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "prompt_tokens": PROMPT, "frames": frames, "batch_per_gpu": 1,
+                       "weights": "seeded N(0,0.02) -> Q8_0", "l2": "inputs larger than L2 (4.3 GB of weights per frame)",
+                       "parallelism": f"request-level x{world}, no collectives"},
+            "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": int(prompt.nbytes),
+                    "d2h_bytes_per_step": int(hp.num_codebooks * frames * 4)},
+            "roofline": {"bound": "hbm", "kernel": "gemv_q8_0 (Slow-step weight GEMV chain)",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                         "peak_src": pk["src"], "traffic": None, "bytes_per_launch": gb / glaunch,
+                         "launches": glaunch, "ms_per_pass": gms},
+            "frame_roofline": {"achieved": frame_achieved, "frac": frame_achieved / pk["hbm_gbs"], "unit": "GB/s",
+                               "bytes_per_step": step_bytes},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "gpu_launches": int(launches),
+            "setup_s": {"synth": t_synth},
+        }
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist_on:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,203 @@
+/*
+ * s2k.h -- C ABI of the B200-native dual-AR decode path for s2.cpp.
+ *
+ * This is the thin layer that replaces the ggml graph inside
+ * s2::SlowARModel (src/s2_model.cpp) and the per-frame work of s2::generate
+ * (src/s2_generate.cpp).  Plain C types only: pointers, sizes, status codes.
+ * Every entry point below names the reference interface it stands in for.
+ *
+ * Threading: one host thread per model handle at a time, like the reference
+ * (SlowARModel keeps n_past_ and its graph buffers as members,
+ * include/s2_model.h:147-151; Pipeline serialises synthesis with
+ * synthesize_mutex_, include/s2_pipeline.h:111).
+ *
+ * Errors: every call returns s2k_status (0 = OK, negative = error) and sets a
+ * thread-local message readable with s2k_last_error().  No exception crosses
+ * this boundary (the reference's model layer also reports bool + stderr,
+ * src/s2_model.cpp:863-875, 1064-1086).
+ */
+#ifndef S2K_H
+#define S2K_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define S2K_API __declspec(dllexport)
+#else
+#define S2K_API __attribute__((visibility("default")))
+#endif
+
+#define S2K_ABI_VERSION 1
+
+typedef int32_t s2k_status;
+enum {
+    S2K_OK = 0,
+    S2K_ERR_ARG = -1,         /* bad argument / shape / name */
+    S2K_ERR_OOM = -2,         /* device or pinned allocation failed */
+    S2K_ERR_CUDA = -3,        /* CUDA runtime error */
+    S2K_ERR_KV_FULL = -4,     /* n_past + n_tokens > max_seq_len (src/s2_model.cpp:870-875) */
+    S2K_ERR_STATE = -5,       /* missing tensors, model not finalized, ... */
+    S2K_ERR_TIMEOUT = -6,     /* a bounded device-side wait gave up */
+    S2K_ERR_UNSUPPORTED = -7, /* quant type / shape not supported */
+    S2K_ERR_NO_DEVICE = -8    /* no CUDA device visible */
+};
+
+/* ggml type ids accepted by s2k_model_upload_tensor */
+enum {
+    S2K_TYPE_F32 = 0,
+    S2K_TYPE_F16 = 1,
+    S2K_TYPE_Q8_0 = 8,
+    S2K_TYPE_Q4_K = 12,
+    S2K_TYPE_Q6_K = 14
+};
+
+/* Mirrors s2::ModelHParams (include/s2_model.h:38-69) plus head_dim, which the
+ * reference derives from q_norm / wo (src/s2_model.cpp:879-884). */
+typedef struct s2k_hparams {
+    int32_t context_length;
+    int32_t vocab_size;
+    int32_t embedding_length;
+    int32_t feed_forward_length;
+    int32_t block_count;
+    int32_t head_count;
+    int32_t head_count_kv;
+    int32_t head_dim;
+    int32_t codebook_size;
+    int32_t num_codebooks;
+    int32_t semantic_begin_id;
+    int32_t semantic_end_id;
+    float rope_freq_base;
+    float rms_norm_eps;
+    int32_t tie_word_embeddings;
+    int32_t attention_qk_norm;
+    int32_t scale_codebook_embeddings;
+    int32_t fast_context_length;
+    int32_t fast_embedding_length;
+    int32_t fast_feed_forward_length;
+    int32_t fast_block_count;
+    int32_t fast_head_count;
+    int32_t fast_head_count_kv;
+    int32_t fast_head_dim;
+    float fast_rope_freq_base;
+    float fast_rms_norm_eps;
+    int32_t fast_attention_qk_norm;
+    int32_t fast_has_project_in;
+    int32_t has_fast_decoder;
+} s2k_hparams;
+
+/* Mirrors s2::GenerateParams (include/s2_generate.h:23-32) and the
+ * TokenizerConfig::im_end_id generate() reads (src/s2_generate.cpp:26).
+ * seed / seq_id key the counter-based sampler RNG that replaces the
+ * reference's std::random_device-seeded mt19937 (src/s2_sampler.cpp:94). */
+typedef struct s2k_gen_params {
+    int32_t max_new_tokens;
+    float temperature;
+    float top_p;
+    int32_t top_k;
+    int32_t min_tokens_before_end;
+    int32_t im_end_id;
+    uint64_t seed;
+    uint32_t seq_id;
+} s2k_gen_params;
+
+/* Mirrors s2::FrameCallbackData + FrameCallback (include/s2_generate.h:14-21):
+ * return non-zero to continue, 0 to abort generation. */
+typedef int32_t (*s2k_frame_callback)(const int32_t *codes, int32_t frame_index,
+                                      int32_t total_frames, int32_t num_codebooks, void *user);
+
+typedef struct s2k_model s2k_model;
+typedef struct s2k_seq s2k_seq;
+
+S2K_API int32_t s2k_abi_version(void);
+S2K_API const char *s2k_last_error(void);
+S2K_API s2k_status s2k_device_count(int32_t *count);
+
+/* Replaces SlowARModel::load_shared's ggml context, backends and schedulers
+ * (src/s2_model.cpp:204-608): creates the model on CUDA device `device`. */
+S2K_API s2k_status s2k_model_create(int32_t device, const s2k_hparams *hp, s2k_model **out);
+
+/* Replaces the ggml_backend_tensor_set of one model tensor in
+ * read_all_tensor_data (src/s2_pipeline.cpp:326-343).  `host` holds the GGUF
+ * tensor bytes exactly as stored on disk (ggml ne order [in, out]); the
+ * blocks are re-laid out on the device for coalesced 128-bit loads.  Names
+ * are the GGUF names SlowARModel binds (src/s2_model.cpp:374-423). */
+S2K_API s2k_status s2k_model_upload_tensor(s2k_model *m, const char *name, int32_t ggml_type,
+                                           const int64_t ne[4], const void *host, size_t nbytes);
+
+/* Checks every required tensor is bound (the req_t checks of
+ * src/s2_model.cpp:366-428) and prepares the decode kernels. */
+S2K_API s2k_status s2k_model_finalize(s2k_model *m);
+S2K_API void s2k_model_free(s2k_model *m);
+/* SlowARModel::hparams (include/s2_model.h:130) */
+S2K_API s2k_status s2k_model_get_hparams(const s2k_model *m, s2k_hparams *out);
+/* Device bytes of the re-laid-out weights. */
+S2K_API size_t s2k_model_weight_bytes(const s2k_model *m);
+/* The cudaStream_t all of this model's work runs on (for event timing). */
+S2K_API void *s2k_model_stream(s2k_model *m);
+
+/* SlowARModel::init_kv_cache (src/s2_model.cpp:717-765): a sequence owning a
+ * paged f16 KV cache (16-token pages) for up to max_seq_len positions. */
+S2K_API s2k_status s2k_seq_create(s2k_model *m, int32_t max_seq_len, s2k_seq **out);
+/* SlowARModel::reset (src/s2_model.cpp:767-769): n_past = 0. */
+S2K_API s2k_status s2k_seq_reset(s2k_seq *s);
+/* SlowARModel::clear_kv_cache (src/s2_model.cpp:771-787). */
+S2K_API void s2k_seq_free(s2k_seq *s);
+S2K_API int32_t s2k_seq_n_past(const s2k_seq *s);
+
+/* SlowARModel::eval_cached, reached through prefill_fast / step
+ * (src/s2_model.cpp:788-791, 855-1097).  flat_tokens is [n_tokens][num_codebooks+1]
+ * token-major.  hidden_out [embedding_length] and logits_out [vocab_size] are
+ * host buffers (either may be NULL). */
+S2K_API s2k_status s2k_eval(s2k_model *m, s2k_seq *s, const int32_t *flat_tokens,
+                            int32_t n_tokens, float *hidden_out, float *logits_out);
+
+/* SlowARModel::fast_decode (src/s2_model.cpp:1099-1255): hidden [embedding_length],
+ * prefix [n_prefix] codebook values, n_prefix < num_codebooks; logits_out
+ * [codebook_size]. */
+S2K_API s2k_status s2k_fast_decode(s2k_model *m, const float *hidden, const int32_t *prefix,
+                                   int32_t n_prefix, float *logits_out);
+
+/* s2::generate (src/s2_generate.cpp:11-216) with the frame loop on the device:
+ * prompt is the PromptTensor grid [num_codebooks+1][cols] row-major
+ * (include/s2_prompt.h:11-15); codes_out receives [num_codebooks][n_frames]
+ * cb-major, compacted like src/s2_generate.cpp:201-213 (capacity
+ * num_codebooks * max_new_tokens).  The sequence is reset first (the
+ * clear/init_kv_cache the Pipeline does, src/s2_pipeline.cpp:838-851) and
+ * must hold cols + max_new_tokens positions.  on_frame may be NULL. */
+S2K_API s2k_status s2k_generate(s2k_model *m, s2k_seq *s, const int32_t *prompt, int32_t cols,
+                                const s2k_gen_params *gp, int32_t *codes_out,
+                                int32_t *n_frames_out, s2k_frame_callback on_frame, void *user);
+
+/* Same as s2k_generate with device-resident buffers: d_prompt_tm is the
+ * token-major [cols][num_codebooks+1] prompt and d_codes_out the
+ * [num_codebooks][max_new_tokens] (uncompacted) codes, both device pointers. */
+S2K_API s2k_status s2k_generate_device(s2k_model *m, s2k_seq *s, const int32_t *d_prompt_tm,
+                                       int32_t cols, const s2k_gen_params *gp,
+                                       int32_t *d_codes_out, int32_t *n_frames_out);
+
+/* Sampler on the device for one logits row already in device memory
+ * (s2::sample_token, src/s2_sampler.cpp:42-99; tie break = lowest index).
+ * u is the uniform draw used when temperature > 0.  Host logits in, token out. */
+S2K_API s2k_status s2k_sample(s2k_model *m, const float *logits, int32_t n, float temperature,
+                              float top_p, int32_t top_k, double u, int32_t *token_out);
+
+/* Profiling hook for the dominant kernel (no reference counterpart): launches
+ * every Slow-step weight GEMV (per layer wqkv, wo, w1|w3, w2, then the LM head)
+ * `reps` times back to back on the model stream, as the decode step issues
+ * them, and reports the mean device time per pass and the weight bytes one
+ * pass streams.  Activations are scratch; KV and sequences are untouched. */
+S2K_API s2k_status s2k_profile_gemv(s2k_model *m, int32_t reps, double *bytes_per_pass,
+                                    double *ms_per_pass, int32_t *launches_per_pass);
+
+/* Counts kernel launches issued by the library since the last reset. */
+S2K_API uint64_t s2k_launch_count(int32_t reset);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* S2K_H */

@@ -1,0 +1,246 @@
+"""ctypes binding of the CPU oracle (libs2oracle.so).
+
+TEST INFRASTRUCTURE ONLY: the parity checker for the CUDA path and the
+"port" CPU baseline.  Only tests/, __graft_entry__.smoke() and bench.py's
+cpu_baseline leg import this module.  See s2_oracle.h for the reference
+functions it restates.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libs2oracle.so")
+
+_lib = None
+
+
+def build() -> str:
+    src = [os.path.join(HERE, f) for f in ("s2_oracle.c", "s2_oracle.h", "Makefile")]
+    if not os.path.exists(LIB_PATH) or any(os.path.getmtime(s) > os.path.getmtime(LIB_PATH) for s in src):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+class _HP(ctypes.Structure):
+    pass
+
+
+def _hp_fields():
+    from_fields = [
+        "context_length", "vocab_size", "embedding_length", "feed_forward_length", "block_count", "head_count",
+        "head_count_kv", "head_dim", "codebook_size", "num_codebooks", "semantic_begin_id", "semantic_end_id",
+        "rope_freq_base", "rms_norm_eps", "tie_word_embeddings", "attention_qk_norm", "scale_codebook_embeddings",
+        "fast_context_length", "fast_embedding_length", "fast_feed_forward_length", "fast_block_count",
+        "fast_head_count", "fast_head_count_kv", "fast_head_dim", "fast_rope_freq_base", "fast_rms_norm_eps",
+        "fast_attention_qk_norm", "fast_has_project_in", "has_fast_decoder"]
+    floats = {"rope_freq_base", "rms_norm_eps", "fast_rope_freq_base", "fast_rms_norm_eps"}
+    return [(f, ctypes.c_float if f in floats else ctypes.c_int32) for f in from_fields]
+
+
+_HP._fields_ = _hp_fields()
+
+
+class _GP(ctypes.Structure):
+    _fields_ = [("max_new_tokens", ctypes.c_int32), ("temperature", ctypes.c_float), ("top_p", ctypes.c_float),
+                ("top_k", ctypes.c_int32), ("min_tokens_before_end", ctypes.c_int32), ("im_end_id", ctypes.c_int32),
+                ("seed", ctypes.c_uint64), ("seq_id", ctypes.c_uint32)]
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+        sig = {
+            "so_row_bytes": ([ctypes.c_int, i64], i64),
+            "so_dequant_row": ([ctypes.c_int, vp, vp, i64], ctypes.c_int),
+            "so_quantize_act_q8_0": ([vp, i64, vp], None),
+            "so_quantize_act_q8_K": ([vp, i64, vp], None),
+            "so_vec_dot": ([ctypes.c_int, vp, vp, i64], ctypes.c_float),
+            "so_matvec": ([ctypes.c_int, vp, i64, i64, vp, vp], None),
+            "so_fp32_to_fp16": ([ctypes.c_float], ctypes.c_uint16),
+            "so_fp16_to_fp32": ([ctypes.c_uint16], ctypes.c_float),
+            "so_philox4x32_10": ([vp, vp, vp], None),
+            "so_philox_uniform": ([ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32], ctypes.c_double),
+            "so_model_create": ([ctypes.POINTER(_HP)], vp),
+            "so_model_free": ([vp], None),
+            "so_model_set_tensor": ([vp, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(i64), vp, ctypes.c_size_t], ctypes.c_int),
+            "so_model_check": ([vp], ctypes.c_int),
+            "so_kv_init": ([vp, i32], ctypes.c_int),
+            "so_kv_clear": ([vp], None),
+            "so_n_past": ([vp], i32),
+            "so_eval": ([vp, vp, i32, vp, vp], ctypes.c_int),
+            "so_fast_decode": ([vp, vp, vp, i32, vp], ctypes.c_int),
+            "so_sample_token": ([vp, i32, ctypes.c_float, ctypes.c_float, i32, ctypes.c_double], i32),
+            "so_generate": ([vp, vp, i32, ctypes.POINTER(_GP), vp, ctypes.POINTER(i32)], ctypes.c_int),
+            "so_set_threads": ([ctypes.c_int], None),
+            "so_generate_timed": ([vp, vp, i32, ctypes.POINTER(_GP), vp, ctypes.POINTER(i32),
+                                   ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
+        }
+        for name, (a, r) in sig.items():
+            f = getattr(L, name)
+            f.argtypes = a
+            f.restype = r
+        _lib = L
+    return _lib
+
+
+def set_threads(n: int) -> None:
+    lib().so_set_threads(n)
+
+
+def dequant_row(ggml_type: int, data: np.ndarray, n: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    rc = lib().so_dequant_row(ggml_type, np.ascontiguousarray(data).ctypes.data, out.ctypes.data, n)
+    assert rc == 0
+    return out
+
+
+def quantize_act_q8_0(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size // 32 * 34, dtype=np.uint8)
+    lib().so_quantize_act_q8_0(x.ctypes.data, x.size, out.ctypes.data)
+    return out
+
+
+def quantize_act_q8_K(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size // 256 * 292, dtype=np.uint8)
+    lib().so_quantize_act_q8_K(x.ctypes.data, x.size, out.ctypes.data)
+    return out
+
+
+def vec_dot(ggml_type: int, wrow: np.ndarray, act: np.ndarray, n: int) -> float:
+    return float(lib().so_vec_dot(ggml_type, np.ascontiguousarray(wrow).ctypes.data,
+                                  np.ascontiguousarray(act).ctypes.data, n))
+
+
+def matvec(ggml_type: int, w: np.ndarray, rows: int, n: int, x: np.ndarray) -> np.ndarray:
+    y = np.empty(rows, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    lib().so_matvec(ggml_type, np.ascontiguousarray(w).ctypes.data, rows, n, x.ctypes.data, y.ctypes.data)
+    return y
+
+
+def philox(ctr, key):
+    c = (ctypes.c_uint32 * 4)(*ctr)
+    k = (ctypes.c_uint32 * 2)(*key)
+    o = (ctypes.c_uint32 * 4)()
+    lib().so_philox4x32_10(c, k, o)
+    return list(o)
+
+
+def philox_uniform(seed: int, frame: int, purpose: int, seq: int = 0) -> float:
+    return float(lib().so_philox_uniform(seed, frame, purpose, seq))
+
+
+def sample_token(logits: np.ndarray, temperature: float, top_p: float, top_k: int, u: float = 0.0) -> int:
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(lib().so_sample_token(x.ctypes.data, x.size, temperature, top_p, top_k, u))
+
+
+class OracleModel:
+    """CPU restatement of s2::SlowARModel's compute (eval_cached, fast_decode)."""
+
+    def __init__(self, hp):
+        h = _HP()
+        for name, _ in _HP._fields_:
+            setattr(h, name, getattr(hp, name))
+        self.hp = hp
+        self._m = lib().so_model_create(ctypes.byref(h))
+        self._keep = []
+
+    def set_tensor(self, name: str, ggml_type: int, ne, data: np.ndarray) -> None:
+        data = np.ascontiguousarray(data)
+        self._keep.append(data)
+        ne4 = (ctypes.c_int64 * 4)(*[int(x) for x in (list(ne) + [1, 1, 1, 1])[:4]])
+        rc = lib().so_model_set_tensor(self._m, name.encode(), ggml_type, ne4, data.ctypes.data, data.nbytes)
+        if rc != 0:
+            raise RuntimeError(f"oracle rejected tensor {name} ({rc})")
+
+    def load_tensors(self, tensors) -> None:
+        for spec, buf in tensors:
+            self.set_tensor(spec.name, spec.type, spec.ne, buf)
+        rc = lib().so_model_check(self._m)
+        if rc != 0:
+            raise RuntimeError(f"oracle model incomplete ({rc})")
+
+    def init_kv_cache(self, max_seq_len: int) -> None:
+        assert lib().so_kv_init(self._m, max_seq_len) == 0
+
+    def clear_kv_cache(self) -> None:
+        lib().so_kv_clear(self._m)
+
+    @property
+    def n_past(self) -> int:
+        return int(lib().so_n_past(self._m))
+
+    def eval(self, flat_tokens: np.ndarray, n_tokens: int):
+        flat = np.ascontiguousarray(flat_tokens, dtype=np.int32)
+        hidden = np.empty(self.hp.embedding_length, dtype=np.float32)
+        logits = np.empty(self.hp.vocab_size, dtype=np.float32)
+        rc = lib().so_eval(self._m, flat.ctypes.data, n_tokens, hidden.ctypes.data, logits.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"oracle eval failed ({rc})")
+        return hidden, logits
+
+    def fast_decode(self, hidden: np.ndarray, prefix) -> np.ndarray:
+        h = np.ascontiguousarray(hidden, dtype=np.float32)
+        p = np.ascontiguousarray(np.asarray(prefix, dtype=np.int32))
+        out = np.empty(self.hp.codebook_size, dtype=np.float32)
+        rc = lib().so_fast_decode(self._m, h.ctypes.data, p.ctypes.data if p.size else None, int(p.size),
+                                  out.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"oracle fast_decode failed ({rc})")
+        return out
+
+    def generate(self, prompt: np.ndarray, max_new_tokens: int, temperature: float = 0.0, top_p: float = 0.8,
+                 top_k: int = 30, min_tokens_before_end: int = 0, im_end_id: int = -1, seed: int = 0,
+                 seq_id: int = 0) -> np.ndarray:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        rows, cols = p.shape
+        self.init_kv_cache(cols + max_new_tokens)
+        ncb = max(self.hp.num_codebooks, 1)
+        codes = np.zeros(ncb * max(max_new_tokens, 1), dtype=np.int32)
+        nf = ctypes.c_int32(0)
+        gp = _GP(max_new_tokens, temperature, top_p, top_k, min_tokens_before_end, im_end_id, seed, seq_id)
+        rc = lib().so_generate(self._m, p.ctypes.data, cols, ctypes.byref(gp), codes.ctypes.data, ctypes.byref(nf))
+        if rc != 0:
+            raise RuntimeError(f"oracle generate failed ({rc})")
+        n = nf.value
+        return codes[: ncb * n].reshape(ncb, n)
+
+    def generate_timed(self, prompt: np.ndarray, max_new_tokens: int, **kw):
+        """generate() plus the reference's [Metrics] split: (codes, prefill_ms, loop_ms)."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        rows, cols = p.shape
+        self.init_kv_cache(cols + max_new_tokens)
+        ncb = max(self.hp.num_codebooks, 1)
+        codes = np.zeros(ncb * max(max_new_tokens, 1), dtype=np.int32)
+        nf = ctypes.c_int32(0)
+        gp = _GP(max_new_tokens, kw.get("temperature", 0.0), kw.get("top_p", 0.8), kw.get("top_k", 30),
+                 kw.get("min_tokens_before_end", 0), kw.get("im_end_id", -1), kw.get("seed", 0), kw.get("seq_id", 0))
+        pm, lm = ctypes.c_double(0), ctypes.c_double(0)
+        rc = lib().so_generate_timed(self._m, p.ctypes.data, cols, ctypes.byref(gp), codes.ctypes.data,
+                                     ctypes.byref(nf), ctypes.byref(pm), ctypes.byref(lm))
+        if rc != 0:
+            raise RuntimeError(f"oracle generate failed ({rc})")
+        n = nf.value
+        return codes[: ncb * n].reshape(ncb, n), pm.value, lm.value
+
+    def close(self) -> None:
+        if self._m:
+            lib().so_model_free(self._m)
+            self._m = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

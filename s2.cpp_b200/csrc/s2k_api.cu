@@ -1,0 +1,1110 @@
+// s2k_api.cu -- the C ABI of include/s2k.h: model and weight upload,
+// sequences with a paged f16 KV cache, the eval_cached / fast_decode entry
+// points, and the on-device frame loop captured as one CUDA graph per frame.
+#include "../../include/s2k.h"
+#include "s2k_common.cuh"
+#include "s2k_device.h"
+#include "s2k_kernels.h"
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstddef>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace s2k {
+
+static std::atomic<unsigned long long> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
+static thread_local std::string g_err;
+static s2k_status fail(s2k_status code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CU(expr)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (expr);                                                                   \
+        if (e_ != cudaSuccess)                                                                     \
+            return fail(e_ == cudaErrorMemoryAllocation ? S2K_ERR_OOM : S2K_ERR_CUDA, "%s: %s (%s:%d)", #expr, \
+                        cudaGetErrorString(e_), __FILE__, __LINE__);                               \
+    } while (0)
+
+struct Layer {
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    DevMat wqkv, wo, w13, w2;
+    bool has_w1 = false, has_w3 = false;
+};
+
+// Activations of one transformer stack for up to T tokens.
+struct Work {
+    int T = 0, dim = 0, qs = 0, kvs = 0, ff = 0, H = 0, n_splits_max = 0;
+    float *x = nullptr, *h = nullptr, *qkv = nullptr, *attn = nullptr, *ff_buf = nullptr;
+    float *kcur = nullptr, *vcur = nullptr, *part = nullptr;
+    int *counters = nullptr;
+};
+
+}  // namespace s2k
+
+using namespace s2k;
+
+struct s2k_model {
+    s2k_hparams hp{};
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    DevMat embed, cb_embed, fast_embed, fast_out;
+    float *norm = nullptr, *fast_norm = nullptr;
+    std::vector<Layer> layers, fast_layers;
+    std::vector<void *> allocs;
+    bool finalized = false;
+    int *d_err = nullptr;
+    // staging for uploads
+    uint8_t *staging = nullptr;
+    size_t staging_bytes = 0;
+    // Slow workspace (ws_gen changes whenever it is reallocated: captured
+    // frame graphs hold its pointers)
+    Work sw;
+    int ws_gen = 0;
+    float *logits = nullptr, *hidden = nullptr;
+    int *tokens = nullptr;
+    int tokens_cap = 0;
+    // Fast workspace (T <= num_codebooks)
+    Work fw;
+    std::vector<float *> fkcur, fvcur;
+    float *flogits = nullptr, *fhidden = nullptr;
+    int *fcodes = nullptr;
+    // standalone sampler scratch
+    float *samp_logits = nullptr;
+    int samp_cap = 0;
+    int *samp_out = nullptr;
+
+    template <class T>
+    cudaError_t alloc(T **p, size_t n) {
+        void *v = nullptr;
+        cudaError_t e = cudaMalloc(&v, std::max<size_t>(n, 1) * sizeof(T));
+        if (e == cudaSuccess) {
+            allocs.push_back(v);
+            *p = reinterpret_cast<T *>(v);
+        }
+        return e;
+    }
+    void release(void *p) {
+        if (!p) return;
+        auto it = std::find(allocs.begin(), allocs.end(), p);
+        if (it != allocs.end()) allocs.erase(it);
+        cudaFree(p);
+    }
+};
+
+struct s2k_seq {
+    s2k_model *m = nullptr;
+    int max_seq_len = 0, n_pages = 0;
+    __half *k = nullptr, *v = nullptr;
+    int *block_table = nullptr;
+    SeqDev *dev = nullptr;
+    HostStatus *hstat = nullptr;      // mapped pinned
+    HostStatus *hstat_dev = nullptr;  // device alias
+    int n_past = 0;                   // host mirror
+    int *codes = nullptr;             // [ncb][codes_cap]
+    int codes_cap = 0;
+    int *prompt = nullptr;
+    int prompt_cap = 0;
+    cudaGraphExec_t frame_exec = nullptr;
+    size_t frame_nodes = 0;
+    int frame_gen = -1;
+    KvPaged kv() const {
+        KvPaged p;
+        p.k = k;
+        p.v = v;
+        p.block_table = block_table;
+        p.n_layers = m->hp.block_count;
+        p.n_kv_heads = m->hp.head_count_kv;
+        p.head_dim = m->hp.head_dim;
+        p.n_pages = n_pages;
+        return p;
+    }
+};
+
+// ---------------------------------------------------------------------------
+// helpers
+// ---------------------------------------------------------------------------
+static int cuda_set(int dev) { return cudaSetDevice(dev) == cudaSuccess ? 0 : -1; }
+
+static s2k_status check_err_word(s2k_model *m) {
+    int h = 0;
+    CU(cudaMemcpy(&h, m->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h) {
+        CU(cudaMemset(m->d_err, 0, sizeof(int)));
+        if (h & (ERR_WAIT_FULL | ERR_WAIT_EMPTY)) return fail(S2K_ERR_TIMEOUT, "device wait timed out (flags 0x%x)", h);
+        return fail(S2K_ERR_ARG, "device reported invalid input (flags 0x%x)", h);
+    }
+    return S2K_OK;
+}
+
+static int n_splits_for(int T) {
+    if (T <= 1) return 16;
+    if (T >= 16) return 1;
+    return std::max(1, 16 / T);
+}
+
+static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int dim, int H, int Hkv, int hd, int ff) {
+    w.T = T;
+    w.dim = dim;
+    w.qs = H * hd;
+    w.kvs = Hkv * hd;
+    w.ff = ff;
+    w.H = H;
+    w.n_splits_max = 16;
+    const size_t tn = (size_t)std::max(T, 1);
+    cudaError_t e;
+    if ((e = m->alloc(&w.x, tn * dim))) return e;
+    if ((e = m->alloc(&w.h, tn * dim))) return e;
+    if ((e = m->alloc(&w.qkv, tn * (w.qs + 2 * w.kvs)))) return e;
+    if ((e = m->alloc(&w.attn, tn * w.qs))) return e;
+    if ((e = m->alloc(&w.ff_buf, tn * 2 * ff))) return e;
+    if ((e = m->alloc(&w.kcur, tn * w.kvs))) return e;
+    if ((e = m->alloc(&w.vcur, tn * w.kvs))) return e;
+    const size_t ts = std::max<size_t>(tn * n_splits_for(T), 16);
+    if ((e = m->alloc(&w.part, ts * H * (hd + 2)))) return e;
+    if ((e = m->alloc(&w.counters, tn * Hkv))) return e;
+    return cudaMemset(w.counters, 0, tn * Hkv * sizeof(int));
+}
+
+static void work_free(s2k_model *m, Work &w) {
+    for (void *p : {(void *)w.x, (void *)w.h, (void *)w.qkv, (void *)w.attn, (void *)w.ff_buf, (void *)w.kcur,
+                    (void *)w.vcur, (void *)w.part, (void *)w.counters})
+        m->release(p);
+    w = Work();
+}
+
+static s2k_status ensure_slow_work(s2k_model *m, int T) {
+    if (m->sw.T >= T) return S2K_OK;
+    work_free(m, m->sw);
+    m->ws_gen++;
+    const s2k_hparams &hp = m->hp;
+    CU(work_alloc(m, m->sw, T, hp.embedding_length, hp.head_count, hp.head_count_kv, hp.head_dim,
+                  hp.feed_forward_length));
+    return S2K_OK;
+}
+
+// ---------------------------------------------------------------------------
+// stacks
+// ---------------------------------------------------------------------------
+struct StackCall {
+    bool fast;
+    int T;
+    const int *pos_base;  // device n_past (Slow) or null
+    int pos_add;
+    int cur_base;
+    KvPaged kv;  // Slow only
+    int n_splits;
+    const int *done;
+};
+
+static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
+    const s2k_hparams &hp = m->hp;
+    Work &w = c.fast ? m->fw : m->sw;
+    const std::vector<Layer> &layers = c.fast ? m->fast_layers : m->layers;
+    const int H = c.fast ? hp.fast_head_count : hp.head_count;
+    const int Hkv = c.fast ? hp.fast_head_count_kv : hp.head_count_kv;
+    const int hd = c.fast ? hp.fast_head_dim : hp.head_dim;
+    const float eps = c.fast ? hp.fast_rms_norm_eps : hp.rms_norm_eps;
+    const float base = c.fast ? hp.fast_rope_freq_base : hp.rope_freq_base;
+    const float theta_scale = powf(base, -2.0f / (float)hd);
+    const int qkvs = w.qs + 2 * w.kvs;
+    const int dim = w.dim;
+    cudaStream_t st = m->stream;
+    cudaError_t e;
+    for (size_t il = 0; il < layers.size(); ++il) {
+        const Layer &L = layers[il];
+        GemvArgs g;
+        g.w = &L.wqkv;
+        g.x = w.x;
+        g.ldx = dim;
+        g.M = c.T;
+        g.in_mode = IN_RMSNORM;
+        g.norm_w = L.attn_norm;
+        g.eps = eps;
+        g.y = w.qkv;
+        g.ldy = qkvs;
+        g.done = c.done;
+        g.err = m->d_err;
+        if ((e = launch_gemv(g, m->num_sms, st))) return e;
+
+        QkPrepArgs q;
+        q.qkv = w.qkv;
+        q.ldqkv = qkvs;
+        q.T = c.T;
+        q.H = H;
+        q.Hkv = Hkv;
+        q.hd = hd;
+        q.q_norm = L.q_norm;
+        q.k_norm = L.k_norm;
+        q.eps = eps;
+        q.theta_scale = theta_scale;
+        q.pos_base = c.pos_base;
+        q.pos_add = c.pos_add;
+        q.kcur = c.fast ? m->fkcur[il] : w.kcur;
+        q.vcur = c.fast ? m->fvcur[il] : w.vcur;
+        q.cur_base = c.cur_base;
+        q.kv = c.kv;
+        q.layer = (int)il;
+        q.done = c.done;
+        q.err = m->d_err;
+        if ((e = launch_qk_prep(q, st))) return e;
+
+        AttnArgs a;
+        a.q = w.qkv;
+        a.ldq = qkvs;
+        a.T = c.T;
+        a.H = H;
+        a.Hkv = Hkv;
+        a.hd = hd;
+        a.scale = 1.0f / sqrtf((float)hd);
+        a.n_cached = c.fast ? nullptr : c.pos_base;
+        a.kv = c.kv;
+        a.layer = (int)il;
+        a.kcur = q.kcur;
+        a.vcur = q.vcur;
+        a.cur_base = c.cur_base;
+        a.n_splits = c.n_splits;
+        a.part = w.part;
+        a.counters = w.counters;
+        a.out = w.attn;
+        a.done = c.done;
+        a.err = m->d_err;
+        if ((e = launch_attention(a, st))) return e;
+
+        GemvArgs o = g;
+        o.w = &L.wo;
+        o.x = w.attn;
+        o.ldx = w.qs;
+        o.in_mode = IN_PLAIN;
+        o.norm_w = nullptr;
+        o.y = w.h;
+        o.ldy = dim;
+        o.res = w.x;
+        o.ldres = dim;
+        if ((e = launch_gemv(o, m->num_sms, st))) return e;
+
+        GemvArgs f1 = g;
+        f1.w = &L.w13;
+        f1.x = w.h;
+        f1.ldx = dim;
+        f1.in_mode = IN_RMSNORM;
+        f1.norm_w = L.ffn_norm;
+        f1.y = w.ff_buf;
+        f1.ldy = 2 * w.ff;
+        if ((e = launch_gemv(f1, m->num_sms, st))) return e;
+
+        GemvArgs f2 = g;
+        f2.w = &L.w2;
+        f2.x = w.ff_buf;
+        f2.ldx = 2 * w.ff;
+        f2.in_mode = IN_SWIGLU;
+        f2.norm_w = nullptr;
+        f2.y = w.x;
+        f2.ldy = dim;
+        f2.res = w.h;
+        f2.ldres = dim;
+        if ((e = launch_gemv(f2, m->num_sms, st))) return e;
+    }
+    return cudaSuccess;
+}
+
+// Slow step over T tokens already in `tokens_dev` ([T][ncb+1]): embedding,
+// 36 layers, final norm + tied LM head on the last token, n_past += T.
+static cudaError_t enqueue_slow(s2k_model *m, s2k_seq *s, int T, const int *tokens_dev, const int *done) {
+    const s2k_hparams &hp = m->hp;
+    cudaStream_t st = m->stream;
+    cudaError_t e;
+    EmbedArgs ea;
+    ea.tok_emb = &m->embed;
+    ea.cb_emb = &m->cb_embed;
+    ea.tokens = tokens_dev;
+    ea.T = T;
+    ea.ncb = hp.num_codebooks;
+    ea.cb_size = hp.codebook_size;
+    ea.sem_begin = hp.semantic_begin_id;
+    ea.sem_end = hp.semantic_end_id;
+    ea.scale_cb = hp.scale_codebook_embeddings;
+    ea.sem_scale = 1.0f / sqrtf((float)(hp.num_codebooks + 1));
+    ea.x = m->sw.x;
+    ea.done = done;
+    ea.err = m->d_err;
+    if ((e = launch_embed_slow(ea, st))) return e;
+    StackCall c;
+    c.fast = false;
+    c.T = T;
+    c.pos_base = &s->dev->state.n_past;
+    c.pos_add = 0;
+    c.cur_base = 0;
+    c.kv = s->kv();
+    c.n_splits = n_splits_for(T);
+    c.done = done;
+    if ((e = run_stack(m, c))) return e;
+    GemvArgs hd;
+    hd.w = &m->embed;
+    hd.x = m->sw.x + (size_t)(T - 1) * hp.embedding_length;
+    hd.ldx = hp.embedding_length;
+    hd.M = 1;
+    hd.in_mode = IN_RMSNORM;
+    hd.norm_w = m->norm;
+    hd.eps = hp.rms_norm_eps;
+    hd.y = m->logits;
+    hd.ldy = hp.vocab_size;
+    hd.act_out = m->hidden;
+    hd.done = done;
+    hd.err = m->d_err;
+    if ((e = launch_gemv(hd, m->num_sms, st))) return e;
+    return launch_advance(s->dev, T, done, st);
+}
+
+// One Fast-AR pass over rows already in fw.x.
+static cudaError_t enqueue_fast(s2k_model *m, int T, int pos_add, const int *done) {
+    const s2k_hparams &hp = m->hp;
+    cudaError_t e;
+    StackCall c;
+    c.fast = true;
+    c.T = T;
+    c.pos_base = nullptr;
+    c.pos_add = pos_add;
+    c.cur_base = pos_add;
+    c.n_splits = 1;
+    c.done = done;
+    if ((e = run_stack(m, c))) return e;
+    GemvArgs hd;
+    hd.w = &m->fast_out;
+    hd.x = m->fw.x + (size_t)(T - 1) * hp.fast_embedding_length;
+    hd.ldx = hp.fast_embedding_length;
+    hd.M = 1;
+    hd.in_mode = IN_RMSNORM;
+    hd.norm_w = m->fast_norm;
+    hd.eps = hp.fast_rms_norm_eps;
+    hd.y = m->flogits;
+    hd.ldy = hp.codebook_size;
+    hd.done = done;
+    hd.err = m->d_err;
+    return launch_gemv(hd, m->num_sms, m->stream);
+}
+
+// All device work of one frame after its main token is known
+// (src/s2_generate.cpp:123-182): 9 Fast-AR passes + samples, commit, Slow step,
+// main-token sampling for the next frame.
+static cudaError_t enqueue_frame(s2k_model *m, s2k_seq *s) {
+    const s2k_hparams &hp = m->hp;
+    cudaStream_t st = m->stream;
+    const int *done = &s->dev->state.done;
+    const int *codes = s->dev->state.codes;
+    cudaError_t e;
+    for (int p = 0; p + 1 < hp.num_codebooks; ++p) {
+        if (p == 0) {
+            if ((e = launch_embed_fast(&m->fast_embed, m->hidden, codes, 0, 2, m->fw.x, hp.fast_embedding_length, done,
+                                       m->d_err, st)))
+                return e;
+            if ((e = enqueue_fast(m, 2, 0, done))) return e;
+        } else {
+            if ((e = launch_embed_fast(&m->fast_embed, nullptr, codes, p, 1, m->fw.x, hp.fast_embedding_length, done,
+                                       m->d_err, st)))
+                return e;
+            if ((e = enqueue_fast(m, 1, p + 1, done))) return e;
+        }
+        if ((e = launch_sample_fast(m->flogits, s->dev, p + 1, m->d_err, st))) return e;
+    }
+    if ((e = launch_frame_commit(s->dev, st))) return e;
+    if ((e = enqueue_slow(m, s, 1, s->dev->state.step_in, done))) return e;
+    return launch_sample_main(m->logits, s->dev, m->d_err, st);
+}
+
+// ---------------------------------------------------------------------------
+// tensor names
+// ---------------------------------------------------------------------------
+enum Slot { SL_NONE, SL_EMBED, SL_CB, SL_NORM, SL_FEMB, SL_FNORM, SL_FOUT, SL_ATTN_NORM, SL_FFN_NORM, SL_QN, SL_KN,
+            SL_WQKV, SL_WO, SL_W1, SL_W2, SL_W3 };
+
+static Slot parse_name(const s2k_model *m, const char *name, bool *fast, int *il) {
+    *fast = false;
+    *il = -1;
+    if (!strcmp(name, "embeddings.weight")) return SL_EMBED;
+    if (!strcmp(name, "codebook_embeddings.weight")) return SL_CB;
+    if (!strcmp(name, "norm.weight")) return SL_NORM;
+    if (!strcmp(name, "fast_embeddings.weight")) return SL_FEMB;
+    if (!strcmp(name, "fast_norm.weight")) return SL_FNORM;
+    if (!strcmp(name, "fast_output.weight")) return SL_FOUT;
+    int off = 0;
+    if (sscanf(name, "layers.%d.%n", il, &off) == 1 && off > 0) {
+        *fast = false;
+    } else if (sscanf(name, "fast_layers.%d.%n", il, &off) == 1 && off > 0) {
+        *fast = true;
+    } else {
+        return SL_NONE;
+    }
+    const int nl = *fast ? m->hp.fast_block_count : m->hp.block_count;
+    if (*il < 0 || *il >= nl) return SL_NONE;
+    const char *s = name + off;
+    if (!strcmp(s, "attention_norm.weight")) return SL_ATTN_NORM;
+    if (!strcmp(s, "ffn_norm.weight")) return SL_FFN_NORM;
+    if (!strcmp(s, "attention.q_norm.weight")) return SL_QN;
+    if (!strcmp(s, "attention.k_norm.weight")) return SL_KN;
+    if (!strcmp(s, "attention.wqkv.weight")) return SL_WQKV;
+    if (!strcmp(s, "attention.wo.weight")) return SL_WO;
+    if (!strcmp(s, "feed_forward.w1.weight")) return SL_W1;
+    if (!strcmp(s, "feed_forward.w2.weight")) return SL_W2;
+    if (!strcmp(s, "feed_forward.w3.weight")) return SL_W3;
+    return SL_NONE;
+}
+
+static s2k_status upload_vec(s2k_model *m, float **dst, int type, const int64_t ne[4], const void *host, size_t nbytes,
+                             int64_t expect, const char *name) {
+    if (type != S2K_TYPE_F32) return fail(S2K_ERR_UNSUPPORTED, "%s: norm weights must be F32 (type %d)", name, type);
+    if (ne[0] != expect || (ne[1] > 1) || nbytes != (size_t)expect * 4)
+        return fail(S2K_ERR_ARG, "%s: expected [%lld] f32, got ne0=%lld bytes=%zu", name, (long long)expect,
+                    (long long)ne[0], nbytes);
+    if (!*dst) CU(m->alloc(dst, (size_t)expect));
+    CU(cudaMemcpyAsync(*dst, host, nbytes, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    return S2K_OK;
+}
+
+static s2k_status ensure_mat(s2k_model *m, DevMat &dm, int type, int rows, int cols) {
+    if (dm.q) {
+        if (dm.rows != rows || dm.cols != cols || dm.type != type) return fail(S2K_ERR_ARG, "matrix shape changed");
+        return S2K_OK;
+    }
+    dm.type = type;
+    dm.rows = rows;
+    dm.cols = cols;
+    CU(m->alloc(&dm.q, (size_t)rows * cols));
+    CU(m->alloc(&dm.d, (size_t)rows * (cols / 32)));
+    return S2K_OK;
+}
+
+static s2k_status upload_mat(s2k_model *m, DevMat &dm, int type, const int64_t ne[4], const void *host, size_t nbytes,
+                             int64_t expect_in, int64_t expect_out, int dst_rows, int row_stride, int row_offset,
+                             const char *name) {
+    if (type != S2K_TYPE_Q8_0)
+        return fail(S2K_ERR_UNSUPPORTED, "%s: ggml type %d not supported by this build (Q8_0 only)", name, type);
+    if (ne[0] != expect_in || ne[1] != expect_out)
+        return fail(S2K_ERR_ARG, "%s: expected ne [%lld, %lld], got [%lld, %lld]", name, (long long)expect_in,
+                    (long long)expect_out, (long long)ne[0], (long long)ne[1]);
+    if (ne[0] % 256 != 0) return fail(S2K_ERR_UNSUPPORTED, "%s: row length %lld not a multiple of 256", name, (long long)ne[0]);
+    const size_t row_bytes = (size_t)ne[0] / 32 * 34;
+    if (nbytes != row_bytes * (size_t)ne[1])
+        return fail(S2K_ERR_ARG, "%s: %zu bytes, expected %zu", name, nbytes, row_bytes * (size_t)ne[1]);
+    s2k_status rc = ensure_mat(m, dm, type, dst_rows, (int)ne[0]);
+    if (rc) return rc;
+    const size_t chunk_rows = std::max<size_t>(1, (size_t)(256u << 20) / row_bytes);
+    if (!m->staging) {
+        m->staging_bytes = chunk_rows * row_bytes;
+        CU(m->alloc(&m->staging, m->staging_bytes));
+    }
+    const size_t rows_per = std::max<size_t>(1, m->staging_bytes / row_bytes);
+    const int nb = (int)(ne[0] / 32);
+    for (size_t r0 = 0; r0 < (size_t)ne[1]; r0 += rows_per) {
+        const size_t nr = std::min(rows_per, (size_t)ne[1] - r0);
+        CU(cudaMemcpyAsync(m->staging, (const uint8_t *)host + r0 * row_bytes, nr * row_bytes, cudaMemcpyHostToDevice,
+                           m->stream));
+        DevMat view = dm;
+        view.q = dm.q + (r0 * row_stride) * (size_t)dm.cols;
+        view.d = dm.d + (r0 * row_stride) * (size_t)nb;
+        CU(launch_relayout_q8_0(m->staging, (int)nr, (int)ne[0], &view, row_stride, row_offset, m->stream));
+        CU(cudaStreamSynchronize(m->stream));
+    }
+    return S2K_OK;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+S2K_API int32_t s2k_abi_version(void) { return S2K_ABI_VERSION; }
+
+S2K_API const char *s2k_last_error(void) { return g_err.c_str(); }
+
+S2K_API uint64_t s2k_launch_count(int32_t reset) {
+    return reset ? g_launches.exchange(0) : g_launches.load();
+}
+
+S2K_API s2k_status s2k_device_count(int32_t *count) {
+    if (!count) return fail(S2K_ERR_ARG, "count is NULL");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        *count = 0;
+        return fail(S2K_ERR_NO_DEVICE, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+    }
+    *count = n;
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_model_create(int32_t device, const s2k_hparams *hp, s2k_model **out) {
+    if (!hp || !out) return fail(S2K_ERR_ARG, "NULL argument");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return fail(S2K_ERR_NO_DEVICE, "no CUDA device");
+    if (device < 0 || device >= n) return fail(S2K_ERR_ARG, "device %d out of range (%d devices)", device, n);
+    if (hp->embedding_length <= 0 || hp->block_count <= 0 || hp->head_count <= 0 || hp->head_count_kv <= 0 ||
+        hp->head_dim != 128 || hp->head_count % hp->head_count_kv != 0 || hp->head_count / hp->head_count_kv > 8 ||
+        hp->vocab_size <= 0 || hp->num_codebooks < 0 || hp->num_codebooks > 15 || hp->feed_forward_length <= 0)
+        return fail(S2K_ERR_UNSUPPORTED, "unsupported hparams (head_dim must be 128, GQA group <= 8, <= 15 codebooks)");
+    if (hp->has_fast_decoder &&
+        (hp->fast_head_dim != 128 || hp->fast_head_count % hp->fast_head_count_kv != 0 ||
+         hp->fast_head_count / hp->fast_head_count_kv > 8 || hp->fast_embedding_length != hp->embedding_length ||
+         hp->fast_has_project_in))
+        return fail(S2K_ERR_UNSUPPORTED, "unsupported Fast-AR hparams (fast_dim must equal dim, no project_in)");
+    if (cudaSetDevice(device) != cudaSuccess) return fail(S2K_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    s2k_model *m = new s2k_model();
+    m->hp = *hp;
+    m->device = device;
+    cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete m;
+        return fail(S2K_ERR_CUDA, "stream create failed");
+    }
+    m->layers.resize(hp->block_count);
+    m->fast_layers.resize(hp->has_fast_decoder ? hp->fast_block_count : 0);
+    if (m->alloc(&m->d_err, 1) != cudaSuccess || cudaMemset(m->d_err, 0, sizeof(int)) != cudaSuccess) {
+        s2k_model_free(m);
+        return fail(S2K_ERR_OOM, "device allocation failed");
+    }
+    *out = m;
+    return S2K_OK;
+}
+
+S2K_API void s2k_model_free(s2k_model *m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+S2K_API s2k_status s2k_model_get_hparams(const s2k_model *m, s2k_hparams *out) {
+    if (!m || !out) return fail(S2K_ERR_ARG, "NULL argument");
+    *out = m->hp;
+    return S2K_OK;
+}
+
+S2K_API size_t s2k_model_weight_bytes(const s2k_model *m) {
+    if (!m) return 0;
+    size_t b = m->embed.bytes() + m->cb_embed.bytes() + m->fast_embed.bytes() + m->fast_out.bytes();
+    for (const auto &L : m->layers) b += L.wqkv.bytes() + L.wo.bytes() + L.w13.bytes() + L.w2.bytes();
+    for (const auto &L : m->fast_layers) b += L.wqkv.bytes() + L.wo.bytes() + L.w13.bytes() + L.w2.bytes();
+    return b;
+}
+
+S2K_API void *s2k_model_stream(s2k_model *m) { return m ? (void *)m->stream : nullptr; }
+
+S2K_API s2k_status s2k_model_upload_tensor(s2k_model *m, const char *name, int32_t type, const int64_t ne[4],
+                                           const void *host, size_t nbytes) {
+    if (!m || !name || !ne || !host) return fail(S2K_ERR_ARG, "NULL argument");
+    if (m->finalized) return fail(S2K_ERR_STATE, "model already finalized");
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    const s2k_hparams &hp = m->hp;
+    bool fast = false;
+    int il = -1;
+    const Slot sl = parse_name(m, name, &fast, &il);
+    if (sl == SL_NONE) return fail(S2K_ERR_ARG, "unknown tensor name '%s'", name);
+    if (fast && !hp.has_fast_decoder) return fail(S2K_ERR_ARG, "'%s' but the model has no fast decoder", name);
+    const int dim = hp.embedding_length;
+    const int ff = fast ? hp.fast_feed_forward_length : hp.feed_forward_length;
+    const int H = fast ? hp.fast_head_count : hp.head_count;
+    const int Hkv = fast ? hp.fast_head_count_kv : hp.head_count_kv;
+    const int hd = fast ? hp.fast_head_dim : hp.head_dim;
+    Layer *L = il >= 0 ? (fast ? &m->fast_layers[il] : &m->layers[il]) : nullptr;
+    switch (sl) {
+    case SL_EMBED: return upload_mat(m, m->embed, type, ne, host, nbytes, dim, hp.vocab_size, hp.vocab_size, 1, 0, name);
+    case SL_CB:
+        return upload_mat(m, m->cb_embed, type, ne, host, nbytes, dim, (int64_t)hp.num_codebooks * hp.codebook_size,
+                          hp.num_codebooks * hp.codebook_size, 1, 0, name);
+    case SL_NORM: return upload_vec(m, &m->norm, type, ne, host, nbytes, dim, name);
+    case SL_FEMB:
+        return upload_mat(m, m->fast_embed, type, ne, host, nbytes, dim, hp.codebook_size, hp.codebook_size, 1, 0, name);
+    case SL_FNORM: return upload_vec(m, &m->fast_norm, type, ne, host, nbytes, dim, name);
+    case SL_FOUT:
+        return upload_mat(m, m->fast_out, type, ne, host, nbytes, dim, hp.codebook_size, hp.codebook_size, 1, 0, name);
+    case SL_ATTN_NORM: return upload_vec(m, &L->attn_norm, type, ne, host, nbytes, dim, name);
+    case SL_FFN_NORM: return upload_vec(m, &L->ffn_norm, type, ne, host, nbytes, dim, name);
+    case SL_QN: return upload_vec(m, &L->q_norm, type, ne, host, nbytes, hd, name);
+    case SL_KN: return upload_vec(m, &L->k_norm, type, ne, host, nbytes, hd, name);
+    case SL_WQKV: {
+        const int rows = (H + 2 * Hkv) * hd;
+        return upload_mat(m, L->wqkv, type, ne, host, nbytes, dim, rows, rows, 1, 0, name);
+    }
+    case SL_WO: return upload_mat(m, L->wo, type, ne, host, nbytes, (int64_t)H * hd, dim, dim, 1, 0, name);
+    case SL_W1: {
+        s2k_status rc = upload_mat(m, L->w13, type, ne, host, nbytes, dim, ff, 2 * ff, 2, 0, name);
+        if (!rc) L->has_w1 = true;
+        return rc;
+    }
+    case SL_W3: {
+        s2k_status rc = upload_mat(m, L->w13, type, ne, host, nbytes, dim, ff, 2 * ff, 2, 1, name);
+        if (!rc) L->has_w3 = true;
+        return rc;
+    }
+    case SL_W2: return upload_mat(m, L->w2, type, ne, host, nbytes, ff, dim, dim, 1, 0, name);
+    default: return fail(S2K_ERR_ARG, "unhandled tensor '%s'", name);
+    }
+}
+
+S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
+    if (!m) return fail(S2K_ERR_ARG, "NULL model");
+    if (m->finalized) return S2K_OK;
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    const s2k_hparams &hp = m->hp;
+    if (!m->embed.q) return fail(S2K_ERR_STATE, "missing tensor: embeddings.weight");
+    if (hp.num_codebooks > 0 && !m->cb_embed.q) return fail(S2K_ERR_STATE, "missing tensor: codebook_embeddings.weight");
+    if (!m->norm) return fail(S2K_ERR_STATE, "missing tensor: norm.weight");
+    auto check_layers = [&](std::vector<Layer> &ls, bool fast) -> s2k_status {
+        const int qkn = fast ? hp.fast_attention_qk_norm : hp.attention_qk_norm;
+        for (size_t i = 0; i < ls.size(); ++i) {
+            Layer &L = ls[i];
+            const char *pre = fast ? "fast_layers" : "layers";
+            if (!L.attn_norm) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.attention_norm.weight", pre, i);
+            if (!L.ffn_norm) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.ffn_norm.weight", pre, i);
+            if (!L.wqkv.q) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.attention.wqkv.weight", pre, i);
+            if (!L.wo.q) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.attention.wo.weight", pre, i);
+            if (!L.has_w1) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.feed_forward.w1.weight", pre, i);
+            if (!L.has_w3) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.feed_forward.w3.weight", pre, i);
+            if (!L.w2.q) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.feed_forward.w2.weight", pre, i);
+            if (qkn && (!L.q_norm || !L.k_norm))
+                return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.attention.q_norm/k_norm.weight", pre, i);
+            if (!qkn) {
+                L.q_norm = nullptr;
+                L.k_norm = nullptr;
+            }
+        }
+        return S2K_OK;
+    };
+    s2k_status rc = check_layers(m->layers, false);
+    if (rc) return rc;
+    if (hp.has_fast_decoder) {
+        if (!m->fast_embed.q) return fail(S2K_ERR_STATE, "missing tensor: fast_embeddings.weight");
+        if (!m->fast_norm) return fail(S2K_ERR_STATE, "missing tensor: fast_norm.weight");
+        if (!m->fast_out.q) return fail(S2K_ERR_STATE, "missing tensor: fast_output.weight");
+        rc = check_layers(m->fast_layers, true);
+        if (rc) return rc;
+    }
+    CU(gemv_setup());
+    CU(sampler_setup());
+    if (m->staging) {
+        m->release(m->staging);
+        m->staging = nullptr;
+        m->staging_bytes = 0;
+    }
+    CU(m->alloc(&m->logits, (size_t)hp.vocab_size));
+    CU(m->alloc(&m->hidden, (size_t)hp.embedding_length));
+    rc = ensure_slow_work(m, 16);
+    if (rc) return rc;
+    if (hp.has_fast_decoder) {
+        const int Tf = std::max(hp.num_codebooks, 2);
+        CU(work_alloc(m, m->fw, Tf, hp.fast_embedding_length, hp.fast_head_count, hp.fast_head_count_kv,
+                      hp.fast_head_dim, hp.fast_feed_forward_length));
+        const int fkvs = hp.fast_head_count_kv * hp.fast_head_dim;
+        m->fkcur.assign(hp.fast_block_count, nullptr);
+        m->fvcur.assign(hp.fast_block_count, nullptr);
+        for (int i = 0; i < hp.fast_block_count; ++i) {
+            CU(m->alloc(&m->fkcur[i], (size_t)Tf * fkvs));
+            CU(m->alloc(&m->fvcur[i], (size_t)Tf * fkvs));
+        }
+        CU(m->alloc(&m->flogits, (size_t)hp.codebook_size));
+        CU(m->alloc(&m->fhidden, (size_t)hp.embedding_length));
+        CU(m->alloc(&m->fcodes, 16));
+    }
+    CU(cudaStreamSynchronize(m->stream));
+    m->finalized = true;
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_seq_create(s2k_model *m, int32_t max_seq_len, s2k_seq **out) {
+    if (!m || !out || max_seq_len <= 0) return fail(S2K_ERR_ARG, "bad argument");
+    if (!m->finalized) return fail(S2K_ERR_STATE, "model not finalized");
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    *out = nullptr;
+    s2k_seq *s = new s2k_seq();
+    s->m = m;
+    s->max_seq_len = max_seq_len;
+    s->n_pages = (max_seq_len + kPage - 1) / kPage;
+    const s2k_hparams &hp = m->hp;
+    const size_t page_elems = (size_t)hp.block_count * hp.head_count_kv * kPage * hp.head_dim;
+    auto cleanup = [&](s2k_status code, const char *what) {
+        s2k_seq_free(s);
+        return fail(code, "s2k_seq_create: %s", what);
+    };
+    if (m->alloc(&s->k, page_elems * s->n_pages) || m->alloc(&s->v, page_elems * s->n_pages))
+        return cleanup(S2K_ERR_OOM, "KV pages");
+    std::vector<int> bt(s->n_pages);
+    for (int i = 0; i < s->n_pages; ++i) bt[i] = i;
+    if (m->alloc(&s->block_table, (size_t)s->n_pages) ||
+        cudaMemcpy(s->block_table, bt.data(), bt.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+        return cleanup(S2K_ERR_OOM, "block table");
+    if (m->alloc(&s->dev, 1) || cudaMemset(s->dev, 0, sizeof(SeqDev)) != cudaSuccess)
+        return cleanup(S2K_ERR_OOM, "sequence state");
+    if (cudaHostAlloc((void **)&s->hstat, sizeof(HostStatus), cudaHostAllocMapped) != cudaSuccess)
+        return cleanup(S2K_ERR_OOM, "host status");
+    memset((void *)s->hstat, 0, sizeof(HostStatus));
+    if (cudaHostGetDevicePointer((void **)&s->hstat_dev, (void *)s->hstat, 0) != cudaSuccess)
+        return cleanup(S2K_ERR_CUDA, "host status mapping");
+    *out = s;
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_seq_reset(s2k_seq *s) {
+    if (!s) return fail(S2K_ERR_ARG, "NULL sequence");
+    if (cuda_set(s->m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    CU(cudaMemsetAsync(&s->dev->state, 0, sizeof(SeqState), s->m->stream));
+    CU(cudaStreamSynchronize(s->m->stream));
+    s->n_past = 0;
+    return S2K_OK;
+}
+
+S2K_API void s2k_seq_free(s2k_seq *s) {
+    if (!s) return;
+    s2k_model *m = s->m;
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(m->stream);
+    if (s->frame_exec) cudaGraphExecDestroy(s->frame_exec);
+    m->release(s->k);
+    m->release(s->v);
+    m->release(s->block_table);
+    m->release(s->dev);
+    m->release(s->codes);
+    m->release(s->prompt);
+    if (s->hstat) cudaFreeHost((void *)s->hstat);
+    delete s;
+}
+
+S2K_API int32_t s2k_seq_n_past(const s2k_seq *s) { return s ? s->n_past : -1; }
+
+static s2k_status check_tokens_host(const s2k_model *m, const int32_t *flat, int32_t T) {
+    const s2k_hparams &hp = m->hp;
+    const int stride = hp.num_codebooks + 1;
+    for (int t = 0; t < T; ++t) {
+        const int tok = flat[t * stride];
+        if (tok < 0 || tok >= hp.vocab_size) return fail(S2K_ERR_ARG, "token %d at %d out of range", tok, t);
+        if (tok >= hp.semantic_begin_id && tok <= hp.semantic_end_id)
+            for (int cb = 0; cb < hp.num_codebooks; ++cb) {
+                const int c = flat[t * stride + 1 + cb];
+                if (c < 0 || c >= hp.codebook_size) return fail(S2K_ERR_ARG, "code %d (cb %d, token %d) out of range", c, cb, t);
+            }
+    }
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_eval(s2k_model *m, s2k_seq *s, const int32_t *flat, int32_t T, float *hidden_out,
+                            float *logits_out) {
+    if (!m || !s || !flat || T <= 0) return fail(S2K_ERR_ARG, "bad argument");
+    if (!m->finalized) return fail(S2K_ERR_STATE, "model not finalized");
+    if (s->m != m) return fail(S2K_ERR_ARG, "sequence belongs to another model");
+    if (s->n_past + T > s->max_seq_len)
+        return fail(S2K_ERR_KV_FULL, "KV cache overflow (%d + %d > %d)", s->n_past, T, s->max_seq_len);
+    s2k_status rc = check_tokens_host(m, flat, T);
+    if (rc) return rc;
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    rc = ensure_slow_work(m, T);
+    if (rc) return rc;
+    const int stride = m->hp.num_codebooks + 1;
+    if (m->tokens_cap < T * stride) {
+        m->release(m->tokens);
+        m->tokens = nullptr;
+        CU(m->alloc(&m->tokens, (size_t)T * stride));
+        m->tokens_cap = T * stride;
+    }
+    CU(cudaMemcpyAsync(m->tokens, flat, (size_t)T * stride * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    CU(enqueue_slow(m, s, T, m->tokens, nullptr));
+    if (hidden_out)
+        CU(cudaMemcpyAsync(hidden_out, m->hidden, (size_t)m->hp.embedding_length * 4, cudaMemcpyDeviceToHost, m->stream));
+    if (logits_out)
+        CU(cudaMemcpyAsync(logits_out, m->logits, (size_t)m->hp.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    rc = check_err_word(m);
+    if (rc) return rc;
+    s->n_past += T;
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_fast_decode(s2k_model *m, const float *hidden, const int32_t *prefix, int32_t n_prefix,
+                                   float *logits_out) {
+    if (!m || !hidden || !logits_out || n_prefix < 0 || (n_prefix > 0 && !prefix)) return fail(S2K_ERR_ARG, "bad argument");
+    if (!m->finalized) return fail(S2K_ERR_STATE, "model not finalized");
+    const s2k_hparams &hp = m->hp;
+    if (!hp.has_fast_decoder) return fail(S2K_ERR_STATE, "model has no fast decoder");
+    if (n_prefix >= hp.num_codebooks)
+        return fail(S2K_ERR_ARG, "prefix too long (%d >= %d)", n_prefix, hp.num_codebooks);
+    for (int i = 0; i < n_prefix; ++i)
+        if (prefix[i] < 0 || prefix[i] >= hp.codebook_size) return fail(S2K_ERR_ARG, "prefix code %d out of range", prefix[i]);
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    const int T = n_prefix + 1;
+    CU(cudaMemcpyAsync(m->fhidden, hidden, (size_t)hp.embedding_length * 4, cudaMemcpyHostToDevice, m->stream));
+    if (n_prefix > 0)
+        CU(cudaMemcpyAsync(m->fcodes, prefix, (size_t)n_prefix * 4, cudaMemcpyHostToDevice, m->stream));
+    CU(launch_embed_fast(&m->fast_embed, m->fhidden, m->fcodes, 0, T, m->fw.x, hp.fast_embedding_length, nullptr,
+                         m->d_err, m->stream));
+    CU(enqueue_fast(m, T, 0, nullptr));
+    CU(cudaMemcpyAsync(logits_out, m->flogits, (size_t)hp.codebook_size * 4, cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    return check_err_word(m);
+}
+
+S2K_API s2k_status s2k_sample(s2k_model *m, const float *logits, int32_t n, float temperature, float top_p,
+                              int32_t top_k, double u, int32_t *token_out) {
+    if (!m || !logits || !token_out || n <= 0 || n > 8192) return fail(S2K_ERR_ARG, "bad argument (n <= 8192)");
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    if (m->samp_cap < n) {
+        m->release(m->samp_logits);
+        m->samp_logits = nullptr;
+        CU(m->alloc(&m->samp_logits, (size_t)n));
+        m->samp_cap = n;
+    }
+    if (!m->samp_out) CU(m->alloc(&m->samp_out, 1));
+    CU(cudaMemcpyAsync(m->samp_logits, logits, (size_t)n * 4, cudaMemcpyHostToDevice, m->stream));
+    CU(launch_sample_one(m->samp_logits, n, temperature, top_p, top_k, u, m->samp_out, m->d_err, m->stream));
+    CU(cudaMemcpyAsync(token_out, m->samp_out, 4, cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    return check_err_word(m);
+}
+
+// Frame graph: captured once per sequence; it reads everything that changes
+// per frame or per call (positions, tokens, sampling parameters, output
+// pointer) from the sequence's device state.
+static s2k_status ensure_frame_graph(s2k_model *m, s2k_seq *s) {
+    if (s->frame_exec && s->frame_gen == m->ws_gen) return S2K_OK;
+    if (s->frame_exec) {
+        cudaGraphExecDestroy(s->frame_exec);
+        s->frame_exec = nullptr;
+    }
+    cudaGraph_t g = nullptr;
+    const unsigned long long before = g_launches.load();
+    CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = enqueue_frame(m, s);
+    cudaError_t e2 = cudaStreamEndCapture(m->stream, &g);
+    g_launches.store(before);
+    if (e != cudaSuccess || e2 != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return fail(S2K_ERR_CUDA, "frame capture failed: %s / %s", cudaGetErrorString(e), cudaGetErrorString(e2));
+    }
+    size_t n = 0;
+    cudaGraphGetNodes(g, nullptr, &n);
+    s->frame_nodes = n;
+    e = cudaGraphInstantiate(&s->frame_exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+        s->frame_exec = nullptr;
+        return fail(S2K_ERR_CUDA, "frame graph instantiate: %s", cudaGetErrorString(e));
+    }
+    s->frame_gen = m->ws_gen;
+    return S2K_OK;
+}
+
+static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_prompt_tm, int32_t cols,
+                                const s2k_gen_params *gp, int32_t *d_codes, int32_t codes_ld, int32_t *n_frames_out) {
+    const s2k_hparams &hp = m->hp;
+    if (cols <= 0 || gp->max_new_tokens < 0) return fail(S2K_ERR_ARG, "bad prompt length / max_new_tokens");
+    if (cols + gp->max_new_tokens > s->max_seq_len)
+        return fail(S2K_ERR_KV_FULL, "sequence holds %d positions, need %d", s->max_seq_len, cols + gp->max_new_tokens);
+    if (!hp.has_fast_decoder && hp.num_codebooks > 1) return fail(S2K_ERR_STATE, "model has no fast decoder");
+    s2k_status rc = ensure_slow_work(m, cols);
+    if (rc) return rc;
+    SampleCfg c;
+    memset(&c, 0, sizeof(c));
+    c.temperature = gp->temperature;
+    c.top_p = gp->top_p;
+    c.top_k = gp->top_k;
+    c.min_tokens_before_end = gp->min_tokens_before_end;
+    c.im_end = gp->im_end_id;
+    c.max_new_tokens = gp->max_new_tokens;
+    c.seed = gp->seed;
+    c.seq_id = gp->seq_id;
+    c.sem_begin = hp.semantic_begin_id;
+    c.sem_end = hp.semantic_end_id;
+    c.cb_size = hp.codebook_size;
+    c.ncb = std::max(hp.num_codebooks, 1);
+    c.vocab = hp.vocab_size;
+    c.codes_out = d_codes;
+    c.codes_ld = codes_ld;
+    // the Pipeline clears and re-inits the KV cache per synthesis (src/s2_pipeline.cpp:838-851)
+    CU(cudaMemsetAsync(&s->dev->state, 0, sizeof(SeqState), m->stream));
+    CU(cudaMemcpyAsync(&s->dev->cfg, &c, sizeof(SampleCfg), cudaMemcpyHostToDevice, m->stream));
+    HostStatus *hs = s->hstat_dev;
+    CU(cudaMemcpyAsync(&s->dev->host, &hs, sizeof(HostStatus *), cudaMemcpyHostToDevice, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    s->hstat->n_frames = 0;
+    s->hstat->done = 0;
+    s->n_past = 0;
+    // prefill (generate(): prefill_fast of the whole prompt, src/s2_generate.cpp:51)
+    CU(enqueue_slow(m, s, cols, d_prompt_tm, nullptr));
+    CU(launch_sample_main(m->logits, s->dev, m->d_err, m->stream));
+    rc = ensure_frame_graph(m, s);
+    if (rc) return rc;
+    constexpr int kLookahead = 4;
+    cudaEvent_t ev[kLookahead];
+    for (int i = 0; i < kLookahead; ++i) CU(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
+    s2k_status out_rc = S2K_OK;
+    for (int f = 0; f < gp->max_new_tokens; ++f) {
+        if (f >= kLookahead) {
+            cudaError_t e = cudaEventSynchronize(ev[f % kLookahead]);
+            if (e != cudaSuccess) {
+                out_rc = fail(S2K_ERR_CUDA, "frame %d: %s", f, cudaGetErrorString(e));
+                break;
+            }
+        }
+        if (s->hstat->done) break;
+        cudaError_t e = cudaGraphLaunch(s->frame_exec, m->stream);
+        if (e == cudaSuccess) e = cudaEventRecord(ev[f % kLookahead], m->stream);
+        if (e != cudaSuccess) {
+            out_rc = fail(S2K_ERR_CUDA, "frame %d launch: %s", f, cudaGetErrorString(e));
+            break;
+        }
+        count_launch((int)s->frame_nodes);
+    }
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    for (int i = 0; i < kLookahead; ++i) cudaEventDestroy(ev[i]);
+    if (out_rc) return out_rc;
+    if (e != cudaSuccess) return fail(S2K_ERR_CUDA, "generate: %s", cudaGetErrorString(e));
+    rc = check_err_word(m);
+    if (rc) return rc;
+    *n_frames_out = s->hstat->n_frames;
+    s->n_past = cols + *n_frames_out;
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_generate_device(s2k_model *m, s2k_seq *s, const int32_t *d_prompt_tm, int32_t cols,
+                                       const s2k_gen_params *gp, int32_t *d_codes_out, int32_t *n_frames_out) {
+    if (!m || !s || !d_prompt_tm || !gp || !d_codes_out || !n_frames_out) return fail(S2K_ERR_ARG, "NULL argument");
+    if (!m->finalized) return fail(S2K_ERR_STATE, "model not finalized");
+    if (s->m != m) return fail(S2K_ERR_ARG, "sequence belongs to another model");
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    return generate_core(m, s, d_prompt_tm, cols, gp, d_codes_out, std::max(gp->max_new_tokens, 1), n_frames_out);
+}
+
+S2K_API s2k_status s2k_generate(s2k_model *m, s2k_seq *s, const int32_t *prompt, int32_t cols,
+                                const s2k_gen_params *gp, int32_t *codes_out, int32_t *n_frames_out,
+                                s2k_frame_callback on_frame, void *user) {
+    if (!m || !s || !prompt || !gp || !codes_out || !n_frames_out || cols <= 0) return fail(S2K_ERR_ARG, "bad argument");
+    if (!m->finalized) return fail(S2K_ERR_STATE, "model not finalized");
+    if (s->m != m) return fail(S2K_ERR_ARG, "sequence belongs to another model");
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    const s2k_hparams &hp = m->hp;
+    const int rows = hp.num_codebooks + 1;
+    const int ncb = std::max(hp.num_codebooks, 1);
+    // PromptTensor [rows][cols] -> token-major, as generate() does (src/s2_generate.cpp:37-44)
+    std::vector<int32_t> tm((size_t)rows * cols);
+    for (int r = 0; r < rows; ++r)
+        for (int c = 0; c < cols; ++c) tm[(size_t)c * rows + r] = prompt[(size_t)r * cols + c];
+    s2k_status rc = check_tokens_host(m, tm.data(), cols);
+    if (rc) return rc;
+    if (s->prompt_cap < rows * cols) {
+        m->release(s->prompt);
+        s->prompt = nullptr;
+        CU(m->alloc(&s->prompt, (size_t)rows * cols));
+        s->prompt_cap = rows * cols;
+    }
+    const int ld = std::max(gp->max_new_tokens, 1);
+    if (s->codes_cap < ld) {
+        m->release(s->codes);
+        s->codes = nullptr;
+        CU(m->alloc(&s->codes, (size_t)ncb * ld));
+        s->codes_cap = ld;
+    }
+    CU(cudaMemcpyAsync(s->prompt, tm.data(), tm.size() * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
+    int32_t nf = 0;
+    rc = generate_core(m, s, s->prompt, cols, gp, s->codes, ld, &nf);
+    if (rc) return rc;
+    std::vector<int32_t> full((size_t)ncb * ld);
+    CU(cudaMemcpy(full.data(), s->codes, full.size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
+    if (on_frame) {
+        std::vector<int32_t> fr(ncb);
+        for (int f = 0; f < nf; ++f) {
+            for (int cb = 0; cb < ncb; ++cb) fr[cb] = full[(size_t)cb * ld + f];
+            if (!on_frame(fr.data(), f, f + 1, ncb, user)) {
+                nf = f + 1;
+                break;
+            }
+        }
+    }
+    for (int cb = 0; cb < ncb; ++cb)
+        for (int f = 0; f < nf; ++f) codes_out[(size_t)cb * nf + f] = full[(size_t)cb * ld + f];
+    *n_frames_out = nf;
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_profile_gemv(s2k_model *m, int32_t reps, double *bytes_per_pass, double *ms_per_pass,
+                                    int32_t *launches_per_pass) {
+    if (!m || reps <= 0 || !bytes_per_pass || !ms_per_pass || !launches_per_pass) return fail(S2K_ERR_ARG, "bad argument");
+    if (!m->finalized) return fail(S2K_ERR_STATE, "model not finalized");
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    const s2k_hparams &hp = m->hp;
+    Work &w = m->sw;
+    double bytes = 0;
+    int launches = 0;
+    auto pass = [&](bool count) -> cudaError_t {
+        cudaError_t e;
+        for (const Layer &L : m->layers) {
+            GemvArgs g;
+            g.M = 1;
+            g.err = m->d_err;
+            g.eps = hp.rms_norm_eps;
+            g.w = &L.wqkv; g.x = w.x; g.ldx = w.dim; g.in_mode = IN_RMSNORM; g.norm_w = L.attn_norm;
+            g.y = w.qkv; g.ldy = w.qs + 2 * w.kvs;
+            if ((e = launch_gemv(g, m->num_sms, m->stream))) return e;
+            GemvArgs o = g;
+            o.w = &L.wo; o.x = w.attn; o.ldx = w.qs; o.in_mode = IN_PLAIN; o.norm_w = nullptr; o.y = w.h; o.ldy = w.dim;
+            o.res = w.x; o.ldres = w.dim;
+            if ((e = launch_gemv(o, m->num_sms, m->stream))) return e;
+            GemvArgs f1 = g;
+            f1.w = &L.w13; f1.x = w.h; f1.ldx = w.dim; f1.norm_w = L.ffn_norm; f1.y = w.ff_buf; f1.ldy = 2 * w.ff;
+            if ((e = launch_gemv(f1, m->num_sms, m->stream))) return e;
+            GemvArgs f2 = g;
+            f2.w = &L.w2; f2.x = w.ff_buf; f2.ldx = 2 * w.ff; f2.in_mode = IN_SWIGLU; f2.norm_w = nullptr; f2.y = w.x;
+            f2.ldy = w.dim; f2.res = w.h; f2.ldres = w.dim;
+            if ((e = launch_gemv(f2, m->num_sms, m->stream))) return e;
+            if (count) {
+                bytes += (double)(L.wqkv.bytes() + L.wo.bytes() + L.w13.bytes() + L.w2.bytes());
+                launches += 4;
+            }
+        }
+        GemvArgs hd;
+        hd.w = &m->embed; hd.x = w.x; hd.ldx = w.dim; hd.M = 1; hd.in_mode = IN_RMSNORM; hd.norm_w = m->norm;
+        hd.eps = hp.rms_norm_eps; hd.y = m->logits; hd.ldy = hp.vocab_size; hd.err = m->d_err;
+        if ((e = launch_gemv(hd, m->num_sms, m->stream))) return e;
+        if (count) {
+            bytes += (double)m->embed.bytes();
+            launches += 1;
+        }
+        return cudaSuccess;
+    };
+    // deterministic finite activations
+    CU(cudaMemsetAsync(w.x, 0, (size_t)w.dim * sizeof(float), m->stream));
+    CU(cudaMemsetAsync(w.attn, 0, (size_t)w.qs * sizeof(float), m->stream));
+    CU(pass(true));  // warm-up
+    cudaEvent_t e0, e1;
+    CU(cudaEventCreate(&e0));
+    CU(cudaEventCreate(&e1));
+    CU(cudaEventRecord(e0, m->stream));
+    for (int r = 0; r < reps; ++r) CU(pass(false));
+    CU(cudaEventRecord(e1, m->stream));
+    CU(cudaEventSynchronize(e1));
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *bytes_per_pass = bytes;
+    *ms_per_pass = ms / reps;
+    *launches_per_pass = launches;
+    return check_err_word(m);
+}
+
+}  // extern "C"

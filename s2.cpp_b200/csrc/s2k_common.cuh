@@ -1,0 +1,134 @@
+// s2k_common.cuh -- shared device helpers for the sm_100a decode kernels:
+// mbarrier / bulk-async-copy wrappers, programmatic dependent launch,
+// bounded waits and the error-flag convention.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace s2k {
+
+// Error bits a kernel ORs into the model's device error word.
+enum : int {
+    ERR_WAIT_FULL = 1,    // consumer gave up waiting for a weight stage
+    ERR_WAIT_EMPTY = 2,   // producer gave up waiting for a free stage
+    ERR_BAD_TOKEN = 4,    // token / code id out of range
+    ERR_BAD_POS = 8,      // position beyond the sequence's pages
+    ERR_SAMPLER = 16,     // sampler found no finite candidate
+};
+
+// ~2 s at 1.9 GHz: long enough never to fire on a healthy GPU, short enough
+// that a lost copy turns into an error status instead of a hang.
+constexpr long long kWaitLimitCycles = 4000000000LL;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase.  Returns false (and sets `code` in *err)
+// when the limit is reached.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    if (mbar_test(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_test(bar, parity)) {
+        if (clock64() - t0 > kWaitLimitCycles) {
+            if (err) atomicOr(err, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+// 1-D bulk async copy global -> shared (TMA engine, no tensor map), completing
+// `bytes` of transaction count on `bar`.  dst/src 16-byte aligned, bytes % 16 == 0.
+// Weights are read once per pass: hint L2 to evict them first.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// Programmatic dependent launch (PDL): let the next kernel in the stream start
+// its weight prefetch now; wait for the previous kernel's results later.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Named barrier among the first `nthreads` threads (ids 1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// ggml-cpu x86 quantize_row_q8_0 on one 32-value block held one value per
+// lane: d = amax/127 (stored fp16), q = round-half-even(x * 127/amax).
+// Returns q for this lane; *d_out (all lanes) gets the fp16-rounded scale.
+__device__ __forceinline__ int quant_q8_0_lane(float v, float *d_out) {
+    const float amax = warp_max(fabsf(v));
+    const float d = __fdiv_rn(amax, 127.f);
+    const float id = amax != 0.0f ? __fdiv_rn(127.f, amax) : 0.0f;
+    *d_out = __half2float(__float2half_rn(d));
+    return __float2int_rn(__fmul_rn(v, id));
+}
+
+// x / (1 + exp(-x)), ggml_silu_f32
+__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+
+}  // namespace s2k

@@ -1,0 +1,46 @@
+// s2k_device.h -- per-sequence device state shared by the frame-loop kernels.
+#pragma once
+
+namespace s2k {
+
+// Mapped pinned memory the host polls while frames run.
+struct HostStatus {
+    volatile int n_frames;
+    volatile int done;
+    int pad[2];
+};
+
+// Generation parameters as the kernels read them (device copy, so a captured
+// frame graph does not depend on them).
+struct SampleCfg {
+    float temperature, top_p;
+    int top_k;
+    int min_tokens_before_end;
+    int im_end;
+    int max_new_tokens;
+    unsigned long long seed;
+    unsigned int seq_id;
+    int sem_begin, sem_end, cb_size, ncb, vocab;
+    int *codes_out;  // [ncb][codes_ld] cb-major
+    int codes_ld;
+};
+
+struct SeqState {
+    int n_past;      // positions in the KV cache
+    int n_frames;    // frames completed
+    int done;        // generation finished
+    int main_token;  // main token of the frame being built
+    int codes[16];   // codes of the frame being built
+    int step_in[17]; // [main, cb0..] input of the next Slow step
+    int ras[10];     // repetition-aware-sampling window
+    int n_ras;
+    int pad[2];
+};
+
+struct SeqDev {
+    SeqState state;
+    SampleCfg cfg;
+    HostStatus *host;  // device alias of mapped pinned memory (may be null)
+};
+
+}  // namespace s2k

@@ -1,0 +1,142 @@
+// s2k_kernels.h -- host-side launchers of the decode kernels (internal).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace s2k {
+
+// ---------------------------------------------------------------------------
+// Weight matrix in device layout.
+//   Q8_0 : q = int8 [rows][cols], d = fp16 [rows][cols/32]  (split planes so a
+//          row of quants is one contiguous, 16-byte aligned run)
+// ---------------------------------------------------------------------------
+struct DevMat {
+    int type = -1;  // ggml type id
+    int rows = 0, cols = 0;
+    int8_t *q = nullptr;
+    __half *d = nullptr;
+    size_t bytes() const;
+};
+
+enum GemvIn : int {
+    IN_PLAIN = 0,    // activation = x
+    IN_RMSNORM = 1,  // activation = (x * rsqrt(mean(x^2)+eps)) * norm_w
+    IN_SWIGLU = 2,   // activation[i] = silu(x[2i]) * x[2i+1]   (x = interleaved gate/up)
+};
+
+struct GemvArgs {
+    const DevMat *w = nullptr;
+    const float *x = nullptr;  // [M][ldx]
+    int ldx = 0;
+    int M = 1;
+    int in_mode = IN_PLAIN;
+    const float *norm_w = nullptr;
+    float eps = 0.f;
+    float *y = nullptr;  // [M][ldy]
+    int ldy = 0;
+    const float *res = nullptr;  // optional residual [M][ldres], y = res + W.x
+    int ldres = 0;
+    float *act_out = nullptr;  // optional: CTA 0 stores the (normed) f32 activation [M][K]
+    const int *done = nullptr;  // optional early-exit flag (frame loop)
+    int *err = nullptr;
+};
+
+// Launch with programmatic-dependent-launch attribute on `st`.
+cudaError_t launch_gemv(const GemvArgs &a, int num_sms, cudaStream_t st);
+// smem bytes a gemv launch for (K, M) needs (to set the function attribute once).
+cudaError_t gemv_setup();
+
+// Q8_0 GGUF blocks (34 B) in device staging -> split planes, dst rows
+// dst_row = row*row_stride + row_offset (row_stride 2 interleaves w1/w3).
+cudaError_t launch_relayout_q8_0(const uint8_t *src, int rows, int cols, DevMat *dst, int row_stride,
+                                 int row_offset, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Attention
+// ---------------------------------------------------------------------------
+struct KvPaged {
+    __half *k = nullptr, *v = nullptr;  // [page][layer][kv_head][16][head_dim]
+    const int *block_table = nullptr;   // logical page -> physical page
+    int n_layers = 0, n_kv_heads = 0, head_dim = 0, n_pages = 0;
+};
+constexpr int kPage = 16;
+
+struct QkPrepArgs {
+    float *qkv = nullptr;  // [T][ldqkv] raw projections, q rotated in place
+    int ldqkv = 0;
+    int T = 1, H = 0, Hkv = 0, hd = 128;
+    const float *q_norm = nullptr, *k_norm = nullptr;  // null: no qk-norm
+    float eps = 0.f;
+    float theta_scale = 1.f;
+    const int *pos_base = nullptr;  // device: position of token 0 (n_past); null = 0
+    int pos_add = 0;                // added to *pos_base
+    float *kcur = nullptr, *vcur = nullptr;  // f32 [*][Hkv][hd] at index cur_base + t
+    int cur_base = 0;
+    KvPaged kv;  // if kv.k: also store f16 K/V of (layer) at the token's position
+    int layer = 0;
+    const int *done = nullptr;
+    int *err = nullptr;
+};
+cudaError_t launch_qk_prep(const QkPrepArgs &a, cudaStream_t st);
+
+struct AttnArgs {
+    const float *q = nullptr;  // [T][ldq] rotated queries (head h at h*hd)
+    int ldq = 0;
+    int T = 1, H = 0, Hkv = 0, hd = 128;
+    float scale = 1.f;
+    const int *n_cached = nullptr;  // device: # positions held in the paged cache (null = 0)
+    KvPaged kv;
+    int layer = 0;
+    const float *kcur = nullptr, *vcur = nullptr;  // f32 [*][Hkv][hd], position n_cached + j at index j
+    int cur_base = 0;  // token t attends to cur indices [0, cur_base + t]
+    int n_splits = 1;
+    float *part = nullptr;  // scratch [T][H][n_splits][hd + 2]
+    int *counters = nullptr;  // scratch [T][Hkv], zero between launches
+    float *out = nullptr;  // [T][H*hd]
+    const int *done = nullptr;
+    int *err = nullptr;
+};
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Embeddings / sampling / frame bookkeeping
+// ---------------------------------------------------------------------------
+struct EmbedArgs {
+    const DevMat *tok_emb = nullptr;  // embeddings (Slow) or fast_embeddings (Fast)
+    const DevMat *cb_emb = nullptr;   // codebook_embeddings (Slow only)
+    const int *tokens = nullptr;      // Slow: [T][ncb+1]; Fast: codes
+    int T = 1;
+    int ncb = 0, cb_size = 0, sem_begin = 0, sem_end = -1;
+    int scale_cb = 0;
+    float sem_scale = 1.f;
+    float *x = nullptr;  // [T][dim]
+    const int *done = nullptr;
+    int *err = nullptr;
+};
+cudaError_t launch_embed_slow(const EmbedArgs &a, cudaStream_t st);
+// Fast-AR input rows: row r (r < n_rows) of x = (r == 0 && hidden) ? hidden : fast_emb[codes[code0 + r - (hidden?1:0)]]
+cudaError_t launch_embed_fast(const DevMat *fast_emb, const float *hidden, const int *codes, int code0,
+                              int n_rows, float *x, int dim, const int *done, int *err, cudaStream_t st);
+
+// Frame-loop launchers (state structs in s2k_device.h).
+struct SeqDev;
+cudaError_t sampler_setup();
+// After a Slow step (or the prefill): sample the main token of the next frame
+// with the semantic mask, stop test, RAS, window push, codes[0].
+cudaError_t launch_sample_main(const float *logits, SeqDev *sd, int *err, cudaStream_t st);
+// After the Fast-AR pass for codebook cb: sample codes[cb].
+cudaError_t launch_sample_fast(const float *logits, SeqDev *sd, int cb, int *err, cudaStream_t st);
+// End of the Fast-AR loop: store the frame's codes, n_frames++, step input.
+cudaError_t launch_frame_commit(SeqDev *sd, cudaStream_t st);
+// After the Slow step kernels: n_past += T.
+cudaError_t launch_advance(SeqDev *sd, int T, const int *done, cudaStream_t st);
+// Standalone sampler (s2k_sample)
+cudaError_t launch_sample_one(const float *logits, int n, float temperature, float top_p, int top_k,
+                              double u, int *out, int *err, cudaStream_t st);
+
+// launch accounting
+void count_launch(int n = 1);
+
+}  // namespace s2k

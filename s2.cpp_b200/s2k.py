@@ -1,0 +1,298 @@
+"""Python binding of the s2k C ABI (include/s2k.h) and a mirror of the
+reference's model interface for the dual-AR decode path.
+
+`SlowARModel` keeps s2::SlowARModel's method names and argument meaning
+(include/s2_model.h:92-130): init_kv_cache, clear_kv_cache, reset,
+prefill_fast, prefill, step, fast_decode, hparams.  `generate` mirrors
+s2::generate (include/s2_generate.h:40-45).  Results come back as numpy
+arrays; failures raise S2KError with the library's message (the reference
+returns false and prints to stderr).
+
+The library is the in-tree libs2k.so built by build.py; importing this module
+on a machine without it raises, there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Callable, Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libs2k.so")
+
+S2K_OK = 0
+STATUS = {-1: "ERR_ARG", -2: "ERR_OOM", -3: "ERR_CUDA", -4: "ERR_KV_FULL", -5: "ERR_STATE",
+          -6: "ERR_TIMEOUT", -7: "ERR_UNSUPPORTED", -8: "ERR_NO_DEVICE"}
+
+# symbols declared in include/s2k.h (checked by the CPU tests)
+EXPORTED = [
+    "s2k_abi_version", "s2k_last_error", "s2k_device_count", "s2k_model_create", "s2k_model_upload_tensor",
+    "s2k_model_finalize", "s2k_model_free", "s2k_model_get_hparams", "s2k_model_weight_bytes",
+    "s2k_model_stream", "s2k_seq_create", "s2k_seq_reset", "s2k_seq_free", "s2k_seq_n_past", "s2k_eval",
+    "s2k_fast_decode", "s2k_generate", "s2k_generate_device", "s2k_sample", "s2k_launch_count",
+    "s2k_profile_gemv",
+]
+
+
+class S2KError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+class _HParams(ctypes.Structure):
+    _fields_ = [
+        ("context_length", ctypes.c_int32), ("vocab_size", ctypes.c_int32), ("embedding_length", ctypes.c_int32),
+        ("feed_forward_length", ctypes.c_int32), ("block_count", ctypes.c_int32), ("head_count", ctypes.c_int32),
+        ("head_count_kv", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("codebook_size", ctypes.c_int32),
+        ("num_codebooks", ctypes.c_int32), ("semantic_begin_id", ctypes.c_int32),
+        ("semantic_end_id", ctypes.c_int32), ("rope_freq_base", ctypes.c_float), ("rms_norm_eps", ctypes.c_float),
+        ("tie_word_embeddings", ctypes.c_int32), ("attention_qk_norm", ctypes.c_int32),
+        ("scale_codebook_embeddings", ctypes.c_int32), ("fast_context_length", ctypes.c_int32),
+        ("fast_embedding_length", ctypes.c_int32), ("fast_feed_forward_length", ctypes.c_int32),
+        ("fast_block_count", ctypes.c_int32), ("fast_head_count", ctypes.c_int32),
+        ("fast_head_count_kv", ctypes.c_int32), ("fast_head_dim", ctypes.c_int32),
+        ("fast_rope_freq_base", ctypes.c_float), ("fast_rms_norm_eps", ctypes.c_float),
+        ("fast_attention_qk_norm", ctypes.c_int32), ("fast_has_project_in", ctypes.c_int32),
+        ("has_fast_decoder", ctypes.c_int32),
+    ]
+
+
+class _GenParams(ctypes.Structure):
+    _fields_ = [("max_new_tokens", ctypes.c_int32), ("temperature", ctypes.c_float), ("top_p", ctypes.c_float),
+                ("top_k", ctypes.c_int32), ("min_tokens_before_end", ctypes.c_int32),
+                ("im_end_id", ctypes.c_int32), ("seed", ctypes.c_uint64), ("seq_id", ctypes.c_uint32)]
+
+
+FRAME_CB = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32,
+                            ctypes.c_int32, ctypes.c_void_p)
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libs2k.so (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: run `python s2.cpp_b200/build.py` (needs nvcc)")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i32, i64p = ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_int64)
+    sig = {
+        "s2k_abi_version": ([], i32),
+        "s2k_last_error": ([], ctypes.c_char_p),
+        "s2k_device_count": ([ctypes.POINTER(i32)], i32),
+        "s2k_model_create": ([i32, ctypes.POINTER(_HParams), ctypes.POINTER(vp)], i32),
+        "s2k_model_upload_tensor": ([vp, ctypes.c_char_p, i32, i64p, vp, ctypes.c_size_t], i32),
+        "s2k_model_finalize": ([vp], i32),
+        "s2k_model_free": ([vp], None),
+        "s2k_model_get_hparams": ([vp, ctypes.POINTER(_HParams)], i32),
+        "s2k_model_weight_bytes": ([vp], ctypes.c_size_t),
+        "s2k_model_stream": ([vp], vp),
+        "s2k_seq_create": ([vp, i32, ctypes.POINTER(vp)], i32),
+        "s2k_seq_reset": ([vp], i32),
+        "s2k_seq_free": ([vp], None),
+        "s2k_seq_n_past": ([vp], i32),
+        "s2k_eval": ([vp, vp, vp, i32, vp, vp], i32),
+        "s2k_fast_decode": ([vp, vp, vp, i32, vp], i32),
+        "s2k_generate": ([vp, vp, vp, i32, ctypes.POINTER(_GenParams), vp, ctypes.POINTER(i32), FRAME_CB, vp], i32),
+        "s2k_generate_device": ([vp, vp, vp, i32, ctypes.POINTER(_GenParams), vp, ctypes.POINTER(i32)], i32),
+        "s2k_sample": ([vp, vp, i32, ctypes.c_float, ctypes.c_float, i32, ctypes.c_double, ctypes.POINTER(i32)], i32),
+        "s2k_launch_count": ([i32], ctypes.c_uint64),
+        "s2k_profile_gemv": ([vp, i32, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                              ctypes.POINTER(i32)], i32),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    _lib = L
+    return L
+
+
+def _check(rc: int) -> None:
+    if rc != S2K_OK:
+        raise S2KError(rc, lib().s2k_last_error().decode(errors="replace"))
+
+
+def device_count() -> int:
+    n = ctypes.c_int32(0)
+    rc = lib().s2k_device_count(ctypes.byref(n))
+    return n.value if rc == S2K_OK else 0
+
+
+def _hp_struct(hp) -> _HParams:
+    s = _HParams()
+    for name, _ in _HParams._fields_:
+        setattr(s, name, getattr(hp, name))
+    return s
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class SlowARModel:
+    """The dual-AR model on one CUDA device, mirroring s2::SlowARModel."""
+
+    def __init__(self, hparams, device: int = 0):
+        self._m = ctypes.c_void_p()
+        self._seq = ctypes.c_void_p()
+        self._hp = hparams
+        _check(lib().s2k_model_create(device, ctypes.byref(_hp_struct(hparams)), ctypes.byref(self._m)))
+        self.device = device
+
+    # --- loading (SlowARModel::load_shared + read_tensor_data) ---
+    def upload_tensor(self, name: str, ggml_type: int, ne, data: np.ndarray) -> None:
+        ne4 = (ctypes.c_int64 * 4)(*[int(x) for x in (list(ne) + [1, 1, 1, 1])[:4]])
+        data = np.ascontiguousarray(data)
+        _check(lib().s2k_model_upload_tensor(self._m, name.encode(), ggml_type, ne4, _ptr(data), data.nbytes))
+
+    def finalize(self) -> None:
+        _check(lib().s2k_model_finalize(self._m))
+
+    def load_tensors(self, tensors) -> None:
+        """tensors: iterable of (spec, bytes) as produced by synthetic.make_model."""
+        for spec, buf in tensors:
+            self.upload_tensor(spec.name, spec.type, spec.ne, buf)
+        self.finalize()
+
+    def hparams(self):
+        return self._hp
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._m
+
+    @property
+    def seq_handle(self) -> ctypes.c_void_p:
+        return self._seq
+
+    def weight_bytes(self) -> int:
+        return int(lib().s2k_model_weight_bytes(self._m))
+
+    def stream(self) -> int:
+        return int(lib().s2k_model_stream(self._m) or 0)
+
+    # --- KV cache (init_kv_cache / reset / clear_kv_cache) ---
+    def init_kv_cache(self, max_seq_len: int) -> None:
+        self.clear_kv_cache()
+        _check(lib().s2k_seq_create(self._m, max_seq_len, ctypes.byref(self._seq)))
+        self._max_seq_len = max_seq_len
+
+    def reset(self) -> None:
+        _check(lib().s2k_seq_reset(self._seq))
+
+    def clear_kv_cache(self) -> None:
+        if self._seq:
+            lib().s2k_seq_free(self._seq)
+            self._seq = ctypes.c_void_p()
+        self._max_seq_len = 0
+
+    @property
+    def n_past(self) -> int:
+        return int(lib().s2k_seq_n_past(self._seq)) if self._seq else 0
+
+    # --- eval_cached / prefill_fast / prefill / step ---
+    def _eval(self, flat_tokens: np.ndarray, n_tokens: int):
+        flat = np.ascontiguousarray(flat_tokens, dtype=np.int32)
+        if flat.size != n_tokens * (self._hp.num_codebooks + 1):
+            raise S2KError(-1, f"expected {n_tokens * (self._hp.num_codebooks + 1)} ints, got {flat.size}")
+        hidden = np.empty(self._hp.embedding_length, dtype=np.float32)
+        logits = np.empty(self._hp.vocab_size, dtype=np.float32)
+        _check(lib().s2k_eval(self._m, self._seq, _ptr(flat), n_tokens, _ptr(hidden), _ptr(logits)))
+        return hidden, logits
+
+    def prefill_fast(self, flat_tokens: np.ndarray, n_tokens: int):
+        return self._eval(flat_tokens, n_tokens)
+
+    def prefill(self, flat_tokens: np.ndarray, n_tokens: int):
+        return self._eval(flat_tokens, n_tokens)
+
+    def step(self, flat_tokens: np.ndarray):
+        return self._eval(flat_tokens, 1)
+
+    def fast_decode(self, hidden: np.ndarray, prefix_codes) -> np.ndarray:
+        h = np.ascontiguousarray(hidden, dtype=np.float32)
+        p = np.ascontiguousarray(np.asarray(prefix_codes, dtype=np.int32))
+        out = np.empty(self._hp.codebook_size, dtype=np.float32)
+        _check(lib().s2k_fast_decode(self._m, _ptr(h), _ptr(p) if p.size else None, int(p.size), _ptr(out)))
+        return out
+
+    def sample(self, logits: np.ndarray, temperature: float, top_p: float, top_k: int, u: float = 0.0) -> int:
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        tok = ctypes.c_int32(0)
+        _check(lib().s2k_sample(self._m, _ptr(x), int(x.size), temperature, top_p, top_k, u, ctypes.byref(tok)))
+        return tok.value
+
+    # --- generate ---
+    def generate(self, prompt: np.ndarray, max_new_tokens: int = 1024, temperature: float = 0.8,
+                 top_p: float = 0.8, top_k: int = 30, min_tokens_before_end: int = 0, im_end_id: int = -1,
+                 seed: int = 0, seq_id: int = 0,
+                 on_frame: Optional[Callable[[np.ndarray, int, int], bool]] = None) -> np.ndarray:
+        """prompt: PromptTensor grid [num_codebooks+1][cols].  Returns codes
+        [num_codebooks][n_frames] (GenerateResult.codes)."""
+        hp = self._hp
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        rows, cols = p.shape
+        if rows != hp.num_codebooks + 1:
+            raise S2KError(-1, f"prompt must have {hp.num_codebooks + 1} rows")
+        need = cols + max_new_tokens
+        if not self._seq or self._max_seq() < need:
+            self.init_kv_cache(need)
+        ncb = max(hp.num_codebooks, 1)
+        codes = np.zeros(ncb * max(max_new_tokens, 1), dtype=np.int32)
+        nf = ctypes.c_int32(0)
+        gp = _GenParams(max_new_tokens, temperature, top_p, top_k, min_tokens_before_end, im_end_id, seed, seq_id)
+        if on_frame is not None:
+            def _cb(codes_ptr, idx, total, ncb_, user):
+                arr = np.ctypeslib.as_array(codes_ptr, shape=(ncb_,)).copy()
+                return 1 if on_frame(arr, idx, total) else 0
+            cb = FRAME_CB(_cb)
+        else:
+            cb = FRAME_CB()
+        _check(lib().s2k_generate(self._m, self._seq, _ptr(p), cols, ctypes.byref(gp), _ptr(codes),
+                                  ctypes.byref(nf), cb, None))
+        n = nf.value
+        return codes[: ncb * n].reshape(ncb, n)
+
+    def _max_seq(self) -> int:
+        return getattr(self, "_max_seq_len", 0)
+
+    def profile_gemv(self, reps: int = 5):
+        """(bytes per pass, ms per pass, launches per pass) of the Slow-step GEMVs."""
+        b, ms, n = ctypes.c_double(0), ctypes.c_double(0), ctypes.c_int32(0)
+        _check(lib().s2k_profile_gemv(self._m, reps, ctypes.byref(b), ctypes.byref(ms), ctypes.byref(n)))
+        return b.value, ms.value, n.value
+
+    def generate_device(self, d_prompt_tm: int, cols: int, d_codes: int, max_new_tokens: int,
+                        temperature: float = 0.0, top_p: float = 0.8, top_k: int = 30,
+                        min_tokens_before_end: int = 0, im_end_id: int = -1, seed: int = 0, seq_id: int = 0) -> int:
+        """s2k_generate_device on device pointers; returns the frame count."""
+        need = cols + max_new_tokens
+        if not self._seq or self._max_seq() < need:
+            self.init_kv_cache(need)
+        nf = ctypes.c_int32(0)
+        gp = _GenParams(max_new_tokens, temperature, top_p, top_k, min_tokens_before_end, im_end_id, seed, seq_id)
+        _check(lib().s2k_generate_device(self._m, self._seq, ctypes.c_void_p(d_prompt_tm), cols, ctypes.byref(gp),
+                                         ctypes.c_void_p(d_codes), ctypes.byref(nf)))
+        return nf.value
+
+    def close(self) -> None:
+        if getattr(self, "_m", None):
+            self.clear_kv_cache()
+            lib().s2k_model_free(self._m)
+            self._m = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def launch_count(reset: bool = False) -> int:
+    return int(lib().s2k_launch_count(1 if reset else 0))

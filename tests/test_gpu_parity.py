@@ -1,0 +1,201 @@
+"""GPU parity: the CUDA path through the C ABI vs the CPU oracle on the same
+seeded weights and inputs.
+
+Bars (from the task's parity contract):
+  * per-step logits: max|delta| <= 1e-2 * std(logits)   (LOGIT_TOL below)
+  * greedy decode: identical semantic and codebook tokens for 64 frames
+  * sampler: identical token for identical logits and uniform draw
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+import s2k
+import synthetic
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-2
+
+
+def assert_close(got: np.ndarray, want: np.ndarray, what: str) -> None:
+    assert np.isfinite(got).all(), f"{what}: non-finite values"
+    err = float(np.abs(got - want).max())
+    bound = LOGIT_TOL * float(want.std())
+    assert err <= bound, f"{what}: max|delta| {err:.3e} > {bound:.3e}"
+
+
+@pytest.fixture(scope="module")
+def small_gpu(small_model_data):
+    hp, tensors = small_model_data
+    m = s2k.SlowARModel(hp)
+    m.load_tensors(tensors)
+    yield m
+    m.close()
+
+
+def test_prefill_and_steps_small(small_gpu, small_oracle, small_model_data):
+    hp, _ = small_model_data
+    p = synthetic.text_prompt(hp, 16)
+    small_gpu.init_kv_cache(64)
+    small_oracle.init_kv_cache(64)
+    hg, lg = small_gpu.prefill_fast(p.T.reshape(-1), 16)
+    ho, lo = small_oracle.eval(p.T.reshape(-1), 16)
+    assert_close(hg, ho, "prefill hidden")
+    assert_close(lg, lo, "prefill logits")
+    rng = np.random.default_rng(5)
+    for i in range(6):
+        tok = np.zeros(hp.num_codebooks + 1, np.int32)
+        if i % 2 == 0:  # semantic token with codes
+            tok[1:] = rng.integers(0, hp.codebook_size, hp.num_codebooks)
+            tok[0] = hp.semantic_begin_id + tok[1]
+        else:
+            tok[0] = rng.integers(0, hp.semantic_begin_id)
+        hg, lg = small_gpu.step(tok)
+        ho, lo = small_oracle.eval(tok, 1)
+        assert_close(hg, ho, f"step {i} hidden")
+        assert_close(lg, lo, f"step {i} logits")
+    assert small_gpu.n_past == small_oracle.n_past == 22
+
+
+def test_semantic_prefill_small(small_gpu, small_oracle, small_model_data):
+    hp, _ = small_model_data
+    p = synthetic.semantic_prompt(hp, 24)
+    small_gpu.init_kv_cache(32)
+    small_oracle.init_kv_cache(32)
+    hg, lg = small_gpu.prefill_fast(p.T.reshape(-1), 24)
+    ho, lo = small_oracle.eval(p.T.reshape(-1), 24)
+    assert_close(hg, ho, "semantic prefill hidden")
+    assert_close(lg, lo, "semantic prefill logits")
+
+
+def test_fast_decode_small(small_gpu, small_oracle, small_model_data):
+    hp, _ = small_model_data
+    rng = np.random.default_rng(7)
+    hidden = rng.standard_normal(hp.embedding_length).astype(np.float32)
+    for n in range(hp.num_codebooks):
+        prefix = rng.integers(0, hp.codebook_size, n).astype(np.int32)
+        assert_close(small_gpu.fast_decode(hidden, prefix), small_oracle.fast_decode(hidden, prefix),
+                     f"fast_decode prefix {n}")
+
+
+@pytest.mark.parametrize("n", [4096, 4097, 1000])
+def test_sampler_matches_oracle(small_gpu, n):
+    rng = np.random.default_rng(n)
+    cases = [(0.0, 0.8, 30), (1.0, 0.9, 30), (0.7, 0.9, 0), (1.3, 1.0, 5), (0.8, 0.8, 4096), (1.0, 0.05, 30)]
+    for trial in range(8):
+        x = (rng.standard_normal(n) * rng.uniform(0.5, 4)).astype(np.float32)
+        for temp, top_p, top_k in cases:
+            u = float(rng.uniform())
+            want = oracle.sample_token(x, temp, top_p, top_k, u)
+            got = small_gpu.sample(x, temp, top_p, top_k, u)
+            assert got == want, (trial, temp, top_p, top_k, u, got, want)
+
+
+def test_generate_greedy_64_frames_small(small_gpu, small_oracle, small_model_data):
+    hp, _ = small_model_data
+    p = synthetic.text_prompt(hp, 20)
+    want = small_oracle.generate(p, 64, temperature=0.0, seed=99, im_end_id=-1)
+    got = small_gpu.generate(p, 64, temperature=0.0, seed=99, im_end_id=-1)
+    assert got.shape == want.shape == (hp.num_codebooks, 64)
+    assert np.array_equal(got, want)
+
+
+def test_generate_sampled_small(small_gpu, small_oracle, small_model_data):
+    hp, _ = small_model_data
+    p = synthetic.semantic_prompt(hp, 12)
+    kw = dict(temperature=0.7, top_p=0.9, top_k=30, seed=5, im_end_id=-1)
+    want = small_oracle.generate(p, 32, **kw)
+    got = small_gpu.generate(p, 32, **kw)
+    assert np.array_equal(got, want)
+
+
+def test_generate_stops_at_im_end(small_gpu, small_oracle, small_model_data):
+    hp, _ = small_model_data
+    p = synthetic.text_prompt(hp, 8)
+    free = small_oracle.generate(p, 30, temperature=0.0, seed=1, im_end_id=-1)
+    # make the 6th frame's main token the end token, blocked for 3 frames
+    im_end = int(hp.semantic_begin_id + free[0, 5])
+    want = small_oracle.generate(p, 30, temperature=0.0, seed=1, im_end_id=im_end, min_tokens_before_end=3)
+    got = small_gpu.generate(p, 30, temperature=0.0, seed=1, im_end_id=im_end, min_tokens_before_end=3)
+    assert np.array_equal(got, want)
+    assert got.shape[1] < 30
+
+
+def test_on_frame_callback_and_abort(small_gpu, small_model_data):
+    hp, _ = small_model_data
+    p = synthetic.text_prompt(hp, 8)
+    seen = []
+
+    def cb(codes, idx, total):
+        seen.append((idx, codes.copy()))
+        return idx < 4
+
+    out = small_gpu.generate(p, 16, temperature=0.0, seed=1, on_frame=cb)
+    assert out.shape[1] == 5 and len(seen) == 5
+    for idx, c in seen:
+        assert np.array_equal(c, out[:, idx])
+
+
+def test_error_paths(small_gpu, small_model_data):
+    hp, _ = small_model_data
+    small_gpu.init_kv_cache(4)
+    p = synthetic.text_prompt(hp, 4)
+    small_gpu.prefill_fast(p.T.reshape(-1), 4)
+    with pytest.raises(s2k.S2KError) as e:
+        small_gpu.step(np.zeros(hp.num_codebooks + 1, np.int32))
+    assert e.value.status == -4  # KV full
+    small_gpu.init_kv_cache(8)
+    bad = np.zeros(hp.num_codebooks + 1, np.int32)
+    bad[0] = hp.vocab_size
+    with pytest.raises(s2k.S2KError) as e:
+        small_gpu.step(bad)
+    assert e.value.status == -1
+    with pytest.raises(s2k.S2KError):
+        small_gpu.fast_decode(np.zeros(hp.embedding_length, np.float32), np.zeros(hp.num_codebooks, np.int32))
+    # the model still works after rejected calls
+    small_gpu.step(np.zeros(hp.num_codebooks + 1, np.int32))
+
+
+@pytest.fixture(scope="module")
+def mid_pair():
+    hp = synthetic.preset("mid")
+    tensors = list(synthetic.make_model(hp, seed=21, norm_std=0.1))
+    m = s2k.SlowARModel(hp)
+    m.load_tensors(tensors)
+    om = oracle.OracleModel(hp)
+    om.load_tensors(tensors)
+    yield hp, m, om
+    m.close()
+    om.close()
+
+
+def test_mid_real_widths(mid_pair):
+    """d 2560, GQA 32/8, ff 9728, vocab 155,648: the shapes of the real model."""
+    hp, m, om = mid_pair
+    p = synthetic.semantic_prompt(hp, 8)
+    m.init_kv_cache(32)
+    om.init_kv_cache(32)
+    hg, lg = m.prefill_fast(p.T.reshape(-1), 8)
+    ho, lo = om.eval(p.T.reshape(-1), 8)
+    assert_close(lg, lo, "mid prefill logits")
+    for i in range(3):
+        tok = np.zeros(hp.num_codebooks + 1, np.int32)
+        tok[1:] = np.arange(hp.num_codebooks) * 37 + i
+        tok[0] = hp.semantic_begin_id + tok[1]
+        hg, lg = m.step(tok)
+        ho, lo = om.eval(tok, 1)
+        assert_close(lg, lo, f"mid step {i} logits")
+    for n in (0, 1, 5, 9):
+        prefix = (np.arange(n) * 411 % hp.codebook_size).astype(np.int32)
+        assert_close(m.fast_decode(ho, prefix), om.fast_decode(ho, prefix), f"mid fast_decode {n}")
+
+
+def test_mid_generate_greedy(mid_pair):
+    hp, m, om = mid_pair
+    p = synthetic.text_prompt(hp, 16)
+    want = om.generate(p, 8, temperature=0.0, seed=4, im_end_id=-1)
+    got = m.generate(p, 8, temperature=0.0, seed=4, im_end_id=-1)
+    assert np.array_equal(got, want)
