@@ -194,6 +194,15 @@ S2K_API s2k_status s2k_sample(s2k_model *m, const float *logits, int32_t n, floa
 S2K_API s2k_status s2k_profile_gemv(s2k_model *m, int32_t reps, double *bytes_per_pass,
                                     double *ms_per_pass, int32_t *launches_per_pass);
 
+/* Debugging aid (no reference counterpart): copies up to nbytes of a named
+ * device buffer to host memory.  Names: "x", "h", "qkv", "attn", "ff",
+ * "kcur", "vcur", "logits", "hidden" (Slow workspace), "fx", "fh", "fqkv",
+ * "fattn", "fff", "flogits" (Fast workspace), "kv_k", "kv_v" (the sequence's
+ * f16 KV pages, [page][layer][kv_head][16][head_dim]).  *copied gets the
+ * number of bytes written. */
+S2K_API s2k_status s2k_debug_copy(s2k_model *m, s2k_seq *s, const char *name, void *host,
+                                  size_t nbytes, size_t *copied);
+
 /* Counts kernel launches issued by the library since the last reset. */
 S2K_API uint64_t s2k_launch_count(int32_t reset);
 

@@ -116,6 +116,30 @@ double so_philox_uniform(uint64_t seed, uint32_t frame, uint32_t purpose, uint32
 }
 
 /* ------------------------------------------------------------------------ */
+/* exp with a fixed sequence of IEEE float operations: the CUDA kernels run  */
+/* the same steps (s2k_common.cuh det_expf), so both return identical bits.  */
+/* Cody-Waite reduction x = k ln2 + r, Taylor series of exp(r) to degree 7,  */
+/* scaling by 2^k.  Accuracy ~1-2 ulp, like libm expf.                       */
+/* ------------------------------------------------------------------------ */
+
+float so_det_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return INFINITY;
+    if (x < -103.972084045410156f) return 0.0f;
+    const float k = rintf(x * 1.44269502162933349609f);
+    const float r = (x - k * 0.693145751953125f) - k * 1.42860682030941723212e-6f;
+    float p = 1.98412698412698412526e-4f;
+    p = p * r + 1.38888888888888894189e-3f;
+    p = p * r + 8.33333333333333321769e-3f;
+    p = p * r + 4.16666666666666643537e-2f;
+    p = p * r + 1.66666666666666657415e-1f;
+    p = p * r + 0.5f;
+    p = p * r + 1.0f;
+    p = p * r + 1.0f;
+    return ldexpf(p, (int)k);
+}
+
+/* ------------------------------------------------------------------------ */
 /* block formats                                                             */
 /* ------------------------------------------------------------------------ */
 
@@ -273,20 +297,26 @@ static inline int32_t dot_i8(const int8_t *a, const int8_t *b, int n) {
     return s;
 }
 
-/* vec_dot_q8_0_q8_0: sum_b (int sum_b) * (d_w * d_x) */
+/* Every dot below follows the arithmetic convention the CUDA kernels share:
+ * each block term is formed exactly (or as ggml rounds its float scale), the
+ * terms are summed in double and the row result is rounded to float once.
+ * This is the limit every ggml backend's float accumulation approximates, and
+ * it makes the result independent of summation order. */
+
+/* vec_dot_q8_0_q8_0: sum_b (int sum_b) * (d_w * d_x); d_w*d_x is exact in float */
 static float dot_q8_0(const uint8_t *w, const uint8_t *a, int64_t n) {
-    float sumf = 0.0f;
+    double acc = 0.0;
     for (int64_t b = 0; b < n / QK8_0; ++b, w += 34, a += 34) {
         const int32_t s = dot_i8((const int8_t *)(w + 2), (const int8_t *)(a + 2), QK8_0);
-        sumf += (float)s * (so_fp16_to_fp32(rd16(w)) * so_fp16_to_fp32(rd16(a)));
+        acc += (double)s * (double)(so_fp16_to_fp32(rd16(w)) * so_fp16_to_fp32(rd16(a)));
     }
-    return sumf;
+    return (float)acc;
 }
 
 /* vec_dot_q4_K_q8_K: per super-block
  *   (d_w*d_x) * sum_j sc_j*(q4 . q8)_j  -  (dmin_w*d_x) * sum_j m_j*bsum_j */
 static float dot_q4_K(const uint8_t *w, const uint8_t *a, int64_t n) {
-    float sumf = 0.0f;
+    double sumf = 0.0;
     for (int64_t b = 0; b < n / QK_K; ++b, w += 144, a += 292) {
         float dx;
         memcpy(&dx, a, 4);
@@ -309,15 +339,14 @@ static float dot_q4_K(const uint8_t *w, const uint8_t *a, int64_t n) {
         }
         const float d = so_fp16_to_fp32(rd16(w)) * dx;
         const float dmin = so_fp16_to_fp32(rd16(w + 2)) * dx;
-        sumf += d * (float)isum;
-        sumf -= dmin * (float)msum;
+        sumf += (double)d * (double)isum - (double)dmin * (double)msum;
     }
-    return sumf;
+    return (float)sumf;
 }
 
 /* vec_dot_q6_K_q8_K: per super-block (d_w*d_x) * sum_j sc_j*((q6-32) . q8)_j */
 static float dot_q6_K(const uint8_t *w, const uint8_t *a, int64_t n) {
-    float sumf = 0.0f;
+    double sumf = 0.0;
     int8_t q6[QK_K];
     for (int64_t b = 0; b < n / QK_K; ++b, w += 210, a += 292) {
         const uint8_t *ql = w, *qh = w + 128;
@@ -334,9 +363,10 @@ static float dot_q6_K(const uint8_t *w, const uint8_t *a, int64_t n) {
         const int8_t *q8 = (const int8_t *)(a + 4);
         int32_t isum = 0;
         for (int j = 0; j < 16; ++j) isum += (int32_t)sc[j] * dot_i8(q6 + 16 * j, q8 + 16 * j, 16);
-        sumf += (so_fp16_to_fp32(rd16(w + 208)) * dx) * (float)isum;
+        const float d = so_fp16_to_fp32(rd16(w + 208)) * dx;
+        sumf += (double)d * (double)isum;
     }
-    return sumf;
+    return (float)sumf;
 }
 
 /* ggml_vec_dot_f16 with the activation converted to f16 (vec_dot_type F16) */
@@ -574,7 +604,7 @@ static void rope_head(float *v, int hd, int32_t pos, float theta_scale) {
     }
 }
 
-static inline float silu_f(float x) { return x / (1.0f + expf(-x)); }
+static inline float silu_f(float x) { return x / (1.0f + so_det_expf(-x)); }
 
 /* One transformer stack over T tokens (shared by the Slow-AR and the Fast-AR).
  * x: [T][dim] residual stream, updated in place.
@@ -646,29 +676,31 @@ static void run_layers(so_model *m, int fast, float *x, int T, int32_t n_past) {
                 const float *q = qkv + (int64_t)t * qkvs + hh * hd;
                 const int kvh = hh / rep;
                 const int len = n_past + t + 1;
+                /* KQ (exact products summed in double, rounded once), ggml_scale,
+                 * diag_mask_inf (keys j >= len excluded), soft_max (max, exp,
+                 * double sum, scale by float(1/sum)), then V.KQ in double. */
                 float *sc = (float *)malloc(sizeof(float) * (size_t)n_kv);
                 float mx = -INFINITY;
-                for (int j = 0; j < n_kv; ++j) {
-                    if (j >= len) { sc[j] = -INFINITY; continue; }
+                for (int j = 0; j < len; ++j) {
                     const float *kk = kf + (int64_t)j * kvs + kvh * hd;
-                    float s = 0.0f;
-                    for (int d = 0; d < hd; ++d) s += kk[d] * q[d];
-                    sc[j] = s * attn_scale;
+                    double s = 0.0;
+                    for (int d = 0; d < hd; ++d) s += (double)kk[d] * (double)q[d];
+                    sc[j] = (float)s * attn_scale;
                     if (sc[j] > mx) mx = sc[j];
                 }
                 double sum = 0.0;
-                for (int j = 0; j < n_kv; ++j) {
-                    const float e = expf(sc[j] - mx);
+                for (int j = 0; j < len; ++j) {
+                    const float e = so_det_expf(sc[j] - mx);
                     sc[j] = e;
                     sum += (double)e;
                 }
                 const float inv = (float)(1.0 / sum);
-                for (int j = 0; j < n_kv; ++j) sc[j] *= inv;
+                for (int j = 0; j < len; ++j) sc[j] = sc[j] * inv;
                 float *o = attn + (int64_t)t * qs + hh * hd;
                 for (int d = 0; d < hd; ++d) {
-                    float s = 0.0f;
-                    for (int j = 0; j < n_kv; ++j) s += vf[(int64_t)j * kvs + kvh * hd + d] * sc[j];
-                    o[d] = s;
+                    double s = 0.0;
+                    for (int j = 0; j < len; ++j) s += (double)vf[(int64_t)j * kvs + kvh * hd + d] * (double)sc[j];
+                    o[d] = (float)s;
                 }
                 free(sc);
             }
@@ -784,10 +816,13 @@ int32_t so_sample_token(const float *logits, int32_t n, float temperature, float
     const int32_t k = top_k > 0 ? (top_k < n ? top_k : n) : n;
     const float tp = top_p < 0.0f ? 0.0f : (top_p > 1.0f ? 1.0f : top_p);
     /* softmax at T = 1 over all sorted logits */
+    /* softmax_from_sorted_logits with the shared exp and a double-summed,
+     * once-rounded normaliser */
     float *p = (float *)malloc(sizeof(float) * (size_t)n);
     const float mx = it[0].v;
-    float sum = 0.0f;
-    for (int32_t i = 0; i < n; ++i) { p[i] = expf(it[i].v - mx); sum += p[i]; }
+    double sumd = 0.0;
+    for (int32_t i = 0; i < n; ++i) { p[i] = so_det_expf(it[i].v - mx); sumd += (double)p[i]; }
+    const float sum = (float)sumd;
     if (sum > 0.0f) for (int32_t i = 0; i < n; ++i) p[i] /= sum;
     so_item *f = (so_item *)malloc(sizeof(so_item) * (size_t)n);
     int32_t nf = 0;
@@ -804,7 +839,7 @@ int32_t so_sample_token(const float *logits, int32_t n, float temperature, float
         float m2 = f[0].v;
         for (int32_t i = 1; i < nf; ++i) if (f[i].v > m2) m2 = f[i].v;
         float s = 0.0f;
-        for (int32_t i = 0; i < nf; ++i) { q[i] = expf((f[i].v - m2) / temperature); s += q[i]; }
+        for (int32_t i = 0; i < nf; ++i) { q[i] = so_det_expf((f[i].v - m2) / temperature); s += q[i]; }
         if (s > 0.0f) for (int32_t i = 0; i < nf; ++i) q[i] /= s;
         float sp = 0.0f;
         for (int32_t i = 0; i < nf; ++i) sp += q[i];

@@ -21,6 +21,15 @@
  *   - rms_norm (double accumulation), rope mode 0 with the cumulative
  *     theta *= theta_scale recurrence, soft_max, swiglu.
  *
+ * Rounding convention (shared with the CUDA kernels): every reduction that
+ * feeds an activation quantizer is evaluated as exactly-formed terms summed
+ * in double and rounded to float once, and exp is so_det_expf.  ggml's own
+ * float accumulation order is implementation-defined (SIMD width, thread
+ * split); this convention is the order-free limit of it, and it lets the GPU
+ * and this oracle agree bit for bit, which a Q8_0-quantized network needs:
+ * any 1-ulp difference can flip an int8 activation and is then amplified
+ * layer by layer.
+ *
  * RNG: the reference draws from a thread_local mt19937 seeded by
  * std::random_device (src/s2_sampler.cpp:94), which no test can pin.  Both
  * this oracle and the CUDA sampler instead draw u ~ U[0,1) from Philox4x32-10
@@ -96,6 +105,8 @@ float so_vec_dot(int type, const void *wrow, const void *act, int64_t n);
 /* y[r] = W[r,:] . x for a [rows x n] GGUF-native matrix, x f32; n_threads<=0: all */
 void so_matvec(int type, const void *w, int64_t rows, int64_t n, const float *x, float *y);
 uint16_t so_fp32_to_fp16(float f);
+/* exp(x) by a fixed float operation sequence shared with the CUDA kernels */
+float so_det_expf(float x);
 float so_fp16_to_fp32(uint16_t h);
 void so_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);
 double so_philox_uniform(uint64_t seed, uint32_t frame, uint32_t purpose, uint32_t seq);

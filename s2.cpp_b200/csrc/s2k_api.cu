@@ -48,10 +48,11 @@ struct Layer {
 
 // Activations of one transformer stack for up to T tokens.
 struct Work {
-    int T = 0, dim = 0, qs = 0, kvs = 0, ff = 0, H = 0, n_splits_max = 0;
+    int T = 0, L = 0, dim = 0, qs = 0, kvs = 0, ff = 0, H = 0;
     float *x = nullptr, *h = nullptr, *qkv = nullptr, *attn = nullptr, *ff_buf = nullptr;
-    float *kcur = nullptr, *vcur = nullptr, *part = nullptr;
-    int *counters = nullptr;
+    float *kcur = nullptr, *vcur = nullptr, *scores = nullptr, *stats = nullptr;
+    double *part = nullptr;
+    int *counters = nullptr, *counters2 = nullptr;
 };
 
 }  // namespace s2k
@@ -84,6 +85,9 @@ struct s2k_model {
     std::vector<float *> fkcur, fvcur;
     float *flogits = nullptr, *fhidden = nullptr;
     int *fcodes = nullptr;
+    // RoPE cos/sin tables [positions][head_dim/2]
+    float2 *rope_slow = nullptr, *rope_fast = nullptr;
+    int rope_slow_n = 0, rope_fast_n = 0;
     // standalone sampler scratch
     float *samp_logits = nullptr;
     int samp_cap = 0;
@@ -158,14 +162,15 @@ static int n_splits_for(int T) {
     return std::max(1, 16 / T);
 }
 
-static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int dim, int H, int Hkv, int hd, int ff) {
+// T: tokens per call; L: longest key range (positions) a call attends over.
+static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int Hkv, int hd, int ff) {
     w.T = T;
+    w.L = L;
     w.dim = dim;
     w.qs = H * hd;
     w.kvs = Hkv * hd;
     w.ff = ff;
     w.H = H;
-    w.n_splits_max = 16;
     const size_t tn = (size_t)std::max(T, 1);
     cudaError_t e;
     if ((e = m->alloc(&w.x, tn * dim))) return e;
@@ -175,26 +180,55 @@ static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int dim, int H, int 
     if ((e = m->alloc(&w.ff_buf, tn * 2 * ff))) return e;
     if ((e = m->alloc(&w.kcur, tn * w.kvs))) return e;
     if ((e = m->alloc(&w.vcur, tn * w.kvs))) return e;
+    if ((e = m->alloc(&w.scores, tn * H * (size_t)L))) return e;
+    if ((e = m->alloc(&w.stats, tn * H * 2))) return e;
     const size_t ts = std::max<size_t>(tn * n_splits_for(T), 16);
-    if ((e = m->alloc(&w.part, ts * H * (hd + 2)))) return e;
+    if ((e = m->alloc(&w.part, ts * H * hd))) return e;
     if ((e = m->alloc(&w.counters, tn * Hkv))) return e;
-    return cudaMemset(w.counters, 0, tn * Hkv * sizeof(int));
+    if ((e = m->alloc(&w.counters2, tn * Hkv))) return e;
+    if ((e = cudaMemset(w.counters, 0, tn * Hkv * sizeof(int)))) return e;
+    return cudaMemset(w.counters2, 0, tn * Hkv * sizeof(int));
 }
 
 static void work_free(s2k_model *m, Work &w) {
     for (void *p : {(void *)w.x, (void *)w.h, (void *)w.qkv, (void *)w.attn, (void *)w.ff_buf, (void *)w.kcur,
-                    (void *)w.vcur, (void *)w.part, (void *)w.counters})
+                    (void *)w.vcur, (void *)w.scores, (void *)w.stats, (void *)w.part, (void *)w.counters,
+                    (void *)w.counters2})
         m->release(p);
     w = Work();
 }
 
-static s2k_status ensure_slow_work(s2k_model *m, int T) {
-    if (m->sw.T >= T) return S2K_OK;
+static s2k_status ensure_slow_work(s2k_model *m, int T, int L) {
+    if (m->sw.T >= T && m->sw.L >= L) return S2K_OK;
+    T = std::max(T, m->sw.T);
+    L = std::max(L, m->sw.L);
     work_free(m, m->sw);
     m->ws_gen++;
     const s2k_hparams &hp = m->hp;
-    CU(work_alloc(m, m->sw, T, hp.embedding_length, hp.head_count, hp.head_count_kv, hp.head_dim,
+    CU(work_alloc(m, m->sw, T, L, hp.embedding_length, hp.head_count, hp.head_count_kv, hp.head_dim,
                   hp.feed_forward_length));
+    return S2K_OK;
+}
+
+// RoPE (ggml_rope_ext mode 0, freq_scale 1, ext_factor 0, attn_factor 1) as
+// ggml's CPU path evaluates it (ggml_rope_cache_init): theta starts at the
+// position and is multiplied by base^(-2/n_dims) once per pair; cos/sin are
+// the libm float functions of that theta.  Stored as (cos, sin) per
+// [position][pair] and uploaded once, so every kernel reads the same bits the
+// CPU computes.
+static s2k_status upload_rope(s2k_model *m, float2 **dst, int *n_out, int n_pos, int hd, float base) {
+    std::vector<float2> tab((size_t)n_pos * (hd / 2));
+    const float ts = powf(base, -2.0f / (float)hd);
+    for (int p = 0; p < n_pos; ++p) {
+        float theta = (float)p;
+        for (int i = 0; i < hd / 2; ++i) {
+            tab[(size_t)p * (hd / 2) + i] = make_float2(cosf(theta), sinf(theta));
+            theta *= ts;
+        }
+    }
+    CU(m->alloc(dst, tab.size()));
+    CU(cudaMemcpy(*dst, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    *n_out = n_pos;
     return S2K_OK;
 }
 
@@ -220,8 +254,6 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
     const int Hkv = c.fast ? hp.fast_head_count_kv : hp.head_count_kv;
     const int hd = c.fast ? hp.fast_head_dim : hp.head_dim;
     const float eps = c.fast ? hp.fast_rms_norm_eps : hp.rms_norm_eps;
-    const float base = c.fast ? hp.fast_rope_freq_base : hp.rope_freq_base;
-    const float theta_scale = powf(base, -2.0f / (float)hd);
     const int qkvs = w.qs + 2 * w.kvs;
     const int dim = w.dim;
     cudaStream_t st = m->stream;
@@ -252,7 +284,8 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         q.q_norm = L.q_norm;
         q.k_norm = L.k_norm;
         q.eps = eps;
-        q.theta_scale = theta_scale;
+        q.rope = c.fast ? m->rope_fast : m->rope_slow;
+        q.rope_positions = c.fast ? m->rope_fast_n : m->rope_slow_n;
         q.pos_base = c.pos_base;
         q.pos_add = c.pos_add;
         q.kcur = c.fast ? m->fkcur[il] : w.kcur;
@@ -279,8 +312,12 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         a.vcur = q.vcur;
         a.cur_base = c.cur_base;
         a.n_splits = c.n_splits;
+        a.scores = w.scores;
+        a.ld_scores = w.L;
+        a.stats = w.stats;
         a.part = w.part;
         a.counters = w.counters;
+        a.counters2 = w.counters2;
         a.out = w.attn;
         a.done = c.done;
         a.err = m->d_err;
@@ -707,11 +744,20 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     }
     CU(m->alloc(&m->logits, (size_t)hp.vocab_size));
     CU(m->alloc(&m->hidden, (size_t)hp.embedding_length));
-    rc = ensure_slow_work(m, 16);
+    rc = upload_rope(m, &m->rope_slow, &m->rope_slow_n, std::max(hp.context_length, 1), hp.head_dim,
+                     hp.rope_freq_base);
+    if (rc) return rc;
+    if (hp.has_fast_decoder) {
+        rc = upload_rope(m, &m->rope_fast, &m->rope_fast_n,
+                         std::max(hp.fast_context_length, hp.num_codebooks + 1), hp.fast_head_dim,
+                         hp.fast_rope_freq_base);
+        if (rc) return rc;
+    }
+    rc = ensure_slow_work(m, 16, 64);
     if (rc) return rc;
     if (hp.has_fast_decoder) {
         const int Tf = std::max(hp.num_codebooks, 2);
-        CU(work_alloc(m, m->fw, Tf, hp.fast_embedding_length, hp.fast_head_count, hp.fast_head_count_kv,
+        CU(work_alloc(m, m->fw, Tf, Tf, hp.fast_embedding_length, hp.fast_head_count, hp.fast_head_count_kv,
                       hp.fast_head_dim, hp.fast_feed_forward_length));
         const int fkvs = hp.fast_head_count_kv * hp.fast_head_dim;
         m->fkcur.assign(hp.fast_block_count, nullptr);
@@ -732,6 +778,8 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
 S2K_API s2k_status s2k_seq_create(s2k_model *m, int32_t max_seq_len, s2k_seq **out) {
     if (!m || !out || max_seq_len <= 0) return fail(S2K_ERR_ARG, "bad argument");
     if (!m->finalized) return fail(S2K_ERR_STATE, "model not finalized");
+    if (max_seq_len > m->rope_slow_n)
+        return fail(S2K_ERR_ARG, "max_seq_len %d exceeds context_length %d", max_seq_len, m->rope_slow_n);
     if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
     *out = nullptr;
     s2k_seq *s = new s2k_seq();
@@ -814,7 +862,7 @@ S2K_API s2k_status s2k_eval(s2k_model *m, s2k_seq *s, const int32_t *flat, int32
     s2k_status rc = check_tokens_host(m, flat, T);
     if (rc) return rc;
     if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
-    rc = ensure_slow_work(m, T);
+    rc = ensure_slow_work(m, T, s->max_seq_len);
     if (rc) return rc;
     const int stride = m->hp.num_codebooks + 1;
     if (m->tokens_cap < T * stride) {
@@ -916,7 +964,7 @@ static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_promp
     if (cols + gp->max_new_tokens > s->max_seq_len)
         return fail(S2K_ERR_KV_FULL, "sequence holds %d positions, need %d", s->max_seq_len, cols + gp->max_new_tokens);
     if (!hp.has_fast_decoder && hp.num_codebooks > 1) return fail(S2K_ERR_STATE, "model has no fast decoder");
-    s2k_status rc = ensure_slow_work(m, cols);
+    s2k_status rc = ensure_slow_work(m, cols, s->max_seq_len);
     if (rc) return rc;
     SampleCfg c;
     memset(&c, 0, sizeof(c));
@@ -1105,6 +1153,45 @@ S2K_API s2k_status s2k_profile_gemv(s2k_model *m, int32_t reps, double *bytes_pe
     *ms_per_pass = ms / reps;
     *launches_per_pass = launches;
     return check_err_word(m);
+}
+
+S2K_API s2k_status s2k_debug_copy(s2k_model *m, s2k_seq *s, const char *name, void *host, size_t nbytes,
+                                  size_t *copied) {
+    if (!m || !name || !host || !copied) return fail(S2K_ERR_ARG, "NULL argument");
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    const s2k_hparams &hp = m->hp;
+    const void *src = nullptr;
+    size_t bytes = 0;
+    const Work &w = m->sw, &f = m->fw;
+    const std::string n(name);
+    auto pick = [&](const void *p, size_t b) { src = p; bytes = b; };
+    if (n == "x") pick(w.x, (size_t)w.T * w.dim * 4);
+    else if (n == "h") pick(w.h, (size_t)w.T * w.dim * 4);
+    else if (n == "qkv") pick(w.qkv, (size_t)w.T * (w.qs + 2 * w.kvs) * 4);
+    else if (n == "attn") pick(w.attn, (size_t)w.T * w.qs * 4);
+    else if (n == "ff") pick(w.ff_buf, (size_t)w.T * 2 * w.ff * 4);
+    else if (n == "kcur") pick(w.kcur, (size_t)w.T * w.kvs * 4);
+    else if (n == "vcur") pick(w.vcur, (size_t)w.T * w.kvs * 4);
+    else if (n == "logits") pick(m->logits, (size_t)hp.vocab_size * 4);
+    else if (n == "hidden") pick(m->hidden, (size_t)hp.embedding_length * 4);
+    else if (n == "fx") pick(f.x, (size_t)f.T * f.dim * 4);
+    else if (n == "fh") pick(f.h, (size_t)f.T * f.dim * 4);
+    else if (n == "fqkv") pick(f.qkv, (size_t)f.T * (f.qs + 2 * f.kvs) * 4);
+    else if (n == "fattn") pick(f.attn, (size_t)f.T * f.qs * 4);
+    else if (n == "fff") pick(f.ff_buf, (size_t)f.T * 2 * f.ff * 4);
+    else if (n == "flogits") pick(m->flogits, (size_t)hp.codebook_size * 4);
+    else if ((n == "kv_k" || n == "kv_v") && s) {
+        const size_t page_elems = (size_t)hp.block_count * hp.head_count_kv * kPage * hp.head_dim;
+        pick(n == "kv_k" ? (const void *)s->k : (const void *)s->v, page_elems * s->n_pages * 2);
+    } else {
+        return fail(S2K_ERR_ARG, "unknown buffer '%s'", name);
+    }
+    if (!src) return fail(S2K_ERR_STATE, "buffer '%s' not allocated", name);
+    const size_t nb = std::min(nbytes, bytes);
+    CU(cudaStreamSynchronize(m->stream));
+    CU(cudaMemcpy(host, src, nb, cudaMemcpyDeviceToHost));
+    *copied = nb;
+    return S2K_OK;
 }
 
 }  // extern "C"

@@ -1,15 +1,26 @@
-// s2k_attn.cu -- per-head QK-norm + RoPE + KV store, and GQA flash-decode
+// s2k_attn.cu -- per-head QK-norm + RoPE + KV store, and GQA decode/prefill
 // attention over a paged f16 KV cache plus the current call's f32 K/V.
 //
 // Reference semantics (src/s2_model.cpp:970-1039 Slow, 1163-1212 Fast):
 //   q/k per-head rms_norm_weighted (eps, q_norm / k_norm)      :979-982
-//   ggml_rope_ext mode 0, n_dims = head_dim, freq_scale 1,
-//     theta = pos * theta_scale^i by repeated multiplication  :984-989
+//   ggml_rope_ext mode 0, n_dims = head_dim, freq_scale 1       :984-989
+//     (cos/sin come from a table the host builds with ggml's recurrence
+//      theta_i = theta_{i-1} * base^(-2/n_dims), theta_0 = pos)
 //   K/V of this call stored as f16 at n_past                   :991-1005
 //   keys/values: past from the f16 cache (f16 -> f32), this
 //     call's tokens from the un-rounded f32 projections        :1007-1020
 //   GQA: query head h reads kv head h / (H/Hkv)                :57-68
 //   softmax((K.Q) * 1/sqrt(hd), causal from n_past) . V        :1023-1039
+//
+// Arithmetic (shared with the CPU oracle so the two agree bit for bit):
+//   s_j  = float(sum_d double(k_j[d]) * double(q[d])) * scale
+//   p_j  = det_expf(s_j - max_j s_j),  inv = float(1 / sum_j double(p_j))
+//   out  = float(sum_j double(v_j[d]) * double(p_j * inv))
+// Products of two floats are exact in double and the double sums are rounded
+// to float once, so the split over CTAs does not change the result.
+//
+// Two kernels per layer: attn_scores (scores + last-CTA softmax statistics)
+// and attn_values (weighted values + last-CTA merge of the splits).
 #include "s2k_common.cuh"
 #include "s2k_kernels.h"
 
@@ -19,15 +30,15 @@ namespace s2k {
 __global__ void qk_prep_kernel(QkPrepArgs a) {
     pdl_launch_dependents();
     pdl_wait();
-    if (a.done && *a.done) return;
+    if (a.done && __ldcg(a.done)) return;
     const int t = blockIdx.x, y = blockIdx.y, i = threadIdx.x, hd = a.hd;
     float *row = a.qkv + (size_t)t * a.ldqkv;
-    const int pos = (a.pos_base ? *a.pos_base : 0) + a.pos_add + t;
+    const int pos = (a.pos_base ? __ldcg(a.pos_base) : 0) + a.pos_add + t;
     const bool isq = y < a.H;
     const bool isk = !isq && y < a.H + a.Hkv;
     const int head = isq ? y : (isk ? y - a.H : y - a.H - a.Hkv);
     float *v = row + (isq ? head * hd : (isk ? (a.H + head) * hd : (a.H + a.Hkv + head) * hd));
-    float x0 = v[2 * i], x1 = v[2 * i + 1];
+    float x0 = __ldcg(v + 2 * i), x1 = __ldcg(v + 2 * i + 1);
     if (isq || isk) {
         const float *nw = isq ? a.q_norm : a.k_norm;
         if (nw) {
@@ -43,11 +54,13 @@ __global__ void qk_prep_kernel(QkPrepArgs a) {
             x0 = __fmul_rn(__fmul_rn(x0, sc), nw[2 * i]);
             x1 = __fmul_rn(__fmul_rn(x1, sc), nw[2 * i + 1]);
         }
-        float theta = (float)pos;
-        for (int k = 0; k < i; ++k) theta = __fmul_rn(theta, a.theta_scale);
-        const float c = cosf(theta), s = sinf(theta);
-        const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        if (pos < 0 || pos >= a.rope_positions) {
+            if (i == 0 && a.err) atomicOr(a.err, ERR_BAD_POS);
+            return;
+        }
+        const float2 cs = a.rope[(size_t)pos * (hd / 2) + i];  // (cos, sin)
+        const float y0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+        const float y1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
         x0 = y0;
         x1 = y1;
     }
@@ -65,7 +78,7 @@ __global__ void qk_prep_kernel(QkPrepArgs a) {
             if (i == 0 && a.err) atomicOr(a.err, ERR_BAD_POS);
             return;
         }
-        const int page = a.kv.block_table[pg];
+        const int page = __ldcg(a.kv.block_table + pg);
         __half *dst = (isk ? a.kv.k : a.kv.v) +
                       ((((size_t)page * a.kv.n_layers + a.layer) * a.kv.n_kv_heads + head) * kPage + slot) * hd;
         dst[2 * i] = __float2half_rn(x0);
@@ -73,167 +86,202 @@ __global__ void qk_prep_kernel(QkPrepArgs a) {
     }
 }
 
-cudaError_t launch_qk_prep(const QkPrepArgs &a, cudaStream_t st) {
-    if (a.hd % 64 != 0 || a.hd > 256) return cudaErrorInvalidValue;
+static cudaLaunchConfig_t pdl_cfg(dim3 g, dim3 b, size_t smem, cudaStream_t st, cudaLaunchAttribute *attr) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.T, a.H + 2 * a.Hkv);
-    cfg.blockDim = dim3(a.hd / 2);
+    cfg.gridDim = g;
+    cfg.blockDim = b;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    return cfg;
+}
+
+cudaError_t launch_qk_prep(const QkPrepArgs &a, cudaStream_t st) {
+    if (a.hd % 64 != 0 || a.hd > 256 || !a.rope) return cudaErrorInvalidValue;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.T, a.H + 2 * a.Hkv), dim3(a.hd / 2), 0, st, attr);
     count_launch();
     return cudaLaunchKernelEx(&cfg, qk_prep_kernel, a);
 }
 
-// grid (Hkv, T, n_splits), block 128 (4 warps).  Each CTA covers the G query
-// heads of one kv head over one slice of keys, keeping an online softmax per
-// head; the last CTA of a (token, kv head) merges the slices in split order.
 constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxGroup = 8;
 
+__device__ __forceinline__ void key_range(const AttnArgs &a, int t, int sp, int nc, int *Lk, int *j0, int *j1) {
+    *Lk = nc + a.cur_base + t + 1;
+    *j0 = (int)(((long long)*Lk * sp) / a.n_splits);
+    *j1 = (int)(((long long)*Lk * (sp + 1)) / a.n_splits);
+}
+
 template <int HD>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnArgs a) {
-    constexpr int DPL = HD / 32;  // dims per lane
+__device__ __forceinline__ void load_kv_row(const AttnArgs &a, const __half *cache, const float *cur, int j, int nc,
+                                            int g, int lane, float out[HD / 32]) {
+    constexpr int DPL = HD / 32;
+    if (j < nc) {
+        const int page = __ldcg(a.kv.block_table + j / kPage), slot = j % kPage;
+        const size_t off =
+            ((((size_t)page * a.kv.n_layers + a.layer) * a.kv.n_kv_heads + g) * kPage + slot) * HD + lane * DPL;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) out[d] = __half2float(__ldcg(cache + off + d));
+    } else {
+        const size_t off = ((size_t)(j - nc) * a.Hkv + g) * HD + lane * DPL;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) out[d] = __ldcg(cur + off + d);
+    }
+}
+
+// grid (Hkv, T, n_splits).  Writes s_j for the split's keys; the last CTA of a
+// (token, kv head) computes max_j s_j and inv = 1/sum_j exp(s_j - max) per head.
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a) {
+    constexpr int DPL = HD / 32;
     pdl_launch_dependents();
     pdl_wait();
-    if (a.done && *a.done) return;
+    if (a.done && __ldcg(a.done)) return;
     const int g = blockIdx.x, t = blockIdx.y, sp = blockIdx.z;
     const int G = a.H / a.Hkv;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nc = a.n_cached ? *a.n_cached : 0;
-    const int Lk = nc + a.cur_base + t + 1;
-    const int j0 = (int)(((long long)Lk * sp) / a.n_splits);
-    const int j1 = (int)(((long long)Lk * (sp + 1)) / a.n_splits);
-
-    float q[kMaxGroup][DPL], acc[kMaxGroup][DPL], m[kMaxGroup], l[kMaxGroup];
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) {
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) {
-            acc[h][d] = 0.f;
-            q[h][d] = (h < G) ? a.q[(size_t)t * a.ldq + (size_t)(g * G + h) * HD + lane * DPL + d] : 0.f;
-        }
-    }
-    for (int j = j0 + warp; j < j1; j += kAttnWarps) {
-        float kv_k[DPL], kv_v[DPL];
-        if (j < nc) {
-            const int page = a.kv.block_table[j / kPage], slot = j % kPage;
-            const size_t off = ((((size_t)page * a.kv.n_layers + a.layer) * a.kv.n_kv_heads + g) * kPage + slot) * HD +
-                               lane * DPL;
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) {
-                kv_k[d] = __half2float(a.kv.k[off + d]);
-                kv_v[d] = __half2float(a.kv.v[off + d]);
-            }
-        } else {
-            const size_t off = ((size_t)(j - nc) * a.Hkv + g) * HD + lane * DPL;
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) {
-                kv_k[d] = a.kcur[off + d];
-                kv_v[d] = a.vcur[off + d];
-            }
-        }
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) {
-            if (h < G) {
-                float s = 0.f;
-#pragma unroll
-                for (int d = 0; d < DPL; ++d) s += kv_k[d] * q[h][d];
-                s = warp_sum(s) * a.scale;
-                const float mn = fmaxf(m[h], s);
-                const float corr = expf(m[h] - mn);
-                const float p = expf(s - mn);
-                l[h] = l[h] * corr + p;
-#pragma unroll
-                for (int d = 0; d < DPL; ++d) acc[h][d] = acc[h][d] * corr + p * kv_v[d];
-                m[h] = mn;
-            }
-        }
-    }
-
-    // merge the 4 warps
-    __shared__ float s_m[kAttnWarps][kMaxGroup], s_l[kAttnWarps][kMaxGroup];
-    __shared__ float s_acc[kAttnWarps][kMaxGroup][HD];
-    __shared__ int s_last;
-    if (lane == 0) {
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) {
-            s_m[warp][h] = m[h];
-            s_l[warp][h] = l[h];
-        }
-    }
+    const int nc = a.n_cached ? __ldcg(a.n_cached) : 0;
+    int Lk, j0, j1;
+    key_range(a, t, sp, nc, &Lk, &j0, &j1);
+    float q[kMaxGroup][DPL];
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h)
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) s_acc[warp][h][lane * DPL + d] = acc[h][d];
-    __syncthreads();
-    const int NS = a.n_splits;
-    for (int h = 0; h < G; ++h) {
-        float M = -INFINITY;
-        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w][h]);
-        const size_t base = (((size_t)t * a.H + g * G + h) * NS + sp) * (HD + 2);
-        for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-            float A = 0.f;
-            if (M != -INFINITY)
-                for (int w = 0; w < kAttnWarps; ++w) A += s_acc[w][h][d] * expf(s_m[w][h] - M);
-            a.part[base + d] = A;
-        }
-        if (threadIdx.x == 0) {
-            float Ls = 0.f;
-            if (M != -INFINITY)
-                for (int w = 0; w < kAttnWarps; ++w) Ls += s_l[w][h] * expf(s_m[w][h] - M);
-            a.part[base + HD] = M;
-            a.part[base + HD + 1] = Ls;
+        for (int d = 0; d < DPL; ++d)
+            q[h][d] = (h < G) ? __ldcg(a.q + (size_t)t * a.ldq + (size_t)(g * G + h) * HD + lane * DPL + d) : 0.f;
+    float *scores = a.scores + ((size_t)t * a.H + (size_t)g * G) * a.ld_scores;
+    for (int j = j0 + warp; j < j1; j += kAttnWarps) {
+        float k[DPL];
+        load_kv_row<HD>(a, a.kv.k, a.kcur, j, nc, g, lane, k);
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h) {
+            if (h < G) {
+                double s = 0.0;
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) s += (double)k[d] * (double)q[h][d];
+                s = warp_sum_d(s);
+                if (lane == 0) scores[(size_t)h * a.ld_scores + j] = __fmul_rn((float)s, a.scale);
+            }
         }
     }
+    __shared__ int s_last;
+    __shared__ float s_red[kAttnWarps];
+    __shared__ double s_dred[kAttnWarps];
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) {
-        const int old = atomicAdd(&a.counters[t * a.Hkv + g], 1);
-        s_last = (old == NS - 1);
-    }
+    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[t * a.Hkv + g], 1) == a.n_splits - 1;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
     for (int h = 0; h < G; ++h) {
-        const size_t hb = ((size_t)t * a.H + g * G + h) * NS * (HD + 2);
-        float M = -INFINITY;
-        for (int s = 0; s < NS; ++s) M = fmaxf(M, __ldcg(&a.part[hb + s * (HD + 2) + HD]));
-        float Ls = 0.f;
-        for (int s = 0; s < NS; ++s) {
-            const float ms = __ldcg(&a.part[hb + s * (HD + 2) + HD]);
-            if (ms != -INFINITY) Ls += __ldcg(&a.part[hb + s * (HD + 2) + HD + 1]) * expf(ms - M);
+        const float *sh = scores + (size_t)h * a.ld_scores;
+        float mx = -INFINITY;
+        for (int j = threadIdx.x; j < Lk; j += kAttnThreads) mx = fmaxf(mx, __ldcg(sh + j));
+        mx = warp_max(mx);
+        if (lane == 0) s_red[warp] = mx;
+        __syncthreads();
+        mx = s_red[0];
+        for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, s_red[w]);
+        double sum = 0.0;
+        for (int j = threadIdx.x; j < Lk; j += kAttnThreads) sum += (double)det_expf(__fsub_rn(__ldcg(sh + j), mx));
+        sum = warp_sum_d(sum);
+        if (lane == 0) s_dred[warp] = sum;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double tot = 0.0;
+            for (int w = 0; w < kAttnWarps; ++w) tot += s_dred[w];
+            float *st = a.stats + ((size_t)t * a.H + g * G + h) * 2;
+            st[0] = mx;
+            st[1] = (float)(1.0 / tot);
         }
-        for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-            float A = 0.f;
-            for (int s = 0; s < NS; ++s) {
-                const float ms = __ldcg(&a.part[hb + s * (HD + 2) + HD]);
-                if (ms != -INFINITY) A += __ldcg(&a.part[hb + s * (HD + 2) + d]) * expf(ms - M);
-            }
-            a.out[(size_t)t * a.H * HD + (size_t)(g * G + h) * HD + d] = A / Ls;
-        }
+        __syncthreads();
     }
     if (threadIdx.x == 0) a.counters[t * a.Hkv + g] = 0;
 }
 
+// grid (Hkv, T, n_splits).  Accumulates double(v_j) * double(p_j * inv) over the
+// split's keys; the last CTA of a (token, kv head) sums the splits in order.
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) attn_values_kernel(AttnArgs a) {
+    constexpr int DPL = HD / 32;
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.done && __ldcg(a.done)) return;
+    const int g = blockIdx.x, t = blockIdx.y, sp = blockIdx.z;
+    const int G = a.H / a.Hkv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nc = a.n_cached ? __ldcg(a.n_cached) : 0;
+    int Lk, j0, j1;
+    key_range(a, t, sp, nc, &Lk, &j0, &j1);
+    float mx[kMaxGroup], inv[kMaxGroup];
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h) {
+        mx[h] = h < G ? __ldcg(a.stats + ((size_t)t * a.H + g * G + h) * 2) : 0.f;
+        inv[h] = h < G ? __ldcg(a.stats + ((size_t)t * a.H + g * G + h) * 2 + 1) : 0.f;
+    }
+    const float *scores = a.scores + ((size_t)t * a.H + (size_t)g * G) * a.ld_scores;
+    double acc[kMaxGroup][DPL];
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h)
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) acc[h][d] = 0.0;
+    for (int j = j0 + warp; j < j1; j += kAttnWarps) {
+        float v[DPL];
+        load_kv_row<HD>(a, a.kv.v, a.vcur, j, nc, g, lane, v);
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h) {
+            if (h < G) {
+                const float p = __fmul_rn(det_expf(__fsub_rn(__ldcg(scores + (size_t)h * a.ld_scores + j), mx[h])), inv[h]);
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) acc[h][d] += (double)v[d] * (double)p;
+            }
+        }
+    }
+    __shared__ double s_acc[kAttnWarps][HD];
+    __shared__ int s_last;
+    double *part = a.part + ((size_t)t * a.H + (size_t)g * G) * a.n_splits * HD;
+    for (int h = 0; h < G; ++h) {
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) s_acc[warp][lane * DPL + d] = acc[h][d];
+        __syncthreads();
+        for (int d = threadIdx.x; d < HD; d += kAttnThreads) {
+            double s = s_acc[0][d];
+            for (int w = 1; w < kAttnWarps; ++w) s += s_acc[w][d];
+            part[((size_t)h * a.n_splits + sp) * HD + d] = s;
+        }
+        __syncthreads();
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters2[t * a.Hkv + g], 1) == a.n_splits - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int h = 0; h < G; ++h)
+        for (int d = threadIdx.x; d < HD; d += kAttnThreads) {
+            double s = 0.0;
+            for (int k = 0; k < a.n_splits; ++k) s += __ldcg(part + ((size_t)h * a.n_splits + k) * HD + d);
+            a.out[(size_t)t * a.H * HD + (size_t)(g * G + h) * HD + d] = (float)s;
+        }
+    if (threadIdx.x == 0) a.counters2[t * a.Hkv + g] = 0;
+}
+
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
-    if (a.hd != 128 || a.H % a.Hkv != 0 || a.H / a.Hkv > kMaxGroup || a.n_splits < 1) return cudaErrorInvalidValue;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.Hkv, a.T, a.n_splits);
-    cfg.blockDim = dim3(kAttnWarps * 32);
-    cfg.stream = st;
+    if (a.hd != 128 || a.H % a.Hkv != 0 || a.H / a.Hkv > kMaxGroup || a.n_splits < 1 || !a.scores || !a.stats ||
+        !a.part || !a.counters || !a.counters2)
+        return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.Hkv, a.T, a.n_splits), dim3(kAttnThreads), 0, st, attr);
     count_launch();
-    return cudaLaunchKernelEx(&cfg, attn_kernel<128>, a);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_scores_kernel<128>, a);
+    if (e != cudaSuccess) return e;
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, attn_values_kernel<128>, a);
 }
 
 }  // namespace s2k

@@ -128,7 +128,29 @@ __device__ __forceinline__ int quant_q8_0_lane(float v, float *d_out) {
     return __float2int_rn(__fmul_rn(v, id));
 }
 
+// exp(x) for float x with a fixed sequence of IEEE float operations, so the
+// CUDA kernels and the CPU oracle (oracle/s2_oracle.c, det_expf) return the
+// same bits: Cody-Waite reduction x = k*ln2 + r (ln2 split so k*LN2_HI is
+// exact), exp(r) by its Taylor series to degree 7 (|r| <= ln2/2, truncation
+// < 1e-8 relative), then scaling by 2^k.
+__device__ __forceinline__ float det_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return INFINITY;
+    if (x < -103.972084045410156f) return 0.0f;
+    const float k = rintf(__fmul_rn(x, 1.44269502162933349609f));
+    const float r = __fsub_rn(__fsub_rn(x, __fmul_rn(k, 0.693145751953125f)), __fmul_rn(k, 1.42860682030941723212e-6f));
+    float p = 1.98412698412698412526e-4f;  // 1/5040
+    p = __fadd_rn(__fmul_rn(p, r), 1.38888888888888894189e-3f);  // 1/720
+    p = __fadd_rn(__fmul_rn(p, r), 8.33333333333333321769e-3f);  // 1/120
+    p = __fadd_rn(__fmul_rn(p, r), 4.16666666666666643537e-2f);  // 1/24
+    p = __fadd_rn(__fmul_rn(p, r), 1.66666666666666657415e-1f);  // 1/6
+    p = __fadd_rn(__fmul_rn(p, r), 0.5f);
+    p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+    p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+    return ldexpf(p, (int)k);
+}
+
 // x / (1 + exp(-x)), ggml_silu_f32
-__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, det_expf(-x))); }
 
 }  // namespace s2k

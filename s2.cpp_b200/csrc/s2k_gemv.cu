@@ -21,6 +21,13 @@
 //     in shared memory, then compute with dp4a from shared memory; lane pairs
 //     hold the two 16-byte halves of one 32-weight block so each block's
 //     integer sum is exact before it is scaled, as in ggml.
+//
+// Arithmetic: each block term s_b * (d_w * d_x) is exact in double (s_b < 2^19,
+// d_w * d_x is a product of two fp16 values, exact in float), the terms are
+// summed in double and the row result is rounded to float once.  The result
+// is therefore independent of the summation order, which is what lets the CPU
+// oracle reproduce it bit for bit (a sum of the same exact terms in another
+// order differs only below float resolution).
 #include "s2k_common.cuh"
 #include "s2k_kernels.h"
 
@@ -53,7 +60,7 @@ __host__ __device__ inline GemvLayout gemv_layout(int K, int MT) {
     L.off_bar = (off + 15) & ~15;
     off = L.off_bar + 2 * kStages * 8 + 16;
     L.off_red = (off + 15) & ~15;
-    off = L.off_red + 2 * kNcw * MT * 4 + kNcw * MT * 8 + MT * 4;
+    off = L.off_red + 2 * kNcw * MT * 8 + kNcw * MT * 8 + MT * 4;
     L.off_ring = (off + 127) & ~127;
     L.total = L.off_ring + kStages * L.stage_bytes;
     return L;
@@ -62,9 +69,9 @@ __host__ __device__ inline GemvLayout gemv_layout(int K, int MT) {
 template <int MT>
 __global__ void __launch_bounds__(kThreads, 2)
     gemv_q8_0_kernel(const int8_t *__restrict__ wq, const __half *__restrict__ wd, int R, int K,
-                     const float *__restrict__ x, int ldx, int M, int in_mode,
-                     const float *__restrict__ norm_w, float eps, float *__restrict__ y, int ldy,
-                     const float *__restrict__ res, int ldres, float *__restrict__ act_out,
+                     const float *x, int ldx, int M, int in_mode,
+                     const float *__restrict__ norm_w, float eps, float *y, int ldy,
+                     const float *res, int ldres, float *act_out,
                      const int *done, int *err) {
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvLayout L = gemv_layout(K, MT);
@@ -73,8 +80,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
     uint64_t *empty = full + kStages;
     volatile int *s_flags = reinterpret_cast<volatile int *>(empty + kStages);  // [0] abort, [1] cap
-    float *red = reinterpret_cast<float *>(smem + L.off_red);                    // [2][kNcw][MT]
-    double *nred = reinterpret_cast<double *>(red + 2 * kNcw * MT);              // [kNcw][MT]
+    double *red = reinterpret_cast<double *>(smem + L.off_red);                  // [2][kNcw][MT]
+    double *nred = red + 2 * kNcw * MT;                                          // [kNcw][MT]
     float *s_scale = reinterpret_cast<float *>(nred + kNcw * MT);                // [MT]
     uint8_t *ring = smem + L.off_ring;
 
@@ -145,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int m = 0; m < M; ++m) {
             double s = 0.0;
             for (int i = tid; i < K; i += nct) {
-                const float v = x[(size_t)m * ldx + i];
+                const float v = __ldcg(x + (size_t)m * ldx + i);
                 s += (double)__fmul_rn(v, v);
             }
             s = warp_sum_d(s);
@@ -165,10 +172,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int i = b * 32 + lane;
         float v;
         if (in_mode == IN_SWIGLU) {
-            const float g = x[(size_t)m * ldx + 2 * i], u = x[(size_t)m * ldx + 2 * i + 1];
+            const float g = __ldcg(x + (size_t)m * ldx + 2 * i), u = __ldcg(x + (size_t)m * ldx + 2 * i + 1);
             v = __fmul_rn(silu(g), u);
         } else {
-            v = x[(size_t)m * ldx + i];
+            v = __ldcg(x + (size_t)m * ldx + i);
             if (in_mode == IN_RMSNORM) v = __fmul_rn(__fmul_rn(v, s_scale[m]), norm_w[i]);
         }
         if (act_out != nullptr && blockIdx.x == 0) act_out[(size_t)m * K + i] = v;
@@ -193,9 +200,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!broken && !mbar_wait(&full[slot], (t / kStages) & 1, err, ERR_WAIT_FULL)) broken = true;
         const int8_t *sq = reinterpret_cast<const int8_t *>(ring + (size_t)slot * L.stage_bytes);
         const __half *sd = reinterpret_cast<const __half *>(sq + (size_t)S * K);
-        float acc[MT];
+        double acc[MT];
 #pragma unroll
-        for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+        for (int m = 0; m < MT; ++m) acc[m] = 0.0;
         if (!broken && row_local < rows) {
             const int8_t *wrow = sq + (size_t)row_local * K;
             const __half *drow = sd + (size_t)row_local * NB;
@@ -220,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                             s = dp4a(wv.w, xv.w, s);
                         }
                         s += __shfl_xor_sync(0xffffffffu, s, 1);
-                        if (valid && !(lane & 1)) acc[m] += (float)s * (dw * xd[m * NB + (c >> 1)]);
+                        if (valid && !(lane & 1)) acc[m] += (double)s * (double)(dw * xd[m * NB + (c >> 1)]);
                     }
                 }
             }
@@ -228,17 +235,17 @@ __global__ void __launch_bounds__(kThreads, 2)
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
 #pragma unroll
-        for (int m = 0; m < MT; ++m) acc[m] = warp_sum(acc[m]);
+        for (int m = 0; m < MT; ++m) acc[m] = warp_sum_d(acc[m]);
         if (WPR == 1) {
             if (lane == 0 && row_local < rows && !broken) {
                 const int r = rb + row_local;
                 for (int m = 0; m < M; ++m) {
-                    const float v = acc[m];
-                    y[(size_t)m * ldy + r] = res ? res[(size_t)m * ldres + r] + v : v;
+                    const float v = (float)acc[m];
+                    y[(size_t)m * ldy + r] = res ? __ldcg(res + (size_t)m * ldres + r) + v : v;
                 }
             }
         } else {
-            float *rr = red + (t & 1) * kNcw * MT;
+            double *rr = red + (t & 1) * kNcw * MT;
             if (lane == 0) {
 #pragma unroll
                 for (int m = 0; m < MT; ++m) rr[warp * MT + m] = acc[m];
@@ -247,9 +254,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (slice == 0 && lane == 0 && row_local < rows && !broken) {
                 const int r = rb + row_local;
                 for (int m = 0; m < M; ++m) {
-                    float v = rr[(row_local * WPR) * MT + m];
-                    for (int s2 = 1; s2 < WPR; ++s2) v += rr[(row_local * WPR + s2) * MT + m];
-                    y[(size_t)m * ldy + r] = res ? res[(size_t)m * ldres + r] + v : v;
+                    double a = rr[(row_local * WPR) * MT + m];
+                    for (int s2 = 1; s2 < WPR; ++s2) a += rr[(row_local * WPR + s2) * MT + m];
+                    const float v = (float)a;
+                    y[(size_t)m * ldy + r] = res ? __ldcg(res + (size_t)m * ldres + r) + v : v;
                 }
             }
         }

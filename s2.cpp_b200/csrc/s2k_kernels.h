@@ -69,7 +69,8 @@ struct QkPrepArgs {
     int T = 1, H = 0, Hkv = 0, hd = 128;
     const float *q_norm = nullptr, *k_norm = nullptr;  // null: no qk-norm
     float eps = 0.f;
-    float theta_scale = 1.f;
+    const float2 *rope = nullptr;  // [rope_positions][hd/2] (cos, sin)
+    int rope_positions = 0;
     const int *pos_base = nullptr;  // device: position of token 0 (n_past); null = 0
     int pos_add = 0;                // added to *pos_base
     float *kcur = nullptr, *vcur = nullptr;  // f32 [*][Hkv][hd] at index cur_base + t
@@ -92,9 +93,13 @@ struct AttnArgs {
     const float *kcur = nullptr, *vcur = nullptr;  // f32 [*][Hkv][hd], position n_cached + j at index j
     int cur_base = 0;  // token t attends to cur indices [0, cur_base + t]
     int n_splits = 1;
-    float *part = nullptr;  // scratch [T][H][n_splits][hd + 2]
+    float *scores = nullptr;  // scratch [T][H][ld_scores]
+    int ld_scores = 0;        // >= longest key range of the call
+    float *stats = nullptr;   // scratch [T][H][2] (max, 1/sum)
+    double *part = nullptr;   // scratch [T][H][n_splits][hd]
     int *counters = nullptr;  // scratch [T][Hkv], zero between launches
-    float *out = nullptr;  // [T][H*hd]
+    int *counters2 = nullptr; // scratch [T][Hkv], zero between launches
+    float *out = nullptr;     // [T][H*hd]
     const int *done = nullptr;
     int *err = nullptr;
 };

@@ -7,7 +7,9 @@
 //       semantic mask, 1/sqrt(num_codebooks+1) scale for semantic tokens)
 //   Fast input rows        src/s2_model.cpp:1139-1157 ([hidden ; fast_emb[prefix]],
 //       no per-codebook offset)
-//   sample_token           src/s2_sampler.cpp:42-99
+//   sample_token           src/s2_sampler.cpp:42-99 (exp via det_expf, the
+//       normaliser of the T=1 softmax summed in double and rounded once, so
+//       the CPU oracle reproduces the same draw)
 //   frame loop             src/s2_generate.cpp:57-183 (semantic mask, im_end
 //       blocking before min_tokens_before_end, RAS: window 10, resample at
 //       T=1.0 / top-p 0.9 when a semantic token repeats, sem_code clamp)
@@ -28,9 +30,9 @@ __device__ __forceinline__ float deq_q8_0(const DevMat &w, long long row, int co
 __global__ void embed_slow_kernel(EmbedArgs a, DevMat E, DevMat C) {
     pdl_launch_dependents();
     pdl_wait();
-    if (a.done && *a.done) return;
+    if (a.done && __ldcg(a.done)) return;
     const int t = blockIdx.x, dim = E.cols, stride = a.ncb + 1;
-    int tok = a.tokens[t * stride];
+    int tok = __ldcg(a.tokens + t * stride);
     if (tok < 0 || tok >= E.rows) {
         if (threadIdx.x == 0 && a.err) atomicOr(a.err, ERR_BAD_TOKEN);
         tok = 0;
@@ -40,7 +42,7 @@ __global__ void embed_slow_kernel(EmbedArgs a, DevMat E, DevMat C) {
     bool ok = true;
     if (sem) {
         for (int cb = 0; cb < a.ncb; ++cb) {
-            ids[cb] = a.tokens[t * stride + 1 + cb] + cb * a.cb_size;
+            ids[cb] = __ldcg(a.tokens + t * stride + 1 + cb) + cb * a.cb_size;
             if (ids[cb] < 0 || ids[cb] >= C.rows) ok = false;
         }
     }
@@ -80,13 +82,13 @@ __global__ void embed_fast_kernel(DevMat F, const float *hidden, const int *code
                                   const int *done, int *err) {
     pdl_launch_dependents();
     pdl_wait();
-    if (done && *done) return;
+    if (done && __ldcg(done)) return;
     const int r = blockIdx.x;
     if (hidden && r == 0) {
-        for (int i = threadIdx.x; i < dim; i += blockDim.x) x[i] = hidden[i];
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) x[i] = __ldcg(hidden + i);
         return;
     }
-    int c = codes[code0 + r - (hidden ? 1 : 0)];
+    int c = __ldcg(codes + code0 + r - (hidden ? 1 : 0));
     if (c < 0 || c >= F.rows) {
         if (threadIdx.x == 0 && err) atomicOr(err, ERR_BAD_TOKEN);
         c = 0;
@@ -121,6 +123,7 @@ struct SampSmem {
     int idx[kSampMax];
     float rf[32];
     int ri[32];
+    double rd[32];
     int result;
 };
 
@@ -204,20 +207,21 @@ __device__ int block_sample(SampSmem &sm, int n, F cand, float temp, float top_p
         }
     }
     const float mx = sm.key[0];
-    float part = 0.f;
-    for (int i = tid; i < n; i += nt) part += expf(sm.key[i] - mx);
-    part = warp_sum(part);
-    if (lane == 0) sm.rf[warp] = part;
+    double part = 0.0;
+    for (int i = tid; i < n; i += nt) part += (double)det_expf(__fsub_rn(sm.key[i], mx));
+    part = warp_sum_d(part);
+    if (lane == 0) sm.rd[warp] = part;
     __syncthreads();
     if (tid == 0) {
-        float S = 0.f;
-        for (int w = 0; w < nw; ++w) S += sm.rf[w];
+        double Sd = 0.0;
+        for (int w = 0; w < nw; ++w) Sd += sm.rd[w];
+        const float S = (float)Sd;
         const int k = top_k > 0 ? min(top_k, n) : n;
         const float tp = fminf(fmaxf(top_p, 0.f), 1.f);
         float cum = 0.f;
         int nf = 0;
         for (int i = 0; i < k; ++i) {
-            float p = expf(sm.key[i] - mx);
+            float p = det_expf(__fsub_rn(sm.key[i], mx));
             if (S > 0.f) p = __fdiv_rn(p, S);
             cum = __fadd_rn(cum, p);
             if (i > 0 && cum > tp) break;
@@ -226,10 +230,10 @@ __device__ int block_sample(SampSmem &sm, int n, F cand, float temp, float top_p
         if (nf == 0) nf = 1;
         const float m2 = sm.key[0];
         float s = 0.f;
-        for (int i = 0; i < nf; ++i) s = __fadd_rn(s, expf(__fdiv_rn(sm.key[i] - m2, temp)));
+        for (int i = 0; i < nf; ++i) s = __fadd_rn(s, det_expf(__fdiv_rn(__fsub_rn(sm.key[i], m2), temp)));
         float sp = 0.f;
         for (int i = 0; i < nf; ++i) {
-            float e = expf(__fdiv_rn(sm.key[i] - m2, temp));
+            float e = det_expf(__fdiv_rn(__fsub_rn(sm.key[i], m2), temp));
             if (s > 0.f) e = __fdiv_rn(e, s);
             sp = __fadd_rn(sp, e);
         }
@@ -237,14 +241,14 @@ __device__ int block_sample(SampSmem &sm, int n, F cand, float temp, float top_p
         if (sp > 0.f) {
             double tot = 0.0;
             for (int i = 0; i < nf; ++i) {
-                float e = expf(__fdiv_rn(sm.key[i] - m2, temp));
+                float e = det_expf(__fdiv_rn(__fsub_rn(sm.key[i], m2), temp));
                 if (s > 0.f) e = __fdiv_rn(e, s);
                 tot += (double)__fdiv_rn(e, sp);
             }
             pick = nf - 1;
             double c = 0.0;
             for (int i = 0; i < nf - 1; ++i) {
-                float e = expf(__fdiv_rn(sm.key[i] - m2, temp));
+                float e = det_expf(__fdiv_rn(__fsub_rn(sm.key[i], m2), temp));
                 if (s > 0.f) e = __fdiv_rn(e, s);
                 c += (double)__fdiv_rn(e, sp) / tot;
                 if (c >= u) { pick = i; break; }
@@ -285,16 +289,27 @@ __device__ double philox_uniform(unsigned long long seed, unsigned frame, unsign
 
 enum { RNG_MAIN = 0, RNG_RAS = 1, RNG_FAST0 = 2 };
 
+// Frame-loop state is written by the previous kernels of the same PDL chain:
+// read it through L2 (ld.global.cg), never from a possibly stale L1 line.
+__device__ __forceinline__ SampleCfg load_cfg(const SampleCfg *p) {
+    SampleCfg c;
+    const int *w = reinterpret_cast<const int *>(p);
+    int *o = reinterpret_cast<int *>(&c);
+#pragma unroll
+    for (int i = 0; i < (int)(sizeof(SampleCfg) / 4); ++i) o[i] = __ldcg(w + i);
+    return c;
+}
+
 struct SlowCand {
     const float *logits;
     int sem_begin, nsem, im_end, extra, block;
     __device__ void operator()(int i, float &v, int &ix) const {
         if (i < nsem) {
             ix = sem_begin + i;
-            v = (block && ix == im_end) ? -INFINITY : logits[ix];
+            v = (block && ix == im_end) ? -INFINITY : __ldcg(logits + ix);
         } else {
             ix = im_end;
-            v = block ? -INFINITY : logits[im_end];
+            v = block ? -INFINITY : __ldcg(logits + im_end);
         }
     }
 };
@@ -303,7 +318,7 @@ struct DenseCand {
     const float *logits;
     __device__ void operator()(int i, float &v, int &ix) const {
         ix = i;
-        v = logits[i];
+        v = __ldcg(logits + i);
     }
 };
 
@@ -324,8 +339,8 @@ __global__ void __launch_bounds__(kSampThreads) sample_main_kernel(const float *
     SampSmem &sm = *reinterpret_cast<SampSmem *>(smem_raw);
     pdl_launch_dependents();
     pdl_wait();
-    SeqState &st = sd->state;
-    const SampleCfg c = sd->cfg;
+    volatile SeqState &st = sd->state;
+    const SampleCfg c = load_cfg(&sd->cfg);
     if (st.done) return;
     const int f = st.n_frames;
     const int block = f < c.min_tokens_before_end;
@@ -337,10 +352,11 @@ __global__ void __launch_bounds__(kSampThreads) sample_main_kernel(const float *
         if (threadIdx.x == 0) {
             st.main_token = tok;
             st.done = 1;
-            if (sd->host) {
-                sd->host->n_frames = f;
+            HostStatus *hs = (HostStatus *)__ldcg((const unsigned long long *)&sd->host);
+            if (hs) {
+                hs->n_frames = f;
                 __threadfence_system();
-                sd->host->done = 1;
+                hs->done = 1;
             }
         }
         return;
@@ -370,8 +386,8 @@ __global__ void __launch_bounds__(kSampThreads) sample_fast_kernel(const float *
     SampSmem &sm = *reinterpret_cast<SampSmem *>(smem_raw);
     pdl_launch_dependents();
     pdl_wait();
-    SeqState &st = sd->state;
-    const SampleCfg c = sd->cfg;
+    volatile SeqState &st = sd->state;
+    const SampleCfg c = load_cfg(&sd->cfg);
     if (st.done) return;
     DenseCand cand{logits};
     const int tok = block_sample(sm, c.cb_size, cand, c.temperature, c.top_p, c.top_k,
@@ -382,8 +398,8 @@ __global__ void __launch_bounds__(kSampThreads) sample_fast_kernel(const float *
 __global__ void frame_commit_kernel(SeqDev *sd) {
     pdl_launch_dependents();
     pdl_wait();
-    SeqState &st = sd->state;
-    const SampleCfg c = sd->cfg;
+    volatile SeqState &st = sd->state;
+    const SampleCfg c = load_cfg(&sd->cfg);
     if (st.done) return;
     const int f = st.n_frames;
     const int i = threadIdx.x;
@@ -395,15 +411,17 @@ __global__ void frame_commit_kernel(SeqDev *sd) {
     if (i == 0) {
         st.step_in[0] = st.main_token;
         st.n_frames = f + 1;
-        if (sd->host) sd->host->n_frames = f + 1;
+        HostStatus *hs = (HostStatus *)__ldcg((const unsigned long long *)&sd->host);
+        if (hs) hs->n_frames = f + 1;
     }
 }
 
 __global__ void advance_kernel(SeqDev *sd, int T, const int *done) {
     pdl_launch_dependents();
     pdl_wait();
-    if (done && *done) return;
-    sd->state.n_past += T;
+    if (done && __ldcg(done)) return;
+    volatile SeqState &st = sd->state;
+    st.n_past = st.n_past + T;
 }
 
 static cudaLaunchConfig_t pdl_cfg(dim3 g, dim3 b, size_t smem, cudaStream_t st, cudaLaunchAttribute *attr) {

@@ -32,7 +32,7 @@ EXPORTED = [
     "s2k_model_finalize", "s2k_model_free", "s2k_model_get_hparams", "s2k_model_weight_bytes",
     "s2k_model_stream", "s2k_seq_create", "s2k_seq_reset", "s2k_seq_free", "s2k_seq_n_past", "s2k_eval",
     "s2k_fast_decode", "s2k_generate", "s2k_generate_device", "s2k_sample", "s2k_launch_count",
-    "s2k_profile_gemv",
+    "s2k_profile_gemv", "s2k_debug_copy",
 ]
 
 
@@ -104,6 +104,7 @@ def lib() -> ctypes.CDLL:
         "s2k_launch_count": ([i32], ctypes.c_uint64),
         "s2k_profile_gemv": ([vp, i32, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                               ctypes.POINTER(i32)], i32),
+        "s2k_debug_copy": ([vp, vp, ctypes.c_char_p, vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)], i32),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -261,6 +262,16 @@ class SlowARModel:
 
     def _max_seq(self) -> int:
         return getattr(self, "_max_seq_len", 0)
+
+    def debug_buffer(self, name: str, dtype=np.float32, nbytes: int = 1 << 30) -> np.ndarray:
+        """Copy of a named device buffer (see s2k_debug_copy)."""
+        buf = np.empty(nbytes // np.dtype(dtype).itemsize, dtype=dtype) if nbytes < (1 << 30) else None
+        if buf is None:
+            # size probe: copy into a small buffer first is not possible; allocate generously
+            buf = np.empty((256 << 20) // np.dtype(dtype).itemsize, dtype=dtype)
+        got = ctypes.c_size_t(0)
+        _check(lib().s2k_debug_copy(self._m, self._seq, name.encode(), _ptr(buf), buf.nbytes, ctypes.byref(got)))
+        return buf[: got.value // np.dtype(dtype).itemsize].copy()
 
     def profile_gemv(self, reps: int = 5):
         """(bytes per pass, ms per pass, launches per pass) of the Slow-step GEMVs."""
