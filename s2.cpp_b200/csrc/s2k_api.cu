@@ -341,15 +341,16 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         f1.ldx = dim;
         f1.in_mode = IN_RMSNORM;
         f1.norm_w = L.ffn_norm;
+        f1.epi = EPI_SWIGLU;
         f1.y = w.ff_buf;
-        f1.ldy = 2 * w.ff;
+        f1.ldy = w.ff;
         if ((e = launch_gemv(f1, m->num_sms, st))) return e;
 
         GemvArgs f2 = g;
         f2.w = &L.w2;
         f2.x = w.ff_buf;
-        f2.ldx = 2 * w.ff;
-        f2.in_mode = IN_SWIGLU;
+        f2.ldx = w.ff;
+        f2.in_mode = IN_PLAIN;
         f2.norm_w = nullptr;
         f2.y = w.x;
         f2.ldy = dim;
@@ -1113,10 +1114,11 @@ S2K_API s2k_status s2k_profile_gemv(s2k_model *m, int32_t reps, double *bytes_pe
             o.res = w.x; o.ldres = w.dim;
             if ((e = launch_gemv(o, m->num_sms, m->stream))) return e;
             GemvArgs f1 = g;
-            f1.w = &L.w13; f1.x = w.h; f1.ldx = w.dim; f1.norm_w = L.ffn_norm; f1.y = w.ff_buf; f1.ldy = 2 * w.ff;
+            f1.w = &L.w13; f1.x = w.h; f1.ldx = w.dim; f1.norm_w = L.ffn_norm; f1.epi = EPI_SWIGLU; f1.y = w.ff_buf;
+            f1.ldy = w.ff;
             if ((e = launch_gemv(f1, m->num_sms, m->stream))) return e;
             GemvArgs f2 = g;
-            f2.w = &L.w2; f2.x = w.ff_buf; f2.ldx = 2 * w.ff; f2.in_mode = IN_SWIGLU; f2.norm_w = nullptr; f2.y = w.x;
+            f2.w = &L.w2; f2.x = w.ff_buf; f2.ldx = w.ff; f2.in_mode = IN_PLAIN; f2.norm_w = nullptr; f2.y = w.x;
             f2.ldy = w.dim; f2.res = w.h; f2.ldres = w.dim;
             if ((e = launch_gemv(f2, m->num_sms, m->stream))) return e;
             if (count) {
@@ -1169,7 +1171,7 @@ S2K_API s2k_status s2k_debug_copy(s2k_model *m, s2k_seq *s, const char *name, vo
     else if (n == "h") pick(w.h, (size_t)w.T * w.dim * 4);
     else if (n == "qkv") pick(w.qkv, (size_t)w.T * (w.qs + 2 * w.kvs) * 4);
     else if (n == "attn") pick(w.attn, (size_t)w.T * w.qs * 4);
-    else if (n == "ff") pick(w.ff_buf, (size_t)w.T * 2 * w.ff * 4);
+    else if (n == "ff") pick(w.ff_buf, (size_t)w.T * w.ff * 4);
     else if (n == "kcur") pick(w.kcur, (size_t)w.T * w.kvs * 4);
     else if (n == "vcur") pick(w.vcur, (size_t)w.T * w.kvs * 4);
     else if (n == "logits") pick(m->logits, (size_t)hp.vocab_size * 4);
@@ -1178,7 +1180,7 @@ S2K_API s2k_status s2k_debug_copy(s2k_model *m, s2k_seq *s, const char *name, vo
     else if (n == "fh") pick(f.h, (size_t)f.T * f.dim * 4);
     else if (n == "fqkv") pick(f.qkv, (size_t)f.T * (f.qs + 2 * f.kvs) * 4);
     else if (n == "fattn") pick(f.attn, (size_t)f.T * f.qs * 4);
-    else if (n == "fff") pick(f.ff_buf, (size_t)f.T * 2 * f.ff * 4);
+    else if (n == "fff") pick(f.ff_buf, (size_t)f.T * f.ff * 4);
     else if (n == "flogits") pick(m->flogits, (size_t)hp.codebook_size * 4);
     else if ((n == "kv_k" || n == "kv_v") && s) {
         const size_t page_elems = (size_t)hp.block_count * hp.head_count_kv * kPage * hp.head_dim;

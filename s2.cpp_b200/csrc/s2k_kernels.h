@@ -23,7 +23,10 @@ struct DevMat {
 enum GemvIn : int {
     IN_PLAIN = 0,    // activation = x
     IN_RMSNORM = 1,  // activation = (x * rsqrt(mean(x^2)+eps)) * norm_w
-    IN_SWIGLU = 2,   // activation[i] = silu(x[2i]) * x[2i+1]   (x = interleaved gate/up)
+};
+enum GemvEpi : int {
+    EPI_STORE = 0,   // y[r] = W[r].x  (+ res[r] when res is given)
+    EPI_SWIGLU = 1,  // rows interleaved (gate, up): y[i] = silu(W[2i].x) * W[2i+1].x
 };
 
 struct GemvArgs {
@@ -34,6 +37,7 @@ struct GemvArgs {
     int in_mode = IN_PLAIN;
     const float *norm_w = nullptr;
     float eps = 0.f;
+    int epi = EPI_STORE;
     float *y = nullptr;  // [M][ldy]
     int ldy = 0;
     const float *res = nullptr;  // optional residual [M][ldres], y = res + W.x
