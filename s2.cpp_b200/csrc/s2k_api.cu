@@ -5,6 +5,7 @@
 #include "s2k_common.cuh"
 #include "s2k_device.h"
 #include "s2k_kernels.h"
+#include "s2k_mega.h"
 
 #include <algorithm>
 #include <atomic>
@@ -127,6 +128,11 @@ struct s2k_seq {
     cudaGraphExec_t frame_exec = nullptr;
     size_t frame_nodes = 0;
     int frame_gen = -1;
+    // persistent-kernel frame program: segments of ops in device memory
+    MegaOp *mega_ops = nullptr;
+    MegaCtl *mega_ctl = nullptr;
+    std::vector<int> seg_start, seg_len, seg_mt;
+    bool use_mega = false;
     KvPaged kv() const {
         KvPaged p;
         p.k = k;
@@ -738,6 +744,7 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     }
     CU(gemv_setup());
     CU(sampler_setup());
+    CU(mega_setup());
     if (m->staging) {
         m->release(m->staging);
         m->staging = nullptr;
@@ -832,6 +839,8 @@ S2K_API void s2k_seq_free(s2k_seq *s) {
     m->release(s->dev);
     m->release(s->codes);
     m->release(s->prompt);
+    m->release(s->mega_ops);
+    m->release(s->mega_ctl);
     if (s->hstat) cudaFreeHost((void *)s->hstat);
     delete s;
 }
@@ -926,6 +935,193 @@ S2K_API s2k_status s2k_sample(s2k_model *m, const float *logits, int32_t n, floa
     return check_err_word(m);
 }
 
+// ---------------------------------------------------------------------------
+// persistent-kernel frame program
+// ---------------------------------------------------------------------------
+static MegaOp mk_gemv(const DevMat &w, const float *x, int ldx, int M, int in_mode, const float *nw, float eps,
+                      int epi, float *y, int ldy, const float *res, int ldres, float *act_out) {
+    MegaOp o;
+    memset(&o, 0, sizeof(o));
+    o.kind = MK_GEMV;
+    o.g.wq = w.q;
+    o.g.wd = w.d;
+    o.g.R = w.rows;
+    o.g.K = w.cols;
+    o.g.x = x;
+    o.g.ldx = ldx;
+    o.g.M = M;
+    o.g.in_mode = in_mode;
+    o.g.norm_w = nw;
+    o.g.eps = eps;
+    o.g.epi = epi;
+    o.g.y = y;
+    o.g.ldy = ldy;
+    o.g.res = res;
+    o.g.ldres = ldres;
+    o.g.act_out = act_out;
+    return o;
+}
+
+// One transformer stack (a4-a11 of the reference step) as persistent-kernel ops.
+static bool add_layers(s2k_model *m, s2k_seq *s, bool fast, int T, int pos_add, std::vector<MegaOp> &ops) {
+    const s2k_hparams &hp = m->hp;
+    Work &w = fast ? m->fw : m->sw;
+    const std::vector<Layer> &layers = fast ? m->fast_layers : m->layers;
+    const int H = fast ? hp.fast_head_count : hp.head_count;
+    const int Hkv = fast ? hp.fast_head_count_kv : hp.head_count_kv;
+    const int hd = fast ? hp.fast_head_dim : hp.head_dim;
+    const float eps = fast ? hp.fast_rms_norm_eps : hp.rms_norm_eps;
+    const int qkvs = w.qs + 2 * w.kvs, dim = w.dim;
+    for (size_t il = 0; il < layers.size(); ++il) {
+        const Layer &L = layers[il];
+        ops.push_back(mk_gemv(L.wqkv, w.x, dim, T, IN_RMSNORM, L.attn_norm, eps, EPI_STORE, w.qkv, qkvs, nullptr, 0,
+                              nullptr));
+        MegaOp a;
+        memset(&a, 0, sizeof(a));
+        a.kind = MK_ATTN;
+        a.a.qkv = w.qkv;
+        a.a.ldqkv = qkvs;
+        a.a.T = T;
+        a.a.H = H;
+        a.a.Hkv = Hkv;
+        a.a.hd = hd;
+        a.a.q_norm = L.q_norm;
+        a.a.k_norm = L.k_norm;
+        a.a.eps = eps;
+        a.a.scale = 1.0f / sqrtf((float)hd);
+        a.a.rope = fast ? m->rope_fast : m->rope_slow;
+        a.a.rope_positions = fast ? m->rope_fast_n : m->rope_slow_n;
+        a.a.pos_base = fast ? nullptr : &s->dev->state.n_past;
+        a.a.pos_add = pos_add;
+        a.a.n_cached_from_pos_base = fast ? 0 : 1;
+        a.a.kcur = fast ? m->fkcur[il] : w.kcur;
+        a.a.vcur = fast ? m->fvcur[il] : w.vcur;
+        a.a.cur_base = fast ? pos_add : 0;
+        if (!fast) {
+            a.a.kv_k = s->k;
+            a.a.kv_v = s->v;
+            a.a.block_table = s->block_table;
+            a.a.kv_layers = hp.block_count;
+            a.a.kv_pages = s->n_pages;
+        }
+        a.a.layer = (int)il;
+        a.a.scores = w.scores;
+        a.a.ld_scores = w.L;
+        a.a.out = w.attn;
+        if (T * H > w.T * w.H || hd != 128) return false;
+        ops.push_back(a);
+        ops.push_back(mk_gemv(L.wo, w.attn, w.qs, T, IN_PLAIN, nullptr, eps, EPI_STORE, w.h, dim, w.x, dim, nullptr));
+        ops.push_back(mk_gemv(L.w13, w.h, dim, T, IN_RMSNORM, L.ffn_norm, eps, EPI_SWIGLU, w.ff_buf, w.ff, nullptr, 0,
+                              nullptr));
+        ops.push_back(mk_gemv(L.w2, w.ff_buf, w.ff, T, IN_PLAIN, nullptr, eps, EPI_STORE, w.x, dim, w.h, dim, nullptr));
+    }
+    return true;
+}
+
+// Builds the segments of one frame: 9 Fast-AR passes and the Slow step.
+// Returns false (and the caller uses the per-op kernels) when a shape falls
+// outside the persistent kernel's limits.
+static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
+    const s2k_hparams &hp = m->hp;
+    std::vector<MegaOp> ops;
+    s->seg_start.clear();
+    s->seg_len.clear();
+    s->seg_mt.clear();
+    bool ok = true;
+    for (int p = 0; p + 1 < hp.num_codebooks; ++p) {
+        const int T = p == 0 ? 2 : 1, pos_add = p == 0 ? 0 : p + 1;
+        const int start = (int)ops.size();
+        MegaOp e;
+        memset(&e, 0, sizeof(e));
+        e.kind = MK_EMBED_FAST;
+        e.ef.fq = m->fast_embed.q;
+        e.ef.fd = m->fast_embed.d;
+        e.ef.f_rows = m->fast_embed.rows;
+        e.ef.hidden = p == 0 ? m->hidden : nullptr;
+        e.ef.codes = s->dev->state.codes;
+        e.ef.code0 = p;
+        e.ef.n_rows = T;
+        e.ef.dim = hp.fast_embedding_length;
+        e.ef.x = m->fw.x;
+        ops.push_back(e);
+        ok = ok && add_layers(m, s, true, T, pos_add, ops);
+        ops.push_back(mk_gemv(m->fast_out, m->fw.x + (size_t)(T - 1) * hp.fast_embedding_length,
+                              hp.fast_embedding_length, 1, IN_RMSNORM, m->fast_norm, hp.fast_rms_norm_eps, EPI_STORE,
+                              m->flogits, hp.codebook_size, nullptr, 0, nullptr));
+        s->seg_start.push_back(start);
+        s->seg_len.push_back((int)ops.size() - start);
+        s->seg_mt.push_back(T);
+    }
+    {
+        const int start = (int)ops.size();
+        MegaOp e;
+        memset(&e, 0, sizeof(e));
+        e.kind = MK_EMBED_SLOW;
+        e.es.eq = m->embed.q;
+        e.es.ed = m->embed.d;
+        e.es.e_rows = m->embed.rows;
+        e.es.dim = hp.embedding_length;
+        e.es.cq = hp.num_codebooks > 0 ? m->cb_embed.q : nullptr;
+        e.es.cd = hp.num_codebooks > 0 ? m->cb_embed.d : nullptr;
+        e.es.c_rows = hp.num_codebooks > 0 ? m->cb_embed.rows : 0;
+        e.es.tokens = s->dev->state.step_in;
+        e.es.T = 1;
+        e.es.ncb = hp.num_codebooks;
+        e.es.cb_size = hp.codebook_size;
+        e.es.sem_begin = hp.semantic_begin_id;
+        e.es.sem_end = hp.semantic_end_id;
+        e.es.scale_cb = hp.scale_codebook_embeddings;
+        e.es.sem_scale = 1.0f / sqrtf((float)(hp.num_codebooks + 1));
+        e.es.x = m->sw.x;
+        ops.push_back(e);
+        ok = ok && add_layers(m, s, false, 1, 0, ops);
+        ops.push_back(mk_gemv(m->embed, m->sw.x, hp.embedding_length, 1, IN_RMSNORM, m->norm, hp.rms_norm_eps,
+                              EPI_STORE, m->logits, hp.vocab_size, nullptr, 0, m->hidden));
+        MegaOp adv;
+        memset(&adv, 0, sizeof(adv));
+        adv.kind = MK_ADVANCE;
+        adv.adv.n_past = &s->dev->state.n_past;
+        adv.adv.T = 1;
+        ops.push_back(adv);
+        s->seg_start.push_back(start);
+        s->seg_len.push_back((int)ops.size() - start);
+        s->seg_mt.push_back(1);
+    }
+    for (const MegaOp &o : ops)
+        if (o.kind == MK_GEMV && !mega_gemv_ok(o.g)) ok = false;
+    s->use_mega = ok;
+    if (!ok) return S2K_OK;
+    m->release(s->mega_ops);
+    s->mega_ops = nullptr;
+    CU(m->alloc(&s->mega_ops, ops.size()));
+    CU(cudaMemcpy(s->mega_ops, ops.data(), ops.size() * sizeof(MegaOp), cudaMemcpyHostToDevice));
+    if (!s->mega_ctl) CU(m->alloc(&s->mega_ctl, 16));
+    return S2K_OK;
+}
+
+// The frame with the persistent kernel: one cooperative launch per segment,
+// the samplers between them.
+static cudaError_t enqueue_frame_mega(s2k_model *m, s2k_seq *s) {
+    const s2k_hparams &hp = m->hp;
+    cudaStream_t st = m->stream;
+    const int *done = &s->dev->state.done;
+    const int nseg = (int)s->seg_start.size();
+    cudaError_t e;
+    if ((e = cudaMemsetAsync(s->mega_ctl, 0, sizeof(MegaCtl) * nseg, st))) return e;
+    for (int p = 0; p + 1 < hp.num_codebooks; ++p) {
+        if ((e = launch_mega(s->mega_ops + s->seg_start[p], s->seg_len[p], s->seg_mt[p], s->mega_ctl + p, done,
+                             m->d_err, m->num_sms, st)))
+            return e;
+        if ((e = launch_sample_fast(m->flogits, s->dev, p + 1, m->d_err, st))) return e;
+    }
+    if ((e = launch_frame_commit(s->dev, st))) return e;
+    const int last = nseg - 1;
+    if ((e = launch_mega(s->mega_ops + s->seg_start[last], s->seg_len[last], s->seg_mt[last], s->mega_ctl + last, done,
+                         m->d_err, m->num_sms, st)))
+        return e;
+    return launch_sample_main(m->logits, s->dev, m->d_err, st);
+}
+
 // Frame graph: captured once per sequence; it reads everything that changes
 // per frame or per call (positions, tokens, sampling parameters, output
 // pointer) from the sequence's device state.
@@ -937,8 +1133,10 @@ static s2k_status ensure_frame_graph(s2k_model *m, s2k_seq *s) {
     }
     cudaGraph_t g = nullptr;
     const unsigned long long before = g_launches.load();
+    s2k_status brc = build_mega(m, s);
+    if (brc) return brc;
     CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-    cudaError_t e = enqueue_frame(m, s);
+    cudaError_t e = s->use_mega ? enqueue_frame_mega(m, s) : enqueue_frame(m, s);
     cudaError_t e2 = cudaStreamEndCapture(m->stream, &g);
     g_launches.store(before);
     if (e != cudaSuccess || e2 != cudaSuccess) {

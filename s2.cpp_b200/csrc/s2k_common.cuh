@@ -16,6 +16,7 @@ enum : int {
     ERR_BAD_TOKEN = 4,    // token / code id out of range
     ERR_BAD_POS = 8,      // position beyond the sequence's pages
     ERR_SAMPLER = 16,     // sampler found no finite candidate
+    ERR_GRID = 32,        // a grid barrier of the persistent kernel timed out
 };
 
 // ~2 s at 1.9 GHz: long enough never to fire on a healthy GPU, short enough

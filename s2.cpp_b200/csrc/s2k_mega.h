@@ -1,0 +1,116 @@
+// s2k_mega.h -- op descriptors of the persistent decode kernel (internal).
+//
+// A "segment" is a list of ops (a Fast-AR pass, or the Slow-AR step) run by
+// one cooperative launch of mega_kernel: one CTA per SM, a producer warp that
+// streams the weights of every GEMV op of the segment in order through a
+// shared-memory ring, and consumer warps that run the ops one after another
+// with a grid barrier between them.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "s2k_kernels.h"
+
+namespace s2k {
+
+enum MegaKind : int {
+    MK_GEMV = 1,
+    MK_ATTN = 2,
+    MK_EMBED_SLOW = 3,
+    MK_EMBED_FAST = 4,
+    MK_ADVANCE = 5,
+};
+
+struct MegaGemv {
+    const int8_t *wq;  // [R][K] int8
+    const __half *wd;  // [R][K/32]
+    int R, K;
+    const float *x;  // [M][ldx]
+    int ldx, M, in_mode;
+    const float *norm_w;
+    float eps;
+    int epi;
+    float *y;
+    int ldy;
+    const float *res;
+    int ldres;
+    float *act_out;
+};
+
+struct MegaAttn {
+    float *qkv;  // [T][ldqkv] raw projections
+    int ldqkv, T, H, Hkv, hd;
+    const float *q_norm, *k_norm;
+    float eps, scale;
+    const float2 *rope;
+    int rope_positions;
+    const int *pos_base;  // device n_past (Slow) or null
+    int pos_add;          // position of token 0 = *pos_base + pos_add
+    int n_cached_from_pos_base;  // 1: keys < *pos_base come from the paged cache
+    float *kcur, *vcur;   // f32 [positions][Hkv][hd]; index = cur_base + t
+    int cur_base;
+    __half *kv_k, *kv_v;  // paged f16 cache [page][layer][kv_head][16][hd] (Slow only)
+    const int *block_table;
+    int kv_layers, kv_pages;
+    int layer;
+    float *scores;        // scratch [T*H][ld_scores]
+    int ld_scores;
+    float *out;           // [T][H*hd]
+};
+
+struct MegaEmbedSlow {
+    const int8_t *eq;  // token embeddings (Q8_0 planes), [rows][dim]
+    const __half *ed;
+    int e_rows, dim;
+    const int8_t *cq;  // codebook embeddings, [c_rows][dim]
+    const __half *cd;
+    int c_rows;
+    const int *tokens;  // [T][ncb+1]
+    int T, ncb, cb_size, sem_begin, sem_end, scale_cb;
+    float sem_scale;
+    float *x;
+};
+
+struct MegaEmbedFast {
+    const int8_t *fq;  // fast_embeddings (Q8_0 planes), [f_rows][dim]
+    const __half *fd;
+    int f_rows;
+    const float *hidden;  // null: no hidden row
+    const int *codes;
+    int code0, n_rows, dim;
+    float *x;
+};
+
+struct MegaAdvance {
+    int *n_past;
+    int T;
+};
+
+struct MegaOp {
+    int kind;
+    int pad_;
+    union {
+        MegaGemv g;
+        MegaAttn a;
+        MegaEmbedSlow es;
+        MegaEmbedFast ef;
+        MegaAdvance adv;
+    };
+};
+
+// Grid-barrier counter of one segment launch (zeroed before the launch).
+struct MegaCtl {
+    unsigned int count;
+    unsigned int pad[31];
+};
+
+cudaError_t mega_setup();
+// Launch one segment: ops in device memory, ctl zeroed on `st` before.
+cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, const int *done, int *err, int num_sms,
+                        cudaStream_t st);
+// Host-side validation of a GEMV op for the persistent kernel.
+bool mega_gemv_ok(const MegaGemv &g);
+
+}  // namespace s2k
