@@ -30,6 +30,13 @@
  * any 1-ulp difference can flip an int8 activation and is then amplified
  * layer by layer.
  *
+ * Pinning: the block formats are pinned (gguf-py known-answer vectors).  The
+ * model-level math (eval / fast_decode / generate) is parity unpinned: the
+ * reference's ggml backend cannot be built here and the reference ships no
+ * golden vectors, so the restatement is checked by its own semantic tests
+ * (prefill vs incremental, sampler rules, stop rules) and the CUDA path is
+ * checked bit for bit against it.
+ *
  * RNG: the reference draws from a thread_local mt19937 seeded by
  * std::random_device (src/s2_sampler.cpp:94), which no test can pin.  Both
  * this oracle and the CUDA sampler instead draw u ~ U[0,1) from Philox4x32-10
