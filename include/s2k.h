@@ -186,6 +186,24 @@ S2K_API s2k_status s2k_generate_device(s2k_model *m, s2k_seq *s, const int32_t *
 S2K_API s2k_status s2k_sample(s2k_model *m, const float *logits, int32_t n, float temperature,
                               float top_p, int32_t top_k, double u, int32_t *token_out);
 
+/* Largest logits row s2k_sample_noalloc accepts (its fixed device scratch). */
+#define S2K_SAMPLE_NOALLOC_MAX_N 8192
+
+/* Allocation-free variant of s2k_sample; it has no counterpart in the
+ * reference.  Same arguments, result and tie break as s2k_sample, but it
+ * allocates no device memory: the logits staging row, the result slot and
+ * the error word live in one fixed file-scope device array of
+ * S2K_SAMPLE_NOALLOC_MAX_N floats + 256 bytes (32.25 KiB) per device.
+ * n > S2K_SAMPLE_NOALLOC_MAX_N is rejected with S2K_ERR_ARG.
+ * The first call on a device looks up that array's address (set-up); make
+ * it before any stream capture on that device.  The error word is cleared
+ * on the model stream at the start of every call.  The scratch is shared by
+ * every model on the device: calls that overlap in time (other threads,
+ * other models on the same device) race on it and must be serialised by the
+ * caller. */
+S2K_API s2k_status s2k_sample_noalloc(s2k_model *m, const float *logits, int32_t n, float temperature,
+                                      float top_p, int32_t top_k, double u, int32_t *token_out);
+
 /* Profiling hook for the dominant kernel (no reference counterpart): launches
  * every Slow-step weight GEMV (per layer wqkv, wo, w1|w3, w2, then the LM head)
  * `reps` times back to back on the model stream, as the decode step issues

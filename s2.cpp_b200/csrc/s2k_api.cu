@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -933,6 +934,52 @@ S2K_API s2k_status s2k_sample(s2k_model *m, const float *logits, int32_t n, floa
     CU(cudaMemcpyAsync(token_out, m->samp_out, 4, cudaMemcpyDeviceToHost, m->stream));
     CU(cudaStreamSynchronize(m->stream));
     return check_err_word(m);
+}
+
+// ---------------------------------------------------------------------------
+// allocation-free sampler entry: fixed per-device scratch in a static
+// __device__ array -- [0, 4*max) logits row, then the token slot and the
+// error word (the only part that must start at zero: cleared every call).
+// ---------------------------------------------------------------------------
+static_assert(S2K_SAMPLE_NOALLOC_MAX_N <= 8192, "the sampler kernel takes at most 8192 logits");
+constexpr size_t kNoAllocTokOff = (size_t)S2K_SAMPLE_NOALLOC_MAX_N * sizeof(float);
+static __device__ __align__(256) unsigned char g_sample_scratch[kNoAllocTokOff + 256];
+constexpr int kNoAllocMaxDevices = 64;
+static void *g_sample_scratch_ptr[kNoAllocMaxDevices];
+static std::mutex g_sample_scratch_mu;
+
+S2K_API s2k_status s2k_sample_noalloc(s2k_model *m, const float *logits, int32_t n, float temperature, float top_p,
+                                      int32_t top_k, double u, int32_t *token_out) {
+    if (!m || !logits || !token_out) return fail(S2K_ERR_ARG, "bad argument");
+    if (n <= 0 || n > S2K_SAMPLE_NOALLOC_MAX_N)
+        return fail(S2K_ERR_ARG, "s2k_sample_noalloc: n = %d outside its fixed scratch (1..%d logits)", n,
+                    S2K_SAMPLE_NOALLOC_MAX_N);
+    if (m->device < 0 || m->device >= kNoAllocMaxDevices) return fail(S2K_ERR_ARG, "device %d out of range", m->device);
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    void *base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_sample_scratch_mu);
+        if (!g_sample_scratch_ptr[m->device]) {
+            void *p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_sample_scratch);
+            if (e != cudaSuccess || !p)
+                return fail(S2K_ERR_CUDA, "cudaGetSymbolAddress(sampler scratch) failed: %s", cudaGetErrorString(e));
+            g_sample_scratch_ptr[m->device] = p;
+        }
+        base = g_sample_scratch_ptr[m->device];
+    }
+    float *d_logits = static_cast<float *>(base);
+    int *d_tok = reinterpret_cast<int *>(static_cast<unsigned char *>(base) + kNoAllocTokOff);
+    int *d_err = d_tok + 1;
+    int h[2] = {0, 0};
+    CU(cudaMemsetAsync(d_err, 0, sizeof(int), m->stream));
+    CU(cudaMemcpyAsync(d_logits, logits, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, m->stream));
+    CU(launch_sample_one(d_logits, n, temperature, top_p, top_k, u, d_tok, d_err, m->stream));
+    CU(cudaMemcpyAsync(h, d_tok, sizeof(h), cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    if (h[1]) return fail(S2K_ERR_ARG, "device reported invalid input (flags 0x%x)", h[1]);
+    *token_out = h[0];
+    return S2K_OK;
 }
 
 // ---------------------------------------------------------------------------

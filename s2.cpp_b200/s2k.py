@@ -23,6 +23,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libs2k.so")
 
 S2K_OK = 0
+SAMPLE_NOALLOC_MAX_N = 8192  # S2K_SAMPLE_NOALLOC_MAX_N
 STATUS = {-1: "ERR_ARG", -2: "ERR_OOM", -3: "ERR_CUDA", -4: "ERR_KV_FULL", -5: "ERR_STATE",
           -6: "ERR_TIMEOUT", -7: "ERR_UNSUPPORTED", -8: "ERR_NO_DEVICE"}
 
@@ -32,7 +33,7 @@ EXPORTED = [
     "s2k_model_finalize", "s2k_model_free", "s2k_model_get_hparams", "s2k_model_weight_bytes",
     "s2k_model_stream", "s2k_seq_create", "s2k_seq_reset", "s2k_seq_free", "s2k_seq_n_past", "s2k_eval",
     "s2k_fast_decode", "s2k_generate", "s2k_generate_device", "s2k_sample", "s2k_launch_count",
-    "s2k_profile_gemv", "s2k_debug_copy",
+    "s2k_profile_gemv", "s2k_debug_copy", "s2k_sample_noalloc",
 ]
 
 
@@ -101,6 +102,8 @@ def lib() -> ctypes.CDLL:
         "s2k_generate": ([vp, vp, vp, i32, ctypes.POINTER(_GenParams), vp, ctypes.POINTER(i32), FRAME_CB, vp], i32),
         "s2k_generate_device": ([vp, vp, vp, i32, ctypes.POINTER(_GenParams), vp, ctypes.POINTER(i32)], i32),
         "s2k_sample": ([vp, vp, i32, ctypes.c_float, ctypes.c_float, i32, ctypes.c_double, ctypes.POINTER(i32)], i32),
+        "s2k_sample_noalloc": ([vp, vp, i32, ctypes.c_float, ctypes.c_float, i32, ctypes.c_double,
+                                ctypes.POINTER(i32)], i32),
         "s2k_launch_count": ([i32], ctypes.c_uint64),
         "s2k_profile_gemv": ([vp, i32, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                               ctypes.POINTER(i32)], i32),
@@ -227,6 +230,16 @@ class SlowARModel:
         x = np.ascontiguousarray(logits, dtype=np.float32)
         tok = ctypes.c_int32(0)
         _check(lib().s2k_sample(self._m, _ptr(x), int(x.size), temperature, top_p, top_k, u, ctypes.byref(tok)))
+        return tok.value
+
+    def sample_noalloc(self, logits: np.ndarray, temperature: float, top_p: float, top_k: int,
+                       u: float = 0.0) -> int:
+        """`sample` through s2k_sample_noalloc: fixed device scratch, at most
+        SAMPLE_NOALLOC_MAX_N logits; concurrent calls on one device race."""
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        tok = ctypes.c_int32(0)
+        _check(lib().s2k_sample_noalloc(self._m, _ptr(x), int(x.size), temperature, top_p, top_k, u,
+                                        ctypes.byref(tok)))
         return tok.value
 
     # --- generate ---
