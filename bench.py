@@ -165,6 +165,8 @@ def main() -> None:
     ap.add_argument("--frames", type=int, default=FRAMES)
     ap.add_argument("--cpu-frames", type=int, default=2, help="frames in the CPU oracle sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--preset", choices=["s2pro", "mid"], default="s2pro",
+                    help="model shape; 'mid' (2+1 layers, real widths) is for small profiler captures only")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -188,7 +190,7 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
                                 device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
-    hp = synthetic.preset("s2pro")
+    hp = synthetic.preset(args.preset)
     threads = max(1, (os.cpu_count() or 8) // max(world, 1))
     t0 = time.time()
     tensors = build_weights(hp, threads)
@@ -200,7 +202,7 @@ def main() -> None:
         tensors = None
     frames = args.frames
     prompt = synthetic.text_prompt(hp, PROMPT, seed=7 + rank)  # this rank's utterance
-    m.init_kv_cache(PROMPT + frames)
+    m.init_kv_cache(PROMPT + frames + 1)  # + 1: the slot the kernel profile below writes
     d_prompt = torch.from_numpy(np.ascontiguousarray(prompt.T)).to(f"cuda:{local}")
     d_codes = torch.zeros((hp.num_codebooks, frames), dtype=torch.int32, device=f"cuda:{local}")
     stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
@@ -251,10 +253,16 @@ def main() -> None:
         e2e_s = float(t.item())
     e2e_value = world * args.steps * frames / e2e_s
 
-    # dominant kernel: the Slow-step GEMV chain (every weight GEMV of a step), events on its stream
-    gb, gms, glaunch = m.profile_gemv(reps=5)
+    # dominant kernel: the persistent decode kernel (mega_kernel), one launch per
+    # Fast-AR pass and one per Slow step; each launch event-timed on its stream
+    ms_s, ms_f, b_s, b_f = m.profile_frame(reps=5)
+    nf = hp.num_codebooks - 1
+    mk_bytes = (b_s + nf * b_f) / (nf + 1)
+    mk_ms = (ms_s + nf * ms_f) / (nf + 1)
     pk = peaks()
-    achieved = gb / (gms / 1e3) / 1e9
+    achieved = mk_bytes / (mk_ms / 1e3) / 1e9
+    # the standalone GEMV kernel of s2k_eval / s2k_fast_decode, for comparison
+    gb, gms, glaunch = m.profile_gemv(reps=5)
     fb = frame_bytes(hp, PROMPT, frames)
     step_bytes = fb  # + prefill weights, counted separately below
     frame_achieved = step_bytes / (ms_per_step / 1e3) / 1e9
@@ -271,15 +279,21 @@ def main() -> None:
             "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q8_0", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "prompt_tokens": PROMPT, "frames": frames, "batch_per_gpu": 1,
+            "config": {"workload": WORKLOAD if args.preset == "s2pro" else f"{args.preset} preset (profiling only)",
+                       "prompt_tokens": PROMPT, "frames": frames, "batch_per_gpu": 1,
                        "weights": "seeded N(0,0.02) -> Q8_0", "l2": "inputs larger than L2 (4.3 GB of weights per frame)",
                        "parallelism": f"request-level x{world}, no collectives"},
             "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": int(prompt.nbytes),
                     "d2h_bytes_per_step": int(hp.num_codebooks * frames * 4)},
-            "roofline": {"bound": "hbm", "kernel": "gemv_q8_0 (Slow-step weight GEMV chain)",
+            "roofline": {"bound": "hbm", "kernel": "mega_kernel (persistent decode kernel, 9 Fast-pass + 1 Slow-step "
+                                                   "launches per frame)",
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                         "peak_src": pk["src"], "traffic": None, "bytes_per_launch": gb / glaunch,
-                         "launches": glaunch, "ms_per_pass": gms},
+                         "peak_src": pk["src"], "traffic": None, "bytes_per_launch": mk_bytes,
+                         "launch_ms": mk_ms, "slow_launch": {"ms": ms_s, "bytes": b_s},
+                         "fast_launch": {"ms": ms_f, "bytes": b_f}},
+            "gemv_roofline": {"kernel": "gemv_q8_0 (standalone, s2k_eval path): Slow-step weight GEMV chain",
+                              "achieved": gb / (gms / 1e3) / 1e9, "frac": gb / (gms / 1e3) / 1e9 / pk["hbm_gbs"],
+                              "unit": "GB/s", "launches": glaunch, "ms_per_pass": gms},
             "frame_roofline": {"achieved": frame_achieved, "frac": frame_achieved / pk["hbm_gbs"], "unit": "GB/s",
                                "bytes_per_step": step_bytes},
             "cpu_baseline": cpu,

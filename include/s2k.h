@@ -212,6 +212,18 @@ S2K_API s2k_status s2k_sample_noalloc(s2k_model *m, const float *logits, int32_t
 S2K_API s2k_status s2k_profile_gemv(s2k_model *m, int32_t reps, double *bytes_per_pass,
                                     double *ms_per_pass, int32_t *launches_per_pass);
 
+/* Profiling hook for the persistent decode kernel (no reference counterpart).
+ * Needs a sequence that has run s2k_generate / s2k_generate_device (its frame
+ * program is built) with n_past < max_seq_len.  Launches `reps` times (1..64)
+ * the kernel's Fast-AR pass segment for codebook 1 and its Slow-step segment
+ * without the n_past advance, each bracketed by CUDA events on the model
+ * stream, and reports the mean device time of each and the algorithmic bytes
+ * each streams (weights at 34/32 B per Q8_0 weight; the Slow segment adds the
+ * f16 K/V of n_past cached positions).  The Slow segment rewrites the cache
+ * slot at n_past, which the next step writes anyway; n_past is unchanged. */
+S2K_API s2k_status s2k_profile_frame(s2k_model *m, s2k_seq *s, int32_t reps, double *ms_slow,
+                                     double *ms_fast, double *bytes_slow, double *bytes_fast);
+
 /* Debugging aid (no reference counterpart): copies up to nbytes of a named
  * device buffer to host memory.  Names: "x", "h", "qkv", "attn", "ff",
  * "kcur", "vcur", "logits", "hidden" (Slow workspace), "fx", "fh", "fqkv",

@@ -1402,6 +1402,61 @@ S2K_API s2k_status s2k_profile_gemv(s2k_model *m, int32_t reps, double *bytes_pe
     return check_err_word(m);
 }
 
+S2K_API s2k_status s2k_profile_frame(s2k_model *m, s2k_seq *s, int32_t reps, double *ms_slow, double *ms_fast,
+                                     double *bytes_slow, double *bytes_fast) {
+    if (!m || !s || reps <= 0 || reps > 64 || !ms_slow || !ms_fast || !bytes_slow || !bytes_fast)
+        return fail(S2K_ERR_ARG, "bad argument (1 <= reps <= 64)");
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    if (!s->frame_exec || s->frame_gen != m->ws_gen || !s->use_mega || s->seg_start.size() < 2)
+        return fail(S2K_ERR_STATE, "no persistent-kernel frame program for this sequence (run generate first)");
+    if (s->n_past >= s->max_seq_len)
+        return fail(S2K_ERR_KV_FULL, "profiling writes position n_past = %d; the sequence holds %d", s->n_past,
+                    s->max_seq_len);
+    const s2k_hparams &hp = m->hp;
+    const int nseg = (int)s->seg_start.size();
+    const int fseg = nseg > 2 ? 1 : 0, sseg = nseg - 1;
+    // the Slow segment ends with the n_past advance: leave it out
+    const int slow_len = s->seg_len[sseg] - 1;
+    double bs = (double)m->embed.bytes(), bf = (double)m->fast_out.bytes();
+    for (const Layer &L : m->layers) bs += (double)(L.wqkv.bytes() + L.wo.bytes() + L.w13.bytes() + L.w2.bytes());
+    for (const Layer &L : m->fast_layers) bf += (double)(L.wqkv.bytes() + L.wo.bytes() + L.w13.bytes() + L.w2.bytes());
+    bs += (double)s->n_past * hp.block_count * 2.0 * hp.head_count_kv * hp.head_dim * sizeof(__half);
+    std::vector<cudaEvent_t> ev(4 * (size_t)reps, nullptr);
+    for (auto &e : ev) CU(cudaEventCreate(&e));
+    cudaError_t err = cudaSuccess;
+    for (int r = 0; r < reps && err == cudaSuccess; ++r) {
+        MegaCtl *cf = s->mega_ctl + fseg, *cs = s->mega_ctl + sseg;
+        if ((err = cudaMemsetAsync(cf, 0, sizeof(MegaCtl), m->stream))) break;
+        if ((err = cudaEventRecord(ev[4 * r], m->stream))) break;
+        if ((err = launch_mega(s->mega_ops + s->seg_start[fseg], s->seg_len[fseg], s->seg_mt[fseg], cf, nullptr,
+                               m->d_err, m->num_sms, m->stream)))
+            break;
+        if ((err = cudaEventRecord(ev[4 * r + 1], m->stream))) break;
+        if ((err = cudaMemsetAsync(cs, 0, sizeof(MegaCtl), m->stream))) break;
+        if ((err = cudaEventRecord(ev[4 * r + 2], m->stream))) break;
+        if ((err = launch_mega(s->mega_ops + s->seg_start[sseg], slow_len, s->seg_mt[sseg], cs, nullptr, m->d_err,
+                               m->num_sms, m->stream)))
+            break;
+        err = cudaEventRecord(ev[4 * r + 3], m->stream);
+    }
+    if (err == cudaSuccess) err = cudaStreamSynchronize(m->stream);
+    double tf = 0, ts = 0;
+    for (int r = 0; r < reps && err == cudaSuccess; ++r) {
+        float a = 0, b = 0;
+        cudaEventElapsedTime(&a, ev[4 * r], ev[4 * r + 1]);
+        cudaEventElapsedTime(&b, ev[4 * r + 2], ev[4 * r + 3]);
+        tf += a;
+        ts += b;
+    }
+    for (auto &e : ev) cudaEventDestroy(e);
+    CU(err);
+    *ms_fast = tf / reps;
+    *ms_slow = ts / reps;
+    *bytes_fast = bf;
+    *bytes_slow = bs;
+    return check_err_word(m);
+}
+
 S2K_API s2k_status s2k_debug_copy(s2k_model *m, s2k_seq *s, const char *name, void *host, size_t nbytes,
                                   size_t *copied) {
     if (!m || !name || !host || !copied) return fail(S2K_ERR_ARG, "NULL argument");

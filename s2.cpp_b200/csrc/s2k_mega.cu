@@ -36,6 +36,7 @@ constexpr int kMNormMax = 4096;
 constexpr int kMMaxRows = 64;
 constexpr int kMaxT = 2;
 constexpr int kHD = 128;
+constexpr int kPtabMax = kMaxT * kMKMax / (int)sizeof(int);  // cached pages whose ids fit the staged table
 
 struct MStage {
     int S, WPR, BPL;
@@ -84,10 +85,12 @@ struct MSmem {
     // attention
     float aq[kHD];
     float ak[kMaxT][kHD], av[kMaxT][kHD];
-    double vpart[kMNC / kHD][kHD];
+    double vpart[kMW][kHD];
     float red_f[kMW];
     double red_d[kMW];
 };
+
+static_assert(sizeof(MSmem) <= 227 * 1024, "persistent kernel shared memory exceeds the per-CTA limit");
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     unsigned v;
@@ -449,8 +452,16 @@ __device__ __forceinline__ const float *key_ptr_f32(const MegaAttn &a, MSmem &sm
     return value ? sm.av[c - a.cur_base] : sm.ak[c - a.cur_base];
 }
 
+// Row of cached key/value position j for kv head g in the paged f16 cache.
+__device__ __forceinline__ const __half *kv_row(const MegaAttn &a, const __half *base, const int *ptab, int g, int j) {
+    const int pg = j / kPage, slot = j - pg * kPage;
+    const int page = pg < kPtabMax ? ptab[pg] : __ldcg(a.block_table + pg);
+    return base + ((((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage + slot) * kHD;
+}
+
 __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int *const ptab = reinterpret_cast<int *>(sm.xq);
     const int units = a.T * a.H;
     const int grp = a.H / a.Hkv;
     for (int u = cta; u < units; u += G) {
@@ -458,6 +469,9 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
         const int base = a.pos_base ? __ldcg(a.pos_base) : 0;
         const int nc = a.n_cached_from_pos_base ? base : 0;
         const int pos0 = base + a.pos_add;
+        // page table of the cached keys, staged in the (idle) GEMV activation buffer
+        const int npg = a.kv_k ? (nc + kPage - 1) / kPage : 0;
+        for (int i = tid; i < min(npg, kPtabMax); i += kMNC) ptab[i] = __ldcg(a.block_table + i);
         // 1. q of (t, h): threads 0..63 (pair i)
         {
             const bool act = tid < 64;
@@ -523,13 +537,15 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
         for (int j = tid; j < Lk; j += kMNC) {
             double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
             if (j < nc) {
-                const int page = __ldcg(a.block_table + j / kPage), slot = j % kPage;
-                const __half *kp =
-                    a.kv_k + ((((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage + slot) * kHD;
-#pragma unroll 4
-                for (int d = 0; d < kHD; d += 8) {
-                    const uint4 raw = __ldcg(reinterpret_cast<const uint4 *>(kp + d));
-                    const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+                // the whole 256-byte key row in flight at once
+                const uint4 *kp = reinterpret_cast<const uint4 *>(kv_row(a, a.kv_k, ptab, g, j));
+                uint4 raw[kHD / 8];
+#pragma unroll
+                for (int c = 0; c < kHD / 8; ++c) raw[c] = __ldcg(kp + c);
+#pragma unroll
+                for (int c = 0; c < kHD / 8; ++c) {
+                    const int d = 8 * c;
+                    const __half2 *hh = reinterpret_cast<const __half2 *>(&raw[c]);
                     const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
                     const float2 f2 = __half22float2(hh[2]), f3 = __half22float2(hh[3]);
                     s0 += (double)f0.x * (double)sm.aq[d] + (double)f0.y * (double)sm.aq[d + 1];
@@ -571,29 +587,63 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
         const float inv = (float)(1.0 / tot);
         for (int j = tid; j < Lk; j += kMNC) sc[j] = __fmul_rn(det_expf(__fsub_rn(sc[j], mx)), inv);
         named_sync(3, kMNC);
-        // 4. values: thread (d, key group kg)
+        // 4. values: warp w takes keys w, w + kMW, ...; lane takes dims 4*lane..4*lane+3.
+        // kVU keys per warp are loaded before any is used.
         {
-            constexpr int NKG = kMNC / kHD;
-            const int d = tid & (kHD - 1), kg = tid >> 7;
-            double acc = 0.0;
-            for (int j = kg; j < Lk; j += NKG) {
-                float vv;
-                if (j < nc) {
-                    const int page = __ldcg(a.block_table + j / kPage), slot = j % kPage;
-                    vv = __half2float(__ldcg(a.kv_v + ((((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage + slot) * kHD + d));
-                } else {
-                    const int c = j - nc;
-                    const float *vp = key_ptr_f32(a, sm, c, g, true);
-                    vv = c < a.cur_base ? __ldcg(vp + d) : vp[d];
+            constexpr int kVU = 8;
+            double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
+            int j = warp;
+            for (; j + (kVU - 1) * kMW < nc; j += kVU * kMW) {
+                uint2 raw[kVU];
+                float pr[kVU];
+#pragma unroll
+                for (int q = 0; q < kVU; ++q) {
+                    const int jj = j + q * kMW;
+                    raw[q] = __ldcg(reinterpret_cast<const uint2 *>(kv_row(a, a.kv_v, ptab, g, jj) + 4 * lane));
+                    pr[q] = sc[jj];
                 }
-                acc += (double)vv * (double)sc[j];
+#pragma unroll
+                for (int q = 0; q < kVU; ++q) {
+                    const __half2 *hh = reinterpret_cast<const __half2 *>(&raw[q]);
+                    const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
+                    const double pd = (double)pr[q];
+                    acc0 += (double)f0.x * pd;
+                    acc1 += (double)f0.y * pd;
+                    acc2 += (double)f1.x * pd;
+                    acc3 += (double)f1.y * pd;
+                }
             }
-            sm.vpart[kg][d] = acc;
+            for (; j < nc; j += kMW) {
+                const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(kv_row(a, a.kv_v, ptab, g, j) + 4 * lane));
+                const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+                const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
+                const double pd = (double)sc[j];
+                acc0 += (double)f0.x * pd;
+                acc1 += (double)f0.y * pd;
+                acc2 += (double)f1.x * pd;
+                acc3 += (double)f1.y * pd;
+            }
+            // keys of this call (f32): j = nc + c
+            for (int c = warp; c < Lk - nc; c += kMW) {
+                const float *vp = key_ptr_f32(a, sm, c, g, true) + 4 * lane;
+                const bool gl = c < a.cur_base;
+                const float v0 = gl ? __ldcg(vp) : vp[0], v1 = gl ? __ldcg(vp + 1) : vp[1];
+                const float v2 = gl ? __ldcg(vp + 2) : vp[2], v3 = gl ? __ldcg(vp + 3) : vp[3];
+                const double pd = (double)sc[nc + c];
+                acc0 += (double)v0 * pd;
+                acc1 += (double)v1 * pd;
+                acc2 += (double)v2 * pd;
+                acc3 += (double)v3 * pd;
+            }
+            sm.vpart[warp][4 * lane] = acc0;
+            sm.vpart[warp][4 * lane + 1] = acc1;
+            sm.vpart[warp][4 * lane + 2] = acc2;
+            sm.vpart[warp][4 * lane + 3] = acc3;
         }
         named_sync(3, kMNC);
         if (tid < kHD) {
             double o = sm.vpart[0][tid];
-            for (int k = 1; k < kMNC / kHD; ++k) o += sm.vpart[k][tid];
+            for (int k = 1; k < kMW; ++k) o += sm.vpart[k][tid];
             a.out[(size_t)t * a.H * kHD + (size_t)h * kHD + tid] = (float)o;
         }
         named_sync(3, kMNC);

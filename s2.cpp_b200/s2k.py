@@ -34,6 +34,7 @@ EXPORTED = [
     "s2k_model_stream", "s2k_seq_create", "s2k_seq_reset", "s2k_seq_free", "s2k_seq_n_past", "s2k_eval",
     "s2k_fast_decode", "s2k_generate", "s2k_generate_device", "s2k_sample", "s2k_launch_count",
     "s2k_profile_gemv", "s2k_debug_copy", "s2k_sample_noalloc",
+    "s2k_profile_frame",
 ]
 
 
@@ -108,6 +109,7 @@ def lib() -> ctypes.CDLL:
         "s2k_profile_gemv": ([vp, i32, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                               ctypes.POINTER(i32)], i32),
         "s2k_debug_copy": ([vp, vp, ctypes.c_char_p, vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)], i32),
+        "s2k_profile_frame": ([vp, vp, i32] + [ctypes.POINTER(ctypes.c_double)] * 4, i32),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -291,6 +293,14 @@ class SlowARModel:
         b, ms, n = ctypes.c_double(0), ctypes.c_double(0), ctypes.c_int32(0)
         _check(lib().s2k_profile_gemv(self._m, reps, ctypes.byref(b), ctypes.byref(ms), ctypes.byref(n)))
         return b.value, ms.value, n.value
+
+    def profile_frame(self, reps: int = 5):
+        """Persistent decode kernel, event-timed per launch: (ms Slow segment,
+        ms Fast pass, bytes Slow segment, bytes Fast pass).  Needs a prior
+        generate on this model's sequence with a free KV position."""
+        v = [ctypes.c_double(0) for _ in range(4)]
+        _check(lib().s2k_profile_frame(self._m, self._seq, reps, *[ctypes.byref(x) for x in v]))
+        return tuple(x.value for x in v)
 
     def generate_device(self, d_prompt_tm: int, cols: int, d_codes: int, max_new_tokens: int,
                         temperature: float = 0.0, top_p: float = 0.8, top_k: int = 30,
