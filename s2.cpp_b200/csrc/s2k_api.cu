@@ -523,15 +523,17 @@ static s2k_status upload_vec(s2k_model *m, float **dst, int type, const int64_t 
 }
 
 static s2k_status ensure_mat(s2k_model *m, DevMat &dm, int type, int rows, int cols) {
-    if (dm.q) {
+    if (dm.w) {
         if (dm.rows != rows || dm.cols != cols || dm.type != type) return fail(S2K_ERR_ARG, "matrix shape changed");
         return S2K_OK;
     }
+    if (rows % kTR != 0 || cols % kTK != 0)
+        return fail(S2K_ERR_UNSUPPORTED, "matrix [%d x %d]: rows must be a multiple of %d and columns of %d", rows,
+                    cols, kTR, kTK);
     dm.type = type;
     dm.rows = rows;
     dm.cols = cols;
-    CU(m->alloc(&dm.q, (size_t)rows * cols));
-    CU(m->alloc(&dm.d, (size_t)rows * (cols / 32)));
+    CU(m->alloc(&dm.w, dm.bytes()));
     return S2K_OK;
 }
 
@@ -555,15 +557,11 @@ static s2k_status upload_mat(s2k_model *m, DevMat &dm, int type, const int64_t n
         CU(m->alloc(&m->staging, m->staging_bytes));
     }
     const size_t rows_per = std::max<size_t>(1, m->staging_bytes / row_bytes);
-    const int nb = (int)(ne[0] / 32);
     for (size_t r0 = 0; r0 < (size_t)ne[1]; r0 += rows_per) {
         const size_t nr = std::min(rows_per, (size_t)ne[1] - r0);
         CU(cudaMemcpyAsync(m->staging, (const uint8_t *)host + r0 * row_bytes, nr * row_bytes, cudaMemcpyHostToDevice,
                            m->stream));
-        DevMat view = dm;
-        view.q = dm.q + (r0 * row_stride) * (size_t)dm.cols;
-        view.d = dm.d + (r0 * row_stride) * (size_t)nb;
-        CU(launch_relayout_q8_0(m->staging, (int)nr, (int)ne[0], &view, row_stride, row_offset, m->stream));
+        CU(launch_relayout_q8_0(m->staging, (int)r0, (int)nr, (int)ne[0], &dm, row_stride, row_offset, m->stream));
         CU(cudaStreamSynchronize(m->stream));
     }
     return S2K_OK;
@@ -710,8 +708,8 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     if (m->finalized) return S2K_OK;
     if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
     const s2k_hparams &hp = m->hp;
-    if (!m->embed.q) return fail(S2K_ERR_STATE, "missing tensor: embeddings.weight");
-    if (hp.num_codebooks > 0 && !m->cb_embed.q) return fail(S2K_ERR_STATE, "missing tensor: codebook_embeddings.weight");
+    if (!m->embed.w) return fail(S2K_ERR_STATE, "missing tensor: embeddings.weight");
+    if (hp.num_codebooks > 0 && !m->cb_embed.w) return fail(S2K_ERR_STATE, "missing tensor: codebook_embeddings.weight");
     if (!m->norm) return fail(S2K_ERR_STATE, "missing tensor: norm.weight");
     auto check_layers = [&](std::vector<Layer> &ls, bool fast) -> s2k_status {
         const int qkn = fast ? hp.fast_attention_qk_norm : hp.attention_qk_norm;
@@ -720,11 +718,11 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
             const char *pre = fast ? "fast_layers" : "layers";
             if (!L.attn_norm) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.attention_norm.weight", pre, i);
             if (!L.ffn_norm) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.ffn_norm.weight", pre, i);
-            if (!L.wqkv.q) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.attention.wqkv.weight", pre, i);
-            if (!L.wo.q) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.attention.wo.weight", pre, i);
+            if (!L.wqkv.w) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.attention.wqkv.weight", pre, i);
+            if (!L.wo.w) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.attention.wo.weight", pre, i);
             if (!L.has_w1) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.feed_forward.w1.weight", pre, i);
             if (!L.has_w3) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.feed_forward.w3.weight", pre, i);
-            if (!L.w2.q) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.feed_forward.w2.weight", pre, i);
+            if (!L.w2.w) return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.feed_forward.w2.weight", pre, i);
             if (qkn && (!L.q_norm || !L.k_norm))
                 return fail(S2K_ERR_STATE, "missing tensor: %s.%zu.attention.q_norm/k_norm.weight", pre, i);
             if (!qkn) {
@@ -737,9 +735,9 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     s2k_status rc = check_layers(m->layers, false);
     if (rc) return rc;
     if (hp.has_fast_decoder) {
-        if (!m->fast_embed.q) return fail(S2K_ERR_STATE, "missing tensor: fast_embeddings.weight");
+        if (!m->fast_embed.w) return fail(S2K_ERR_STATE, "missing tensor: fast_embeddings.weight");
         if (!m->fast_norm) return fail(S2K_ERR_STATE, "missing tensor: fast_norm.weight");
-        if (!m->fast_out.q) return fail(S2K_ERR_STATE, "missing tensor: fast_output.weight");
+        if (!m->fast_out.w) return fail(S2K_ERR_STATE, "missing tensor: fast_output.weight");
         rc = check_layers(m->fast_layers, true);
         if (rc) return rc;
     }
@@ -990,8 +988,7 @@ static MegaOp mk_gemv(const DevMat &w, const float *x, int ldx, int M, int in_mo
     MegaOp o;
     memset(&o, 0, sizeof(o));
     o.kind = MK_GEMV;
-    o.g.wq = w.q;
-    o.g.wd = w.d;
+    o.g.w = w.w;
     o.g.R = w.rows;
     o.g.K = w.cols;
     o.g.x = x;
@@ -1081,8 +1078,7 @@ static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
         MegaOp e;
         memset(&e, 0, sizeof(e));
         e.kind = MK_EMBED_FAST;
-        e.ef.fq = m->fast_embed.q;
-        e.ef.fd = m->fast_embed.d;
+        e.ef.f = m->fast_embed.w;
         e.ef.f_rows = m->fast_embed.rows;
         e.ef.hidden = p == 0 ? m->hidden : nullptr;
         e.ef.codes = s->dev->state.codes;
@@ -1104,12 +1100,10 @@ static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
         MegaOp e;
         memset(&e, 0, sizeof(e));
         e.kind = MK_EMBED_SLOW;
-        e.es.eq = m->embed.q;
-        e.es.ed = m->embed.d;
+        e.es.e = m->embed.w;
         e.es.e_rows = m->embed.rows;
         e.es.dim = hp.embedding_length;
-        e.es.cq = hp.num_codebooks > 0 ? m->cb_embed.q : nullptr;
-        e.es.cd = hp.num_codebooks > 0 ? m->cb_embed.d : nullptr;
+        e.es.c = hp.num_codebooks > 0 ? m->cb_embed.w : nullptr;
         e.es.c_rows = hp.num_codebooks > 0 ? m->cb_embed.rows : 0;
         e.es.tokens = s->dev->state.step_in;
         e.es.T = 1;

@@ -60,6 +60,9 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
 // when the limit is reached.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     if (mbar_test(bar, parity)) return true;
+    // once a wait has timed out, the copies it waited for will not come:
+    // later waits give up at once instead of each spending the full limit
+    if (err && (*reinterpret_cast<volatile int *>(err) & (ERR_WAIT_FULL | ERR_WAIT_EMPTY | ERR_GRID))) return false;
     const long long t0 = clock64();
     while (!mbar_test(bar, parity)) {
         if (clock64() - t0 > kWaitLimitCycles) {

@@ -5,28 +5,20 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "s2k_tgemv.cuh"
+
 namespace s2k {
 
 // ---------------------------------------------------------------------------
 // Weight matrix in device layout.
-//   Q8_0 : q = int8 [rows][cols], d = fp16 [rows][cols/32]  (split planes so a
-//          row of quants is one contiguous, 16-byte aligned run)
+//   Q8_0 : 32 x 512 tiles of int8 quants + fp16 scales (s2k_tgemv.cuh); rows %
+//          32 == 0 and cols % 512 == 0.
 // ---------------------------------------------------------------------------
 struct DevMat {
     int type = -1;  // ggml type id
     int rows = 0, cols = 0;
-    int8_t *q = nullptr;
-    __half *d = nullptr;
+    uint8_t *w = nullptr;
     size_t bytes() const;
-};
-
-enum GemvIn : int {
-    IN_PLAIN = 0,    // activation = x
-    IN_RMSNORM = 1,  // activation = (x * rsqrt(mean(x^2)+eps)) * norm_w
-};
-enum GemvEpi : int {
-    EPI_STORE = 0,   // y[r] = W[r].x  (+ res[r] when res is given)
-    EPI_SWIGLU = 1,  // rows interleaved (gate, up): y[i] = silu(W[2i].x) * W[2i+1].x
 };
 
 struct GemvArgs {
@@ -52,9 +44,10 @@ cudaError_t launch_gemv(const GemvArgs &a, int num_sms, cudaStream_t st);
 // smem bytes a gemv launch for (K, M) needs (to set the function attribute once).
 cudaError_t gemv_setup();
 
-// Q8_0 GGUF blocks (34 B) in device staging -> split planes, dst rows
-// dst_row = row*row_stride + row_offset (row_stride 2 interleaves w1/w3).
-cudaError_t launch_relayout_q8_0(const uint8_t *src, int rows, int cols, DevMat *dst, int row_stride,
+// Q8_0 GGUF blocks (34 B) of rows [row0, row0 + rows) in device staging ->
+// tiles of dst; source row r lands in dst row r * row_stride + row_offset
+// (row_stride 2 interleaves w1/w3).
+cudaError_t launch_relayout_q8_0(const uint8_t *src, int row0, int rows, int cols, DevMat *dst, int row_stride,
                                  int row_offset, cudaStream_t st);
 
 // ---------------------------------------------------------------------------

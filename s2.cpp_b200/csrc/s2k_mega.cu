@@ -6,8 +6,8 @@
 // time for the per-layer matrices).  Launched as separate kernels, each op
 // pays launch, dependency and prologue latency while HBM idles.  Here a
 // producer warp per CTA streams the CTA's rows of every GEMV of the segment,
-// back to back, through a 7-stage shared-memory ring (cp.async.bulk +
-// mbarriers); it runs ahead across op boundaries, so HBM keeps streaming while
+// back to back, as 17 KB weight tiles through a 10-stage shared-memory ring
+// (cp.async.bulk + mbarriers); it runs ahead across op boundaries, so HBM keeps streaming while
 // the consumer warps wait at a grid barrier, normalize and quantize the next
 // activation, or run attention.
 //
@@ -23,63 +23,28 @@
 
 namespace s2k {
 
-// 12 consumer warps + 1 producer: at most 4 warps per SM sub-partition, so
-// each thread can hold 128 registers.
-constexpr int kMW = 12;                    // consumer warps
+// 8 consumer warps (the tile engine's mapping, s2k_tgemv.cuh) + 1 producer.
+constexpr int kMW = kTW;                   // consumer warps
 constexpr int kMNC = kMW * 32;             // consumer threads
 constexpr int kMThreads = kMNC + 32;       // + producer warp
-constexpr int kMStages = 4;
-constexpr int kMSlot = 40 * 1024;
-constexpr int kCPL = 5;                    // 16-byte weight chunks per lane per row slice
+constexpr int kMStages = 10;               // ring of 17 KB weight tiles
 constexpr int kMKMax = 10240;
-constexpr int kMNormMax = 4096;
-constexpr int kMMaxRows = 64;
 constexpr int kMaxT = 2;
 constexpr int kHD = 128;
 constexpr int kPtabMax = kMaxT * kMKMax / (int)sizeof(int);  // cached pages whose ids fit the staged table
 
-struct MStage {
-    int S, WPR, BPL;
-};
-
-// S rows per stage and WPR warps per row with S * WPR = kMW; BPL = 16-byte
-// chunks per lane of a row slice.
-__host__ __device__ inline MStage mega_stage(int K) {
-    const int row_bytes = K + K / 16;
-    const int cand[6] = {12, 6, 4, 3, 2, 1};
-    int S = 1;
-    for (int i = 0; i < 6; ++i)
-        if (cand[i] * row_bytes <= kMSlot) {
-            S = cand[i];
-            break;
-        }
-    MStage r;
-    r.S = S;
-    r.WPR = kMW / S;
-    const int NC = K / 16;
-    const int CPS = (NC + r.WPR - 1) / r.WPR;
-    r.BPL = (CPS + 31) / 32;
-    return r;
-}
-
 bool mega_gemv_ok(const MegaGemv &g) {
-    if (g.K % 256 != 0 || g.K > kMKMax || g.M < 1 || g.M > kMaxT || g.R <= 0) return false;
-    const MStage st = mega_stage(g.K);
-    if (st.S * (g.K + g.K / 16) > kMSlot || st.BPL > kCPL) return false;
-    if (g.in_mode == IN_RMSNORM && g.K > kMNormMax) return false;
-    if (g.epi == EPI_SWIGLU && (g.R % 2 != 0 || g.res != nullptr)) return false;
+    if (!tg_shape_ok(g.R, g.K, g.M, g.in_mode, g.epi, g.res != nullptr, kMKMax, kMaxT)) return false;
+    if (g.in_mode == IN_RMSNORM && g.norm_w == nullptr) return false;
     return true;
 }
 
 struct MSmem {
-    uint8_t ring[kMStages][kMSlot];
+    uint8_t ring[kMStages][kTileBytes];
     uint64_t full[kMStages], empty[kMStages];
-    int8_t xq[kMaxT * kMKMax];
+    int8_t xq[kMaxT * kMKMax];  // quantized activation (GEMV); page table (attention)
     float xd[kMaxT * kMKMax / 32];
-    float nw[kMNormMax];
-    float res[kMaxT * kMMaxRows];
-    double rowacc[kMStages][kMW][kMaxT];  // cross-warp row partials of a stage
-    int rowcnt[kMStages][kMW];            // arrivals per row (unit) of a stage
+    float nw[kNormMax];
     double tok[kMW][kMaxT];
     float scale[kMaxT];
     // attention
@@ -109,7 +74,8 @@ __device__ __forceinline__ void grid_arrive(MegaCtl *ctl) {
 
 __device__ __forceinline__ void grid_wait(MegaCtl *ctl, unsigned target, int *err) {
     if (threadIdx.x == 0) {
-        if (ld_acquire_u32(&ctl->count) < target) {
+        if (ld_acquire_u32(&ctl->count) < target &&
+            !(*reinterpret_cast<volatile int *>(err) & (ERR_WAIT_FULL | ERR_WAIT_EMPTY | ERR_GRID))) {
             const long long t0 = clock64();
             while (ld_acquire_u32(&ctl->count) < target) {
                 if (clock64() - t0 > kWaitLimitCycles) {
@@ -122,15 +88,8 @@ __device__ __forceinline__ void grid_wait(MegaCtl *ctl, unsigned target, int *er
     named_sync(1, kMNC);
 }
 
-__device__ __forceinline__ void gemv_rows(const MegaGemv &g, int cta, int G, int *r0, int *r1) {
-    const int unit = g.epi == EPI_SWIGLU ? 2 : 1;
-    const int NU = g.R / unit;
-    *r0 = unit * (int)(((long long)NU * cta) / G);
-    *r1 = unit * (int)(((long long)NU * (cta + 1)) / G);
-}
-
 // ---------------------------------------------------------------------------
-// producer: the weight stream of every GEMV op of the segment
+// producer: the weight tiles of every GEMV op of the segment, in op order
 // ---------------------------------------------------------------------------
 __device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, int G, int *err) {
     const uint64_t pol = policy_evict_first();
@@ -138,282 +97,31 @@ __device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, 
     for (int i = 0; i < n_ops; ++i) {
         if (ops[i].kind != MK_GEMV) continue;
         const MegaGemv g = ops[i].g;
-        int r0, r1;
-        gemv_rows(g, cta, G, &r0, &r1);
-        const MStage st = mega_stage(g.K);
-        for (int rb = r0; rb < r1; rb += st.S, ++ps) {
+        long long u0, u1;
+        tg_range(g.R, g.K, cta, G, &u0, &u1);
+        for (long long u = u0; u < u1; ++u, ++ps) {
             const int slot = ps % kMStages;
             if (ps >= kMStages && !mbar_wait(&sm.empty[slot], ((ps / kMStages) - 1) & 1, err, ERR_WAIT_EMPTY))
                 return;
-            const int rows = min(st.S, r1 - rb);
-            const uint32_t qb = (uint32_t)rows * (uint32_t)g.K;
-            const uint32_t db = (uint32_t)rows * (uint32_t)(g.K / 16);
-            mbar_arrive_expect_tx(&sm.full[slot], qb + db);
-            bulk_g2s(sm.ring[slot], g.wq + (size_t)rb * g.K, qb, &sm.full[slot], pol);
-            bulk_g2s(sm.ring[slot] + (size_t)st.S * g.K, reinterpret_cast<const uint8_t *>(g.wd) + (size_t)rb * (g.K / 16),
-                     db, &sm.full[slot], pol);
+            mbar_arrive_expect_tx(&sm.full[slot], kTileBytes);
+            bulk_g2s(sm.ring[slot], g.w + (size_t)u * kTileBytes, kTileBytes, &sm.full[slot], pol);
         }
     }
 }
 
-__device__ __forceinline__ int dot_block8(const int4 &w0, const int4 &w1, const int (&xb)[8]) {
-    int s0 = dp4a(w0.x, xb[0], 0);
-    int s1 = dp4a(w1.x, xb[4], 0);
-    s0 = dp4a(w0.y, xb[1], s0);
-    s1 = dp4a(w1.y, xb[5], s1);
-    s0 = dp4a(w0.z, xb[2], s0);
-    s1 = dp4a(w1.z, xb[6], s1);
-    s0 = dp4a(w0.w, xb[3], s0);
-    s1 = dp4a(w1.w, xb[7], s1);
-    return s0 + s1;
-}
-
 // ---------------------------------------------------------------------------
-// GEMV op (consumer side)
+// GEMV op (consumer side): activation prologue, then this CTA's tiles
 // ---------------------------------------------------------------------------
-// Lane 0 of a warp holding a row slice's sum: combine the row's slices (and
-// the gate/up pair) in shared memory; the last warp to arrive writes the
-// output.  The terms are exact, so the arrival order does not change the
-// rounded result.
-template <int MT>
-__device__ __forceinline__ void combine_row(MSmem &sm, int slot, int row_local, int unit, int need, int M,
-                                            const double (&acc)[MT], int epi, float *y, int ldy, int rb, int r0,
-                                            const float *res) {
-    if (need == 1) {
-        const int r = rb + row_local;
-#pragma unroll
-        for (int m = 0; m < MT; ++m)
-            if (m < M) {
-                const float val = (float)acc[m];
-                y[(size_t)m * ldy + r] = res ? sm.res[m * kMMaxRows + (r - r0)] + val : val;
-            }
-        return;
-    }
-    const int grp = row_local / unit;
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-        if (m < M) atomicAdd(&sm.rowacc[slot][row_local][m], acc[m]);
-    __threadfence_block();
-    if (atomicAdd(&sm.rowcnt[slot][grp], 1) != need - 1) return;
-    __threadfence_block();
-    volatile double *ra = &sm.rowacc[slot][0][0];
-    if (epi == EPI_SWIGLU) {
-#pragma unroll
-        for (int m = 0; m < MT; ++m)
-            if (m < M) {
-                const double gg = ra[(2 * grp) * kMaxT + m], up = ra[(2 * grp + 1) * kMaxT + m];
-                y[(size_t)m * ldy + rb / 2 + grp] = __fmul_rn(silu((float)gg), (float)up);
-                ra[(2 * grp) * kMaxT + m] = 0.0;
-                ra[(2 * grp + 1) * kMaxT + m] = 0.0;
-            }
-    } else {
-        const int r = rb + row_local;
-#pragma unroll
-        for (int m = 0; m < MT; ++m)
-            if (m < M) {
-                const float val = (float)ra[row_local * kMaxT + m];
-                y[(size_t)m * ldy + r] = res ? sm.res[m * kMMaxRows + (r - r0)] + val : val;
-                ra[row_local * kMaxT + m] = 0.0;
-            }
-    }
-    sm.rowcnt[slot][grp] = 0;
-}
-
 template <int MT>
 __device__ void mega_gemv(const MegaGemv &gref, MSmem &sm, int cta, int G, int &cs, int *err) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // op fields in registers (stores through y must not force re-reads of the op)
-    const int K = gref.K, R = gref.R, M = gref.M, ldx = gref.ldx, ldy = gref.ldy, ldres = gref.ldres;
-    const int in_mode = gref.in_mode, epi = gref.epi;
-    const float eps = gref.eps;
-    const float *const x = gref.x;
-    const float *const res = gref.res;
-    const float *const norm_w = gref.norm_w;
-    float *const y = gref.y;
-    float *const act_out = gref.act_out;
-    const int NB = K >> 5;
-    const int unit = epi == EPI_SWIGLU ? 2 : 1;
-    const int NU = R / unit;
-    const int r0 = unit * (int)(((long long)NU * cta) / G);
-    const int r1 = unit * (int)(((long long)NU * (cta + 1)) / G);
-    if (r1 <= r0) return;
-    const MStage st = mega_stage(K);
-
-    if (in_mode == IN_RMSNORM)
-        for (int i = tid; i < K / 4; i += kMNC)
-            reinterpret_cast<float4 *>(sm.nw)[i] = __ldg(reinterpret_cast<const float4 *>(norm_w) + i);
-    const int nrows = r1 - r0;
-    if (res != nullptr)
-        for (int i = tid; i < M * nrows; i += kMNC) {
-            const int m = i / nrows, r = i - m * nrows;
-            sm.res[m * kMMaxRows + r] = __ldcg(res + (size_t)m * ldres + r0 + r);
-        }
-
-    // activation -> Q8_0 blocks in shared memory; one block per thread
-    const int items = M * NB;
-    const bool single = items <= kMNC;
-    {
-        float4 v[8];
-        if (in_mode == IN_RMSNORM) {
-            double tk[MT];
-#pragma unroll
-            for (int m = 0; m < MT; ++m) tk[m] = 0.0;
-            for (int it = tid; it < items; it += kMNC) {
-                const int m = it / NB, b = it - m * NB;
-                const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)m * ldx + b * 32);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + j);
-                double s = 0.0;
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    s += (double)__fmul_rn(v[j].x, v[j].x) + (double)__fmul_rn(v[j].y, v[j].y) +
-                         (double)__fmul_rn(v[j].z, v[j].z) + (double)__fmul_rn(v[j].w, v[j].w);
-#pragma unroll
-                for (int mm = 0; mm < MT; ++mm)
-                    if (mm == m) tk[mm] += s;
-            }
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                const double t = warp_sum_d(tk[m]);
-                if (lane == 0) sm.tok[warp][m] = t;
-            }
-            named_sync(1, kMNC);
-            if (tid < M) {
-                double tot = 0.0;
-                for (int w = 0; w < kMW; ++w) tot += sm.tok[w][tid];
-                const float mean = (float)(tot / (double)K);
-                sm.scale[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-            }
-            named_sync(1, kMNC);
-        }
-        for (int it = tid; it < items; it += kMNC) {
-            const int m = it / NB, b = it - m * NB;
-            if (!(single && in_mode == IN_RMSNORM)) {
-                const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)m * ldx + b * 32);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + j);
-            }
-            if (in_mode == IN_RMSNORM) {
-                const float sc = sm.scale[m];
-                const float4 *nw = reinterpret_cast<const float4 *>(sm.nw + b * 32);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float4 w4 = nw[j];
-                    v[j].x = __fmul_rn(__fmul_rn(v[j].x, sc), w4.x);
-                    v[j].y = __fmul_rn(__fmul_rn(v[j].y, sc), w4.y);
-                    v[j].z = __fmul_rn(__fmul_rn(v[j].z, sc), w4.z);
-                    v[j].w = __fmul_rn(__fmul_rn(v[j].w, sc), w4.w);
-                }
-            }
-            if (act_out != nullptr && cta == 0) {
-                float4 *dst = reinterpret_cast<float4 *>(act_out + (size_t)m * K + b * 32);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) dst[j] = v[j];
-            }
-            float amax = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                amax = fmaxf(fmaxf(fmaxf(amax, fabsf(v[j].x)), fmaxf(fabsf(v[j].y), fabsf(v[j].z))), fabsf(v[j].w));
-            const float d = __fdiv_rn(amax, 127.f);
-            const float id = amax != 0.0f ? __fdiv_rn(127.f, amax) : 0.0f;
-            int pk[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int q0 = __float2int_rn(__fmul_rn(v[j].x, id)), q1 = __float2int_rn(__fmul_rn(v[j].y, id));
-                const int q2 = __float2int_rn(__fmul_rn(v[j].z, id)), q3 = __float2int_rn(__fmul_rn(v[j].w, id));
-                pk[j] = (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) | ((q3 & 0xff) << 24);
-            }
-            int4 *dq = reinterpret_cast<int4 *>(sm.xq + m * K + b * 32);
-            dq[0] = make_int4(pk[0], pk[1], pk[2], pk[3]);
-            dq[1] = make_int4(pk[4], pk[5], pk[6], pk[7]);
-            sm.xd[m * NB + b] = __half2float(__float2half_rn(d));
-        }
-    }
+    const MegaGemv g = gref;  // op fields in registers
+    long long u0, u1;
+    tg_range(g.R, g.K, cta, G, &u0, &u1);
+    if (u0 == u1) return;  // no row tile of this op here (R / 32 < G)
+    // the CTA owning row tile 0 stores act_out
+    tg_prologue<MT, kMNC>(g, sm.xq, sm.xd, sm.nw, &sm.tok[0][0], kMaxT, sm.scale, u0 == 0, 1);
     named_sync(1, kMNC);
-
-    // warp -> (row in stage, K slice); lane -> 16-byte chunks c0 + lane + 32j of
-    // the slice (consecutive lanes read consecutive 16 bytes: no bank
-    // conflicts).  A chunk is half a Q8_0 block; its term s_half * (d_w * d_x)
-    // is exact in double, so halves need not be paired before accumulating.
-    // The lane's activation chunks are the same for every row: registers.
-    const int S = st.S, WPR = st.WPR;
-    const int row_local = warp / WPR, slice = warp - row_local * WPR;
-    const int NC = K >> 4;
-    const int CPS = (NC + WPR - 1) / WPR;
-    const int c_begin = slice * CPS, c_end = min(NC, c_begin + CPS);
-    int cj[kCPL];
-    bool cv[kCPL];
-#pragma unroll
-    for (int j = 0; j < kCPL; ++j) {
-        const int c = c_begin + lane + 32 * j;
-        cv[j] = c < c_end;
-        cj[j] = cv[j] ? c : c_begin;
-    }
-    int xr[MT][kCPL][4];
-    float xs[MT][kCPL];
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-        for (int j = 0; j < kCPL; ++j) {
-            const int mm = m < M ? m : 0;
-            const int4 a = *reinterpret_cast<const int4 *>(sm.xq + mm * K + cj[j] * 16);
-            xr[m][j][0] = a.x;
-            xr[m][j][1] = a.y;
-            xr[m][j][2] = a.z;
-            xr[m][j][3] = a.w;
-            xs[m][j] = sm.xd[mm * NB + (cj[j] >> 1)];
-        }
-    // arrivals a row group (one row, or one gate/up pair) collects before it is finalized
-    const int need = WPR * unit;
-
-    for (int rb = r0; rb < r1; rb += S, ++cs) {
-        const int slot = cs % kMStages;
-        const int rows = min(S, r1 - rb);
-        mbar_wait(&sm.full[slot], (cs / kMStages) & 1, err, ERR_WAIT_FULL);
-        double acc[MT];
-#pragma unroll
-        for (int m = 0; m < MT; ++m) acc[m] = 0.0;
-        const bool have = row_local < rows;
-        if (have) {
-            const int8_t *sq = reinterpret_cast<const int8_t *>(sm.ring[slot]);
-            const int8_t *wrow = sq + (size_t)row_local * K;
-            const __half *drow = reinterpret_cast<const __half *>(sq + (size_t)S * K) + (size_t)row_local * NB;
-            int4 wv[kCPL];
-            float dw[kCPL];
-#pragma unroll
-            for (int j = 0; j < kCPL; ++j)
-                if (cv[j]) {
-                    wv[j] = *reinterpret_cast<const int4 *>(wrow + cj[j] * 16);
-                    dw[j] = __half2float(drow[cj[j] >> 1]);
-                }
-#pragma unroll
-            for (int j = 0; j < kCPL; ++j)
-                if (cv[j]) {
-#pragma unroll
-                    for (int m = 0; m < MT; ++m)
-                        if (m < M) {
-                            int sh = dp4a(wv[j].x, xr[m][j][0], 0);
-                            sh = dp4a(wv[j].y, xr[m][j][1], sh);
-                            sh = dp4a(wv[j].z, xr[m][j][2], sh);
-                            sh = dp4a(wv[j].w, xr[m][j][3], sh);
-                            acc[m] += (double)sh * (double)(dw[j] * xs[m][j]);
-                        }
-                }
-        }
-        __syncwarp();
-        if (!have) {
-            if (lane == 0) mbar_arrive(&sm.empty[slot]);
-            continue;
-        }
-#pragma unroll
-        for (int m = 0; m < MT; ++m) acc[m] = warp_sum_d(acc[m]);
-        if (lane == 0) {
-            combine_row<MT>(sm, slot, row_local, unit, need, M, acc, epi, y, ldy, rb, r0, res);
-            // release the slot only after the combine: its row accumulators are
-            // reused when the slot comes round again
-            mbar_arrive(&sm.empty[slot]);
-        }
-    }
+    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, cs, sm.xq, sm.xd, cta, G, err);
 }
 
 // ---------------------------------------------------------------------------
@@ -650,9 +358,7 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
     }
 }
 
-__device__ __forceinline__ float deq_row(const int8_t *q, const __half *d, int cols, long long row, int col) {
-    return (float)q[row * cols + col] * __half2float(d[row * (cols >> 5) + (col >> 5)]);
-}
+
 
 __device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err) {
     const int stride = e.ncb + 1;
@@ -664,7 +370,7 @@ __device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err
             tok = 0;
         }
         const bool sem = tok >= e.sem_begin && tok <= e.sem_end;
-        float x = deq_row(e.eq, e.ed, e.dim, tok, i);
+        float x = tq_elem(e.e, e.dim, tok, i);
         if (sem && e.ncb > 0) {
             float s = 0.f;
             for (int cb = 0; cb < e.ncb; ++cb) {
@@ -673,7 +379,7 @@ __device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err
                     if (i == 0) atomicOr(err, ERR_BAD_TOKEN);
                     id = 0;
                 }
-                const float r = deq_row(e.cq, e.cd, e.dim, id, i);
+                const float r = tq_elem(e.c, e.dim, id, i);
                 s = cb == 0 ? r : __fadd_rn(s, r);
             }
             x = __fadd_rn(x, s);
@@ -697,7 +403,7 @@ __device__ void mega_embed_fast(const MegaEmbedFast &e, int cta, int G, int *err
                 if (i == 0) atomicOr(err, ERR_BAD_TOKEN);
                 c = 0;
             }
-            x = deq_row(e.fq, e.fd, e.dim, c, i);
+            x = tq_elem(e.f, e.dim, c, i);
         }
         e.x[(size_t)r * e.dim + i] = x;
     }
@@ -718,8 +424,6 @@ __global__ void __launch_bounds__(kMThreads, 1)
         }
         fence_mbar_init();
     }
-    for (int i = threadIdx.x; i < kMStages * kMW * kMaxT; i += blockDim.x) (&sm.rowacc[0][0][0])[i] = 0.0;
-    for (int i = threadIdx.x; i < kMStages * kMW; i += blockDim.x) (&sm.rowcnt[0][0])[i] = 0;
     __syncthreads();
     if (warp == kMW) {
         if (lane == 0) mega_producer(ops, n_ops, sm, cta, G, err);

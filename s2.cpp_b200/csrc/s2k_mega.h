@@ -23,21 +23,7 @@ enum MegaKind : int {
     MK_ADVANCE = 5,
 };
 
-struct MegaGemv {
-    const int8_t *wq;  // [R][K] int8
-    const __half *wd;  // [R][K/32]
-    int R, K;
-    const float *x;  // [M][ldx]
-    int ldx, M, in_mode;
-    const float *norm_w;
-    float eps;
-    int epi;
-    float *y;
-    int ldy;
-    const float *res;
-    int ldres;
-    float *act_out;
-};
+using MegaGemv = TGemv;  // s2k_tgemv.cuh
 
 struct MegaAttn {
     float *qkv;  // [T][ldqkv] raw projections
@@ -61,11 +47,9 @@ struct MegaAttn {
 };
 
 struct MegaEmbedSlow {
-    const int8_t *eq;  // token embeddings (Q8_0 planes), [rows][dim]
-    const __half *ed;
+    const uint8_t *e;  // token embeddings (Q8_0 tiles), [e_rows][dim]
     int e_rows, dim;
-    const int8_t *cq;  // codebook embeddings, [c_rows][dim]
-    const __half *cd;
+    const uint8_t *c;  // codebook embeddings (Q8_0 tiles), [c_rows][dim]
     int c_rows;
     const int *tokens;  // [T][ncb+1]
     int T, ncb, cb_size, sem_begin, sem_end, scale_cb;
@@ -74,8 +58,7 @@ struct MegaEmbedSlow {
 };
 
 struct MegaEmbedFast {
-    const int8_t *fq;  // fast_embeddings (Q8_0 planes), [f_rows][dim]
-    const __half *fd;
+    const uint8_t *f;  // fast_embeddings (Q8_0 tiles), [f_rows][dim]
     int f_rows;
     const float *hidden;  // null: no hidden row
     const int *codes;

@@ -22,8 +22,7 @@
 namespace s2k {
 
 __device__ __forceinline__ float deq_q8_0(const DevMat &w, long long row, int col) {
-    const int nb = w.cols >> 5;
-    return (float)w.q[row * w.cols + col] * __half2float(w.d[row * nb + (col >> 5)]);
+    return tq_elem(w.w, w.cols, row, col);
 }
 
 // grid T, block 256
