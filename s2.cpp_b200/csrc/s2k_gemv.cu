@@ -107,8 +107,9 @@ __global__ void __launch_bounds__(kThreads, 1) tgemv_kernel(TGemv g, const int *
     // the CTA owning row tile 0 stores act_out
     tg_prologue<MT, kTNC>(g, sm.xq, sm.xd, sm.nw, &sm.tok[0][0], MT, sm.scale, u0 == 0, 1);
     named_sync(1, kTNC);
-    int cs = 0;
-    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, NS, cs, sm.xq, sm.xd, blockIdx.x, gridDim.x, err);
+    int slot = 0;
+    uint32_t phase = 0;
+    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, NS, slot, phase, sm.xq, sm.xd, blockIdx.x, gridDim.x, err);
 }
 
 size_t DevMat::bytes() const {

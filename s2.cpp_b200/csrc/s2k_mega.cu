@@ -113,7 +113,7 @@ __device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, 
 // GEMV op (consumer side): activation prologue, then this CTA's tiles
 // ---------------------------------------------------------------------------
 template <int MT>
-__device__ void mega_gemv(const MegaGemv &gref, MSmem &sm, int cta, int G, int &cs, int *err) {
+__device__ void mega_gemv(const MegaGemv &gref, MSmem &sm, int cta, int G, int &slot, uint32_t &phase, int *err) {
     const MegaGemv g = gref;  // op fields in registers
     long long u0, u1;
     tg_range(g.R, g.K, cta, G, &u0, &u1);
@@ -121,7 +121,7 @@ __device__ void mega_gemv(const MegaGemv &gref, MSmem &sm, int cta, int G, int &
     // the CTA owning row tile 0 stores act_out
     tg_prologue<MT, kMNC>(g, sm.xq, sm.xd, sm.nw, &sm.tok[0][0], kMaxT, sm.scale, u0 == 0, 1);
     named_sync(1, kMNC);
-    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, cs, sm.xq, sm.xd, cta, G, err);
+    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.xq, sm.xd, cta, G, err);
 }
 
 // ---------------------------------------------------------------------------
@@ -429,12 +429,13 @@ __global__ void __launch_bounds__(kMThreads, 1)
         if (lane == 0) mega_producer(ops, n_ops, sm, cta, G, err);
         return;
     }
-    int cs = 0;
+    int cslot = 0;  // ring position of the consumers
+    uint32_t cphase = 0;
     for (int i = 0; i < n_ops; ++i) {
         const int kind = ops[i].kind;
         if (i > 0) grid_wait(ctl, (unsigned)(i * G), err);
         switch (kind) {
-        case MK_GEMV: mega_gemv<MT>(ops[i].g, sm, cta, G, cs, err); break;
+        case MK_GEMV: mega_gemv<MT>(ops[i].g, sm, cta, G, cslot, cphase, err); break;
         case MK_ATTN: mega_attn(ops[i].a, sm, cta, G, err); break;
         case MK_EMBED_SLOW: mega_embed_slow(ops[i].es, cta, G, err); break;
         case MK_EMBED_FAST: mega_embed_fast(ops[i].ef, cta, G, err); break;

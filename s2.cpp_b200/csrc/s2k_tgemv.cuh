@@ -19,9 +19,8 @@
 // Consumer mapping: 8 consumer warps, warp w owns rows 4w..4w+3 of every
 // tile; lane l owns 16-byte column chunk l of the tile, i.e. half of Q8_0
 // block l/2.  A lane keeps its 4 x MT partial row sums in registers across
-// all K-tiles of a row tile; the warp reduces them once per row tile (the
-// butterfly leaves every lane with the sums) and lanes 0..3 store one row
-// each.  Rows (2i, 2i+1) of a SwiGLU matrix (gate/up interleaved at upload)
+// all K-tiles of a row tile; the warp reduces them once per row tile with a
+// transposing butterfly and lanes 0, 8, 16, 24 store one row each.  Rows (2i, 2i+1) of a SwiGLU matrix (gate/up interleaved at upload)
 // sit in the same warp, so the epilogue needs no cross-warp exchange.
 //
 // Arithmetic (identical to ggml's vec_dot_q8_0_q8_0 terms, summed order-free):
@@ -44,6 +43,7 @@ constexpr int kTRW = kTR / kTW;                  // rows per warp
 constexpr int kNormMax = 4096;                   // longest RMSNorm'd activation row
 
 static_assert(kTileBytes % 16 == 0, "bulk copies need 16-byte multiples");
+static_assert(kTRW == 4, "the row-tile reduction is written for 4 rows per warp");
 
 enum GemvIn : int {
     IN_PLAIN = 0,    // activation = x
@@ -87,217 +87,291 @@ __device__ __forceinline__ void tg_range(int R, int K, int cta, int G, long long
     *u1 = (RT * (cta + 1) / G) * NKT;
 }
 
-// Quantize one 32-value block held in registers (ggml x86 quantize_row_q8_0:
-// d = amax/127 stored fp16, q = round-half-even(x * 127/amax)).
-__device__ __forceinline__ void tg_quant_block(const float4 (&v)[8], int8_t *xq_blk, float *xd_blk) {
-    float amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-        amax = fmaxf(fmaxf(fmaxf(amax, fabsf(v[j].x)), fmaxf(fabsf(v[j].y), fabsf(v[j].z))), fabsf(v[j].w));
+// One 8-value chunk of an activation row: chunk c of token m covers columns
+// 8*c' .. 8*c'+7 with c' = c % (K/8).  Four consecutive lanes hold the four
+// chunks of one 32-value Q8_0 block.
+struct Chunk8 {
+    float4 a, b;
+};
+
+__device__ __forceinline__ double sumsq8(const Chunk8 &c) {
+    return (double)__fmul_rn(c.a.x, c.a.x) + (double)__fmul_rn(c.a.y, c.a.y) + (double)__fmul_rn(c.a.z, c.a.z) +
+           (double)__fmul_rn(c.a.w, c.a.w) + (double)__fmul_rn(c.b.x, c.b.x) + (double)__fmul_rn(c.b.y, c.b.y) +
+           (double)__fmul_rn(c.b.z, c.b.z) + (double)__fmul_rn(c.b.w, c.b.w);
+}
+
+__device__ __forceinline__ float4 mul4(float4 v, float sc, float4 w) {
+    return make_float4(__fmul_rn(__fmul_rn(v.x, sc), w.x), __fmul_rn(__fmul_rn(v.y, sc), w.y),
+                       __fmul_rn(__fmul_rn(v.z, sc), w.z), __fmul_rn(__fmul_rn(v.w, sc), w.w));
+}
+
+__device__ __forceinline__ int pack4(float4 v, float id) {
+    const int q0 = __float2int_rn(__fmul_rn(v.x, id)), q1 = __float2int_rn(__fmul_rn(v.y, id));
+    const int q2 = __float2int_rn(__fmul_rn(v.z, id)), q3 = __float2int_rn(__fmul_rn(v.w, id));
+    return (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) | ((q3 & 0xff) << 24);
+}
+
+// Quantize the chunk this lane holds (ggml x86 quantize_row_q8_0 on its
+// 32-value block: d = amax/127 stored fp16, q = round-half-even(x * 127/amax));
+// all 32 lanes must call it, valid = this lane holds a chunk.
+__device__ __forceinline__ void quant_chunk(const Chunk8 &c, bool valid, int8_t *xq_chunk, float *xd_blk,
+                                            bool first_of_block) {
+    float amax = fmaxf(fmaxf(fmaxf(fabsf(c.a.x), fabsf(c.a.y)), fmaxf(fabsf(c.a.z), fabsf(c.a.w))),
+                       fmaxf(fmaxf(fabsf(c.b.x), fabsf(c.b.y)), fmaxf(fabsf(c.b.z), fabsf(c.b.w))));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    if (!valid) return;
     const float d = __fdiv_rn(amax, 127.f);
     const float id = amax != 0.0f ? __fdiv_rn(127.f, amax) : 0.0f;
-    int pk[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int q0 = __float2int_rn(__fmul_rn(v[j].x, id)), q1 = __float2int_rn(__fmul_rn(v[j].y, id));
-        const int q2 = __float2int_rn(__fmul_rn(v[j].z, id)), q3 = __float2int_rn(__fmul_rn(v[j].w, id));
-        pk[j] = (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) | ((q3 & 0xff) << 24);
-    }
-    int4 *dq = reinterpret_cast<int4 *>(xq_blk);
-    dq[0] = make_int4(pk[0], pk[1], pk[2], pk[3]);
-    dq[1] = make_int4(pk[4], pk[5], pk[6], pk[7]);
-    *xd_blk = __half2float(__float2half_rn(d));
-}
-
-__device__ __forceinline__ double sumsq_block(const float4 (&v)[8]) {
-    double s = 0.0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-        s += (double)__fmul_rn(v[j].x, v[j].x) + (double)__fmul_rn(v[j].y, v[j].y) +
-             (double)__fmul_rn(v[j].z, v[j].z) + (double)__fmul_rn(v[j].w, v[j].w);
-    return s;
-}
-
-__device__ __forceinline__ void load_block(const float *src, float4 (&v)[8]) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = __ldcg(reinterpret_cast<const float4 *>(src) + j);
+    *reinterpret_cast<int2 *>(xq_chunk) = make_int2(pack4(c.a, id), pack4(c.b, id));
+    if (first_of_block) *xd_blk = __half2float(__float2half_rn(d));
 }
 
 // Prologue (all NT consumer threads): activation rows -> Q8_0 blocks in shared
 // memory (xq [M][K] int8, xd [M][K/32] fp16-rounded scales as float), with the
 // RMSNorm of rms_norm_weighted (src/s2_model.cpp:46-55) when in_mode says so.
 // nws [kNormMax] receives the norm weights; tok [NT/32][tok_ld] (tok_ld >= MT)
-// and scale [MT] are small shared scratch arrays.  write_act: this CTA stores
-// act_out (exactly one CTA of the grid should).  The caller synchronizes the
-// consumer threads after it returns.
-// A thread owns whole 32-value blocks (item = token * NB + block).  The norm
-// weights are copied to shared memory by loads issued together with the
-// activation loads, so at decode widths (one block per thread) the prologue
-// costs one L2 round trip, and the activation block stays in registers
-// between the sum of squares and the quantizer.
+// is small shared scratch.  write_act: this CTA stores act_out (exactly one
+// CTA of the grid should).  The caller synchronizes the consumer threads after
+// it returns.
+// Thread t owns 8-value chunks t, t + NT, ... (CPT of them per pass, all loads
+// of a pass issued before any is used), so the whole CTA quantizes in
+// parallel and a pass costs one L2 round trip.  Every thread derives the
+// RMSNorm scale itself from the per-warp partial sums.
 template <int MT, int NT>
 __device__ __forceinline__ void tg_prologue(const TGemv &g, int8_t *xq, float *xd, float *nws, double *tok,
-                                            int tok_ld, float *scale, bool write_act, int bar_id) {
+                                            int tok_ld, float * /*unused*/, bool write_act, int bar_id) {
+    constexpr int CPT = 5;  // chunks per thread per pass
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = g.K, NB = K >> 5, M = g.M;
-    const int items = M * NB;
+    const int K = g.K, KC = K >> 3, M = g.M;
+    const int nchunks = M * KC;
     const bool rms = g.in_mode == IN_RMSNORM;
-    const bool one = items <= NT;
-    float4 v[8];
-    if (one && tid < items) load_block(g.x + (size_t)(tid / NB) * g.ldx + (tid % NB) * 32, v);
+    const bool resident = nchunks <= CPT * NT;  // all chunks of the op in registers in one pass
+    Chunk8 c[CPT];
+    float sc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) sc[m] = 1.f;
+    if (resident) {
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+            const int ci = tid + j * NT;
+            if (ci < nchunks) {
+                const int m = ci / KC, off = (ci - m * KC) * 8;
+                const float4 *src = reinterpret_cast<const float4 *>(g.x + (size_t)m * g.ldx + off);
+                c[j].a = __ldcg(src);
+                c[j].b = __ldcg(src + 1);
+            }
+        }
+    }
     if (rms) {
         for (int i = tid; i < K / 4; i += NT)
             reinterpret_cast<float4 *>(nws)[i] = __ldg(reinterpret_cast<const float4 *>(g.norm_w) + i);
         double tk[MT];
 #pragma unroll
         for (int m = 0; m < MT; ++m) tk[m] = 0.0;
-        for (int it = tid; it < items; it += NT) {
-            const int m = it / NB, b = it - m * NB;
-            if (!one) load_block(g.x + (size_t)m * g.ldx + b * 32, v);
-            const double s = sumsq_block(v);
+        if (resident) {
 #pragma unroll
-            for (int mm = 0; mm < MT; ++mm)
-                if (mm == m) tk[mm] += s;
+            for (int j = 0; j < CPT; ++j) {
+                const int ci = tid + j * NT;
+                if (ci < nchunks) {
+                    const double s = sumsq8(c[j]);
+                    const int m = ci / KC;
+#pragma unroll
+                    for (int mm = 0; mm < MT; ++mm)
+                        if (mm == m) tk[mm] += s;
+                }
+            }
+        } else {
+            for (int ci = tid; ci < nchunks; ci += NT) {
+                const int m = ci / KC, off = (ci - m * KC) * 8;
+                const float4 *src = reinterpret_cast<const float4 *>(g.x + (size_t)m * g.ldx + off);
+                Chunk8 t;
+                t.a = __ldcg(src);
+                t.b = __ldcg(src + 1);
+                const double s = sumsq8(t);
+#pragma unroll
+                for (int mm = 0; mm < MT; ++mm)
+                    if (mm == m) tk[mm] += s;
+            }
         }
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
             const double t = warp_sum_d(tk[m]);
             if (lane == 0) tok[warp * tok_ld + m] = t;
         }
-        named_sync(bar_id, NT);  // tok and nws complete
-        if (tid < M) {
-            double tot = 0.0;
-            for (int w = 0; w < NT / 32; ++w) tot += tok[w * tok_ld + tid];
-            const float mean = (float)(tot / (double)K);
-            scale[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, g.eps)));
-        }
-        named_sync(bar_id, NT);
-    }
-    for (int it = tid; it < items; it += NT) {
-        const int m = it / NB, b = it - m * NB;
-        if (!one) load_block(g.x + (size_t)m * g.ldx + b * 32, v);
-        if (rms) {
-            const float sc = scale[m];
-            const float4 *nw = reinterpret_cast<const float4 *>(nws + b * 32);
+        named_sync(bar_id, NT);  // per-warp sums and norm weights complete
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float4 w4 = nw[j];
-                v[j].x = __fmul_rn(__fmul_rn(v[j].x, sc), w4.x);
-                v[j].y = __fmul_rn(__fmul_rn(v[j].y, sc), w4.y);
-                v[j].z = __fmul_rn(__fmul_rn(v[j].z, sc), w4.z);
-                v[j].w = __fmul_rn(__fmul_rn(v[j].w, sc), w4.w);
+        for (int m = 0; m < MT; ++m)
+            if (m < M) {
+                double tot = 0.0;
+                for (int w = 0; w < NT / 32; ++w) tot += tok[w * tok_ld + m];
+                const float mean = (float)(tot / (double)K);
+                sc[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, g.eps)));
             }
-        }
-        if (g.act_out != nullptr && write_act) {
-            float4 *dst = reinterpret_cast<float4 *>(g.act_out + (size_t)m * K + b * 32);
+    }
+    auto finish = [&](Chunk8 &ch, int ci, bool valid) {
+        const int m = valid ? ci / KC : 0, off = valid ? (ci - m * KC) * 8 : 0;
+        if (valid && rms) {
+            float s = sc[0];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) dst[j] = v[j];
+            for (int mm = 1; mm < MT; ++mm)
+                if (mm == m) s = sc[mm];
+            const float4 *nw = reinterpret_cast<const float4 *>(nws + off);
+            ch.a = mul4(ch.a, s, nw[0]);
+            ch.b = mul4(ch.b, s, nw[1]);
         }
-        tg_quant_block(v, xq + (size_t)m * K + b * 32, xd + m * NB + b);
+        if (valid && g.act_out != nullptr && write_act) {
+            float4 *dst = reinterpret_cast<float4 *>(g.act_out + (size_t)m * K + off);
+            dst[0] = ch.a;
+            dst[1] = ch.b;
+        }
+        quant_chunk(ch, valid, xq + (size_t)m * K + off, xd + m * (K >> 5) + (off >> 5), (off & 31) == 0);
+    };
+    if (resident) {
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+            const int ci = tid + j * NT;
+            if (j * NT < nchunks) finish(c[j], ci, ci < nchunks);  // warp-uniform guard: all lanes shuffle
+        }
+    } else {
+        for (int base = 0; base < nchunks; base += NT) {
+            const int ci = base + tid;
+            Chunk8 t;
+            t.a = t.b = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (ci < nchunks) {
+                const int m = ci / KC, off = (ci - m * KC) * 8;
+                const float4 *src = reinterpret_cast<const float4 *>(g.x + (size_t)m * g.ldx + off);
+                t.a = __ldcg(src);
+                t.b = __ldcg(src + 1);
+            }
+            finish(t, ci, ci < nchunks);
+        }
     }
 }
 
-// Epilogue of row tile rt: lane i < 4 stores row 4w + i (EPI_STORE, with the
-// residual resv[m] it prefetched) or, for SwiGLU, lane p < 2 stores output
-// pair p of the warp.  tot[i][m] are the warp-reduced row sums (all lanes).
+// Reduce a warp's 4 row partials (per token) across the 32 lanes with a
+// transposing butterfly: after it, lane L holds the sum of row
+// r = 2 * (L >> 4) + ((L >> 3) & 1), so lane 8r owns row r.  6 double
+// shuffles per token instead of 20 for four separate butterflies.
+__device__ __forceinline__ double reduce4_transpose(double a0, double a1, double a2, double a3, int lane) {
+    const bool hi16 = lane & 16;
+    // level xor 16: keep rows {0,1} (low half) or {2,3} (high half)
+    const double s0 = hi16 ? a0 : a2, s1 = hi16 ? a1 : a3;  // the pair this lane gives away
+    const double k0 = hi16 ? a2 : a0, k1 = hi16 ? a3 : a1;  // the pair it keeps
+    const double b0 = k0 + __shfl_xor_sync(0xffffffffu, s0, 16);
+    const double b1 = k1 + __shfl_xor_sync(0xffffffffu, s1, 16);
+    // level xor 8: keep the first (bit 3 clear) or second row of the pair
+    const bool hi8 = lane & 8;
+    double v = (hi8 ? b1 : b0) + __shfl_xor_sync(0xffffffffu, hi8 ? b0 : b1, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    return v;
+}
+
+// Epilogue of row tile rt for warp `warp`: tot[m] is this lane's reduced sum
+// of row r(lane) (see reduce4_transpose).  EPI_STORE: lane 8r stores row r
+// (+ the residual resv[m] it prefetched); EPI_SWIGLU: lane 16p stores output
+// pair p = silu(gate row 2p) * (up row 2p+1, fetched from lane 16p + 8).
 template <int MT>
-__device__ __forceinline__ void tg_emit(const TGemv &g, int rt, int warp, int lane, const double (&tot)[kTRW][MT],
+__device__ __forceinline__ void tg_emit(const TGemv &g, int rt, int warp, int lane, const double (&tot)[MT],
                                         const float (&resv)[MT]) {
     const int row0 = rt * kTR + warp * kTRW;
     if (g.epi == EPI_SWIGLU) {
-        if (lane < kTRW / 2) {
+        double up[MT];
 #pragma unroll
-            for (int p = 0; p < kTRW / 2; ++p)
-                if (p == lane)
+        for (int m = 0; m < MT; ++m) up[m] = __shfl_down_sync(0xffffffffu, tot[m], 8);
+        if ((lane & 15) == 0) {
+            const int p = lane >> 4;
 #pragma unroll
-                    for (int m = 0; m < MT; ++m)
-                        if (m < g.M)
-                            g.y[(size_t)m * g.ldy + row0 / 2 + p] =
-                                __fmul_rn(silu((float)tot[2 * p][m]), (float)tot[2 * p + 1][m]);
+            for (int m = 0; m < MT; ++m)
+                if (m < g.M)
+                    g.y[(size_t)m * g.ldy + row0 / 2 + p] = __fmul_rn(silu((float)tot[m]), (float)up[m]);
         }
-    } else if (lane < kTRW) {
+    } else if ((lane & 7) == 0) {
+        const int r = 2 * (lane >> 4) + ((lane >> 3) & 1);
 #pragma unroll
-        for (int i = 0; i < kTRW; ++i)
-            if (i == lane)
-#pragma unroll
-                for (int m = 0; m < MT; ++m)
-                    if (m < g.M) {
-                        const float val = (float)tot[i][m];
-                        g.y[(size_t)m * g.ldy + row0 + i] = g.res ? __fadd_rn(resv[m], val) : val;
-                    }
+        for (int m = 0; m < MT; ++m)
+            if (m < g.M) {
+                const float val = (float)tot[m];
+                g.y[(size_t)m * g.ldy + row0 + r] = g.res ? __fadd_rn(resv[m], val) : val;
+            }
     }
 }
 
 // Consumer (the kTNC consumer threads): this CTA's row tiles of one GEMV,
-// after the prologue filled xq / xd.  cs counts stages consumed over the
-// ring's lifetime.
+// after the prologue filled xq / xd.  The ring position (slot, phase) is
+// carried across ops by the caller.
 template <int MT>
 __device__ __forceinline__ void tg_consume(const TGemv &g, const uint8_t *ring, uint64_t *full, uint64_t *empty,
-                                           int nst, int &cs, const int8_t *xq, const float *xd, int cta, int G,
-                                           int *err) {
+                                           int nst, int &slot, uint32_t &phase, const int8_t *xq, const float *xd,
+                                           int cta, int G, int *err) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = g.K, NKT = K / kTK, NB = K >> 5, M = g.M;
-    long long u0, u1;
-    tg_range(g.R, K, cta, G, &u0, &u1);
-    double acc[kTRW][MT];
-#pragma unroll
-    for (int i = 0; i < kTRW; ++i)
-#pragma unroll
-        for (int m = 0; m < MT; ++m) acc[i][m] = 0.0;
-    float resv[MT];
-#pragma unroll
-    for (int m = 0; m < MT; ++m) resv[m] = 0.f;
+    const int RT = g.R / kTR;
+    const int rt0 = (int)((long long)RT * cta / G), rt1 = (int)((long long)RT * (cta + 1) / G);
     const int rbase = warp * kTRW;
-    for (long long u = u0; u < u1; ++u, ++cs) {
-        const int rt = (int)(u / NKT), kt = (int)(u - (long long)rt * NKT);
-        const int slot = cs % nst;
-        if (kt == 0 && g.res != nullptr && lane < kTRW) {
-            // residual of this lane's output row, needed at the row tile's end
-#pragma unroll
-            for (int m = 0; m < MT; ++m)
-                if (m < M) resv[m] = __ldcg(g.res + (size_t)m * g.ldres + (size_t)rt * kTR + rbase + lane);
-        }
-        // this lane's activation chunk of K-tile kt, per token
-        int4 xa[MT];
-        float xs[MT];
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-            const int mm = m < M ? m : 0;
-            xa[m] = *reinterpret_cast<const int4 *>(xq + (size_t)mm * K + kt * kTK + lane * 16);
-            xs[m] = xd[mm * NB + kt * (kTK / 32) + (lane >> 1)];
-        }
-        mbar_wait(&full[slot], (cs / nst) & 1, err, ERR_WAIT_FULL);
-        const uint8_t *t = ring + (size_t)slot * kTileBytes;
-        int4 wv[kTRW];
-        float dw[kTRW];
-#pragma unroll
-        for (int i = 0; i < kTRW; ++i) {
-            wv[i] = *reinterpret_cast<const int4 *>(t + (rbase + i) * kTK + lane * 16);
-            dw[i] = __half2float(reinterpret_cast<const __half *>(t + kTileQ)[(rbase + i) * (kTK / 32) + (lane >> 1)]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);  // data is in registers: the slot may refill
-#pragma unroll
-        for (int i = 0; i < kTRW; ++i)
-#pragma unroll
-            for (int m = 0; m < MT; ++m)
-                if (m < M) {
-                    int sh = dp4a(wv[i].x, xa[m].x, 0);
-                    sh = dp4a(wv[i].y, xa[m].y, sh);
-                    sh = dp4a(wv[i].z, xa[m].z, sh);
-                    sh = dp4a(wv[i].w, xa[m].w, sh);
-                    acc[i][m] += (double)sh * (double)__fmul_rn(dw[i], xs[m]);
-                }
-        if (kt != NKT - 1) continue;
-#pragma unroll
-        for (int i = 0; i < kTRW; ++i)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) acc[i][m] = warp_sum_d(acc[i][m]);
-        tg_emit<MT>(g, rt, warp, lane, acc, resv);
+    // lane 8r reads / writes row r of the warp's four (see reduce4_transpose)
+    const int my_row = 2 * (lane >> 4) + ((lane >> 3) & 1);
+    for (int rt = rt0; rt < rt1; ++rt) {
+        double acc[kTRW][MT];
 #pragma unroll
         for (int i = 0; i < kTRW; ++i)
 #pragma unroll
             for (int m = 0; m < MT; ++m) acc[i][m] = 0.0;
+        float resv[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) resv[m] = 0.f;
+        if (g.res != nullptr && (lane & 7) == 0) {
+            // residual of this lane's output row, needed at the row tile's end
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+                if (m < M) resv[m] = __ldcg(g.res + (size_t)m * g.ldres + (size_t)rt * kTR + rbase + my_row);
+        }
+        const int8_t *xql = xq + lane * 16;
+        const float *xdl = xd + (lane >> 1);
+        for (int kt = 0; kt < NKT; ++kt) {
+            // this lane's activation chunk of K-tile kt, per token
+            int4 xa[MT];
+            float xs[MT];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const int mm = m < M ? m : 0;
+                xa[m] = *reinterpret_cast<const int4 *>(xql + (size_t)mm * K + kt * kTK);
+                xs[m] = xdl[mm * NB + kt * (kTK / 32)];
+            }
+            mbar_wait(&full[slot], phase, err, ERR_WAIT_FULL);
+            const uint8_t *t = ring + (size_t)slot * kTileBytes;
+            int4 wv[kTRW];
+            float dw[kTRW];
+#pragma unroll
+            for (int i = 0; i < kTRW; ++i) {
+                wv[i] = *reinterpret_cast<const int4 *>(t + (rbase + i) * kTK + lane * 16);
+                dw[i] = __half2float(
+                    reinterpret_cast<const __half *>(t + kTileQ)[(rbase + i) * (kTK / 32) + (lane >> 1)]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);  // data is in registers: the slot may refill
+            if (++slot == nst) {
+                slot = 0;
+                phase ^= 1u;
+            }
+#pragma unroll
+            for (int i = 0; i < kTRW; ++i)
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                    if (m < M) {
+                        int sh = dp4a(wv[i].x, xa[m].x, 0);
+                        sh = dp4a(wv[i].y, xa[m].y, sh);
+                        sh = dp4a(wv[i].z, xa[m].z, sh);
+                        sh = dp4a(wv[i].w, xa[m].w, sh);
+                        acc[i][m] += (double)sh * (double)__fmul_rn(dw[i], xs[m]);
+                    }
+        }
+        double tot[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) tot[m] = reduce4_transpose(acc[0][m], acc[1][m], acc[2][m], acc[3][m], lane);
+        tg_emit<MT>(g, rt, warp, lane, tot, resv);
     }
 }
 
