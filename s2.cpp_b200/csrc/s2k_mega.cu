@@ -20,6 +20,7 @@
 #include "s2k_mega.h"
 
 #include <algorithm>
+#include <cstddef>
 
 namespace s2k {
 
@@ -31,7 +32,8 @@ constexpr int kMStages = 10;               // ring of 17 KB weight tiles
 constexpr int kMKMax = 10240;
 constexpr int kMaxT = 2;
 constexpr int kHD = 128;
-constexpr int kPtabMax = kMaxT * kMKMax / (int)sizeof(int);  // cached pages whose ids fit the staged table
+constexpr int kPtab = 512;                 // cached pages whose ids are staged in shared memory
+constexpr int kAttnKeys = 1024;            // longest key range whose scores stay on chip
 
 bool mega_gemv_ok(const MegaGemv &g) {
     if (!tg_shape_ok(g.R, g.K, g.M, g.in_mode, g.epi, g.res != nullptr, kMKMax, kMaxT)) return false;
@@ -42,20 +44,30 @@ bool mega_gemv_ok(const MegaGemv &g) {
 struct MSmem {
     uint8_t ring[kMStages][kTileBytes];
     uint64_t full[kMStages], empty[kMStages];
-    int8_t xq[kMaxT * kMKMax];  // quantized activation (GEMV); page table (attention)
+    int8_t xq[kMaxT * kMKMax];  // quantized activation (GEMV)
     float xd[kMaxT * kMKMax / 32];
-    float nw[kNormMax];
+    float nw[kNormMax];  // norm weights (GEMV); probabilities (attention)
     double tok[kMW][kMaxT];
     float scale[kMaxT];
     // attention
     float aq[kHD];
-    float ak[kMaxT][kHD], av[kMaxT][kHD];
+    double aqd[kHD];  // q as doubles for the score loops
+    alignas(16) float ak[kMaxT][kHD];  // read as float4
+    alignas(16) float av[kMaxT][kHD];
     double vpart[kMW][kHD];
     float red_f[kMW];
     double red_d[kMW];
+    int ptab[kPtab];  // page ids of the sequence's first kPtab pages (Slow segment)
+    int ptab_ready;
 };
 
 static_assert(sizeof(MSmem) <= 227 * 1024, "persistent kernel shared memory exceeds the per-CTA limit");
+static_assert(kAttnKeys <= kNormMax, "attention probabilities live in the norm-weight buffer");
+// shared arrays read with 16-byte vector loads
+static_assert(offsetof(MSmem, ring) % 16 == 0 && kTileBytes % 16 == 0, "ring alignment");
+static_assert(offsetof(MSmem, xq) % 16 == 0 && offsetof(MSmem, nw) % 16 == 0, "activation buffer alignment");
+static_assert(offsetof(MSmem, ak) % 16 == 0 && offsetof(MSmem, av) % 16 == 0, "key / value row alignment");
+static_assert(kAttnKeys % kMNC == 0, "keys per thread");
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     unsigned v;
@@ -127,26 +139,27 @@ __device__ void mega_gemv(const MegaGemv &gref, MSmem &sm, int cta, int G, int &
 // ---------------------------------------------------------------------------
 // attention op: one CTA per (token, query head) unit
 // ---------------------------------------------------------------------------
-// x0/x1 = pair (2i, 2i+1) of a head vector held by 64 threads (i = thread);
-// optional per-head RMSNorm (reduction over the 64 threads of warps w0, w0+1)
-// then RoPE from the table.
-__device__ __forceinline__ void head_norm_rope(float &x0, float &x1, const float *nw, float eps, const float2 *rope,
-                                               int pos, int i, int red_slot, MSmem &sm, bool active) {
-    if (nw) {
+// x0/x1 = pair (2i, 2i+1) of a head vector held by 64 consecutive threads
+// (i = index in the group); optional per-head RMSNorm (nw0/nw1 = the pair's
+// norm weights, prefetched; reduction over the 64 threads of warps w0, w0+1,
+// partial sums in red_d[red_slot..+1]) then RoPE with the prefetched (cos,
+// sin) of the pair.  Every consumer thread must call it (one named barrier).
+__device__ __forceinline__ void head_norm_rope(float &x0, float &x1, bool has_norm, float nw0, float nw1, float eps,
+                                               float2 cs, int red_slot, MSmem &sm, bool active) {
+    if (has_norm) {
         double s = active ? (double)__fmul_rn(x0, x0) + (double)__fmul_rn(x1, x1) : 0.0;
         s = warp_sum_d(s);
-        if ((threadIdx.x & 31) == 0 && threadIdx.x < 64) sm.red_d[red_slot + (threadIdx.x >> 5)] = s;
+        if ((threadIdx.x & 31) == 0 && active) sm.red_d[red_slot + ((threadIdx.x >> 5) & 1)] = s;
     }
     named_sync(3, kMNC);
     if (active) {
-        if (nw) {
+        if (has_norm) {
             const double tot = sm.red_d[red_slot] + sm.red_d[red_slot + 1];
             const float mean = (float)(tot / (double)kHD);
             const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-            x0 = __fmul_rn(__fmul_rn(x0, sc), nw[2 * i]);
-            x1 = __fmul_rn(__fmul_rn(x1, sc), nw[2 * i + 1]);
+            x0 = __fmul_rn(__fmul_rn(x0, sc), nw0);
+            x1 = __fmul_rn(__fmul_rn(x1, sc), nw1);
         }
-        const float2 cs = rope[(size_t)pos * (kHD / 2) + i];
         const float y0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
         const float y1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
         x0 = y0;
@@ -160,64 +173,147 @@ __device__ __forceinline__ const float *key_ptr_f32(const MegaAttn &a, MSmem &sm
     return value ? sm.av[c - a.cur_base] : sm.ak[c - a.cur_base];
 }
 
-// Row of cached key/value position j for kv head g in the paged f16 cache.
+// Row of cached key/value position j for kv head g in the paged f16 cache;
+// ptab holds the first kPtab page ids of the sequence (staged per segment).
 __device__ __forceinline__ const __half *kv_row(const MegaAttn &a, const __half *base, const int *ptab, int g, int j) {
     const int pg = j / kPage, slot = j - pg * kPage;
-    const int page = pg < kPtabMax ? ptab[pg] : __ldcg(a.block_table + pg);
+    const int page = pg < kPtab ? ptab[pg] : __ldcg(a.block_table + pg);
     return base + ((((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage + slot) * kHD;
 }
 
+// Dot product of a cached f16 key row (16 x 16 bytes, already loaded) with q.
+__device__ __forceinline__ float key_score(const uint4 (&raw)[kHD / 8], const double *aq, float scale) {
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+#pragma unroll
+    for (int c = 0; c < kHD / 8; ++c) {
+        const int d = 8 * c;
+        const __half2 *hh = reinterpret_cast<const __half2 *>(&raw[c]);
+        const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
+        const float2 f2 = __half22float2(hh[2]), f3 = __half22float2(hh[3]);
+        s0 += (double)f0.x * aq[d] + (double)f0.y * aq[d + 1];
+        s1 += (double)f1.x * aq[d + 2] + (double)f1.y * aq[d + 3];
+        s2 += (double)f2.x * aq[d + 4] + (double)f2.y * aq[d + 5];
+        s3 += (double)f3.x * aq[d + 6] + (double)f3.y * aq[d + 7];
+    }
+    return __fmul_rn((float)((s0 + s1) + (s2 + s3)), scale);
+}
+
+// Attention of one (token t, query head h) unit per CTA (restates
+// src/s2_model.cpp:979-1039: qk-norm, RoPE mode 0, f16 cache of past
+// positions + f32 keys/values of this call, GQA h -> h / (H / Hkv), exact
+// softmax, weighted value sum).
+//
+// Latency plan: every global load that does not depend on another is issued
+// at the start of the unit -- q / k / v of this call, norm weights, RoPE
+// (cos, sin) -- together with L2 prefetches of the cached key and value rows,
+// so the key and value loads after the q / k normalization hit L2.  Scores stay in registers and the
+// probabilities in shared memory (up to kAttnKeys keys; longer contexts go
+// through the global score scratch).
 __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    int *const ptab = reinterpret_cast<int *>(sm.xq);
     const int units = a.T * a.H;
     const int grp = a.H / a.Hkv;
+    float *const pbuf = sm.nw;  // probabilities (the GEMV norm buffer is idle during attention)
+    if (a.kv_k && cta < units && !sm.ptab_ready) {
+        // the block table and n_past do not change within a segment: stage the
+        // page ids once, at the first attention op this CTA runs
+        const int nc = a.n_cached_from_pos_base && a.pos_base ? __ldcg(a.pos_base) : 0;
+        const int npg = min((nc + kPage - 1) / kPage, kPtab);
+        for (int i = tid; i < npg; i += kMNC) sm.ptab[i] = __ldcg(a.block_table + i);
+        named_sync(3, kMNC);
+        if (tid == 0) sm.ptab_ready = 1;
+    }
     for (int u = cta; u < units; u += G) {
         const int t = u / a.H, h = u - t * a.H, g = h / grp;
         const int base = a.pos_base ? __ldcg(a.pos_base) : 0;
         const int nc = a.n_cached_from_pos_base ? base : 0;
         const int pos0 = base + a.pos_add;
-        // page table of the cached keys, staged in the (idle) GEMV activation buffer
-        const int npg = a.kv_k ? (nc + kPage - 1) / kPage : 0;
-        for (int i = tid; i < min(npg, kPtabMax); i += kMNC) ptab[i] = __ldcg(a.block_table + i);
-        // 1. q of (t, h): threads 0..63 (pair i)
-        {
-            const bool act = tid < 64;
-            const int i = tid & 63;
-            float x0 = 0.f, x1 = 0.f;
-            if (act) {
-                const float *src = a.qkv + (size_t)t * a.ldqkv + (size_t)h * kHD;
-                x0 = __ldcg(src + 2 * i);
-                x1 = __ldcg(src + 2 * i + 1);
+        const int Lk = nc + a.cur_base + t + 1;
+        const bool in_smem = Lk <= kAttnKeys;
+        if (pos0 + t >= a.rope_positions && tid == 0) atomicOr(err, ERR_BAD_POS);
+        // ---- A. independent loads ----
+        const int i = tid & 63;
+        const bool grp_q = tid < 64, grp_k = tid >= 64 && tid < 128, grp_v = tid >= 128 && tid < 192;
+        float qx0 = 0.f, qx1 = 0.f, qn0 = 0.f, qn1 = 0.f;
+        float2 qcs = make_float2(0.f, 0.f);
+        float kx0[kMaxT], kx1[kMaxT], vx0[kMaxT], vx1[kMaxT];
+        float2 kcs[kMaxT];
+        float kn0 = 0.f, kn1 = 0.f;
+        if (grp_q) {
+            const float *src = a.qkv + (size_t)t * a.ldqkv + (size_t)h * kHD;
+            qx0 = __ldcg(src + 2 * i);
+            qx1 = __ldcg(src + 2 * i + 1);
+            if (a.q_norm) {
+                qn0 = __ldg(a.q_norm + 2 * i);
+                qn1 = __ldg(a.q_norm + 2 * i + 1);
             }
-            if (pos0 + t >= a.rope_positions) {
-                if (tid == 0) atomicOr(err, ERR_BAD_POS);
-            }
-            head_norm_rope(x0, x1, a.q_norm, a.eps, a.rope, min(pos0 + t, a.rope_positions - 1), i,
-                           0, sm, act);
-            if (act) {
-                sm.aq[2 * i] = x0;
-                sm.aq[2 * i + 1] = x1;
+            qcs = __ldg(a.rope + (size_t)min(pos0 + t, a.rope_positions - 1) * (kHD / 2) + i);
+        }
+#pragma unroll
+        for (int tt = 0; tt < kMaxT; ++tt) {
+            kx0[tt] = kx1[tt] = vx0[tt] = vx1[tt] = 0.f;
+            kcs[tt] = make_float2(0.f, 0.f);
+            if (tt <= t) {
+                const float *row = a.qkv + (size_t)tt * a.ldqkv;
+                if (grp_k) {
+                    kx0[tt] = __ldcg(row + (size_t)(a.H + g) * kHD + 2 * i);
+                    kx1[tt] = __ldcg(row + (size_t)(a.H + g) * kHD + 2 * i + 1);
+                    kcs[tt] = __ldg(a.rope + (size_t)min(pos0 + tt, a.rope_positions - 1) * (kHD / 2) + i);
+                }
+                if (grp_v) {
+                    vx0[tt] = __ldcg(row + (size_t)(a.H + a.Hkv + g) * kHD + 2 * i);
+                    vx1[tt] = __ldcg(row + (size_t)(a.H + a.Hkv + g) * kHD + 2 * i + 1);
+                }
             }
         }
-        // 2. k, v of the op's tokens 0..t for kv head g
+        if (grp_k && a.k_norm) {
+            kn0 = __ldg(a.k_norm + 2 * i);
+            kn1 = __ldg(a.k_norm + 2 * i + 1);
+        }
+        // cached key and value rows -> L2 while q and k are normalized
+        for (int j = tid; j < nc; j += kMNC) {
+            const char *kp = reinterpret_cast<const char *>(kv_row(a, a.kv_k, sm.ptab, g, j));
+            const char *vp = reinterpret_cast<const char *>(kv_row(a, a.kv_v, sm.ptab, g, j));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(kp));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(kp + 128));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(vp));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(vp + 128));
+        }
+        // ---- B. q: norm + RoPE ----
+        head_norm_rope(qx0, qx1, a.q_norm != nullptr, qn0, qn1, a.eps, qcs, 0, sm, grp_q);
+        if (grp_q) {
+            sm.aq[2 * i] = qx0;
+            sm.aq[2 * i + 1] = qx1;
+            sm.aqd[2 * i] = (double)qx0;
+            sm.aqd[2 * i + 1] = (double)qx1;
+        }
+        // ---- C. k, v of this call's tokens 0..t ----
         for (int tt = 0; tt <= t; ++tt) {
-            const bool actk = tid < 64, actv = tid >= 64 && tid < 128;
-            const int i = tid & 63;
-            const float *row = a.qkv + (size_t)tt * a.ldqkv;
-            float x0 = 0.f, x1 = 0.f;
-            if (actk) {
-                x0 = __ldcg(row + (size_t)(a.H + g) * kHD + 2 * i);
-                x1 = __ldcg(row + (size_t)(a.H + g) * kHD + 2 * i + 1);
-            }
-            head_norm_rope(x0, x1, a.k_norm, a.eps, a.rope, min(pos0 + tt, a.rope_positions - 1), i, 2, sm, actk);
-            if (actk) {
+            float x0 = kx0[0], x1 = kx1[0];
+            float2 cs = kcs[0];
+#pragma unroll
+            for (int q = 1; q < kMaxT; ++q)
+                if (q == tt) {
+                    x0 = kx0[q];
+                    x1 = kx1[q];
+                    cs = kcs[q];
+                }
+            // k pairs sit on threads 64..127 (warps 2, 3): reduction slots 2, 3
+            head_norm_rope(x0, x1, a.k_norm != nullptr, kn0, kn1, a.eps, cs, 2, sm, grp_k);
+            if (grp_k) {
                 sm.ak[tt][2 * i] = x0;
                 sm.ak[tt][2 * i + 1] = x1;
             }
-            if (actv) {
-                sm.av[tt][2 * i] = __ldcg(row + (size_t)(a.H + a.Hkv + g) * kHD + 2 * i);
-                sm.av[tt][2 * i + 1] = __ldcg(row + (size_t)(a.H + a.Hkv + g) * kHD + 2 * i + 1);
+            if (grp_v) {
+                float v0 = vx0[0], v1 = vx1[0];
+#pragma unroll
+                for (int q = 1; q < kMaxT; ++q)
+                    if (q == tt) {
+                        v0 = vx0[q];
+                        v1 = vx1[q];
+                    }
+                sm.av[tt][2 * i] = v0;
+                sm.av[tt][2 * i + 1] = v1;
             }
         }
         named_sync(3, kMNC);
@@ -238,47 +334,30 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
                 }
             }
         }
-        // 3. scores
-        const int Lk = nc + a.cur_base + t + 1;
-        float *sc = a.scores + (size_t)u * a.ld_scores;
-        float mx = -INFINITY;
-        for (int j = tid; j < Lk; j += kMNC) {
-            double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
-            if (j < nc) {
-                // the whole 256-byte key row in flight at once
-                const uint4 *kp = reinterpret_cast<const uint4 *>(kv_row(a, a.kv_k, ptab, g, j));
-                uint4 raw[kHD / 8];
+        // ---- D. scores -> sc (pbuf in shared memory when the keys fit) ----
+        float *const sc = in_smem ? pbuf : a.scores + (size_t)u * a.ld_scores;
+        // cached keys: one f16 row per thread (rows were prefetched into L2)
+        for (int j = tid; j < nc; j += kMNC) {
+            const uint4 *kp = reinterpret_cast<const uint4 *>(kv_row(a, a.kv_k, sm.ptab, g, j));
+            uint4 raw[kHD / 8];
 #pragma unroll
-                for (int c = 0; c < kHD / 8; ++c) raw[c] = __ldcg(kp + c);
-#pragma unroll
-                for (int c = 0; c < kHD / 8; ++c) {
-                    const int d = 8 * c;
-                    const __half2 *hh = reinterpret_cast<const __half2 *>(&raw[c]);
-                    const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
-                    const float2 f2 = __half22float2(hh[2]), f3 = __half22float2(hh[3]);
-                    s0 += (double)f0.x * (double)sm.aq[d] + (double)f0.y * (double)sm.aq[d + 1];
-                    s1 += (double)f1.x * (double)sm.aq[d + 2] + (double)f1.y * (double)sm.aq[d + 3];
-                    s2 += (double)f2.x * (double)sm.aq[d + 4] + (double)f2.y * (double)sm.aq[d + 5];
-                    s3 += (double)f3.x * (double)sm.aq[d + 6] + (double)f3.y * (double)sm.aq[d + 7];
-                }
-            } else {
-                const int c = j - nc;
-                const float *kp = key_ptr_f32(a, sm, c, g, false);
-                const bool gl = c < a.cur_base;
-#pragma unroll 4
-                for (int d = 0; d < kHD; d += 4) {
-                    const float k0 = gl ? __ldcg(kp + d) : kp[d], k1 = gl ? __ldcg(kp + d + 1) : kp[d + 1];
-                    const float k2 = gl ? __ldcg(kp + d + 2) : kp[d + 2], k3 = gl ? __ldcg(kp + d + 3) : kp[d + 3];
-                    s0 += (double)k0 * (double)sm.aq[d];
-                    s1 += (double)k1 * (double)sm.aq[d + 1];
-                    s2 += (double)k2 * (double)sm.aq[d + 2];
-                    s3 += (double)k3 * (double)sm.aq[d + 3];
-                }
-            }
-            const float s = __fmul_rn((float)((s0 + s1) + (s2 + s3)), a.scale);
-            sc[j] = s;
-            mx = fmaxf(mx, s);
+            for (int c = 0; c < kHD / 8; ++c) raw[c] = __ldcg(kp + c);
+            sc[j] = key_score(raw, sm.aqd, a.scale);
         }
+        // keys of this call (f32 rows): one warp per key, lane = 4 dims
+        for (int c = warp; c < Lk - nc; c += kMW) {
+            const bool gl = c < a.cur_base;
+            const float4 k4 = gl ? __ldcg(reinterpret_cast<const float4 *>(key_ptr_f32(a, sm, c, g, false)) + lane)
+                                 : reinterpret_cast<const float4 *>(key_ptr_f32(a, sm, c, g, false))[lane];
+            double p = (double)k4.x * sm.aqd[4 * lane] + (double)k4.y * sm.aqd[4 * lane + 1] +
+                       (double)k4.z * sm.aqd[4 * lane + 2] + (double)k4.w * sm.aqd[4 * lane + 3];
+            p = warp_sum_d(p);
+            if (lane == 0) sc[nc + c] = __fmul_rn((float)p, a.scale);
+        }
+        named_sync(3, kMNC);
+        // ---- E. exact softmax: max, sum in double, p' = exp(s - max) * (1 / sum) ----
+        float mx = -INFINITY;
+        for (int j = tid; j < Lk; j += kMNC) mx = fmaxf(mx, sc[j]);
         mx = warp_max(mx);
         if (lane == 0) sm.red_f[warp] = mx;
         named_sync(3, kMNC);
@@ -287,34 +366,30 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
         double sum = 0.0;
         for (int j = tid; j < Lk; j += kMNC) sum += (double)det_expf(__fsub_rn(sc[j], mx));
         sum = warp_sum_d(sum);
-        named_sync(3, kMNC);  // red_f reads done before red_d / red_f reuse
         if (lane == 0) sm.red_d[warp] = sum;
         named_sync(3, kMNC);
         double tot = 0.0;
         for (int w = 0; w < kMW; ++w) tot += sm.red_d[w];
         const float inv = (float)(1.0 / tot);
         for (int j = tid; j < Lk; j += kMNC) sc[j] = __fmul_rn(det_expf(__fsub_rn(sc[j], mx)), inv);
+        float *const pr = sc;
         named_sync(3, kMNC);
-        // 4. values: warp w takes keys w, w + kMW, ...; lane takes dims 4*lane..4*lane+3.
-        // kVU keys per warp are loaded before any is used.
+        // ---- F. values: warp w takes keys w, w + kMW, ...; lane takes dims 4*lane..4*lane+3;
+        // kVU keys per warp are loaded before any is used (rows were prefetched into L2) ----
         {
-            constexpr int kVU = 8;
+            constexpr int kVU = 16;
             double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
             int j = warp;
             for (; j + (kVU - 1) * kMW < nc; j += kVU * kMW) {
                 uint2 raw[kVU];
-                float pr[kVU];
 #pragma unroll
-                for (int q = 0; q < kVU; ++q) {
-                    const int jj = j + q * kMW;
-                    raw[q] = __ldcg(reinterpret_cast<const uint2 *>(kv_row(a, a.kv_v, ptab, g, jj) + 4 * lane));
-                    pr[q] = sc[jj];
-                }
+                for (int q = 0; q < kVU; ++q)
+                    raw[q] = __ldcg(reinterpret_cast<const uint2 *>(kv_row(a, a.kv_v, sm.ptab, g, j + q * kMW) + 4 * lane));
 #pragma unroll
                 for (int q = 0; q < kVU; ++q) {
                     const __half2 *hh = reinterpret_cast<const __half2 *>(&raw[q]);
                     const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
-                    const double pd = (double)pr[q];
+                    const double pd = (double)pr[j + q * kMW];
                     acc0 += (double)f0.x * pd;
                     acc1 += (double)f0.y * pd;
                     acc2 += (double)f1.x * pd;
@@ -322,10 +397,10 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
                 }
             }
             for (; j < nc; j += kMW) {
-                const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(kv_row(a, a.kv_v, ptab, g, j) + 4 * lane));
+                const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(kv_row(a, a.kv_v, sm.ptab, g, j) + 4 * lane));
                 const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
                 const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
-                const double pd = (double)sc[j];
+                const double pd = (double)pr[j];
                 acc0 += (double)f0.x * pd;
                 acc1 += (double)f0.y * pd;
                 acc2 += (double)f1.x * pd;
@@ -337,7 +412,7 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
                 const bool gl = c < a.cur_base;
                 const float v0 = gl ? __ldcg(vp) : vp[0], v1 = gl ? __ldcg(vp + 1) : vp[1];
                 const float v2 = gl ? __ldcg(vp + 2) : vp[2], v3 = gl ? __ldcg(vp + 3) : vp[3];
-                const double pd = (double)sc[nc + c];
+                const double pd = (double)pr[nc + c];
                 acc0 += (double)v0 * pd;
                 acc1 += (double)v1 * pd;
                 acc2 += (double)v2 * pd;
@@ -357,8 +432,6 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
         named_sync(3, kMNC);
     }
 }
-
-
 
 __device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err) {
     const int stride = e.ncb + 1;
@@ -423,6 +496,7 @@ __global__ void __launch_bounds__(kMThreads, 1)
             mbar_init(&sm.empty[i], kMW);
         }
         fence_mbar_init();
+        sm.ptab_ready = 0;
     }
     __syncthreads();
     if (warp == kMW) {
