@@ -30,6 +30,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "s2.cpp_b200"))
 
+import shard  # noqa: E402
 import synthetic  # noqa: E402
 
 PROMPT = 64
@@ -171,9 +172,7 @@ def main() -> None:
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    rank, world, local = shard.dist_env()
 
     if args.impl == "reference":
         run_reference(args, rank)
@@ -185,10 +184,8 @@ def main() -> None:
 
     dist_on = world > 1
     if dist_on:
-        import datetime
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
-                                device_id=torch.device("cuda", local))
+        shard.init("nccl", local, timeout_s=300)
     torch.cuda.set_device(local)
     hp = synthetic.preset(args.preset)
     threads = max(1, (os.cpu_count() or 8) // max(world, 1))
@@ -201,13 +198,14 @@ def main() -> None:
         del tensors
         tensors = None
     frames = args.frames
-    prompt = synthetic.text_prompt(hp, PROMPT, seed=7 + rank)  # this rank's utterance
+    utt = shard.utterance_for_rank(rank)  # this rank's utterance
+    prompt = synthetic.text_prompt(hp, PROMPT, seed=utt["prompt_seed"])
     m.init_kv_cache(PROMPT + frames + 1)  # + 1: the slot the kernel profile below writes
     d_prompt = torch.from_numpy(np.ascontiguousarray(prompt.T)).to(f"cuda:{local}")
     d_codes = torch.zeros((hp.num_codebooks, frames), dtype=torch.int32, device=f"cuda:{local}")
     stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
     kw = dict(temperature=0.0, top_p=0.8, top_k=30, min_tokens_before_end=frames, im_end_id=-1, seed=SEED,
-              seq_id=rank)
+              seq_id=utt["seq_id"])
 
     def step():
         n = m.generate_device(d_prompt.data_ptr(), PROMPT, d_codes.data_ptr(), frames, **kw)
@@ -232,11 +230,9 @@ def main() -> None:
     ms = ev0.elapsed_time(ev1)
     if dist_on:
         dist.barrier()
-        t = torch.tensor([ms], device=f"cuda:{local}", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = shard.max_over_ranks(ms, f"cuda:{local}")
     ms_per_step = ms / args.steps
-    value = world * args.steps * frames / (ms / 1e3)
+    value = shard.aggregate_rate(world, args.steps, frames, ms)
 
     # end to end through the host API: host prompt in, host codes out
     e2e_times = []
@@ -246,12 +242,8 @@ def main() -> None:
         out = m.generate(prompt, frames, **kw)
         e2e_times.append(time.perf_counter() - a)
         assert out.shape == (hp.num_codebooks, frames)
-    e2e_s = float(np.sum(e2e_times))
-    if dist_on:
-        t = torch.tensor([e2e_s], device=f"cuda:{local}", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e_value = world * args.steps * frames / e2e_s
+    e2e_s = shard.max_over_ranks(float(np.sum(e2e_times)), f"cuda:{local}")
+    e2e_value = shard.aggregate_rate(world, args.steps, frames, e2e_s * 1e3)
 
     # dominant kernel: the persistent decode kernel (mega_kernel), one launch per
     # Fast-AR pass and one per Slow step; each launch event-timed on its stream
