@@ -41,6 +41,16 @@ WORKLOAD = ("dual-AR frame loop, S2 Pro shape (36+4 layers, d2560, GQA 32/8, ff 
             "Q8_0, bs=1: 64-token text prompt prefill + 200 greedy frames")
 
 
+# DRAM traffic / algorithmic bytes of the persistent kernel, measured with
+# ncu (dram__bytes_read.sum + dram__bytes_write.sum) on the same kernel with
+# 2 Slow + 1 Fast-AR layers at full widths (bench.py --preset mid, launches
+# 18 and 19): Slow segment 644.02 MB for 638.36 MB, Fast-AR segment 122.31 MB
+# for 118.37 MB.  Traffic grows with the bytes streamed, so full-size
+# launches are scaled by these ratios.
+TRAFFIC_RATIO_SLOW = 644.02 / 638.36
+TRAFFIC_RATIO_FAST = 122.31 / 118.37
+
+
 def peaks() -> dict:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -280,7 +290,10 @@ def main() -> None:
             "roofline": {"bound": "hbm", "kernel": "mega_kernel (persistent decode kernel, 9 Fast-pass + 1 Slow-step "
                                                    "launches per frame)",
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                         "peak_src": pk["src"], "traffic": None, "bytes_per_launch": mk_bytes,
+                         "peak_src": pk["src"],
+                         "traffic": (TRAFFIC_RATIO_SLOW * b_s + nf * TRAFFIC_RATIO_FAST * b_f) / (nf + 1),
+                         "traffic_src": "ncu dram bytes of the same kernel at 2+1 layers, scaled by bytes streamed",
+                         "bytes_per_launch": mk_bytes,
                          "launch_ms": mk_ms, "slow_launch": {"ms": ms_s, "bytes": b_s},
                          "fast_launch": {"ms": ms_f, "bytes": b_f}},
             "gemv_roofline": {"kernel": "gemv_q8_0 (standalone, s2k_eval path): Slow-step weight GEMV chain",
