@@ -224,6 +224,32 @@ S2K_API s2k_status s2k_profile_gemv(s2k_model *m, int32_t reps, double *bytes_pe
 S2K_API s2k_status s2k_profile_frame(s2k_model *m, s2k_seq *s, int32_t reps, double *ms_slow,
                                      double *ms_fast, double *bytes_slow, double *bytes_fast);
 
+/* Profiling hook for the persistent decode kernel (no reference counterpart).
+ * Same preconditions as s2k_profile_frame.  Launches segment `segment` of the
+ * sequence's frame program `reps` times (1..64; segments 0..num_codebooks-2 are
+ * the Fast-AR passes, the last is the Slow step without its n_past advance)
+ * with an in-kernel trace: op i's time is from the grid barrier that releases
+ * it to the one that releases op i+1, as CTA 0 sees them (globaltimer), so it
+ * includes that op's barrier.  op_us[i] gets the mean in microseconds and
+ * op_kind[i] the op kind (1 GEMV, 2 attention, 3 Slow embedding, 4 Fast
+ * embedding); *n_ops the number of ops (at most cap). */
+S2K_API s2k_status s2k_profile_ops(s2k_model *m, s2k_seq *s, int32_t segment, int32_t reps, double *op_us,
+                                   int32_t *op_kind, int32_t cap, int32_t *n_ops);
+
+/* Profiling hook for the persistent decode kernel (no reference counterpart).
+ * Same preconditions as s2k_profile_ops.  Launches segment `segment` twice
+ * with the in-kernel trace and returns the second launch's stamps:
+ * stamps[((op * n_ctas) + cta) * 8 + k], globaltimer nanoseconds (0 where a
+ * stamp does not apply), for op = 0..n_ops (the entry at op = n_ops is the
+ * end of the launch, k = 0 only) and k = 0 op start (its grid barrier
+ * released), 1 GEMV activation prologue done, 2 op work done, 3 the CTA's
+ * producer warp issued the op's last weight tile, 4 RMSNorm partial sums
+ * formed, 5 RMSNorm scale known, 6 first weight tile ready, 7 activation
+ * quantized (before the CTA barrier that ends the prologue).  cap is the
+ * capacity of stamps in entries. */
+S2K_API s2k_status s2k_profile_trace(s2k_model *m, s2k_seq *s, int32_t segment, uint64_t *stamps, size_t cap,
+                                     int32_t *n_ops, int32_t *n_ctas);
+
 /* Debugging aid (no reference counterpart): copies up to nbytes of a named
  * device buffer to host memory.  Names: "x", "h", "qkv", "attn", "ff",
  * "kcur", "vcur", "logits", "hidden" (Slow workspace), "fx", "fh", "fqkv",

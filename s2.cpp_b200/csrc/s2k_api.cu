@@ -1451,6 +1451,89 @@ S2K_API s2k_status s2k_profile_frame(s2k_model *m, s2k_seq *s, int32_t reps, dou
     return check_err_word(m);
 }
 
+// Runs `reps` traced launches of one frame-program segment (the Slow step
+// without its n_past advance) and returns the stamps of every launch,
+// [rep][op][cta][kTraceSlots] (launch_mega's trace layout).
+static s2k_status trace_segment(s2k_model *m, s2k_seq *s, int segment, int reps, std::vector<unsigned long long> &tr,
+                                int *len_out, std::vector<int> *kinds) {
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    if (!s->frame_exec || s->frame_gen != m->ws_gen || !s->use_mega || s->seg_start.empty())
+        return fail(S2K_ERR_STATE, "no persistent-kernel frame program for this sequence (run generate first)");
+    const int nseg = (int)s->seg_start.size();
+    if (segment < 0 || segment >= nseg) return fail(S2K_ERR_ARG, "segment %d outside 0..%d", segment, nseg - 1);
+    if (s->n_past >= s->max_seq_len)
+        return fail(S2K_ERR_KV_FULL, "profiling writes position n_past = %d; the sequence holds %d", s->n_past,
+                    s->max_seq_len);
+    // the Slow segment ends with the n_past advance: leave it out
+    const int len = s->seg_len[segment] - (segment == nseg - 1 ? 1 : 0);
+    if (kinds) {
+        std::vector<MegaOp> hops((size_t)len);
+        CU(cudaMemcpy(hops.data(), s->mega_ops + s->seg_start[segment], (size_t)len * sizeof(MegaOp),
+                      cudaMemcpyDeviceToHost));
+        kinds->resize((size_t)len);
+        for (int i = 0; i < len; ++i) (*kinds)[(size_t)i] = hops[(size_t)i].kind;
+    }
+    const size_t per = (size_t)(len + 1) * m->num_sms * kTraceSlots;
+    unsigned long long *d_tr = nullptr;
+    CU(m->alloc(&d_tr, (size_t)reps * per));
+    CU(cudaMemsetAsync(d_tr, 0, (size_t)reps * per * sizeof(unsigned long long), m->stream));
+    MegaCtl *ctl = s->mega_ctl + segment;
+    cudaError_t err = cudaSuccess;
+    for (int r = 0; r < reps && err == cudaSuccess; ++r) {
+        if ((err = cudaMemsetAsync(ctl, 0, sizeof(MegaCtl), m->stream))) break;
+        err = launch_mega(s->mega_ops + s->seg_start[segment], len, s->seg_mt[segment], ctl, nullptr, m->d_err,
+                          m->num_sms, m->stream, d_tr + (size_t)r * per);
+    }
+    tr.assign((size_t)reps * per, 0ull);
+    if (err == cudaSuccess)
+        err = cudaMemcpyAsync(tr.data(), d_tr, tr.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                              m->stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(m->stream);
+    m->release(d_tr);
+    CU(err);
+    *len_out = len;
+    return check_err_word(m);
+}
+
+S2K_API s2k_status s2k_profile_ops(s2k_model *m, s2k_seq *s, int32_t segment, int32_t reps, double *op_us,
+                                   int32_t *op_kind, int32_t cap, int32_t *n_ops) {
+    if (!m || !s || reps <= 0 || reps > 64 || !op_us || !op_kind || cap <= 0 || !n_ops)
+        return fail(S2K_ERR_ARG, "bad argument (1 <= reps <= 64)");
+    std::vector<unsigned long long> tr;
+    std::vector<int> kinds;
+    int len = 0;
+    s2k_status rc = trace_segment(m, s, segment, reps, tr, &len, &kinds);
+    if (rc) return rc;
+    if (len > cap) return fail(S2K_ERR_ARG, "segment %d has %d ops, capacity %d", segment, len, cap);
+    const size_t G = (size_t)m->num_sms, per = (size_t)(len + 1) * G * kTraceSlots;
+    for (int i = 0; i < len; ++i) {
+        double t = 0;
+        for (int r = 0; r < reps; ++r) {
+            const unsigned long long *b = tr.data() + (size_t)r * per;
+            t += (double)(b[(size_t)(i + 1) * G * kTraceSlots] - b[(size_t)i * G * kTraceSlots]);  // CTA 0 starts
+        }
+        op_us[i] = t / reps / 1e3;
+        op_kind[i] = kinds[(size_t)i];
+    }
+    *n_ops = len;
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_profile_trace(s2k_model *m, s2k_seq *s, int32_t segment, uint64_t *stamps, size_t cap,
+                                     int32_t *n_ops, int32_t *n_ctas) {
+    if (!m || !s || !stamps || !n_ops || !n_ctas) return fail(S2K_ERR_ARG, "NULL argument");
+    std::vector<unsigned long long> tr;
+    int len = 0;
+    s2k_status rc = trace_segment(m, s, segment, 2, tr, &len, nullptr);  // the first launch warms up
+    if (rc) return rc;
+    const size_t per = tr.size() / 2;
+    if (per > cap) return fail(S2K_ERR_ARG, "trace needs %zu entries, capacity %zu", per, cap);
+    memcpy(stamps, tr.data() + per, per * sizeof(uint64_t));
+    *n_ops = len;
+    *n_ctas = m->num_sms;
+    return S2K_OK;
+}
+
 S2K_API s2k_status s2k_debug_copy(s2k_model *m, s2k_seq *s, const char *name, void *host, size_t nbytes,
                                   size_t *copied) {
     if (!m || !name || !host || !copied) return fail(S2K_ERR_ARG, "NULL argument");

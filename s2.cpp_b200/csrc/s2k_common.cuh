@@ -23,6 +23,12 @@ enum : int {
 // that a lost copy turns into an error status instead of a hang.
 constexpr long long kWaitLimitCycles = 4000000000LL;
 
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -83,6 +89,13 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
+}
+
+// Bulk L2 prefetch of [src, src + bytes) (no completion tracking): the TMA
+// engine pulls the range from HBM into L2 so a later bulk copy hits L2.
+// src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {

@@ -21,6 +21,7 @@
 
 #include <algorithm>
 #include <cstddef>
+#include <cstdlib>
 
 namespace s2k {
 
@@ -34,10 +35,16 @@ constexpr int kMaxT = 2;
 constexpr int kHD = 128;
 constexpr int kPtab = 512;                 // cached pages whose ids are staged in shared memory
 constexpr int kAttnKeys = 1024;            // longest key range whose scores stay on chip
+constexpr int kMPC = 5;                    // 8-value activation chunks per consumer thread per prologue pass
 
 bool mega_gemv_ok(const MegaGemv &g) {
     if (!tg_shape_ok(g.R, g.K, g.M, g.in_mode, g.epi, g.res != nullptr, kMKMax, kMaxT)) return false;
     if (g.in_mode == IN_RMSNORM && g.norm_w == nullptr) return false;
+    // one-pass RMSNorm prologue; 32-byte activation and norm-weight loads
+    if (g.in_mode == IN_RMSNORM && g.M * g.K > 8 * kMPC * kMNC) return false;
+    if (g.ldx % 8 != 0 || reinterpret_cast<uintptr_t>(g.x) % 32 != 0) return false;
+    if (g.act_out != nullptr && reinterpret_cast<uintptr_t>(g.act_out) % 16 != 0) return false;
+    if (g.norm_w != nullptr && reinterpret_cast<uintptr_t>(g.norm_w) % 32 != 0) return false;
     return true;
 }
 
@@ -76,11 +83,16 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
 }
 
 // consumer-only grid barrier halves
-__device__ __forceinline__ void grid_arrive(MegaCtl *ctl) {
+__device__ __forceinline__ void grid_arrive(MegaCtl *ctl, int flags) {
     named_sync(1, kMNC);
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(&ctl->count, 1u);
+        if (flags & 1) {
+            // release-add: orders this CTA's writes (seen through the named barrier) before the count
+            asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(&ctl->count), "r"(1u) : "memory");
+        } else {
+            __threadfence();
+            atomicAdd(&ctl->count, 1u);
+        }
     }
 }
 
@@ -103,21 +115,45 @@ __device__ __forceinline__ void grid_wait(MegaCtl *ctl, unsigned target, int *er
 // ---------------------------------------------------------------------------
 // producer: the weight tiles of every GEMV op of the segment, in op order
 // ---------------------------------------------------------------------------
-__device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, int G, int *err) {
-    const uint64_t pol = policy_evict_first();
-    int ps = 0;
-    for (int i = 0; i < n_ops; ++i) {
-        if (ops[i].kind != MK_GEMV) continue;
-        const MegaGemv g = ops[i].g;
-        long long u0, u1;
-        tg_range(g.R, g.K, cta, G, &u0, &u1);
-        for (long long u = u0; u < u1; ++u, ++ps) {
-            const int slot = ps % kMStages;
-            if (ps >= kMStages && !mbar_wait(&sm.empty[slot], ((ps / kMStages) - 1) & 1, err, ERR_WAIT_EMPTY))
-                return;
-            mbar_arrive_expect_tx(&sm.full[slot], kTileBytes);
-            bulk_g2s(sm.ring[slot], g.w + (size_t)u * kTileBytes, kTileBytes, &sm.full[slot], pol);
+// Walks this CTA's weight tiles of a segment in the order the consumers use
+// them (GEMV ops in op order, each op's tile range in address order).
+struct TileCursor {
+    int op = -1;
+    long long u = 0, u1 = 0;
+    const uint8_t *w = nullptr;
+
+    __device__ __forceinline__ const uint8_t *next(const MegaOp *ops, int n_ops, int cta, int G) {
+        while (u >= u1) {
+            if (++op >= n_ops) return nullptr;
+            if (ops[op].kind != MK_GEMV) continue;
+            tg_range(ops[op].g.R, ops[op].g.K, cta, G, &u, &u1);
+            w = ops[op].g.w;
         }
+        return w + (size_t)(u++) * kTileBytes;
+    }
+};
+
+// The ring holds kMStages tiles; a second cursor runs `l2_ahead` tiles past
+// the ring's head and pulls those tiles into L2 with bulk prefetches, so HBM
+// keeps streaming while the consumers sit in a grid barrier, an activation
+// prologue or attention (the ring alone covers ~4 us of HBM time per SM).
+__device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, int G, int l2_ahead, int *err,
+                              unsigned long long *trace) {
+    const uint64_t pol = policy_evict_first();
+    TileCursor ld, pf;
+    long long pf_n = 0;  // tiles the prefetch cursor has passed
+    // the first kMStages tiles go straight into the empty ring
+    for (int i = 0; i < kMStages && pf.next(ops, n_ops, cta, G); ++i) ++pf_n;
+    const uint8_t *src;
+    for (long long ps = 0; (src = ld.next(ops, n_ops, cta, G)) != nullptr; ++ps) {
+        for (const uint8_t *p; pf_n < ps + kMStages + l2_ahead && (p = pf.next(ops, n_ops, cta, G)) != nullptr; ++pf_n)
+            bulk_prefetch_l2(p, kTileBytes);
+        const int slot = (int)(ps % kMStages);
+        if (ps >= kMStages && !mbar_wait(&sm.empty[slot], (uint32_t)((ps / kMStages) - 1) & 1u, err, ERR_WAIT_EMPTY))
+            return;
+        mbar_arrive_expect_tx(&sm.full[slot], kTileBytes);
+        bulk_g2s(sm.ring[slot], src, kTileBytes, &sm.full[slot], pol);
+        if (trace != nullptr && ld.u == ld.u1) trace[((size_t)ld.op * G + cta) * kTraceSlots + 3] = globaltimer_ns();
     }
 }
 
@@ -125,15 +161,19 @@ __device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, 
 // GEMV op (consumer side): activation prologue, then this CTA's tiles
 // ---------------------------------------------------------------------------
 template <int MT>
-__device__ void mega_gemv(const MegaGemv &gref, MSmem &sm, int cta, int G, int &slot, uint32_t &phase, int *err) {
+__device__ void mega_gemv(const MegaGemv &gref, const F8 (&nw)[kMPC], MSmem &sm, int cta, int G, int &slot,
+                          uint32_t &phase, int *err, unsigned long long *tr) {
     const MegaGemv g = gref;  // op fields in registers
     long long u0, u1;
     tg_range(g.R, g.K, cta, G, &u0, &u1);
     if (u0 == u1) return;  // no row tile of this op here (R / 32 < G)
     // the CTA owning row tile 0 stores act_out
-    tg_prologue<MT, kMNC>(g, sm.xq, sm.xd, sm.nw, &sm.tok[0][0], kMaxT, sm.scale, u0 == 0, 1);
+    tg_prologue8<MT, kMNC, kMPC>(g, nw, sm.xq, sm.xd, &sm.tok[0][0], kMaxT, u0 == 0, 1,
+                                 tr != nullptr ? tr + 4 : nullptr);
     named_sync(1, kMNC);
-    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.xq, sm.xd, cta, G, err);
+    if (tr != nullptr && threadIdx.x == 0) tr[1] = globaltimer_ns();
+    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.xq, sm.xd, cta, G, err,
+                   tr != nullptr ? tr + 6 : nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -209,7 +249,11 @@ __device__ __forceinline__ float key_score(const uint4 (&raw)[kHD / 8], const do
 // so the key and value loads after the q / k normalization hit L2.  Scores stay in registers and the
 // probabilities in shared memory (up to kAttnKeys keys; longer contexts go
 // through the global score scratch).
-__device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err) {
+__device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err, unsigned long long *tr) {
+    // tr (profiling, first unit only): [4] q/k/v normed and stored, [5] scores, [6] softmax, [7] values
+    auto mark = [&](int u, int k) {
+        if (tr != nullptr && u == cta && threadIdx.x == 0) tr[k] = globaltimer_ns();
+    };
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int units = a.T * a.H;
     const int grp = a.H / a.Hkv;
@@ -334,6 +378,7 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
                 }
             }
         }
+        mark(u, 4);
         // ---- D. scores -> sc (pbuf in shared memory when the keys fit) ----
         float *const sc = in_smem ? pbuf : a.scores + (size_t)u * a.ld_scores;
         // cached keys: one f16 row per thread (rows were prefetched into L2)
@@ -355,6 +400,7 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
             if (lane == 0) sc[nc + c] = __fmul_rn((float)p, a.scale);
         }
         named_sync(3, kMNC);
+        mark(u, 5);
         // ---- E. exact softmax: max, sum in double, p' = exp(s - max) * (1 / sum) ----
         float mx = -INFINITY;
         for (int j = tid; j < Lk; j += kMNC) mx = fmaxf(mx, sc[j]);
@@ -374,6 +420,7 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
         for (int j = tid; j < Lk; j += kMNC) sc[j] = __fmul_rn(det_expf(__fsub_rn(sc[j], mx)), inv);
         float *const pr = sc;
         named_sync(3, kMNC);
+        mark(u, 6);
         // ---- F. values: warp w takes keys w, w + kMW, ...; lane takes dims 4*lane..4*lane+3;
         // kVU keys per warp are loaded before any is used (rows were prefetched into L2) ----
         {
@@ -424,6 +471,7 @@ __device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err
             sm.vpart[warp][4 * lane + 3] = acc3;
         }
         named_sync(3, kMNC);
+        mark(u, 7);
         if (tid < kHD) {
             double o = sm.vpart[0][tid];
             for (int k = 1; k < kMW; ++k) o += sm.vpart[k][tid];
@@ -484,7 +532,8 @@ __device__ void mega_embed_fast(const MegaEmbedFast &e, int cta, int G, int *err
 
 template <int MT>
 __global__ void __launch_bounds__(kMThreads, 1)
-    mega_kernel(const MegaOp *__restrict__ ops, int n_ops, MegaCtl *ctl, const int *done, int *err) {
+    mega_kernel(const MegaOp *__restrict__ ops, int n_ops, MegaCtl *ctl, const int *done, int *err, int l2_ahead,
+                unsigned long long *trace, int flags) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     MSmem &sm = *reinterpret_cast<MSmem *>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -500,17 +549,31 @@ __global__ void __launch_bounds__(kMThreads, 1)
     }
     __syncthreads();
     if (warp == kMW) {
-        if (lane == 0) mega_producer(ops, n_ops, sm, cta, G, err);
+        if (lane == 0) mega_producer(ops, n_ops, sm, cta, G, l2_ahead, err, trace);
         return;
     }
+    // trace: per op and CTA, [start, prologue done, work done, producer's last tile issued]
+    auto stamp = [&](int i, int k) {
+        if (trace != nullptr && threadIdx.x == 0) trace[((size_t)i * G + cta) * kTraceSlots + k] = globaltimer_ns();
+    };
     int cslot = 0;  // ring position of the consumers
     uint32_t cphase = 0;
     for (int i = 0; i < n_ops; ++i) {
         const int kind = ops[i].kind;
+        // RMSNorm weights of the next GEMV do not depend on the previous op: load them before the barrier
+        F8 nw[kMPC];
+        if (kind == MK_GEMV) tg_norm_preload<kMPC, kMNC>(ops[i].g, nw);
         if (i > 0) grid_wait(ctl, (unsigned)(i * G), err);
+        stamp(i, 0);
+        stamp(i, 1);
         switch (kind) {
-        case MK_GEMV: mega_gemv<MT>(ops[i].g, sm, cta, G, cslot, cphase, err); break;
-        case MK_ATTN: mega_attn(ops[i].a, sm, cta, G, err); break;
+        case MK_GEMV:
+            mega_gemv<MT>(ops[i].g, nw, sm, cta, G, cslot, cphase, err,
+                          trace != nullptr ? trace + ((size_t)i * G + cta) * kTraceSlots : nullptr);
+            break;
+        case MK_ATTN:
+            mega_attn(ops[i].a, sm, cta, G, err, trace != nullptr ? trace + ((size_t)i * G + cta) * kTraceSlots : nullptr);
+            break;
         case MK_EMBED_SLOW: mega_embed_slow(ops[i].es, cta, G, err); break;
         case MK_EMBED_FAST: mega_embed_fast(ops[i].ef, cta, G, err); break;
         case MK_ADVANCE:
@@ -521,8 +584,22 @@ __global__ void __launch_bounds__(kMThreads, 1)
             break;
         default: break;
         }
-        grid_arrive(ctl);
+        stamp(i, 2);
+        grid_arrive(ctl, flags);
     }
+    if (trace != nullptr) {
+        grid_wait(ctl, (unsigned)(n_ops * G), err);
+        stamp(n_ops, 0);
+    }
+}
+
+// Tiles per CTA the producer prefetches into L2 beyond its ring: 148 CTAs x
+// 24 tiles x 17 KB = 62 MB of the 126 MB L2.  S2K_L2_AHEAD (read at each
+// launch or graph capture) overrides it; 0 turns the run-ahead off.
+int mega_l2_ahead() {
+    const char *e = getenv("S2K_L2_AHEAD");
+    const int d = e ? atoi(e) : 0;
+    return d < 0 ? 0 : (d > 64 ? 64 : d);
 }
 
 cudaError_t mega_setup() {
@@ -533,7 +610,7 @@ cudaError_t mega_setup() {
 }
 
 cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, const int *done, int *err, int num_sms,
-                        cudaStream_t st) {
+                        cudaStream_t st, unsigned long long *trace) {
     if (mt < 1 || mt > kMaxT) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
@@ -546,8 +623,11 @@ cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, co
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     count_launch();
-    if (mt == 1) return cudaLaunchKernelEx(&cfg, mega_kernel<1>, d_ops, n_ops, ctl, done, err);
-    return cudaLaunchKernelEx(&cfg, mega_kernel<2>, d_ops, n_ops, ctl, done, err);
+    const int ahead = mega_l2_ahead();
+    const char *fe = getenv("S2K_MEGA_FLAGS");
+    const int flags = fe ? atoi(fe) : 0;
+    if (mt == 1) return cudaLaunchKernelEx(&cfg, mega_kernel<1>, d_ops, n_ops, ctl, done, err, ahead, trace, flags);
+    return cudaLaunchKernelEx(&cfg, mega_kernel<2>, d_ops, n_ops, ctl, done, err, ahead, trace, flags);
 }
 
 }  // namespace s2k

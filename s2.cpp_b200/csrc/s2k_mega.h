@@ -91,8 +91,19 @@ struct MegaCtl {
 
 cudaError_t mega_setup();
 // Launch one segment: ops in device memory, ctl zeroed on `st` before.
+// trace (optional, (n_ops + 1) x grid x kTraceSlots entries): per op and CTA
+// the globaltimer (ns) at [0] op start (the grid barrier after the previous op
+// has released), [1] GEMV prologue done, [2] op work done, [3] the producer's
+// last weight tile of the op issued, [4] RMSNorm partial sums formed (the
+// activation loads have landed), [5] RMSNorm scale known, [6] first weight
+// tile ready for the consumers, [7] activation quantized (before the CTA
+// barrier that ends the prologue); entry [n_ops][cta][0] is taken after a final
+// grid barrier.  Slots a launch does not reach stay as they were.
+constexpr int kTraceSlots = 8;
 cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, const int *done, int *err, int num_sms,
-                        cudaStream_t st);
+                        cudaStream_t st, unsigned long long *trace = nullptr);
+// Tiles per CTA the producer keeps in flight into L2 beyond its ring.
+int mega_l2_ahead();
 // Host-side validation of a GEMV op for the persistent kernel.
 bool mega_gemv_ok(const MegaGemv &g);
 

@@ -140,7 +140,8 @@ __device__ __forceinline__ void quant_chunk(const Chunk8 &c, bool valid, int8_t 
 // RMSNorm scale itself from the per-warp partial sums.
 template <int MT, int NT>
 __device__ __forceinline__ void tg_prologue(const TGemv &g, int8_t *xq, float *xd, float *nws, double *tok,
-                                            int tok_ld, float * /*unused*/, bool write_act, int bar_id) {
+                                            int tok_ld, float * /*unused*/, bool write_act, int bar_id,
+                                            unsigned long long *ts = nullptr) {
     constexpr int CPT = 5;  // chunks per thread per pass
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = g.K, KC = K >> 3, M = g.M;
@@ -199,6 +200,7 @@ __device__ __forceinline__ void tg_prologue(const TGemv &g, int8_t *xq, float *x
             const double t = warp_sum_d(tk[m]);
             if (lane == 0) tok[warp * tok_ld + m] = t;
         }
+        if (ts != nullptr && tid == 0) ts[0] = globaltimer_ns();
         named_sync(bar_id, NT);  // per-warp sums and norm weights complete
 #pragma unroll
         for (int m = 0; m < MT; ++m)
@@ -208,6 +210,7 @@ __device__ __forceinline__ void tg_prologue(const TGemv &g, int8_t *xq, float *x
                 const float mean = (float)(tot / (double)K);
                 sc[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, g.eps)));
             }
+        if (ts != nullptr && tid == 0) ts[1] = globaltimer_ns();
     }
     auto finish = [&](Chunk8 &ch, int ci, bool valid) {
         const int m = valid ? ci / KC : 0, off = valid ? (ci - m * KC) * 8 : 0;
@@ -247,6 +250,163 @@ __device__ __forceinline__ void tg_prologue(const TGemv &g, int8_t *xq, float *x
             finish(t, ci, ci < nchunks);
         }
     }
+    if (ts != nullptr && tid == 0) ts[3] = globaltimer_ns();
+}
+
+// ---------------------------------------------------------------------------
+// Prologue of the persistent kernel: one 8-value chunk per lane and pass.
+// Chunk v of the [M][K] activation (elements 8v..8v+7 of row m, counting
+// within the row) is owned by thread v % NT in pass v / (PC * NT); a warp
+// loads 1 KB of contiguous activation with one 32-byte load per lane, and
+// lanes 4k..4k+3 hold one 32-value Q8_0 block.  RMSNorm weights of a thread's
+// chunks are loaded into registers by tg_norm_preload before the grid barrier
+// (they do not depend on the previous op); an RMSNorm'd activation must fit
+// one pass (M * K <= 8 * PC * NT, checked on the host).  Rounding to the
+// nearest integer (ties to even) is done by adding 1.5 * 2^23, which leaves
+// round(x) in the low mantissa bits for |x| < 2^22 -- the same rounding as
+// ggml's nearest_int and _mm256_round_ps -- so no float-to-int conversion is
+// issued per value.
+// ---------------------------------------------------------------------------
+struct F8 {
+    float v[8];
+};
+
+__device__ __forceinline__ F8 ld_cg_f8(const float *p) {
+    F8 r;
+    asm volatile("ld.global.cg.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=f"(r.v[0]), "=f"(r.v[1]), "=f"(r.v[2]), "=f"(r.v[3]), "=f"(r.v[4]), "=f"(r.v[5]), "=f"(r.v[6]),
+                   "=f"(r.v[7])
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ F8 ld_nc_f8(const float *p) {
+    F8 r;
+    asm("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=f"(r.v[0]), "=f"(r.v[1]), "=f"(r.v[2]), "=f"(r.v[3]), "=f"(r.v[4]), "=f"(r.v[5]), "=f"(r.v[6]),
+          "=f"(r.v[7])
+        : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ int tg_row_of(int v, int KC, int M) {
+    int m = 0;
+    while (m + 1 < M && v >= (m + 1) * KC) ++m;
+    return m;
+}
+
+template <int PC, int NT>
+__device__ __forceinline__ void tg_norm_preload(const TGemv &g, F8 (&nw)[PC]) {
+    if (g.in_mode != IN_RMSNORM) return;
+    const int KC = g.K >> 3, nv = g.M * KC, tid = threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < PC; ++j) {
+        const int v = tid + j * NT;
+        if (v < nv) nw[j] = ld_nc_f8(g.norm_w + 8 * (v - tg_row_of(v, KC, g.M) * KC));
+    }
+}
+
+// round-half-even(x) for |x| < 2^22, low byte only
+__device__ __forceinline__ uint32_t rne_byte(float x) {
+    return (uint32_t)__float_as_int(__fadd_rn(x, 12582912.f));
+}
+
+__device__ __forceinline__ uint32_t pack4_rne(float a, float b, float c, float d, float id) {
+    const uint32_t qa = rne_byte(__fmul_rn(a, id)), qb = rne_byte(__fmul_rn(b, id));
+    const uint32_t qc = rne_byte(__fmul_rn(c, id)), qd = rne_byte(__fmul_rn(d, id));
+    return __byte_perm(__byte_perm(qa, qb, 0x0040), __byte_perm(qc, qd, 0x0040), 0x5410);
+}
+
+template <int MT, int NT, int PC>
+__device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC], int8_t *xq, float *xd, double *tok,
+                                             int tok_ld, bool write_act, int bar_id,
+                                             unsigned long long *ts = nullptr) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = g.K, KC = K >> 3, M = g.M, nv = M * KC;
+    const bool rms = g.in_mode == IN_RMSNORM;
+    float sc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) sc[m] = 1.f;
+    for (int base = 0; base < nv; base += PC * NT) {
+        F8 xv[PC];
+        int mrow[PC];
+#pragma unroll
+        for (int j = 0; j < PC; ++j) {
+            const int v = base + tid + j * NT;
+            mrow[j] = 0;
+            if (v < nv) {
+                const int m = tg_row_of(v, KC, M);
+                mrow[j] = m;
+                xv[j] = ld_cg_f8(g.x + (size_t)m * g.ldx + 8 * (v - m * KC));
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) xv[j].v[e] = 0.f;
+            }
+        }
+        if (rms) {  // single pass (host check): every element of every row is in xv
+            double tk[MT];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) tk[m] = 0.0;
+#pragma unroll
+            for (int j = 0; j < PC; ++j)
+                if (base + tid + j * NT < nv) {
+                    double s = 0.0;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) s += (double)__fmul_rn(xv[j].v[e], xv[j].v[e]);
+#pragma unroll
+                    for (int m = 0; m < MT; ++m)
+                        if (m == mrow[j]) tk[m] += s;
+                }
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const double t = warp_sum_d(tk[m]);
+                if (lane == 0) tok[warp * tok_ld + m] = t;
+            }
+            if (ts != nullptr && tid == 0) ts[0] = globaltimer_ns();
+            named_sync(bar_id, NT);
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+                if (m < M) {
+                    double tot = 0.0;
+                    for (int w = 0; w < NT / 32; ++w) tot += tok[w * tok_ld + m];
+                    const float mean = (float)(tot / (double)K);
+                    sc[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, g.eps)));
+                }
+            if (ts != nullptr && tid == 0) ts[1] = globaltimer_ns();
+        }
+#pragma unroll
+        for (int j = 0; j < PC; ++j) {
+            const int v = base + tid + j * NT;
+            // 4-lane groups are wholly in or out (nv % 4 == 0): all lanes of a live warp shuffle
+            if (base + warp * 32 + j * NT >= nv) continue;
+            const bool valid = v < nv;
+            F8 y = xv[j];
+            if (rms && valid) {
+                float s = sc[0];
+#pragma unroll
+                for (int m = 1; m < MT; ++m)
+                    if (m == mrow[j]) s = sc[m];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y.v[e] = __fmul_rn(__fmul_rn(y.v[e], s), nw[j].v[e]);
+            }
+            if (valid && write_act && g.act_out != nullptr) {  // act_out is [M][K] contiguous
+                float4 *dst = reinterpret_cast<float4 *>(g.act_out + 8 * (size_t)v);
+                dst[0] = make_float4(y.v[0], y.v[1], y.v[2], y.v[3]);
+                dst[1] = make_float4(y.v[4], y.v[5], y.v[6], y.v[7]);
+            }
+            float amax = fabsf(y.v[0]);
+#pragma unroll
+            for (int e = 1; e < 8; ++e) amax = fmaxf(amax, fabsf(y.v[e]));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            if (!valid) continue;
+            const float id = amax != 0.0f ? __fdiv_rn(127.f, amax) : 0.0f;
+            *reinterpret_cast<uint2 *>(xq + 8 * (size_t)v) =
+                make_uint2(pack4_rne(y.v[0], y.v[1], y.v[2], y.v[3], id), pack4_rne(y.v[4], y.v[5], y.v[6], y.v[7], id));
+            if ((lane & 3) == 0) xd[v >> 2] = __half2float(__float2half_rn(__fdiv_rn(amax, 127.f)));
+        }
+    }
+    if (ts != nullptr && tid == 0) ts[3] = globaltimer_ns();
 }
 
 // Reduce a warp's 4 row partials (per token) across the 32 lanes with a
@@ -305,7 +465,7 @@ __device__ __forceinline__ void tg_emit(const TGemv &g, int rt, int warp, int la
 template <int MT>
 __device__ __forceinline__ void tg_consume(const TGemv &g, const uint8_t *ring, uint64_t *full, uint64_t *empty,
                                            int nst, int &slot, uint32_t &phase, const int8_t *xq, const float *xd,
-                                           int cta, int G, int *err) {
+                                           int cta, int G, int *err, unsigned long long *t_first = nullptr) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = g.K, NKT = K / kTK, NB = K >> 5, M = g.M;
     const int RT = g.R / kTR;
@@ -341,6 +501,7 @@ __device__ __forceinline__ void tg_consume(const TGemv &g, const uint8_t *ring, 
                 xs[m] = xdl[mm * NB + kt * (kTK / 32)];
             }
             mbar_wait(&full[slot], phase, err, ERR_WAIT_FULL);
+            if (t_first != nullptr && tid == 0 && rt == rt0 && kt == 0) *t_first = globaltimer_ns();
             const uint8_t *t = ring + (size_t)slot * kTileBytes;
             int4 wv[kTRW];
             float dw[kTRW];

@@ -34,7 +34,7 @@ EXPORTED = [
     "s2k_model_stream", "s2k_seq_create", "s2k_seq_reset", "s2k_seq_free", "s2k_seq_n_past", "s2k_eval",
     "s2k_fast_decode", "s2k_generate", "s2k_generate_device", "s2k_sample", "s2k_launch_count",
     "s2k_profile_gemv", "s2k_debug_copy", "s2k_sample_noalloc",
-    "s2k_profile_frame",
+    "s2k_profile_frame", "s2k_profile_ops", "s2k_profile_trace",
 ]
 
 
@@ -110,6 +110,10 @@ def lib() -> ctypes.CDLL:
                               ctypes.POINTER(i32)], i32),
         "s2k_debug_copy": ([vp, vp, ctypes.c_char_p, vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)], i32),
         "s2k_profile_frame": ([vp, vp, i32] + [ctypes.POINTER(ctypes.c_double)] * 4, i32),
+        "s2k_profile_ops": ([vp, vp, i32, i32, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i32), i32,
+                             ctypes.POINTER(i32)], i32),
+        "s2k_profile_trace": ([vp, vp, i32, ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.POINTER(i32),
+                               ctypes.POINTER(i32)], i32),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -301,6 +305,30 @@ class SlowARModel:
         v = [ctypes.c_double(0) for _ in range(4)]
         _check(lib().s2k_profile_frame(self._m, self._seq, reps, *[ctypes.byref(x) for x in v]))
         return tuple(x.value for x in v)
+
+    def profile_ops(self, segment: int, reps: int = 5):
+        """Per-op device time (us) and kind of one persistent-kernel segment
+        (s2k_profile_ops); segment -1 is the Slow step."""
+        cap = 4096
+        us = (ctypes.c_double * cap)()
+        kind = (ctypes.c_int32 * cap)()
+        n = ctypes.c_int32(0)
+        if segment < 0:
+            segment += self._hp.num_codebooks
+        _check(lib().s2k_profile_ops(self._m, self._seq, segment, reps, us, kind, cap, ctypes.byref(n)))
+        return np.array(us[: n.value]), np.array(kind[: n.value], dtype=np.int32)
+
+    def profile_trace(self, segment: int) -> np.ndarray:
+        """Per-op, per-CTA stamps of one persistent-kernel segment launch
+        (s2k_profile_trace): uint64 ns array [n_ops + 1][n_ctas][8]."""
+        if segment < 0:
+            segment += self._hp.num_codebooks
+        cap = 1 << 20
+        buf = (ctypes.c_uint64 * cap)()
+        n, g = ctypes.c_int32(0), ctypes.c_int32(0)
+        _check(lib().s2k_profile_trace(self._m, self._seq, segment, buf, cap, ctypes.byref(n), ctypes.byref(g)))
+        a = np.frombuffer(buf, dtype=np.uint64, count=(n.value + 1) * g.value * 8).copy()
+        return a.reshape(n.value + 1, g.value, 8)
 
     def generate_device(self, d_prompt_tm: int, cols: int, d_codes: int, max_new_tokens: int,
                         temperature: float = 0.0, top_p: float = 0.8, top_k: int = 30,
