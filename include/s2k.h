@@ -239,14 +239,17 @@ S2K_API s2k_status s2k_profile_ops(s2k_model *m, s2k_seq *s, int32_t segment, in
 /* Profiling hook for the persistent decode kernel (no reference counterpart).
  * Same preconditions as s2k_profile_ops.  Launches segment `segment` twice
  * with the in-kernel trace and returns the second launch's stamps:
- * stamps[((op * n_ctas) + cta) * 8 + k], globaltimer nanoseconds (0 where a
+ * stamps[((op * n_ctas) + cta) * 12 + k], globaltimer nanoseconds (0 where a
  * stamp does not apply), for op = 0..n_ops (the entry at op = n_ops is the
  * end of the launch, k = 0 only) and k = 0 op start (its grid barrier
- * released), 1 GEMV activation prologue done, 2 op work done, 3 the CTA's
- * producer warp issued the op's last weight tile, 4 RMSNorm partial sums
+ * released), 1 GEMV activation prologue done, 2 op work done; GEMV ops: 3 the
+ * CTA's producer warp issued the op's last weight tile, 4 RMSNorm partial sums
  * formed, 5 RMSNorm scale known, 6 first weight tile ready, 7 activation
- * quantized (before the CTA barrier that ends the prologue).  cap is the
- * capacity of stamps in entries. */
+ * quantized (before the CTA barrier that ends the prologue); attention ops
+ * (first unit of the CTA): 3 split arrival counted, 4 keys / values in shared
+ * memory, 5 scores, 6 split softmax, 7 split values, 8 queries and this
+ * call's keys rotated, 9 CTA barrier after them, 10 split partials written.
+ * cap is the capacity of stamps in entries. */
 S2K_API s2k_status s2k_profile_trace(s2k_model *m, s2k_seq *s, int32_t segment, uint64_t *stamps, size_t cap,
                                      int32_t *n_ops, int32_t *n_ctas);
 

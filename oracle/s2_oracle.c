@@ -23,6 +23,8 @@
 
 #define QK8_0 32
 #define QK_K 256
+/* keys per attention split (the CUDA kernels split the same way) */
+#define SO_ATTN_SPLIT 64
 
 /* ------------------------------------------------------------------------ */
 /* fp16                                                                      */
@@ -669,40 +671,65 @@ static void run_layers(so_model *m, int fast, float *x, int T, int32_t n_past) {
                 m->kv_v[lo + i] = so_fp32_to_fp16(vf[(int64_t)n_past * kvs + i]);
             }
         }
-        /* attention: KQ = K.Q, scale, diag_mask_inf(n_past), soft_max, V.KQ */
+        /* attention: KQ = K.Q, scale, diag_mask_inf(n_past), soft_max, V.KQ
+         * (src/s2_model.cpp:1023-1039), in fixed splits of SO_ATTN_SPLIT keys
+         * (the convention the CUDA kernels share, so both agree bit for bit):
+         *   s_j = float(sum_d double(k_j[d]) * double(q[d])) * scale
+         *   split i: m_i = max s_j, e_j = det_expf(s_j - m_i),
+         *            S_i = sum double(e_j), O_i[d] = sum double(v_j[d]) * double(e_j)
+         *   M = max m_i, w_i = det_expf(m_i - M),
+         *   out[d] = float((sum_i O_i[d] * double(w_i)) / (sum_i S_i * double(w_i)))
+         * i.e. softmax(s) . V with the exponentials factored per split;
+         * keys j >= len (the causal mask) are never visited. */
 #pragma omp parallel for collapse(2) schedule(static)
         for (int t = 0; t < T; ++t) {
             for (int hh = 0; hh < H; ++hh) {
                 const float *q = qkv + (int64_t)t * qkvs + hh * hd;
                 const int kvh = hh / rep;
                 const int len = n_past + t + 1;
-                /* KQ (exact products summed in double, rounded once), ggml_scale,
-                 * diag_mask_inf (keys j >= len excluded), soft_max (max, exp,
-                 * double sum, scale by float(1/sum)), then V.KQ in double. */
-                float *sc = (float *)malloc(sizeof(float) * (size_t)n_kv);
-                float mx = -INFINITY;
-                for (int j = 0; j < len; ++j) {
-                    const float *kk = kf + (int64_t)j * kvs + kvh * hd;
-                    double s = 0.0;
-                    for (int d = 0; d < hd; ++d) s += (double)kk[d] * (double)q[d];
-                    sc[j] = (float)s * attn_scale;
-                    if (sc[j] > mx) mx = sc[j];
+                const int nsp = (len + SO_ATTN_SPLIT - 1) / SO_ATTN_SPLIT;
+                float *sc = (float *)malloc(sizeof(float) * SO_ATTN_SPLIT);
+                float *ms = (float *)malloc(sizeof(float) * (size_t)nsp);
+                double *ss = (double *)malloc(sizeof(double) * (size_t)nsp);
+                double *os = (double *)malloc(sizeof(double) * (size_t)nsp * hd);
+                float M = -INFINITY;
+                for (int i = 0; i < nsp; ++i) {
+                    const int j0 = i * SO_ATTN_SPLIT, j1 = j0 + SO_ATTN_SPLIT < len ? j0 + SO_ATTN_SPLIT : len;
+                    float mx = -INFINITY;
+                    for (int j = j0; j < j1; ++j) {
+                        const float *kk = kf + (int64_t)j * kvs + kvh * hd;
+                        double s = 0.0;
+                        for (int d = 0; d < hd; ++d) s += (double)kk[d] * (double)q[d];
+                        sc[j - j0] = (float)s * attn_scale;
+                        if (sc[j - j0] > mx) mx = sc[j - j0];
+                    }
+                    double sum = 0.0;
+                    for (int j = j0; j < j1; ++j) {
+                        sc[j - j0] = so_det_expf(sc[j - j0] - mx);
+                        sum += (double)sc[j - j0];
+                    }
+                    for (int d = 0; d < hd; ++d) {
+                        double o = 0.0;
+                        for (int j = j0; j < j1; ++j) o += (double)vf[(int64_t)j * kvs + kvh * hd + d] * (double)sc[j - j0];
+                        os[(size_t)i * hd + d] = o;
+                    }
+                    ms[i] = mx;
+                    ss[i] = sum;
+                    if (mx > M) M = mx;
                 }
-                double sum = 0.0;
-                for (int j = 0; j < len; ++j) {
-                    const float e = so_det_expf(sc[j] - mx);
-                    sc[j] = e;
-                    sum += (double)e;
+                double S = 0.0;
+                for (int i = 0; i < nsp; ++i) {
+                    const float w = so_det_expf(ms[i] - M);
+                    ms[i] = w;
+                    S += ss[i] * (double)w;
                 }
-                const float inv = (float)(1.0 / sum);
-                for (int j = 0; j < len; ++j) sc[j] = sc[j] * inv;
                 float *o = attn + (int64_t)t * qs + hh * hd;
                 for (int d = 0; d < hd; ++d) {
-                    double s = 0.0;
-                    for (int j = 0; j < len; ++j) s += (double)vf[(int64_t)j * kvs + kvh * hd + d] * (double)sc[j];
-                    o[d] = (float)s;
+                    double acc = 0.0;
+                    for (int i = 0; i < nsp; ++i) acc += os[(size_t)i * hd + d] * (double)ms[i];
+                    o[d] = (float)(acc / S);
                 }
-                free(sc);
+                free(sc); free(ms); free(ss); free(os);
             }
         }
         matmat(L->wo.type, L->wo.data, dim, qs, T, attn, tmp, dim);

@@ -52,9 +52,12 @@ struct Layer {
 struct Work {
     int T = 0, L = 0, dim = 0, qs = 0, kvs = 0, ff = 0, H = 0;
     float *x = nullptr, *h = nullptr, *qkv = nullptr, *attn = nullptr, *ff_buf = nullptr;
-    float *kcur = nullptr, *vcur = nullptr, *scores = nullptr, *stats = nullptr;
-    double *part = nullptr;
-    int *counters = nullptr, *counters2 = nullptr;
+    float *kcur = nullptr, *vcur = nullptr, *scores = nullptr;
+    // persistent-kernel attention: per (token, kv head, split) the split's
+    // O_i [G][hd] and (m_i, S_i) [G][2]; arrival counters per (token, kv head)
+    double *part = nullptr, *part_ms = nullptr;
+    int *counters = nullptr;
+    int n_split_max = 0;
 };
 
 }  // namespace s2k
@@ -163,12 +166,6 @@ static s2k_status check_err_word(s2k_model *m) {
     return S2K_OK;
 }
 
-static int n_splits_for(int T) {
-    if (T <= 1) return 16;
-    if (T >= 16) return 1;
-    return std::max(1, 16 / T);
-}
-
 // T: tokens per call; L: longest key range (positions) a call attends over.
 static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int Hkv, int hd, int ff) {
     w.T = T;
@@ -188,19 +185,17 @@ static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int 
     if ((e = m->alloc(&w.kcur, tn * w.kvs))) return e;
     if ((e = m->alloc(&w.vcur, tn * w.kvs))) return e;
     if ((e = m->alloc(&w.scores, tn * H * (size_t)L))) return e;
-    if ((e = m->alloc(&w.stats, tn * H * 2))) return e;
-    const size_t ts = std::max<size_t>(tn * n_splits_for(T), 16);
-    if ((e = m->alloc(&w.part, ts * H * hd))) return e;
+    w.n_split_max = (L + kAttnSplit - 1) / kAttnSplit;
+    const size_t units = tn * Hkv * (size_t)w.n_split_max;
+    if ((e = m->alloc(&w.part, units * (H / Hkv) * hd))) return e;
+    if ((e = m->alloc(&w.part_ms, units * (H / Hkv) * 2))) return e;
     if ((e = m->alloc(&w.counters, tn * Hkv))) return e;
-    if ((e = m->alloc(&w.counters2, tn * Hkv))) return e;
-    if ((e = cudaMemset(w.counters, 0, tn * Hkv * sizeof(int)))) return e;
-    return cudaMemset(w.counters2, 0, tn * Hkv * sizeof(int));
+    return cudaMemset(w.counters, 0, tn * Hkv * sizeof(int));
 }
 
 static void work_free(s2k_model *m, Work &w) {
     for (void *p : {(void *)w.x, (void *)w.h, (void *)w.qkv, (void *)w.attn, (void *)w.ff_buf, (void *)w.kcur,
-                    (void *)w.vcur, (void *)w.scores, (void *)w.stats, (void *)w.part, (void *)w.counters,
-                    (void *)w.counters2})
+                    (void *)w.vcur, (void *)w.scores, (void *)w.part, (void *)w.part_ms, (void *)w.counters})
         m->release(p);
     w = Work();
 }
@@ -249,7 +244,7 @@ struct StackCall {
     int pos_add;
     int cur_base;
     KvPaged kv;  // Slow only
-    int n_splits;
+    int max_keys;  // upper bound of any token's key range
     const int *done;
 };
 
@@ -318,13 +313,9 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         a.kcur = q.kcur;
         a.vcur = q.vcur;
         a.cur_base = c.cur_base;
-        a.n_splits = c.n_splits;
+        a.max_keys = c.max_keys;
         a.scores = w.scores;
         a.ld_scores = w.L;
-        a.stats = w.stats;
-        a.part = w.part;
-        a.counters = w.counters;
-        a.counters2 = w.counters2;
         a.out = w.attn;
         a.done = c.done;
         a.err = m->d_err;
@@ -396,7 +387,7 @@ static cudaError_t enqueue_slow(s2k_model *m, s2k_seq *s, int T, const int *toke
     c.pos_add = 0;
     c.cur_base = 0;
     c.kv = s->kv();
-    c.n_splits = n_splits_for(T);
+    c.max_keys = m->sw.L;
     c.done = done;
     if ((e = run_stack(m, c))) return e;
     GemvArgs hd;
@@ -426,7 +417,7 @@ static cudaError_t enqueue_fast(s2k_model *m, int T, int pos_add, const int *don
     c.pos_base = nullptr;
     c.pos_add = pos_add;
     c.cur_base = pos_add;
-    c.n_splits = 1;
+    c.max_keys = pos_add + T;
     c.done = done;
     if ((e = run_stack(m, c))) return e;
     GemvArgs hd;
@@ -744,6 +735,7 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     CU(gemv_setup());
     CU(sampler_setup());
     CU(mega_setup());
+    CU(attn_setup());
     if (m->staging) {
         m->release(m->staging);
         m->staging = nullptr;
@@ -1049,10 +1041,12 @@ static bool add_layers(s2k_model *m, s2k_seq *s, bool fast, int T, int pos_add, 
             a.a.kv_pages = s->n_pages;
         }
         a.a.layer = (int)il;
-        a.a.scores = w.scores;
-        a.a.ld_scores = w.L;
+        a.a.part = w.part;
+        a.a.part_ms = w.part_ms;
+        a.a.counters = w.counters;
+        a.a.n_split_max = w.n_split_max;
         a.a.out = w.attn;
-        if (T * H > w.T * w.H || hd != 128) return false;
+        if (T * H > w.T * w.H || !mega_attn_ok(a.a, fast ? pos_add + T : s->max_seq_len)) return false;
         ops.push_back(a);
         ops.push_back(mk_gemv(L.wo, w.attn, w.qs, T, IN_PLAIN, nullptr, eps, EPI_STORE, w.h, dim, w.x, dim, nullptr));
         ops.push_back(mk_gemv(L.w13, w.h, dim, T, IN_RMSNORM, L.ffn_norm, eps, EPI_SWIGLU, w.ff_buf, w.ff, nullptr, 0,
@@ -1130,6 +1124,7 @@ static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
     }
     for (const MegaOp &o : ops)
         if (o.kind == MK_GEMV && !mega_gemv_ok(o.g)) ok = false;
+    if (hp.num_codebooks > 16) ok = false;  // the persistent kernel's embedding sums at most 16 codebooks
     s->use_mega = ok;
     if (!ok) return S2K_OK;
     m->release(s->mega_ops);

@@ -12,15 +12,20 @@
 //   GQA: query head h reads kv head h / (H/Hkv)                :57-68
 //   softmax((K.Q) * 1/sqrt(hd), causal from n_past) . V        :1023-1039
 //
-// Arithmetic (shared with the CPU oracle so the two agree bit for bit):
+// Arithmetic (shared with the CPU oracle so the two agree bit for bit): keys
+// are taken in fixed splits of kAttnSplit (64) positions,
 //   s_j  = float(sum_d double(k_j[d]) * double(q[d])) * scale
-//   p_j  = det_expf(s_j - max_j s_j),  inv = float(1 / sum_j double(p_j))
-//   out  = float(sum_j double(v_j[d]) * double(p_j * inv))
-// Products of two floats are exact in double and the double sums are rounded
-// to float once, so the split over CTAs does not change the result.
+//   split i: m_i = max s_j,  e_j = det_expf(s_j - m_i),
+//            S_i = sum double(e_j),  O_i[d] = sum double(v_j[d]) * double(e_j)
+//   M = max_i m_i,  w_i = det_expf(m_i - M)
+//   out  = float((sum_i O_i[d] * double(w_i)) / (sum_i S_i * double(w_i)))
+// i.e. softmax . V with the exponentials factored per split.  Products of two
+// floats are exact in double and every double sum is rounded to float once,
+// so the order of the sums inside a split does not change the result.
 //
-// Two kernels per layer: attn_scores (scores + last-CTA softmax statistics)
-// and attn_values (weighted values + last-CTA merge of the splits).
+// One kernel per layer: attn_split_kernel, one CTA per (kv head, token) that
+// walks the splits in order (scores, split maxima, then per split the
+// exponentials, S_i and O_i folded into the running sums with w_i).
 #include "s2k_common.cuh"
 #include "s2k_kernels.h"
 
@@ -111,177 +116,157 @@ constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxGroup = 8;
 
-__device__ __forceinline__ void key_range(const AttnArgs &a, int t, int sp, int nc, int *Lk, int *j0, int *j1) {
-    *Lk = nc + a.cur_base + t + 1;
-    *j0 = (int)(((long long)*Lk * sp) / a.n_splits);
-    *j1 = (int)(((long long)*Lk * (sp + 1)) / a.n_splits);
-}
-
-template <int HD>
 __device__ __forceinline__ void load_kv_row(const AttnArgs &a, const __half *cache, const float *cur, int j, int nc,
-                                            int g, int lane, float out[HD / 32]) {
-    constexpr int DPL = HD / 32;
+                                            int g, int lane, float out[4]) {
     if (j < nc) {
         const int page = __ldcg(a.kv.block_table + j / kPage), slot = j % kPage;
         const size_t off =
-            ((((size_t)page * a.kv.n_layers + a.layer) * a.kv.n_kv_heads + g) * kPage + slot) * HD + lane * DPL;
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) out[d] = __half2float(__ldcg(cache + off + d));
+            ((((size_t)page * a.kv.n_layers + a.layer) * a.kv.n_kv_heads + g) * kPage + slot) * 128 + lane * 4;
+        const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(cache + off));
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+        out[0] = f0.x;
+        out[1] = f0.y;
+        out[2] = f1.x;
+        out[3] = f1.y;
     } else {
-        const size_t off = ((size_t)(j - nc) * a.Hkv + g) * HD + lane * DPL;
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) out[d] = __ldcg(cur + off + d);
+        const float4 v = __ldcg(reinterpret_cast<const float4 *>(cur + ((size_t)(j - nc) * a.Hkv + g) * 128) + lane);
+        out[0] = v.x;
+        out[1] = v.y;
+        out[2] = v.z;
+        out[3] = v.w;
     }
 }
 
-// grid (Hkv, T, n_splits).  Writes s_j for the split's keys; the last CTA of a
-// (token, kv head) computes max_j s_j and inv = 1/sum_j exp(s_j - max) per head.
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a) {
-    constexpr int DPL = HD / 32;
+// Dynamic shared memory of attn_split_kernel for G query heads per kv head
+// and at most nsp splits.
+size_t attn_split_smem(int G, int nsp) {
+    return (size_t)kAttnWarps * G * 128 * sizeof(double)  // per-warp O_i partials
+           + (size_t)G * kAttnSplit * sizeof(float)        // e_j of the split
+           + (size_t)G * nsp * sizeof(float);              // split maxima m_i
+}
+
+// grid (Hkv, T), block kAttnThreads; hd = 128 (lane owns dims 4*lane..4*lane+3).
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
     pdl_launch_dependents();
     pdl_wait();
     if (a.done && __ldcg(a.done)) return;
-    const int g = blockIdx.x, t = blockIdx.y, sp = blockIdx.z;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int g = blockIdx.x, t = blockIdx.y;
     const int G = a.H / a.Hkv;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nc = a.n_cached ? __ldcg(a.n_cached) : 0;
-    int Lk, j0, j1;
-    key_range(a, t, sp, nc, &Lk, &j0, &j1);
-    float q[kMaxGroup][DPL];
+    const int Lk = nc + a.cur_base + t + 1;
+    const int nsp = (Lk + kAttnSplit - 1) / kAttnSplit;
+    double *red = reinterpret_cast<double *>(smem);                    // [kAttnWarps][G][128]
+    float *ebuf = reinterpret_cast<float *>(red + kAttnWarps * G * 128);  // [G][kAttnSplit]
+    float *msp = ebuf + G * kAttnSplit;                                 // [G][nsp]
+    float q[kMaxGroup][4];
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h)
 #pragma unroll
-        for (int d = 0; d < DPL; ++d)
-            q[h][d] = (h < G) ? __ldcg(a.q + (size_t)t * a.ldq + (size_t)(g * G + h) * HD + lane * DPL + d) : 0.f;
+        for (int d = 0; d < 4; ++d)
+            q[h][d] = (h < G) ? __ldcg(a.q + (size_t)t * a.ldq + (size_t)(g * G + h) * 128 + lane * 4 + d) : 0.f;
     float *scores = a.scores + ((size_t)t * a.H + (size_t)g * G) * a.ld_scores;
-    for (int j = j0 + warp; j < j1; j += kAttnWarps) {
-        float k[DPL];
-        load_kv_row<HD>(a, a.kv.k, a.kcur, j, nc, g, lane, k);
+    // pass A: every score of the key range
+    for (int j = warp; j < Lk; j += kAttnWarps) {
+        float k[4];
+        load_kv_row(a, a.kv.k, a.kcur, j, nc, g, lane, k);
 #pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) {
+        for (int h = 0; h < kMaxGroup; ++h)
             if (h < G) {
                 double s = 0.0;
 #pragma unroll
-                for (int d = 0; d < DPL; ++d) s += (double)k[d] * (double)q[h][d];
+                for (int d = 0; d < 4; ++d) s += (double)k[d] * (double)q[h][d];
                 s = warp_sum_d(s);
                 if (lane == 0) scores[(size_t)h * a.ld_scores + j] = __fmul_rn((float)s, a.scale);
             }
-        }
     }
-    __shared__ int s_last;
-    __shared__ float s_red[kAttnWarps];
-    __shared__ double s_dred[kAttnWarps];
-    __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[t * a.Hkv + g], 1) == a.n_splits - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int h = 0; h < G; ++h) {
-        const float *sh = scores + (size_t)h * a.ld_scores;
+    // split maxima
+    for (int p = tid; p < G * nsp; p += kAttnThreads) {
+        const int h = p / nsp, i = p - h * nsp;
+        const int j0 = i * kAttnSplit, j1 = min(j0 + kAttnSplit, Lk);
         float mx = -INFINITY;
-        for (int j = threadIdx.x; j < Lk; j += kAttnThreads) mx = fmaxf(mx, __ldcg(sh + j));
-        mx = warp_max(mx);
-        if (lane == 0) s_red[warp] = mx;
-        __syncthreads();
-        mx = s_red[0];
-        for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, s_red[w]);
-        double sum = 0.0;
-        for (int j = threadIdx.x; j < Lk; j += kAttnThreads) sum += (double)det_expf(__fsub_rn(__ldcg(sh + j), mx));
-        sum = warp_sum_d(sum);
-        if (lane == 0) s_dred[warp] = sum;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            double tot = 0.0;
-            for (int w = 0; w < kAttnWarps; ++w) tot += s_dred[w];
-            float *st = a.stats + ((size_t)t * a.H + g * G + h) * 2;
-            st[0] = mx;
-            st[1] = (float)(1.0 / tot);
-        }
-        __syncthreads();
+        for (int j = j0; j < j1; ++j) mx = fmaxf(mx, scores[(size_t)h * a.ld_scores + j]);
+        msp[h * nsp + i] = mx;
     }
-    if (threadIdx.x == 0) a.counters[t * a.Hkv + g] = 0;
-}
-
-// grid (Hkv, T, n_splits).  Accumulates double(v_j) * double(p_j * inv) over the
-// split's keys; the last CTA of a (token, kv head) sums the splits in order.
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) attn_values_kernel(AttnArgs a) {
-    constexpr int DPL = HD / 32;
-    pdl_launch_dependents();
-    pdl_wait();
-    if (a.done && __ldcg(a.done)) return;
-    const int g = blockIdx.x, t = blockIdx.y, sp = blockIdx.z;
-    const int G = a.H / a.Hkv;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nc = a.n_cached ? __ldcg(a.n_cached) : 0;
-    int Lk, j0, j1;
-    key_range(a, t, sp, nc, &Lk, &j0, &j1);
-    float mx[kMaxGroup], inv[kMaxGroup];
+    __syncthreads();
+    // pass B: thread tid owns output dim d = tid of every head
+    double acc[kMaxGroup], ssum[kMaxGroup];
+    float M[kMaxGroup];
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h) {
-        mx[h] = h < G ? __ldcg(a.stats + ((size_t)t * a.H + g * G + h) * 2) : 0.f;
-        inv[h] = h < G ? __ldcg(a.stats + ((size_t)t * a.H + g * G + h) * 2 + 1) : 0.f;
+        acc[h] = 0.0;
+        ssum[h] = 0.0;
+        M[h] = -INFINITY;
+        if (h < G)
+            for (int i = 0; i < nsp; ++i) M[h] = fmaxf(M[h], msp[h * nsp + i]);
     }
-    const float *scores = a.scores + ((size_t)t * a.H + (size_t)g * G) * a.ld_scores;
-    double acc[kMaxGroup][DPL];
+    for (int i = 0; i < nsp; ++i) {
+        const int j0 = i * kAttnSplit, cnt = min(kAttnSplit, Lk - j0);
+        for (int p = tid; p < G * kAttnSplit; p += kAttnThreads) {
+            const int h = p / kAttnSplit, jj = p - h * kAttnSplit;
+            ebuf[p] = jj < cnt ? det_expf(__fsub_rn(scores[(size_t)h * a.ld_scores + j0 + jj], msp[h * nsp + i])) : 0.f;
+        }
+        __syncthreads();
+        double o[kMaxGroup][4];
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h)
+#pragma unroll
+            for (int d = 0; d < 4; ++d) o[h][d] = 0.0;
+        for (int jj = warp; jj < cnt; jj += kAttnWarps) {
+            float v[4];
+            load_kv_row(a, a.kv.v, a.vcur, j0 + jj, nc, g, lane, v);
+#pragma unroll
+            for (int h = 0; h < kMaxGroup; ++h)
+                if (h < G) {
+                    const double e = (double)ebuf[h * kAttnSplit + jj];
+#pragma unroll
+                    for (int d = 0; d < 4; ++d) o[h][d] += (double)v[d] * e;
+                }
+        }
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h)
+            if (h < G)
+#pragma unroll
+                for (int d = 0; d < 4; ++d) red[((size_t)warp * G + h) * 128 + lane * 4 + d] = o[h][d];
+        __syncthreads();
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h)
+            if (h < G) {
+                double oi = red[(size_t)h * 128 + tid];
+                for (int w = 1; w < kAttnWarps; ++w) oi += red[((size_t)w * G + h) * 128 + tid];
+                double si = 0.0;
+                for (int jj = 0; jj < cnt; ++jj) si += (double)ebuf[h * kAttnSplit + jj];
+                const float wi = det_expf(__fsub_rn(msp[h * nsp + i], M[h]));
+                acc[h] += oi * (double)wi;
+                ssum[h] += si * (double)wi;
+            }
+        __syncthreads();
+    }
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h)
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) acc[h][d] = 0.0;
-    for (int j = j0 + warp; j < j1; j += kAttnWarps) {
-        float v[DPL];
-        load_kv_row<HD>(a, a.kv.v, a.vcur, j, nc, g, lane, v);
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) {
-            if (h < G) {
-                const float p = __fmul_rn(det_expf(__fsub_rn(__ldcg(scores + (size_t)h * a.ld_scores + j), mx[h])), inv[h]);
-#pragma unroll
-                for (int d = 0; d < DPL; ++d) acc[h][d] += (double)v[d] * (double)p;
-            }
-        }
-    }
-    __shared__ double s_acc[kAttnWarps][HD];
-    __shared__ int s_last;
-    double *part = a.part + ((size_t)t * a.H + (size_t)g * G) * a.n_splits * HD;
-    for (int h = 0; h < G; ++h) {
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) s_acc[warp][lane * DPL + d] = acc[h][d];
-        __syncthreads();
-        for (int d = threadIdx.x; d < HD; d += kAttnThreads) {
-            double s = s_acc[0][d];
-            for (int w = 1; w < kAttnWarps; ++w) s += s_acc[w][d];
-            part[((size_t)h * a.n_splits + sp) * HD + d] = s;
-        }
-        __syncthreads();
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters2[t * a.Hkv + g], 1) == a.n_splits - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int h = 0; h < G; ++h)
-        for (int d = threadIdx.x; d < HD; d += kAttnThreads) {
-            double s = 0.0;
-            for (int k = 0; k < a.n_splits; ++k) s += __ldcg(part + ((size_t)h * a.n_splits + k) * HD + d);
-            a.out[(size_t)t * a.H * HD + (size_t)(g * G + h) * HD + d] = (float)s;
-        }
-    if (threadIdx.x == 0) a.counters2[t * a.Hkv + g] = 0;
+        if (h < G) a.out[(size_t)t * a.H * 128 + (size_t)(g * G + h) * 128 + tid] = (float)(acc[h] / ssum[h]);
+}
+
+constexpr size_t kAttnSmemMax = 200 * 1024;
+
+cudaError_t attn_setup() {
+    return cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmemMax);
 }
 
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
-    if (a.hd != 128 || a.H % a.Hkv != 0 || a.H / a.Hkv > kMaxGroup || a.n_splits < 1 || !a.scores || !a.stats ||
-        !a.part || !a.counters || !a.counters2)
+    const int G = a.Hkv > 0 ? a.H / a.Hkv : 0;
+    if (a.hd != 128 || G < 1 || a.H % a.Hkv != 0 || G > kMaxGroup || !a.scores || a.max_keys < 1)
         return cudaErrorInvalidValue;
+    const int nsp = (a.max_keys + kAttnSplit - 1) / kAttnSplit;
+    const size_t smem = attn_split_smem(G, nsp);
+    if (smem > kAttnSmemMax) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.Hkv, a.T, a.n_splits), dim3(kAttnThreads), 0, st, attr);
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.Hkv, a.T), dim3(kAttnThreads), smem, st, attr);
     count_launch();
-    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_scores_kernel<128>, a);
-    if (e != cudaSuccess) return e;
-    count_launch();
-    return cudaLaunchKernelEx(&cfg, attn_values_kernel<128>, a);
+    return cudaLaunchKernelEx(&cfg, attn_split_kernel, a);
 }
 
 }  // namespace s2k

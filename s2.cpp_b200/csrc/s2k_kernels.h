@@ -89,18 +89,17 @@ struct AttnArgs {
     int layer = 0;
     const float *kcur = nullptr, *vcur = nullptr;  // f32 [*][Hkv][hd], position n_cached + j at index j
     int cur_base = 0;  // token t attends to cur indices [0, cur_base + t]
-    int n_splits = 1;
+    int max_keys = 0;  // upper bound of any token's key range (sizes the split-maxima buffer)
     float *scores = nullptr;  // scratch [T][H][ld_scores]
     int ld_scores = 0;        // >= longest key range of the call
-    float *stats = nullptr;   // scratch [T][H][2] (max, 1/sum)
-    double *part = nullptr;   // scratch [T][H][n_splits][hd]
-    int *counters = nullptr;  // scratch [T][Hkv], zero between launches
-    int *counters2 = nullptr; // scratch [T][Hkv], zero between launches
     float *out = nullptr;     // [T][H*hd]
     const int *done = nullptr;
     int *err = nullptr;
 };
+// keys per attention split (the CPU oracle splits the same way)
+constexpr int kAttnSplit = 64;
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st);
+cudaError_t attn_setup();  // once per device before the first launch_attention
 
 // ---------------------------------------------------------------------------
 // Embeddings / sampling / frame bookkeeping

@@ -28,13 +28,12 @@ namespace s2k {
 // 8 consumer warps (the tile engine's mapping, s2k_tgemv.cuh) + 1 producer.
 constexpr int kMW = kTW;                   // consumer warps
 constexpr int kMNC = kMW * 32;             // consumer threads
-constexpr int kMThreads = kMNC + 32;       // + producer warp
+constexpr int kMThreads = kMNC + 64;       // + producer warp + helper warp (attention K/V prefetch)
 constexpr int kMStages = 10;               // ring of 17 KB weight tiles
 constexpr int kMKMax = 10240;
 constexpr int kMaxT = 2;
 constexpr int kHD = 128;
 constexpr int kPtab = 512;                 // cached pages whose ids are staged in shared memory
-constexpr int kAttnKeys = 1024;            // longest key range whose scores stay on chip
 constexpr int kMPC = 5;                    // 8-value activation chunks per consumer thread per prologue pass
 
 bool mega_gemv_ok(const MegaGemv &g) {
@@ -48,33 +47,70 @@ bool mega_gemv_ok(const MegaGemv &g) {
     return true;
 }
 
+constexpr int kAG = 4;    // most query heads per kv head (one attention unit serves a whole group)
+constexpr int kAF32 = 32;  // most f32 key rows of a unit (Fast-AR context)
+constexpr int kCombineFast = 8;  // splits the combining unit reads in one round trip
+
+// Attention unit buffers: the split's keys and values (f16 cache pages of the
+// Slow step, or f32 rows of the Fast-AR), this call's rotated keys/values
+// (Slow), the group's rotated queries as doubles (quarter rows padded to 33
+// so the four quarters of a key read four different banks), the split's
+// scores and exponentials, and the upper-half value partials.
+struct AttnSm {
+    union KV {
+        __half h[kAttnSplit][kHD];
+        float f[kAF32][kHD];
+    };
+    alignas(128) KV k;
+    alignas(128) KV v;
+    alignas(16) float kc[kMaxT][kHD];
+    alignas(16) float vc[kMaxT][kHD];
+    double q[kAG][4][33];
+    float s[kAG][kAttnSplit];
+    double e[kAG][kAttnSplit];
+    double o[kAG][kHD];
+    float m[kAG];
+    double S[kAG];
+    int last;
+};
+
+bool mega_attn_ok(const MegaAttn &a, int max_keys) {
+    if (a.hd != kHD || a.Hkv < 1 || a.H % a.Hkv != 0 || a.H / a.Hkv > kAG || a.T < 1 || a.T > kMaxT) return false;
+    if (a.part == nullptr || a.part_ms == nullptr || a.counters == nullptr) return false;
+    if ((max_keys + kAttnSplit - 1) / kAttnSplit > a.n_split_max) return false;
+    if (a.kv_k == nullptr) {  // Fast-AR: every key an f32 row of one split
+        if (a.cur_base + a.T > kAF32 || a.cur_base + a.T > kAttnSplit || a.n_cached_from_pos_base) return false;
+    } else if (a.cur_base != 0) {
+        return false;
+    }
+    return true;
+}
+
+struct GemvSm {
+    int8_t xq[kMaxT * kMKMax];  // quantized activation
+    float xd[kMaxT * kMKMax / 32];
+};
+
 struct MSmem {
     uint8_t ring[kMStages][kTileBytes];
     uint64_t full[kMStages], empty[kMStages];
-    int8_t xq[kMaxT * kMKMax];  // quantized activation (GEMV)
-    float xd[kMaxT * kMKMax / 32];
-    float nw[kNormMax];  // norm weights (GEMV); probabilities (attention)
+    uint64_t abar;  // K/V page copies of an attention unit
+    alignas(128) union {
+        GemvSm g;
+        AttnSm a;
+    } u;
     double tok[kMW][kMaxT];
-    float scale[kMaxT];
-    // attention
-    float aq[kHD];
-    double aqd[kHD];  // q as doubles for the score loops
-    alignas(16) float ak[kMaxT][kHD];  // read as float4
-    alignas(16) float av[kMaxT][kHD];
-    double vpart[kMW][kHD];
-    float red_f[kMW];
-    double red_d[kMW];
     int ptab[kPtab];  // page ids of the sequence's first kPtab pages (Slow segment)
     int ptab_ready;
+    int cur_op;  // op the consumers are running (written by consumer thread 0, read by the helper warp)
 };
 
 static_assert(sizeof(MSmem) <= 227 * 1024, "persistent kernel shared memory exceeds the per-CTA limit");
-static_assert(kAttnKeys <= kNormMax, "attention probabilities live in the norm-weight buffer");
-// shared arrays read with 16-byte vector loads
+// shared arrays read with vector loads or written by bulk copies
 static_assert(offsetof(MSmem, ring) % 16 == 0 && kTileBytes % 16 == 0, "ring alignment");
-static_assert(offsetof(MSmem, xq) % 16 == 0 && offsetof(MSmem, nw) % 16 == 0, "activation buffer alignment");
-static_assert(offsetof(MSmem, ak) % 16 == 0 && offsetof(MSmem, av) % 16 == 0, "key / value row alignment");
-static_assert(kAttnKeys % kMNC == 0, "keys per thread");
+static_assert(offsetof(MSmem, u) % 128 == 0, "activation / key buffer alignment");
+static_assert(sizeof(AttnSm::KV) == kAttnSplit * kHD * sizeof(__half) && kAttnSplit % kPage == 0,
+              "a split's cache pages fill the key buffer");
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     unsigned v;
@@ -137,8 +173,8 @@ struct TileCursor {
 // the ring's head and pulls those tiles into L2 with bulk prefetches, so HBM
 // keeps streaming while the consumers sit in a grid barrier, an activation
 // prologue or attention (the ring alone covers ~4 us of HBM time per SM).
-__device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, int G, int l2_ahead, int *err,
-                              unsigned long long *trace) {
+__device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, int G, int l2_ahead, int depth,
+                              int *err, unsigned long long *trace) {
     const uint64_t pol = policy_evict_first();
     TileCursor ld, pf;
     long long pf_n = 0;  // tiles the prefetch cursor has passed
@@ -149,11 +185,50 @@ __device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, 
         for (const uint8_t *p; pf_n < ps + kMStages + l2_ahead && (p = pf.next(ops, n_ops, cta, G)) != nullptr; ++pf_n)
             bulk_prefetch_l2(p, kTileBytes);
         const int slot = (int)(ps % kMStages);
-        if (ps >= kMStages && !mbar_wait(&sm.empty[slot], (uint32_t)((ps / kMStages) - 1) & 1u, err, ERR_WAIT_EMPTY))
-            return;
+        // at most `depth` tiles in flight: wait until tile ps - depth has been consumed
+        // (depth == kMStages: the slot's previous tile)
+        if (ps >= depth) {
+            const long long q = ps - depth;
+            if (!mbar_wait(&sm.empty[q % kMStages], (uint32_t)(q / kMStages) & 1u, err, ERR_WAIT_EMPTY)) return;
+        }
         mbar_arrive_expect_tx(&sm.full[slot], kTileBytes);
         bulk_g2s(sm.ring[slot], src, kTileBytes, &sm.full[slot], pol);
         if (trace != nullptr && ld.u == ld.u1) trace[((size_t)ld.op * G + cta) * kTraceSlots + 3] = globaltimer_ns();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// helper warp: K/V pages of the next attention op -> L2
+// ---------------------------------------------------------------------------
+// The cache pages an attention unit reads do not depend on the layer's QKV
+// projection, only the current token's row does.  When the consumers start
+// the op before a Slow attention op (its QKV GEMV), one lane pulls the pages
+// of this CTA's attention units into L2, so the unit's bulk copies do not
+// queue behind the weight stream in HBM.
+__device__ void mega_kv_prefetch(const MegaOp *ops, int n_ops, MSmem &sm, int cta, int G) {
+    volatile int *cur = &sm.cur_op;
+    for (int j = 1; j < n_ops; ++j) {
+        if (ops[j].kind != MK_ATTN || ops[j].a.kv_k == nullptr) continue;
+        const long long t0 = clock64();
+        while (*cur < j - 1) {
+            if (clock64() - t0 > kWaitLimitCycles) return;  // the consumers stopped (their error is reported)
+            __nanosleep(256);
+        }
+        const MegaAttn &a = ops[j].a;
+        const int nc = a.n_cached_from_pos_base && a.pos_base ? __ldcg(a.pos_base) : 0;
+        const int nspl = (nc + a.cur_base + a.T + kAttnSplit - 1) / kAttnSplit;
+        const int units = a.T * a.Hkv * nspl;
+        for (int u = cta; u < units; u += G) {
+            const int t = u / (a.Hkv * nspl), r = u - t * (a.Hkv * nspl), g = r / nspl, i = r - g * nspl;
+            const int j0 = i * kAttnSplit, cnt = min(kAttnSplit, nc + a.cur_base + t + 1 - j0);
+            const int ncp = max(0, min(cnt, nc - j0));
+            for (int p = 0; p < (ncp + kPage - 1) / kPage; ++p) {
+                const int page = __ldcg(a.block_table + j0 / kPage + p);
+                const size_t off = (((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage * kHD;
+                bulk_prefetch_l2(a.kv_k + off, kPage * kHD * sizeof(__half));
+                bulk_prefetch_l2(a.kv_v + off, kPage * kHD * sizeof(__half));
+            }
+        }
     }
 }
 
@@ -168,324 +243,420 @@ __device__ void mega_gemv(const MegaGemv &gref, const F8 (&nw)[kMPC], MSmem &sm,
     tg_range(g.R, g.K, cta, G, &u0, &u1);
     if (u0 == u1) return;  // no row tile of this op here (R / 32 < G)
     // the CTA owning row tile 0 stores act_out
-    tg_prologue8<MT, kMNC, kMPC>(g, nw, sm.xq, sm.xd, &sm.tok[0][0], kMaxT, u0 == 0, 1,
+    tg_prologue8<MT, kMNC, kMPC>(g, nw, sm.u.g.xq, sm.u.g.xd, &sm.tok[0][0], kMaxT, u0 == 0, 1,
                                  tr != nullptr ? tr + 4 : nullptr);
     named_sync(1, kMNC);
     if (tr != nullptr && threadIdx.x == 0) tr[1] = globaltimer_ns();
-    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.xq, sm.xd, cta, G, err,
+    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.u.g.xq, sm.u.g.xd, cta, G, err,
                    tr != nullptr ? tr + 6 : nullptr);
 }
 
 // ---------------------------------------------------------------------------
-// attention op: one CTA per (token, query head) unit
+// attention op: one CTA per (token, kv head, split of kAttnSplit keys) unit
 // ---------------------------------------------------------------------------
-// x0/x1 = pair (2i, 2i+1) of a head vector held by 64 consecutive threads
-// (i = index in the group); optional per-head RMSNorm (nw0/nw1 = the pair's
-// norm weights, prefetched; reduction over the 64 threads of warps w0, w0+1,
-// partial sums in red_d[red_slot..+1]) then RoPE with the prefetched (cos,
-// sin) of the pair.  Every consumer thread must call it (one named barrier).
-__device__ __forceinline__ void head_norm_rope(float &x0, float &x1, bool has_norm, float nw0, float nw1, float eps,
-                                               float2 cs, int red_slot, MSmem &sm, bool active) {
-    if (has_norm) {
-        double s = active ? (double)__fmul_rn(x0, x0) + (double)__fmul_rn(x1, x1) : 0.0;
-        s = warp_sum_d(s);
-        if ((threadIdx.x & 31) == 0 && active) sm.red_d[red_slot + ((threadIdx.x >> 5) & 1)] = s;
-    }
-    named_sync(3, kMNC);
-    if (active) {
-        if (has_norm) {
-            const double tot = sm.red_d[red_slot] + sm.red_d[red_slot + 1];
-            const float mean = (float)(tot / (double)kHD);
-            const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-            x0 = __fmul_rn(__fmul_rn(x0, sc), nw0);
-            x1 = __fmul_rn(__fmul_rn(x1, sc), nw1);
-        }
-        const float y0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-        const float y1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-        x0 = y0;
-        x1 = y1;
-    }
-}
-
-__device__ __forceinline__ const float *key_ptr_f32(const MegaAttn &a, MSmem &sm, int c, int g, bool value) {
-    // current-call key index c (positions >= n_cached): persistent f32 buffer or this op's tokens
-    if (c < a.cur_base) return (value ? a.vcur : a.kcur) + ((size_t)c * a.Hkv + g) * kHD;
-    return value ? sm.av[c - a.cur_base] : sm.ak[c - a.cur_base];
-}
-
-// Row of cached key/value position j for kv head g in the paged f16 cache;
-// ptab holds the first kPtab page ids of the sequence (staged per segment).
-__device__ __forceinline__ const __half *kv_row(const MegaAttn &a, const __half *base, const int *ptab, int g, int j) {
-    const int pg = j / kPage, slot = j - pg * kPage;
-    const int page = pg < kPtab ? ptab[pg] : __ldcg(a.block_table + pg);
-    return base + ((((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage + slot) * kHD;
-}
-
-// Dot product of a cached f16 key row (16 x 16 bytes, already loaded) with q.
-__device__ __forceinline__ float key_score(const uint4 (&raw)[kHD / 8], const double *aq, float scale) {
-    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
-#pragma unroll
-    for (int c = 0; c < kHD / 8; ++c) {
-        const int d = 8 * c;
-        const __half2 *hh = reinterpret_cast<const __half2 *>(&raw[c]);
-        const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
-        const float2 f2 = __half22float2(hh[2]), f3 = __half22float2(hh[3]);
-        s0 += (double)f0.x * aq[d] + (double)f0.y * aq[d + 1];
-        s1 += (double)f1.x * aq[d + 2] + (double)f1.y * aq[d + 3];
-        s2 += (double)f2.x * aq[d + 4] + (double)f2.y * aq[d + 5];
-        s3 += (double)f3.x * aq[d + 6] + (double)f3.y * aq[d + 7];
-    }
-    return __fmul_rn((float)((s0 + s1) + (s2 + s3)), scale);
-}
-
-// Attention of one (token t, query head h) unit per CTA (restates
-// src/s2_model.cpp:979-1039: qk-norm, RoPE mode 0, f16 cache of past
-// positions + f32 keys/values of this call, GQA h -> h / (H / Hkv), exact
-// softmax, weighted value sum).
+// Restates src/s2_model.cpp:979-1039 for the whole query-head group of one kv
+// head (GQA h -> h / (H / Hkv)): per-head qk-norm, RoPE mode 0, past keys and
+// values from the f16 cache, this call's keys and values un-rounded f32, and
+// softmax . V in the split convention the CPU oracle shares:
+//   s_j = float(sum_d double(k_j[d]) * double(q[d])) * scale
+//   split i: m_i = max s_j, e_j = det_expf(s_j - m_i),
+//            S_i = sum double(e_j), O_i[d] = sum double(v_j[d]) * double(e_j)
+//   out = float((sum_i O_i[d] * double(w_i)) / (sum_i S_i * double(w_i))),
+//         w_i = det_expf(m_i - max_i m_i)
+// A single-split unit writes out directly; otherwise each unit stores its
+// (O_i, m_i, S_i) and the last unit of the (token, kv head) to arrive combines
+// the splits in order.
 //
-// Latency plan: every global load that does not depend on another is issued
-// at the start of the unit -- q / k / v of this call, norm weights, RoPE
-// (cos, sin) -- together with L2 prefetches of the cached key and value rows,
-// so the key and value loads after the q / k normalization hit L2.  Scores stay in registers and the
-// probabilities in shared memory (up to kAttnKeys keys; longer contexts go
-// through the global score scratch).
-__device__ void mega_attn(const MegaAttn &a, MSmem &sm, int cta, int G, int *err, unsigned long long *tr) {
-    // tr (profiling, first unit only): [4] q/k/v normed and stored, [5] scores, [6] softmax, [7] values
-    auto mark = [&](int u, int k) {
-        if (tr != nullptr && u == cta && threadIdx.x == 0) tr[k] = globaltimer_ns();
-    };
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int units = a.T * a.H;
+// Latency plan: the split's cache pages are bulk-copied into shared memory at
+// the start of the unit, while warps 0..G-1 normalize and rotate the queries
+// and warps 4..7 this call's keys and values.  Scores use four threads per
+// key (32 dims each), values two threads per output dim (even / odd keys).
+
+// One 128-dim head vector held as 4 dims per lane (dims 4*lane..4*lane+3):
+// optional RMSNorm (w = this lane's norm weights) and RoPE with cs = this
+// lane's two (cos, sin) pairs, with the arithmetic of rms_norm_weighted and
+// ggml_rope_ext mode 0.
+__device__ __forceinline__ float4 head_norm_rope_warp(float4 x, bool has_norm, float4 w, float eps, float4 cs) {
+    if (has_norm) {
+        double s = (double)__fmul_rn(x.x, x.x) + (double)__fmul_rn(x.y, x.y) + (double)__fmul_rn(x.z, x.z) +
+                   (double)__fmul_rn(x.w, x.w);
+        s = warp_sum_d(s);
+        const float mean = (float)(s / (double)kHD);
+        const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+        x = make_float4(__fmul_rn(__fmul_rn(x.x, sc), w.x), __fmul_rn(__fmul_rn(x.y, sc), w.y),
+                        __fmul_rn(__fmul_rn(x.z, sc), w.z), __fmul_rn(__fmul_rn(x.w, sc), w.w));
+    }
+    const float y0 = __fsub_rn(__fmul_rn(x.x, cs.x), __fmul_rn(x.y, cs.y));
+    const float y1 = __fadd_rn(__fmul_rn(x.x, cs.y), __fmul_rn(x.y, cs.x));
+    const float y2 = __fsub_rn(__fmul_rn(x.z, cs.z), __fmul_rn(x.w, cs.w));
+    const float y3 = __fadd_rn(__fmul_rn(x.z, cs.w), __fmul_rn(x.w, cs.z));
+    return make_float4(y0, y1, y2, y3);
+}
+
+// Norm weights and (cos, sin) pairs a consumer thread needs in its first
+// attention unit (unit = cta): warps 0..G-1 normalize query head `warp` of
+// the unit's group, warps 4 and 6 this call's keys of tokens 0 and 1.  None
+// of it depends on the previous op, so the loads are issued before the grid
+// barrier.
+struct AttnPre {
+    float4 nw, cs;
+};
+
+__device__ __forceinline__ const float2 *rope_row(const MegaAttn &a, int pos) {
+    return a.rope + (size_t)min(max(pos, 0), a.rope_positions - 1) * (kHD / 2);
+}
+
+__device__ __forceinline__ AttnPre attn_preload(const MegaAttn &a, int u) {
+    AttnPre p;
+    p.nw = p.cs = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = a.H / a.Hkv;
-    float *const pbuf = sm.nw;  // probabilities (the GEMV norm buffer is idle during attention)
-    if (a.kv_k && cta < units && !sm.ptab_ready) {
+    const int base = a.pos_base ? __ldcg(a.pos_base) : 0;
+    const int nc = a.n_cached_from_pos_base ? base : 0;
+    const int pos0 = base + a.pos_add;
+    const int nspl = (nc + a.cur_base + a.T + kAttnSplit - 1) / kAttnSplit;
+    if (u >= a.T * a.Hkv * nspl) return p;
+    const int t = u / (a.Hkv * nspl);
+    int pos = -1;
+    const float *nw = nullptr;
+    if (warp < grp) {
+        pos = pos0 + t;
+        nw = a.q_norm;
+    } else if (warp >= 4 && ((warp - 4) & 1) == 0 && ((warp - 4) >> 1) <= t) {
+        pos = pos0 + ((warp - 4) >> 1);
+        nw = a.k_norm;
+    }
+    if (nw != nullptr) p.nw = __ldg(reinterpret_cast<const float4 *>(nw) + lane);
+    if (pos >= 0) p.cs = __ldg(reinterpret_cast<const float4 *>(rope_row(a, pos)) + lane);
+    return p;
+}
+
+__device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int cta, int G, int *err,
+                          unsigned long long *tr, uint32_t &apar) {
+    AttnSm &as = sm.u.a;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int grp = a.H / a.Hkv;
+    const bool slow = a.kv_k != nullptr;
+    const int base = a.pos_base ? __ldcg(a.pos_base) : 0;
+    const int nc = a.n_cached_from_pos_base ? base : 0;  // positions in the paged cache
+    const int pos0 = base + a.pos_add;                    // position of this call's token 0
+    const int nspl = (nc + a.cur_base + a.T + kAttnSplit - 1) / kAttnSplit;
+    const int units = a.T * a.Hkv * nspl;
+    auto mark = [&](int u, int k) {
+        if (tr != nullptr && u == cta && tid == 0) tr[k] = globaltimer_ns();
+    };
+    if (slow && cta < units && !sm.ptab_ready) {
         // the block table and n_past do not change within a segment: stage the
         // page ids once, at the first attention op this CTA runs
-        const int nc = a.n_cached_from_pos_base && a.pos_base ? __ldcg(a.pos_base) : 0;
         const int npg = min((nc + kPage - 1) / kPage, kPtab);
         for (int i = tid; i < npg; i += kMNC) sm.ptab[i] = __ldcg(a.block_table + i);
         named_sync(3, kMNC);
         if (tid == 0) sm.ptab_ready = 1;
     }
     for (int u = cta; u < units; u += G) {
-        const int t = u / a.H, h = u - t * a.H, g = h / grp;
-        const int base = a.pos_base ? __ldcg(a.pos_base) : 0;
-        const int nc = a.n_cached_from_pos_base ? base : 0;
-        const int pos0 = base + a.pos_add;
-        const int Lk = nc + a.cur_base + t + 1;
-        const bool in_smem = Lk <= kAttnKeys;
-        if (pos0 + t >= a.rope_positions && tid == 0) atomicOr(err, ERR_BAD_POS);
-        // ---- A. independent loads ----
-        const int i = tid & 63;
-        const bool grp_q = tid < 64, grp_k = tid >= 64 && tid < 128, grp_v = tid >= 128 && tid < 192;
-        float qx0 = 0.f, qx1 = 0.f, qn0 = 0.f, qn1 = 0.f;
-        float2 qcs = make_float2(0.f, 0.f);
-        float kx0[kMaxT], kx1[kMaxT], vx0[kMaxT], vx1[kMaxT];
-        float2 kcs[kMaxT];
-        float kn0 = 0.f, kn1 = 0.f;
-        if (grp_q) {
-            const float *src = a.qkv + (size_t)t * a.ldqkv + (size_t)h * kHD;
-            qx0 = __ldcg(src + 2 * i);
-            qx1 = __ldcg(src + 2 * i + 1);
-            if (a.q_norm) {
-                qn0 = __ldg(a.q_norm + 2 * i);
-                qn1 = __ldg(a.q_norm + 2 * i + 1);
+        const int t = u / (a.Hkv * nspl), r = u - t * (a.Hkv * nspl), g = r / nspl, i = r - g * nspl;
+        const int Lk = nc + a.cur_base + t + 1;  // keys of token t
+        const int nsp = (Lk + kAttnSplit - 1) / kAttnSplit;
+        if (i >= nsp) continue;  // CTA-uniform
+        const int j0 = i * kAttnSplit, cnt = min(kAttnSplit, Lk - j0);
+        const int ncp = slow ? max(0, min(cnt, nc - j0)) : 0;  // cached keys of the split
+        const int npg = (ncp + kPage - 1) / kPage;
+        // ---- A. the split's cache pages -> shared memory (bulk copies) ----
+        if (npg > 0 && tid == 0) {
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&sm.abar, (uint32_t)(2 * npg * kPage * kHD * sizeof(__half)));
+            for (int p = 0; p < npg; ++p) {
+                const int pg = j0 / kPage + p;
+                const int page = pg < kPtab ? sm.ptab[pg] : __ldcg(a.block_table + pg);
+                const size_t off = (((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage * kHD;
+                bulk_g2s_plain(&as.k.h[p * kPage][0], a.kv_k + off, kPage * kHD * sizeof(__half), &sm.abar);
+                bulk_g2s_plain(&as.v.h[p * kPage][0], a.kv_v + off, kPage * kHD * sizeof(__half), &sm.abar);
             }
-            qcs = __ldg(a.rope + (size_t)min(pos0 + t, a.rope_positions - 1) * (kHD / 2) + i);
         }
-#pragma unroll
-        for (int tt = 0; tt < kMaxT; ++tt) {
-            kx0[tt] = kx1[tt] = vx0[tt] = vx1[tt] = 0.f;
-            kcs[tt] = make_float2(0.f, 0.f);
+        // ---- B. queries (warps 0..grp-1), this call's keys / values (warps 4..7) ----
+        const bool has_cur = j0 + cnt > nc + a.cur_base;  // the split reaches this call's tokens
+        const bool own = (nc + a.cur_base + t) / kAttnSplit == i;  // token t's own key lies in this split
+        if (warp < grp) {
+            const int h = g * grp + warp;
+            const int pos = pos0 + t;
+            if (pos >= a.rope_positions && lane == 0) atomicOr(err, ERR_BAD_POS);
+            const float4 x = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (size_t)t * a.ldqkv + (size_t)h * kHD) + lane);
+            const AttnPre pp = u == cta ? pre : attn_preload(a, u);
+            const float4 y = head_norm_rope_warp(x, a.q_norm != nullptr, pp.nw, a.eps, pp.cs);
+            double *qd = &as.q[warp][lane >> 3][4 * (lane & 7)];
+            qd[0] = (double)y.x;
+            qd[1] = (double)y.y;
+            qd[2] = (double)y.z;
+            qd[3] = (double)y.w;
+        } else if (warp >= 4 && has_cur) {
+            const int tt = (warp - 4) >> 1, isv = (warp - 4) & 1;
             if (tt <= t) {
-                const float *row = a.qkv + (size_t)tt * a.ldqkv;
-                if (grp_k) {
-                    kx0[tt] = __ldcg(row + (size_t)(a.H + g) * kHD + 2 * i);
-                    kx1[tt] = __ldcg(row + (size_t)(a.H + g) * kHD + 2 * i + 1);
-                    kcs[tt] = __ldg(a.rope + (size_t)min(pos0 + tt, a.rope_positions - 1) * (kHD / 2) + i);
+                const int pos = pos0 + tt;
+                const float *row = a.qkv + (size_t)tt * a.ldqkv + (size_t)(a.H + (isv ? a.Hkv : 0) + g) * kHD;
+                float4 x = __ldcg(reinterpret_cast<const float4 *>(row) + lane);
+                if (!isv) {
+                    const AttnPre pp = u == cta ? pre : attn_preload(a, u);
+                    x = head_norm_rope_warp(x, a.k_norm != nullptr, pp.nw, a.eps, pp.cs);
                 }
-                if (grp_v) {
-                    vx0[tt] = __ldcg(row + (size_t)(a.H + a.Hkv + g) * kHD + 2 * i);
-                    vx1[tt] = __ldcg(row + (size_t)(a.H + a.Hkv + g) * kHD + 2 * i + 1);
-                }
-            }
-        }
-        if (grp_k && a.k_norm) {
-            kn0 = __ldg(a.k_norm + 2 * i);
-            kn1 = __ldg(a.k_norm + 2 * i + 1);
-        }
-        // cached key and value rows -> L2 while q and k are normalized
-        for (int j = tid; j < nc; j += kMNC) {
-            const char *kp = reinterpret_cast<const char *>(kv_row(a, a.kv_k, sm.ptab, g, j));
-            const char *vp = reinterpret_cast<const char *>(kv_row(a, a.kv_v, sm.ptab, g, j));
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(kp));
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(kp + 128));
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(vp));
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(vp + 128));
-        }
-        // ---- B. q: norm + RoPE ----
-        head_norm_rope(qx0, qx1, a.q_norm != nullptr, qn0, qn1, a.eps, qcs, 0, sm, grp_q);
-        if (grp_q) {
-            sm.aq[2 * i] = qx0;
-            sm.aq[2 * i + 1] = qx1;
-            sm.aqd[2 * i] = (double)qx0;
-            sm.aqd[2 * i + 1] = (double)qx1;
-        }
-        // ---- C. k, v of this call's tokens 0..t ----
-        for (int tt = 0; tt <= t; ++tt) {
-            float x0 = kx0[0], x1 = kx1[0];
-            float2 cs = kcs[0];
-#pragma unroll
-            for (int q = 1; q < kMaxT; ++q)
-                if (q == tt) {
-                    x0 = kx0[q];
-                    x1 = kx1[q];
-                    cs = kcs[q];
-                }
-            // k pairs sit on threads 64..127 (warps 2, 3): reduction slots 2, 3
-            head_norm_rope(x0, x1, a.k_norm != nullptr, kn0, kn1, a.eps, cs, 2, sm, grp_k);
-            if (grp_k) {
-                sm.ak[tt][2 * i] = x0;
-                sm.ak[tt][2 * i + 1] = x1;
-            }
-            if (grp_v) {
-                float v0 = vx0[0], v1 = vx1[0];
-#pragma unroll
-                for (int q = 1; q < kMaxT; ++q)
-                    if (q == tt) {
-                        v0 = vx0[q];
-                        v1 = vx1[q];
+                float *dst = slow ? (isv ? as.vc[tt] : as.kc[tt]) : (isv ? as.v.f[a.cur_base + tt] : as.k.f[a.cur_base + tt]);
+                reinterpret_cast<float4 *>(dst)[lane] = x;
+                if (tt == t && own) {
+                    // token t's K/V: f32 for the later calls of this frame, f16 into the cache (Slow)
+                    float *cur = (isv ? a.vcur : a.kcur) + ((size_t)(a.cur_base + t) * a.Hkv + g) * kHD;
+                    reinterpret_cast<float4 *>(cur)[lane] = x;
+                    if (slow) {
+                        const int pg = pos / kPage, slot = pos - pg * kPage;
+                        if (pos >= 0 && pg < a.kv_pages) {
+                            const int page = __ldcg(a.block_table + pg);
+                            __half *c = (isv ? a.kv_v : a.kv_k) +
+                                        ((((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage + slot) * kHD;
+                            __half2 *c2 = reinterpret_cast<__half2 *>(c) + 2 * lane;
+                            c2[0] = __floats2half2_rn(x.x, x.y);
+                            c2[1] = __floats2half2_rn(x.z, x.w);
+                        } else if (lane == 0) {
+                            atomicOr(err, ERR_BAD_POS);
+                        }
                     }
-                sm.av[tt][2 * i] = v0;
-                sm.av[tt][2 * i + 1] = v1;
+                }
+            }
+        }
+        mark(u, 8);
+        if (!slow) {
+            // earlier Fast-AR positions of this frame: f32 rows written by the previous passes
+            for (int idx = tid; idx < a.cur_base * 64; idx += kMNC) {
+                const int row = idx >> 6, isv = (idx >> 5) & 1, c4 = idx & 31;
+                const float4 x = __ldcg(reinterpret_cast<const float4 *>((isv ? a.vcur : a.kcur) +
+                                                                         ((size_t)row * a.Hkv + g) * kHD) + c4);
+                reinterpret_cast<float4 *>(isv ? as.v.f[row] : as.k.f[row])[c4] = x;
             }
         }
         named_sync(3, kMNC);
-        // the first query head of the group stores token t's K/V
-        if (h % grp == 0 && tid < kHD) {
-            const size_t ci = ((size_t)(a.cur_base + t) * a.Hkv + g) * kHD + tid;
-            a.kcur[ci] = sm.ak[t][tid];
-            a.vcur[ci] = sm.av[t][tid];
-            if (a.kv_k) {
-                const int pos = pos0 + t, pg = pos / kPage, slot = pos % kPage;
-                if (pos >= 0 && pg < a.kv_pages) {
-                    const int page = __ldcg(a.block_table + pg);
-                    const size_t off = ((((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage + slot) * kHD + tid;
-                    a.kv_k[off] = __float2half_rn(sm.ak[t][tid]);
-                    a.kv_v[off] = __float2half_rn(sm.av[t][tid]);
-                } else if (tid == 0) {
-                    atomicOr(err, ERR_BAD_POS);
-                }
-            }
+        mark(u, 9);
+        if (npg > 0) {
+            mbar_wait(&sm.abar, apar, err, ERR_WAIT_FULL);
+            apar ^= 1u;
         }
         mark(u, 4);
-        // ---- D. scores -> sc (pbuf in shared memory when the keys fit) ----
-        float *const sc = in_smem ? pbuf : a.scores + (size_t)u * a.ld_scores;
-        // cached keys: one f16 row per thread (rows were prefetched into L2)
-        for (int j = tid; j < nc; j += kMNC) {
-            const uint4 *kp = reinterpret_cast<const uint4 *>(kv_row(a, a.kv_k, sm.ptab, g, j));
-            uint4 raw[kHD / 8];
+        // ---- C. scores: thread (key jj = tid / 4, quarter c = tid % 4) over 32 dims ----
+        {
+            const int jj = tid >> 2, c = tid & 3;
+            double acc[kAG];
 #pragma unroll
-            for (int c = 0; c < kHD / 8; ++c) raw[c] = __ldcg(kp + c);
-            sc[j] = key_score(raw, sm.aqd, a.scale);
-        }
-        // keys of this call (f32 rows): one warp per key, lane = 4 dims
-        for (int c = warp; c < Lk - nc; c += kMW) {
-            const bool gl = c < a.cur_base;
-            const float4 k4 = gl ? __ldcg(reinterpret_cast<const float4 *>(key_ptr_f32(a, sm, c, g, false)) + lane)
-                                 : reinterpret_cast<const float4 *>(key_ptr_f32(a, sm, c, g, false))[lane];
-            double p = (double)k4.x * sm.aqd[4 * lane] + (double)k4.y * sm.aqd[4 * lane + 1] +
-                       (double)k4.z * sm.aqd[4 * lane + 2] + (double)k4.w * sm.aqd[4 * lane + 3];
-            p = warp_sum_d(p);
-            if (lane == 0) sc[nc + c] = __fmul_rn((float)p, a.scale);
+            for (int h = 0; h < kAG; ++h) acc[h] = 0.0;
+            if (jj < cnt) {
+                const int j = j0 + jj;
+                if (j < nc) {
+                    const uint4 *kp = reinterpret_cast<const uint4 *>(&as.k.h[jj][32 * c]);
+#pragma unroll
+                    for (int qd = 0; qd < 4; ++qd) {
+                        const uint4 raw = kp[qd];
+                        const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+                        for (int p = 0; p < 4; ++p) {
+                            const float2 f = __half22float2(hh[p]);
+                            const double k0 = (double)f.x, k1 = (double)f.y;
+#pragma unroll
+                            for (int h = 0; h < kAG; ++h)
+                                acc[h] += k0 * as.q[h][c][8 * qd + 2 * p] + k1 * as.q[h][c][8 * qd + 2 * p + 1];
+                        }
+                    }
+                } else {
+                    const float *kr = slow ? &as.kc[j - nc][32 * c] : &as.k.f[jj][32 * c];
+#pragma unroll
+                    for (int d4 = 0; d4 < 8; ++d4) {
+                        const float4 f = reinterpret_cast<const float4 *>(kr)[d4];
+#pragma unroll
+                        for (int h = 0; h < kAG; ++h)
+                            acc[h] += (double)f.x * as.q[h][c][4 * d4] + (double)f.y * as.q[h][c][4 * d4 + 1] +
+                                      (double)f.z * as.q[h][c][4 * d4 + 2] + (double)f.w * as.q[h][c][4 * d4 + 3];
+                    }
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < kAG; ++h) {
+                acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
+                acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 2);
+            }
+            if (c == 0 && jj < cnt)
+#pragma unroll
+                for (int h = 0; h < kAG; ++h)
+                    if (h < grp) as.s[h][jj] = __fmul_rn((float)acc[h], a.scale);
         }
         named_sync(3, kMNC);
         mark(u, 5);
-        // ---- E. exact softmax: max, sum in double, p' = exp(s - max) * (1 / sum) ----
-        float mx = -INFINITY;
-        for (int j = tid; j < Lk; j += kMNC) mx = fmaxf(mx, sc[j]);
-        mx = warp_max(mx);
-        if (lane == 0) sm.red_f[warp] = mx;
-        named_sync(3, kMNC);
-        mx = sm.red_f[0];
-        for (int w = 1; w < kMW; ++w) mx = fmaxf(mx, sm.red_f[w]);
-        double sum = 0.0;
-        for (int j = tid; j < Lk; j += kMNC) sum += (double)det_expf(__fsub_rn(sc[j], mx));
-        sum = warp_sum_d(sum);
-        if (lane == 0) sm.red_d[warp] = sum;
-        named_sync(3, kMNC);
-        double tot = 0.0;
-        for (int w = 0; w < kMW; ++w) tot += sm.red_d[w];
-        const float inv = (float)(1.0 / tot);
-        for (int j = tid; j < Lk; j += kMNC) sc[j] = __fmul_rn(det_expf(__fsub_rn(sc[j], mx)), inv);
-        float *const pr = sc;
+        // ---- D. the split's softmax statistics: warp h for head h ----
+        if (warp < grp) {
+            const float s0 = lane < cnt ? as.s[warp][lane] : -INFINITY;
+            const float s1 = lane + 32 < cnt ? as.s[warp][lane + 32] : -INFINITY;
+            const float mx = warp_max(fmaxf(s0, s1));
+            const float e0 = lane < cnt ? det_expf(__fsub_rn(s0, mx)) : 0.f;
+            const float e1 = lane + 32 < cnt ? det_expf(__fsub_rn(s1, mx)) : 0.f;
+            as.e[warp][lane] = (double)e0;
+            as.e[warp][lane + 32] = (double)e1;
+            const double S = warp_sum_d((double)e0 + (double)e1);
+            if (lane == 0) {
+                as.m[warp] = mx;
+                as.S[warp] = S;
+            }
+        }
         named_sync(3, kMNC);
         mark(u, 6);
-        // ---- F. values: warp w takes keys w, w + kMW, ...; lane takes dims 4*lane..4*lane+3;
-        // kVU keys per warp are loaded before any is used (rows were prefetched into L2) ----
-        {
-            constexpr int kVU = 16;
-            double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
-            int j = warp;
-            for (; j + (kVU - 1) * kMW < nc; j += kVU * kMW) {
-                uint2 raw[kVU];
+        // ---- E. values: thread (dim d = tid % 128, key parity kh = tid / 128) ----
+        const int d = tid & (kHD - 1), kh = tid >> 7;
+        double o[kAG];
 #pragma unroll
-                for (int q = 0; q < kVU; ++q)
-                    raw[q] = __ldcg(reinterpret_cast<const uint2 *>(kv_row(a, a.kv_v, sm.ptab, g, j + q * kMW) + 4 * lane));
+        for (int h = 0; h < kAG; ++h) o[h] = 0.0;
+        for (int jj = kh; jj < cnt; jj += 2) {
+            const int j = j0 + jj;
+            const double vd = j < nc ? (double)__half2float(as.v.h[jj][d])
+                                     : (double)(slow ? as.vc[j - nc][d] : as.v.f[jj][d]);
 #pragma unroll
-                for (int q = 0; q < kVU; ++q) {
-                    const __half2 *hh = reinterpret_cast<const __half2 *>(&raw[q]);
-                    const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
-                    const double pd = (double)pr[j + q * kMW];
-                    acc0 += (double)f0.x * pd;
-                    acc1 += (double)f0.y * pd;
-                    acc2 += (double)f1.x * pd;
-                    acc3 += (double)f1.y * pd;
-                }
-            }
-            for (; j < nc; j += kMW) {
-                const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(kv_row(a, a.kv_v, sm.ptab, g, j) + 4 * lane));
-                const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
-                const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
-                const double pd = (double)pr[j];
-                acc0 += (double)f0.x * pd;
-                acc1 += (double)f0.y * pd;
-                acc2 += (double)f1.x * pd;
-                acc3 += (double)f1.y * pd;
-            }
-            // keys of this call (f32): j = nc + c
-            for (int c = warp; c < Lk - nc; c += kMW) {
-                const float *vp = key_ptr_f32(a, sm, c, g, true) + 4 * lane;
-                const bool gl = c < a.cur_base;
-                const float v0 = gl ? __ldcg(vp) : vp[0], v1 = gl ? __ldcg(vp + 1) : vp[1];
-                const float v2 = gl ? __ldcg(vp + 2) : vp[2], v3 = gl ? __ldcg(vp + 3) : vp[3];
-                const double pd = (double)pr[nc + c];
-                acc0 += (double)v0 * pd;
-                acc1 += (double)v1 * pd;
-                acc2 += (double)v2 * pd;
-                acc3 += (double)v3 * pd;
-            }
-            sm.vpart[warp][4 * lane] = acc0;
-            sm.vpart[warp][4 * lane + 1] = acc1;
-            sm.vpart[warp][4 * lane + 2] = acc2;
-            sm.vpart[warp][4 * lane + 3] = acc3;
+            for (int h = 0; h < kAG; ++h) o[h] += vd * as.e[h][jj];
         }
+        if (kh == 1)
+#pragma unroll
+            for (int h = 0; h < kAG; ++h) as.o[h][d] = o[h];
         named_sync(3, kMNC);
         mark(u, 7);
-        if (tid < kHD) {
-            double o = sm.vpart[0][tid];
-            for (int k = 1; k < kMW; ++k) o += sm.vpart[k][tid];
-            a.out[(size_t)t * a.H * kHD + (size_t)h * kHD + tid] = (float)o;
+        if (kh == 0)
+#pragma unroll
+            for (int h = 0; h < kAG; ++h) o[h] += as.o[h][d];
+        if (nsp == 1) {
+            if (kh == 0)
+#pragma unroll
+                for (int h = 0; h < kAG; ++h)
+                    if (h < grp) a.out[(size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d] = (float)(o[h] / as.S[h]);
+        } else {
+            const size_t pu = ((size_t)t * a.Hkv + g) * a.n_split_max;
+            if (kh == 0)
+#pragma unroll
+                for (int h = 0; h < kAG; ++h)
+                    if (h < grp) a.part[((pu + i) * grp + h) * kHD + d] = o[h];
+            if (tid < grp) {
+                a.part_ms[((pu + i) * grp + tid) * 2] = (double)as.m[tid];
+                a.part_ms[((pu + i) * grp + tid) * 2 + 1] = as.S[tid];
+            }
+            named_sync(3, kMNC);
+            if (tid == 0) {
+                __threadfence();
+                mark(u, 10);
+                as.last = atomicAdd(a.counters + t * a.Hkv + g, 1) == nsp - 1;
+                mark(u, 3);
+            }
+            named_sync(3, kMNC);
+            if (as.last) {
+                __threadfence();
+                // combine in split order; (m_k, S_k) staged in shared memory in chunks of
+                // kAttnSplit splits (one parallel load each), weights w_k = det_expf(m_k - M)
+                // kept as doubles in as.o; thread (d, kh) sums heads kh, kh + 2
+                if (nsp <= kCombineFast) {
+                    // one round trip: (m_k, S_k) staged by threads p < grp * nsp while every
+                    // thread loads its own O_k[h][d] of heads kh, kh + 2 into registers
+                    double ov[2][kCombineFast];
+#pragma unroll
+                    for (int x = 0; x < 2; ++x)
+#pragma unroll
+                        for (int k = 0; k < kCombineFast; ++k)
+                            ov[x][k] = (kh + 2 * x < grp && k < nsp)
+                                           ? __ldcg(a.part + ((pu + k) * grp + kh + 2 * x) * kHD + d)
+                                           : 0.0;
+                    if (tid < grp * nsp) {
+                        const int h = tid / nsp, k = tid - h * nsp;
+                        const double2 ms = __ldcg(reinterpret_cast<const double2 *>(a.part_ms + ((pu + k) * grp + h) * 2));
+                        as.s[h][k] = (float)ms.x;
+                        as.e[h][k] = ms.y;
+                    }
+                    named_sync(3, kMNC);
+#pragma unroll
+                    for (int x = 0; x < 2; ++x) {
+                        const int h = kh + 2 * x;
+                        if (h < grp) {
+                            float M = as.s[h][0];
+                            for (int k = 1; k < nsp; ++k) M = fmaxf(M, as.s[h][k]);
+                            double acc = 0.0, S = 0.0;
+#pragma unroll
+                            for (int k = 0; k < kCombineFast; ++k)
+                                if (k < nsp) {
+                                    const double w = (double)det_expf(__fsub_rn(as.s[h][k], M));
+                                    acc += ov[x][k] * w;
+                                    S += as.e[h][k] * w;
+                                }
+                            a.out[(size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d] = (float)(acc / S);
+                        }
+                    }
+                    if (tid == 0) a.counters[t * a.Hkv + g] = 0;
+                    named_sync(3, kMNC);
+                    continue;
+                }
+                const int nch = (nsp + kAttnSplit - 1) / kAttnSplit;
+                auto stage = [&](int kb, int kn) {
+                    for (int p = tid; p < grp * kn; p += kMNC) {
+                        const int h = p / kn, k = p - h * kn;
+                        const double2 ms = __ldcg(reinterpret_cast<const double2 *>(a.part_ms + ((pu + kb + k) * grp + h) * 2));
+                        as.s[h][k] = (float)ms.x;
+                        as.e[h][k] = ms.y;
+                    }
+                    named_sync(3, kMNC);
+                };
+                for (int c = 0; c < nch; ++c) {
+                    const int kb = c * kAttnSplit, kn = min(kAttnSplit, nsp - kb);
+                    stage(kb, kn);
+                    if (warp < grp) {
+                        float mx = fmaxf(lane < kn ? as.s[warp][lane] : -INFINITY,
+                                         lane + 32 < kn ? as.s[warp][lane + 32] : -INFINITY);
+                        mx = warp_max(mx);
+                        if (lane == 0) as.m[warp] = c == 0 ? mx : fmaxf(as.m[warp], mx);
+                    }
+                    named_sync(3, kMNC);
+                }
+                double acc[2] = {0.0, 0.0}, S[2] = {0.0, 0.0};
+                for (int c = 0; c < nch; ++c) {
+                    const int kb = c * kAttnSplit, kn = min(kAttnSplit, nsp - kb);
+                    if (nch > 1) stage(kb, kn);  // one chunk: still staged from the max pass
+                    for (int p = tid; p < grp * kn; p += kMNC) {
+                        const int h = p / kn, k = p - h * kn;
+                        as.o[h][k] = (double)det_expf(__fsub_rn(as.s[h][k], as.m[h]));
+                    }
+                    named_sync(3, kMNC);
+#pragma unroll
+                    for (int x = 0; x < 2; ++x) {
+                        const int h = kh + 2 * x;
+                        if (h < grp) {
+                            const double *src = a.part + ((pu + kb) * grp + h) * kHD + d;
+#pragma unroll 8
+                            for (int k = 0; k < kn; ++k) {
+                                acc[x] += __ldcg(src + (size_t)k * grp * kHD) * as.o[h][k];
+                                S[x] += as.e[h][k] * as.o[h][k];
+                            }
+                        }
+                    }
+                    named_sync(3, kMNC);
+                }
+#pragma unroll
+                for (int x = 0; x < 2; ++x) {
+                    const int h = kh + 2 * x;
+                    if (h < grp) a.out[(size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d] = (float)(acc[x] / S[x]);
+                }
+                if (tid == 0) a.counters[t * a.Hkv + g] = 0;
+            }
         }
-        named_sync(3, kMNC);
+        named_sync(3, kMNC);  // the unit's shared buffers are free for the next unit
     }
 }
+
+// Every load a thread needs is issued before any is used (token id, the
+// codebook ids, then all rows' quants and scales), so the op costs about three
+// memory round trips; the codebook sum keeps the reference's order cb0..cb9.
+constexpr int kMaxCb = 16;
 
 __device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err) {
     const int stride = e.ncb + 1;
     for (long long idx = (long long)cta * kMNC + threadIdx.x; idx < (long long)e.T * e.dim; idx += (long long)G * kMNC) {
         const int t = (int)(idx / e.dim), i = (int)(idx - (long long)t * e.dim);
         int tok = __ldcg(e.tokens + t * stride);
+        int ids[kMaxCb];
+#pragma unroll
+        for (int cb = 0; cb < kMaxCb; ++cb) ids[cb] = cb < e.ncb ? __ldcg(e.tokens + t * stride + 1 + cb) : 0;
         if (tok < 0 || tok >= e.e_rows) {
             if (i == 0) atomicOr(err, ERR_BAD_TOKEN);
             tok = 0;
@@ -493,16 +664,23 @@ __device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err
         const bool sem = tok >= e.sem_begin && tok <= e.sem_end;
         float x = tq_elem(e.e, e.dim, tok, i);
         if (sem && e.ncb > 0) {
-            float s = 0.f;
-            for (int cb = 0; cb < e.ncb; ++cb) {
-                int id = __ldcg(e.tokens + t * stride + 1 + cb) + cb * e.cb_size;
-                if (id < 0 || id >= e.c_rows) {
-                    if (i == 0) atomicOr(err, ERR_BAD_TOKEN);
-                    id = 0;
+            float r[kMaxCb];
+#pragma unroll
+            for (int cb = 0; cb < kMaxCb; ++cb) {
+                r[cb] = 0.f;
+                if (cb < e.ncb) {
+                    int id = ids[cb] + cb * e.cb_size;
+                    if (id < 0 || id >= e.c_rows) {
+                        if (i == 0) atomicOr(err, ERR_BAD_TOKEN);
+                        id = 0;
+                    }
+                    r[cb] = tq_elem(e.c, e.dim, id, i);
                 }
-                const float r = tq_elem(e.c, e.dim, id, i);
-                s = cb == 0 ? r : __fadd_rn(s, r);
             }
+            float s = r[0];
+#pragma unroll
+            for (int cb = 1; cb < kMaxCb; ++cb)
+                if (cb < e.ncb) s = __fadd_rn(s, r[cb]);
             x = __fadd_rn(x, s);
         }
         if (e.scale_cb && sem) x = __fmul_rn(x, e.sem_scale);
@@ -530,6 +708,8 @@ __device__ void mega_embed_fast(const MegaEmbedFast &e, int cta, int G, int *err
     }
 }
 
+// 9 warps per CTA: one SM sub-partition holds three of them, so its 16K
+// registers cap a thread at 168 (the launch bound keeps the kernel there).
 template <int MT>
 __global__ void __launch_bounds__(kMThreads, 1)
     mega_kernel(const MegaOp *__restrict__ ops, int n_ops, MegaCtl *ctl, const int *done, int *err, int l2_ahead,
@@ -544,12 +724,19 @@ __global__ void __launch_bounds__(kMThreads, 1)
             mbar_init(&sm.full[i], 1);
             mbar_init(&sm.empty[i], kMW);
         }
+        mbar_init(&sm.abar, 1);
         fence_mbar_init();
         sm.ptab_ready = 0;
+        sm.cur_op = 0;
     }
     __syncthreads();
     if (warp == kMW) {
-        if (lane == 0) mega_producer(ops, n_ops, sm, cta, G, l2_ahead, err, trace);
+        if (lane == 0) mega_producer(ops, n_ops, sm, cta, G, l2_ahead, (flags >> 8) > 0 ? min(flags >> 8, kMStages) : kMStages,
+                                     err, trace);
+        return;
+    }
+    if (warp == kMW + 1) {
+        if (lane == 0) mega_kv_prefetch(ops, n_ops, sm, cta, G);
         return;
     }
     // trace: per op and CTA, [start, prologue done, work done, producer's last tile issued]
@@ -558,12 +745,16 @@ __global__ void __launch_bounds__(kMThreads, 1)
     };
     int cslot = 0;  // ring position of the consumers
     uint32_t cphase = 0;
+    uint32_t apar = 0;  // phase of the attention page barrier
     for (int i = 0; i < n_ops; ++i) {
         const int kind = ops[i].kind;
         // RMSNorm weights of the next GEMV do not depend on the previous op: load them before the barrier
         F8 nw[kMPC];
+        AttnPre ap;
         if (kind == MK_GEMV) tg_norm_preload<kMPC, kMNC>(ops[i].g, nw);
+        if (kind == MK_ATTN) ap = attn_preload(ops[i].a, cta);
         if (i > 0) grid_wait(ctl, (unsigned)(i * G), err);
+        if (threadIdx.x == 0) *reinterpret_cast<volatile int *>(&sm.cur_op) = i;
         stamp(i, 0);
         stamp(i, 1);
         switch (kind) {
@@ -572,7 +763,8 @@ __global__ void __launch_bounds__(kMThreads, 1)
                           trace != nullptr ? trace + ((size_t)i * G + cta) * kTraceSlots : nullptr);
             break;
         case MK_ATTN:
-            mega_attn(ops[i].a, sm, cta, G, err, trace != nullptr ? trace + ((size_t)i * G + cta) * kTraceSlots : nullptr);
+            mega_attn(ops[i].a, ap, sm, cta, G, err,
+                      trace != nullptr ? trace + ((size_t)i * G + cta) * kTraceSlots : nullptr, apar);
             break;
         case MK_EMBED_SLOW: mega_embed_slow(ops[i].es, cta, G, err); break;
         case MK_EMBED_FAST: mega_embed_fast(ops[i].ef, cta, G, err); break;

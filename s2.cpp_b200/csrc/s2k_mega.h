@@ -41,8 +41,12 @@ struct MegaAttn {
     const int *block_table;
     int kv_layers, kv_pages;
     int layer;
-    float *scores;        // scratch [T*H][ld_scores]
-    int ld_scores;
+    // split partials: per (token, kv head, split) O_i [group][hd] and
+    // (m_i, S_i) [group][2], kAttnSplit keys per split; arrival counters per
+    // (token, kv head), zero between ops (the combining unit resets them)
+    double *part, *part_ms;
+    int *counters;
+    int n_split_max;
     float *out;           // [T][H*hd]
 };
 
@@ -97,14 +101,17 @@ cudaError_t mega_setup();
 // last weight tile of the op issued, [4] RMSNorm partial sums formed (the
 // activation loads have landed), [5] RMSNorm scale known, [6] first weight
 // tile ready for the consumers, [7] activation quantized (before the CTA
-// barrier that ends the prologue); entry [n_ops][cta][0] is taken after a final
+// barrier that ends the prologue); attention ops use [3..10] for their phases
+// (see mega_attn); entry [n_ops][cta][0] is taken after a final
 // grid barrier.  Slots a launch does not reach stay as they were.
-constexpr int kTraceSlots = 8;
+constexpr int kTraceSlots = 12;
 cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, const int *done, int *err, int num_sms,
                         cudaStream_t st, unsigned long long *trace = nullptr);
 // Tiles per CTA the producer keeps in flight into L2 beyond its ring.
 int mega_l2_ahead();
 // Host-side validation of a GEMV op for the persistent kernel.
 bool mega_gemv_ok(const MegaGemv &g);
+// Host-side validation of an attention op; max_keys bounds any token's key range.
+bool mega_attn_ok(const MegaAttn &a, int max_keys);
 
 }  // namespace s2k

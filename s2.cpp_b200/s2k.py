@@ -320,15 +320,15 @@ class SlowARModel:
 
     def profile_trace(self, segment: int) -> np.ndarray:
         """Per-op, per-CTA stamps of one persistent-kernel segment launch
-        (s2k_profile_trace): uint64 ns array [n_ops + 1][n_ctas][8]."""
+        (s2k_profile_trace): uint64 ns array [n_ops + 1][n_ctas][12]."""
         if segment < 0:
             segment += self._hp.num_codebooks
         cap = 1 << 20
         buf = (ctypes.c_uint64 * cap)()
         n, g = ctypes.c_int32(0), ctypes.c_int32(0)
         _check(lib().s2k_profile_trace(self._m, self._seq, segment, buf, cap, ctypes.byref(n), ctypes.byref(g)))
-        a = np.frombuffer(buf, dtype=np.uint64, count=(n.value + 1) * g.value * 8).copy()
-        return a.reshape(n.value + 1, g.value, 8)
+        a = np.frombuffer(buf, dtype=np.uint64, count=(n.value + 1) * g.value * 12).copy()
+        return a.reshape(n.value + 1, g.value, 12)
 
     def generate_device(self, d_prompt_tm: int, cols: int, d_codes: int, max_new_tokens: int,
                         temperature: float = 0.0, top_p: float = 0.8, top_k: int = 30,
