@@ -531,13 +531,14 @@ static s2k_status ensure_mat(s2k_model *m, DevMat &dm, int type, int rows, int c
 static s2k_status upload_mat(s2k_model *m, DevMat &dm, int type, const int64_t ne[4], const void *host, size_t nbytes,
                              int64_t expect_in, int64_t expect_out, int dst_rows, int row_stride, int row_offset,
                              const char *name) {
-    if (type != S2K_TYPE_Q8_0)
-        return fail(S2K_ERR_UNSUPPORTED, "%s: ggml type %d not supported by this build (Q8_0 only)", name, type);
+    if (type != S2K_TYPE_Q8_0 && type != S2K_TYPE_Q4_K && type != S2K_TYPE_Q6_K)
+        return fail(S2K_ERR_UNSUPPORTED, "%s: ggml type %d not supported for matrices (Q8_0, Q4_K, Q6_K)", name, type);
     if (ne[0] != expect_in || ne[1] != expect_out)
         return fail(S2K_ERR_ARG, "%s: expected ne [%lld, %lld], got [%lld, %lld]", name, (long long)expect_in,
                     (long long)expect_out, (long long)ne[0], (long long)ne[1]);
     if (ne[0] % 256 != 0) return fail(S2K_ERR_UNSUPPORTED, "%s: row length %lld not a multiple of 256", name, (long long)ne[0]);
-    const size_t row_bytes = (size_t)ne[0] / 32 * 34;
+    const size_t row_bytes = type == S2K_TYPE_Q8_0 ? (size_t)ne[0] / 32 * 34
+                                                  : (size_t)ne[0] / 256 * (type == S2K_TYPE_Q4_K ? 144 : 210);
     if (nbytes != row_bytes * (size_t)ne[1])
         return fail(S2K_ERR_ARG, "%s: %zu bytes, expected %zu", name, nbytes, row_bytes * (size_t)ne[1]);
     s2k_status rc = ensure_mat(m, dm, type, dst_rows, (int)ne[0]);
@@ -552,7 +553,7 @@ static s2k_status upload_mat(s2k_model *m, DevMat &dm, int type, const int64_t n
         const size_t nr = std::min(rows_per, (size_t)ne[1] - r0);
         CU(cudaMemcpyAsync(m->staging, (const uint8_t *)host + r0 * row_bytes, nr * row_bytes, cudaMemcpyHostToDevice,
                            m->stream));
-        CU(launch_relayout_q8_0(m->staging, (int)r0, (int)nr, (int)ne[0], &dm, row_stride, row_offset, m->stream));
+        CU(launch_relayout(m->staging, (int)r0, (int)nr, (int)ne[0], &dm, row_stride, row_offset, m->stream));
         CU(cudaStreamSynchronize(m->stream));
     }
     return S2K_OK;
@@ -981,6 +982,7 @@ static MegaOp mk_gemv(const DevMat &w, const float *x, int ldx, int M, int in_mo
     memset(&o, 0, sizeof(o));
     o.kind = MK_GEMV;
     o.g.w = w.w;
+    o.g.wtype = tw_of(w.type);
     o.g.R = w.rows;
     o.g.K = w.cols;
     o.g.x = x;
@@ -1073,6 +1075,7 @@ static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
         memset(&e, 0, sizeof(e));
         e.kind = MK_EMBED_FAST;
         e.ef.f = m->fast_embed.w;
+        e.ef.ftype = tw_of(m->fast_embed.type);
         e.ef.f_rows = m->fast_embed.rows;
         e.ef.hidden = p == 0 ? m->hidden : nullptr;
         e.ef.codes = s->dev->state.codes;
@@ -1095,6 +1098,8 @@ static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
         memset(&e, 0, sizeof(e));
         e.kind = MK_EMBED_SLOW;
         e.es.e = m->embed.w;
+        e.es.etype = tw_of(m->embed.type);
+        e.es.ctype = hp.num_codebooks > 0 ? tw_of(m->cb_embed.type) : 0;
         e.es.e_rows = m->embed.rows;
         e.es.dim = hp.embedding_length;
         e.es.c = hp.num_codebooks > 0 ? m->cb_embed.w : nullptr;

@@ -22,6 +22,7 @@
 #include "s2k_kernels.h"
 
 #include <algorithm>
+#include <cstdint>
 
 namespace s2k {
 
@@ -34,15 +35,16 @@ struct GemvCfg {
     static constexpr int NS = MT <= 2 ? 9 : (MT <= 4 ? 7 : 5);  // ring stages
 };
 
+constexpr int kPC = 5;  // 8-value activation chunks per consumer thread per prologue pass
+
 template <int MT>
 struct GemvSmem {
     uint8_t ring[GemvCfg<MT>::NS][kTileBytes];
     uint64_t full[GemvCfg<MT>::NS], empty[GemvCfg<MT>::NS];
     int8_t xq[MT * kMaxK];
-    float xd[MT * kMaxK / 32];
-    float nw[kNormMax];
+    float xd[MT * kMaxK / 32];      // Q8_0 block scales, or Q8_K super-block scales
+    int16_t xbs[MT * kMaxK / 16];   // Q8_K block sums
     double tok[kTW][MT];
-    float scale[MT];
     int abort_flag;
 };
 static_assert(sizeof(GemvSmem<8>) <= 227 * 1024, "gemv shared memory");
@@ -58,6 +60,7 @@ __global__ void __launch_bounds__(kThreads, 1) tgemv_kernel(TGemv g, const int *
     long long u0, u1;
     tg_range(g.R, g.K, blockIdx.x, gridDim.x, &u0, &u1);
     const int ntiles = (int)(u1 - u0);
+    const uint32_t tb = (uint32_t)tile_bytes(g.wtype);
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
             mbar_init(&sm.full[i], 1);
@@ -80,14 +83,16 @@ __global__ void __launch_bounds__(kThreads, 1) tgemv_kernel(TGemv g, const int *
                     if (!mbar_wait(&sm.empty[slot], ((t / NS) - 1) & 1, err, ERR_WAIT_EMPTY)) break;
                     if (*reinterpret_cast<volatile int *>(&sm.abort_flag)) break;
                 }
-                mbar_arrive_expect_tx(&sm.full[slot], kTileBytes);
-                bulk_g2s(sm.ring[slot], g.w + (size_t)(u0 + t) * kTileBytes, kTileBytes, &sm.full[slot], pol);
+                mbar_arrive_expect_tx(&sm.full[slot], tb);
+                bulk_g2s(sm.ring[slot], g.w + (size_t)(u0 + t) * tb, tb, &sm.full[slot], pol);
             }
         }
         return;
     }
 
     // ---------------- consumers ----------------
+    F8 nw[kPC];  // norm weights do not depend on the previous kernel: load them before waiting for it
+    tg_norm_preload<kPC, kTNC>(g, nw);
     pdl_wait();
     const bool early = sm.abort_flag == 2;
     if (early || (done != nullptr && *reinterpret_cast<const volatile int *>(done) != 0)) {
@@ -105,16 +110,22 @@ __global__ void __launch_bounds__(kThreads, 1) tgemv_kernel(TGemv g, const int *
     }
     if (ntiles == 0) return;
     // the CTA owning row tile 0 stores act_out
-    tg_prologue<MT, kTNC>(g, sm.xq, sm.xd, sm.nw, &sm.tok[0][0], MT, sm.scale, u0 == 0, 1);
+    tg_prologue8<MT, kTNC, kPC>(g, nw, sm.xq, sm.xd, sm.xbs, &sm.tok[0][0], MT, u0 == 0, 1);
     named_sync(1, kTNC);
     int slot = 0;
     uint32_t phase = 0;
-    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, NS, slot, phase, sm.xq, sm.xd, blockIdx.x, gridDim.x, err);
+    tg_consume_any<MT>(g, &sm.ring[0][0], sm.full, sm.empty, NS, slot, phase, sm.xq, sm.xd, sm.xbs, blockIdx.x,
+                       gridDim.x, err);
+}
+
+int tw_of(int ggml_type) {
+    return ggml_type == 12 ? TW_Q4_K : (ggml_type == 14 ? TW_Q6_K : (ggml_type == 8 ? TW_Q8_0 : -1));
 }
 
 size_t DevMat::bytes() const {
-    if (type == 8) return (size_t)(rows / kTR) * (size_t)(cols / kTK) * kTileBytes;
-    return 0;
+    const int tw = tw_of(type);
+    if (tw < 0) return 0;
+    return (size_t)(rows / kTR) * (size_t)(cols / kTK) * tile_bytes(tw);
 }
 
 cudaError_t gemv_setup() {
@@ -137,6 +148,7 @@ static cudaError_t launch_one(const GemvArgs &a, int m0, int M, int grid, cudaSt
     const DevMat &w = *a.w;
     TGemv g;
     g.w = w.w;
+    g.wtype = tw_of(w.type);
     g.R = w.rows;
     g.K = w.cols;
     g.x = a.x + (size_t)m0 * a.ldx;
@@ -167,7 +179,9 @@ static cudaError_t launch_one(const GemvArgs &a, int m0, int M, int grid, cudaSt
 
 cudaError_t launch_gemv(const GemvArgs &a, int num_sms, cudaStream_t st) {
     const DevMat &w = *a.w;
-    if (w.type != 8 || !w.w) return cudaErrorInvalidValue;
+    if (tw_of(w.type) < 0 || !w.w) return cudaErrorInvalidValue;
+    if (a.ldx % 8 != 0 || reinterpret_cast<uintptr_t>(a.x) % 32 != 0) return cudaErrorInvalidValue;
+    if (a.in_mode == IN_RMSNORM && reinterpret_cast<uintptr_t>(a.norm_w) % 32 != 0) return cudaErrorInvalidValue;
     if (!tg_shape_ok(w.rows, w.cols, std::min(a.M, kMaxMT), a.in_mode, a.epi, a.res != nullptr, kMaxK, kMaxMT))
         return cudaErrorInvalidValue;
     if (a.in_mode == IN_RMSNORM && a.norm_w == nullptr) return cudaErrorInvalidValue;
@@ -217,6 +231,50 @@ cudaError_t launch_relayout_q8_0(const uint8_t *src, int row0, int rows, int col
     const int grid = (int)std::min<long long>((total + block - 1) / block, 148 * 16);
     count_launch();
     relayout_q8_0_kernel<<<grid, block, 0, st>>>(src, row0, rows, cols, dst->w, row_stride, row_offset);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// GGUF Q4_K / Q6_K super-blocks -> tiles
+// ---------------------------------------------------------------------------
+// One thread per source super-block: super-block b of source row r goes to
+// destination row dr = r * row_stride + row_offset, tile (dr / 32, b / 2),
+// super-block slot sb = b % 2 of row dr % 32 (layout in s2k_tgemv.cuh).
+__global__ void relayout_k_kernel(const uint8_t *__restrict__ src, int row0, int rows, int cols, int wtype,
+                                  uint8_t *__restrict__ dst, int row_stride, int row_offset) {
+    const int nsb = cols / 256, nkt = cols / kTK;
+    const int sbb = wtype == TW_Q4_K ? 144 : 210;
+    const long long total = (long long)rows * nsb;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int rr = (int)(i / nsb), b = (int)(i - (long long)rr * nsb);
+        const uint8_t *blk = src + i * sbb;
+        const long long dr = (long long)(row0 + rr) * row_stride + row_offset;
+        uint8_t *tile = dst + ((size_t)(dr / kTR) * nkt + (size_t)(b / 2)) * tile_bytes(wtype);
+        const int rb = (int)(dr % kTR) * 2 + (b & 1);
+        if (wtype == TW_Q4_K) {  // d dmin scales[12] | qs[128]
+            for (int j = 0; j < 16; ++j) tile[kQ4kHdr + rb * 16 + j] = blk[j];
+            for (int j = 0; j < 128; ++j) tile[rb * 128 + j] = blk[16 + j];
+        } else {  // ql[128] qh[64] scales[16] d
+            for (int j = 0; j < 128; ++j) tile[rb * 128 + j] = blk[j];
+            for (int j = 0; j < 64; ++j) tile[kQ6kQh + rb * 64 + j] = blk[128 + j];
+            for (int j = 0; j < 16; ++j) tile[kQ6kSc + rb * 16 + j] = blk[192 + j];
+            tile[kQ6kD + rb * 2] = blk[208];
+            tile[kQ6kD + rb * 2 + 1] = blk[209];
+        }
+    }
+}
+
+cudaError_t launch_relayout(const uint8_t *src, int row0, int rows, int cols, DevMat *dst, int row_stride,
+                            int row_offset, cudaStream_t st) {
+    const int tw = tw_of(dst->type);
+    if (tw == TW_Q8_0) return launch_relayout_q8_0(src, row0, rows, cols, dst, row_stride, row_offset, st);
+    if (tw < 0) return cudaErrorInvalidValue;
+    const long long total = (long long)rows * (cols / 256);
+    const int block = 256;
+    const int grid = (int)std::min<long long>((total + block - 1) / block, 148 * 16);
+    count_launch();
+    relayout_k_kernel<<<grid, block, 0, st>>>(src, row0, rows, cols, tw, dst->w, row_stride, row_offset);
     return cudaGetLastError();
 }
 

@@ -10,9 +10,10 @@
 namespace s2k {
 
 // ---------------------------------------------------------------------------
-// Weight matrix in device layout.
-//   Q8_0 : 32 x 512 tiles of int8 quants + fp16 scales (s2k_tgemv.cuh); rows %
-//          32 == 0 and cols % 512 == 0.
+// Weight matrix in device layout: 32 x 512 tiles (s2k_tgemv.cuh) of
+//   Q8_0 : int8 quants + fp16 scales,
+//   Q4_K / Q6_K : GGUF super-blocks split into quant / scale planes;
+// rows % 32 == 0 and cols % 512 == 0.
 // ---------------------------------------------------------------------------
 struct DevMat {
     int type = -1;  // ggml type id
@@ -49,6 +50,11 @@ cudaError_t gemv_setup();
 // (row_stride 2 interleaves w1/w3).
 cudaError_t launch_relayout_q8_0(const uint8_t *src, int row0, int rows, int cols, DevMat *dst, int row_stride,
                                  int row_offset, cudaStream_t st);
+// Same for any tile type (dst->type: ggml Q8_0, Q4_K or Q6_K blocks in src).
+cudaError_t launch_relayout(const uint8_t *src, int row0, int rows, int cols, DevMat *dst, int row_stride,
+                            int row_offset, cudaStream_t st);
+// Tile-engine weight type (TWType) of a ggml type id, -1 if not a tile type.
+int tw_of(int ggml_type);
 
 // ---------------------------------------------------------------------------
 // Attention

@@ -37,6 +37,7 @@ constexpr int kPtab = 512;                 // cached pages whose ids are staged 
 constexpr int kMPC = 5;                    // 8-value activation chunks per consumer thread per prologue pass
 
 bool mega_gemv_ok(const MegaGemv &g) {
+    if (g.wtype != TW_Q8_0 && g.wtype != TW_Q4_K && g.wtype != TW_Q6_K) return false;
     if (!tg_shape_ok(g.R, g.K, g.M, g.in_mode, g.epi, g.res != nullptr, kMKMax, kMaxT)) return false;
     if (g.in_mode == IN_RMSNORM && g.norm_w == nullptr) return false;
     // one-pass RMSNorm prologue; 32-byte activation and norm-weight loads
@@ -88,7 +89,8 @@ bool mega_attn_ok(const MegaAttn &a, int max_keys) {
 
 struct GemvSm {
     int8_t xq[kMaxT * kMKMax];  // quantized activation
-    float xd[kMaxT * kMKMax / 32];
+    float xd[kMaxT * kMKMax / 32];  // Q8_0 block scales, or Q8_K super-block scales
+    int16_t xbs[kMaxT * kMKMax / 16];  // Q8_K block sums
 };
 
 struct MSmem {
@@ -157,6 +159,7 @@ struct TileCursor {
     int op = -1;
     long long u = 0, u1 = 0;
     const uint8_t *w = nullptr;
+    uint32_t bytes = 0;  // tile size of the current op's weight type
 
     __device__ __forceinline__ const uint8_t *next(const MegaOp *ops, int n_ops, int cta, int G) {
         while (u >= u1) {
@@ -164,8 +167,9 @@ struct TileCursor {
             if (ops[op].kind != MK_GEMV) continue;
             tg_range(ops[op].g.R, ops[op].g.K, cta, G, &u, &u1);
             w = ops[op].g.w;
+            bytes = (uint32_t)tile_bytes(ops[op].g.wtype);
         }
-        return w + (size_t)(u++) * kTileBytes;
+        return w + (size_t)(u++) * bytes;
     }
 };
 
@@ -183,7 +187,7 @@ __device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, 
     const uint8_t *src;
     for (long long ps = 0; (src = ld.next(ops, n_ops, cta, G)) != nullptr; ++ps) {
         for (const uint8_t *p; pf_n < ps + kMStages + l2_ahead && (p = pf.next(ops, n_ops, cta, G)) != nullptr; ++pf_n)
-            bulk_prefetch_l2(p, kTileBytes);
+            bulk_prefetch_l2(p, pf.bytes);
         const int slot = (int)(ps % kMStages);
         // at most `depth` tiles in flight: wait until tile ps - depth has been consumed
         // (depth == kMStages: the slot's previous tile)
@@ -191,8 +195,8 @@ __device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, 
             const long long q = ps - depth;
             if (!mbar_wait(&sm.empty[q % kMStages], (uint32_t)(q / kMStages) & 1u, err, ERR_WAIT_EMPTY)) return;
         }
-        mbar_arrive_expect_tx(&sm.full[slot], kTileBytes);
-        bulk_g2s(sm.ring[slot], src, kTileBytes, &sm.full[slot], pol);
+        mbar_arrive_expect_tx(&sm.full[slot], ld.bytes);
+        bulk_g2s(sm.ring[slot], src, ld.bytes, &sm.full[slot], pol);
         if (trace != nullptr && ld.u == ld.u1) trace[((size_t)ld.op * G + cta) * kTraceSlots + 3] = globaltimer_ns();
     }
 }
@@ -243,11 +247,11 @@ __device__ void mega_gemv(const MegaGemv &gref, const F8 (&nw)[kMPC], MSmem &sm,
     tg_range(g.R, g.K, cta, G, &u0, &u1);
     if (u0 == u1) return;  // no row tile of this op here (R / 32 < G)
     // the CTA owning row tile 0 stores act_out
-    tg_prologue8<MT, kMNC, kMPC>(g, nw, sm.u.g.xq, sm.u.g.xd, &sm.tok[0][0], kMaxT, u0 == 0, 1,
+    tg_prologue8<MT, kMNC, kMPC>(g, nw, sm.u.g.xq, sm.u.g.xd, sm.u.g.xbs, &sm.tok[0][0], kMaxT, u0 == 0, 1,
                                  tr != nullptr ? tr + 4 : nullptr);
     named_sync(1, kMNC);
     if (tr != nullptr && threadIdx.x == 0) tr[1] = globaltimer_ns();
-    tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.u.g.xq, sm.u.g.xd, cta, G, err,
+    tg_consume_any<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.u.g.xq, sm.u.g.xd, sm.u.g.xbs, cta, G, err,
                    tr != nullptr ? tr + 6 : nullptr);
 }
 
@@ -662,7 +666,7 @@ __device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err
             tok = 0;
         }
         const bool sem = tok >= e.sem_begin && tok <= e.sem_end;
-        float x = tq_elem(e.e, e.dim, tok, i);
+        float x = tq_elem(e.e, e.etype, e.dim, tok, i);
         if (sem && e.ncb > 0) {
             float r[kMaxCb];
 #pragma unroll
@@ -674,7 +678,7 @@ __device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err
                         if (i == 0) atomicOr(err, ERR_BAD_TOKEN);
                         id = 0;
                     }
-                    r[cb] = tq_elem(e.c, e.dim, id, i);
+                    r[cb] = tq_elem(e.c, e.ctype, e.dim, id, i);
                 }
             }
             float s = r[0];
@@ -702,7 +706,7 @@ __device__ void mega_embed_fast(const MegaEmbedFast &e, int cta, int G, int *err
                 if (i == 0) atomicOr(err, ERR_BAD_TOKEN);
                 c = 0;
             }
-            x = tq_elem(e.f, e.dim, c, i);
+            x = tq_elem(e.f, e.ftype, e.dim, c, i);
         }
         e.x[(size_t)r * e.dim + i] = x;
     }

@@ -51,10 +51,10 @@ struct MegaAttn {
 };
 
 struct MegaEmbedSlow {
-    const uint8_t *e;  // token embeddings (Q8_0 tiles), [e_rows][dim]
-    int e_rows, dim;
-    const uint8_t *c;  // codebook embeddings (Q8_0 tiles), [c_rows][dim]
-    int c_rows;
+    const uint8_t *e;  // token embeddings (tiles of weight type etype), [e_rows][dim]
+    int etype, e_rows, dim;
+    const uint8_t *c;  // codebook embeddings (tiles of weight type ctype), [c_rows][dim]
+    int ctype, c_rows;
     const int *tokens;  // [T][ncb+1]
     int T, ncb, cb_size, sem_begin, sem_end, scale_cb;
     float sem_scale;
@@ -62,8 +62,8 @@ struct MegaEmbedSlow {
 };
 
 struct MegaEmbedFast {
-    const uint8_t *f;  // fast_embeddings (Q8_0 tiles), [f_rows][dim]
-    int f_rows;
+    const uint8_t *f;  // fast_embeddings (tiles of weight type ftype), [f_rows][dim]
+    int ftype, f_rows;
     const float *hidden;  // null: no hidden row
     const int *codes;
     int code0, n_rows, dim;

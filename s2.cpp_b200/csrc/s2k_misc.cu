@@ -21,8 +21,8 @@
 
 namespace s2k {
 
-__device__ __forceinline__ float deq_q8_0(const DevMat &w, long long row, int col) {
-    return tq_elem(w.w, w.cols, row, col);
+__device__ __forceinline__ float deq_elem(const DevMat &w, long long row, int col) {
+    return tq_elem(w.w, w.type == 12 ? TW_Q4_K : (w.type == 14 ? TW_Q6_K : TW_Q8_0), w.cols, row, col);
 }
 
 // grid T, block 256
@@ -50,10 +50,10 @@ __global__ void embed_slow_kernel(EmbedArgs a, DevMat E, DevMat C) {
         for (int cb = 0; cb < a.ncb; ++cb) ids[cb] = 0;
     }
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-        float e = deq_q8_0(E, tok, i);
+        float e = deq_elem(E, tok, i);
         if (sem && a.ncb > 0) {
-            float s = deq_q8_0(C, ids[0], i);
-            for (int cb = 1; cb < a.ncb; ++cb) s = __fadd_rn(s, deq_q8_0(C, ids[cb], i));
+            float s = deq_elem(C, ids[0], i);
+            for (int cb = 1; cb < a.ncb; ++cb) s = __fadd_rn(s, deq_elem(C, ids[cb], i));
             e = __fadd_rn(e, s);
         }
         if (a.scale_cb && sem) e = __fmul_rn(e, a.sem_scale);
@@ -62,7 +62,8 @@ __global__ void embed_slow_kernel(EmbedArgs a, DevMat E, DevMat C) {
 }
 
 cudaError_t launch_embed_slow(const EmbedArgs &a, cudaStream_t st) {
-    if (a.tok_emb->type != 8 || (a.ncb > 0 && a.cb_emb->type != 8) || a.ncb > 16) return cudaErrorInvalidValue;
+    if (tw_of(a.tok_emb->type) < 0 || (a.ncb > 0 && tw_of(a.cb_emb->type) < 0) || a.ncb > 16)
+        return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.T);
     cfg.blockDim = dim3(256);
@@ -92,12 +93,12 @@ __global__ void embed_fast_kernel(DevMat F, const float *hidden, const int *code
         if (threadIdx.x == 0 && err) atomicOr(err, ERR_BAD_TOKEN);
         c = 0;
     }
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)r * dim + i] = deq_q8_0(F, c, i);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)r * dim + i] = deq_elem(F, c, i);
 }
 
 cudaError_t launch_embed_fast(const DevMat *fast_emb, const float *hidden, const int *codes, int code0, int n_rows,
                               float *x, int dim, const int *done, int *err, cudaStream_t st) {
-    if (fast_emb->type != 8) return cudaErrorInvalidValue;
+    if (tw_of(fast_emb->type) < 0) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_rows);
     cfg.blockDim = dim3(256);

@@ -42,6 +42,26 @@ constexpr int kTNC = kTW * 32;                   // consumer threads
 constexpr int kTRW = kTR / kTW;                  // rows per warp
 constexpr int kNormMax = 4096;                   // longest RMSNorm'd activation row
 
+// K-quant tiles (32 rows x 512 columns = 2 super-blocks of 256 per row):
+//   Q4_K: qs [32][2][128] (nibbles as stored by ggml), then per (row, super-
+//         block) the 16-byte header d, dmin (fp16), 12 packed 6-bit scale/min
+//         bytes: 9216 bytes (144 per super-block, as GGUF).
+//   Q6_K: ql [32][2][128], qh [32][2][64], scales [32][2][16] (int8),
+//         d [32][2] (fp16): 13440 bytes (210 per super-block).
+constexpr int kTileBytesQ4K = kTR * 2 * 144;
+constexpr int kTileBytesQ6K = kTR * 2 * 210;
+constexpr int kQ4kHdr = kTR * 2 * 128;                  // offset of the Q4_K headers
+constexpr int kQ6kQh = kTR * 2 * 128, kQ6kSc = kQ6kQh + kTR * 2 * 64, kQ6kD = kQ6kSc + kTR * 2 * 16;
+static_assert(kTileBytesQ4K <= kTileBytes && kTileBytesQ6K <= kTileBytes, "ring slots hold one tile of any type");
+static_assert(kTileBytesQ4K % 16 == 0 && kTileBytesQ6K % 16 == 0, "bulk copies need 16-byte multiples");
+
+// weight types of the tile engine (TGemv::wtype)
+enum TWType : int { TW_Q8_0 = 0, TW_Q4_K = 1, TW_Q6_K = 2 };
+
+__host__ __device__ constexpr int tile_bytes(int wtype) {
+    return wtype == TW_Q4_K ? kTileBytesQ4K : (wtype == TW_Q6_K ? kTileBytesQ6K : kTileBytes);
+}
+
 static_assert(kTileBytes % 16 == 0, "bulk copies need 16-byte multiples");
 static_assert(kTRW == 4, "the row-tile reduction is written for 4 rows per warp");
 
@@ -57,6 +77,7 @@ enum GemvEpi : int {
 // One GEMV on a tiled Q8_0 matrix (plain data: lives in device op lists).
 struct TGemv {
     const uint8_t *w;  // tiles
+    int wtype;         // TWType
     int R, K;          // R % 32 == 0, K % 512 == 0
     const float *x;    // [M][ldx]
     int ldx, M, in_mode;
@@ -70,11 +91,43 @@ struct TGemv {
     float *act_out;  // optional: CTA 0 stores the (normed) activation [M][K]
 };
 
-// Element (r, c) of a tiled Q8_0 matrix with K columns, dequantized as ggml
-// does (q * d in float).
-__device__ __forceinline__ float tq_elem(const uint8_t *w, int K, long long r, int c) {
-    const uint8_t *t = w + ((size_t)(r / kTR) * (K / kTK) + (size_t)(c / kTK)) * kTileBytes;
+// ggml get_scale_min_k4: 12 bytes hold 8 six-bit scales and 8 six-bit mins
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *q, int *sc, int *mn) {
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *mn = q[j + 4] & 63;
+    } else {
+        *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        *mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+// Element (r, c) of a tiled matrix with K columns, dequantized as ggml's
+// dequantize_row_q8_0 / _q4_K / _q6_K do (float products in the same order).
+__device__ __forceinline__ float tq_elem(const uint8_t *w, int wtype, int K, long long r, int c) {
+    const uint8_t *t = w + ((size_t)(r / kTR) * (K / kTK) + (size_t)(c / kTK)) * tile_bytes(wtype);
     const int rl = (int)(r % kTR), cl = c % kTK;
+    if (wtype == TW_Q4_K) {
+        const int sb = cl >> 8, cc = cl & 255, j = cc >> 5;
+        const uint8_t *hd = t + kQ4kHdr + (rl * 2 + sb) * 16;
+        const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(hd)));
+        const float dmin = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(hd + 2)));
+        int sc, mn;
+        q4k_scale_min(j, hd + 4, &sc, &mn);
+        const uint8_t qb = t[(rl * 2 + sb) * 128 + ((cc >> 6) << 5) + (cc & 31)];
+        const int q = (cc & 32) ? (qb >> 4) : (qb & 0xF);
+        return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)mn));
+    }
+    if (wtype == TW_Q6_K) {
+        const int sb = cl >> 8, cc = cl & 255, h = cc >> 7, k = (cc >> 5) & 3, l = cc & 31;
+        const int rb = rl * 2 + sb;
+        const uint8_t ql = t[rb * 128 + 64 * h + l + ((k & 1) << 5)];
+        const uint8_t qh = t[kQ6kQh + rb * 64 + 32 * h + l];
+        const int q = (((k & 2) ? (ql >> 4) : (ql & 0xF)) | (((qh >> (2 * k)) & 3) << 4)) - 32;
+        const int8_t sc = (int8_t)t[kQ6kSc + rb * 16 + 8 * h + (l >> 4) + 2 * k];
+        const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(t + kQ6kD + rb * 2)));
+        return __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
+    }
     const float q = (float)(int8_t)__ldg(t + rl * kTK + cl);
     const __half d = __ldg(reinterpret_cast<const __half *>(t + kTileQ) + rl * (kTK / 32) + cl / 32);
     return q * __half2float(d);
@@ -85,172 +138,6 @@ __device__ __forceinline__ void tg_range(int R, int K, int cta, int G, long long
     const long long RT = R / kTR, NKT = K / kTK;
     *u0 = (RT * cta / G) * NKT;
     *u1 = (RT * (cta + 1) / G) * NKT;
-}
-
-// One 8-value chunk of an activation row: chunk c of token m covers columns
-// 8*c' .. 8*c'+7 with c' = c % (K/8).  Four consecutive lanes hold the four
-// chunks of one 32-value Q8_0 block.
-struct Chunk8 {
-    float4 a, b;
-};
-
-__device__ __forceinline__ double sumsq8(const Chunk8 &c) {
-    return (double)__fmul_rn(c.a.x, c.a.x) + (double)__fmul_rn(c.a.y, c.a.y) + (double)__fmul_rn(c.a.z, c.a.z) +
-           (double)__fmul_rn(c.a.w, c.a.w) + (double)__fmul_rn(c.b.x, c.b.x) + (double)__fmul_rn(c.b.y, c.b.y) +
-           (double)__fmul_rn(c.b.z, c.b.z) + (double)__fmul_rn(c.b.w, c.b.w);
-}
-
-__device__ __forceinline__ float4 mul4(float4 v, float sc, float4 w) {
-    return make_float4(__fmul_rn(__fmul_rn(v.x, sc), w.x), __fmul_rn(__fmul_rn(v.y, sc), w.y),
-                       __fmul_rn(__fmul_rn(v.z, sc), w.z), __fmul_rn(__fmul_rn(v.w, sc), w.w));
-}
-
-__device__ __forceinline__ int pack4(float4 v, float id) {
-    const int q0 = __float2int_rn(__fmul_rn(v.x, id)), q1 = __float2int_rn(__fmul_rn(v.y, id));
-    const int q2 = __float2int_rn(__fmul_rn(v.z, id)), q3 = __float2int_rn(__fmul_rn(v.w, id));
-    return (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) | ((q3 & 0xff) << 24);
-}
-
-// Quantize the chunk this lane holds (ggml x86 quantize_row_q8_0 on its
-// 32-value block: d = amax/127 stored fp16, q = round-half-even(x * 127/amax));
-// all 32 lanes must call it, valid = this lane holds a chunk.
-__device__ __forceinline__ void quant_chunk(const Chunk8 &c, bool valid, int8_t *xq_chunk, float *xd_blk,
-                                            bool first_of_block) {
-    float amax = fmaxf(fmaxf(fmaxf(fabsf(c.a.x), fabsf(c.a.y)), fmaxf(fabsf(c.a.z), fabsf(c.a.w))),
-                       fmaxf(fmaxf(fabsf(c.b.x), fabsf(c.b.y)), fmaxf(fabsf(c.b.z), fabsf(c.b.w))));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    if (!valid) return;
-    const float d = __fdiv_rn(amax, 127.f);
-    const float id = amax != 0.0f ? __fdiv_rn(127.f, amax) : 0.0f;
-    *reinterpret_cast<int2 *>(xq_chunk) = make_int2(pack4(c.a, id), pack4(c.b, id));
-    if (first_of_block) *xd_blk = __half2float(__float2half_rn(d));
-}
-
-// Prologue (all NT consumer threads): activation rows -> Q8_0 blocks in shared
-// memory (xq [M][K] int8, xd [M][K/32] fp16-rounded scales as float), with the
-// RMSNorm of rms_norm_weighted (src/s2_model.cpp:46-55) when in_mode says so.
-// nws [kNormMax] receives the norm weights; tok [NT/32][tok_ld] (tok_ld >= MT)
-// is small shared scratch.  write_act: this CTA stores act_out (exactly one
-// CTA of the grid should).  The caller synchronizes the consumer threads after
-// it returns.
-// Thread t owns 8-value chunks t, t + NT, ... (CPT of them per pass, all loads
-// of a pass issued before any is used), so the whole CTA quantizes in
-// parallel and a pass costs one L2 round trip.  Every thread derives the
-// RMSNorm scale itself from the per-warp partial sums.
-template <int MT, int NT>
-__device__ __forceinline__ void tg_prologue(const TGemv &g, int8_t *xq, float *xd, float *nws, double *tok,
-                                            int tok_ld, float * /*unused*/, bool write_act, int bar_id,
-                                            unsigned long long *ts = nullptr) {
-    constexpr int CPT = 5;  // chunks per thread per pass
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = g.K, KC = K >> 3, M = g.M;
-    const int nchunks = M * KC;
-    const bool rms = g.in_mode == IN_RMSNORM;
-    const bool resident = nchunks <= CPT * NT;  // all chunks of the op in registers in one pass
-    Chunk8 c[CPT];
-    float sc[MT];
-#pragma unroll
-    for (int m = 0; m < MT; ++m) sc[m] = 1.f;
-    if (resident) {
-#pragma unroll
-        for (int j = 0; j < CPT; ++j) {
-            const int ci = tid + j * NT;
-            if (ci < nchunks) {
-                const int m = ci / KC, off = (ci - m * KC) * 8;
-                const float4 *src = reinterpret_cast<const float4 *>(g.x + (size_t)m * g.ldx + off);
-                c[j].a = __ldcg(src);
-                c[j].b = __ldcg(src + 1);
-            }
-        }
-    }
-    if (rms) {
-        for (int i = tid; i < K / 4; i += NT)
-            reinterpret_cast<float4 *>(nws)[i] = __ldg(reinterpret_cast<const float4 *>(g.norm_w) + i);
-        double tk[MT];
-#pragma unroll
-        for (int m = 0; m < MT; ++m) tk[m] = 0.0;
-        if (resident) {
-#pragma unroll
-            for (int j = 0; j < CPT; ++j) {
-                const int ci = tid + j * NT;
-                if (ci < nchunks) {
-                    const double s = sumsq8(c[j]);
-                    const int m = ci / KC;
-#pragma unroll
-                    for (int mm = 0; mm < MT; ++mm)
-                        if (mm == m) tk[mm] += s;
-                }
-            }
-        } else {
-            for (int ci = tid; ci < nchunks; ci += NT) {
-                const int m = ci / KC, off = (ci - m * KC) * 8;
-                const float4 *src = reinterpret_cast<const float4 *>(g.x + (size_t)m * g.ldx + off);
-                Chunk8 t;
-                t.a = __ldcg(src);
-                t.b = __ldcg(src + 1);
-                const double s = sumsq8(t);
-#pragma unroll
-                for (int mm = 0; mm < MT; ++mm)
-                    if (mm == m) tk[mm] += s;
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-            const double t = warp_sum_d(tk[m]);
-            if (lane == 0) tok[warp * tok_ld + m] = t;
-        }
-        if (ts != nullptr && tid == 0) ts[0] = globaltimer_ns();
-        named_sync(bar_id, NT);  // per-warp sums and norm weights complete
-#pragma unroll
-        for (int m = 0; m < MT; ++m)
-            if (m < M) {
-                double tot = 0.0;
-                for (int w = 0; w < NT / 32; ++w) tot += tok[w * tok_ld + m];
-                const float mean = (float)(tot / (double)K);
-                sc[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, g.eps)));
-            }
-        if (ts != nullptr && tid == 0) ts[1] = globaltimer_ns();
-    }
-    auto finish = [&](Chunk8 &ch, int ci, bool valid) {
-        const int m = valid ? ci / KC : 0, off = valid ? (ci - m * KC) * 8 : 0;
-        if (valid && rms) {
-            float s = sc[0];
-#pragma unroll
-            for (int mm = 1; mm < MT; ++mm)
-                if (mm == m) s = sc[mm];
-            const float4 *nw = reinterpret_cast<const float4 *>(nws + off);
-            ch.a = mul4(ch.a, s, nw[0]);
-            ch.b = mul4(ch.b, s, nw[1]);
-        }
-        if (valid && g.act_out != nullptr && write_act) {
-            float4 *dst = reinterpret_cast<float4 *>(g.act_out + (size_t)m * K + off);
-            dst[0] = ch.a;
-            dst[1] = ch.b;
-        }
-        quant_chunk(ch, valid, xq + (size_t)m * K + off, xd + m * (K >> 5) + (off >> 5), (off & 31) == 0);
-    };
-    if (resident) {
-#pragma unroll
-        for (int j = 0; j < CPT; ++j) {
-            const int ci = tid + j * NT;
-            if (j * NT < nchunks) finish(c[j], ci, ci < nchunks);  // warp-uniform guard: all lanes shuffle
-        }
-    } else {
-        for (int base = 0; base < nchunks; base += NT) {
-            const int ci = base + tid;
-            Chunk8 t;
-            t.a = t.b = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (ci < nchunks) {
-                const int m = ci / KC, off = (ci - m * KC) * 8;
-                const float4 *src = reinterpret_cast<const float4 *>(g.x + (size_t)m * g.ldx + off);
-                t.a = __ldcg(src);
-                t.b = __ldcg(src + 1);
-            }
-            finish(t, ci, ci < nchunks);
-        }
-    }
-    if (ts != nullptr && tid == 0) ts[3] = globaltimer_ns();
 }
 
 // ---------------------------------------------------------------------------
@@ -317,19 +204,79 @@ __device__ __forceinline__ uint32_t pack4_rne(float a, float b, float c, float d
     return __byte_perm(__byte_perm(qa, qb, 0x0040), __byte_perm(qc, qd, 0x0040), 0x5410);
 }
 
+// Q8_K quantization of the 256 values held by the 32 lanes of a warp (8 per
+// lane, lane order = value order), ggml quantize_row_q8_K_ref: the value of
+// largest magnitude (first one on ties) sets iscale = -127 / max,
+// q = min(127, nearest_int(iscale * x)), d = 1 / iscale, bsums of 16 values.
+__device__ __forceinline__ void quant_q8k_warp(const float (&y)[8], int lane, bool store, int8_t *xq8, float *d_out,
+                                               int16_t *bs_out) {
+    float ax = -1.f, mv = 0.f;
+    int mi = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const float a = fabsf(y[e]);
+        if (a > ax) {
+            ax = a;
+            mv = y[e];
+            mi = e;
+        }
+    }
+    int gi = lane * 8 + mi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oax = __shfl_xor_sync(0xffffffffu, ax, o);
+        const float omv = __shfl_xor_sync(0xffffffffu, mv, o);
+        const int ogi = __shfl_xor_sync(0xffffffffu, gi, o);
+        if (oax > ax || (oax == ax && ogi < gi)) {
+            ax = oax;
+            mv = omv;
+            gi = ogi;
+        }
+    }
+    uint32_t w0 = 0, w1 = 0;
+    int qsum = 0;
+    float d = 0.f;
+    if (ax > 0.f) {
+        const float iscale = __fdiv_rn(-127.f, mv);
+        int q[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            q[e] = min(127, __float_as_int(__fadd_rn(__fmul_rn(iscale, y[e]), 12582912.f)) - 0x4B400000);
+            qsum += q[e];
+        }
+        w0 = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+        w1 = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
+        d = __fdiv_rn(1.0f, iscale);
+    }
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+    if (!store) return;
+    *reinterpret_cast<uint2 *>(xq8) = make_uint2(w0, w1);
+    if ((lane & 1) == 0) bs_out[lane >> 1] = (int16_t)qsum;
+    if (lane == 0) *d_out = d;
+}
+
+// Prologue of the tile engine.  Quantizes the [M][K] activation (after the
+// RMSNorm of rms_norm_weighted, src/s2_model.cpp:46-55, when in_mode says so)
+// into shared memory: Q8_0 for Q8_0 weights (xq int8 [M][K], xd [M][K/32]
+// fp16-rounded scales), Q8_K for K-quant weights (xq, xd [M][K/256] float
+// scales, xbs [M][K/16] block sums).  nw holds the norm weights of the
+// thread's pass-0 chunks when the activation fits one pass (tg_norm_preload);
+// otherwise they are loaded here.  tok [NT/32][tok_ld] is shared scratch.
 template <int MT, int NT, int PC>
-__device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC], int8_t *xq, float *xd, double *tok,
-                                             int tok_ld, bool write_act, int bar_id,
+__device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC], int8_t *xq, float *xd, int16_t *xbs,
+                                             double *tok, int tok_ld, bool write_act, int bar_id,
                                              unsigned long long *ts = nullptr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = g.K, KC = K >> 3, M = g.M, nv = M * KC;
     const bool rms = g.in_mode == IN_RMSNORM;
+    const bool q8k = g.wtype != TW_Q8_0;
+    const bool one_pass = nv <= PC * NT;
     float sc[MT];
 #pragma unroll
     for (int m = 0; m < MT; ++m) sc[m] = 1.f;
-    for (int base = 0; base < nv; base += PC * NT) {
-        F8 xv[PC];
-        int mrow[PC];
+    F8 xv[PC];
+    int mrow[PC];
+    auto load_pass = [&](int base) {
 #pragma unroll
         for (int j = 0; j < PC; ++j) {
             const int v = base + tid + j * NT;
@@ -343,13 +290,16 @@ __device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC],
                 for (int e = 0; e < 8; ++e) xv[j].v[e] = 0.f;
             }
         }
-        if (rms) {  // single pass (host check): every element of every row is in xv
-            double tk[MT];
+    };
+    load_pass(0);
+    if (rms) {
+        double tk[MT];
 #pragma unroll
-            for (int m = 0; m < MT; ++m) tk[m] = 0.0;
+        for (int m = 0; m < MT; ++m) tk[m] = 0.0;
+        if (one_pass) {
 #pragma unroll
             for (int j = 0; j < PC; ++j)
-                if (base + tid + j * NT < nv) {
+                if (tid + j * NT < nv) {
                     double s = 0.0;
 #pragma unroll
                     for (int e = 0; e < 8; ++e) s += (double)__fmul_rn(xv[j].v[e], xv[j].v[e]);
@@ -357,27 +307,41 @@ __device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC],
                     for (int m = 0; m < MT; ++m)
                         if (m == mrow[j]) tk[m] += s;
                 }
+        } else {
+            for (int v = tid; v < nv; v += NT) {
+                const int m = tg_row_of(v, KC, M);
+                const F8 x = ld_cg_f8(g.x + (size_t)m * g.ldx + 8 * (v - m * KC));
+                double s = 0.0;
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                const double t = warp_sum_d(tk[m]);
-                if (lane == 0) tok[warp * tok_ld + m] = t;
+                for (int e = 0; e < 8; ++e) s += (double)__fmul_rn(x.v[e], x.v[e]);
+#pragma unroll
+                for (int mm = 0; mm < MT; ++mm)
+                    if (mm == m) tk[mm] += s;
             }
-            if (ts != nullptr && tid == 0) ts[0] = globaltimer_ns();
-            named_sync(bar_id, NT);
-#pragma unroll
-            for (int m = 0; m < MT; ++m)
-                if (m < M) {
-                    double tot = 0.0;
-                    for (int w = 0; w < NT / 32; ++w) tot += tok[w * tok_ld + m];
-                    const float mean = (float)(tot / (double)K);
-                    sc[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, g.eps)));
-                }
-            if (ts != nullptr && tid == 0) ts[1] = globaltimer_ns();
         }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const double t = warp_sum_d(tk[m]);
+            if (lane == 0) tok[warp * tok_ld + m] = t;
+        }
+        if (ts != nullptr && tid == 0) ts[0] = globaltimer_ns();
+        named_sync(bar_id, NT);
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+            if (m < M) {
+                double tot = 0.0;
+                for (int w = 0; w < NT / 32; ++w) tot += tok[w * tok_ld + m];
+                const float mean = (float)(tot / (double)K);
+                sc[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, g.eps)));
+            }
+        if (ts != nullptr && tid == 0) ts[1] = globaltimer_ns();
+    }
+    for (int base = 0; base < nv; base += PC * NT) {
+        if (base > 0) load_pass(base);
 #pragma unroll
         for (int j = 0; j < PC; ++j) {
             const int v = base + tid + j * NT;
-            // 4-lane groups are wholly in or out (nv % 4 == 0): all lanes of a live warp shuffle
+            // 32-chunk warp groups are wholly in or out (nv % 32 == 0 for K % 256 == 0)
             if (base + warp * 32 + j * NT >= nv) continue;
             const bool valid = v < nv;
             F8 y = xv[j];
@@ -386,13 +350,18 @@ __device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC],
 #pragma unroll
                 for (int m = 1; m < MT; ++m)
                     if (m == mrow[j]) s = sc[m];
+                const F8 w = one_pass ? nw[j] : ld_nc_f8(g.norm_w + 8 * (v - mrow[j] * KC));
 #pragma unroll
-                for (int e = 0; e < 8; ++e) y.v[e] = __fmul_rn(__fmul_rn(y.v[e], s), nw[j].v[e]);
+                for (int e = 0; e < 8; ++e) y.v[e] = __fmul_rn(__fmul_rn(y.v[e], s), w.v[e]);
             }
             if (valid && write_act && g.act_out != nullptr) {  // act_out is [M][K] contiguous
                 float4 *dst = reinterpret_cast<float4 *>(g.act_out + 8 * (size_t)v);
                 dst[0] = make_float4(y.v[0], y.v[1], y.v[2], y.v[3]);
                 dst[1] = make_float4(y.v[4], y.v[5], y.v[6], y.v[7]);
+            }
+            if (q8k) {
+                quant_q8k_warp(y.v, lane, valid, xq + 8 * (size_t)v, xd + (v >> 5), xbs + ((v >> 5) << 4));
+                continue;
             }
             float amax = fabsf(y.v[0]);
 #pragma unroll
@@ -534,6 +503,205 @@ __device__ __forceinline__ void tg_consume(const TGemv &g, const uint8_t *ring, 
         for (int m = 0; m < MT; ++m) tot[m] = reduce4_transpose(acc[0][m], acc[1][m], acc[2][m], acc[3][m], lane);
         tg_emit<MT>(g, rt, warp, lane, tot, resv);
     }
+}
+
+// ---------------------------------------------------------------------------
+// K-quant consumers (Q8_K activation: xq int8 [M][K], xd [M][K/256] scales,
+// xbs [M][K/16] block sums).  Lane mapping per warp: row r = lane / 8 of the
+// warp's four rows (lane 8r holds row r after the reduction, as tg_emit
+// expects), s = lane % 8 picks super-block sb = s / 4 of the K-tile and a
+// quarter of its values.  Per super-block the integer sums are exact and the
+// block term is formed as ggml's vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K scale
+// it (d_w * d_x in float), then the terms are summed in double.
+// ---------------------------------------------------------------------------
+template <int MT>
+__device__ __forceinline__ void tg_consume_q4k(const TGemv &g, const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                                               int nst, int &slot, uint32_t &phase, const int8_t *xq,
+                                               const float *xd, const int16_t *xbs, int cta, int G, int *err,
+                                               unsigned long long *t_first = nullptr) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = g.K, NKT = K / kTK, M = g.M, NSB = K >> 8;
+    const int RT = g.R / kTR;
+    const int rt0 = (int)((long long)RT * cta / G), rt1 = (int)((long long)RT * (cta + 1) / G);
+    const int r = lane >> 3, s = lane & 7, sb = s >> 2, c = s & 3;
+    const int row_in_tile = warp * kTRW + r;
+    for (int rt = rt0; rt < rt1; ++rt) {
+        double acc[MT];
+        float resv[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            acc[m] = 0.0;
+            resv[m] = 0.f;
+        }
+        if (g.res != nullptr && s == 0) {
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+                if (m < M) resv[m] = __ldcg(g.res + (size_t)m * g.ldres + (size_t)rt * kTR + row_in_tile);
+        }
+        for (int kt = 0; kt < NKT; ++kt) {
+            const int sbg = kt * 2 + sb;  // super-block of the row
+            int4 xa[MT][4];
+            uint2 bsv[MT];
+            float dx[MT];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const int mm = m < M ? m : 0;
+                const int8_t *xp = xq + (size_t)mm * K + sbg * 256 + 64 * c;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) xa[m][i] = reinterpret_cast<const int4 *>(xp)[i];
+                bsv[m] = *reinterpret_cast<const uint2 *>(xbs + (size_t)mm * (K >> 4) + sbg * 16 + 4 * c);
+                dx[m] = xd[mm * NSB + sbg];
+            }
+            mbar_wait(&full[slot], phase, err, ERR_WAIT_FULL);
+            if (t_first != nullptr && tid == 0 && rt == rt0 && kt == 0) *t_first = globaltimer_ns();
+            const uint8_t *t = ring + (size_t)slot * kTileBytes;
+            const int4 q0 = *reinterpret_cast<const int4 *>(t + (row_in_tile * 2 + sb) * 128 + 32 * c);
+            const int4 q1 = *reinterpret_cast<const int4 *>(t + (row_in_tile * 2 + sb) * 128 + 32 * c + 16);
+            const int4 hd = *reinterpret_cast<const int4 *>(t + kQ4kHdr + (row_in_tile * 2 + sb) * 16);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == nst) {
+                slot = 0;
+                phase ^= 1u;
+            }
+            const uint8_t *scb = reinterpret_cast<const uint8_t *>(&hd) + 4;
+            int sc0, mn0, sc1, mn1;
+            q4k_scale_min(2 * c, scb, &sc0, &mn0);
+            q4k_scale_min(2 * c + 1, scb, &sc1, &mn1);
+            const float dw = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff)));
+            const float dmw = __half2float(__ushort_as_half((unsigned short)((unsigned)hd.x >> 16)));
+            const int qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+                if (m < M) {
+                    const int xw[16] = {xa[m][0].x, xa[m][0].y, xa[m][0].z, xa[m][0].w, xa[m][1].x, xa[m][1].y,
+                                        xa[m][1].z, xa[m][1].w, xa[m][2].x, xa[m][2].y, xa[m][2].z, xa[m][2].w,
+                                        xa[m][3].x, xa[m][3].y, xa[m][3].z, xa[m][3].w};
+                    int slo = 0, shi = 0;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        slo = dp4a(qw[i] & 0x0F0F0F0F, xw[i], slo);
+                        shi = dp4a((qw[i] >> 4) & 0x0F0F0F0F, xw[8 + i], shi);
+                    }
+                    const int b0 = (int)(short)(bsv[m].x & 0xffff), b1 = (int)(short)(bsv[m].x >> 16);
+                    const int b2 = (int)(short)(bsv[m].y & 0xffff), b3 = (int)(short)(bsv[m].y >> 16);
+                    int isum = sc0 * slo + sc1 * shi;
+                    int msum = mn0 * (b0 + b1) + mn1 * (b2 + b3);
+                    isum += __shfl_xor_sync(0xffffffffu, isum, 1);
+                    isum += __shfl_xor_sync(0xffffffffu, isum, 2);
+                    msum += __shfl_xor_sync(0xffffffffu, msum, 1);
+                    msum += __shfl_xor_sync(0xffffffffu, msum, 2);
+                    if (c == 0) {
+                        const double d = (double)__fmul_rn(dw, dx[m]), dmn = (double)__fmul_rn(dmw, dx[m]);
+                        acc[m] += fma(d, (double)isum, -(dmn * (double)msum));
+                    }
+                }
+        }
+        double tot[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) tot[m] = acc[m] + __shfl_xor_sync(0xffffffffu, acc[m], 4);
+        tg_emit<MT>(g, rt, warp, lane, tot, resv);
+    }
+}
+
+template <int MT>
+__device__ __forceinline__ void tg_consume_q6k(const TGemv &g, const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                                               int nst, int &slot, uint32_t &phase, const int8_t *xq,
+                                               const float *xd, int cta, int G, int *err,
+                                               unsigned long long *t_first = nullptr) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = g.K, NKT = K / kTK, M = g.M, NSB = K >> 8;
+    const int RT = g.R / kTR;
+    const int rt0 = (int)((long long)RT * cta / G), rt1 = (int)((long long)RT * (cta + 1) / G);
+    const int r = lane >> 3, s = lane & 7, sb = s >> 2, h = (s >> 1) & 1, is = s & 1;
+    const int row_in_tile = warp * kTRW + r;
+    const int rb = row_in_tile * 2 + sb;
+    for (int rt = rt0; rt < rt1; ++rt) {
+        double acc[MT];
+        float resv[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            acc[m] = 0.0;
+            resv[m] = 0.f;
+        }
+        if (g.res != nullptr && s == 0) {
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+                if (m < M) resv[m] = __ldcg(g.res + (size_t)m * g.ldres + (size_t)rt * kTR + row_in_tile);
+        }
+        for (int kt = 0; kt < NKT; ++kt) {
+            const int sbg = kt * 2 + sb;
+            int4 xa[MT][4];  // values 128h + 32k + 16is .. +16, k = 0..3
+            float dx[MT];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const int mm = m < M ? m : 0;
+                const int8_t *xp = xq + (size_t)mm * K + sbg * 256 + 128 * h + 16 * is;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) xa[m][k] = *reinterpret_cast<const int4 *>(xp + 32 * k);
+                dx[m] = xd[mm * NSB + sbg];
+            }
+            mbar_wait(&full[slot], phase, err, ERR_WAIT_FULL);
+            if (t_first != nullptr && tid == 0 && rt == rt0 && kt == 0) *t_first = globaltimer_ns();
+            const uint8_t *t = ring + (size_t)slot * kTileBytes;
+            const int4 A = *reinterpret_cast<const int4 *>(t + rb * 128 + 64 * h + 16 * is);
+            const int4 B = *reinterpret_cast<const int4 *>(t + rb * 128 + 64 * h + 32 + 16 * is);
+            const int4 Q = *reinterpret_cast<const int4 *>(t + kQ6kQh + rb * 64 + 32 * h + 16 * is);
+            const int8_t *scp = reinterpret_cast<const int8_t *>(t + kQ6kSc + rb * 16 + 8 * h + is);
+            const int sc0 = scp[0], sc1 = scp[2], sc2 = scp[4], sc3 = scp[6];
+            const float dw = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(t + kQ6kD + rb * 2)));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == nst) {
+                slot = 0;
+                phase ^= 1u;
+            }
+            const int aw[4] = {A.x, A.y, A.z, A.w}, bw[4] = {B.x, B.y, B.z, B.w}, qw[4] = {Q.x, Q.y, Q.z, Q.w};
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+                if (m < M) {
+                    const int x0[4] = {xa[m][0].x, xa[m][0].y, xa[m][0].z, xa[m][0].w};
+                    const int x1[4] = {xa[m][1].x, xa[m][1].y, xa[m][1].z, xa[m][1].w};
+                    const int x2[4] = {xa[m][2].x, xa[m][2].y, xa[m][2].z, xa[m][2].w};
+                    const int x3[4] = {xa[m][3].x, xa[m][3].y, xa[m][3].z, xa[m][3].w};
+                    int s1 = 0, s2 = 0, s3 = 0, s4 = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const unsigned a = (unsigned)aw[i], b = (unsigned)bw[i], q = (unsigned)qw[i];
+                        const unsigned v1 = __vsub4((a & 0x0F0F0F0Fu) | ((q & 0x03030303u) << 4), 0x20202020u);
+                        const unsigned v2 = __vsub4((b & 0x0F0F0F0Fu) | (((q >> 2) & 0x03030303u) << 4), 0x20202020u);
+                        const unsigned v3 = __vsub4(((a >> 4) & 0x0F0F0F0Fu) | (((q >> 4) & 0x03030303u) << 4), 0x20202020u);
+                        const unsigned v4 = __vsub4(((b >> 4) & 0x0F0F0F0Fu) | (((q >> 6) & 0x03030303u) << 4), 0x20202020u);
+                        s1 = dp4a((int)v1, x0[i], s1);
+                        s2 = dp4a((int)v2, x1[i], s2);
+                        s3 = dp4a((int)v3, x2[i], s3);
+                        s4 = dp4a((int)v4, x3[i], s4);
+                    }
+                    int isum = sc0 * s1 + sc1 * s2 + sc2 * s3 + sc3 * s4;
+                    isum += __shfl_xor_sync(0xffffffffu, isum, 1);
+                    isum += __shfl_xor_sync(0xffffffffu, isum, 2);
+                    if ((s & 3) == 0) acc[m] += (double)__fmul_rn(dw, dx[m]) * (double)isum;
+                }
+        }
+        double tot[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) tot[m] = acc[m] + __shfl_xor_sync(0xffffffffu, acc[m], 4);
+        tg_emit<MT>(g, rt, warp, lane, tot, resv);
+    }
+}
+
+// The consumer of the op's weight type.
+template <int MT>
+__device__ __forceinline__ void tg_consume_any(const TGemv &g, const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                                               int nst, int &slot, uint32_t &phase, const int8_t *xq,
+                                               const float *xd, const int16_t *xbs, int cta, int G, int *err,
+                                               unsigned long long *t_first = nullptr) {
+    if (g.wtype == TW_Q4_K)
+        tg_consume_q4k<MT>(g, ring, full, empty, nst, slot, phase, xq, xd, xbs, cta, G, err, t_first);
+    else if (g.wtype == TW_Q6_K)
+        tg_consume_q6k<MT>(g, ring, full, empty, nst, slot, phase, xq, xd, cta, G, err, t_first);
+    else
+        tg_consume<MT>(g, ring, full, empty, nst, slot, phase, xq, xd, cta, G, err, t_first);
 }
 
 // Host-side check of a GEMV for the tiled kernels.

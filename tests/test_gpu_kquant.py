@@ -1,0 +1,75 @@
+"""GPU parity for K-quant weights (the mixed Q4_K_M scheme: Q4_K attention /
+FFN-up / embedding tables, Q6_K FFN-down and output projections) against the
+CPU oracle, through the C ABI.  Same bars as the Q8_0 parity tests: logits
+within 1e-2 * std(logits), identical greedy codes."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+import s2k
+import synthetic
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-2
+
+
+def assert_close(got: np.ndarray, want: np.ndarray, what: str) -> None:
+    assert np.isfinite(got).all(), f"{what}: non-finite values"
+    err = float(np.abs(got - want).max())
+    bound = LOGIT_TOL * float(want.std())
+    assert err <= bound, f"{what}: max|delta| {err:.3e} > {bound:.3e}"
+
+
+@pytest.fixture(scope="module")
+def kq_pair():
+    hp = synthetic.preset("small")
+    tensors = list(synthetic.make_model(hp, seed=21, quant="q4_k_m", norm_std=0.1))
+    assert {spec.type for spec, _ in tensors} >= {synthetic.GGML_Q4_K, synthetic.GGML_Q6_K}
+    m = s2k.SlowARModel(hp)
+    m.load_tensors(tensors)
+    om = oracle.OracleModel(hp)
+    om.load_tensors(tensors)
+    yield hp, m, om
+    m.close()
+    om.close()
+
+
+def test_kquant_prefill_steps_fast(kq_pair):
+    hp, m, om = kq_pair
+    p = synthetic.semantic_prompt(hp, 16)
+    m.init_kv_cache(64)
+    om.init_kv_cache(64)
+    hg, lg = m.prefill_fast(p.T.reshape(-1), 16)
+    ho, lo = om.eval(p.T.reshape(-1), 16)
+    assert_close(hg, ho, "kquant prefill hidden")
+    assert_close(lg, lo, "kquant prefill logits")
+    rng = np.random.default_rng(3)
+    for i in range(4):
+        tok = np.zeros(hp.num_codebooks + 1, np.int32)
+        tok[1:] = rng.integers(0, hp.codebook_size, hp.num_codebooks)
+        tok[0] = hp.semantic_begin_id + tok[1] if i % 2 == 0 else rng.integers(0, hp.semantic_begin_id)
+        hg, lg = m.step(tok)
+        ho, lo = om.eval(tok, 1)
+        assert_close(lg, lo, f"kquant step {i} logits")
+    for n in range(hp.num_codebooks):
+        prefix = rng.integers(0, hp.codebook_size, n).astype(np.int32)
+        assert_close(m.fast_decode(ho, prefix), om.fast_decode(ho, prefix), f"kquant fast_decode {n}")
+
+
+def test_kquant_generate_greedy_64(kq_pair):
+    hp, m, om = kq_pair
+    p = synthetic.text_prompt(hp, 20)
+    want = om.generate(p, 64, temperature=0.0, seed=7, im_end_id=-1)
+    got = m.generate(p, 64, temperature=0.0, seed=7, im_end_id=-1)
+    assert got.shape == want.shape == (hp.num_codebooks, 64)
+    assert np.array_equal(got, want)
+
+
+def test_kquant_weight_bytes(kq_pair):
+    """Device bytes equal the GGUF bytes of every matrix (the re-layout keeps 144 / 210 B per super-block)."""
+    hp, m, _ = kq_pair
+    gguf = sum(spec.nbytes for spec in synthetic.tensor_specs(hp, "q4_k_m", 0.1) if spec.ne1 > 1)
+    assert m.weight_bytes() == gguf
