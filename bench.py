@@ -59,15 +59,33 @@ def peaks() -> dict:
     return {"hbm_gbs": 6650.0, "src": "fallback"}
 
 
-def frame_bytes(hp, ctx0: int, frames: int) -> float:
-    """Algorithmic bytes of one step: weights streamed per frame (Slow step +
-    9 Fast-AR passes) + f16 KV read by the Slow step, + the prefill's weights."""
-    q8 = 34 / 32
-    d, ff = hp.embedding_length, hp.feed_forward_length
-    qkv = (hp.head_count + 2 * hp.head_count_kv) * hp.head_dim
-    layer = d * qkv + hp.head_count * hp.head_dim * d + 3 * d * ff
-    slow = (hp.block_count * layer + hp.vocab_size * d) * q8
-    fast = (hp.fast_block_count * layer + hp.codebook_size * d) * q8
+def workload(preset: str, quant: str, prompt: int, frames: int) -> str:
+    if preset != "s2pro":
+        return f"{preset} preset (profiling only)"
+    if quant == "q8_0" and prompt == PROMPT and frames == FRAMES:
+        return WORKLOAD
+    return (f"dual-AR frame loop, S2 Pro shape, {quant}, bs=1: {prompt}-token text prompt prefill + "
+            f"{frames} greedy frames")
+
+
+def weight_stream_bytes(hp, quant: str) -> tuple[float, float]:
+    """GGUF bytes of the matrices one Slow step and one Fast-AR pass stream in
+    full (the embedding tables are gathered row by row and not counted)."""
+    slow = fast = 0.0
+    for spec in synthetic.tensor_specs(hp, quant):
+        if spec.ne1 <= 1 or spec.name in ("codebook_embeddings.weight", "fast_embeddings.weight"):
+            continue
+        if spec.name.startswith("fast_"):
+            fast += spec.nbytes
+        else:
+            slow += spec.nbytes
+    return slow, fast
+
+
+def frame_bytes(hp, ctx0: int, frames: int, quant: str = "q8_0") -> float:
+    """Algorithmic bytes of one step's frames: weights streamed per frame (Slow
+    step + 9 Fast-AR passes) + f16 KV read by the Slow step."""
+    slow, fast = weight_stream_bytes(hp, quant)
     kv_per_pos = hp.block_count * 2 * hp.head_count_kv * hp.head_dim * 2
     total = 0.0
     for f in range(frames):
@@ -114,29 +132,29 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def build_weights(hp, threads: int):
+def build_weights(hp, threads: int, quant: str = "q8_0"):
     synthetic._lib().s2synth_set_threads(threads)
-    return list(synthetic.make_model(hp, seed=SEED, norm_std=0.0))
+    return list(synthetic.make_model(hp, seed=SEED, quant=quant, norm_std=0.0))
 
 
-def cpu_sample(hp, tensors, frames_sample: int) -> dict:
+def cpu_sample(hp, tensors, frames_sample: int, prompt_len: int = PROMPT, frames: int = FRAMES) -> dict:
     """The CPU oracle (C restatement of the reference path) on a bounded sample:
-    the 64-token prefill + `frames_sample` frames, scaled to the 200-frame step."""
+    the prompt prefill + `frames_sample` frames, scaled to the step's frames."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle  # noqa: E402  (cpu_baseline leg only)
     cores = os.cpu_count() or 1
     oracle.set_threads(cores)
     om = oracle.OracleModel(hp)
     om.load_tensors(tensors)
-    prompt = synthetic.text_prompt(hp, PROMPT, seed=7)
+    prompt = synthetic.text_prompt(hp, prompt_len, seed=7)
     _, pre_ms, loop_ms = om.generate_timed(prompt, frames_sample, temperature=0.0, seed=SEED,
                                            min_tokens_before_end=frames_sample)
     om.close()
     per_frame = loop_ms / frames_sample
-    step_s = (pre_ms + FRAMES * per_frame) / 1e3
-    return {"value": FRAMES / step_s, "unit": "frames/s", "cores": cores, "kind": "port",
-            "sample": f"oracle generate: {PROMPT}-token prefill ({pre_ms / 1e3:.1f} s) + {frames_sample} frames "
-                      f"({per_frame / 1e3:.2f} s/frame), scaled to {FRAMES} frames",
+    step_s = (pre_ms + frames * per_frame) / 1e3
+    return {"value": frames / step_s, "unit": "frames/s", "cores": cores, "kind": "port",
+            "sample": f"oracle generate: {prompt_len}-token prefill ({pre_ms / 1e3:.1f} s) + {frames_sample} frames "
+                      f"({per_frame / 1e3:.2f} s/frame), scaled to {frames} frames",
             "prefill_s": pre_ms / 1e3, "s_per_frame": per_frame / 1e3}
 
 
@@ -174,6 +192,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--frames", type=int, default=FRAMES)
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens prefilled before the frames")
+    ap.add_argument("--quant", choices=sorted(synthetic.QUANT_SCHEMES), default="q8_0",
+                    help="weight quantization scheme (q4_k_m: the mixed Q4_K / Q6_K workload)")
     ap.add_argument("--cpu-frames", type=int, default=2, help="frames in the CPU oracle sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--preset", choices=["s2pro", "mid"], default="s2pro",
@@ -200,7 +221,7 @@ def main() -> None:
     hp = synthetic.preset(args.preset)
     threads = max(1, (os.cpu_count() or 8) // max(world, 1))
     t0 = time.time()
-    tensors = build_weights(hp, threads)
+    tensors = build_weights(hp, threads, args.quant)
     t_synth = time.time() - t0
     m = s2k.SlowARModel(hp, device=local)
     m.load_tensors(tensors)
@@ -209,8 +230,9 @@ def main() -> None:
         tensors = None
     frames = args.frames
     utt = shard.utterance_for_rank(rank)  # this rank's utterance
-    prompt = synthetic.text_prompt(hp, PROMPT, seed=utt["prompt_seed"])
-    m.init_kv_cache(PROMPT + frames + 1)  # + 1: the slot the kernel profile below writes
+    P = args.prompt
+    prompt = synthetic.text_prompt(hp, P, seed=utt["prompt_seed"])
+    m.init_kv_cache(P + frames + 1)  # + 1: the slot the kernel profile below writes
     d_prompt = torch.from_numpy(np.ascontiguousarray(prompt.T)).to(f"cuda:{local}")
     d_codes = torch.zeros((hp.num_codebooks, frames), dtype=torch.int32, device=f"cuda:{local}")
     stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
@@ -218,7 +240,7 @@ def main() -> None:
               seq_id=utt["seq_id"])
 
     def step():
-        n = m.generate_device(d_prompt.data_ptr(), PROMPT, d_codes.data_ptr(), frames, **kw)
+        n = m.generate_device(d_prompt.data_ptr(), P, d_codes.data_ptr(), frames, **kw)
         assert n == frames, n
 
     for _ in range(args.warmup):
@@ -265,14 +287,14 @@ def main() -> None:
     achieved = mk_bytes / (mk_ms / 1e3) / 1e9
     # the standalone GEMV kernel of s2k_eval / s2k_fast_decode, for comparison
     gb, gms, glaunch = m.profile_gemv(reps=5)
-    fb = frame_bytes(hp, PROMPT, frames)
+    fb = frame_bytes(hp, P, frames, args.quant)
     step_bytes = fb  # + prefill weights, counted separately below
     frame_achieved = step_bytes / (ms_per_step / 1e3) / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and tensors is not None:
         try:
-            cpu = cpu_sample(hp, tensors, args.cpu_frames)
+            cpu = cpu_sample(hp, tensors, args.cpu_frames, P, frames)
         except Exception as e:  # reported, never fatal
             cpu = {"value": None, "error": str(e)}
 
@@ -280,10 +302,11 @@ def main() -> None:
         line = {
             "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q8_0", "data": "synthetic",
-            "config": {"workload": WORKLOAD if args.preset == "s2pro" else f"{args.preset} preset (profiling only)",
-                       "prompt_tokens": PROMPT, "frames": frames, "batch_per_gpu": 1,
-                       "weights": "seeded N(0,0.02) -> Q8_0", "l2": "inputs larger than L2 (4.3 GB of weights per frame)",
+            "vs_baseline": None, "dtype": args.quant, "data": "synthetic",
+            "config": {"workload": workload(args.preset, args.quant, P, frames),
+                       "prompt_tokens": P, "frames": frames, "batch_per_gpu": 1,
+                       "weights": f"seeded N(0,0.02) -> {args.quant}",
+                       "l2": f"inputs larger than L2 ({weight_stream_bytes(hp, args.quant)[0] / 1e9:.1f} GB of Slow weights per frame)",
                        "parallelism": f"request-level x{world}, no collectives"},
             "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": int(prompt.nbytes),
                     "d2h_bytes_per_step": int(hp.num_codebooks * frames * 4)},

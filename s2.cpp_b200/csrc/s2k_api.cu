@@ -58,7 +58,17 @@ struct Work {
     double *part = nullptr, *part_ms = nullptr;
     int *counters = nullptr;
     int n_split_max = 0;
+    // tensor-core prefill: quantized activation rows, their block scales,
+    // split-K partials and arrival counters (Slow work only)
+    int8_t *pf_xq = nullptr;
+    double *pf_dx = nullptr, *pf_part = nullptr;
+    size_t pf_part_n = 0;
+    int *pf_counters = nullptr;
 };
+
+// Tokens per call from which the Slow stack's Q8_0 GEMMs run on the tensor
+// cores (s2k_prefill.cu) instead of the tile GEMV.
+constexpr int kPrefillMinT = 8;
 
 }  // namespace s2k
 
@@ -74,6 +84,7 @@ struct s2k_model {
     std::vector<Layer> layers, fast_layers;
     std::vector<void *> allocs;
     bool finalized = false;
+    bool prefill_mma = false;  // the tensor-core prefill path could be set up on this device
     int *d_err = nullptr;
     // staging for uploads
     uint8_t *staging = nullptr;
@@ -167,7 +178,9 @@ static s2k_status check_err_word(s2k_model *m) {
 }
 
 // T: tokens per call; L: longest key range (positions) a call attends over.
-static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int Hkv, int hd, int ff) {
+// prefill: the Slow work, whose prompt-sized calls use the tensor-core GEMM.
+static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int Hkv, int hd, int ff,
+                              bool prefill) {
     w.T = T;
     w.L = L;
     w.dim = dim;
@@ -190,12 +203,33 @@ static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int 
     if ((e = m->alloc(&w.part, units * (H / Hkv) * hd))) return e;
     if ((e = m->alloc(&w.part_ms, units * (H / Hkv) * 2))) return e;
     if ((e = m->alloc(&w.counters, tn * Hkv))) return e;
-    return cudaMemset(w.counters, 0, tn * Hkv * sizeof(int));
+    if ((e = cudaMemset(w.counters, 0, tn * Hkv * sizeof(int)))) return e;
+    if (prefill && T >= kPrefillMinT && m->prefill_mma) {
+        const int kmax = std::max(std::max(dim, w.qs), ff);
+        if ((e = m->alloc(&w.pf_xq, tn * kmax))) return e;
+        if ((e = m->alloc(&w.pf_dx, tn * kmax / 32))) return e;
+        // split-K partials of the largest split GEMM (launch_prefill_gemm's rule)
+        const int tt = (T + 63) / 64;
+        const int shapes[4][2] = {{w.qs + 2 * w.kvs, dim}, {dim, w.qs}, {2 * ff, dim}, {dim, ff}};
+        size_t need = 0;
+        for (const auto &rk : shapes) {
+            const int rb = rk[0] / 128, nkt = rk[1] / 512;
+            const int ns = std::min(8, std::min(nkt, std::max(1, m->num_sms / std::max(1, rb * tt))));
+            if (ns > 1) need = std::max(need, (size_t)ns * tn * rk[0]);
+        }
+        w.pf_part_n = need;
+        if (need && (e = m->alloc(&w.pf_part, need))) return e;
+        const size_t nctr = (size_t)(2 * ff / 128 + 1) * tt + 16;
+        if ((e = m->alloc(&w.pf_counters, nctr))) return e;
+        if ((e = cudaMemset(w.pf_counters, 0, nctr * sizeof(int)))) return e;
+    }
+    return cudaSuccess;
 }
 
 static void work_free(s2k_model *m, Work &w) {
     for (void *p : {(void *)w.x, (void *)w.h, (void *)w.qkv, (void *)w.attn, (void *)w.ff_buf, (void *)w.kcur,
-                    (void *)w.vcur, (void *)w.scores, (void *)w.part, (void *)w.part_ms, (void *)w.counters})
+                    (void *)w.vcur, (void *)w.scores, (void *)w.part, (void *)w.part_ms, (void *)w.counters,
+                    (void *)w.pf_xq, (void *)w.pf_dx, (void *)w.pf_part, (void *)w.pf_counters})
         m->release(p);
     w = Work();
 }
@@ -208,7 +242,7 @@ static s2k_status ensure_slow_work(s2k_model *m, int T, int L) {
     m->ws_gen++;
     const s2k_hparams &hp = m->hp;
     CU(work_alloc(m, m->sw, T, L, hp.embedding_length, hp.head_count, hp.head_count_kv, hp.head_dim,
-                  hp.feed_forward_length));
+                  hp.feed_forward_length, true));
     return S2K_OK;
 }
 
@@ -248,6 +282,35 @@ struct StackCall {
     const int *done;
 };
 
+// One stack GEMM: prompt-sized Slow calls on Q8_0 weights go through the
+// tensor cores (activation rows quantized once, then tcgen05 int8 MMAs,
+// s2k_prefill.cu); everything else through the tile GEMV.
+static cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool prefill) {
+    if (prefill && m->prefill_mma && w.pf_xq && g.M >= kPrefillMinT && g.M <= w.T && prefill_ok(*g.w, g.M) &&
+        g.act_out == nullptr) {
+        cudaError_t e = launch_quant_rows_q8(g.x, g.ldx, g.M, g.w->cols, g.in_mode == IN_RMSNORM ? g.norm_w : nullptr,
+                                             g.eps, w.pf_xq, w.pf_dx, nullptr, m->stream);
+        if (e != cudaSuccess) return e;
+        PrefillArgs a;
+        a.w = g.w;
+        a.T = g.M;
+        a.xq = w.pf_xq;
+        a.dx = w.pf_dx;
+        a.epi = g.epi;
+        a.y = g.y;
+        a.ldy = g.ldy;
+        a.res = g.res;
+        a.ldres = g.ldres;
+        a.part = w.pf_part;
+        a.part_doubles = w.pf_part_n;
+        a.counters = w.pf_counters;
+        a.num_sms = m->num_sms;
+        a.err = m->d_err;
+        return launch_prefill_gemm(a, m->stream);
+    }
+    return launch_gemv(g, m->num_sms, m->stream);
+}
+
 static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
     const s2k_hparams &hp = m->hp;
     Work &w = c.fast ? m->fw : m->sw;
@@ -274,7 +337,7 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         g.ldy = qkvs;
         g.done = c.done;
         g.err = m->d_err;
-        if ((e = launch_gemv(g, m->num_sms, st))) return e;
+        if ((e = stack_gemm(m, w, g, !c.fast))) return e;
 
         QkPrepArgs q;
         q.qkv = w.qkv;
@@ -331,7 +394,7 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         o.ldy = dim;
         o.res = w.x;
         o.ldres = dim;
-        if ((e = launch_gemv(o, m->num_sms, st))) return e;
+        if ((e = stack_gemm(m, w, o, !c.fast))) return e;
 
         GemvArgs f1 = g;
         f1.w = &L.w13;
@@ -342,7 +405,7 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         f1.epi = EPI_SWIGLU;
         f1.y = w.ff_buf;
         f1.ldy = w.ff;
-        if ((e = launch_gemv(f1, m->num_sms, st))) return e;
+        if ((e = stack_gemm(m, w, f1, !c.fast))) return e;
 
         GemvArgs f2 = g;
         f2.w = &L.w2;
@@ -354,7 +417,7 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         f2.ldy = dim;
         f2.res = w.h;
         f2.ldres = dim;
-        if ((e = launch_gemv(f2, m->num_sms, st))) return e;
+        if ((e = stack_gemm(m, w, f2, !c.fast))) return e;
     }
     return cudaSuccess;
 }
@@ -737,6 +800,8 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     CU(sampler_setup());
     CU(mega_setup());
     CU(attn_setup());
+    m->prefill_mma = prefill_setup() == cudaSuccess;
+    cudaGetLastError();  // a device without the tensor-map entry point keeps the GEMV path
     if (m->staging) {
         m->release(m->staging);
         m->staging = nullptr;
@@ -758,7 +823,7 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     if (hp.has_fast_decoder) {
         const int Tf = std::max(hp.num_codebooks, 2);
         CU(work_alloc(m, m->fw, Tf, Tf, hp.fast_embedding_length, hp.fast_head_count, hp.fast_head_count_kv,
-                      hp.fast_head_dim, hp.fast_feed_forward_length));
+                      hp.fast_head_dim, hp.fast_feed_forward_length, false));
         const int fkvs = hp.fast_head_count_kv * hp.fast_head_dim;
         m->fkcur.assign(hp.fast_block_count, nullptr);
         m->fvcur.assign(hp.fast_block_count, nullptr);

@@ -57,6 +57,34 @@ cudaError_t launch_relayout(const uint8_t *src, int row0, int rows, int cols, De
 int tw_of(int ggml_type);
 
 // ---------------------------------------------------------------------------
+// Prefill GEMM on the tensor cores (s2k_prefill.cu), Q8_0 weights:
+// y[T][R] (+ res, or SwiGLU of interleaved rows) from activations already
+// quantized by launch_quant_rows_q8.
+// ---------------------------------------------------------------------------
+struct PrefillArgs {
+    const DevMat *w = nullptr;
+    int T = 0;
+    const int8_t *xq = nullptr;  // [T][K] int8
+    const double *dx = nullptr;  // [T][K/32] block scales
+    int epi = EPI_STORE;
+    float *y = nullptr;
+    int ldy = 0;
+    const float *res = nullptr;
+    int ldres = 0;
+    double *part = nullptr;  // split-K partials
+    size_t part_doubles = 0;
+    int *counters = nullptr;  // >= (R/128) * ceil(T/64) ints, zero between launches
+    int num_sms = 148;
+    int *err = nullptr;
+};
+cudaError_t prefill_setup();
+bool prefill_ok(const DevMat &w, int T);
+cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st);
+// x [T][ldx] (optional RMSNorm with norm_w, eps) -> xq [T][K] int8, dx [T][K/32]
+cudaError_t launch_quant_rows_q8(const float *x, int ldx, int T, int K, const float *norm_w, float eps, int8_t *xq,
+                                 double *dx, float *act_out, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
 // Attention
 // ---------------------------------------------------------------------------
 struct KvPaged {

@@ -1,0 +1,28 @@
+"""GPU: the tensor-core prefill GEMM (tcgen05 int8 MMAs with the double-
+precision block-scale epilogue) on prompts of one to three token tiles,
+ragged last tile and split-K partials included, against the CPU oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import s2k
+import synthetic
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("n", [8, 64, 150])
+def test_prefill_mma_matches_oracle(small_model_data, small_oracle, n):
+    hp, tensors = small_model_data
+    m = s2k.SlowARModel(hp)
+    m.load_tensors(tensors)
+    p = synthetic.semantic_prompt(hp, n, seed=n)
+    m.init_kv_cache(n + 4)
+    small_oracle.init_kv_cache(n + 4)
+    hg, lg = m.prefill_fast(p.T.reshape(-1), n)
+    ho, lo = small_oracle.eval(p.T.reshape(-1), n)
+    m.close()
+    for got, want, what in ((hg, ho, "hidden"), (lg, lo, "logits")):
+        err = float(np.abs(got - want).max())
+        assert err <= 1e-2 * float(want.std()), f"{what}: {err}"
