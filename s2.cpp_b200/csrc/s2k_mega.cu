@@ -54,8 +54,8 @@ constexpr int kCombineFast = 8;  // splits the combining unit reads in one round
 
 // Attention unit buffers: the split's keys and values (f16 cache pages of the
 // Slow step, or f32 rows of the Fast-AR), this call's rotated keys/values
-// (Slow), the group's rotated queries as doubles (quarter rows padded to 33
-// so the four quarters of a key read four different banks), the split's
+// (Slow), the group's rotated queries as doubles (quarter rows padded so the
+// four quarters of a key read different banks), the split's
 // scores and exponentials, and the upper-half value partials.
 struct AttnSm {
     union KV {
@@ -66,9 +66,9 @@ struct AttnSm {
     alignas(128) KV v;
     alignas(16) float kc[kMaxT][kHD];
     alignas(16) float vc[kMaxT][kHD];
-    double q[kAG][4][33];
+    alignas(16) double q[kAG][4][34];  // quarter rows padded to 34: 16-byte loads, four banks apart
     float s[kAG][kAttnSplit];
-    double e[kAG][kAttnSplit];
+    alignas(16) double e[kAttnSplit][kAG];  // exponentials, the group's heads side by side
     double o[kAG][kHD];
     float m[kAG];
     double S[kAG];
@@ -180,6 +180,18 @@ struct TileCursor {
 __device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, int G, int l2_ahead, int depth,
                               int *err, unsigned long long *trace) {
     const uint64_t pol = policy_evict_first();
+    if (n_ops > 0 && ops[0].kind == MK_EMBED_SLOW) {
+        // The Slow step's embedding gathers rows the sampler chose an instant
+        // ago (three dependent memory round trips); 25 MB of weight tiles issued
+        // at launch would queue ahead of each of them.  Start the stream once
+        // the consumers have moved on to the first GEMV.
+        const volatile int *cur = &sm.cur_op;
+        const long long t0 = clock64();
+        while (*cur < 1) {
+            if (clock64() - t0 > kWaitLimitCycles) return;  // the consumers stopped (their error is reported)
+            __nanosleep(64);
+        }
+    }
     TileCursor ld, pf;
     long long pf_n = 0;  // tiles the prefetch cursor has passed
     // the first kMStages tiles go straight into the empty ring
@@ -366,7 +378,7 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
         const int ncp = slow ? max(0, min(cnt, nc - j0)) : 0;  // cached keys of the split
         const int npg = (ncp + kPage - 1) / kPage;
         // ---- A. the split's cache pages -> shared memory (bulk copies) ----
-        if (npg > 0 && tid == 0) {
+        if (npg > 0 && tid == kMNC - 32) {  // warp 7 (this call's v of token 1: idle at T = 1) issues the copies
             fence_proxy_async_smem();
             mbar_arrive_expect_tx(&sm.abar, (uint32_t)(2 * npg * kPage * kHD * sizeof(__half)));
             for (int p = 0; p < npg; ++p) {
@@ -387,7 +399,7 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
             const float4 x = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (size_t)t * a.ldqkv + (size_t)h * kHD) + lane);
             const AttnPre pp = u == cta ? pre : attn_preload(a, u);
             const float4 y = head_norm_rope_warp(x, a.q_norm != nullptr, pp.nw, a.eps, pp.cs);
-            double *qd = &as.q[warp][lane >> 3][4 * (lane & 7)];
+            double *qd = &as.q[warp][lane >> 3][4 * (lane & 7)];  // 16-byte aligned: 34-double rows
             qd[0] = (double)y.x;
             qd[1] = (double)y.y;
             qd[2] = (double)y.z;
@@ -460,8 +472,10 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
                             const float2 f = __half22float2(hh[p]);
                             const double k0 = (double)f.x, k1 = (double)f.y;
 #pragma unroll
-                            for (int h = 0; h < kAG; ++h)
-                                acc[h] += k0 * as.q[h][c][8 * qd + 2 * p] + k1 * as.q[h][c][8 * qd + 2 * p + 1];
+                            for (int h = 0; h < kAG; ++h) {
+                                const double2 qq = *reinterpret_cast<const double2 *>(&as.q[h][c][8 * qd + 2 * p]);
+                                acc[h] += k0 * qq.x + k1 * qq.y;
+                            }
                         }
                     }
                 } else {
@@ -470,9 +484,11 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
                     for (int d4 = 0; d4 < 8; ++d4) {
                         const float4 f = reinterpret_cast<const float4 *>(kr)[d4];
 #pragma unroll
-                        for (int h = 0; h < kAG; ++h)
-                            acc[h] += (double)f.x * as.q[h][c][4 * d4] + (double)f.y * as.q[h][c][4 * d4 + 1] +
-                                      (double)f.z * as.q[h][c][4 * d4 + 2] + (double)f.w * as.q[h][c][4 * d4 + 3];
+                        for (int h = 0; h < kAG; ++h) {
+                            const double2 q0 = *reinterpret_cast<const double2 *>(&as.q[h][c][4 * d4]);
+                            const double2 q1 = *reinterpret_cast<const double2 *>(&as.q[h][c][4 * d4 + 2]);
+                            acc[h] += (double)f.x * q0.x + (double)f.y * q0.y + (double)f.z * q1.x + (double)f.w * q1.y;
+                        }
                     }
                 }
             }
@@ -495,8 +511,8 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
             const float mx = warp_max(fmaxf(s0, s1));
             const float e0 = lane < cnt ? det_expf(__fsub_rn(s0, mx)) : 0.f;
             const float e1 = lane + 32 < cnt ? det_expf(__fsub_rn(s1, mx)) : 0.f;
-            as.e[warp][lane] = (double)e0;
-            as.e[warp][lane + 32] = (double)e1;
+            as.e[lane][warp] = (double)e0;
+            as.e[lane + 32][warp] = (double)e1;
             const double S = warp_sum_d((double)e0 + (double)e1);
             if (lane == 0) {
                 as.m[warp] = mx;
@@ -510,12 +526,17 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
         double o[kAG];
 #pragma unroll
         for (int h = 0; h < kAG; ++h) o[h] = 0.0;
+#pragma unroll 4
         for (int jj = kh; jj < cnt; jj += 2) {
             const int j = j0 + jj;
             const double vd = j < nc ? (double)__half2float(as.v.h[jj][d])
                                      : (double)(slow ? as.vc[j - nc][d] : as.v.f[jj][d]);
-#pragma unroll
-            for (int h = 0; h < kAG; ++h) o[h] += vd * as.e[h][jj];
+            const double2 e01 = *reinterpret_cast<const double2 *>(&as.e[jj][0]);
+            const double2 e23 = *reinterpret_cast<const double2 *>(&as.e[jj][2]);
+            o[0] += vd * e01.x;
+            o[1] += vd * e01.y;
+            o[2] += vd * e23.x;
+            o[3] += vd * e23.y;
         }
         if (kh == 1)
 #pragma unroll
@@ -542,14 +563,17 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
             }
             named_sync(3, kMNC);
             if (tid == 0) {
-                __threadfence();
                 mark(u, 10);
-                as.last = atomicAdd(a.counters + t * a.Hkv + g, 1) == nsp - 1;
+                // release: the CTA's partials (ordered before this thread by the CTA
+                // barrier) become visible before the count; acquire: the other
+                // units' partials are visible to this CTA after the next barrier
+                unsigned old;
+                asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + t * a.Hkv + g) : "memory");
+                as.last = (int)old == nsp - 1;
                 mark(u, 3);
             }
             named_sync(3, kMNC);
             if (as.last) {
-                __threadfence();
                 // combine in split order; (m_k, S_k) staged in shared memory in chunks of
                 // kAttnSplit splits (one parallel load each), weights w_k = det_expf(m_k - M)
                 // kept as doubles in as.o; thread (d, kh) sums heads kh, kh + 2
@@ -568,7 +592,7 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
                         const int h = tid / nsp, k = tid - h * nsp;
                         const double2 ms = __ldcg(reinterpret_cast<const double2 *>(a.part_ms + ((pu + k) * grp + h) * 2));
                         as.s[h][k] = (float)ms.x;
-                        as.e[h][k] = ms.y;
+                        as.e[k][h] = ms.y;
                     }
                     named_sync(3, kMNC);
 #pragma unroll
@@ -583,7 +607,7 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
                                 if (k < nsp) {
                                     const double w = (double)det_expf(__fsub_rn(as.s[h][k], M));
                                     acc += ov[x][k] * w;
-                                    S += as.e[h][k] * w;
+                                    S += as.e[k][h] * w;
                                 }
                             a.out[(size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d] = (float)(acc / S);
                         }
@@ -598,7 +622,7 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
                         const int h = p / kn, k = p - h * kn;
                         const double2 ms = __ldcg(reinterpret_cast<const double2 *>(a.part_ms + ((pu + kb + k) * grp + h) * 2));
                         as.s[h][k] = (float)ms.x;
-                        as.e[h][k] = ms.y;
+                        as.e[k][h] = ms.y;
                     }
                     named_sync(3, kMNC);
                 };
@@ -630,7 +654,7 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
 #pragma unroll 8
                             for (int k = 0; k < kn; ++k) {
                                 acc[x] += __ldcg(src + (size_t)k * grp * kHD) * as.o[h][k];
-                                S[x] += as.e[h][k] * as.o[h][k];
+                                S[x] += as.e[k][h] * as.o[h][k];
                             }
                         }
                     }

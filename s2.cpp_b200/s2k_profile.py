@@ -1,0 +1,139 @@
+#!/usr/bin/env python
+"""Profiling entry points of the decode path (B200), for the summaries kept
+with the repository.
+
+  python s2.cpp_b200/s2k_profile.py prefill [--preset s2pro] [--quant q8_0] [--tokens 64,256,1024]
+      CUDA-event time of prefill_fast (the whole Slow stack over a text
+      prompt) and its dense-equivalent GEMM rate.
+
+  python s2.cpp_b200/s2k_profile.py ops [--preset s2pro] [--quant q8_0] [--frames 200]
+      Generates `frames` greedy frames after a 64-token prompt, then traces one
+      Fast-AR pass and the Slow step of the persistent decode kernel
+      (s2k_profile_trace) and prints, per op kind of a layer, the mean span and
+      its parts: grid-barrier release, activation prologue, median / slowest
+      CTA's work; and the attention op's phase stamps.
+
+Seeded synthetic weights (no checkpoints offline).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+import s2k  # noqa: E402
+import synthetic  # noqa: E402
+
+OP_NAMES = ["qkv", "attn", "wo", "w13", "w2"]
+
+
+def _model(preset: str, quant: str):
+    hp = synthetic.preset(preset)
+    synthetic._lib().s2synth_set_threads(os.cpu_count() or 8)
+    m = s2k.SlowARModel(hp)
+    m.load_tensors(synthetic.make_model(hp, seed=1234, quant=quant, norm_std=0.0))
+    return hp, m
+
+
+def cmd_prefill(a) -> None:
+    import torch
+    hp, m = _model(a.preset, a.quant)
+    stream = torch.cuda.ExternalStream(m.stream())
+    d, ff = hp.embedding_length, hp.feed_forward_length
+    qkv = (hp.head_count + 2 * hp.head_count_kv) * hp.head_dim
+    params = hp.block_count * (d * qkv + hp.head_count * hp.head_dim * d + 3 * d * ff)
+    for T in [int(x) for x in a.tokens.split(",")]:
+        p = synthetic.text_prompt(hp, T, seed=5).T.reshape(-1).copy()
+        m.init_kv_cache(T + 8)
+        m.prefill_fast(p, T)
+        best = None
+        for _ in range(3):
+            m.init_kv_cache(T + 8)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            m.prefill_fast(p, T)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        print(json.dumps(dict(preset=a.preset, quant=a.quant, tokens=T, ms=round(best, 3),
+                              gemm_tflops_equiv=round(2 * params * T / (best / 1e3) / 1e12, 1))), flush=True)
+    m.close()
+
+
+def _layer_table(tr: np.ndarray, kinds: np.ndarray) -> dict:
+    T = tr.astype(np.int64)
+    n = T.shape[0] - 1
+    st, pro, dn = T[:, :, 0], T[:, :, 1], T[:, :, 2]
+    t0 = st[0].min()
+    rows = []
+    for i in range(n):
+        prev = dn[i - 1].max() if i > 0 else t0
+        nxt = st[i + 1].min()
+        rows.append(dict(span=(nxt - prev) / 1e3, barrier=(np.median(st[i]) - prev) / 1e3,
+                         prologue=np.median(pro[i] - st[i]) / 1e3, work_med=np.median(dn[i] - pro[i]) / 1e3,
+                         work_max=(dn[i] - pro[i]).max() / 1e3))
+    k = list(kinds)
+    first = k.index(2) - 1
+    nl = (n - first - 1) // 5
+    out = {}
+    for j, name in enumerate(OP_NAMES):
+        sel = [rows[first + 5 * l + j] for l in range(nl)]
+        out[name] = {key: round(float(np.mean([r[key] for r in sel])), 2) for key in sel[0]}
+    out["layers"] = nl
+    out["launch_us"] = round(float((st[n].max() - t0) / 1e3), 1)
+    phases = {}
+    names = {8: "qkv_rotated", 9: "cta_barrier", 4: "kv_in_smem", 5: "scores", 6: "softmax", 7: "values",
+             10: "partials_fenced", 3: "arrival_counted", 2: "done"}
+    for slot, nm in names.items():
+        v = []
+        for i in range(n):
+            if kinds[i] != 2:
+                continue
+            for c in range(T.shape[1]):
+                if T[i, c, 4] > 0 and T[i, c, slot] > 0:
+                    v.append((T[i, c, slot] - T[i, c, 0]) / 1e3)
+        if v:
+            phases[nm] = [round(float(np.median(v)), 2), round(float(np.max(v)), 2)]
+    out["attention_phases_us_median_max"] = phases
+    return out
+
+
+def cmd_ops(a) -> None:
+    hp, m = _model(a.preset, a.quant)
+    prompt = synthetic.text_prompt(hp, 64, seed=7)
+    m.init_kv_cache(64 + a.frames + 1)
+    m.generate(prompt, a.frames, temperature=0.0, min_tokens_before_end=a.frames, im_end_id=-1, seed=1234)
+    ms_s, ms_f, b_s, b_f = m.profile_frame(reps=5)
+    print(json.dumps(dict(ms_slow=round(ms_s, 4), ms_fast=round(ms_f, 4), frame_ms=round(ms_s + 9 * ms_f, 4))))
+    for seg, label in ((1, "fast_ar_pass"), (-1, "slow_step")):
+        tr = m.profile_trace(seg)
+        _, kinds = m.profile_ops(seg, reps=1)
+        print(json.dumps({label: _layer_table(tr, kinds)}), flush=True)
+    m.close()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    p = sub.add_parser("prefill")
+    p.add_argument("--preset", default="s2pro")
+    p.add_argument("--quant", default="q8_0")
+    p.add_argument("--tokens", default="64,256,1024")
+    o = sub.add_parser("ops")
+    o.add_argument("--preset", default="s2pro")
+    o.add_argument("--quant", default="q8_0")
+    o.add_argument("--frames", type=int, default=200)
+    a = ap.parse_args()
+    {"prefill": cmd_prefill, "ops": cmd_ops}[a.cmd](a)
+
+
+if __name__ == "__main__":
+    main()
