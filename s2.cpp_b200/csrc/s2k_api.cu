@@ -58,6 +58,9 @@ struct Work {
     double *part = nullptr, *part_ms = nullptr;
     int *counters = nullptr;
     int n_split_max = 0;
+    // persistent kernel: tagged-word copies of x, h, qkv, attention output and
+    // SwiGLU output (8 bytes per value), written and read only inside it
+    uint64_t *lx = nullptr, *lh = nullptr, *lqkv = nullptr, *lattn = nullptr, *lff = nullptr;
     // tensor-core prefill: quantized activation rows, their block scales,
     // split-K partials and arrival counters (Slow work only)
     int8_t *pf_xq = nullptr;
@@ -86,6 +89,7 @@ struct s2k_model {
     bool finalized = false;
     bool prefill_mma = false;  // the tensor-core prefill path could be set up on this device
     int *d_err = nullptr;
+    unsigned *d_epoch = nullptr;  // tag epoch of the persistent kernel's activations (starts at 1)
     // staging for uploads
     uint8_t *staging = nullptr;
     size_t staging_bytes = 0;
@@ -180,7 +184,7 @@ static s2k_status check_err_word(s2k_model *m) {
 // T: tokens per call; L: longest key range (positions) a call attends over.
 // prefill: the Slow work, whose prompt-sized calls use the tensor-core GEMM.
 static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int Hkv, int hd, int ff,
-                              bool prefill) {
+                              int n_layers, bool prefill) {
     w.T = T;
     w.L = L;
     w.dim = dim;
@@ -202,8 +206,20 @@ static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int 
     const size_t units = tn * Hkv * (size_t)w.n_split_max;
     if ((e = m->alloc(&w.part, units * (H / Hkv) * hd))) return e;
     if ((e = m->alloc(&w.part_ms, units * (H / Hkv) * 2))) return e;
-    if ((e = m->alloc(&w.counters, tn * Hkv))) return e;
-    if ((e = cudaMemset(w.counters, 0, tn * Hkv * sizeof(int)))) return e;
+    // split arrival counters per (layer, token, kv head): no reuse within a launch
+    if ((e = m->alloc(&w.counters, (size_t)n_layers * tn * Hkv))) return e;
+    if ((e = cudaMemset(w.counters, 0, (size_t)n_layers * tn * Hkv * sizeof(int)))) return e;
+    if ((e = m->alloc(&w.lx, tn * dim))) return e;
+    if ((e = m->alloc(&w.lh, tn * dim))) return e;
+    if ((e = m->alloc(&w.lqkv, tn * (w.qs + 2 * w.kvs)))) return e;
+    if ((e = m->alloc(&w.lattn, tn * w.qs))) return e;
+    if ((e = m->alloc(&w.lff, tn * ff))) return e;
+    // tag 0 is never a launch's tag (epochs start at 1)
+    if ((e = cudaMemset(w.lx, 0, tn * dim * 8))) return e;
+    if ((e = cudaMemset(w.lh, 0, tn * dim * 8))) return e;
+    if ((e = cudaMemset(w.lqkv, 0, tn * (w.qs + 2 * w.kvs) * 8))) return e;
+    if ((e = cudaMemset(w.lattn, 0, tn * w.qs * 8))) return e;
+    if ((e = cudaMemset(w.lff, 0, tn * ff * 8))) return e;
     if (prefill && T >= kPrefillMinT && m->prefill_mma) {
         const int kmax = std::max(std::max(dim, w.qs), ff);
         if ((e = m->alloc(&w.pf_xq, tn * kmax))) return e;
@@ -229,7 +245,8 @@ static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int 
 static void work_free(s2k_model *m, Work &w) {
     for (void *p : {(void *)w.x, (void *)w.h, (void *)w.qkv, (void *)w.attn, (void *)w.ff_buf, (void *)w.kcur,
                     (void *)w.vcur, (void *)w.scores, (void *)w.part, (void *)w.part_ms, (void *)w.counters,
-                    (void *)w.pf_xq, (void *)w.pf_dx, (void *)w.pf_part, (void *)w.pf_counters})
+                    (void *)w.pf_xq, (void *)w.pf_dx, (void *)w.pf_part, (void *)w.pf_counters, (void *)w.lx,
+                    (void *)w.lh, (void *)w.lqkv, (void *)w.lattn, (void *)w.lff})
         m->release(p);
     w = Work();
 }
@@ -242,7 +259,7 @@ static s2k_status ensure_slow_work(s2k_model *m, int T, int L) {
     m->ws_gen++;
     const s2k_hparams &hp = m->hp;
     CU(work_alloc(m, m->sw, T, L, hp.embedding_length, hp.head_count, hp.head_count_kv, hp.head_dim,
-                  hp.feed_forward_length, true));
+                  hp.feed_forward_length, hp.block_count, true));
     return S2K_OK;
 }
 
@@ -673,7 +690,10 @@ S2K_API s2k_status s2k_model_create(int32_t device, const s2k_hparams *hp, s2k_m
     }
     m->layers.resize(hp->block_count);
     m->fast_layers.resize(hp->has_fast_decoder ? hp->fast_block_count : 0);
-    if (m->alloc(&m->d_err, 1) != cudaSuccess || cudaMemset(m->d_err, 0, sizeof(int)) != cudaSuccess) {
+    const unsigned epoch1 = 1;
+    if (m->alloc(&m->d_err, 1) != cudaSuccess || cudaMemset(m->d_err, 0, sizeof(int)) != cudaSuccess ||
+        m->alloc(&m->d_epoch, 1) != cudaSuccess ||
+        cudaMemcpy(m->d_epoch, &epoch1, sizeof(unsigned), cudaMemcpyHostToDevice) != cudaSuccess) {
         s2k_model_free(m);
         return fail(S2K_ERR_OOM, "device allocation failed");
     }
@@ -823,7 +843,7 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     if (hp.has_fast_decoder) {
         const int Tf = std::max(hp.num_codebooks, 2);
         CU(work_alloc(m, m->fw, Tf, Tf, hp.fast_embedding_length, hp.fast_head_count, hp.fast_head_count_kv,
-                      hp.fast_head_dim, hp.fast_feed_forward_length, false));
+                      hp.fast_head_dim, hp.fast_feed_forward_length, hp.fast_block_count, false));
         const int fkvs = hp.fast_head_count_kv * hp.fast_head_dim;
         m->fkcur.assign(hp.fast_block_count, nullptr);
         m->fvcur.assign(hp.fast_block_count, nullptr);
@@ -1041,32 +1061,44 @@ S2K_API s2k_status s2k_sample_noalloc(s2k_model *m, const float *logits, int32_t
 // ---------------------------------------------------------------------------
 // persistent-kernel frame program
 // ---------------------------------------------------------------------------
-static MegaOp mk_gemv(const DevMat &w, const float *x, int ldx, int M, int in_mode, const float *nw, float eps,
-                      int epi, float *y, int ldy, const float *res, int ldres, float *act_out) {
+// A GEMV op of the persistent kernel.  ll says which of x / res / y are
+// tagged activation words; the tags are the segment-relative indices of the
+// ops that write them (the kernel adds the launch epoch).
+static MegaOp mk_gemv(const DevMat &w, const void *x, int ldx, int M, int in_mode, const float *nw, float eps,
+                      int epi, void *y, int ldy, const void *res, int ldres, float *act_out, int ll = 0,
+                      int x_tag = 0, int res_tag = 0, int y_tag = 0) {
     MegaOp o;
     memset(&o, 0, sizeof(o));
     o.kind = MK_GEMV;
+    o.g.ll = ll;
+    o.g.x_tag = (uint32_t)x_tag;
+    o.g.res_tag = (uint32_t)res_tag;
+    o.g.y_tag = (uint32_t)y_tag;
     o.g.w = w.w;
     o.g.wtype = tw_of(w.type);
     o.g.R = w.rows;
     o.g.K = w.cols;
-    o.g.x = x;
+    o.g.x = static_cast<const float *>(x);
     o.g.ldx = ldx;
     o.g.M = M;
     o.g.in_mode = in_mode;
     o.g.norm_w = nw;
     o.g.eps = eps;
     o.g.epi = epi;
-    o.g.y = y;
+    o.g.y = static_cast<float *>(y);
     o.g.ldy = ldy;
-    o.g.res = res;
+    o.g.res = static_cast<const float *>(res);
     o.g.ldres = ldres;
     o.g.act_out = act_out;
     return o;
 }
 
 // One transformer stack (a4-a11 of the reference step) as persistent-kernel ops.
-static bool add_layers(s2k_model *m, s2k_seq *s, bool fast, int T, int pos_add, std::vector<MegaOp> &ops) {
+// One transformer stack (a4-a11 of the reference step) as persistent-kernel
+// ops on the tagged activation buffers.  start: the segment's first op;
+// x_op: segment-relative index of the op that last wrote x (updated).
+static bool add_layers(s2k_model *m, s2k_seq *s, bool fast, int T, int pos_add, std::vector<MegaOp> &ops, int start,
+                       int &x_op) {
     const s2k_hparams &hp = m->hp;
     Work &w = fast ? m->fw : m->sw;
     const std::vector<Layer> &layers = fast ? m->fast_layers : m->layers;
@@ -1075,14 +1107,18 @@ static bool add_layers(s2k_model *m, s2k_seq *s, bool fast, int T, int pos_add, 
     const int hd = fast ? hp.fast_head_dim : hp.head_dim;
     const float eps = fast ? hp.fast_rms_norm_eps : hp.rms_norm_eps;
     const int qkvs = w.qs + 2 * w.kvs, dim = w.dim;
+    const size_t tn = (size_t)std::max(w.T, 1);
     for (size_t il = 0; il < layers.size(); ++il) {
         const Layer &L = layers[il];
-        ops.push_back(mk_gemv(L.wqkv, w.x, dim, T, IN_RMSNORM, L.attn_norm, eps, EPI_STORE, w.qkv, qkvs, nullptr, 0,
-                              nullptr));
+        const int q_op = (int)ops.size() - start, a_op = q_op + 1, o_op = q_op + 2, f_op = q_op + 3, d_op = q_op + 4;
+        ops.push_back(mk_gemv(L.wqkv, w.lx, dim, T, IN_RMSNORM, L.attn_norm, eps, EPI_STORE, w.lqkv, qkvs, nullptr, 0,
+                              nullptr, LL_X | LL_Y, x_op, 0, q_op));
         MegaOp a;
         memset(&a, 0, sizeof(a));
         a.kind = MK_ATTN;
-        a.a.qkv = w.qkv;
+        a.a.qkv = w.lqkv;
+        a.a.in_tag = (uint32_t)q_op;
+        a.a.out_tag = (uint32_t)a_op;
         a.a.ldqkv = qkvs;
         a.a.T = T;
         a.a.H = H;
@@ -1110,15 +1146,18 @@ static bool add_layers(s2k_model *m, s2k_seq *s, bool fast, int T, int pos_add, 
         a.a.layer = (int)il;
         a.a.part = w.part;
         a.a.part_ms = w.part_ms;
-        a.a.counters = w.counters;
+        a.a.counters = w.counters + il * tn * Hkv;  // per layer: no counter is reused within a launch
         a.a.n_split_max = w.n_split_max;
-        a.a.out = w.attn;
+        a.a.out = w.lattn;
         if (T * H > w.T * w.H || !mega_attn_ok(a.a, fast ? pos_add + T : s->max_seq_len)) return false;
         ops.push_back(a);
-        ops.push_back(mk_gemv(L.wo, w.attn, w.qs, T, IN_PLAIN, nullptr, eps, EPI_STORE, w.h, dim, w.x, dim, nullptr));
-        ops.push_back(mk_gemv(L.w13, w.h, dim, T, IN_RMSNORM, L.ffn_norm, eps, EPI_SWIGLU, w.ff_buf, w.ff, nullptr, 0,
-                              nullptr));
-        ops.push_back(mk_gemv(L.w2, w.ff_buf, w.ff, T, IN_PLAIN, nullptr, eps, EPI_STORE, w.x, dim, w.h, dim, nullptr));
+        ops.push_back(mk_gemv(L.wo, w.lattn, w.qs, T, IN_PLAIN, nullptr, eps, EPI_STORE, w.lh, dim, w.lx, dim, nullptr,
+                              LL_X | LL_RES | LL_Y, a_op, x_op, o_op));
+        ops.push_back(mk_gemv(L.w13, w.lh, dim, T, IN_RMSNORM, L.ffn_norm, eps, EPI_SWIGLU, w.lff, w.ff, nullptr, 0,
+                              nullptr, LL_X | LL_Y, o_op, 0, f_op));
+        ops.push_back(mk_gemv(L.w2, w.lff, w.ff, T, IN_PLAIN, nullptr, eps, EPI_STORE, w.lx, dim, w.lh, dim, nullptr,
+                              LL_X | LL_RES | LL_Y, f_op, o_op, d_op));
+        x_op = d_op;
     }
     return true;
 }
@@ -1147,12 +1186,14 @@ static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
         e.ef.code0 = p;
         e.ef.n_rows = T;
         e.ef.dim = hp.fast_embedding_length;
-        e.ef.x = m->fw.x;
+        e.ef.x = m->fw.lx;
+        e.ef.tag = 0;
         ops.push_back(e);
-        ok = ok && add_layers(m, s, true, T, pos_add, ops);
-        ops.push_back(mk_gemv(m->fast_out, m->fw.x + (size_t)(T - 1) * hp.fast_embedding_length,
+        int x_op = 0;
+        ok = ok && add_layers(m, s, true, T, pos_add, ops, start, x_op);
+        ops.push_back(mk_gemv(m->fast_out, m->fw.lx + (size_t)(T - 1) * hp.fast_embedding_length,
                               hp.fast_embedding_length, 1, IN_RMSNORM, m->fast_norm, hp.fast_rms_norm_eps, EPI_STORE,
-                              m->flogits, hp.codebook_size, nullptr, 0, nullptr));
+                              m->flogits, hp.codebook_size, nullptr, 0, nullptr, LL_X, x_op));
         s->seg_start.push_back(start);
         s->seg_len.push_back((int)ops.size() - start);
         s->seg_mt.push_back(T);
@@ -1177,11 +1218,13 @@ static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
         e.es.sem_end = hp.semantic_end_id;
         e.es.scale_cb = hp.scale_codebook_embeddings;
         e.es.sem_scale = 1.0f / sqrtf((float)(hp.num_codebooks + 1));
-        e.es.x = m->sw.x;
+        e.es.x = m->sw.lx;
+        e.es.tag = 0;
         ops.push_back(e);
-        ok = ok && add_layers(m, s, false, 1, 0, ops);
-        ops.push_back(mk_gemv(m->embed, m->sw.x, hp.embedding_length, 1, IN_RMSNORM, m->norm, hp.rms_norm_eps,
-                              EPI_STORE, m->logits, hp.vocab_size, nullptr, 0, m->hidden));
+        int x_op = 0;
+        ok = ok && add_layers(m, s, false, 1, 0, ops, start, x_op);
+        ops.push_back(mk_gemv(m->embed, m->sw.lx, hp.embedding_length, 1, IN_RMSNORM, m->norm, hp.rms_norm_eps,
+                              EPI_STORE, m->logits, hp.vocab_size, nullptr, 0, m->hidden, LL_X, x_op));
         MegaOp adv;
         memset(&adv, 0, sizeof(adv));
         adv.kind = MK_ADVANCE;
@@ -1194,6 +1237,8 @@ static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
     }
     for (const MegaOp &o : ops)
         if (o.kind == MK_GEMV && !mega_gemv_ok(o.g)) ok = false;
+    for (size_t i = 0; i < s->seg_len.size(); ++i)
+        if (s->seg_len[i] > 255) ok = false;  // op indices are the low 8 bits of the activation tags
     if (hp.num_codebooks > 16) ok = false;  // the persistent kernel's embedding sums at most 16 codebooks
     s->use_mega = ok;
     if (!ok) return S2K_OK;
@@ -1216,14 +1261,14 @@ static cudaError_t enqueue_frame_mega(s2k_model *m, s2k_seq *s) {
     if ((e = cudaMemsetAsync(s->mega_ctl, 0, sizeof(MegaCtl) * nseg, st))) return e;
     for (int p = 0; p + 1 < hp.num_codebooks; ++p) {
         if ((e = launch_mega(s->mega_ops + s->seg_start[p], s->seg_len[p], s->seg_mt[p], s->mega_ctl + p, done,
-                             m->d_err, m->num_sms, st)))
+                             m->d_err, m->num_sms, st, m->d_epoch)))
             return e;
         if ((e = launch_sample_fast(m->flogits, s->dev, p + 1, m->d_err, st))) return e;
     }
     if ((e = launch_frame_commit(s->dev, st))) return e;
     const int last = nseg - 1;
     if ((e = launch_mega(s->mega_ops + s->seg_start[last], s->seg_len[last], s->seg_mt[last], s->mega_ctl + last, done,
-                         m->d_err, m->num_sms, st)))
+                         m->d_err, m->num_sms, st, m->d_epoch)))
         return e;
     return launch_sample_main(m->logits, s->dev, m->d_err, st);
 }
@@ -1488,13 +1533,13 @@ S2K_API s2k_status s2k_profile_frame(s2k_model *m, s2k_seq *s, int32_t reps, dou
         if ((err = cudaMemsetAsync(cf, 0, sizeof(MegaCtl), m->stream))) break;
         if ((err = cudaEventRecord(ev[4 * r], m->stream))) break;
         if ((err = launch_mega(s->mega_ops + s->seg_start[fseg], s->seg_len[fseg], s->seg_mt[fseg], cf, nullptr,
-                               m->d_err, m->num_sms, m->stream)))
+                               m->d_err, m->num_sms, m->stream, m->d_epoch)))
             break;
         if ((err = cudaEventRecord(ev[4 * r + 1], m->stream))) break;
         if ((err = cudaMemsetAsync(cs, 0, sizeof(MegaCtl), m->stream))) break;
         if ((err = cudaEventRecord(ev[4 * r + 2], m->stream))) break;
         if ((err = launch_mega(s->mega_ops + s->seg_start[sseg], slow_len, s->seg_mt[sseg], cs, nullptr, m->d_err,
-                               m->num_sms, m->stream)))
+                               m->num_sms, m->stream, m->d_epoch)))
             break;
         err = cudaEventRecord(ev[4 * r + 3], m->stream);
     }
@@ -1547,7 +1592,7 @@ static s2k_status trace_segment(s2k_model *m, s2k_seq *s, int segment, int reps,
     for (int r = 0; r < reps && err == cudaSuccess; ++r) {
         if ((err = cudaMemsetAsync(ctl, 0, sizeof(MegaCtl), m->stream))) break;
         err = launch_mega(s->mega_ops + s->seg_start[segment], len, s->seg_mt[segment], ctl, nullptr, m->d_err,
-                          m->num_sms, m->stream, d_tr + (size_t)r * per);
+                          m->num_sms, m->stream, m->d_epoch, d_tr + (size_t)r * per);
     }
     tr.assign((size_t)reps * per, 0ull);
     if (err == cudaSuccess)

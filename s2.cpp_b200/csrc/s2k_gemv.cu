@@ -149,6 +149,8 @@ static cudaError_t launch_one(const GemvArgs &a, int m0, int M, int grid, cudaSt
     TGemv g;
     g.w = w.w;
     g.wtype = tw_of(w.type);
+    g.ll = 0;  // plain float activations
+    g.x_tag = g.res_tag = g.y_tag = 0;
     g.R = w.rows;
     g.K = w.cols;
     g.x = a.x + (size_t)m0 * a.ldx;

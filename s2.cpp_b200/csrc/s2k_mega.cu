@@ -120,34 +120,28 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     return v;
 }
 
-// consumer-only grid barrier halves
-__device__ __forceinline__ void grid_arrive(MegaCtl *ctl, int flags) {
-    named_sync(1, kMNC);
-    if (threadIdx.x == 0) {
-        if (flags & 1) {
-            // release-add: orders this CTA's writes (seen through the named barrier) before the count
-            asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(&ctl->count), "r"(1u) : "memory");
-        } else {
-            __threadfence();
-            atomicAdd(&ctl->count, 1u);
-        }
-    }
-}
-
-__device__ __forceinline__ void grid_wait(MegaCtl *ctl, unsigned target, int *err) {
-    if (threadIdx.x == 0) {
-        if (ld_acquire_u32(&ctl->count) < target &&
-            !(*reinterpret_cast<volatile int *>(err) & (ERR_WAIT_FULL | ERR_WAIT_EMPTY | ERR_GRID))) {
-            const long long t0 = clock64();
-            while (ld_acquire_u32(&ctl->count) < target) {
-                if (clock64() - t0 > kWaitLimitCycles) {
-                    atomicOr(err, ERR_GRID);
-                    break;
-                }
+// 4 tagged activation words at element i of base (32-byte aligned), polled
+// until their tags are current (see ll_load8).
+__device__ __forceinline__ float4 ll_wait4(const void *base, size_t i, uint32_t tag, int *err) {
+    const uint64_t *q = reinterpret_cast<const uint64_t *>(base) + i;
+    uint64_t w0, w1, w2, w3;
+    auto load = [&]() {
+        asm volatile("ld.global.cg.v4.u64 {%0,%1,%2,%3}, [%4];" : "=l"(w0), "=l"(w1), "=l"(w2), "=l"(w3) : "l"(q));
+        return (uint32_t)(w0 >> 32) == tag && (uint32_t)(w1 >> 32) == tag && (uint32_t)(w2 >> 32) == tag &&
+               (uint32_t)(w3 >> 32) == tag;
+    };
+    if (!load()) {
+        const long long t0 = clock64();
+        while (!load()) {
+            if (clock64() - t0 > kWaitLimitCycles || (*reinterpret_cast<volatile int *>(err) & ERR_GRID)) {
+                atomicOr(err, ERR_GRID);
+                break;
             }
+            __nanosleep(32);
         }
     }
-    named_sync(1, kMNC);
+    return make_float4(__uint_as_float((uint32_t)w0), __uint_as_float((uint32_t)w1), __uint_as_float((uint32_t)w2),
+                       __uint_as_float((uint32_t)w3));
 }
 
 // ---------------------------------------------------------------------------
@@ -253,14 +247,17 @@ __device__ void mega_kv_prefetch(const MegaOp *ops, int n_ops, MSmem &sm, int ct
 // ---------------------------------------------------------------------------
 template <int MT>
 __device__ void mega_gemv(const MegaGemv &gref, const F8 (&nw)[kMPC], MSmem &sm, int cta, int G, int &slot,
-                          uint32_t &phase, int *err, unsigned long long *tr) {
-    const MegaGemv g = gref;  // op fields in registers
+                          uint32_t &phase, int *err, unsigned long long *tr, uint32_t ep8) {
+    MegaGemv g = gref;  // op fields in registers; the op list holds producer op indices, the launch its epoch
+    g.x_tag |= ep8;
+    g.res_tag |= ep8;
+    g.y_tag |= ep8;
     long long u0, u1;
     tg_range(g.R, g.K, cta, G, &u0, &u1);
     if (u0 == u1) return;  // no row tile of this op here (R / 32 < G)
     // the CTA owning row tile 0 stores act_out
     tg_prologue8<MT, kMNC, kMPC>(g, nw, sm.u.g.xq, sm.u.g.xd, sm.u.g.xbs, &sm.tok[0][0], kMaxT, u0 == 0, 1,
-                                 tr != nullptr ? tr + 4 : nullptr);
+                                 tr != nullptr ? tr + 4 : nullptr, err);
     named_sync(1, kMNC);
     if (tr != nullptr && threadIdx.x == 0) tr[1] = globaltimer_ns();
     tg_consume_any<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.u.g.xq, sm.u.g.xd, sm.u.g.xbs, cta, G, err,
@@ -348,7 +345,8 @@ __device__ __forceinline__ AttnPre attn_preload(const MegaAttn &a, int u) {
 }
 
 __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int cta, int G, int *err,
-                          unsigned long long *tr, uint32_t &apar) {
+                          unsigned long long *tr, uint32_t &apar, uint32_t ep8) {
+    const uint32_t in_tag = ep8 | a.in_tag, out_tag = ep8 | a.out_tag;
     AttnSm &as = sm.u.a;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int grp = a.H / a.Hkv;
@@ -396,7 +394,7 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
             const int h = g * grp + warp;
             const int pos = pos0 + t;
             if (pos >= a.rope_positions && lane == 0) atomicOr(err, ERR_BAD_POS);
-            const float4 x = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (size_t)t * a.ldqkv + (size_t)h * kHD) + lane);
+            const float4 x = ll_wait4(a.qkv, (size_t)t * a.ldqkv + (size_t)h * kHD + 4 * lane, in_tag, err);
             const AttnPre pp = u == cta ? pre : attn_preload(a, u);
             const float4 y = head_norm_rope_warp(x, a.q_norm != nullptr, pp.nw, a.eps, pp.cs);
             double *qd = &as.q[warp][lane >> 3][4 * (lane & 7)];  // 16-byte aligned: 34-double rows
@@ -408,8 +406,8 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
             const int tt = (warp - 4) >> 1, isv = (warp - 4) & 1;
             if (tt <= t) {
                 const int pos = pos0 + tt;
-                const float *row = a.qkv + (size_t)tt * a.ldqkv + (size_t)(a.H + (isv ? a.Hkv : 0) + g) * kHD;
-                float4 x = __ldcg(reinterpret_cast<const float4 *>(row) + lane);
+                float4 x = ll_wait4(a.qkv, (size_t)tt * a.ldqkv + (size_t)(a.H + (isv ? a.Hkv : 0) + g) * kHD + 4 * lane,
+                                    in_tag, err);
                 if (!isv) {
                     const AttnPre pp = u == cta ? pre : attn_preload(a, u);
                     x = head_norm_rope_warp(x, a.k_norm != nullptr, pp.nw, a.eps, pp.cs);
@@ -550,7 +548,9 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
             if (kh == 0)
 #pragma unroll
                 for (int h = 0; h < kAG; ++h)
-                    if (h < grp) a.out[(size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d] = (float)(o[h] / as.S[h]);
+                    if (h < grp)
+                        ll_store(a.out, (size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d, (float)(o[h] / as.S[h]),
+                                 out_tag);
         } else {
             const size_t pu = ((size_t)t * a.Hkv + g) * a.n_split_max;
             if (kh == 0)
@@ -609,7 +609,8 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
                                     acc += ov[x][k] * w;
                                     S += as.e[k][h] * w;
                                 }
-                            a.out[(size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d] = (float)(acc / S);
+                            ll_store(a.out, (size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d, (float)(acc / S),
+                                     out_tag);
                         }
                     }
                     if (tid == 0) a.counters[t * a.Hkv + g] = 0;
@@ -663,7 +664,9 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
 #pragma unroll
                 for (int x = 0; x < 2; ++x) {
                     const int h = kh + 2 * x;
-                    if (h < grp) a.out[(size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d] = (float)(acc[x] / S[x]);
+                    if (h < grp)
+                        ll_store(a.out, (size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d, (float)(acc[x] / S[x]),
+                                 out_tag);
                 }
                 if (tid == 0) a.counters[t * a.Hkv + g] = 0;
             }
@@ -677,7 +680,7 @@ __device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int 
 // memory round trips; the codebook sum keeps the reference's order cb0..cb9.
 constexpr int kMaxCb = 16;
 
-__device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err) {
+__device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err, uint32_t ep8) {
     const int stride = e.ncb + 1;
     for (long long idx = (long long)cta * kMNC + threadIdx.x; idx < (long long)e.T * e.dim; idx += (long long)G * kMNC) {
         const int t = (int)(idx / e.dim), i = (int)(idx - (long long)t * e.dim);
@@ -712,11 +715,11 @@ __device__ void mega_embed_slow(const MegaEmbedSlow &e, int cta, int G, int *err
             x = __fadd_rn(x, s);
         }
         if (e.scale_cb && sem) x = __fmul_rn(x, e.sem_scale);
-        e.x[(size_t)t * e.dim + i] = x;
+        ll_store(e.x, (size_t)t * e.dim + i, x, ep8 | e.tag);
     }
 }
 
-__device__ void mega_embed_fast(const MegaEmbedFast &e, int cta, int G, int *err) {
+__device__ void mega_embed_fast(const MegaEmbedFast &e, int cta, int G, int *err, uint32_t ep8) {
     const int hrow = e.hidden ? 1 : 0;
     for (long long idx = (long long)cta * kMNC + threadIdx.x; idx < (long long)e.n_rows * e.dim;
          idx += (long long)G * kMNC) {
@@ -732,7 +735,7 @@ __device__ void mega_embed_fast(const MegaEmbedFast &e, int cta, int G, int *err
             }
             x = tq_elem(e.f, e.ftype, e.dim, c, i);
         }
-        e.x[(size_t)r * e.dim + i] = x;
+        ll_store(e.x, (size_t)r * e.dim + i, x, ep8 | e.tag);
     }
 }
 
@@ -741,12 +744,16 @@ __device__ void mega_embed_fast(const MegaEmbedFast &e, int cta, int G, int *err
 template <int MT>
 __global__ void __launch_bounds__(kMThreads, 1)
     mega_kernel(const MegaOp *__restrict__ ops, int n_ops, MegaCtl *ctl, const int *done, int *err, int l2_ahead,
-                unsigned long long *trace, int flags) {
+                unsigned long long *trace, int flags, unsigned *epoch) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     MSmem &sm = *reinterpret_cast<MSmem *>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     if (done != nullptr && __ldcg(done) != 0) return;  // finished sequence: the whole grid exits
+    // Tags of this launch's activations: (epoch << 8) | producing op.  The
+    // epoch only changes when the last CTA of a launch exits, so every CTA of
+    // a launch reads the same value here.
+    const uint32_t ep8 = __ldcg(epoch) << 8;
     if (threadIdx.x == 0) {
         for (int i = 0; i < kMStages; ++i) {
             mbar_init(&sm.full[i], 1);
@@ -781,35 +788,52 @@ __global__ void __launch_bounds__(kMThreads, 1)
         AttnPre ap;
         if (kind == MK_GEMV) tg_norm_preload<kMPC, kMNC>(ops[i].g, nw);
         if (kind == MK_ATTN) ap = attn_preload(ops[i].a, cta);
-        if (i > 0) grid_wait(ctl, (unsigned)(i * G), err);
+        // no grid barrier: each op's readers poll the tags of the words they read
+        named_sync(1, kMNC);  // the previous op's shared buffers are free
         if (threadIdx.x == 0) *reinterpret_cast<volatile int *>(&sm.cur_op) = i;
         stamp(i, 0);
         stamp(i, 1);
         switch (kind) {
         case MK_GEMV:
             mega_gemv<MT>(ops[i].g, nw, sm, cta, G, cslot, cphase, err,
-                          trace != nullptr ? trace + ((size_t)i * G + cta) * kTraceSlots : nullptr);
+                          trace != nullptr ? trace + ((size_t)i * G + cta) * kTraceSlots : nullptr, ep8);
             break;
         case MK_ATTN:
             mega_attn(ops[i].a, ap, sm, cta, G, err,
-                      trace != nullptr ? trace + ((size_t)i * G + cta) * kTraceSlots : nullptr, apar);
+                      trace != nullptr ? trace + ((size_t)i * G + cta) * kTraceSlots : nullptr, apar, ep8);
             break;
-        case MK_EMBED_SLOW: mega_embed_slow(ops[i].es, cta, G, err); break;
-        case MK_EMBED_FAST: mega_embed_fast(ops[i].ef, cta, G, err); break;
+        case MK_EMBED_SLOW: mega_embed_slow(ops[i].es, cta, G, err, ep8); break;
+        case MK_EMBED_FAST: mega_embed_fast(ops[i].ef, cta, G, err, ep8); break;
         case MK_ADVANCE:
-            if (cta == 0 && threadIdx.x == 0) {
-                volatile int *np = ops[i].adv.n_past;
-                *np = *np + ops[i].adv.T;
+            // n_past is read by every attention op of the launch: advance it
+            // only once every CTA has finished all earlier ops (a CTA with no
+            // work in the last ops would get here early)
+            if (threadIdx.x == 0) {
+                __threadfence();
+                atomicAdd(&ctl->pad[0], 1u);
+                if (cta == 0) {
+                    const long long t0 = clock64();
+                    while (ld_acquire_u32(&ctl->pad[0]) < (unsigned)G) {
+                        if (clock64() - t0 > kWaitLimitCycles) {
+                            atomicOr(err, ERR_GRID);
+                            break;
+                        }
+                    }
+                    volatile int *np = ops[i].adv.n_past;
+                    *np = *np + ops[i].adv.T;
+                }
             }
             break;
         default: break;
         }
         stamp(i, 2);
-        grid_arrive(ctl, flags);
     }
-    if (trace != nullptr) {
-        grid_wait(ctl, (unsigned)(n_ops * G), err);
-        stamp(n_ops, 0);
+    stamp(n_ops, 0);
+    // the last CTA to finish moves the epoch on (the next launch's tags)
+    named_sync(1, kMNC);
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&ctl->count, 1u) == (unsigned)G - 1) atomicAdd(epoch, 1u);
     }
 }
 
@@ -830,7 +854,7 @@ cudaError_t mega_setup() {
 }
 
 cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, const int *done, int *err, int num_sms,
-                        cudaStream_t st, unsigned long long *trace) {
+                        cudaStream_t st, unsigned *epoch, unsigned long long *trace) {
     if (mt < 1 || mt > kMaxT) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
@@ -846,8 +870,8 @@ cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, co
     const int ahead = mega_l2_ahead();
     const char *fe = getenv("S2K_MEGA_FLAGS");
     const int flags = fe ? atoi(fe) : 0;
-    if (mt == 1) return cudaLaunchKernelEx(&cfg, mega_kernel<1>, d_ops, n_ops, ctl, done, err, ahead, trace, flags);
-    return cudaLaunchKernelEx(&cfg, mega_kernel<2>, d_ops, n_ops, ctl, done, err, ahead, trace, flags);
+    if (mt == 1) return cudaLaunchKernelEx(&cfg, mega_kernel<1>, d_ops, n_ops, ctl, done, err, ahead, trace, flags, epoch);
+    return cudaLaunchKernelEx(&cfg, mega_kernel<2>, d_ops, n_ops, ctl, done, err, ahead, trace, flags, epoch);
 }
 
 }  // namespace s2k

@@ -25,8 +25,13 @@ enum MegaKind : int {
 
 using MegaGemv = TGemv;  // s2k_tgemv.cuh
 
+// Activations the persistent kernel passes between ops (x, h, qkv, attention
+// output, SwiGLU output) are tagged 8-byte words (s2k_tgemv.cuh ll_pack);
+// the *_tag fields hold the index, within the segment, of the op that writes
+// the words an op reads or writes (the kernel adds the launch epoch).
 struct MegaAttn {
-    float *qkv;  // [T][ldqkv] raw projections
+    void *qkv;   // [T][ldqkv] raw projections (tagged words)
+    uint32_t in_tag, out_tag;
     int ldqkv, T, H, Hkv, hd;
     const float *q_norm, *k_norm;
     float eps, scale;
@@ -47,7 +52,7 @@ struct MegaAttn {
     double *part, *part_ms;
     int *counters;
     int n_split_max;
-    float *out;           // [T][H*hd]
+    void *out;            // [T][H*hd] (tagged words)
 };
 
 struct MegaEmbedSlow {
@@ -58,7 +63,8 @@ struct MegaEmbedSlow {
     const int *tokens;  // [T][ncb+1]
     int T, ncb, cb_size, sem_begin, sem_end, scale_cb;
     float sem_scale;
-    float *x;
+    void *x;  // tagged words
+    uint32_t tag;
 };
 
 struct MegaEmbedFast {
@@ -67,7 +73,8 @@ struct MegaEmbedFast {
     const float *hidden;  // null: no hidden row
     const int *codes;
     int code0, n_rows, dim;
-    float *x;
+    void *x;  // tagged words
+    uint32_t tag;
 };
 
 struct MegaAdvance {
@@ -87,7 +94,9 @@ struct MegaOp {
     };
 };
 
-// Grid-barrier counter of one segment launch (zeroed before the launch).
+// Counters of one segment launch (zeroed before the launch): count = CTAs
+// that finished (the last one advances the model's tag epoch), pad[0] = CTAs
+// that reached the n_past advance.
 struct MegaCtl {
     unsigned int count;
     unsigned int pad[31];
@@ -106,7 +115,7 @@ cudaError_t mega_setup();
 // grid barrier.  Slots a launch does not reach stay as they were.
 constexpr int kTraceSlots = 12;
 cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, const int *done, int *err, int num_sms,
-                        cudaStream_t st, unsigned long long *trace = nullptr);
+                        cudaStream_t st, unsigned *epoch, unsigned long long *trace = nullptr);
 // Tiles per CTA the producer keeps in flight into L2 beyond its ring.
 int mega_l2_ahead();
 // Host-side validation of a GEMV op for the persistent kernel.

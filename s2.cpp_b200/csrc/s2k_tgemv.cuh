@@ -89,7 +89,15 @@ struct TGemv {
     const float *res;  // optional residual [M][ldres]
     int ldres;
     float *act_out;  // optional: CTA 0 stores the (normed) activation [M][K]
+    // Tagged activations (persistent kernel): with LL_X / LL_RES / LL_Y set,
+    // x / res / y are arrays of 8-byte (float value, uint32 tag) words, and a
+    // value counts as written only when its tag equals x_tag / res_tag / y_tag
+    // (see ll_pack); readers poll instead of waiting at a grid barrier.
+    int ll;
+    uint32_t x_tag, res_tag, y_tag;
 };
+
+enum : int { LL_X = 1, LL_RES = 2, LL_Y = 4 };
 
 // ggml get_scale_min_k4: 12 bytes hold 8 six-bit scales and 8 six-bit mins
 __device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *q, int *sc, int *mn) {
@@ -174,6 +182,66 @@ __device__ __forceinline__ F8 ld_nc_f8(const float *p) {
           "=f"(r.v[7])
         : "l"(p));
     return r;
+}
+
+// Tagged activation words: low 32 bits the float value, high 32 bits the tag
+// of the op that wrote it.  An aligned 8-byte store is single-copy atomic, so
+// a reader that sees the expected tag sees the value written with it.
+__device__ __forceinline__ uint64_t ll_pack(float v, uint32_t tag) {
+    return ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+}
+
+__device__ __forceinline__ void ll_store(void *base, size_t i, float v, uint32_t tag) {
+    asm volatile("st.global.u64 [%0], %1;" ::"l"(reinterpret_cast<uint64_t *>(base) + i), "l"(ll_pack(v, tag))
+                 : "memory");
+}
+
+// 8 tagged values at p (32-byte aligned); true when every tag equals `tag`.
+__device__ __forceinline__ bool ll_load8(const void *p, uint32_t tag, F8 &out) {
+    uint64_t w[8];
+    const uint64_t *q = reinterpret_cast<const uint64_t *>(p);
+    asm volatile("ld.global.cg.v4.u64 {%0,%1,%2,%3}, [%4];" : "=l"(w[0]), "=l"(w[1]), "=l"(w[2]), "=l"(w[3]) : "l"(q));
+    asm volatile("ld.global.cg.v4.u64 {%0,%1,%2,%3}, [%4];" : "=l"(w[4]), "=l"(w[5]), "=l"(w[6]), "=l"(w[7]) : "l"(q + 4));
+    bool ok = true;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        out.v[e] = __uint_as_float((uint32_t)w[e]);
+        ok &= (uint32_t)(w[e] >> 32) == tag;
+    }
+    return ok;
+}
+
+// Polls 8 tagged values until their tags are current (bounded: sets
+// ERR_GRID in *err and returns what it has when the producer never comes).
+__device__ __forceinline__ F8 ll_wait8(const void *p, uint32_t tag, int *err) {
+    F8 out;
+    if (ll_load8(p, tag, out)) return out;
+    const long long t0 = clock64();
+    while (!ll_load8(p, tag, out)) {
+        if (clock64() - t0 > kWaitLimitCycles || (err && (*reinterpret_cast<volatile int *>(err) & ERR_GRID))) {
+            if (err) atomicOr(err, ERR_GRID);
+            break;
+        }
+        __nanosleep(32);
+    }
+    return out;
+}
+
+__device__ __forceinline__ float ll_wait1(const void *p, size_t i, uint32_t tag, int *err) {
+    const uint64_t *q = reinterpret_cast<const uint64_t *>(p) + i;
+    uint64_t w = __ldcg(reinterpret_cast<const unsigned long long *>(q));
+    if ((uint32_t)(w >> 32) != tag) {
+        const long long t0 = clock64();
+        do {
+            if (clock64() - t0 > kWaitLimitCycles || (err && (*reinterpret_cast<volatile int *>(err) & ERR_GRID))) {
+                if (err) atomicOr(err, ERR_GRID);
+                break;
+            }
+            __nanosleep(32);
+            w = __ldcg(reinterpret_cast<const unsigned long long *>(q));
+        } while ((uint32_t)(w >> 32) != tag);
+    }
+    return __uint_as_float((uint32_t)w);
 }
 
 __device__ __forceinline__ int tg_row_of(int v, int KC, int M) {
@@ -265,7 +333,7 @@ __device__ __forceinline__ void quant_q8k_warp(const float (&y)[8], int lane, bo
 template <int MT, int NT, int PC>
 __device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC], int8_t *xq, float *xd, int16_t *xbs,
                                              double *tok, int tok_ld, bool write_act, int bar_id,
-                                             unsigned long long *ts = nullptr) {
+                                             unsigned long long *ts = nullptr, int *err = nullptr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = g.K, KC = K >> 3, M = g.M, nv = M * KC;
     const bool rms = g.in_mode == IN_RMSNORM;
@@ -276,19 +344,36 @@ __device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC],
     for (int m = 0; m < MT; ++m) sc[m] = 1.f;
     F8 xv[PC];
     int mrow[PC];
+    const bool llx = (g.ll & LL_X) != 0;
     auto load_pass = [&](int base) {
+        bool ready[PC];
 #pragma unroll
         for (int j = 0; j < PC; ++j) {
             const int v = base + tid + j * NT;
             mrow[j] = 0;
+            ready[j] = true;
             if (v < nv) {
                 const int m = tg_row_of(v, KC, M);
                 mrow[j] = m;
-                xv[j] = ld_cg_f8(g.x + (size_t)m * g.ldx + 8 * (v - m * KC));
+                const size_t off = (size_t)m * g.ldx + 8 * (v - m * KC);
+                if (llx)
+                    ready[j] = ll_load8(reinterpret_cast<const uint64_t *>(g.x) + off, g.x_tag, xv[j]);
+                else
+                    xv[j] = ld_cg_f8(g.x + off);
             } else {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) xv[j].v[e] = 0.f;
             }
+        }
+        if (llx) {  // every load of the pass is in flight before the first retry
+#pragma unroll
+            for (int j = 0; j < PC; ++j)
+                if (!ready[j]) {
+                    const int v = base + tid + j * NT;
+                    xv[j] = ll_wait8(reinterpret_cast<const uint64_t *>(g.x) + (size_t)mrow[j] * g.ldx +
+                                         8 * (v - mrow[j] * KC),
+                                     g.x_tag, err);
+                }
         }
     };
     load_pass(0);
@@ -310,7 +395,9 @@ __device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC],
         } else {
             for (int v = tid; v < nv; v += NT) {
                 const int m = tg_row_of(v, KC, M);
-                const F8 x = ld_cg_f8(g.x + (size_t)m * g.ldx + 8 * (v - m * KC));
+                const size_t off = (size_t)m * g.ldx + 8 * (v - m * KC);
+                const F8 x = llx ? ll_wait8(reinterpret_cast<const uint64_t *>(g.x) + off, g.x_tag, err)
+                                 : ld_cg_f8(g.x + off);
                 double s = 0.0;
 #pragma unroll
                 for (int e = 0; e < 8; ++e) s += (double)__fmul_rn(x.v[e], x.v[e]);
@@ -415,7 +502,14 @@ __device__ __forceinline__ void tg_emit(const TGemv &g, int rt, int warp, int la
 #pragma unroll
             for (int m = 0; m < MT; ++m)
                 if (m < g.M)
-                    g.y[(size_t)m * g.ldy + row0 / 2 + p] = __fmul_rn(silu((float)tot[m]), (float)up[m]);
+                {
+                    const float val = __fmul_rn(silu((float)tot[m]), (float)up[m]);
+                    const size_t yi = (size_t)m * g.ldy + row0 / 2 + p;
+                    if (g.ll & LL_Y)
+                        ll_store(g.y, yi, val, g.y_tag);
+                    else
+                        g.y[yi] = val;
+                }
         }
     } else if ((lane & 7) == 0) {
         const int r = 2 * (lane >> 4) + ((lane >> 3) & 1);
@@ -423,7 +517,12 @@ __device__ __forceinline__ void tg_emit(const TGemv &g, int rt, int warp, int la
         for (int m = 0; m < MT; ++m)
             if (m < g.M) {
                 const float val = (float)tot[m];
-                g.y[(size_t)m * g.ldy + row0 + r] = g.res ? __fadd_rn(resv[m], val) : val;
+                const float outv = g.res ? __fadd_rn(resv[m], val) : val;
+                const size_t yi = (size_t)m * g.ldy + row0 + r;
+                if (g.ll & LL_Y)
+                    ll_store(g.y, yi, outv, g.y_tag);
+                else
+                    g.y[yi] = outv;
             }
     }
 }
@@ -455,7 +554,10 @@ __device__ __forceinline__ void tg_consume(const TGemv &g, const uint8_t *ring, 
             // residual of this lane's output row, needed at the row tile's end
 #pragma unroll
             for (int m = 0; m < MT; ++m)
-                if (m < M) resv[m] = __ldcg(g.res + (size_t)m * g.ldres + (size_t)rt * kTR + rbase + my_row);
+                if (m < M) {
+                    const size_t ri = (size_t)m * g.ldres + (size_t)rt * kTR + rbase + my_row;
+                    resv[m] = (g.ll & LL_RES) ? ll_wait1(g.res, ri, g.res_tag, err) : __ldcg(g.res + ri);
+                }
         }
         const int8_t *xql = xq + lane * 16;
         const float *xdl = xd + (lane >> 1);
@@ -536,7 +638,10 @@ __device__ __forceinline__ void tg_consume_q4k(const TGemv &g, const uint8_t *ri
         if (g.res != nullptr && s == 0) {
 #pragma unroll
             for (int m = 0; m < MT; ++m)
-                if (m < M) resv[m] = __ldcg(g.res + (size_t)m * g.ldres + (size_t)rt * kTR + row_in_tile);
+                if (m < M) {
+                    const size_t ri = (size_t)m * g.ldres + (size_t)rt * kTR + row_in_tile;
+                    resv[m] = (g.ll & LL_RES) ? ll_wait1(g.res, ri, g.res_tag, err) : __ldcg(g.res + ri);
+                }
         }
         for (int kt = 0; kt < NKT; ++kt) {
             const int sbg = kt * 2 + sb;  // super-block of the row
@@ -627,7 +732,10 @@ __device__ __forceinline__ void tg_consume_q6k(const TGemv &g, const uint8_t *ri
         if (g.res != nullptr && s == 0) {
 #pragma unroll
             for (int m = 0; m < MT; ++m)
-                if (m < M) resv[m] = __ldcg(g.res + (size_t)m * g.ldres + (size_t)rt * kTR + row_in_tile);
+                if (m < M) {
+                    const size_t ri = (size_t)m * g.ldres + (size_t)rt * kTR + row_in_tile;
+                    resv[m] = (g.ll & LL_RES) ? ll_wait1(g.res, ri, g.res_tag, err) : __ldcg(g.res + ri);
+                }
         }
         for (int kt = 0; kt < NKT; ++kt) {
             const int sbg = kt * 2 + sb;
