@@ -262,6 +262,64 @@ S2K_API s2k_status s2k_profile_trace(s2k_model *m, s2k_seq *s, int32_t segment, 
 S2K_API s2k_status s2k_debug_copy(s2k_model *m, s2k_seq *s, const char *name, void *host,
                                   size_t nbytes, size_t *copied);
 
+/* ---- Continuous batching (no reference counterpart: the reference runs one
+ * synthesis at a time, src/s2_pipeline.cpp:781,810).  Sequences decode
+ * together one frame per call: every live sequence's Fast-AR passes and Slow
+ * step run as one set of batched kernels, so the weights stream once per
+ * frame for the whole batch.  Batching changes no arithmetic: each
+ * sequence's codes are the ones s2k_generate gives for the same prompt and
+ * parameters (the sampling draws are keyed by seed, frame and seq_id). */
+
+/* Prefill + first main token of s (generate(), src/s2_generate.cpp:37-60),
+ * leaving it ready for s2k_batch_frame.  prompt / cols / gp as s2k_generate;
+ * s must hold cols + max_new_tokens + 1 positions. */
+S2K_API s2k_status s2k_seq_begin(s2k_model *m, s2k_seq *s, const int32_t *prompt, int32_t cols,
+                                 const s2k_gen_params *gp);
+/* One frame (src/s2_generate.cpp:123-182) for each unfinished sequence of
+ * seqs[0..n) (sequences begun with s2k_seq_begin; finished ones are
+ * skipped), as batched kernels.  *n_live (may be NULL) gets the number still
+ * unfinished afterwards. */
+S2K_API s2k_status s2k_batch_frame(s2k_model *m, s2k_seq *const *seqs, int32_t n, int32_t *n_live);
+/* Codes of s so far, cb-major [num_codebooks][*n_frames] (capacity
+ * cap_frames frames; codes_out may be NULL), and whether it finished. */
+S2K_API s2k_status s2k_seq_frames(s2k_seq *s, int32_t *codes_out, int32_t cap_frames, int32_t *n_frames,
+                                  int32_t *done);
+
+/* A continuous-batching scheduler over independent utterances: a FIFO of
+ * requests, up to max_batch live sequences decoded together, and one paged
+ * f16 KV pool (16-token pages, pool_pages of them; 0 = max_batch full-length
+ * sequences) shared by all of them.  A request is admitted when a slot and
+ * the pages for its prompt + max_new_tokens + 1 positions are free, is
+ * prefilled, joins the next batched frame, and leaves the batch (its pages
+ * back in the pool) when it stops (im_end or max_new_tokens). */
+typedef struct s2k_sched s2k_sched;
+enum { S2K_REQ_WAITING = 0, S2K_REQ_LIVE = 1, S2K_REQ_DONE = 2 };
+typedef struct {
+    int64_t steps;           /* batched frames run */
+    int64_t frames;          /* frames produced, all requests */
+    int64_t prefill_tokens;  /* prompt positions prefilled */
+    int64_t admitted, finished;
+    int32_t max_live;        /* largest batch so far */
+    int32_t free_pages, pool_pages;
+} s2k_sched_stats;
+S2K_API s2k_status s2k_sched_create(s2k_model *m, int32_t max_batch, int32_t max_seq_len, int32_t pool_pages,
+                                    s2k_sched **out);
+S2K_API void s2k_sched_free(s2k_sched *sc);
+/* Queue a request (prompt / cols / gp as s2k_generate); *req_id numbers
+ * requests 0, 1, ... in submission order. */
+S2K_API s2k_status s2k_sched_submit(s2k_sched *sc, const int32_t *prompt, int32_t cols, const s2k_gen_params *gp,
+                                    int32_t *req_id);
+/* Admit what fits, run one batched frame over the live requests, retire the
+ * finished ones. */
+S2K_API s2k_status s2k_sched_step(s2k_sched *sc, int32_t *n_live, int32_t *n_waiting);
+/* s2k_sched_step until no request is live or waiting. */
+S2K_API s2k_status s2k_sched_run(s2k_sched *sc);
+S2K_API s2k_status s2k_sched_poll(s2k_sched *sc, int32_t req_id, int32_t *state, int32_t *n_frames);
+/* Codes of a finished request, cb-major [num_codebooks][*n_frames]. */
+S2K_API s2k_status s2k_sched_result(s2k_sched *sc, int32_t req_id, int32_t *codes_out, int32_t cap_frames,
+                                    int32_t *n_frames);
+S2K_API s2k_status s2k_sched_get_stats(const s2k_sched *sc, s2k_sched_stats *out);
+
 /* Counts kernel launches issued by the library since the last reset. */
 S2K_API uint64_t s2k_launch_count(int32_t reset);
 

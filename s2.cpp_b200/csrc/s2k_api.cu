@@ -6,6 +6,7 @@
 #include "s2k_device.h"
 #include "s2k_kernels.h"
 #include "s2k_mega.h"
+#include "s2k_model.h"
 
 #include <algorithm>
 #include <atomic>
@@ -23,8 +24,8 @@ namespace s2k {
 static std::atomic<unsigned long long> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
 
-static thread_local std::string g_err;
-static s2k_status fail(s2k_status code, const char *fmt, ...) {
+thread_local std::string g_err;
+s2k_status fail(s2k_status code, const char *fmt, ...) {
     char buf[512];
     va_list ap;
     va_start(ap, fmt);
@@ -34,143 +35,18 @@ static s2k_status fail(s2k_status code, const char *fmt, ...) {
     return code;
 }
 
-#define CU(expr)                                                                                   \
-    do {                                                                                           \
-        cudaError_t e_ = (expr);                                                                   \
-        if (e_ != cudaSuccess)                                                                     \
-            return fail(e_ == cudaErrorMemoryAllocation ? S2K_ERR_OOM : S2K_ERR_CUDA, "%s: %s (%s:%d)", #expr, \
-                        cudaGetErrorString(e_), __FILE__, __LINE__);                               \
-    } while (0)
-
-struct Layer {
-    float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
-    DevMat wqkv, wo, w13, w2;
-    bool has_w1 = false, has_w3 = false;
-};
-
-// Activations of one transformer stack for up to T tokens.
-struct Work {
-    int T = 0, L = 0, dim = 0, qs = 0, kvs = 0, ff = 0, H = 0;
-    float *x = nullptr, *h = nullptr, *qkv = nullptr, *attn = nullptr, *ff_buf = nullptr;
-    float *kcur = nullptr, *vcur = nullptr, *scores = nullptr;
-    // persistent-kernel attention: per (token, kv head, split) the split's
-    // O_i [G][hd] and (m_i, S_i) [G][2]; arrival counters per (token, kv head)
-    double *part = nullptr, *part_ms = nullptr;
-    int *counters = nullptr;
-    int n_split_max = 0;
-    // persistent kernel: tagged-word copies of x, h, qkv, attention output and
-    // SwiGLU output (8 bytes per value), written and read only inside it
-    uint64_t *lx = nullptr, *lh = nullptr, *lqkv = nullptr, *lattn = nullptr, *lff = nullptr;
-    // tensor-core prefill: quantized activation rows, their block scales,
-    // split-K partials and arrival counters (Slow work only)
-    int8_t *pf_xq = nullptr;
-    double *pf_dx = nullptr, *pf_part = nullptr;
-    size_t pf_part_n = 0;
-    int *pf_counters = nullptr;
-};
-
-// Tokens per call from which the Slow stack's Q8_0 GEMMs run on the tensor
-// cores (s2k_prefill.cu) instead of the tile GEMV.
-constexpr int kPrefillMinT = 8;
 
 }  // namespace s2k
 
 using namespace s2k;
 
-struct s2k_model {
-    s2k_hparams hp{};
-    int device = 0;
-    int num_sms = 148;
-    cudaStream_t stream = nullptr;
-    DevMat embed, cb_embed, fast_embed, fast_out;
-    float *norm = nullptr, *fast_norm = nullptr;
-    std::vector<Layer> layers, fast_layers;
-    std::vector<void *> allocs;
-    bool finalized = false;
-    bool prefill_mma = false;  // the tensor-core prefill path could be set up on this device
-    int *d_err = nullptr;
-    unsigned *d_epoch = nullptr;  // tag epoch of the persistent kernel's activations (starts at 1)
-    // staging for uploads
-    uint8_t *staging = nullptr;
-    size_t staging_bytes = 0;
-    // Slow workspace (ws_gen changes whenever it is reallocated: captured
-    // frame graphs hold its pointers)
-    Work sw;
-    int ws_gen = 0;
-    float *logits = nullptr, *hidden = nullptr;
-    int *tokens = nullptr;
-    int tokens_cap = 0;
-    // Fast workspace (T <= num_codebooks)
-    Work fw;
-    std::vector<float *> fkcur, fvcur;
-    float *flogits = nullptr, *fhidden = nullptr;
-    int *fcodes = nullptr;
-    // RoPE cos/sin tables [positions][head_dim/2]
-    float2 *rope_slow = nullptr, *rope_fast = nullptr;
-    int rope_slow_n = 0, rope_fast_n = 0;
-    // standalone sampler scratch
-    float *samp_logits = nullptr;
-    int samp_cap = 0;
-    int *samp_out = nullptr;
-
-    template <class T>
-    cudaError_t alloc(T **p, size_t n) {
-        void *v = nullptr;
-        cudaError_t e = cudaMalloc(&v, std::max<size_t>(n, 1) * sizeof(T));
-        if (e == cudaSuccess) {
-            allocs.push_back(v);
-            *p = reinterpret_cast<T *>(v);
-        }
-        return e;
-    }
-    void release(void *p) {
-        if (!p) return;
-        auto it = std::find(allocs.begin(), allocs.end(), p);
-        if (it != allocs.end()) allocs.erase(it);
-        cudaFree(p);
-    }
-};
-
-struct s2k_seq {
-    s2k_model *m = nullptr;
-    int max_seq_len = 0, n_pages = 0;
-    __half *k = nullptr, *v = nullptr;
-    int *block_table = nullptr;
-    SeqDev *dev = nullptr;
-    HostStatus *hstat = nullptr;      // mapped pinned
-    HostStatus *hstat_dev = nullptr;  // device alias
-    int n_past = 0;                   // host mirror
-    int *codes = nullptr;             // [ncb][codes_cap]
-    int codes_cap = 0;
-    int *prompt = nullptr;
-    int prompt_cap = 0;
-    cudaGraphExec_t frame_exec = nullptr;
-    size_t frame_nodes = 0;
-    int frame_gen = -1;
-    // persistent-kernel frame program: segments of ops in device memory
-    MegaOp *mega_ops = nullptr;
-    MegaCtl *mega_ctl = nullptr;
-    std::vector<int> seg_start, seg_len, seg_mt;
-    bool use_mega = false;
-    KvPaged kv() const {
-        KvPaged p;
-        p.k = k;
-        p.v = v;
-        p.block_table = block_table;
-        p.n_layers = m->hp.block_count;
-        p.n_kv_heads = m->hp.head_count_kv;
-        p.head_dim = m->hp.head_dim;
-        p.n_pages = n_pages;
-        return p;
-    }
-};
 
 // ---------------------------------------------------------------------------
 // helpers
 // ---------------------------------------------------------------------------
-static int cuda_set(int dev) { return cudaSetDevice(dev) == cudaSuccess ? 0 : -1; }
+int cuda_set(int dev) { return cudaSetDevice(dev) == cudaSuccess ? 0 : -1; }
 
-static s2k_status check_err_word(s2k_model *m) {
+s2k_status check_err_word(s2k_model *m) {
     int h = 0;
     CU(cudaMemcpy(&h, m->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (h) {
@@ -183,7 +59,7 @@ static s2k_status check_err_word(s2k_model *m) {
 
 // T: tokens per call; L: longest key range (positions) a call attends over.
 // prefill: the Slow work, whose prompt-sized calls use the tensor-core GEMM.
-static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int Hkv, int hd, int ff,
+cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int Hkv, int hd, int ff,
                               int n_layers, bool prefill) {
     w.T = T;
     w.L = L;
@@ -202,24 +78,27 @@ static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int 
     if ((e = m->alloc(&w.kcur, tn * w.kvs))) return e;
     if ((e = m->alloc(&w.vcur, tn * w.kvs))) return e;
     if ((e = m->alloc(&w.scores, tn * H * (size_t)L))) return e;
+    // persistent-kernel buffers (its calls have at most kMegaTokens tokens)
+    w.Tm = std::min(T, kMegaTokens);
+    const size_t tm = (size_t)std::max(w.Tm, 1);
     w.n_split_max = (L + kAttnSplit - 1) / kAttnSplit;
-    const size_t units = tn * Hkv * (size_t)w.n_split_max;
+    const size_t units = tm * Hkv * (size_t)w.n_split_max;
     if ((e = m->alloc(&w.part, units * (H / Hkv) * hd))) return e;
     if ((e = m->alloc(&w.part_ms, units * (H / Hkv) * 2))) return e;
     // split arrival counters per (layer, token, kv head): no reuse within a launch
-    if ((e = m->alloc(&w.counters, (size_t)n_layers * tn * Hkv))) return e;
-    if ((e = cudaMemset(w.counters, 0, (size_t)n_layers * tn * Hkv * sizeof(int)))) return e;
-    if ((e = m->alloc(&w.lx, tn * dim))) return e;
-    if ((e = m->alloc(&w.lh, tn * dim))) return e;
-    if ((e = m->alloc(&w.lqkv, tn * (w.qs + 2 * w.kvs)))) return e;
-    if ((e = m->alloc(&w.lattn, tn * w.qs))) return e;
-    if ((e = m->alloc(&w.lff, tn * ff))) return e;
+    if ((e = m->alloc(&w.counters, (size_t)n_layers * tm * Hkv))) return e;
+    if ((e = cudaMemset(w.counters, 0, (size_t)n_layers * tm * Hkv * sizeof(int)))) return e;
+    if ((e = m->alloc(&w.lx, tm * dim))) return e;
+    if ((e = m->alloc(&w.lh, tm * dim))) return e;
+    if ((e = m->alloc(&w.lqkv, tm * (w.qs + 2 * w.kvs)))) return e;
+    if ((e = m->alloc(&w.lattn, tm * w.qs))) return e;
+    if ((e = m->alloc(&w.lff, tm * ff))) return e;
     // tag 0 is never a launch's tag (epochs start at 1)
-    if ((e = cudaMemset(w.lx, 0, tn * dim * 8))) return e;
-    if ((e = cudaMemset(w.lh, 0, tn * dim * 8))) return e;
-    if ((e = cudaMemset(w.lqkv, 0, tn * (w.qs + 2 * w.kvs) * 8))) return e;
-    if ((e = cudaMemset(w.lattn, 0, tn * w.qs * 8))) return e;
-    if ((e = cudaMemset(w.lff, 0, tn * ff * 8))) return e;
+    if ((e = cudaMemset(w.lx, 0, tm * dim * 8))) return e;
+    if ((e = cudaMemset(w.lh, 0, tm * dim * 8))) return e;
+    if ((e = cudaMemset(w.lqkv, 0, tm * (w.qs + 2 * w.kvs) * 8))) return e;
+    if ((e = cudaMemset(w.lattn, 0, tm * w.qs * 8))) return e;
+    if ((e = cudaMemset(w.lff, 0, tm * ff * 8))) return e;
     if (prefill && T >= kPrefillMinT && m->prefill_mma) {
         const int kmax = std::max(std::max(dim, w.qs), ff);
         if ((e = m->alloc(&w.pf_xq, tn * kmax))) return e;
@@ -242,7 +121,7 @@ static cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int 
     return cudaSuccess;
 }
 
-static void work_free(s2k_model *m, Work &w) {
+void work_free(s2k_model *m, Work &w) {
     for (void *p : {(void *)w.x, (void *)w.h, (void *)w.qkv, (void *)w.attn, (void *)w.ff_buf, (void *)w.kcur,
                     (void *)w.vcur, (void *)w.scores, (void *)w.part, (void *)w.part_ms, (void *)w.counters,
                     (void *)w.pf_xq, (void *)w.pf_dx, (void *)w.pf_part, (void *)w.pf_counters, (void *)w.lx,
@@ -251,7 +130,7 @@ static void work_free(s2k_model *m, Work &w) {
     w = Work();
 }
 
-static s2k_status ensure_slow_work(s2k_model *m, int T, int L) {
+s2k_status ensure_slow_work(s2k_model *m, int T, int L) {
     if (m->sw.T >= T && m->sw.L >= L) return S2K_OK;
     T = std::max(T, m->sw.T);
     L = std::max(L, m->sw.L);
@@ -288,25 +167,14 @@ static s2k_status upload_rope(s2k_model *m, float2 **dst, int *n_out, int n_pos,
 // ---------------------------------------------------------------------------
 // stacks
 // ---------------------------------------------------------------------------
-struct StackCall {
-    bool fast;
-    int T;
-    const int *pos_base;  // device n_past (Slow) or null
-    int pos_add;
-    int cur_base;
-    KvPaged kv;  // Slow only
-    int max_keys;  // upper bound of any token's key range
-    const int *done;
-};
 
 // One stack GEMM: prompt-sized Slow calls on Q8_0 weights go through the
 // tensor cores (activation rows quantized once, then tcgen05 int8 MMAs,
 // s2k_prefill.cu); everything else through the tile GEMV.
-static cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool prefill) {
-    if (prefill && m->prefill_mma && w.pf_xq && g.M >= kPrefillMinT && g.M <= w.T && prefill_ok(*g.w, g.M) &&
-        g.act_out == nullptr) {
+cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool prefill) {
+    if (prefill && m->prefill_mma && w.pf_xq && g.M >= kPrefillMinT && g.M <= w.T && prefill_ok(*g.w, g.M)) {
         cudaError_t e = launch_quant_rows_q8(g.x, g.ldx, g.M, g.w->cols, g.in_mode == IN_RMSNORM ? g.norm_w : nullptr,
-                                             g.eps, w.pf_xq, w.pf_dx, nullptr, m->stream);
+                                             g.eps, w.pf_xq, w.pf_dx, g.act_out, m->stream);
         if (e != cudaSuccess) return e;
         PrefillArgs a;
         a.w = g.w;
@@ -328,9 +196,9 @@ static cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool pre
     return launch_gemv(g, m->num_sms, m->stream);
 }
 
-static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
+cudaError_t run_stack(s2k_model *m, const StackCall &c) {
     const s2k_hparams &hp = m->hp;
-    Work &w = c.fast ? m->fw : m->sw;
+    Work &w = c.w ? *c.w : (c.fast ? m->fw : m->sw);
     const std::vector<Layer> &layers = c.fast ? m->fast_layers : m->layers;
     const int H = c.fast ? hp.fast_head_count : hp.head_count;
     const int Hkv = c.fast ? hp.fast_head_count_kv : hp.head_count_kv;
@@ -354,7 +222,7 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         g.ldy = qkvs;
         g.done = c.done;
         g.err = m->d_err;
-        if ((e = stack_gemm(m, w, g, !c.fast))) return e;
+        if ((e = stack_gemm(m, w, g, c.mma))) return e;
 
         QkPrepArgs q;
         q.qkv = w.qkv;
@@ -370,8 +238,10 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         q.rope_positions = c.fast ? m->rope_fast_n : m->rope_slow_n;
         q.pos_base = c.pos_base;
         q.pos_add = c.pos_add;
-        q.kcur = c.fast ? m->fkcur[il] : w.kcur;
-        q.vcur = c.fast ? m->fvcur[il] : w.vcur;
+        q.kcur = c.fast ? (c.fk ? c.fk[il] : m->fkcur[il]) : w.kcur;
+        q.vcur = c.fast ? (c.fv ? c.fv[il] : m->fvcur[il]) : w.vcur;
+        q.rows = c.rows;
+        q.seqs = c.seqs;
         q.cur_base = c.cur_base;
         q.kv = c.kv;
         q.layer = (int)il;
@@ -388,6 +258,8 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         a.hd = hd;
         a.scale = 1.0f / sqrtf((float)hd);
         a.n_cached = c.fast ? nullptr : c.pos_base;
+        a.rows = c.rows;
+        a.seqs = c.seqs;
         a.kv = c.kv;
         a.layer = (int)il;
         a.kcur = q.kcur;
@@ -411,7 +283,7 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         o.ldy = dim;
         o.res = w.x;
         o.ldres = dim;
-        if ((e = stack_gemm(m, w, o, !c.fast))) return e;
+        if ((e = stack_gemm(m, w, o, c.mma))) return e;
 
         GemvArgs f1 = g;
         f1.w = &L.w13;
@@ -422,7 +294,7 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         f1.epi = EPI_SWIGLU;
         f1.y = w.ff_buf;
         f1.ldy = w.ff;
-        if ((e = stack_gemm(m, w, f1, !c.fast))) return e;
+        if ((e = stack_gemm(m, w, f1, c.mma))) return e;
 
         GemvArgs f2 = g;
         f2.w = &L.w2;
@@ -434,14 +306,14 @@ static cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         f2.ldy = dim;
         f2.res = w.h;
         f2.ldres = dim;
-        if ((e = stack_gemm(m, w, f2, !c.fast))) return e;
+        if ((e = stack_gemm(m, w, f2, c.mma))) return e;
     }
     return cudaSuccess;
 }
 
 // Slow step over T tokens already in `tokens_dev` ([T][ncb+1]): embedding,
 // 36 layers, final norm + tied LM head on the last token, n_past += T.
-static cudaError_t enqueue_slow(s2k_model *m, s2k_seq *s, int T, const int *tokens_dev, const int *done) {
+cudaError_t enqueue_slow(s2k_model *m, s2k_seq *s, int T, const int *tokens_dev, const int *done) {
     const s2k_hparams &hp = m->hp;
     cudaStream_t st = m->stream;
     cudaError_t e;
@@ -462,6 +334,7 @@ static cudaError_t enqueue_slow(s2k_model *m, s2k_seq *s, int T, const int *toke
     if ((e = launch_embed_slow(ea, st))) return e;
     StackCall c;
     c.fast = false;
+    c.mma = true;
     c.T = T;
     c.pos_base = &s->dev->state.n_past;
     c.pos_add = 0;
@@ -642,7 +515,6 @@ static s2k_status upload_mat(s2k_model *m, DevMat &dm, int type, const int64_t n
 // ---------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------
-extern "C" {
 
 S2K_API int32_t s2k_abi_version(void) { return S2K_ABI_VERSION; }
 
@@ -705,6 +577,7 @@ S2K_API void s2k_model_free(s2k_model *m) {
     if (!m) return;
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    batch_free(m);
     for (void *p : m->allocs) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -860,6 +733,15 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     return S2K_OK;
 }
 
+// The sequence's KV pages and hidden-state buffer as the batched-frame
+// kernels read them from its device state.
+s2k_status seq_publish(s2k_seq *s) {
+    const KvPaged kv = s->kv();
+    CU(cudaMemcpy(&s->dev->kv, &kv, sizeof(KvPaged), cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(&s->dev->hidden, &s->hidden, sizeof(float *), cudaMemcpyHostToDevice));
+    return S2K_OK;
+}
+
 S2K_API s2k_status s2k_seq_create(s2k_model *m, int32_t max_seq_len, s2k_seq **out) {
     if (!m || !out || max_seq_len <= 0) return fail(S2K_ERR_ARG, "bad argument");
     if (!m->finalized) return fail(S2K_ERR_STATE, "model not finalized");
@@ -884,8 +766,10 @@ S2K_API s2k_status s2k_seq_create(s2k_model *m, int32_t max_seq_len, s2k_seq **o
     if (m->alloc(&s->block_table, (size_t)s->n_pages) ||
         cudaMemcpy(s->block_table, bt.data(), bt.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
         return cleanup(S2K_ERR_OOM, "block table");
+    if (m->alloc(&s->hidden, (size_t)hp.embedding_length)) return cleanup(S2K_ERR_OOM, "hidden state");
     if (m->alloc(&s->dev, 1) || cudaMemset(s->dev, 0, sizeof(SeqDev)) != cudaSuccess)
         return cleanup(S2K_ERR_OOM, "sequence state");
+    if (seq_publish(s) != S2K_OK) return cleanup(S2K_ERR_CUDA, "sequence state");
     if (cudaHostAlloc((void **)&s->hstat, sizeof(HostStatus), cudaHostAllocMapped) != cudaSuccess)
         return cleanup(S2K_ERR_OOM, "host status");
     memset((void *)s->hstat, 0, sizeof(HostStatus));
@@ -910,8 +794,11 @@ S2K_API void s2k_seq_free(s2k_seq *s) {
     cudaSetDevice(m->device);
     cudaStreamSynchronize(m->stream);
     if (s->frame_exec) cudaGraphExecDestroy(s->frame_exec);
-    m->release(s->k);
-    m->release(s->v);
+    if (!s->pooled) {
+        m->release(s->k);
+        m->release(s->v);
+    }
+    m->release(s->hidden);
     m->release(s->block_table);
     m->release(s->dev);
     m->release(s->codes);
@@ -924,7 +811,7 @@ S2K_API void s2k_seq_free(s2k_seq *s) {
 
 S2K_API int32_t s2k_seq_n_past(const s2k_seq *s) { return s ? s->n_past : -1; }
 
-static s2k_status check_tokens_host(const s2k_model *m, const int32_t *flat, int32_t T) {
+s2k_status check_tokens_host(const s2k_model *m, const int32_t *flat, int32_t T) {
     const s2k_hparams &hp = m->hp;
     const int stride = hp.num_codebooks + 1;
     for (int t = 0; t < T; ++t) {
@@ -1107,7 +994,8 @@ static bool add_layers(s2k_model *m, s2k_seq *s, bool fast, int T, int pos_add, 
     const int hd = fast ? hp.fast_head_dim : hp.head_dim;
     const float eps = fast ? hp.fast_rms_norm_eps : hp.rms_norm_eps;
     const int qkvs = w.qs + 2 * w.kvs, dim = w.dim;
-    const size_t tn = (size_t)std::max(w.T, 1);
+    const size_t tn = (size_t)std::max(w.Tm, 1);
+    if (T > w.Tm) return false;
     for (size_t il = 0; il < layers.size(); ++il) {
         const Layer &L = layers[il];
         const int q_op = (int)ops.size() - start, a_op = q_op + 1, o_op = q_op + 2, f_op = q_op + 3, d_op = q_op + 4;
@@ -1149,7 +1037,7 @@ static bool add_layers(s2k_model *m, s2k_seq *s, bool fast, int T, int pos_add, 
         a.a.counters = w.counters + il * tn * Hkv;  // per layer: no counter is reused within a launch
         a.a.n_split_max = w.n_split_max;
         a.a.out = w.lattn;
-        if (T * H > w.T * w.H || !mega_attn_ok(a.a, fast ? pos_add + T : s->max_seq_len)) return false;
+        if (T * H > w.Tm * w.H || !mega_attn_ok(a.a, fast ? pos_add + T : s->max_seq_len)) return false;
         ops.push_back(a);
         ops.push_back(mk_gemv(L.wo, w.lattn, w.qs, T, IN_PLAIN, nullptr, eps, EPI_STORE, w.lh, dim, w.lx, dim, nullptr,
                               LL_X | LL_RES | LL_Y, a_op, x_op, o_op));
@@ -1307,15 +1195,8 @@ static s2k_status ensure_frame_graph(s2k_model *m, s2k_seq *s) {
     return S2K_OK;
 }
 
-static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_prompt_tm, int32_t cols,
-                                const s2k_gen_params *gp, int32_t *d_codes, int32_t codes_ld, int32_t *n_frames_out) {
+void fill_sample_cfg(const s2k_model *m, const s2k_gen_params *gp, int *d_codes, int codes_ld, SampleCfg *out) {
     const s2k_hparams &hp = m->hp;
-    if (cols <= 0 || gp->max_new_tokens < 0) return fail(S2K_ERR_ARG, "bad prompt length / max_new_tokens");
-    if (cols + gp->max_new_tokens > s->max_seq_len)
-        return fail(S2K_ERR_KV_FULL, "sequence holds %d positions, need %d", s->max_seq_len, cols + gp->max_new_tokens);
-    if (!hp.has_fast_decoder && hp.num_codebooks > 1) return fail(S2K_ERR_STATE, "model has no fast decoder");
-    s2k_status rc = ensure_slow_work(m, cols, s->max_seq_len);
-    if (rc) return rc;
     SampleCfg c;
     memset(&c, 0, sizeof(c));
     c.temperature = gp->temperature;
@@ -1333,6 +1214,20 @@ static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_promp
     c.vocab = hp.vocab_size;
     c.codes_out = d_codes;
     c.codes_ld = codes_ld;
+    *out = c;
+}
+
+static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_prompt_tm, int32_t cols,
+                                const s2k_gen_params *gp, int32_t *d_codes, int32_t codes_ld, int32_t *n_frames_out) {
+    const s2k_hparams &hp = m->hp;
+    if (cols <= 0 || gp->max_new_tokens < 0) return fail(S2K_ERR_ARG, "bad prompt length / max_new_tokens");
+    if (cols + gp->max_new_tokens > s->max_seq_len)
+        return fail(S2K_ERR_KV_FULL, "sequence holds %d positions, need %d", s->max_seq_len, cols + gp->max_new_tokens);
+    if (!hp.has_fast_decoder && hp.num_codebooks > 1) return fail(S2K_ERR_STATE, "model has no fast decoder");
+    s2k_status rc = ensure_slow_work(m, cols, s->max_seq_len);
+    if (rc) return rc;
+    SampleCfg c;
+    fill_sample_cfg(m, gp, d_codes, codes_ld, &c);
     // the Pipeline clears and re-inits the KV cache per synthesis (src/s2_pipeline.cpp:838-851)
     CU(cudaMemsetAsync(&s->dev->state, 0, sizeof(SeqState), m->stream));
     CU(cudaMemcpyAsync(&s->dev->cfg, &c, sizeof(SampleCfg), cudaMemcpyHostToDevice, m->stream));
@@ -1683,4 +1578,3 @@ S2K_API s2k_status s2k_debug_copy(s2k_model *m, s2k_seq *s, const char *name, vo
     return S2K_OK;
 }
 
-}  // extern "C"

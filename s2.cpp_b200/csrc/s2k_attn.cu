@@ -27,9 +27,23 @@
 // walks the splits in order (scores, split maxima, then per split the
 // exponentials, S_i and O_i folded into the running sums with w_i).
 #include "s2k_common.cuh"
+#include "s2k_device.h"
 #include "s2k_kernels.h"
 
 namespace s2k {
+
+// KV pages of a batched call's sequence (constant while the sequence lives).
+__device__ __forceinline__ KvPaged seq_kv(const SeqDev *sd) {
+    KvPaged kv;
+    kv.k = sd->kv.k;
+    kv.v = sd->kv.v;
+    kv.block_table = sd->kv.block_table;
+    kv.n_layers = sd->kv.n_layers;
+    kv.n_kv_heads = sd->kv.n_kv_heads;
+    kv.head_dim = sd->kv.head_dim;
+    kv.n_pages = sd->kv.n_pages;
+    return kv;
+}
 
 // grid (T, H + 2*Hkv), block hd/2: thread i owns the pair (2i, 2i+1).
 __global__ void qk_prep_kernel(QkPrepArgs a) {
@@ -38,7 +52,18 @@ __global__ void qk_prep_kernel(QkPrepArgs a) {
     if (a.done && __ldcg(a.done)) return;
     const int t = blockIdx.x, y = blockIdx.y, i = threadIdx.x, hd = a.hd;
     float *row = a.qkv + (size_t)t * a.ldqkv;
-    const int pos = (a.pos_base ? __ldcg(a.pos_base) : 0) + a.pos_add + t;
+    int pos, cur_row;
+    KvPaged kv = a.kv;
+    if (a.rows) {
+        const BatchRow r = a.rows[t];
+        const SeqDev *sd = a.seqs ? a.seqs[r.slot] : nullptr;
+        pos = (sd ? __ldcg(&sd->state.n_past) : 0) + r.off;
+        cur_row = r.cur_hi;
+        if (sd) kv = seq_kv(sd);
+    } else {
+        pos = (a.pos_base ? __ldcg(a.pos_base) : 0) + a.pos_add + t;
+        cur_row = a.cur_base + t;
+    }
     const bool isq = y < a.H;
     const bool isk = !isq && y < a.H + a.Hkv;
     const int head = isq ? y : (isk ? y - a.H : y - a.H - a.Hkv);
@@ -74,18 +99,18 @@ __global__ void qk_prep_kernel(QkPrepArgs a) {
         v[2 * i + 1] = x1;
         return;
     }
-    float *cur = (isk ? a.kcur : a.vcur) + ((size_t)(a.cur_base + t) * a.Hkv + head) * hd;
+    float *cur = (isk ? a.kcur : a.vcur) + ((size_t)cur_row * a.Hkv + head) * hd;
     cur[2 * i] = x0;
     cur[2 * i + 1] = x1;
-    if (a.kv.k) {
+    if (kv.k) {
         const int pg = pos / kPage, slot = pos % kPage;
-        if (pos < 0 || pg >= a.kv.n_pages) {
+        if (pos < 0 || pg >= kv.n_pages) {
             if (i == 0 && a.err) atomicOr(a.err, ERR_BAD_POS);
             return;
         }
-        const int page = __ldcg(a.kv.block_table + pg);
-        __half *dst = (isk ? a.kv.k : a.kv.v) +
-                      ((((size_t)page * a.kv.n_layers + a.layer) * a.kv.n_kv_heads + head) * kPage + slot) * hd;
+        const int page = __ldcg(kv.block_table + pg);
+        __half *dst = (isk ? kv.k : kv.v) +
+                      ((((size_t)page * kv.n_layers + a.layer) * kv.n_kv_heads + head) * kPage + slot) * hd;
         dst[2 * i] = __float2half_rn(x0);
         dst[2 * i + 1] = __float2half_rn(x1);
     }
@@ -116,12 +141,14 @@ constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxGroup = 8;
 
-__device__ __forceinline__ void load_kv_row(const AttnArgs &a, const __half *cache, const float *cur, int j, int nc,
-                                            int g, int lane, float out[4]) {
+// Key / value row j of a CTA's key range: positions j < nc from the paged
+// cache, later ones from this call's f32 rows (cur holds the range's first).
+__device__ __forceinline__ void load_kv_row(const AttnArgs &a, const KvPaged &kv, const __half *cache,
+                                            const float *cur, int j, int nc, int g, int lane, float out[4]) {
     if (j < nc) {
-        const int page = __ldcg(a.kv.block_table + j / kPage), slot = j % kPage;
+        const int page = __ldcg(kv.block_table + j / kPage), slot = j % kPage;
         const size_t off =
-            ((((size_t)page * a.kv.n_layers + a.layer) * a.kv.n_kv_heads + g) * kPage + slot) * 128 + lane * 4;
+            ((((size_t)page * kv.n_layers + a.layer) * kv.n_kv_heads + g) * kPage + slot) * 128 + lane * 4;
         const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(cache + off));
         const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
         const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
@@ -155,8 +182,25 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
     const int g = blockIdx.x, t = blockIdx.y;
     const int G = a.H / a.Hkv;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nc = a.n_cached ? __ldcg(a.n_cached) : 0;
-    const int Lk = nc + a.cur_base + t + 1;
+    int nc, Lk;
+    KvPaged kv = a.kv;
+    const float *kc = a.kcur, *vc = a.vcur;
+    if (a.rows) {
+        const BatchRow r = a.rows[t];
+        const SeqDev *sd = a.seqs ? a.seqs[r.slot] : nullptr;
+        nc = sd ? __ldcg(&sd->state.n_past) : 0;
+        if (sd) kv = seq_kv(sd);
+        kc += (size_t)r.cur_lo * a.Hkv * 128;
+        vc += (size_t)r.cur_lo * a.Hkv * 128;
+        Lk = nc + r.cur_hi - r.cur_lo + 1;
+    } else {
+        nc = a.n_cached ? __ldcg(a.n_cached) : 0;
+        Lk = nc + a.cur_base + t + 1;
+    }
+    if (Lk < 1 || Lk > a.ld_scores || Lk > a.max_keys || (nc > 0 && (nc - 1) / kPage >= kv.n_pages)) {
+        if (tid == 0 && a.err) atomicOr(a.err, ERR_BAD_POS);
+        return;
+    }
     const int nsp = (Lk + kAttnSplit - 1) / kAttnSplit;
     double *red = reinterpret_cast<double *>(smem);                    // [kAttnWarps][G][128]
     float *ebuf = reinterpret_cast<float *>(red + kAttnWarps * G * 128);  // [G][kAttnSplit]
@@ -171,7 +215,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
     // pass A: every score of the key range
     for (int j = warp; j < Lk; j += kAttnWarps) {
         float k[4];
-        load_kv_row(a, a.kv.k, a.kcur, j, nc, g, lane, k);
+        load_kv_row(a, kv, kv.k, kc, j, nc, g, lane, k);
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h)
             if (h < G) {
@@ -217,7 +261,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
             for (int d = 0; d < 4; ++d) o[h][d] = 0.0;
         for (int jj = warp; jj < cnt; jj += kAttnWarps) {
             float v[4];
-            load_kv_row(a, a.kv.v, a.vcur, j0 + jj, nc, g, lane, v);
+            load_kv_row(a, kv, kv.v, vc, j0 + jj, nc, g, lane, v);
 #pragma unroll
             for (int h = 0; h < kMaxGroup; ++h)
                 if (h < G) {

@@ -1,6 +1,8 @@
 // s2k_device.h -- per-sequence device state shared by the frame-loop kernels.
 #pragma once
 
+#include "s2k_kernels.h"
+
 namespace s2k {
 
 // Mapped pinned memory the host polls while frames run.
@@ -41,6 +43,9 @@ struct SeqDev {
     SeqState state;
     SampleCfg cfg;
     HostStatus *host;  // device alias of mapped pinned memory (may be null)
+    // read by the batched-frame kernels, set when the sequence is created
+    KvPaged kv;        // the sequence's paged f16 KV cache
+    float *hidden;     // [embedding_length] Slow hidden state for the next Fast-AR pass
 };
 
 }  // namespace s2k

@@ -9,6 +9,17 @@
 
 namespace s2k {
 
+struct SeqDev;  // s2k_device.h
+
+// One token row of a batched call over independent sequences (continuous
+// batching).  The rows of one sequence are contiguous and in position order.
+struct BatchRow {
+    int slot;    // the row's sequence: index into the call's sequence array
+    int off;     // position = base + off; base = the sequence's n_past (Slow stack) or 0 (Fast stack)
+    int cur_lo;  // this call's keys of the row: K/V rows [cur_lo, cur_hi] of kcur / vcur
+    int cur_hi;  // the row's own K/V row in kcur / vcur
+};
+
 // ---------------------------------------------------------------------------
 // Weight matrix in device layout: 32 x 512 tiles (s2k_tgemv.cuh) of
 //   Q8_0 : int8 quants + fp16 scales,
@@ -108,6 +119,10 @@ struct QkPrepArgs {
     int cur_base = 0;
     KvPaged kv;  // if kv.k: also store f16 K/V of (layer) at the token's position
     int layer = 0;
+    // batched call: row t is rows[t]; position, K/V row and (with seqs) the
+    // KV pages it stores to come from the descriptor and its sequence
+    const BatchRow *rows = nullptr;
+    SeqDev *const *seqs = nullptr;
     const int *done = nullptr;
     int *err = nullptr;
 };
@@ -127,6 +142,10 @@ struct AttnArgs {
     float *scores = nullptr;  // scratch [T][H][ld_scores]
     int ld_scores = 0;        // >= longest key range of the call
     float *out = nullptr;     // [T][H*hd]
+    // batched call: row t attends to its sequence's cached positions (with
+    // seqs; none without) and to kcur / vcur rows [cur_lo, cur_hi] of rows[t]
+    const BatchRow *rows = nullptr;
+    SeqDev *const *seqs = nullptr;
     const int *done = nullptr;
     int *err = nullptr;
 };
@@ -147,6 +166,7 @@ struct EmbedArgs {
     int scale_cb = 0;
     float sem_scale = 1.f;
     float *x = nullptr;  // [T][dim]
+    SeqDev *const *seqs = nullptr;  // batched frame: row t's tokens are seqs[t]'s next step input
     const int *done = nullptr;
     int *err = nullptr;
 };
@@ -155,8 +175,13 @@ cudaError_t launch_embed_slow(const EmbedArgs &a, cudaStream_t st);
 cudaError_t launch_embed_fast(const DevMat *fast_emb, const float *hidden, const int *codes, int code0,
                               int n_rows, float *x, int dim, const int *done, int *err, cudaStream_t st);
 
+// Fast-AR input rows of pass `pass` of a batched frame over n sequences:
+// pass 0 rows (2b, 2b+1) = (hidden of b, fast_emb[codes_b[0]]); pass p > 0
+// row b = fast_emb[codes_b[p]].
+cudaError_t launch_embed_fast_batch(const DevMat *fast_emb, SeqDev *const *seqs, int n, int pass, float *x, int dim,
+                                    int *err, cudaStream_t st);
+
 // Frame-loop launchers (state structs in s2k_device.h).
-struct SeqDev;
 cudaError_t sampler_setup();
 // After a Slow step (or the prefill): sample the main token of the next frame
 // with the semantic mask, stop test, RAS, window push, codes[0].
@@ -167,6 +192,15 @@ cudaError_t launch_sample_fast(const float *logits, SeqDev *sd, int cb, int *err
 cudaError_t launch_frame_commit(SeqDev *sd, cudaStream_t st);
 // After the Slow step kernels: n_past += T.
 cudaError_t launch_advance(SeqDev *sd, int T, const int *done, cudaStream_t st);
+// Batched frame over n sequences (one CTA per sequence): logits row b
+// belongs to seqs[b].  sample_main also stores hidden row b as the
+// sequence's hidden state.
+cudaError_t launch_sample_main_batch(const float *logits, size_t ld, SeqDev *const *seqs, int n, const float *hidden,
+                                     int dim, int *err, cudaStream_t st);
+cudaError_t launch_sample_fast_batch(const float *logits, size_t ld, SeqDev *const *seqs, int n, int cb, int *err,
+                                     cudaStream_t st);
+cudaError_t launch_frame_commit_batch(SeqDev *const *seqs, int n, cudaStream_t st);
+cudaError_t launch_advance_batch(SeqDev *const *seqs, int n, int T, cudaStream_t st);
 // Standalone sampler (s2k_sample)
 cudaError_t launch_sample_one(const float *logits, int n, float temperature, float top_p, int top_k,
                               double u, int *out, int *err, cudaStream_t st);

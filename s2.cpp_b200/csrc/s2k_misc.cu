@@ -31,7 +31,8 @@ __global__ void embed_slow_kernel(EmbedArgs a, DevMat E, DevMat C) {
     pdl_wait();
     if (a.done && __ldcg(a.done)) return;
     const int t = blockIdx.x, dim = E.cols, stride = a.ncb + 1;
-    int tok = __ldcg(a.tokens + t * stride);
+    const int *tokens = a.seqs ? a.seqs[t]->state.step_in : a.tokens + t * stride;
+    int tok = __ldcg(tokens);
     if (tok < 0 || tok >= E.rows) {
         if (threadIdx.x == 0 && a.err) atomicOr(a.err, ERR_BAD_TOKEN);
         tok = 0;
@@ -41,7 +42,7 @@ __global__ void embed_slow_kernel(EmbedArgs a, DevMat E, DevMat C) {
     bool ok = true;
     if (sem) {
         for (int cb = 0; cb < a.ncb; ++cb) {
-            ids[cb] = __ldcg(a.tokens + t * stride + 1 + cb) + cb * a.cb_size;
+            ids[cb] = __ldcg(tokens + 1 + cb) + cb * a.cb_size;
             if (ids[cb] < 0 || ids[cb] >= C.rows) ok = false;
         }
     }
@@ -94,6 +95,42 @@ __global__ void embed_fast_kernel(DevMat F, const float *hidden, const int *code
         c = 0;
     }
     for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)r * dim + i] = deq_elem(F, c, i);
+}
+
+// grid n_rows (pass 0: 2n, else n), block 256
+__global__ void embed_fast_batch_kernel(DevMat F, SeqDev *const *seqs, int pass, float *x, int dim, int *err) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int r = blockIdx.x;
+    const int b = pass == 0 ? r >> 1 : r;
+    const SeqDev *sd = seqs[b];
+    if (pass == 0 && (r & 1) == 0) {
+        const float *h = sd->hidden;
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)r * dim + i] = __ldcg(h + i);
+        return;
+    }
+    int c = __ldcg(&sd->state.codes[pass]);
+    if (c < 0 || c >= F.rows) {
+        if (threadIdx.x == 0 && err) atomicOr(err, ERR_BAD_TOKEN);
+        c = 0;
+    }
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)r * dim + i] = deq_elem(F, c, i);
+}
+
+cudaError_t launch_embed_fast_batch(const DevMat *fast_emb, SeqDev *const *seqs, int n, int pass, float *x, int dim,
+                                    int *err, cudaStream_t st) {
+    if (tw_of(fast_emb->type) < 0 || n < 1 || pass < 0 || pass >= 16) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pass == 0 ? 2 * n : n);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, embed_fast_batch_kernel, *fast_emb, seqs, pass, x, dim, err);
 }
 
 cudaError_t launch_embed_fast(const DevMat *fast_emb, const float *hidden, const int *codes, int code0, int n_rows,
@@ -334,11 +371,7 @@ __device__ __forceinline__ SlowCand make_slow_cand(const float *logits, const Sa
     return sc;
 }
 
-__global__ void __launch_bounds__(kSampThreads) sample_main_kernel(const float *logits, SeqDev *sd, int *err) {
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    SampSmem &sm = *reinterpret_cast<SampSmem *>(smem_raw);
-    pdl_launch_dependents();
-    pdl_wait();
+__device__ void sample_main_body(SampSmem &sm, const float *logits, SeqDev *sd, int *err) {
     volatile SeqState &st = sd->state;
     const SampleCfg c = load_cfg(&sd->cfg);
     if (st.done) return;
@@ -381,11 +414,31 @@ __global__ void __launch_bounds__(kSampThreads) sample_main_kernel(const float *
     }
 }
 
-__global__ void __launch_bounds__(kSampThreads) sample_fast_kernel(const float *logits, SeqDev *sd, int cb, int *err) {
+__global__ void __launch_bounds__(kSampThreads) sample_main_kernel(const float *logits, SeqDev *sd, int *err) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     SampSmem &sm = *reinterpret_cast<SampSmem *>(smem_raw);
     pdl_launch_dependents();
     pdl_wait();
+    sample_main_body(sm, logits, sd, err);
+}
+
+// grid n: CTA b samples sequence b's main token from logits row b after
+// storing hidden row b as the sequence's hidden state.
+__global__ void __launch_bounds__(kSampThreads) sample_main_batch_kernel(const float *logits, size_t ld,
+                                                                         SeqDev *const *seqs, const float *hidden,
+                                                                         int dim, int *err) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    SampSmem &sm = *reinterpret_cast<SampSmem *>(smem_raw);
+    pdl_launch_dependents();
+    pdl_wait();
+    const int b = blockIdx.x;
+    SeqDev *sd = seqs[b];
+    float *dst = sd->hidden;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) dst[i] = __ldcg(hidden + (size_t)b * dim + i);
+    sample_main_body(sm, logits + (size_t)b * ld, sd, err);
+}
+
+__device__ void sample_fast_body(SampSmem &sm, const float *logits, SeqDev *sd, int cb, int *err) {
     volatile SeqState &st = sd->state;
     const SampleCfg c = load_cfg(&sd->cfg);
     if (st.done) return;
@@ -395,9 +448,24 @@ __global__ void __launch_bounds__(kSampThreads) sample_fast_kernel(const float *
     if (threadIdx.x == 0) st.codes[cb] = tok;
 }
 
-__global__ void frame_commit_kernel(SeqDev *sd) {
+__global__ void __launch_bounds__(kSampThreads) sample_fast_kernel(const float *logits, SeqDev *sd, int cb, int *err) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    SampSmem &sm = *reinterpret_cast<SampSmem *>(smem_raw);
     pdl_launch_dependents();
     pdl_wait();
+    sample_fast_body(sm, logits, sd, cb, err);
+}
+
+__global__ void __launch_bounds__(kSampThreads) sample_fast_batch_kernel(const float *logits, size_t ld,
+                                                                         SeqDev *const *seqs, int cb, int *err) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    SampSmem &sm = *reinterpret_cast<SampSmem *>(smem_raw);
+    pdl_launch_dependents();
+    pdl_wait();
+    sample_fast_body(sm, logits + (size_t)blockIdx.x * ld, seqs[blockIdx.x], cb, err);
+}
+
+__device__ void frame_commit_body(SeqDev *sd) {
     volatile SeqState &st = sd->state;
     const SampleCfg c = load_cfg(&sd->cfg);
     if (st.done) return;
@@ -414,6 +482,29 @@ __global__ void frame_commit_kernel(SeqDev *sd) {
         HostStatus *hs = (HostStatus *)__ldcg((const unsigned long long *)&sd->host);
         if (hs) hs->n_frames = f + 1;
     }
+}
+
+__global__ void frame_commit_kernel(SeqDev *sd) {
+    pdl_launch_dependents();
+    pdl_wait();
+    frame_commit_body(sd);
+}
+
+// grid n, block 32
+__global__ void frame_commit_batch_kernel(SeqDev *const *seqs) {
+    pdl_launch_dependents();
+    pdl_wait();
+    frame_commit_body(seqs[blockIdx.x]);
+}
+
+// one thread per sequence
+__global__ void advance_batch_kernel(SeqDev *const *seqs, int n, int T) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n) return;
+    volatile SeqState &st = seqs[b]->state;
+    if (!st.done) st.n_past = st.n_past + T;
 }
 
 __global__ void advance_kernel(SeqDev *sd, int T, const int *done) {
@@ -443,6 +534,12 @@ cudaError_t sampler_setup() {
         return e;
     if ((e = cudaFuncSetAttribute(sample_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(SampSmem))))
         return e;
+    if ((e = cudaFuncSetAttribute(sample_main_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  sizeof(SampSmem))))
+        return e;
+    if ((e = cudaFuncSetAttribute(sample_fast_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  sizeof(SampSmem))))
+        return e;
     return cudaSuccess;
 }
 
@@ -465,6 +562,40 @@ cudaError_t launch_frame_commit(SeqDev *sd, cudaStream_t st) {
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(32), 0, st, attr);
     count_launch();
     return cudaLaunchKernelEx(&cfg, frame_commit_kernel, sd);
+}
+
+cudaError_t launch_sample_main_batch(const float *logits, size_t ld, SeqDev *const *seqs, int n, const float *hidden,
+                                     int dim, int *err, cudaStream_t st) {
+    if (n < 1) return cudaErrorInvalidValue;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(n), dim3(kSampThreads), sizeof(SampSmem), st, attr);
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, sample_main_batch_kernel, logits, ld, seqs, hidden, dim, err);
+}
+
+cudaError_t launch_sample_fast_batch(const float *logits, size_t ld, SeqDev *const *seqs, int n, int cb, int *err,
+                                     cudaStream_t st) {
+    if (n < 1) return cudaErrorInvalidValue;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(n), dim3(kSampThreads), sizeof(SampSmem), st, attr);
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, sample_fast_batch_kernel, logits, ld, seqs, cb, err);
+}
+
+cudaError_t launch_frame_commit_batch(SeqDev *const *seqs, int n, cudaStream_t st) {
+    if (n < 1) return cudaErrorInvalidValue;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(n), dim3(32), 0, st, attr);
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, frame_commit_batch_kernel, seqs);
+}
+
+cudaError_t launch_advance_batch(SeqDev *const *seqs, int n, int T, cudaStream_t st) {
+    if (n < 1) return cudaErrorInvalidValue;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3((n + 127) / 128), dim3(128), 0, st, attr);
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, advance_batch_kernel, seqs, n, T);
 }
 
 cudaError_t launch_advance(SeqDev *sd, int T, const int *done, cudaStream_t st) {

@@ -222,6 +222,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // ---------------- epilogue ----------------
         const int q = warp & 3, h = (warp - 2) >> 2;
         const int row_local = q * 32 + lane;
+        // tokens of this warp's half that exist (warp-uniform): the terms of
+        // the padding columns of a short token tile are skipped in groups of 8
+        const int nvalid = min(32, max(0, p.T - (t0 + 32 * h)));
         double acc[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[j] = 0.0;
@@ -231,14 +234,21 @@ __global__ void __launch_bounds__(kPThreads, 1)
             if (ok) ok = mbar_wait(&sm.tfull[buf], (i >> 1) & 1, p.err, ERR_WAIT_FULL);
             if (!ok) break;
             tc_fence_after();
+            if (nvalid > 0) {
 #pragma unroll
-            for (int blk = 0; blk < 4; ++blk) {
-                const int b = (i & 3) * 4 + blk;
-                int s[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * 256 + blk * kPN + 32 * h, s);
-                const double dwr = (double)__half2float(sm.dw[sb][row_local][b]);
+                for (int blk = 0; blk < 4; ++blk) {
+                    const int b = (i & 3) * 4 + blk;
+                    int s[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * 256 + blk * kPN + 32 * h, s);
+                    const double dwr = (double)__half2float(sm.dw[sb][row_local][b]);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) acc[j] = fma(i2d_exact(s[j]), dwr * sm.dx[sb][32 * h + j][b], acc[j]);
+                    for (int g8 = 0; g8 < 4; ++g8)
+                        if (8 * g8 < nvalid) {
+#pragma unroll
+                            for (int j = 8 * g8; j < 8 * g8 + 8; ++j)
+                                acc[j] = fma(i2d_exact(s[j]), dwr * sm.dx[sb][32 * h + j][b], acc[j]);
+                        }
+                }
             }
             tc_fence_before();
             __syncwarp();

@@ -35,7 +35,12 @@ EXPORTED = [
     "s2k_fast_decode", "s2k_generate", "s2k_generate_device", "s2k_sample", "s2k_launch_count",
     "s2k_profile_gemv", "s2k_debug_copy", "s2k_sample_noalloc",
     "s2k_profile_frame", "s2k_profile_ops", "s2k_profile_trace",
+    "s2k_seq_begin", "s2k_batch_frame", "s2k_seq_frames", "s2k_sched_create", "s2k_sched_free",
+    "s2k_sched_submit", "s2k_sched_step", "s2k_sched_run", "s2k_sched_poll", "s2k_sched_result",
+    "s2k_sched_get_stats",
 ]
+
+REQ_WAITING, REQ_LIVE, REQ_DONE = 0, 1, 2  # S2K_REQ_*
 
 
 class S2KError(RuntimeError):
@@ -66,6 +71,12 @@ class _GenParams(ctypes.Structure):
     _fields_ = [("max_new_tokens", ctypes.c_int32), ("temperature", ctypes.c_float), ("top_p", ctypes.c_float),
                 ("top_k", ctypes.c_int32), ("min_tokens_before_end", ctypes.c_int32),
                 ("im_end_id", ctypes.c_int32), ("seed", ctypes.c_uint64), ("seq_id", ctypes.c_uint32)]
+
+
+class _SchedStats(ctypes.Structure):
+    _fields_ = [("steps", ctypes.c_int64), ("frames", ctypes.c_int64), ("prefill_tokens", ctypes.c_int64),
+                ("admitted", ctypes.c_int64), ("finished", ctypes.c_int64), ("max_live", ctypes.c_int32),
+                ("free_pages", ctypes.c_int32), ("pool_pages", ctypes.c_int32)]
 
 
 FRAME_CB = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32,
@@ -114,6 +125,17 @@ def lib() -> ctypes.CDLL:
                              ctypes.POINTER(i32)], i32),
         "s2k_profile_trace": ([vp, vp, i32, ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.POINTER(i32),
                                ctypes.POINTER(i32)], i32),
+        "s2k_seq_begin": ([vp, vp, vp, i32, ctypes.POINTER(_GenParams)], i32),
+        "s2k_batch_frame": ([vp, ctypes.POINTER(vp), i32, ctypes.POINTER(i32)], i32),
+        "s2k_seq_frames": ([vp, vp, i32, ctypes.POINTER(i32), ctypes.POINTER(i32)], i32),
+        "s2k_sched_create": ([vp, i32, i32, i32, ctypes.POINTER(vp)], i32),
+        "s2k_sched_free": ([vp], None),
+        "s2k_sched_submit": ([vp, vp, i32, ctypes.POINTER(_GenParams), ctypes.POINTER(i32)], i32),
+        "s2k_sched_step": ([vp, ctypes.POINTER(i32), ctypes.POINTER(i32)], i32),
+        "s2k_sched_run": ([vp], i32),
+        "s2k_sched_poll": ([vp, i32, ctypes.POINTER(i32), ctypes.POINTER(i32)], i32),
+        "s2k_sched_result": ([vp, i32, vp, i32, ctypes.POINTER(i32)], i32),
+        "s2k_sched_get_stats": ([vp, ctypes.POINTER(_SchedStats)], i32),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -348,6 +370,120 @@ class SlowARModel:
             self.clear_kv_cache()
             lib().s2k_model_free(self._m)
             self._m = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Sequence:
+    """One utterance's decode state (s2k_seq) for batched frames: begin()
+    prefills the prompt, SlowARModel.batch_frame advances several together."""
+
+    def __init__(self, model: "SlowARModel", max_seq_len: int):
+        self._model = model
+        self._hp = model._hp
+        h = ctypes.c_void_p()
+        _check(lib().s2k_seq_create(model.handle, max_seq_len, ctypes.byref(h)))
+        self._s = h
+        self._cap = 0
+
+    def begin(self, prompt: np.ndarray, max_new_tokens: int, temperature: float = 0.8, top_p: float = 0.8,
+              top_k: int = 30, min_tokens_before_end: int = 0, im_end_id: int = -1, seed: int = 0,
+              seq_id: int = 0) -> None:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        gp = _GenParams(max_new_tokens, temperature, top_p, top_k, min_tokens_before_end, im_end_id, seed, seq_id)
+        _check(lib().s2k_seq_begin(self._model.handle, self._s, _ptr(p), p.shape[1], ctypes.byref(gp)))
+        self._cap = max(max_new_tokens, 1)
+
+    def frames(self):
+        """(codes [num_codebooks][n_frames], done)."""
+        ncb = max(self._hp.num_codebooks, 1)
+        buf = np.zeros(ncb * max(self._cap, 1), dtype=np.int32)
+        nf, done = ctypes.c_int32(0), ctypes.c_int32(0)
+        _check(lib().s2k_seq_frames(self._s, _ptr(buf), self._cap, ctypes.byref(nf), ctypes.byref(done)))
+        return buf[: ncb * nf.value].reshape(ncb, nf.value), bool(done.value)
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._s
+
+    def close(self) -> None:
+        if getattr(self, "_s", None):
+            lib().s2k_seq_free(self._s)
+            self._s = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def batch_frame(model: "SlowARModel", seqs) -> int:
+    """One batched frame over the unfinished sequences in `seqs`; returns how
+    many are still unfinished."""
+    arr = (ctypes.c_void_p * len(seqs))(*[s.handle for s in seqs])
+    live = ctypes.c_int32(0)
+    _check(lib().s2k_batch_frame(model.handle, arr, len(seqs), ctypes.byref(live)))
+    return live.value
+
+
+class BatchScheduler:
+    """Continuous batching over independent utterances (s2k_sched_*): submit
+    requests, run, collect each request's codes [num_codebooks][n_frames]."""
+
+    def __init__(self, model: "SlowARModel", max_batch: int, max_seq_len: int, pool_pages: int = 0):
+        self._model = model
+        self._hp = model._hp
+        h = ctypes.c_void_p()
+        _check(lib().s2k_sched_create(model.handle, max_batch, max_seq_len, pool_pages, ctypes.byref(h)))
+        self._sc = h
+
+    def submit(self, prompt: np.ndarray, max_new_tokens: int, temperature: float = 0.8, top_p: float = 0.8,
+               top_k: int = 30, min_tokens_before_end: int = 0, im_end_id: int = -1, seed: int = 0,
+               seq_id: int = 0) -> int:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        if p.shape[0] != self._hp.num_codebooks + 1:
+            raise S2KError(-1, f"prompt must have {self._hp.num_codebooks + 1} rows")
+        gp = _GenParams(max_new_tokens, temperature, top_p, top_k, min_tokens_before_end, im_end_id, seed, seq_id)
+        rid = ctypes.c_int32(0)
+        _check(lib().s2k_sched_submit(self._sc, _ptr(p), p.shape[1], ctypes.byref(gp), ctypes.byref(rid)))
+        return rid.value
+
+    def step(self):
+        """(live, waiting) after admitting, one batched frame and retiring."""
+        nl, nw = ctypes.c_int32(0), ctypes.c_int32(0)
+        _check(lib().s2k_sched_step(self._sc, ctypes.byref(nl), ctypes.byref(nw)))
+        return nl.value, nw.value
+
+    def run(self) -> None:
+        _check(lib().s2k_sched_run(self._sc))
+
+    def poll(self, req_id: int):
+        st, nf = ctypes.c_int32(0), ctypes.c_int32(0)
+        _check(lib().s2k_sched_poll(self._sc, req_id, ctypes.byref(st), ctypes.byref(nf)))
+        return st.value, nf.value
+
+    def result(self, req_id: int) -> np.ndarray:
+        nf = ctypes.c_int32(0)
+        _check(lib().s2k_sched_result(self._sc, req_id, None, 0, ctypes.byref(nf)))
+        ncb = max(self._hp.num_codebooks, 1)
+        buf = np.zeros(ncb * max(nf.value, 1), dtype=np.int32)
+        _check(lib().s2k_sched_result(self._sc, req_id, _ptr(buf), nf.value, ctypes.byref(nf)))
+        return buf[: ncb * nf.value].reshape(ncb, nf.value)
+
+    def stats(self) -> dict:
+        st = _SchedStats()
+        _check(lib().s2k_sched_get_stats(self._sc, ctypes.byref(st)))
+        return {name: getattr(st, name) for name, _ in _SchedStats._fields_}
+
+    def close(self) -> None:
+        if getattr(self, "_sc", None):
+            lib().s2k_sched_free(self._sc)
+            self._sc = None
 
     def __del__(self):
         try:

@@ -44,3 +44,17 @@ def test_no_device_error_paths():
     assert e.value.status == -8
     msg = s2k.lib().s2k_last_error().decode()
     assert msg
+
+
+def test_sched_stats_struct_layout_matches_header():
+    txt = open(os.path.join(ROOT, "include", "s2k.h")).read()
+    body = re.search(r"typedef struct \{(.*?)\} s2k_sched_stats;", txt, flags=re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    names = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if decl:
+            names += [n.strip() for n in decl.split(None, 1)[1].split(",")]
+    assert names == [f for f, _ in s2k._SchedStats._fields_]
+    # 5 int64 + 3 int32, padded to 8-byte alignment
+    assert ctypes.sizeof(s2k._SchedStats) == 56
