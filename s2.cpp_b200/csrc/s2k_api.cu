@@ -60,7 +60,7 @@ s2k_status check_err_word(s2k_model *m) {
 // T: tokens per call; L: longest key range (positions) a call attends over.
 // prefill: the Slow work, whose prompt-sized calls use the tensor-core GEMM.
 cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int Hkv, int hd, int ff,
-                              int n_layers, bool prefill) {
+                              int n_layers, bool prefill, int flash_rows) {
     w.T = T;
     w.L = L;
     w.dim = dim;
@@ -99,18 +99,31 @@ cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int 
     if ((e = cudaMemset(w.lqkv, 0, tm * (w.qs + 2 * w.kvs) * 8))) return e;
     if ((e = cudaMemset(w.lattn, 0, tm * w.qs * 8))) return e;
     if ((e = cudaMemset(w.lff, 0, tm * ff * 8))) return e;
+    if (flash_rows > 0) {
+        w.fl_T = std::min(flash_rows, T);
+        w.fl_nsp = (L + kAttnSplit - 1) / kAttnSplit;
+        const size_t units = (size_t)w.fl_T * Hkv * w.fl_nsp * (H / Hkv);
+        if ((e = m->alloc(&w.fl_part, units * hd))) return e;
+        if ((e = m->alloc(&w.fl_ms, units * 2))) return e;
+        if ((e = m->alloc(&w.fl_counters, (size_t)w.fl_T * Hkv))) return e;
+        if ((e = cudaMemset(w.fl_counters, 0, (size_t)w.fl_T * Hkv * sizeof(int)))) return e;
+    }
     if (prefill && T >= kPrefillMinT && m->prefill_mma) {
         const int kmax = std::max(std::max(dim, w.qs), ff);
         if ((e = m->alloc(&w.pf_xq, tn * kmax))) return e;
         if ((e = m->alloc(&w.pf_dx, tn * kmax / 32))) return e;
-        // split-K partials of the largest split GEMM (launch_prefill_gemm's rule)
+        // split-K partials of the largest split GEMM over every call size up
+        // to T rows (launch_prefill_gemm's rule: splits from the token tiles)
         const int tt = (T + 63) / 64;
         const int shapes[4][2] = {{w.qs + 2 * w.kvs, dim}, {dim, w.qs}, {2 * ff, dim}, {dim, ff}};
         size_t need = 0;
-        for (const auto &rk : shapes) {
-            const int rb = rk[0] / 128, nkt = rk[1] / 512;
-            const int ns = std::min(8, std::min(nkt, std::max(1, m->num_sms / std::max(1, rb * tt))));
-            if (ns > 1) need = std::max(need, (size_t)ns * tn * rk[0]);
+        for (int ti = 1; ti <= tt; ++ti) {
+            const size_t rows = (size_t)std::min(T, 64 * ti);
+            for (const auto &rk : shapes) {
+                const int rb = rk[0] / 128, nkt = rk[1] / 512;
+                const int ns = std::min(8, std::min(nkt, std::max(1, m->num_sms / std::max(1, rb * ti))));
+                if (ns > 1) need = std::max(need, (size_t)ns * rows * rk[0]);
+            }
         }
         w.pf_part_n = need;
         if (need && (e = m->alloc(&w.pf_part, need))) return e;
@@ -124,7 +137,8 @@ cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int 
 void work_free(s2k_model *m, Work &w) {
     for (void *p : {(void *)w.x, (void *)w.h, (void *)w.qkv, (void *)w.attn, (void *)w.ff_buf, (void *)w.kcur,
                     (void *)w.vcur, (void *)w.scores, (void *)w.part, (void *)w.part_ms, (void *)w.counters,
-                    (void *)w.pf_xq, (void *)w.pf_dx, (void *)w.pf_part, (void *)w.pf_counters, (void *)w.lx,
+                    (void *)w.pf_xq, (void *)w.pf_dx, (void *)w.pf_part, (void *)w.pf_counters, (void *)w.fl_part,
+                    (void *)w.fl_ms, (void *)w.fl_counters, (void *)w.lx,
                     (void *)w.lh, (void *)w.lqkv, (void *)w.lattn, (void *)w.lff})
         m->release(p);
     w = Work();
@@ -138,7 +152,7 @@ s2k_status ensure_slow_work(s2k_model *m, int T, int L) {
     m->ws_gen++;
     const s2k_hparams &hp = m->hp;
     CU(work_alloc(m, m->sw, T, L, hp.embedding_length, hp.head_count, hp.head_count_kv, hp.head_dim,
-                  hp.feed_forward_length, hp.block_count, true));
+                  hp.feed_forward_length, hp.block_count, true, 1));
     return S2K_OK;
 }
 
@@ -266,6 +280,13 @@ cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         a.vcur = q.vcur;
         a.cur_base = c.cur_base;
         a.max_keys = c.max_keys;
+        if (c.T <= w.fl_T) {
+            a.fl_part = w.fl_part;
+            a.fl_ms = w.fl_ms;
+            a.fl_counters = w.fl_counters;
+            a.fl_nsp = w.fl_nsp;
+        }
+        a.num_sms = m->num_sms;
         a.scores = w.scores;
         a.ld_scores = w.L;
         a.out = w.attn;
@@ -716,7 +737,7 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     if (hp.has_fast_decoder) {
         const int Tf = std::max(hp.num_codebooks, 2);
         CU(work_alloc(m, m->fw, Tf, Tf, hp.fast_embedding_length, hp.fast_head_count, hp.fast_head_count_kv,
-                      hp.fast_head_dim, hp.fast_feed_forward_length, hp.fast_block_count, false));
+                      hp.fast_head_dim, hp.fast_feed_forward_length, hp.fast_block_count, false, Tf));
         const int fkvs = hp.fast_head_count_kv * hp.fast_head_dim;
         m->fkcur.assign(hp.fast_block_count, nullptr);
         m->fvcur.assign(hp.fast_block_count, nullptr);

@@ -30,6 +30,8 @@
 #include "s2k_device.h"
 #include "s2k_kernels.h"
 
+#include <algorithm>
+
 namespace s2k {
 
 // KV pages of a batched call's sequence (constant while the sequence lives).
@@ -296,8 +298,213 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
 
 constexpr size_t kAttnSmemMax = 200 * 1024;
 
+// ---------------------------------------------------------------------------
+// Split-parallel attention for calls with few rows (decode steps, batched
+// frames): one CTA per (split i, kv head g, row t).  The CTA copies the
+// split's cached K / V rows (4 pages of 16 positions, 4 KB each per layer and
+// kv head) into shared memory with 16-byte cp.async, forms the split's
+// scores, m_i, e_j, S_i and O_i for the G query heads of kv head g, and
+// writes them to the partials; the CTA that arrives last for (t, g) combines
+// the splits in split order exactly as attn_split_kernel does.  Keys of this
+// call (positions >= the cached count) are read as f32 from kcur / vcur.
+// ---------------------------------------------------------------------------
+constexpr int kFlThreads = 128;
+
+// 16-byte chunk c of cached key row jj sits at chunk c ^ (jj & 15) of the
+// row in shared memory, so the score loop's 8-byte reads of 16 different
+// rows hit different banks.
+__device__ __forceinline__ int fl_swz(int jj, int c) { return c ^ (jj & 15); }
+
+// Most splits a flash-attention row may have (32768 positions).
+constexpr int kFlMaxSplits = 512;
+
+// e_j of the split, reused by the combine for the split weights w_i
+__host__ __device__ __forceinline__ int fl_ew(int nsp_cap) { return nsp_cap > kAttnSplit ? nsp_cap : kAttnSplit; }
+
+size_t attn_flash_smem(int G, int nsp_cap) {
+    return (size_t)2 * kAttnSplit * 128 * sizeof(__half)  // K, V tiles
+           + (size_t)G * 128 * sizeof(double)              // queries
+           + (size_t)G * fl_ew(nsp_cap) * sizeof(double)   // e_j / w_i
+           + (size_t)G * kAttnSplit * sizeof(float)        // scores
+           + 64;
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kFlThreads) attn_flash_kernel(AttnArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.done && __ldcg(a.done)) return;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int g = blockIdx.y, t = blockIdx.z;
+    const int G = a.H / a.Hkv;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __half *ks = reinterpret_cast<__half *>(smem);                  // [64][128]
+    __half *vs = ks + kAttnSplit * 128;                              // [64][128]
+    const int EW = fl_ew(a.fl_nsp);
+    double *qs = reinterpret_cast<double *>(vs + kAttnSplit * 128);  // [G][128]
+    double *es = qs + G * 128;                                       // [G][EW]
+    float *ss = reinterpret_cast<float *>(es + G * EW);              // [G][64]
+    int *flag = reinterpret_cast<int *>(ss + G * kAttnSplit);
+    int nc, Lk;
+    KvPaged kv = a.kv;
+    const float *kc = a.kcur, *vc = a.vcur;
+    if (a.rows) {
+        const BatchRow r = a.rows[t];
+        const SeqDev *sd = a.seqs ? a.seqs[r.slot] : nullptr;
+        nc = sd ? __ldcg(&sd->state.n_past) : 0;
+        if (sd) kv = seq_kv(sd);
+        kc += (size_t)r.cur_lo * a.Hkv * 128;
+        vc += (size_t)r.cur_lo * a.Hkv * 128;
+        Lk = nc + r.cur_hi - r.cur_lo + 1;
+    } else {
+        nc = a.n_cached ? __ldcg(a.n_cached) : 0;
+        Lk = nc + a.cur_base + t + 1;
+    }
+    const int nsp = (Lk + kAttnSplit - 1) / kAttnSplit;
+    if (Lk < 1 || nsp > a.fl_nsp || Lk > a.max_keys || (nc > 0 && (nc - 1) / kPage >= kv.n_pages)) {
+        if (tid == 0 && blockIdx.x == 0 && a.err) atomicOr(a.err, ERR_BAD_POS);
+        return;
+    }
+    // splits blockIdx.x, blockIdx.x + gridDim.x, ... of this row
+    int done_splits = 0;
+    for (int i = blockIdx.x; i < nsp; i += gridDim.x, ++done_splits) {
+        const int j0 = i * kAttnSplit, cnt = min(kAttnSplit, Lk - j0);
+        const int ncache = max(0, min(cnt, nc - j0));  // cached keys of the split: [0, ncache)
+        // cached K / V rows: 16 chunks of 16 bytes per row
+        for (int c = tid; c < ncache * 16; c += kFlThreads) {
+            const int jj = c >> 4, ch = c & 15, j = j0 + jj;
+            const int page = __ldcg(kv.block_table + j / kPage);
+            const size_t off = ((((size_t)page * kv.n_layers + a.layer) * kv.n_kv_heads + g) * kPage + j % kPage) * 128 + ch * 8;
+            cp_async16(ks + jj * 128 + fl_swz(jj, ch) * 8, kv.k + off);
+            cp_async16(vs + jj * 128 + fl_swz(jj, ch) * 8, kv.v + off);
+        }
+        if (done_splits == 0)
+            for (int p = tid; p < G * 128; p += kFlThreads)
+                qs[p] = (double)__ldcg(a.q + (size_t)t * a.ldq + (size_t)g * G * 128 + p);
+        cp_async_wait_all();
+        __syncthreads();
+        // scores: thread -> key jj = tid % 64, heads h = tid / 64, tid / 64 + 2, ...
+        {
+            const int jj = tid & (kAttnSplit - 1);
+            if (jj < cnt) {
+                for (int h = tid >> 6; h < G; h += kFlThreads / kAttnSplit) {
+                    double acc = 0.0;
+                    if (jj < ncache) {
+#pragma unroll 4
+                        for (int c = 0; c < 16; ++c) {
+                            const uint4 raw = *reinterpret_cast<const uint4 *>(ks + jj * 128 + fl_swz(jj, c) * 8);
+                            const __half2 *hv = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const float2 f = __half22float2(hv[u]);
+                                acc += (double)f.x * qs[h * 128 + c * 8 + 2 * u];
+                                acc += (double)f.y * qs[h * 128 + c * 8 + 2 * u + 1];
+                            }
+                        }
+                    } else {
+                        const float *kr = kc + ((size_t)(j0 + jj - nc) * a.Hkv + g) * 128;
+                        for (int d = 0; d < 128; d += 4) {
+                            const float4 f = __ldcg(reinterpret_cast<const float4 *>(kr + d));
+                            acc += (double)f.x * qs[h * 128 + d];
+                            acc += (double)f.y * qs[h * 128 + d + 1];
+                            acc += (double)f.z * qs[h * 128 + d + 2];
+                            acc += (double)f.w * qs[h * 128 + d + 3];
+                        }
+                    }
+                    ss[h * kAttnSplit + jj] = __fmul_rn((float)acc, a.scale);
+                }
+            }
+        }
+        __syncthreads();
+        // split maximum, exponentials and their sum: warp w handles heads w, w + 4, ...
+        double *ms_out = a.fl_ms + ((((size_t)t * a.Hkv + g) * a.fl_nsp + i) * G) * 2;
+        for (int h = warp; h < G; h += kFlThreads / 32) {
+            float mx = -INFINITY;
+            for (int jj = lane; jj < cnt; jj += 32) mx = fmaxf(mx, ss[h * kAttnSplit + jj]);
+            mx = warp_max(mx);
+            double se = 0.0;
+            for (int jj = lane; jj < kAttnSplit; jj += 32) {
+                const float e = jj < cnt ? det_expf(__fsub_rn(ss[h * kAttnSplit + jj], mx)) : 0.f;
+                es[h * EW + jj] = (double)e;
+                se += (double)e;
+            }
+            se = warp_sum_d(se);
+            if (lane == 0) {
+                ms_out[h * 2] = (double)mx;
+                ms_out[h * 2 + 1] = se;
+            }
+        }
+        __syncthreads();
+        // O_i: thread owns dimension d = tid of every head
+        double *po = a.fl_part + (((size_t)t * a.Hkv + g) * a.fl_nsp + i) * G * 128;
+        {
+            double o[kMaxGroup];
+#pragma unroll
+            for (int h = 0; h < kMaxGroup; ++h) o[h] = 0.0;
+            const int d = tid;
+            for (int jj = 0; jj < cnt; ++jj) {
+                float v;
+                if (jj < ncache) v = __half2float(vs[jj * 128 + fl_swz(jj, d >> 3) * 8 + (d & 7)]);
+                else v = __ldcg(vc + ((size_t)(j0 + jj - nc) * a.Hkv + g) * 128 + d);
+                const double vd = (double)v;
+#pragma unroll
+                for (int h = 0; h < kMaxGroup; ++h)
+                    if (h < G) o[h] += vd * es[h * EW + jj];
+            }
+#pragma unroll
+            for (int h = 0; h < kMaxGroup; ++h)
+                if (h < G) po[h * 128 + d] = o[h];
+        }
+        __syncthreads();  // shared tiles are refilled by the next split
+    }
+    if (done_splits == 0) return;
+    // the last split of (t, g) to arrive combines
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        int *ctr = a.fl_counters + (size_t)t * a.Hkv + g;
+        const int prev = atomicAdd(ctr, done_splits);
+        *flag = prev + done_splits == nsp;
+        if (prev + done_splits == nsp) *ctr = 0;
+    }
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    const double *pall = a.fl_part + (((size_t)t * a.Hkv + g) * a.fl_nsp) * G * 128;
+    const double *msall = a.fl_ms + (((size_t)t * a.Hkv + g) * a.fl_nsp) * G * 2;
+    // split weights w_i = det_expf(m_i - M) per head, into es ([G][nsp] <= [G][EW])
+    for (int h = warp; h < G; h += kFlThreads / 32) {
+        float M = -INFINITY;
+        for (int k = lane; k < nsp; k += 32) M = fmaxf(M, (float)__ldcg(msall + ((size_t)k * G + h) * 2));
+        M = warp_max(M);
+        for (int k = lane; k < nsp; k += 32)
+            es[h * EW + k] = (double)det_expf(__fsub_rn((float)__ldcg(msall + ((size_t)k * G + h) * 2), M));
+    }
+    __syncthreads();
+    const int d = tid;
+    for (int h = 0; h < G; ++h) {
+        double acc = 0.0, ssum = 0.0;
+        for (int k = 0; k < nsp; ++k) {
+            const double wi = es[h * EW + k];
+            acc += __ldcg(pall + ((size_t)k * G + h) * 128 + d) * wi;
+            ssum += __ldcg(msall + ((size_t)k * G + h) * 2 + 1) * wi;
+        }
+        a.out[(size_t)t * a.H * 128 + (size_t)(g * G + h) * 128 + d] = (float)(acc / ssum);
+    }
+}
+
 cudaError_t attn_setup() {
-    return cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmemMax);
+    cudaError_t e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kAttnSmemMax);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(attn_flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)attn_flash_smem(kMaxGroup, kFlMaxSplits));
 }
 
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
@@ -305,6 +512,17 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
     if (a.hd != 128 || G < 1 || a.H % a.Hkv != 0 || G > kMaxGroup || !a.scores || a.max_keys < 1)
         return cudaErrorInvalidValue;
     const int nsp = (a.max_keys + kAttnSplit - 1) / kAttnSplit;
+    if (a.fl_part && a.fl_ms && a.fl_counters && nsp <= a.fl_nsp && a.fl_nsp <= kFlMaxSplits) {
+        cudaLaunchAttribute attr[1];
+        // CTAs per (kv head, row): enough for ~8 CTAs per SM, each taking
+        // every gx-th split of its row
+        const int want = (8 * a.num_sms + a.Hkv * a.T - 1) / (a.Hkv * a.T);
+        const int gx = std::max(1, std::min(nsp, want));
+        cudaLaunchConfig_t cfg =
+            pdl_cfg(dim3(gx, a.Hkv, a.T), dim3(kFlThreads), attn_flash_smem(G, a.fl_nsp), st, attr);
+        count_launch();
+        return cudaLaunchKernelEx(&cfg, attn_flash_kernel, a);
+    }
     const size_t smem = attn_split_smem(G, nsp);
     if (smem > kAttnSmemMax) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];

@@ -88,7 +88,7 @@ static s2k_status ensure_batch(s2k_model *m, int cap, int L) {
     b->S = std::max(hp.num_codebooks, 2);
     const int S = b->S;
     CU(work_alloc(m, b->slow, cap, L, hp.embedding_length, hp.head_count, hp.head_count_kv, hp.head_dim,
-                  hp.feed_forward_length, hp.block_count, true));
+                  hp.feed_forward_length, hp.block_count, true, cap));
     CU(m->alloc(&b->logits, (size_t)cap * hp.vocab_size));
     CU(m->alloc(&b->hidden, (size_t)cap * hp.embedding_length));
     CU(m->alloc(&b->seqs, (size_t)cap));
@@ -99,7 +99,7 @@ static s2k_status ensure_batch(s2k_model *m, int cap, int L) {
     CU(cudaMemcpy(b->rows_slow, rs.data(), rs.size() * sizeof(BatchRow), cudaMemcpyHostToDevice));
     if (hp.has_fast_decoder) {
         CU(work_alloc(m, b->fast, 2 * cap, S, hp.fast_embedding_length, hp.fast_head_count, hp.fast_head_count_kv,
-                      hp.fast_head_dim, hp.fast_feed_forward_length, hp.fast_block_count, true));
+                      hp.fast_head_dim, hp.fast_feed_forward_length, hp.fast_block_count, true, 2 * cap));
         const size_t fkvs = (size_t)hp.fast_head_count_kv * hp.fast_head_dim;
         b->fk.assign(hp.fast_block_count, nullptr);
         b->fv.assign(hp.fast_block_count, nullptr);

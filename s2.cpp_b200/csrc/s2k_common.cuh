@@ -62,19 +62,25 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Polls of a bounded wait between looks at the error word: that look is a
+// global-memory round trip, so it stays off the fast path of a wait.
+constexpr unsigned kErrPollEvery = 64;
+
 // Bounded wait on an mbarrier phase.  Returns false (and sets `code` in *err)
-// when the limit is reached.
+// when the limit is reached.  Once some wait has timed out (an error flag is
+// set), the copies the others wait for will not come either: they give up at
+// their next look at the error word instead of each spending the full limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     if (mbar_test(bar, parity)) return true;
-    // once a wait has timed out, the copies it waited for will not come:
-    // later waits give up at once instead of each spending the full limit
-    if (err && (*reinterpret_cast<volatile int *>(err) & (ERR_WAIT_FULL | ERR_WAIT_EMPTY | ERR_GRID))) return false;
     const long long t0 = clock64();
-    while (!mbar_test(bar, parity)) {
+    for (unsigned it = 1; !mbar_test(bar, parity); ++it) {
         if (clock64() - t0 > kWaitLimitCycles) {
             if (err) atomicOr(err, code);
             return false;
         }
+        if (err && it % kErrPollEvery == 0 &&
+            (*reinterpret_cast<volatile int *>(err) & (ERR_WAIT_FULL | ERR_WAIT_EMPTY | ERR_GRID)))
+            return false;
     }
     return true;
 }

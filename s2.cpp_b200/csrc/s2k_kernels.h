@@ -146,6 +146,14 @@ struct AttnArgs {
     // seqs; none without) and to kcur / vcur rows [cur_lo, cur_hi] of rows[t]
     const BatchRow *rows = nullptr;
     SeqDev *const *seqs = nullptr;
+    // split-parallel path (one CTA per (split, kv head, row)): per-split
+    // partials O_i [T][Hkv][fl_nsp][G][hd] and (m_i, S_i) [T][Hkv][fl_nsp][G][2],
+    // arrival counters [T][Hkv] (zero between launches); null = one CTA per
+    // (kv head, row)
+    double *fl_part = nullptr, *fl_ms = nullptr;
+    int *fl_counters = nullptr;
+    int fl_nsp = 0;
+    int num_sms = 148;
     const int *done = nullptr;
     int *err = nullptr;
 };

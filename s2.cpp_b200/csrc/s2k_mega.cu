@@ -132,12 +132,12 @@ __device__ __forceinline__ float4 ll_wait4(const void *base, size_t i, uint32_t 
     };
     if (!load()) {
         const long long t0 = clock64();
-        while (!load()) {
-            if (clock64() - t0 > kWaitLimitCycles || (*reinterpret_cast<volatile int *>(err) & ERR_GRID)) {
+        for (unsigned it = 1; !load(); ++it) {
+            if (clock64() - t0 > kWaitLimitCycles ||
+                (it % kErrPollEvery == 0 && (*reinterpret_cast<volatile int *>(err) & ERR_GRID))) {
                 atomicOr(err, ERR_GRID);
                 break;
             }
-            __nanosleep(32);
         }
     }
     return make_float4(__uint_as_float((uint32_t)w0), __uint_as_float((uint32_t)w1), __uint_as_float((uint32_t)w2),

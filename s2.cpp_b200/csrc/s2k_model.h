@@ -51,11 +51,18 @@ struct Work {
     double *pf_dx = nullptr, *pf_part = nullptr;
     size_t pf_part_n = 0;
     int *pf_counters = nullptr;
+    // split-parallel attention (calls of up to fl_T rows): per-split partials
+    double *fl_part = nullptr, *fl_ms = nullptr;
+    int *fl_counters = nullptr;
+    int fl_T = 0, fl_nsp = 0;
 };
 
 // Tokens per call from which the Slow stack's Q8_0 GEMMs run on the tensor
 // cores (s2k_prefill.cu) instead of the tile GEMV.
-constexpr int kPrefillMinT = 8;
+#ifndef S2K_PREFILL_MIN_T
+#define S2K_PREFILL_MIN_T 8
+#endif
+constexpr int kPrefillMinT = S2K_PREFILL_MIN_T;
 // Most tokens of one persistent-kernel call (the first Fast-AR pass: hidden + code 0).
 constexpr int kMegaTokens = 2;
 
@@ -186,8 +193,9 @@ int cuda_set(int dev);
 s2k_status check_err_word(s2k_model *m);
 // T: tokens per call; L: longest key range (positions) a call attends over.
 // prefill: also the buffers of the tensor-core GEMM path (T >= kPrefillMinT).
+// flash_rows: calls of up to this many rows use the split-parallel attention.
 cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int Hkv, int hd, int ff, int n_layers,
-                       bool prefill);
+                       bool prefill, int flash_rows = 0);
 void work_free(s2k_model *m, Work &w);
 s2k_status ensure_slow_work(s2k_model *m, int T, int L);
 cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool prefill);

@@ -43,9 +43,9 @@ namespace s2k {
 constexpr int kPM = 128;                 // weight rows per CTA tile (MMA M)
 constexpr int kPN = 64;                  // tokens per CTA tile (MMA N)
 constexpr int kPKC = 128;                // K columns per stage (4 Q8_0 blocks, one 128-byte swizzle row)
-constexpr int kPStages = 4;
-constexpr int kPThreads = 320;           // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr int kPEpiWarps = 8;
+constexpr int kPStages = 8;
+constexpr int kPEpiWarps = 16;
+constexpr int kPThreads = (2 + kPEpiWarps) * 32;  // warp 0 TMA, warp 1 MMA, warps 2..17 epilogue
 constexpr int kPTmemCols = 512;          // 2 buffers x 4 blocks x 64 columns
 constexpr uint32_t kPStageA = kPM * kPKC;  // 16 KB
 constexpr uint32_t kPStageB = kPN * kPKC;  // 8 KB
@@ -122,6 +122,15 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
     asm volatile(
@@ -220,14 +229,23 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
     } else {
         // ---------------- epilogue ----------------
-        const int q = warp & 3, h = (warp - 2) >> 2;
+        // Epilogue warp e = warp - 2 reads TMEM lane quarter q = warp % 4
+        // (weight rows 32q .. 32q+31, one per lane).  The tile's existing
+        // tokens are cut into TQ groups of 16 and the 4 blocks of a chunk
+        // into BS = 4 / TQ phases, so all 16 warps work whatever the token
+        // count: warp e takes token group e/4 % TQ and the blocks b with
+        // b % BS == e/4 / TQ.  Phase partials are added in phase order at the
+        // end (block terms are exact, their double sums order-free).
+        const int q = warp & 3, h4 = (warp - 2) >> 2;
         const int row_local = q * 32 + lane;
-        // tokens of this warp's half that exist (warp-uniform): the terms of
-        // the padding columns of a short token tile are skipped in groups of 8
-        const int nvalid = min(32, max(0, p.T - (t0 + 32 * h)));
-        double acc[32];
+        const int nv_tile = min(kPN, p.T - t0);
+        const int TQ = nv_tile <= 16 ? 1 : (nv_tile <= 32 ? 2 : 4);
+        const int BS = 4 / TQ;
+        const int tg = h4 % TQ, bp = h4 / TQ;
+        const int nvalid = min(16, max(0, nv_tile - 16 * tg));  // warp-uniform
+        double acc[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[j] = 0.0;
+        for (int j = 0; j < 16; ++j) acc[j] = 0.0;
         for (int i = 0; i < nchunk && ok; ++i) {
             const int buf = i & 1, ti = i >> 2, sb = ti & 1;
             if ((i & 3) == 0) ok = mbar_wait(&sm.sfull[sb], (ti >> 1) & 1, p.err, ERR_WAIT_FULL);
@@ -235,18 +253,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
             if (!ok) break;
             tc_fence_after();
             if (nvalid > 0) {
-#pragma unroll
-                for (int blk = 0; blk < 4; ++blk) {
+                for (int blk = bp; blk < 4; blk += BS) {
                     const int b = (i & 3) * 4 + blk;
-                    int s[32];
-                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * 256 + blk * kPN + 32 * h, s);
+                    int s[16];
+                    tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + buf * 256 + blk * kPN + 16 * tg, s);
                     const double dwr = (double)__half2float(sm.dw[sb][row_local][b]);
+                    const double *dxc = &sm.dx[sb][16 * tg][b];
 #pragma unroll
-                    for (int g8 = 0; g8 < 4; ++g8)
+                    for (int g8 = 0; g8 < 2; ++g8)
                         if (8 * g8 < nvalid) {
 #pragma unroll
                             for (int j = 8 * g8; j < 8 * g8 + 8; ++j)
-                                acc[j] = fma(i2d_exact(s[j]), dwr * sm.dx[sb][32 * h + j][b], acc[j]);
+                                acc[j] = fma(i2d_exact(s[j]), dwr * dxc[j * 16], acc[j]);
                         }
                 }
             }
@@ -257,26 +275,44 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 if ((i & 3) == 3 || i == nchunk - 1) mbar_arrive(&sm.sempty[sb]);
             }
         }
+        // ---------------- phase partials ----------------
+        // (the stage buffers are idle: every copy was consumed by an MMA whose
+        // completion every epilogue warp has waited for)
+        double *red = reinterpret_cast<double *>(&sm.a[0][0]);  // [16 warps][16 tokens][32 lanes]
+        if (BS > 1) {
+            if (bp > 0)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) red[((warp - 2) * 16 + j) * 32 + lane] = acc[j];
+            named_sync(1, kPEpiWarps * 32);
+            if (bp == 0)
+                for (int ph = 1; ph < BS; ++ph) {
+                    const int we = (ph * TQ + tg) * 4 + ((warp - 2) & 3);  // epilogue warp of (q, tg, ph)
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[j] += red[(we * 16 + j) * 32 + lane];
+                }
+        }
         // ---------------- output ----------------
         const int row = rb * kPM + row_local;
-        if (p.nsplit == 1) {
+        if (bp == 0 && nvalid > 0) {
+            if (p.nsplit == 1) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int t = t0 + 32 * h + j;
-                if (p.epi == EPI_SWIGLU) {
-                    const double up = __shfl_down_sync(0xffffffffu, acc[j], 1);
-                    if ((lane & 1) == 0 && t < p.T)
-                        p.y[(size_t)t * p.ldy + row / 2] = __fmul_rn(silu((float)acc[j]), (float)up);
-                } else if (t < p.T) {
-                    const float v = (float)acc[j];
-                    p.y[(size_t)t * p.ldy + row] = p.res ? __fadd_rn(p.res[(size_t)t * p.ldres + row], v) : v;
+                for (int j = 0; j < 16; ++j) {
+                    const int t = t0 + 16 * tg + j;
+                    if (p.epi == EPI_SWIGLU) {
+                        const double up = __shfl_down_sync(0xffffffffu, acc[j], 1);
+                        if ((lane & 1) == 0 && j < nvalid)
+                            p.y[(size_t)t * p.ldy + row / 2] = __fmul_rn(silu((float)acc[j]), (float)up);
+                    } else if (j < nvalid) {
+                        const float v = (float)acc[j];
+                        p.y[(size_t)t * p.ldy + row] = p.res ? __fadd_rn(p.res[(size_t)t * p.ldres + row], v) : v;
+                    }
                 }
-            }
-        } else {
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int t = t0 + 32 * h + j;
-                if (t < p.T) p.part[((size_t)split * p.T + t) * p.R + row] = acc[j];
+                for (int j = 0; j < 16; ++j) {
+                    const int t = t0 + 16 * tg + j;
+                    if (j < nvalid) p.part[((size_t)split * p.T + t) * p.R + row] = acc[j];
+                }
             }
         }
     }
@@ -292,10 +328,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
         __syncthreads();
         if (sm.last && warp >= 2) {
             __threadfence();
-            const int q = warp & 3, h = (warp - 2) >> 2;
+            // epilogue warp (q, g): rows 32q + lane, tokens 16g .. 16g + 15 of the tile
+            const int q = warp & 3, g = (warp - 2) >> 2;
             const int row = rb * kPM + q * 32 + lane;
-            for (int j = 0; j < 32; ++j) {
-                const int t = t0 + 32 * h + j;
+            for (int j = 0; j < 16; ++j) {
+                const int t = t0 + 16 * g + j;
                 double sum = 0.0;
                 if (t < p.T)
                     for (int k = 0; k < p.nsplit; ++k) sum += __ldcg(p.part + ((size_t)k * p.T + t) * p.R + row);
@@ -321,8 +358,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
 // ---------------------------------------------------------------------------
 // activation rows -> Q8_0 (int8 [T][K] + double block scales [T][K/32])
 // ---------------------------------------------------------------------------
-// One CTA per token row; the arithmetic of the GEMV prologue (RMSNorm of
-// rms_norm_weighted when norm_w is given, ggml x86 quantize_row_q8_0).
+// Grid (token row, chunk of kQBlocks blocks); the arithmetic of the GEMV
+// prologue (RMSNorm of rms_norm_weighted when norm_w is given, ggml x86
+// quantize_row_q8_0).  Every CTA of a row forms the row's sum of squares
+// itself (an L2 re-read of the row) so the chunks need no second launch.
+constexpr int kQBlocks = 32;
+
 __global__ void __launch_bounds__(256) quant_rows_q8_kernel(const float *x, int ldx, int K, const float *norm_w,
                                                            float eps, int8_t *xq, double *dx, float *act_out) {
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -331,9 +372,10 @@ __global__ void __launch_bounds__(256) quant_rows_q8_kernel(const float *x, int 
     float sc = 1.f;
     if (norm_w != nullptr) {
         double s = 0.0;
-        for (int i = tid; i < K; i += 256) {
-            const float v = __ldcg(row + i);
-            s += (double)__fmul_rn(v, v);
+        for (int i = tid * 4; i < K; i += 256 * 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(row + i));
+            s += (double)__fmul_rn(v.x, v.x) + (double)__fmul_rn(v.y, v.y);
+            s += (double)__fmul_rn(v.z, v.z) + (double)__fmul_rn(v.w, v.w);
         }
         s = warp_sum_d(s);
         if (lane == 0) red[warp] = s;
@@ -343,8 +385,9 @@ __global__ void __launch_bounds__(256) quant_rows_q8_kernel(const float *x, int 
         const float mean = (float)(tot / (double)K);
         sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
     }
-    // lane owns one value of a 32-value block; warp w handles blocks w, w + 8, ...
-    for (int b = warp; b < K / 32; b += 8) {
+    // lane owns one value of a 32-value block; warp w handles blocks w, w + 8, ... of the chunk
+    const int b0 = blockIdx.y * kQBlocks, b1 = min(K / 32, b0 + kQBlocks);
+    for (int b = b0 + warp; b < b1; b += 8) {
         float v = __ldcg(row + b * 32 + lane);
         if (norm_w != nullptr) v = __fmul_rn(__fmul_rn(v, sc), __ldg(norm_w + b * 32 + lane));
         if (act_out != nullptr) act_out[(size_t)t * K + b * 32 + lane] = v;
@@ -446,9 +489,10 @@ cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st) {
 
 cudaError_t launch_quant_rows_q8(const float *x, int ldx, int T, int K, const float *norm_w, float eps, int8_t *xq,
                                  double *dx, float *act_out, cudaStream_t st) {
-    if (K % 32 != 0 || T < 1) return cudaErrorInvalidValue;
+    if (K % 32 != 0 || T < 1 || ldx % 4 != 0 || reinterpret_cast<uintptr_t>(x) % 16 != 0) return cudaErrorInvalidValue;
     count_launch();
-    quant_rows_q8_kernel<<<T, 256, 0, st>>>(x, ldx, K, norm_w, eps, xq, dx, act_out);
+    const int nch = (K / 32 + kQBlocks - 1) / kQBlocks;
+    quant_rows_q8_kernel<<<dim3(T, nch), 256, 0, st>>>(x, ldx, K, norm_w, eps, xq, dx, act_out);
     return cudaGetLastError();
 }
 

@@ -217,12 +217,12 @@ __device__ __forceinline__ F8 ll_wait8(const void *p, uint32_t tag, int *err) {
     F8 out;
     if (ll_load8(p, tag, out)) return out;
     const long long t0 = clock64();
-    while (!ll_load8(p, tag, out)) {
-        if (clock64() - t0 > kWaitLimitCycles || (err && (*reinterpret_cast<volatile int *>(err) & ERR_GRID))) {
+    for (unsigned it = 1; !ll_load8(p, tag, out); ++it) {
+        if (clock64() - t0 > kWaitLimitCycles ||
+            (err && it % kErrPollEvery == 0 && (*reinterpret_cast<volatile int *>(err) & ERR_GRID))) {
             if (err) atomicOr(err, ERR_GRID);
             break;
         }
-        __nanosleep(32);
     }
     return out;
 }
@@ -232,12 +232,13 @@ __device__ __forceinline__ float ll_wait1(const void *p, size_t i, uint32_t tag,
     uint64_t w = __ldcg(reinterpret_cast<const unsigned long long *>(q));
     if ((uint32_t)(w >> 32) != tag) {
         const long long t0 = clock64();
+        unsigned it = 0;
         do {
-            if (clock64() - t0 > kWaitLimitCycles || (err && (*reinterpret_cast<volatile int *>(err) & ERR_GRID))) {
+            if (clock64() - t0 > kWaitLimitCycles ||
+                (err && ++it % kErrPollEvery == 0 && (*reinterpret_cast<volatile int *>(err) & ERR_GRID))) {
                 if (err) atomicOr(err, ERR_GRID);
                 break;
             }
-            __nanosleep(32);
             w = __ldcg(reinterpret_cast<const unsigned long long *>(q));
         } while ((uint32_t)(w >> 32) != tag);
     }
