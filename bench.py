@@ -14,6 +14,12 @@ utterance with no collective on the data path (request-level sharding,
 synchronize on both sides, max over ranks.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python bench.py --workload ragged [--utterances 64] [--steps 1] [--warmup 1]
+
+--workload ragged measures continuous batching instead: 64 utterances
+(prompts ~U[64, 1024] tokens, ~U[100, 1500] frames, stop by length) dealt
+round-robin to the GPUs, each GPU decoding its share as one continuously
+refilled batch (s2k_sched_*); frames/s over the whole job, prefills included.
 """
 from __future__ import annotations
 
@@ -185,6 +191,126 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+RAGGED_UTTS = 64
+RAGGED_METRIC = "codec frames/s, continuous ragged batching (Q8_0), aggregate over GPUs"
+
+
+def ragged_requests(hp, n_utts: int, frames_scale: float = 1.0):
+    """The continuous-batching workload: n_utts independent utterances with
+    seeded prompt lengths ~U[64, 1024] and target frame counts ~U[100, 1500]
+    (scaled by frames_scale), stop by length (no end token)."""
+    rng = np.random.default_rng(SEED)
+    out = []
+    for i in range(n_utts):
+        cols = int(rng.integers(64, 1025))
+        frames = max(1, int(round(int(rng.integers(100, 1501)) * frames_scale)))
+        prompt = synthetic.text_prompt(hp, cols, seed=SEED + 17 * i)
+        out.append((i, prompt, frames))
+    return out
+
+
+def run_ragged(args, rank: int, world: int, local: int) -> None:
+    """Continuous ragged batching: the utterances are dealt round-robin to the
+    ranks; each rank's scheduler admits, prefills and decodes its share as one
+    continuously refilled batch over a 16-token-page KV pool."""
+    import torch
+    import torch.distributed as dist
+    import s2k  # noqa: E402
+
+    dist_on = world > 1
+    if dist_on:
+        torch.cuda.set_device(local)
+        shard.init("nccl", local, timeout_s=600)
+    torch.cuda.set_device(local)
+    hp = synthetic.preset(args.preset)
+    threads = max(1, (os.cpu_count() or 8) // max(world, 1))
+    tensors = build_weights(hp, threads, args.quant)
+    m = s2k.SlowARModel(hp, device=local)
+    m.load_tensors(tensors)
+    del tensors
+    reqs = [r for r in ragged_requests(hp, args.utterances, args.frames_scale) if r[0] % world == rank]
+    max_len = max(p.shape[1] + f + 1 for _, p, f in reqs)
+    stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
+    kw = dict(temperature=0.0, top_p=0.8, top_k=30, im_end_id=-1, seed=SEED)
+
+    def job(rs, sched):
+        for i, p, f in rs:
+            sched.submit(p, f, seq_id=i, **kw)
+        sched.run()
+
+    sc = s2k.BatchScheduler(m, max_batch=len(reqs), max_seq_len=max_len)
+    # warm-up: every batch size once (one more request finishes each frame),
+    # so the timed run instantiates no frame graph
+    warm = [(i, synthetic.text_prompt(hp, 16, seed=i), i + 1) for i in range(len(reqs))]
+    for _ in range(args.warmup):
+        job(warm, sc)
+    torch.cuda.synchronize()
+    if dist_on:
+        dist.barrier()
+    st0 = sc.stats()
+    clocks = Clocks(local)
+    s2k.launch_count(reset=True)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        job(reqs, sc)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    wall_ms = (time.perf_counter() - t_wall) * 1e3
+    launches = s2k.launch_count()
+    clk = clocks.stop()
+    st1 = sc.stats()
+    ms = ev0.elapsed_time(ev1)
+    frames_rank = sum(f for _, _, f in reqs) * args.steps
+    assert st1["frames"] - st0["frames"] == frames_rank, (st1, st0, frames_rank)
+    if dist_on:
+        dist.barrier()
+    ms_max = shard.max_over_ranks(ms, f"cuda:{local}")
+    wall_max = shard.max_over_ranks(wall_ms, f"cuda:{local}")
+    frames_all = sum(f for _, _, f in ragged_requests(hp, args.utterances, args.frames_scale)) * args.steps
+    value = frames_all / (ms_max / 1e3)
+    e2e = frames_all / (wall_max / 1e3)
+    slow_b, fast_b = weight_stream_bytes(hp, args.quant)
+    kv_per_pos = hp.block_count * 2 * hp.head_count_kv * hp.head_dim * 2
+    steps_run = st1["steps"] - st0["steps"]
+    dec_bytes = steps_run * (slow_b + (hp.num_codebooks - 1) * fast_b) + (st1["kv_positions"] - st0["kv_positions"]) * kv_per_pos
+    pk = peaks()
+    res = sc.result(len(warm) * args.warmup)  # first timed request: shape check
+    assert res.shape == (hp.num_codebooks, reqs[0][2]), res.shape
+    sc.close()
+    m.close()
+    if rank == 0:
+        line = {
+            "metric": RAGGED_METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": args.quant, "data": "synthetic",
+            "config": {"workload": (f"{args.utterances} utterances, prompts ~U[64,1024] tokens, frames ~U[100,1500]"
+                                    f" x{args.frames_scale:g}, stop by length, S2 Pro shape, {args.quant}; round-robin "
+                                    f"over {world} GPU(s), one continuous batch per GPU, 16-token KV pages"),
+                       "utterances": args.utterances, "frames_total": frames_all // args.steps,
+                       "max_batch_per_gpu": st1["max_live"],
+                       "l2": "inputs larger than L2 (4.3 GB of Slow weights per batched frame)",
+                       "parallelism": f"request-level x{world}, no collectives"},
+            "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": int(sum(p.nbytes for _, p, _ in reqs)),
+                    "d2h_bytes_per_step": int(4 * hp.num_codebooks * frames_rank // args.steps),
+                    "note": "host prompts in, host codes out through s2k_sched_*; wall clock"},
+            "frame_roofline": {"achieved": dec_bytes / (ms / 1e3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                               "frac": dec_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"],
+                               "bytes": dec_bytes, "batched_frames": steps_run,
+                               "note": "weights once per batched frame + f16 KV of every live sequence, over the "
+                                       "whole job's time (prefill included)"},
+            "prefill_tokens": st1["prefill_tokens"] - st0["prefill_tokens"],
+            "clocks": clk,
+            "gpu_launches": int(launches),
+        }
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -199,6 +325,12 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--preset", choices=["s2pro", "mid"], default="s2pro",
                     help="model shape; 'mid' (2+1 layers, real widths) is for small profiler captures only")
+    ap.add_argument("--workload", choices=["frames", "ragged"], default="frames",
+                    help="frames: one utterance per GPU at batch 1 (default); ragged: continuous batching of "
+                         "--utterances utterances dealt round-robin to the GPUs")
+    ap.add_argument("--utterances", type=int, default=RAGGED_UTTS)
+    ap.add_argument("--frames-scale", type=float, default=1.0,
+                    help="ragged: scale of the target frame counts (1.0 = U[100, 1500])")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -207,6 +339,9 @@ def main() -> None:
 
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "ragged":
+        run_ragged(args, rank, world, local)
         return
 
     import torch

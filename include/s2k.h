@@ -299,6 +299,7 @@ typedef struct {
     int64_t frames;          /* frames produced, all requests */
     int64_t prefill_tokens;  /* prompt positions prefilled */
     int64_t admitted, finished;
+    int64_t kv_positions;    /* cached positions the batched Slow steps attended over */
     int32_t max_live;        /* largest batch so far */
     int32_t free_pages, pool_pages;
 } s2k_sched_stats;

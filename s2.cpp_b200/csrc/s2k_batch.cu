@@ -598,6 +598,7 @@ S2K_API s2k_status s2k_sched_step(s2k_sched *sc, int32_t *n_live, int32_t *n_wai
             live_slots.push_back(i);
         }
     if (!live.empty()) {
+        for (s2k_seq *s : live) sc->stats.kv_positions += s->n_past;
         rc = batch_frame_core(m, live.data(), (int)live.size());
         if (rc) return rc;
         sc->stats.steps++;

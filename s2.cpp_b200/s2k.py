@@ -75,7 +75,8 @@ class _GenParams(ctypes.Structure):
 
 class _SchedStats(ctypes.Structure):
     _fields_ = [("steps", ctypes.c_int64), ("frames", ctypes.c_int64), ("prefill_tokens", ctypes.c_int64),
-                ("admitted", ctypes.c_int64), ("finished", ctypes.c_int64), ("max_live", ctypes.c_int32),
+                ("admitted", ctypes.c_int64), ("finished", ctypes.c_int64), ("kv_positions", ctypes.c_int64),
+                ("max_live", ctypes.c_int32),
                 ("free_pages", ctypes.c_int32), ("pool_pages", ctypes.c_int32)]
 
 
