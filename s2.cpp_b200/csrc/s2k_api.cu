@@ -112,24 +112,15 @@ cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int 
         const int kmax = std::max(std::max(dim, w.qs), ff);
         if ((e = m->alloc(&w.pf_xq, tn * kmax))) return e;
         if ((e = m->alloc(&w.pf_dx, tn * kmax / 32))) return e;
-        // split-K partials of the largest split GEMM over every call size up
-        // to T rows (launch_prefill_gemm's rule: splits from the token tiles)
-        const int tt = (T + 63) / 64;
-        const int shapes[4][2] = {{w.qs + 2 * w.kvs, dim}, {dim, w.qs}, {2 * ff, dim}, {dim, ff}};
-        size_t need = 0;
-        for (int ti = 1; ti <= tt; ++ti) {
-            const size_t rows = (size_t)std::min(T, 64 * ti);
-            for (const auto &rk : shapes) {
-                const int rb = rk[0] / 128, nkt = rk[1] / 512;
-                const int ns = std::min(8, std::min(nkt, std::max(1, m->num_sms / std::max(1, rb * ti))));
-                if (ns > 1) need = std::max(need, (size_t)ns * rows * rk[0]);
-            }
-        }
-        w.pf_part_n = need;
-        if (need && (e = m->alloc(&w.pf_part, need))) return e;
-        const size_t nctr = (size_t)(2 * ff / 128 + 1) * tt + 16;
-        if ((e = m->alloc(&w.pf_counters, nctr))) return e;
-        if ((e = cudaMemset(w.pf_counters, 0, nctr * sizeof(int)))) return e;
+        // stream-K partials (one CTA per SM), and K-tile
+        // counters for every (row block, token tile) of the largest GEMM
+        w.pf_part_n = prefill_part_doubles(m->num_sms);
+        if ((e = m->alloc(&w.pf_part, w.pf_part_n))) return e;
+        const int max_rows = std::max({w.qs + 2 * w.kvs, 2 * ff, dim, m->hp.vocab_size, m->hp.codebook_size});
+        const int tt = (T + 15) / 16;
+        w.pf_n_counters = (size_t)(max_rows / 128 + 1) * tt;
+        if ((e = m->alloc(&w.pf_counters, w.pf_n_counters))) return e;
+        if ((e = cudaMemset(w.pf_counters, 0, w.pf_n_counters * sizeof(int)))) return e;
     }
     return cudaSuccess;
 }
@@ -137,7 +128,8 @@ cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int 
 void work_free(s2k_model *m, Work &w) {
     for (void *p : {(void *)w.x, (void *)w.h, (void *)w.qkv, (void *)w.attn, (void *)w.ff_buf, (void *)w.kcur,
                     (void *)w.vcur, (void *)w.scores, (void *)w.part, (void *)w.part_ms, (void *)w.counters,
-                    (void *)w.pf_xq, (void *)w.pf_dx, (void *)w.pf_part, (void *)w.pf_counters, (void *)w.fl_part,
+                    (void *)w.pf_xq, (void *)w.pf_dx, (void *)w.pf_part, (void *)w.pf_counters,
+                    (void *)w.fl_part,
                     (void *)w.fl_ms, (void *)w.fl_counters, (void *)w.lx,
                     (void *)w.lh, (void *)w.lqkv, (void *)w.lattn, (void *)w.lff})
         m->release(p);
@@ -203,6 +195,7 @@ cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool prefill) {
         a.part = w.pf_part;
         a.part_doubles = w.pf_part_n;
         a.counters = w.pf_counters;
+        a.n_counters = w.pf_n_counters;
         a.num_sms = m->num_sms;
         a.err = m->d_err;
         return launch_prefill_gemm(a, m->stream);

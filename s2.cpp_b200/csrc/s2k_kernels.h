@@ -82,13 +82,15 @@ struct PrefillArgs {
     int ldy = 0;
     const float *res = nullptr;
     int ldres = 0;
-    double *part = nullptr;  // split-K partials
+    double *part = nullptr;  // stream-K partials (>= prefill_part_doubles(num_sms))
     size_t part_doubles = 0;
-    int *counters = nullptr;  // >= (R/128) * ceil(T/64) ints, zero between launches
+    int *counters = nullptr;  // >= (R/128) * ceil(T/16) ints, zero between launches
+    size_t n_counters = 0;
     int num_sms = 148;
     int *err = nullptr;
 };
 cudaError_t prefill_setup();
+size_t prefill_part_doubles(int ctas);
 bool prefill_ok(const DevMat &w, int T);
 cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st);
 // x [T][ldx] (optional RMSNorm with norm_w, eps) -> xq [T][K] int8, dx [T][K/32]

@@ -49,7 +49,7 @@ struct Work {
     // split-K partials and arrival counters (Slow work only)
     int8_t *pf_xq = nullptr;
     double *pf_dx = nullptr, *pf_part = nullptr;
-    size_t pf_part_n = 0;
+    size_t pf_part_n = 0, pf_n_counters = 0;
     int *pf_counters = nullptr;
     // split-parallel attention (calls of up to fl_T rows): per-split partials
     double *fl_part = nullptr, *fl_ms = nullptr;

@@ -11,24 +11,26 @@
 // double and rounded to float once, as the GEMV kernels and the CPU oracle.
 // So prefill through the tensor cores is bit-compatible with the decode path.
 //
-// Structure (one CTA per SM; 128 weight rows x 64 tokens per CTA tile, split
-// over K when the tile grid is small):
+// Structure (one CTA per SM, each taking an equal run of (128 weight rows x
+// 64 tokens x 512 columns) units, stream-K; see prefill_q8_kernel):
 //   warp 0      TMA producer: weight tile slabs (4-D tensor map over the tile
 //               layout of s2k_tgemv.cuh, 128 rows x 128 columns, 128-byte
 //               swizzle), activation slabs (2-D map, 64 tokens x 128 columns),
 //               and per 512-column K-tile the weight scales (bulk copies) and
-//               activation scales (2-D map) into a 4-stage ring.  No
-//               multicast loads anywhere.
+//               activation scales (2-D map) into an 8-stage ring; the first
+//               stages' weights are requested before the previous kernel has
+//               finished (programmatic dependent launch).  No multicast loads
+//               anywhere.
 //   warp 1      MMA issuer (one elected lane): per stage four MMAs (one per
 //               32-column block) into TMEM columns of a double-buffered 4 x 64
 //               accumulator area, then tcgen05.commit to the stage's empty
 //               barrier and the TMEM buffer's full barrier.
-//   warps 2..9  epilogue: warp w reads TMEM lane quarter w % 4 (32 weight
-//               rows) and token half (w - 2) / 4 (32 tokens) with
-//               tcgen05.ld.32x32b.x32, forms the block terms in double.
-// Split-K partials go to global scratch; the last CTA of a (row block, token
-// tile) to arrive adds them in split order and runs the epilogue (residual or
-// SwiGLU), like the GEMV kernels'.
+//   warps 2..17 epilogue: warp w reads TMEM lane quarter w % 4 (32 weight
+//               rows) with tcgen05.ld.32x32b.x16 and forms the block terms in
+//               double for its share of (16-token group, block phase).
+// Partials of (row block, token tile) pairs split over CTAs go to global
+// scratch; the CTA that completes a pair adds them in K order and runs the
+// epilogue (residual or SwiGLU), like the GEMV kernels'.
 #include "s2k_common.cuh"
 #include "s2k_kernels.h"
 
@@ -48,31 +50,38 @@ constexpr int kPEpiWarps = 16;
 constexpr int kPThreads = (2 + kPEpiWarps) * 32;  // warp 0 TMA, warp 1 MMA, warps 2..17 epilogue
 constexpr int kPTmemCols = 512;          // 2 buffers x 4 blocks x 64 columns
 constexpr uint32_t kPStageA = kPM * kPKC;  // 16 KB
-constexpr uint32_t kPStageB = kPN * kPKC;  // 8 KB
-
-struct PSmem {
+// Token tile N (the MMA's N) follows the call: 16 or 32 tokens leave room for
+// 8 or 4 TMEM accumulator buffers (4 blocks x N columns each), so the MMAs
+// run that many chunks ahead of the epilogue; 64 for larger calls (2 buffers).
+template <int N>
+struct PSmemT {
+    static constexpr int kNB = kPTmemCols / (4 * N);  // TMEM buffers
+    // block-phase partials of the epilogue warps with phase > 0 (N = 16, 32)
+    static constexpr int kRed = N < 64 ? (kPEpiWarps - 4) * 16 * 32 : 1;
     alignas(1024) uint8_t a[kPStages][kPStageA];
-    alignas(1024) uint8_t b[kPStages][kPStageB];
+    alignas(1024) uint8_t b[kPStages][N * kPKC];
     alignas(128) __half dw[2][kPM][16];   // weight block scales of a 512-column K-tile
-    alignas(128) double dx[2][kPN][16];   // activation block scales of the K-tile
+    alignas(128) double dx[2][N][16];     // activation block scales of the K-tile
+    alignas(16) double red[kRed];
     uint64_t full[kPStages], empty[kPStages];
     uint64_t sfull[2], sempty[2];
-    uint64_t tfull[2], tempty[2];
+    uint64_t tfull[kNB], tempty[kNB];
     uint32_t tmem_base;
     int last;
 };
-static_assert(sizeof(PSmem) + 1024 <= 227 * 1024, "prefill GEMM shared memory");
+static_assert(sizeof(PSmemT<16>) + 1024 <= 227 * 1024, "prefill GEMM shared memory");
+static_assert(sizeof(PSmemT<32>) + 1024 <= 227 * 1024, "prefill GEMM shared memory");
+static_assert(sizeof(PSmemT<64>) + 1024 <= 227 * 1024, "prefill GEMM shared memory");
 
 struct PrefillParams {
     int R, K, T;          // weight rows, columns; tokens
-    int nsplit;           // K splits (whole 512-column K-tiles each)
     int epi;              // EPI_STORE / EPI_SWIGLU
     float *y;             // [T][ldy]
     int ldy;
     const float *res;     // optional residual [T][ldres]
     int ldres;
-    double *part;         // split partials [nsplit][T][R] (nsplit > 1)
-    int *counters;        // [R/128][token tiles], zero between launches
+    double *part;         // stream-K partials [gridDim.x][2][kPN][kPM]
+    int *counters;        // K-tiles done per (row block, token tile) [R/128][token tiles], zero between launches
     const __half *wtiles; // weight tiles (scales read by bulk copies)
     int *err;
 };
@@ -103,15 +112,17 @@ __device__ __forceinline__ uint64_t sw128_desc(const void *p) {
 }
 
 // Instruction descriptor: kind::i8, D s32, A and B signed int8, both K-major,
-// N = kPN, M = kPM.
-constexpr uint32_t kIdescI8 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPN >> 3) << 17) |
-                              ((uint32_t)(kPM >> 4) << 24);
+// N tokens, M = kPM.
+template <int N>
+constexpr uint32_t idesc_i8() {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kPM >> 4) << 24);
+}
 
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc) {
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(kIdescI8), "r"(0)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0)
         : "memory");
 }
 
@@ -150,17 +161,63 @@ __device__ __forceinline__ double i2d_exact(int s) {
     return __hiloint2double(0x43300000, (int)((unsigned)s ^ 0x80000000u)) - 4503601774854144.0;
 }
 
+// Work split (stream-K): the (row block, token tile, K-tile) units, K-tile
+// fastest, are dealt out in equal contiguous runs to one CTA per SM, so no
+// partial wave of CTAs is left when the tile count is not a multiple of the
+// SM count.  A CTA's run crosses (row block, token tile) pairs; a pair whose
+// K-tiles are split over several CTAs is finished by the CTA that completes
+// its count: it adds the CTAs' partials in K order and runs the epilogue.
+__device__ __forceinline__ void unit_of(long long u, int NKT, int TT, int &rb, int &tt, int &kt) {
+    kt = (int)(u % NKT);
+    const long long r = u / NKT;
+    tt = (int)(r % TT);
+    rb = (int)(r / TT);
+}
+// first unit of CTA c of G over U units, and the CTA holding unit u
+__device__ __forceinline__ long long ulo_of(int c, long long U, int G) { return (long long)c * U / G; }
+__device__ __forceinline__ int cta_of(long long u, long long U, int G) { return (int)(((u + 1) * G - 1) / U); }
+
+// Outputs of one weight row (this lane's) for tokens t .. t + n - 1 (n <= 8,
+// warp-uniform) from their double sums: residual add or SwiGLU of the
+// interleaved (gate, up) row pair.  Residuals are loaded before any store.
+__device__ __forceinline__ void store_rows8(const PrefillParams &p, const double (&v)[8], int t, int n, int row,
+                                            int lane) {
+    if (p.epi == EPI_SWIGLU) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const double up = __shfl_down_sync(0xffffffffu, v[j], 1);
+            if ((lane & 1) == 0 && j < n) p.y[(size_t)(t + j) * p.ldy + row / 2] = __fmul_rn(silu((float)v[j]), (float)up);
+        }
+        return;
+    }
+    float r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = (p.res && j < n) ? __ldcg(p.res + (size_t)(t + j) * p.ldres + row) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        if (j < n) {
+            const float x = (float)v[j];
+            p.y[(size_t)(t + j) * p.ldy + row] = p.res ? __fadd_rn(r[j], x) : x;
+        }
+}
+
+// 18 warps: 5 of them share a sub-partition's 16K registers, so at most 96
+// registers per thread.
+template <int N>
 __global__ void __launch_bounds__(kPThreads, 1)
     prefill_q8_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                       const __grid_constant__ CUtensorMap dxmap, PrefillParams p) {
+    using Sm = PSmemT<N>;
+    constexpr int NB = Sm::kNB;
     extern __shared__ uint8_t praw[];
-    PSmem &sm = *reinterpret_cast<PSmem *>((reinterpret_cast<uintptr_t>(praw) + 1023) & ~uintptr_t(1023));
+    Sm &sm = *reinterpret_cast<Sm *>((reinterpret_cast<uintptr_t>(praw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int rb = blockIdx.x, tt = blockIdx.y, split = blockIdx.z;
-    const int NKT = p.K / kTK;
-    const int kt0 = NKT * split / p.nsplit, kt1 = NKT * (split + 1) / p.nsplit;
-    const int nchunk = (kt1 - kt0) * (kTK / kPKC);
-    const int t0 = tt * kPN;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int NKT = p.K / kTK, TT = (p.T + N - 1) / N, RB = p.R / kPM;
+    const long long U = (long long)RB * TT * NKT;
+    const long long u_lo = ulo_of(c, U, G), u_hi = ulo_of(c + 1, U, G);
+    const int nchunk = (int)(u_hi - u_lo) * (kTK / kPKC);
+    pdl_launch_dependents();
     if (tid == 0) {
         for (int i = 0; i < kPStages; ++i) {
             mbar_init(&sm.full[i], 1);
@@ -169,6 +226,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.sfull[i], 1);
             mbar_init(&sm.sempty[i], kPEpiWarps);
+        }
+        for (int i = 0; i < NB; ++i) {
             mbar_init(&sm.tfull[i], 1);
             mbar_init(&sm.tempty[i], kPEpiWarps);
         }
@@ -189,40 +248,71 @@ __global__ void __launch_bounds__(kPThreads, 1)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            for (int i = 0; i < nchunk && ok; ++i) {
-                const int kc = kt0 * 4 + i, st = i % kPStages;
-                if ((i & 3) == 0) {  // scales of a new K-tile
-                    const int ti = i >> 2, sb = ti & 1;
-                    if (ti >= 2) ok = mbar_wait(&sm.sempty[sb], ((ti >> 1) - 1) & 1, p.err, ERR_WAIT_EMPTY);
-                    if (!ok) break;
-                    const int kt = kc >> 2;
-                    mbar_arrive_expect_tx(&sm.sfull[sb], 4 * 1024 + kPN * 16 * 8);
+            // Weight tiles and weight scales do not depend on the previous
+            // kernel: the first stages' are issued before waiting for it
+            // (programmatic dependent launch), activations and their scales
+            // after.
+            const int pre = min(nchunk, kPStages);
+            for (int i = 0; i < pre; ++i) {
+                int rb, tt, kt;
+                unit_of(u_lo + (i >> 2), NKT, TT, rb, tt, kt);
+                const int kc = kt * 4 + (i & 3), st = i;
+                if ((i & 3) == 0) {
+                    const int sb = (i >> 2) & 1;
+                    mbar_arrive_expect_tx(&sm.sfull[sb], 4 * 1024 + N * 16 * 8);
                     for (int q = 0; q < 4; ++q) {
                         const uint8_t *tile = reinterpret_cast<const uint8_t *>(p.wtiles) +
                                               ((size_t)(rb * 4 + q) * NKT + kt) * kTileBytes + kTileQ;
                         bulk_g2s_plain(&sm.dw[sb][q * 32][0], tile, 1024, &sm.sfull[sb]);
                     }
-                    tma_load_2d(&sm.dx[sb][0][0], &dxmap, kt * 16, t0, &sm.sfull[sb]);
                 }
-                if (i >= kPStages) ok = mbar_wait(&sm.empty[st], ((i / kPStages) - 1) & 1, p.err, ERR_WAIT_EMPTY);
-                if (!ok) break;
-                mbar_arrive_expect_tx(&sm.full[st], kPStageA + kPStageB);
+                mbar_arrive_expect_tx(&sm.full[st], kPStageA + N * kPKC);
                 tma_load_4d(sm.a[st], &wmap, (kc * kPKC) % kTK, 0, (kc * kPKC) / kTK, rb * 4, &sm.full[st]);
-                tma_load_2d(sm.b[st], &xmap, kc * kPKC, t0, &sm.full[st]);
+            }
+            pdl_wait();
+            for (int i = 0; i < pre; ++i) {
+                int rb, tt, kt;
+                unit_of(u_lo + (i >> 2), NKT, TT, rb, tt, kt);
+                const int kc = kt * 4 + (i & 3);
+                if ((i & 3) == 0) tma_load_2d(&sm.dx[(i >> 2) & 1][0][0], &dxmap, kt * 16, tt * N, &sm.sfull[(i >> 2) & 1]);
+                tma_load_2d(sm.b[i], &xmap, kc * kPKC, tt * N, &sm.full[i]);
+            }
+            for (int i = pre; i < nchunk && ok; ++i) {
+                int rb, tt, kt;
+                unit_of(u_lo + (i >> 2), NKT, TT, rb, tt, kt);
+                const int kc = kt * 4 + (i & 3), st = i % kPStages;
+                if ((i & 3) == 0) {  // scales of a new K-tile
+                    const int ti = i >> 2, sb = ti & 1;
+                    if (ti >= 2) ok = mbar_wait(&sm.sempty[sb], ((ti >> 1) - 1) & 1, p.err, ERR_WAIT_EMPTY);
+                    if (!ok) break;
+                    mbar_arrive_expect_tx(&sm.sfull[sb], 4 * 1024 + N * 16 * 8);
+                    for (int q = 0; q < 4; ++q) {
+                        const uint8_t *tile = reinterpret_cast<const uint8_t *>(p.wtiles) +
+                                              ((size_t)(rb * 4 + q) * NKT + kt) * kTileBytes + kTileQ;
+                        bulk_g2s_plain(&sm.dw[sb][q * 32][0], tile, 1024, &sm.sfull[sb]);
+                    }
+                    tma_load_2d(&sm.dx[sb][0][0], &dxmap, kt * 16, tt * N, &sm.sfull[sb]);
+                }
+                ok = mbar_wait(&sm.empty[st], ((i / kPStages) - 1) & 1, p.err, ERR_WAIT_EMPTY);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&sm.full[st], kPStageA + N * kPKC);
+                tma_load_4d(sm.a[st], &wmap, (kc * kPKC) % kTK, 0, (kc * kPKC) / kTK, rb * 4, &sm.full[st]);
+                tma_load_2d(sm.b[st], &xmap, kc * kPKC, tt * N, &sm.full[st]);
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             for (int i = 0; i < nchunk && ok; ++i) {
-                const int st = i % kPStages, buf = i & 1;
+                const int st = i % kPStages, buf = i % NB;
                 ok = mbar_wait(&sm.full[st], (i / kPStages) & 1, p.err, ERR_WAIT_FULL);
-                if (ok && i >= 2) ok = mbar_wait(&sm.tempty[buf], ((i >> 1) - 1) & 1, p.err, ERR_WAIT_EMPTY);
+                if (ok && i >= NB) ok = mbar_wait(&sm.tempty[buf], ((i / NB) - 1) & 1, p.err, ERR_WAIT_EMPTY);
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll
                 for (int blk = 0; blk < 4; ++blk)
-                    mma_i8(tmem + buf * 256 + blk * kPN, sw128_desc(sm.a[st] + 32 * blk), sw128_desc(sm.b[st] + 32 * blk));
+                    mma_i8(tmem + buf * 4 * N + blk * N, sw128_desc(sm.a[st] + 32 * blk), sw128_desc(sm.b[st] + 32 * blk),
+                           idesc_i8<N>());
                 mma_commit(&sm.empty[st]);
                 mma_commit(&sm.tfull[buf]);
             }
@@ -230,121 +320,153 @@ __global__ void __launch_bounds__(kPThreads, 1)
     } else {
         // ---------------- epilogue ----------------
         // Epilogue warp e = warp - 2 reads TMEM lane quarter q = warp % 4
-        // (weight rows 32q .. 32q+31, one per lane).  The tile's existing
-        // tokens are cut into TQ groups of 16 and the 4 blocks of a chunk
-        // into BS = 4 / TQ phases, so all 16 warps work whatever the token
-        // count: warp e takes token group e/4 % TQ and the blocks b with
-        // b % BS == e/4 / TQ.  Phase partials are added in phase order at the
-        // end (block terms are exact, their double sums order-free).
-        const int q = warp & 3, h4 = (warp - 2) >> 2;
+        // (weight rows 32q .. 32q+31 of the row block, one per lane).  Per
+        // (row block, token tile) segment the tile's existing tokens are cut
+        // into TQ groups of 16 and the 4 blocks of a chunk into BS = 4 / TQ
+        // phases, so all 16 warps work whatever the token count: warp e takes
+        // token group e/4 % TQ and the blocks b with b % BS == e/4 / TQ.
+        // Phase partials are added in phase order at the segment's end (block
+        // terms are exact, their double sums order-free).  Every epilogue
+        // warp runs the same sequence of named barriers: a failed wait only
+        // skips work.
+        pdl_wait();
+        const int e = warp - 2, q = warp & 3, h4 = e >> 2;
         const int row_local = q * 32 + lane;
-        const int nv_tile = min(kPN, p.T - t0);
-        const int TQ = nv_tile <= 16 ? 1 : (nv_tile <= 32 ? 2 : 4);
-        const int BS = 4 / TQ;
-        const int tg = h4 % TQ, bp = h4 / TQ;
-        const int nvalid = min(16, max(0, nv_tile - 16 * tg));  // warp-uniform
         double acc[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = 0.0;
-        for (int i = 0; i < nchunk && ok; ++i) {
-            const int buf = i & 1, ti = i >> 2, sb = ti & 1;
-            if ((i & 3) == 0) ok = mbar_wait(&sm.sfull[sb], (ti >> 1) & 1, p.err, ERR_WAIT_FULL);
-            if (ok) ok = mbar_wait(&sm.tfull[buf], (i >> 1) & 1, p.err, ERR_WAIT_FULL);
-            if (!ok) break;
-            tc_fence_after();
-            if (nvalid > 0) {
-                for (int blk = bp; blk < 4; blk += BS) {
-                    const int b = (i & 3) * 4 + blk;
-                    int s[16];
-                    tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + buf * 256 + blk * kPN + 16 * tg, s);
-                    const double dwr = (double)__half2float(sm.dw[sb][row_local][b]);
-                    const double *dxc = &sm.dx[sb][16 * tg][b];
-#pragma unroll
-                    for (int g8 = 0; g8 < 2; ++g8)
-                        if (8 * g8 < nvalid) {
-#pragma unroll
-                            for (int j = 8 * g8; j < 8 * g8 + 8; ++j)
-                                acc[j] = fma(i2d_exact(s[j]), dwr * dxc[j * 16], acc[j]);
-                        }
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&sm.tempty[buf]);
-                if ((i & 3) == 3 || i == nchunk - 1) mbar_arrive(&sm.sempty[sb]);
-            }
-        }
-        // ---------------- phase partials ----------------
-        // (the stage buffers are idle: every copy was consumed by an MMA whose
-        // completion every epilogue warp has waited for)
-        double *red = reinterpret_cast<double *>(&sm.a[0][0]);  // [16 warps][16 tokens][32 lanes]
-        if (BS > 1) {
-            if (bp > 0)
-#pragma unroll
-                for (int j = 0; j < 16; ++j) red[((warp - 2) * 16 + j) * 32 + lane] = acc[j];
-            named_sync(1, kPEpiWarps * 32);
-            if (bp == 0)
-                for (int ph = 1; ph < BS; ++ph) {
-                    const int we = (ph * TQ + tg) * 4 + ((warp - 2) & 3);  // epilogue warp of (q, tg, ph)
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) acc[j] += red[(we * 16 + j) * 32 + lane];
-                }
-        }
-        // ---------------- output ----------------
-        const int row = rb * kPM + row_local;
-        if (bp == 0 && nvalid > 0) {
-            if (p.nsplit == 1) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int t = t0 + 16 * tg + j;
-                    if (p.epi == EPI_SWIGLU) {
-                        const double up = __shfl_down_sync(0xffffffffu, acc[j], 1);
-                        if ((lane & 1) == 0 && j < nvalid)
-                            p.y[(size_t)t * p.ldy + row / 2] = __fmul_rn(silu((float)acc[j]), (float)up);
-                    } else if (j < nvalid) {
-                        const float v = (float)acc[j];
-                        p.y[(size_t)t * p.ldy + row] = p.res ? __fadd_rn(p.res[(size_t)t * p.ldres + row], v) : v;
+        int rb, tt, kt, seg_kt0 = 0, TQ = 1, BS = 4, tg = 0, bp = 0, nvalid = 0, nv_tile = 0;
+        unit_of(u_lo, NKT, TT, rb, tt, kt);
+        bool first_seg = true;
+        for (int i = 0; i < nchunk; ++i) {
+            const int buf = i % NB, ti = i >> 2, sb = ti & 1;
+            if ((i & 3) == 0) {
+                if (i > 0 && ++kt == NKT) {  // next unit (K-tile fastest)
+                    kt = 0;
+                    if (++tt == TT) {
+                        tt = 0;
+                        ++rb;
                     }
                 }
-            } else {
+                if (i == 0 || kt == 0) {  // a new segment
+                    seg_kt0 = kt;
+                    nv_tile = min(N, p.T - tt * N);
+                    // (64-token tiles keep 4 groups: no phase partials)
+                    TQ = N == 64 ? 4 : (nv_tile <= 16 ? 1 : 2);
+                    BS = 4 / TQ;
+                    tg = h4 % TQ;
+                    bp = h4 / TQ;
+                    nvalid = min(16, max(0, nv_tile - 16 * tg));
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int t = t0 + 16 * tg + j;
-                    if (j < nvalid) p.part[((size_t)split * p.T + t) * p.R + row] = acc[j];
+                    for (int j = 0; j < 16; ++j) acc[j] = 0.0;
+                }
+                if (ok) ok = mbar_wait(&sm.sfull[sb], (ti >> 1) & 1, p.err, ERR_WAIT_FULL);
+            }
+            if (ok) ok = mbar_wait(&sm.tfull[buf], (i / NB) & 1, p.err, ERR_WAIT_FULL);
+            if (ok) {
+                tc_fence_after();
+                if (nvalid > 0) {
+                    for (int blk = bp; blk < 4; blk += BS) {
+                        const int b = (i & 3) * 4 + blk;
+                        int s[16];
+                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + buf * 4 * N + blk * N + 16 * tg, s);
+                        const double dwr = (double)__half2float(sm.dw[sb][row_local][b]);
+                        const double *dxc = &sm.dx[sb][16 * tg][b];
+#pragma unroll
+                        for (int g8 = 0; g8 < 2; ++g8)
+                            if (8 * g8 < nvalid) {
+#pragma unroll
+                                for (int j = 8 * g8; j < 8 * g8 + 8; ++j)
+                                    acc[j] = fma(i2d_exact(s[j]), dwr * dxc[j * 16], acc[j]);
+                            }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&sm.tempty[buf]);
+                    if ((i & 3) == 3) mbar_arrive(&sm.sempty[sb]);
                 }
             }
-        }
-    }
-    if (p.nsplit > 1) {
-        // last CTA of the (row block, token tile) adds the splits in order
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) {
-            int *c = p.counters + rb * gridDim.y + tt;
-            sm.last = atomicAdd(c, 1) == p.nsplit - 1;
-            if (sm.last) *c = 0;
-        }
-        __syncthreads();
-        if (sm.last && warp >= 2) {
-            __threadfence();
-            // epilogue warp (q, g): rows 32q + lane, tokens 16g .. 16g + 15 of the tile
-            const int q = warp & 3, g = (warp - 2) >> 2;
-            const int row = rb * kPM + q * 32 + lane;
-            for (int j = 0; j < 16; ++j) {
-                const int t = t0 + 16 * g + j;
-                double sum = 0.0;
-                if (t < p.T)
-                    for (int k = 0; k < p.nsplit; ++k) sum += __ldcg(p.part + ((size_t)k * p.T + t) * p.R + row);
-                if (p.epi == EPI_SWIGLU) {
-                    const double up = __shfl_down_sync(0xffffffffu, sum, 1);
-                    if ((lane & 1) == 0 && t < p.T)
-                        p.y[(size_t)t * p.ldy + row / 2] = __fmul_rn(silu((float)sum), (float)up);
-                } else if (t < p.T) {
-                    const float v = (float)sum;
-                    p.y[(size_t)t * p.ldy + row] = p.res ? __fadd_rn(p.res[(size_t)t * p.ldres + row], v) : v;
-                }
+            if ((i & 3) != 3 || (kt != NKT - 1 && i != nchunk - 1)) continue;
+            // ---- end of a segment: (rb, tt), K-tiles seg_kt0 .. kt ----
+            if (N < 64 && BS > 1) {
+                // phase partials through shared memory: warps with phase > 0
+                // (epilogue warps 4..15) write, phase 0 adds in phase order
+                if (bp > 0 && ok)
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) sm.red[((e - 4) * 16 + j) * 32 + lane] = acc[j];
+                named_sync(1, kPEpiWarps * 32);
+                if (bp == 0 && ok)
+                    for (int ph = 1; ph < BS; ++ph) {
+                        const int we = (ph * TQ + tg) * 4 + (e & 3);  // epilogue warp of (q, tg, phase ph)
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) acc[j] += sm.red[((we - 4) * 16 + j) * 32 + lane];
+                    }
+                named_sync(1, kPEpiWarps * 32);
             }
+            const int t0 = tt * N;
+            const int row = rb * kPM + row_local;
+            if (seg_kt0 == 0 && kt == NKT - 1) {
+                // the whole K range: this CTA writes the outputs
+                if (bp == 0 && nvalid > 0 && ok)
+#pragma unroll
+                    for (int h8 = 0; h8 < 2; ++h8)
+                        if (8 * h8 < nvalid) {
+                            double v8[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) v8[j] = acc[8 * h8 + j];
+                            store_rows8(p, v8, t0 + 16 * tg + 8 * h8, nvalid - 8 * h8, row, lane);
+                        }
+            } else {
+                // part of the K range: partials to this CTA's slot (0: its
+                // first segment, 1: its last), K-tiles counted per pair
+                const int slot = first_seg ? 0 : 1;
+                double *mine = p.part + ((size_t)c * 2 + slot) * kPN * kPM;
+                if (bp == 0 && nvalid > 0 && ok)
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (j < nvalid) mine[(size_t)(16 * tg + j) * kPM + row_local] = acc[j];
+                __threadfence();
+                named_sync(1, kPEpiWarps * 32);
+                if (e == 0 && lane == 0) {
+                    int *ctr = p.counters + rb * TT + tt;
+                    const int done = kt - seg_kt0 + 1;
+                    const int prev = atomicAdd(ctr, done);
+                    sm.last = prev + done == NKT;
+                    if (prev + done == NKT) *ctr = 0;
+                }
+                named_sync(1, kPEpiWarps * 32);
+                if (sm.last && ok) {
+                    __threadfence();
+                    // the CTAs holding this pair's K-tiles, in K order
+                    const long long u0 = ((long long)rb * TT + tt) * NKT;
+                    const int ca = cta_of(u0, U, G), cb = cta_of(u0 + NKT - 1, U, G);
+                    // warp (q, g): rows 32q + lane, tokens 16g .. 16g + 15 of the tile
+                    const int g = h4;
+                    const int ntok = min(16, nv_tile - 16 * g);
+                    if (ntok > 0) {
+                        const bool first_is_last = ulo_of(ca, U, G) < u0;
+                        for (int h8 = 0; h8 < 2; ++h8) {  // 8 tokens at a time
+                            if (8 * h8 >= ntok) break;
+                            double sum[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) sum[j] = 0.0;
+                            for (int cc = ca; cc <= cb; ++cc) {  // K order
+                                const int sl = (cc == ca && first_is_last) ? 1 : 0;
+                                const double *src =
+                                    p.part + (((size_t)cc * 2 + sl) * kPN + 16 * g + 8 * h8) * kPM + row_local;
+                                double v[8];
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) v[j] = 8 * h8 + j < ntok ? __ldcg(src + (size_t)j * kPM) : 0.0;
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) sum[j] += v[j];
+                            }
+                            store_rows8(p, sum, t0 + 16 * g + 8 * h8, ntok - 8 * h8, row, lane);
+                        }
+                    }
+                }
+                named_sync(1, kPEpiWarps * 32);
+            }
+            first_seg = false;
         }
     }
     tc_fence_before();
@@ -366,6 +488,8 @@ constexpr int kQBlocks = 32;
 
 __global__ void __launch_bounds__(256) quant_rows_q8_kernel(const float *x, int ldx, int K, const float *norm_w,
                                                            float eps, int8_t *xq, double *dx, float *act_out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float *row = x + (size_t)t * ldx;
     __shared__ double red[8];
@@ -420,8 +544,15 @@ static EncodeTiledFn encode_fn() {
 
 cudaError_t prefill_setup() {
     if (!encode_fn()) return cudaErrorNotSupported;
-    return cudaFuncSetAttribute(prefill_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)(sizeof(PSmem) + 1024));
+    cudaError_t e = cudaFuncSetAttribute(prefill_q8_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(sizeof(PSmemT<16>) + 1024));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_q8_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(sizeof(PSmemT<32>) + 1024));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_q8_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(sizeof(PSmemT<64>) + 1024));
+    return e;
 }
 
 bool prefill_ok(const DevMat &w, int T) {
@@ -433,6 +564,7 @@ cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st) {
     EncodeTiledFn enc = encode_fn();
     if (!enc || !prefill_ok(w, a.T) || !a.xq || !a.dx || !a.counters) return cudaErrorInvalidValue;
     const int R = w.rows, K = w.cols, NKT = K / kTK, RT = R / kTR;
+    const int N = a.T <= 16 ? 16 : (a.T <= 32 ? 32 : 64);  // token tile
     CUtensorMap wmap, xmap, dxmap;
     {
         const cuuint64_t dims[4] = {(cuuint64_t)kTK, (cuuint64_t)kTR, (cuuint64_t)NKT, (cuuint64_t)RT};
@@ -447,7 +579,7 @@ cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st) {
     {
         const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)a.T};
         const cuuint64_t strides[1] = {(cuuint64_t)K};
-        const cuuint32_t box[2] = {(cuuint32_t)kPKC, (cuuint32_t)kPN};
+        const cuuint32_t box[2] = {(cuuint32_t)kPKC, (cuuint32_t)N};
         const cuuint32_t es[2] = {1, 1};
         if (enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(a.xq), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -457,22 +589,22 @@ cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st) {
     {
         const cuuint64_t dims[2] = {(cuuint64_t)(K / 32), (cuuint64_t)a.T};
         const cuuint64_t strides[1] = {(cuuint64_t)(K / 32) * 8};
-        const cuuint32_t box[2] = {16, (cuuint32_t)kPN};
+        const cuuint32_t box[2] = {16, (cuuint32_t)N};
         const cuuint32_t es[2] = {1, 1};
         if (enc(&dxmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<double *>(a.dx), dims, strides, box, es,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
     }
-    const int RB = R / kPM, TT = (a.T + kPN - 1) / kPN;
-    int nsplit = std::max(1, std::min(NKT, a.num_sms / std::max(1, RB * TT)));
-    nsplit = std::min(nsplit, 8);
-    if (nsplit > 1 && (!a.part || (size_t)nsplit * a.T * R > a.part_doubles)) nsplit = 1;
+    const int RB = R / kPM, TT = (a.T + N - 1) / N;
+    const long long U = (long long)RB * TT * NKT;
+    const int G = (int)std::min<long long>(a.num_sms, U);
+    if (!a.part || prefill_part_doubles(G) > a.part_doubles || (size_t)RB * TT > a.n_counters)
+        return cudaErrorInvalidValue;
     PrefillParams p;
     p.R = R;
     p.K = K;
     p.T = a.T;
-    p.nsplit = nsplit;
     p.epi = a.epi;
     p.y = a.y;
     p.ldy = a.ldy;
@@ -482,18 +614,39 @@ cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st) {
     p.counters = a.counters;
     p.wtiles = reinterpret_cast<const __half *>(w.w);
     p.err = a.err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = (N == 16 ? sizeof(PSmemT<16>) : N == 32 ? sizeof(PSmemT<32>) : sizeof(PSmemT<64>)) + 1024;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     count_launch();
-    prefill_q8_kernel<<<dim3(RB, TT, nsplit), kPThreads, sizeof(PSmem) + 1024, st>>>(wmap, xmap, dxmap, p);
-    return cudaGetLastError();
+    if (N == 16) return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<16>, wmap, xmap, dxmap, p);
+    if (N == 32) return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<32>, wmap, xmap, dxmap, p);
+    return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<64>, wmap, xmap, dxmap, p);
 }
+
+size_t prefill_part_doubles(int ctas) { return (size_t)ctas * 2 * kPN * kPM; }
 
 cudaError_t launch_quant_rows_q8(const float *x, int ldx, int T, int K, const float *norm_w, float eps, int8_t *xq,
                                  double *dx, float *act_out, cudaStream_t st) {
     if (K % 32 != 0 || T < 1 || ldx % 4 != 0 || reinterpret_cast<uintptr_t>(x) % 16 != 0) return cudaErrorInvalidValue;
     count_launch();
     const int nch = (K / 32 + kQBlocks - 1) / kQBlocks;
-    quant_rows_q8_kernel<<<dim3(T, nch), 256, 0, st>>>(x, ldx, K, norm_w, eps, xq, dx, act_out);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(T, nch);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, quant_rows_q8_kernel, x, ldx, K, norm_w, eps, xq, dx, act_out);
 }
 
 }  // namespace s2k
