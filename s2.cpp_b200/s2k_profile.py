@@ -13,6 +13,13 @@ with the repository.
       its parts: grid-barrier release, activation prologue, median / slowest
       CTA's work; and the attention op's phase stamps.
 
+  python s2.cpp_b200/s2k_profile.py batch [--preset s2pro] [--sizes 1,8,16,32,64] [--context 512]
+      CUDA-event time of one batched frame (s2k_batch_frame: every sequence's
+      Fast-AR passes and Slow step as batched kernels) for each batch size,
+      all sequences at `context` cached positions.  With --profile-one, one
+      frame of the last size runs between cudaProfilerStart / Stop (for
+      `ncu --profile-from-start off`).
+
 Seeded synthetic weights (no checkpoints offline).
 """
 from __future__ import annotations
@@ -120,6 +127,42 @@ def cmd_ops(a) -> None:
     m.close()
 
 
+def cmd_batch(a) -> None:
+    import torch
+    hp, m = _model(a.preset, a.quant)
+    stream = torch.cuda.ExternalStream(m.stream())
+    sizes = [int(x) for x in a.sizes.split(",")]
+    for n in sizes:
+        seqs = []
+        for i in range(n):
+            s = s2k.Sequence(m, a.context + a.frames + 8)
+            s.begin(synthetic.text_prompt(hp, a.context, seed=i), a.frames + 4, temperature=0.0, seed=1, seq_id=i,
+                    min_tokens_before_end=a.frames + 4)
+            seqs.append(s)
+        for _ in range(3):
+            s2k.batch_frame(m, seqs)
+        torch.cuda.synchronize()
+        if a.profile_one and n == sizes[-1]:
+            torch.cuda.profiler.start()
+            s2k.batch_frame(m, seqs)
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+        else:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(a.frames):
+                s2k.batch_frame(m, seqs)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / a.frames
+            print(json.dumps(dict(preset=a.preset, quant=a.quant, sequences=n, context=a.context,
+                                  ms_per_batched_frame=round(ms, 3), frames_per_s=round(n / ms * 1e3, 1))),
+                  flush=True)
+        for s in seqs:
+            s.close()
+    m.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -131,8 +174,15 @@ def main() -> None:
     o.add_argument("--preset", default="s2pro")
     o.add_argument("--quant", default="q8_0")
     o.add_argument("--frames", type=int, default=200)
+    b = sub.add_parser("batch")
+    b.add_argument("--preset", default="s2pro")
+    b.add_argument("--quant", default="q8_0")
+    b.add_argument("--sizes", default="1,8,16,32,64")
+    b.add_argument("--context", type=int, default=512)
+    b.add_argument("--frames", type=int, default=20)
+    b.add_argument("--profile-one", action="store_true")
     a = ap.parse_args()
-    {"prefill": cmd_prefill, "ops": cmd_ops}[a.cmd](a)
+    {"prefill": cmd_prefill, "ops": cmd_ops, "batch": cmd_batch}[a.cmd](a)
 
 
 if __name__ == "__main__":
