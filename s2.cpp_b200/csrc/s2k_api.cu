@@ -498,14 +498,16 @@ static s2k_status ensure_mat(s2k_model *m, DevMat &dm, int type, int rows, int c
 static s2k_status upload_mat(s2k_model *m, DevMat &dm, int type, const int64_t ne[4], const void *host, size_t nbytes,
                              int64_t expect_in, int64_t expect_out, int dst_rows, int row_stride, int row_offset,
                              const char *name) {
-    if (type != S2K_TYPE_Q8_0 && type != S2K_TYPE_Q4_K && type != S2K_TYPE_Q6_K)
-        return fail(S2K_ERR_UNSUPPORTED, "%s: ggml type %d not supported for matrices (Q8_0, Q4_K, Q6_K)", name, type);
+    if (type != S2K_TYPE_Q8_0 && type != S2K_TYPE_Q4_K && type != S2K_TYPE_Q6_K && type != S2K_TYPE_F16)
+        return fail(S2K_ERR_UNSUPPORTED, "%s: ggml type %d not supported for matrices (F16, Q8_0, Q4_K, Q6_K)", name,
+                    type);
     if (ne[0] != expect_in || ne[1] != expect_out)
         return fail(S2K_ERR_ARG, "%s: expected ne [%lld, %lld], got [%lld, %lld]", name, (long long)expect_in,
                     (long long)expect_out, (long long)ne[0], (long long)ne[1]);
     if (ne[0] % 256 != 0) return fail(S2K_ERR_UNSUPPORTED, "%s: row length %lld not a multiple of 256", name, (long long)ne[0]);
-    const size_t row_bytes = type == S2K_TYPE_Q8_0 ? (size_t)ne[0] / 32 * 34
-                                                  : (size_t)ne[0] / 256 * (type == S2K_TYPE_Q4_K ? 144 : 210);
+    const size_t row_bytes = type == S2K_TYPE_F16    ? (size_t)ne[0] * 2
+                             : type == S2K_TYPE_Q8_0 ? (size_t)ne[0] / 32 * 34
+                                                     : (size_t)ne[0] / 256 * (type == S2K_TYPE_Q4_K ? 144 : 210);
     if (nbytes != row_bytes * (size_t)ne[1])
         return fail(S2K_ERR_ARG, "%s: %zu bytes, expected %zu", name, nbytes, row_bytes * (size_t)ne[1]);
     s2k_status rc = ensure_mat(m, dm, type, dst_rows, (int)ne[0]);

@@ -22,6 +22,7 @@
 #include "s2k_kernels.h"
 
 #include <algorithm>
+#include <cstddef>
 #include <cstdint>
 
 namespace s2k {
@@ -36,17 +37,24 @@ struct GemvCfg {
 };
 
 constexpr int kPC = 5;  // 8-value activation chunks per consumer thread per prologue pass
+constexpr int kMaxMTF16 = 4;  // tokens per launch on F16 weights (their activation takes 2 B per value)
 
 template <int MT>
 struct GemvSmem {
     uint8_t ring[GemvCfg<MT>::NS][kTileBytes];
     uint64_t full[GemvCfg<MT>::NS], empty[GemvCfg<MT>::NS];
-    int8_t xq[MT * kMaxK];
+    // quantized activation (int8), or the fp16 activation of F16 weights (2 B
+    // per value over xq, xd, xbs and xh_rest; MT <= kMaxMTF16)
+    alignas(16) int8_t xq[MT * kMaxK];
     float xd[MT * kMaxK / 32];      // Q8_0 block scales, or Q8_K super-block scales
     int16_t xbs[MT * kMaxK / 16];   // Q8_K block sums
+    int8_t xh_rest[MT <= kMaxMTF16 ? MT * kMaxK * 3 / 4 : 16];
     double tok[kTW][MT];
     int abort_flag;
 };
+static_assert(offsetof(GemvSmem<4>, xh_rest) + sizeof(GemvSmem<4>::xh_rest) - offsetof(GemvSmem<4>, xq) >=
+                  (size_t)2 * 4 * kMaxK,
+              "fp16 activation fits xq .. xh_rest");
 static_assert(sizeof(GemvSmem<8>) <= 227 * 1024, "gemv shared memory");
 static_assert(sizeof(GemvSmem<4>) <= 227 * 1024, "gemv shared memory");
 static_assert(sizeof(GemvSmem<2>) <= 227 * 1024, "gemv shared memory");
@@ -58,7 +66,7 @@ __global__ void __launch_bounds__(kThreads, 1) tgemv_kernel(TGemv g, const int *
     GemvSmem<MT> &sm = *reinterpret_cast<GemvSmem<MT> *>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     long long u0, u1;
-    tg_range(g.R, g.K, blockIdx.x, gridDim.x, &u0, &u1);
+    tg_range(g.R, g.K, g.wtype, blockIdx.x, gridDim.x, &u0, &u1);
     const int ntiles = (int)(u1 - u0);
     const uint32_t tb = (uint32_t)tile_bytes(g.wtype);
     if (tid == 0) {
@@ -119,13 +127,14 @@ __global__ void __launch_bounds__(kThreads, 1) tgemv_kernel(TGemv g, const int *
 }
 
 int tw_of(int ggml_type) {
-    return ggml_type == 12 ? TW_Q4_K : (ggml_type == 14 ? TW_Q6_K : (ggml_type == 8 ? TW_Q8_0 : -1));
+    return ggml_type == 12 ? TW_Q4_K
+                           : (ggml_type == 14 ? TW_Q6_K : (ggml_type == 8 ? TW_Q8_0 : (ggml_type == 1 ? TW_F16 : -1)));
 }
 
 size_t DevMat::bytes() const {
     const int tw = tw_of(type);
     if (tw < 0) return 0;
-    return (size_t)(rows / kTR) * (size_t)(cols / kTK) * tile_bytes(tw);
+    return (size_t)(rows / kTR) * (size_t)(cols / tile_cols(tw)) * tile_bytes(tw);
 }
 
 cudaError_t gemv_setup() {
@@ -188,8 +197,9 @@ cudaError_t launch_gemv(const GemvArgs &a, int num_sms, cudaStream_t st) {
         return cudaErrorInvalidValue;
     if (a.in_mode == IN_RMSNORM && a.norm_w == nullptr) return cudaErrorInvalidValue;
     const int grid = std::min(num_sms, w.rows / kTR);
-    for (int m0 = 0; m0 < a.M; m0 += kMaxMT) {
-        const int M = std::min(kMaxMT, a.M - m0);
+    const int mt_max = w.type == 1 ? kMaxMTF16 : kMaxMT;
+    for (int m0 = 0; m0 < a.M; m0 += mt_max) {
+        const int M = std::min(mt_max, a.M - m0);
         cudaError_t e;
         if (M == 1) e = launch_one<1>(a, m0, M, grid, st);
         else if (M == 2) e = launch_one<2>(a, m0, M, grid, st);
@@ -267,11 +277,39 @@ __global__ void relayout_k_kernel(const uint8_t *__restrict__ src, int row0, int
     }
 }
 
+// ---------------------------------------------------------------------------
+// GGUF F16 rows -> tiles of 32 x 256 halves: one thread per 16-byte chunk
+// (8 halves); chunk c of source row r lands in destination row dr = r *
+// row_stride + row_offset, tile (dr / 32, c / 32), at (dr % 32, 8 (c % 32)).
+// ---------------------------------------------------------------------------
+__global__ void relayout_f16_kernel(const uint8_t *__restrict__ src, int row0, int rows, int cols,
+                                    uint8_t *__restrict__ dst, int row_stride, int row_offset) {
+    const int nc = cols / 8, nkt = cols / kTKH;
+    const long long total = (long long)rows * nc;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int rr = (int)(i / nc), c = (int)(i - (long long)rr * nc);
+        const long long dr = (long long)(row0 + rr) * row_stride + row_offset;
+        uint8_t *tile = dst + ((size_t)(dr / kTR) * nkt + (size_t)(c / (kTKH / 8))) * kTileBytesF16;
+        *reinterpret_cast<uint4 *>(tile + ((dr % kTR) * kTKH + 8 * (c % (kTKH / 8))) * 2) =
+            *reinterpret_cast<const uint4 *>(src + i * 16);
+    }
+}
+
 cudaError_t launch_relayout(const uint8_t *src, int row0, int rows, int cols, DevMat *dst, int row_stride,
                             int row_offset, cudaStream_t st) {
     const int tw = tw_of(dst->type);
     if (tw == TW_Q8_0) return launch_relayout_q8_0(src, row0, rows, cols, dst, row_stride, row_offset, st);
     if (tw < 0) return cudaErrorInvalidValue;
+    if (tw == TW_F16) {
+        if (reinterpret_cast<uintptr_t>(src) % 16 != 0 || cols % kTKH != 0) return cudaErrorInvalidValue;
+        const long long total = (long long)rows * (cols / 8);
+        const int block = 256;
+        const int grid = (int)std::min<long long>((total + block - 1) / block, 148 * 16);
+        count_launch();
+        relayout_f16_kernel<<<grid, block, 0, st>>>(src, row0, rows, cols, dst->w, row_stride, row_offset);
+        return cudaGetLastError();
+    }
     const long long total = (long long)rows * (cols / 256);
     const int block = 256;
     const int grid = (int)std::min<long long>((total + block - 1) / block, 148 * 16);

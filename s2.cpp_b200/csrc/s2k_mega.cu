@@ -37,7 +37,7 @@ constexpr int kPtab = 512;                 // cached pages whose ids are staged 
 constexpr int kMPC = 5;                    // 8-value activation chunks per consumer thread per prologue pass
 
 bool mega_gemv_ok(const MegaGemv &g) {
-    if (g.wtype != TW_Q8_0 && g.wtype != TW_Q4_K && g.wtype != TW_Q6_K) return false;
+    if (g.wtype != TW_Q8_0 && g.wtype != TW_Q4_K && g.wtype != TW_Q6_K && g.wtype != TW_F16) return false;
     if (!tg_shape_ok(g.R, g.K, g.M, g.in_mode, g.epi, g.res != nullptr, kMKMax, kMaxT)) return false;
     if (g.in_mode == IN_RMSNORM && g.norm_w == nullptr) return false;
     // one-pass RMSNorm prologue; 32-byte activation and norm-weight loads
@@ -88,10 +88,16 @@ bool mega_attn_ok(const MegaAttn &a, int max_keys) {
 }
 
 struct GemvSm {
-    int8_t xq[kMaxT * kMKMax];  // quantized activation
+    // quantized activation (int8), or the fp16 activation of F16 weights
+    // (2 bytes per value, spilling over xd / xbs, which F16 does not use)
+    alignas(16) int8_t xq[kMaxT * kMKMax];
     float xd[kMaxT * kMKMax / 32];  // Q8_0 block scales, or Q8_K super-block scales
     int16_t xbs[kMaxT * kMKMax / 16];  // Q8_K block sums
+    int8_t xh_rest[kMaxT * kMKMax * 3 / 4];  // the rest of the fp16 activation
 };
+static_assert(offsetof(GemvSm, xd) == kMaxT * kMKMax && offsetof(GemvSm, xh_rest) + sizeof(GemvSm::xh_rest) >=
+                                                            (size_t)2 * kMaxT * kMKMax,
+              "fp16 activation fits xq .. xh_rest");
 
 struct MSmem {
     uint8_t ring[kMStages][kTileBytes];
@@ -159,7 +165,7 @@ struct TileCursor {
         while (u >= u1) {
             if (++op >= n_ops) return nullptr;
             if (ops[op].kind != MK_GEMV) continue;
-            tg_range(ops[op].g.R, ops[op].g.K, cta, G, &u, &u1);
+            tg_range(ops[op].g.R, ops[op].g.K, ops[op].g.wtype, cta, G, &u, &u1);
             w = ops[op].g.w;
             bytes = (uint32_t)tile_bytes(ops[op].g.wtype);
         }
@@ -253,7 +259,7 @@ __device__ void mega_gemv(const MegaGemv &gref, const F8 (&nw)[kMPC], MSmem &sm,
     g.res_tag |= ep8;
     g.y_tag |= ep8;
     long long u0, u1;
-    tg_range(g.R, g.K, cta, G, &u0, &u1);
+    tg_range(g.R, g.K, g.wtype, cta, G, &u0, &u1);
     if (u0 == u1) return;  // no row tile of this op here (R / 32 < G)
     // the CTA owning row tile 0 stores act_out
     tg_prologue8<MT, kMNC, kMPC>(g, nw, sm.u.g.xq, sm.u.g.xd, sm.u.g.xbs, &sm.tok[0][0], kMaxT, u0 == 0, 1,

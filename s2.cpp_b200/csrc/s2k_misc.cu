@@ -22,7 +22,8 @@
 namespace s2k {
 
 __device__ __forceinline__ float deq_elem(const DevMat &w, long long row, int col) {
-    return tq_elem(w.w, w.type == 12 ? TW_Q4_K : (w.type == 14 ? TW_Q6_K : TW_Q8_0), w.cols, row, col);
+    return tq_elem(w.w, w.type == 12 ? TW_Q4_K : (w.type == 14 ? TW_Q6_K : (w.type == 1 ? TW_F16 : TW_Q8_0)), w.cols,
+                   row, col);
 }
 
 // grid T, block 256

@@ -55,12 +55,21 @@ constexpr int kQ6kQh = kTR * 2 * 128, kQ6kSc = kQ6kQh + kTR * 2 * 64, kQ6kD = kQ
 static_assert(kTileBytesQ4K <= kTileBytes && kTileBytesQ6K <= kTileBytes, "ring slots hold one tile of any type");
 static_assert(kTileBytesQ4K % 16 == 0 && kTileBytesQ6K % 16 == 0, "bulk copies need 16-byte multiples");
 
+// F16 tiles: 32 rows x 256 columns of fp16, row-major (16384 bytes), so a
+// row tile of K columns holds K / 256 of them.
+constexpr int kTKH = 256;
+constexpr int kTileBytesF16 = kTR * kTKH * 2;
+static_assert(kTileBytesF16 <= kTileBytes && kTileBytesF16 % 16 == 0, "F16 tiles fit a ring slot");
+
 // weight types of the tile engine (TGemv::wtype)
-enum TWType : int { TW_Q8_0 = 0, TW_Q4_K = 1, TW_Q6_K = 2 };
+enum TWType : int { TW_Q8_0 = 0, TW_Q4_K = 1, TW_Q6_K = 2, TW_F16 = 3 };
 
 __host__ __device__ constexpr int tile_bytes(int wtype) {
-    return wtype == TW_Q4_K ? kTileBytesQ4K : (wtype == TW_Q6_K ? kTileBytesQ6K : kTileBytes);
+    return wtype == TW_Q4_K ? kTileBytesQ4K
+                            : (wtype == TW_Q6_K ? kTileBytesQ6K : (wtype == TW_F16 ? kTileBytesF16 : kTileBytes));
 }
+// columns of one tile
+__host__ __device__ constexpr int tile_cols(int wtype) { return wtype == TW_F16 ? kTKH : kTK; }
 
 static_assert(kTileBytes % 16 == 0, "bulk copies need 16-byte multiples");
 static_assert(kTRW == 4, "the row-tile reduction is written for 4 rows per warp");
@@ -113,6 +122,10 @@ __device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *q, int *sc, 
 // Element (r, c) of a tiled matrix with K columns, dequantized as ggml's
 // dequantize_row_q8_0 / _q4_K / _q6_K do (float products in the same order).
 __device__ __forceinline__ float tq_elem(const uint8_t *w, int wtype, int K, long long r, int c) {
+    if (wtype == TW_F16) {
+        const uint8_t *t = w + ((size_t)(r / kTR) * (K / kTKH) + (size_t)(c / kTKH)) * kTileBytesF16;
+        return __half2float(__ldg(reinterpret_cast<const __half *>(t) + (r % kTR) * kTKH + c % kTKH));
+    }
     const uint8_t *t = w + ((size_t)(r / kTR) * (K / kTK) + (size_t)(c / kTK)) * tile_bytes(wtype);
     const int rl = (int)(r % kTR), cl = c % kTK;
     if (wtype == TW_Q4_K) {
@@ -142,8 +155,8 @@ __device__ __forceinline__ float tq_elem(const uint8_t *w, int wtype, int K, lon
 }
 
 // Tile range [u0, u1) of CTA `cta` of G: whole row tiles.
-__device__ __forceinline__ void tg_range(int R, int K, int cta, int G, long long *u0, long long *u1) {
-    const long long RT = R / kTR, NKT = K / kTK;
+__device__ __forceinline__ void tg_range(int R, int K, int wtype, int cta, int G, long long *u0, long long *u1) {
+    const long long RT = R / kTR, NKT = K / tile_cols(wtype);
     *u0 = (RT * cta / G) * NKT;
     *u1 = (RT * (cta + 1) / G) * NKT;
 }
@@ -262,6 +275,11 @@ __device__ __forceinline__ void tg_norm_preload(const TGemv &g, F8 (&nw)[PC]) {
     }
 }
 
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
 // round-half-even(x) for |x| < 2^22, low byte only
 __device__ __forceinline__ uint32_t rne_byte(float x) {
     return (uint32_t)__float_as_int(__fadd_rn(x, 12582912.f));
@@ -338,7 +356,8 @@ __device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC],
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = g.K, KC = K >> 3, M = g.M, nv = M * KC;
     const bool rms = g.in_mode == IN_RMSNORM;
-    const bool q8k = g.wtype != TW_Q8_0;
+    const bool f16 = g.wtype == TW_F16;
+    const bool q8k = g.wtype != TW_Q8_0 && !f16;
     const bool one_pass = nv <= PC * NT;
     float sc[MT];
 #pragma unroll
@@ -446,6 +465,17 @@ __device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC],
                 float4 *dst = reinterpret_cast<float4 *>(g.act_out + 8 * (size_t)v);
                 dst[0] = make_float4(y.v[0], y.v[1], y.v[2], y.v[3]);
                 dst[1] = make_float4(y.v[4], y.v[5], y.v[6], y.v[7]);
+            }
+            if (f16) {  // the activation rounded to fp16 (ggml's vec_dot_type for F16 weights)
+                if (valid) {
+                    uint4 hv;
+                    hv.x = pack_half2(y.v[0], y.v[1]);
+                    hv.y = pack_half2(y.v[2], y.v[3]);
+                    hv.z = pack_half2(y.v[4], y.v[5]);
+                    hv.w = pack_half2(y.v[6], y.v[7]);
+                    *reinterpret_cast<uint4 *>(xq + 16 * (size_t)v) = hv;
+                }
+                continue;
             }
             if (q8k) {
                 quant_q8k_warp(y.v, lane, valid, xq + 8 * (size_t)v, xd + (v >> 5), xbs + ((v >> 5) << 4));
@@ -799,12 +829,109 @@ __device__ __forceinline__ void tg_consume_q6k(const TGemv &g, const uint8_t *ri
     }
 }
 
+// ---------------------------------------------------------------------------
+// F16 consumer (xq holds the fp16-rounded activation, [M][K] halves).  Lane l
+// owns columns 8l..8l+7 of each 256-column tile.  fp16 values become doubles
+// exactly with integer moves: the sign and the 15 magnitude bits shifted into
+// the double's sign / exponent / mantissa fields give the value times 2^-1008
+// (normals and subnormals alike), and one multiply by 2^1008 restores it.  A
+// product of two fp16 values is exact in double, so fma(w, x, acc) adds the
+// exact product (ggml_vec_dot_f16's terms) and rows are rounded to float once.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void h2_to_d(uint32_t u, double &lo, double &hi) {
+    // magnitude bits 0..14 of a half -> bits 10..24 of the double's high word
+    const uint32_t l = ((u << 16) & 0x80000000u) | ((u << 10) & 0x01FFFC00u);
+    const uint32_t h = (u & 0x80000000u) | ((u >> 6) & 0x01FFFC00u);
+    constexpr double k2p1008 = 0x1p1008;
+    lo = __hiloint2double((int)l, 0) * k2p1008;
+    hi = __hiloint2double((int)h, 0) * k2p1008;
+}
+
+template <int MT>
+__device__ __forceinline__ void tg_consume_f16(const TGemv &g, const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                                               int nst, int &slot, uint32_t &phase, const int8_t *xq, int cta, int G,
+                                               int *err, unsigned long long *t_first = nullptr) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = g.K, NKT = K / kTKH, M = g.M;
+    const int RT = g.R / kTR;
+    const int rt0 = (int)((long long)RT * cta / G), rt1 = (int)((long long)RT * (cta + 1) / G);
+    const int rbase = warp * kTRW;
+    const int my_row = 2 * (lane >> 4) + ((lane >> 3) & 1);
+    const __half *xh = reinterpret_cast<const __half *>(xq);
+    for (int rt = rt0; rt < rt1; ++rt) {
+        double acc[kTRW][MT];
+#pragma unroll
+        for (int i = 0; i < kTRW; ++i)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[i][m] = 0.0;
+        float resv[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) resv[m] = 0.f;
+        if (g.res != nullptr && (lane & 7) == 0) {
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+                if (m < M) {
+                    const size_t ri = (size_t)m * g.ldres + (size_t)rt * kTR + rbase + my_row;
+                    resv[m] = (g.ll & LL_RES) ? ll_wait1(g.res, ri, g.res_tag, err) : __ldcg(g.res + ri);
+                }
+        }
+        for (int kt = 0; kt < NKT; ++kt) {
+            double xv[MT][8];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const int mm = m < M ? m : 0;
+                const uint4 a = *reinterpret_cast<const uint4 *>(xh + (size_t)mm * K + kt * kTKH + lane * 8);
+                h2_to_d(a.x, xv[m][0], xv[m][1]);
+                h2_to_d(a.y, xv[m][2], xv[m][3]);
+                h2_to_d(a.z, xv[m][4], xv[m][5]);
+                h2_to_d(a.w, xv[m][6], xv[m][7]);
+            }
+            mbar_wait(&full[slot], phase, err, ERR_WAIT_FULL);
+            if (t_first != nullptr && tid == 0 && rt == rt0 && kt == 0) *t_first = globaltimer_ns();
+            const uint8_t *t = ring + (size_t)slot * kTileBytes;
+            uint4 wv[kTRW];
+#pragma unroll
+            for (int i = 0; i < kTRW; ++i)
+                wv[i] = *reinterpret_cast<const uint4 *>(t + ((rbase + i) * kTKH + lane * 8) * 2);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == nst) {
+                slot = 0;
+                phase ^= 1u;
+            }
+#pragma unroll
+            for (int i = 0; i < kTRW; ++i) {
+                double w[8];
+                h2_to_d(wv[i].x, w[0], w[1]);
+                h2_to_d(wv[i].y, w[2], w[3]);
+                h2_to_d(wv[i].z, w[4], w[5]);
+                h2_to_d(wv[i].w, w[6], w[7]);
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                    if (m < M)
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[i][m] = fma(w[e], xv[m][e], acc[i][m]);
+            }
+        }
+        double tot[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) tot[m] = reduce4_transpose(acc[0][m], acc[1][m], acc[2][m], acc[3][m], lane);
+        tg_emit<MT>(g, rt, warp, lane, tot, resv);
+    }
+}
+
 // The consumer of the op's weight type.
 template <int MT>
 __device__ __forceinline__ void tg_consume_any(const TGemv &g, const uint8_t *ring, uint64_t *full, uint64_t *empty,
                                                int nst, int &slot, uint32_t &phase, const int8_t *xq,
                                                const float *xd, const int16_t *xbs, int cta, int G, int *err,
                                                unsigned long long *t_first = nullptr) {
+    if constexpr (MT <= 4) {  // (F16 calls carry at most 4 tokens)
+        if (g.wtype == TW_F16) {
+            tg_consume_f16<MT>(g, ring, full, empty, nst, slot, phase, xq, cta, G, err, t_first);
+            return;
+        }
+    }
     if (g.wtype == TW_Q4_K)
         tg_consume_q4k<MT>(g, ring, full, empty, nst, slot, phase, xq, xd, xbs, cta, G, err, t_first);
     else if (g.wtype == TW_Q6_K)
