@@ -111,6 +111,7 @@ cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int 
     if (prefill && T >= kPrefillMinT && m->prefill_mma) {
         const int kmax = std::max(std::max(dim, w.qs), ff);
         if ((e = m->alloc(&w.pf_xq, tn * kmax))) return e;
+        if ((e = m->alloc(&w.pf_xh, tn * kmax))) return e;
         if ((e = m->alloc(&w.pf_dx, tn * kmax / 32))) return e;
         // stream-K partials (one CTA per SM), and K-tile
         // counters for every (row block, token tile) of the largest GEMM
@@ -128,7 +129,7 @@ cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int 
 void work_free(s2k_model *m, Work &w) {
     for (void *p : {(void *)w.x, (void *)w.h, (void *)w.qkv, (void *)w.attn, (void *)w.ff_buf, (void *)w.kcur,
                     (void *)w.vcur, (void *)w.scores, (void *)w.part, (void *)w.part_ms, (void *)w.counters,
-                    (void *)w.pf_xq, (void *)w.pf_dx, (void *)w.pf_part, (void *)w.pf_counters,
+                    (void *)w.pf_xq, (void *)w.pf_dx, (void *)w.pf_part, (void *)w.pf_counters, (void *)w.pf_xh,
                     (void *)w.fl_part,
                     (void *)w.fl_ms, (void *)w.fl_counters, (void *)w.lx,
                     (void *)w.lh, (void *)w.lqkv, (void *)w.lattn, (void *)w.lff})
@@ -177,7 +178,16 @@ static s2k_status upload_rope(s2k_model *m, float2 **dst, int *n_out, int n_pos,
 // One stack GEMM: prompt-sized Slow calls on Q8_0 weights go through the
 // tensor cores (activation rows quantized once, then tcgen05 int8 MMAs,
 // s2k_prefill.cu); everything else through the tile GEMV.
-cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool prefill) {
+cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool prefill, bool f16) {
+    if (f16 && m->prefill_f16 && w.pf_xh && g.M >= kPrefillMinT && g.M <= w.T && prefill_f16_ok(*g.w, g.M)) {
+        const DevMat &W = *g.w;
+        cudaError_t e;
+        if ((e = launch_rows_f16(g.x, g.ldx, g.M, W.cols, g.in_mode == IN_RMSNORM ? g.norm_w : nullptr, g.eps, w.pf_xh,
+                                 g.act_out, m->stream)))
+            return e;
+        return launch_prefill_f16_gemm(W.w, W.rows, W.cols, g.M, w.pf_xh, g.epi, g.y, g.ldy, g.res, g.ldres,
+                                       m->num_sms, m->d_err, m->stream);
+    }
     if (prefill && m->prefill_mma && w.pf_xq && g.M >= kPrefillMinT && g.M <= w.T && prefill_ok(*g.w, g.M)) {
         cudaError_t e = launch_quant_rows_q8(g.x, g.ldx, g.M, g.w->cols, g.in_mode == IN_RMSNORM ? g.norm_w : nullptr,
                                              g.eps, w.pf_xq, w.pf_dx, g.act_out, m->stream);
@@ -229,7 +239,7 @@ cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         g.ldy = qkvs;
         g.done = c.done;
         g.err = m->d_err;
-        if ((e = stack_gemm(m, w, g, c.mma))) return e;
+        if ((e = stack_gemm(m, w, g, c.mma, c.f16mma))) return e;
 
         QkPrepArgs q;
         q.qkv = w.qkv;
@@ -297,7 +307,7 @@ cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         o.ldy = dim;
         o.res = w.x;
         o.ldres = dim;
-        if ((e = stack_gemm(m, w, o, c.mma))) return e;
+        if ((e = stack_gemm(m, w, o, c.mma, c.f16mma))) return e;
 
         GemvArgs f1 = g;
         f1.w = &L.w13;
@@ -308,7 +318,7 @@ cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         f1.epi = EPI_SWIGLU;
         f1.y = w.ff_buf;
         f1.ldy = w.ff;
-        if ((e = stack_gemm(m, w, f1, c.mma))) return e;
+        if ((e = stack_gemm(m, w, f1, c.mma, c.f16mma))) return e;
 
         GemvArgs f2 = g;
         f2.w = &L.w2;
@@ -320,7 +330,7 @@ cudaError_t run_stack(s2k_model *m, const StackCall &c) {
         f2.ldy = dim;
         f2.res = w.h;
         f2.ldres = dim;
-        if ((e = stack_gemm(m, w, f2, c.mma))) return e;
+        if ((e = stack_gemm(m, w, f2, c.mma, c.f16mma))) return e;
     }
     return cudaSuccess;
 }
@@ -349,6 +359,7 @@ cudaError_t enqueue_slow(s2k_model *m, s2k_seq *s, int T, const int *tokens_dev,
     StackCall c;
     c.fast = false;
     c.mma = true;
+    c.f16mma = T >= kPrefillMinT;  // prompt prefill (decode steps stay on the exact GEMV)
     c.T = T;
     c.pos_base = &s->dev->state.n_past;
     c.pos_add = 0;
@@ -710,6 +721,7 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     CU(mega_setup());
     CU(attn_setup());
     m->prefill_mma = prefill_setup() == cudaSuccess;
+    m->prefill_f16 = m->prefill_mma && prefill_f16_setup() == cudaSuccess;
     cudaGetLastError();  // a device without the tensor-map entry point keeps the GEMV path
     if (m->staging) {
         m->release(m->staging);

@@ -93,6 +93,14 @@ cudaError_t prefill_setup();
 size_t prefill_part_doubles(int ctas);
 bool prefill_ok(const DevMat &w, int T);
 cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st);
+// Prefill GEMM on the tensor cores for F16 matrices (s2k_prefill_f16.cu);
+// fp32 accumulation (prefill only: not the decode arithmetic).
+cudaError_t prefill_f16_setup();
+bool prefill_f16_ok(const DevMat &w, int T);
+cudaError_t launch_rows_f16(const float *x, int ldx, int T, int K, const float *norm_w, float eps, __half *xh,
+                            float *act_out, cudaStream_t st);
+cudaError_t launch_prefill_f16_gemm(const uint8_t *wtiles, int R, int K, int T, const __half *xh, int epi, float *y,
+                                    int ldy, const float *res, int ldres, int num_sms, int *err, cudaStream_t st);
 // x [T][ldx] (optional RMSNorm with norm_w, eps) -> xq [T][K] int8, dx [T][K/32]
 cudaError_t launch_quant_rows_q8(const float *x, int ldx, int T, int K, const float *norm_w, float eps, int8_t *xq,
                                  double *dx, float *act_out, cudaStream_t st);

@@ -51,6 +51,7 @@ struct Work {
     double *pf_dx = nullptr, *pf_part = nullptr;
     size_t pf_part_n = 0, pf_n_counters = 0;
     int *pf_counters = nullptr;
+    __half *pf_xh = nullptr;  // fp16 activation rows of the fp16 tensor-core prefill [T][kmax]
     // split-parallel attention (calls of up to fl_T rows): per-split partials
     double *fl_part = nullptr, *fl_ms = nullptr;
     int *fl_counters = nullptr;
@@ -83,6 +84,7 @@ struct s2k_model {
     std::vector<void *> allocs;
     bool finalized = false;
     bool prefill_mma = false;  // the tensor-core prefill path could be set up on this device
+    bool prefill_f16 = false;  // the fp16 tensor-core prefill GEMM (F16 models) could be set up
     int *d_err = nullptr;
     unsigned *d_epoch = nullptr;  // tag epoch of the persistent kernel's activations (starts at 1)
     // staging for uploads
@@ -183,6 +185,7 @@ struct StackCall {
     float *const *fk = nullptr;   // Fast stack: per-layer K/V rows of the call (default m->fkcur / fvcur)
     float *const *fv = nullptr;
     bool mma = false;             // Q8_0 GEMMs of T >= kPrefillMinT rows may use the tensor cores
+    bool f16mma = false;          // prompt prefill: F16 GEMMs may use the fp16 tensor-core GEMM
 };
 
 }  // namespace s2k
@@ -198,7 +201,9 @@ cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int 
                        bool prefill, int flash_rows = 0);
 void work_free(s2k_model *m, Work &w);
 s2k_status ensure_slow_work(s2k_model *m, int T, int L);
-cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool prefill);
+// exact: Q8_0 GEMMs of 8+ rows on the tensor cores (the decode arithmetic);
+// f16: F16 GEMMs of 8+ rows on the fp16 tensor-core GEMM (prefill).
+cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool exact, bool f16 = false);
 cudaError_t run_stack(s2k_model *m, const StackCall &c);
 cudaError_t enqueue_slow(s2k_model *m, s2k_seq *s, int T, const int *tokens_dev, const int *done);
 s2k_status check_tokens_host(const s2k_model *m, const int32_t *flat, int32_t T);

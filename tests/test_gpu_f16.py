@@ -95,3 +95,50 @@ def test_f16_weight_bytes(f16_pair):
     hp, m, _ = f16_pair
     gguf = sum(spec.nbytes for spec in synthetic.tensor_specs(hp, "f16", 0.1) if spec.ne1 > 1)
     assert m.weight_bytes() == gguf
+
+
+@pytest.mark.parametrize("T", [8, 64, 300])
+def test_f16_prefill_tensor_cores(f16_pair, T):
+    """Prompts of 8+ tokens prefill through the fp16 tensor-core GEMM (fp32
+    accumulation; 64- and 256-token tiles, a partial last tile at 300):
+    logits within the tolerance of the oracle, then decode steps too."""
+    hp, m, om = f16_pair
+    p = synthetic.text_prompt(hp, T, seed=T)
+    m.init_kv_cache(T + 8)
+    om.init_kv_cache(T + 8)
+    hg, lg = m.prefill_fast(p.T.reshape(-1), T)
+    ho, lo = om.eval(p.T.reshape(-1), T)
+    assert_close(hg, ho, f"f16 tc prefill hidden T={T}")
+    assert_close(lg, lo, f"f16 tc prefill logits T={T}")
+    for i in range(2):
+        tok = np.zeros(hp.num_codebooks + 1, np.int32)
+        tok[0] = 3 + i
+        hg, lg = m.step(tok)
+        ho, lo = om.eval(tok, 1)
+        assert_close(lg, lo, f"f16 step {i} after tc prefill T={T}")
+
+
+def test_f16_mid_real_widths():
+    """S2 Pro widths (d 2560, GQA 32/8, ff 9728, vocab 155,648), F16: a
+    72-token tensor-core prefill and decode steps against the oracle."""
+    hp = synthetic.preset("mid")
+    tensors = list(synthetic.make_model(hp, seed=29, quant="f16", norm_std=0.1))
+    m = s2k.SlowARModel(hp)
+    m.load_tensors(tensors)
+    om = oracle.OracleModel(hp)
+    om.load_tensors(tensors)
+    p = synthetic.semantic_prompt(hp, 72, seed=2)
+    m.init_kv_cache(80)
+    om.init_kv_cache(80)
+    _, lg = m.prefill_fast(p.T.reshape(-1), 72)
+    ho, lo = om.eval(p.T.reshape(-1), 72)
+    assert_close(lg, lo, "f16 mid prefill logits")
+    tok = np.zeros(hp.num_codebooks + 1, np.int32)
+    tok[0] = 1000
+    _, lg = m.step(tok)
+    ho, lo = om.eval(tok, 1)
+    assert_close(lg, lo, "f16 mid step logits")
+    assert_close(m.fast_decode(ho, np.array([5, 9], np.int32)), om.fast_decode(ho, np.array([5, 9], np.int32)),
+                 "f16 mid fast_decode")
+    m.close()
+    om.close()

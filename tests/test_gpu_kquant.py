@@ -73,3 +73,23 @@ def test_kquant_weight_bytes(kq_pair):
     hp, m, _ = kq_pair
     gguf = sum(spec.nbytes for spec in synthetic.tensor_specs(hp, "q4_k_m", 0.1) if spec.ne1 > 1)
     assert m.weight_bytes() == gguf
+
+
+def test_kquant_prefill_long_prompt(kq_pair):
+    """A 96-token prompt (K-quant prefill stays on the exact tile GEMV:
+    a 16-bit-activation tensor-core path would leave the reference's Q8_K
+    arithmetic by ~8 % of the logits' std)."""
+    hp, m, om = kq_pair
+    p = synthetic.semantic_prompt(hp, 96, seed=4)
+    m.init_kv_cache(128)
+    om.init_kv_cache(128)
+    hg, lg = m.prefill_fast(p.T.reshape(-1), 96)
+    ho, lo = om.eval(p.T.reshape(-1), 96)
+    assert_close(hg, ho, "kquant long prefill hidden")
+    assert_close(lg, lo, "kquant long prefill logits")
+    for i in range(3):
+        tok = np.zeros(hp.num_codebooks + 1, np.int32)
+        tok[0] = 17 + i
+        hg, lg = m.step(tok)
+        ho, lo = om.eval(tok, 1)
+        assert_close(lg, lo, f"kquant step {i} after long prefill")
