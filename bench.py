@@ -311,6 +311,108 @@ def run_ragged(args, rank: int, world: int, local: int) -> None:
         dist.destroy_process_group()
 
 
+LONG_UTTS = 8
+LONG_PROMPT = 4096
+LONG_FRAMES = 2000
+LONG_METRIC = "codec frames/s, F16 weights, long context (4096-token prompt + 2000 sampled frames), aggregate"
+
+
+def run_long(args, rank: int, world: int, local: int) -> None:
+    """F16 long-context decode: LONG_UTTS utterances, each a LONG_PROMPT-token
+    prompt then --frames-scale x LONG_FRAMES frames sampled at temperature 0.7,
+    top-p 0.9 with the device RNG, dealt round-robin to the GPUs.  A GPU with
+    one utterance runs the batch-1 frame loop (s2k_generate_device); a GPU
+    with several decodes them as one continuous batch (s2k_sched_*)."""
+    import torch
+    import torch.distributed as dist
+    import s2k  # noqa: E402
+
+    dist_on = world > 1
+    if dist_on:
+        torch.cuda.set_device(local)
+        shard.init("nccl", local, timeout_s=900)
+    torch.cuda.set_device(local)
+    hp = synthetic.preset(args.preset)
+    threads = max(1, (os.cpu_count() or 8) // max(world, 1))
+    tensors = build_weights(hp, threads, "f16")
+    m = s2k.SlowARModel(hp, device=local)
+    m.load_tensors(tensors)
+    del tensors
+    frames = max(1, int(round(LONG_FRAMES * args.frames_scale)))
+    P = args.long_prompt
+    mine = [i for i in range(args.utterances) if i % world == rank]
+    prompts = {i: synthetic.semantic_prompt(hp, P, seed=SEED + 31 * i) for i in mine}
+    kw = dict(temperature=0.7, top_p=0.9, top_k=0, im_end_id=-1, seed=SEED, min_tokens_before_end=frames)
+    stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
+    if len(mine) == 1:
+        i = mine[0]
+        m.init_kv_cache(P + frames + 1)
+        d_prompt = torch.from_numpy(np.ascontiguousarray(prompts[i].T)).to(f"cuda:{local}")
+        d_codes = torch.zeros((hp.num_codebooks, frames), dtype=torch.int32, device=f"cuda:{local}")
+
+        def job(nf):
+            n = m.generate_device(d_prompt.data_ptr(), P, d_codes.data_ptr(), nf, seq_id=i, **dict(kw, min_tokens_before_end=nf))
+            assert n == nf, n
+        warm = lambda: job(4)  # noqa: E731
+        mode = "batch-1 frame loop"
+    else:
+        sc = s2k.BatchScheduler(m, max_batch=len(mine), max_seq_len=P + frames + 1)
+
+        def job(nf):
+            for i in mine:
+                sc.submit(prompts[i], nf, seq_id=i, **dict(kw, min_tokens_before_end=nf))
+            sc.run()
+        warm = lambda: [job(k) for k in (len(mine),)]  # noqa: E731
+        mode = f"continuous batch of {len(mine)}"
+    for _ in range(args.warmup):
+        warm()
+    torch.cuda.synchronize()
+    if dist_on:
+        dist.barrier()
+    clocks = Clocks(local)
+    s2k.launch_count(reset=True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        job(frames)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    wall_ms = (time.perf_counter() - t_wall) * 1e3
+    launches = s2k.launch_count()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist_on:
+        dist.barrier()
+    ms_max = shard.max_over_ranks(ms, f"cuda:{local}")
+    wall_max = shard.max_over_ranks(wall_ms, f"cuda:{local}")
+    frames_all = args.utterances * frames * args.steps
+    slow_b, fast_b = weight_stream_bytes(hp, "f16")
+    if len(mine) > 1:
+        sc.close()
+    m.close()
+    if rank == 0:
+        line = {
+            "metric": LONG_METRIC, "value": frames_all / (ms_max / 1e3), "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": (f"{args.utterances} utterances x ({P}-token prompt + {frames} frames at T=0.7, "
+                                    f"top-p 0.9, device RNG), S2 Pro shape, F16 weights; round-robin over {world} "
+                                    f"GPU(s), {mode} per GPU"),
+                       "weights_per_frame_bytes": slow_b + (hp.num_codebooks - 1) * fast_b,
+                       "l2": "inputs larger than L2 (8.1 GB of Slow weights per frame)",
+                       "parallelism": f"request-level x{world}, no collectives"},
+            "e2e": {"value": frames_all / (wall_max / 1e3), "unit": "frames/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0, "note": "wall clock of the same run"},
+            "clocks": clk,
+            "gpu_launches": int(launches),
+        }
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -325,10 +427,12 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--preset", choices=["s2pro", "mid"], default="s2pro",
                     help="model shape; 'mid' (2+1 layers, real widths) is for small profiler captures only")
-    ap.add_argument("--workload", choices=["frames", "ragged"], default="frames",
+    ap.add_argument("--workload", choices=["frames", "ragged", "f16long"], default="frames",
                     help="frames: one utterance per GPU at batch 1 (default); ragged: continuous batching of "
-                         "--utterances utterances dealt round-robin to the GPUs")
-    ap.add_argument("--utterances", type=int, default=RAGGED_UTTS)
+                         "--utterances utterances dealt round-robin to the GPUs; f16long: F16 weights, 8 "
+                         "utterances of a 4096-token prompt + 2000 sampled frames")
+    ap.add_argument("--utterances", type=int, default=None)
+    ap.add_argument("--long-prompt", type=int, default=LONG_PROMPT)
     ap.add_argument("--frames-scale", type=float, default=1.0,
                     help="ragged: scale of the target frame counts (1.0 = U[100, 1500])")
     args = ap.parse_args()
@@ -341,7 +445,12 @@ def main() -> None:
         run_reference(args, rank)
         return
     if args.workload == "ragged":
+        args.utterances = args.utterances or RAGGED_UTTS
         run_ragged(args, rank, world, local)
+        return
+    if args.workload == "f16long":
+        args.utterances = args.utterances or LONG_UTTS
+        run_long(args, rank, world, local)
         return
 
     import torch
