@@ -499,9 +499,227 @@ __global__ void __launch_bounds__(kFlThreads) attn_flash_kernel(AttnArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Prompt prefill attention (one sequence, many query rows): one CTA per (kv
+// head g, block of 64 / G query rows), i.e. 64 query vectors (row x group
+// head) sharing each key split's K and V tile in shared memory.  Same split
+// convention and sums as attn_split_kernel, in two passes over the splits:
+//   1. K tile (doubles) -> scores of 64 query vectors x 64 keys with 4 x 4
+//      register blocks (written to the score scratch) and the split maxima
+//      (kept in shared memory);
+//   2. V tile + the split's exponentials (from the stored scores) -> S_i and
+//      O_i per query vector, folded with w_i = det_expf(m_i - M) in split
+//      order.
+// ---------------------------------------------------------------------------
+constexpr int kBlkThreads = 256;
+constexpr int kBlkQV = 64;         // query vectors per CTA
+constexpr int kBlkPad = 129;       // row stride (doubles) of the shared tiles: conflict-free columns
+constexpr int kBlkMaxSplits = 128; // longest key range: 8192 positions
+
+size_t attn_block_smem(int nsp) {
+    return (size_t)2 * kBlkQV * kBlkPad * sizeof(double)  // q (then e) tile, K / V tile
+           + (size_t)kBlkQV * nsp * sizeof(float)           // split maxima
+           + (size_t)kBlkQV * (sizeof(float) + sizeof(double) + sizeof(int)) + 64;
+}
+
+// K or V rows j0 .. j0+63 of the CTA's kv head as doubles (0 past `lim`).
+__device__ __forceinline__ void blk_load_tile(const AttnArgs &a, const __half *cache, const float *cur, int g,
+                                              int nc, int j0, int lim, double *dst) {
+    for (int idx = threadIdx.x; idx < kAttnSplit * 32; idx += kBlkThreads) {
+        const int jj = idx >> 5, d4 = (idx & 31) * 4, j = j0 + jj;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (j < lim) {
+            if (j < nc) {
+                const int page = __ldcg(a.kv.block_table + j / kPage);
+                const size_t off =
+                    ((((size_t)page * a.kv.n_layers + a.layer) * a.kv.n_kv_heads + g) * kPage + j % kPage) * 128 + d4;
+                const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(cache + off));
+                const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+                const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+                v[0] = f0.x;
+                v[1] = f0.y;
+                v[2] = f1.x;
+                v[3] = f1.y;
+            } else {
+                const float4 f = __ldcg(reinterpret_cast<const float4 *>(cur + ((size_t)(j - nc) * a.Hkv + g) * 128 + d4));
+                v[0] = f.x;
+                v[1] = f.y;
+                v[2] = f.z;
+                v[3] = f.w;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) dst[jj * kBlkPad + d4 + u] = (double)v[u];
+    }
+}
+
+__global__ void __launch_bounds__(kBlkThreads, 1) attn_block_kernel(AttnArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.done && __ldcg(a.done)) return;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int g = blockIdx.x;
+    const int G = a.H / a.Hkv, BQ = kBlkQV / G;  // query rows per CTA
+    const int t0 = blockIdx.y * BQ;
+    const int tid = threadIdx.x, qb = tid >> 4, kb = tid & 15;
+    const int nc = a.n_cached ? __ldcg(a.n_cached) : 0;
+    const int nsp_cap = (a.max_keys + kAttnSplit - 1) / kAttnSplit;
+    double *qd = reinterpret_cast<double *>(smem);  // [64][kBlkPad] queries, then the split's e_j
+    double *kd = qd + kBlkQV * kBlkPad;               // [64][kBlkPad] K or V tile
+    float *mi = reinterpret_cast<float *>(kd + kBlkQV * kBlkPad);  // [64][nsp_cap]
+    float *Mx = mi + kBlkQV * nsp_cap;                               // [64]
+    double *ss = reinterpret_cast<double *>(((uintptr_t)(Mx + kBlkQV) + 7) & ~(uintptr_t)7);  // [64]
+    int *lk = reinterpret_cast<int *>(ss + kBlkQV);                  // [64] key range of each query vector
+    // query vector qv: row t0 + qv / G, head g * G + qv % G
+    int lim = 0;  // the block's longest key range
+    for (int qv = tid; qv < kBlkQV; qv += kBlkThreads) {
+        const int t = t0 + qv / G;
+        lk[qv] = t < a.T ? nc + a.cur_base + t + 1 : 0;
+    }
+    {
+        const int tl = min(a.T, t0 + BQ) - 1;
+        lim = nc + a.cur_base + tl + 1;
+    }
+    if (lim > a.ld_scores || lim > a.max_keys || (nc > 0 && (nc - 1) / kPage >= a.kv.n_pages)) {
+        if (tid == 0 && a.err) atomicOr(a.err, ERR_BAD_POS);
+        return;
+    }
+    const int nsp = (lim + kAttnSplit - 1) / kAttnSplit;
+    for (int idx = tid; idx < kBlkQV * 32; idx += kBlkThreads) {
+        const int qv = idx >> 5, d4 = (idx & 31) * 4, t = t0 + qv / G;
+        float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < a.T)
+            f = __ldcg(reinterpret_cast<const float4 *>(a.q + (size_t)t * a.ldq + (size_t)(g * G + qv % G) * 128 + d4));
+        qd[qv * kBlkPad + d4] = (double)f.x;
+        qd[qv * kBlkPad + d4 + 1] = (double)f.y;
+        qd[qv * kBlkPad + d4 + 2] = (double)f.z;
+        qd[qv * kBlkPad + d4 + 3] = (double)f.w;
+    }
+    // ---- pass 1: scores and split maxima ----
+    for (int i = 0; i < nsp; ++i) {
+        const int j0 = i * kAttnSplit;
+        __syncthreads();  // previous tile consumed
+        blk_load_tile(a, a.kv.k, a.kcur, g, nc, j0, lim, kd);
+        __syncthreads();
+        double acc[4][4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+            for (int y = 0; y < 4; ++y) acc[x][y] = 0.0;
+        // thread (qb, kb): query vectors qb + 16x, keys kb + 16y of the split
+#pragma unroll 4
+        for (int d = 0; d < 128; ++d) {
+            double qv4[4], kv4[4];
+#pragma unroll
+            for (int x = 0; x < 4; ++x) qv4[x] = qd[(qb + 16 * x) * kBlkPad + d];
+#pragma unroll
+            for (int y = 0; y < 4; ++y) kv4[y] = kd[(kb + 16 * y) * kBlkPad + d];
+#pragma unroll
+            for (int x = 0; x < 4; ++x)
+#pragma unroll
+                for (int y = 0; y < 4; ++y) acc[x][y] = fma(kv4[y], qv4[x], acc[x][y]);
+        }
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+            const int qv = qb + 16 * x, t = t0 + qv / G, gh = g * G + qv % G;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+                const int j = j0 + kb + 16 * y;
+                if (j < lk[qv]) {
+                    const float sc = __fmul_rn((float)acc[x][y], a.scale);
+                    a.scores[((size_t)t * a.H + gh) * a.ld_scores + j] = sc;
+                    mx = fmaxf(mx, sc);
+                }
+            }
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (kb == 0) mi[qv * nsp_cap + i] = mx;
+        }
+    }
+    __syncthreads();
+    // M per query vector over its own splits
+    for (int qv = tid; qv < kBlkQV; qv += kBlkThreads) {
+        float M = -INFINITY;
+        const int ns = (lk[qv] + kAttnSplit - 1) / kAttnSplit;
+        for (int i = 0; i < ns; ++i) M = fmaxf(M, mi[qv * nsp_cap + i]);
+        Mx[qv] = M;
+    }
+    // ---- pass 2: e_j, S_i, O_i, folded in split order ----
+    // thread (qb, db): query vectors qb + 16x, dims db + 16y
+    double acc[4][8], ssum[4];
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+        ssum[x] = 0.0;
+#pragma unroll
+        for (int y = 0; y < 8; ++y) acc[x][y] = 0.0;
+    }
+    double *ed = qd;  // [64][kBlkPad]: e_j of the split (queries are no longer needed)
+    for (int i = 0; i < nsp; ++i) {
+        const int j0 = i * kAttnSplit;
+        __syncthreads();
+        blk_load_tile(a, a.kv.v, a.vcur, g, nc, j0, lim, kd);
+        for (int idx = tid; idx < kBlkQV * kAttnSplit; idx += kBlkThreads) {
+            const int qv = idx >> 6, jj = idx & 63, j = j0 + jj;
+            float e = 0.f;
+            if (j < lk[qv]) {
+                const int t = t0 + qv / G, gh = g * G + qv % G;
+                e = det_expf(__fsub_rn(__ldcg(a.scores + ((size_t)t * a.H + gh) * a.ld_scores + j), mi[qv * nsp_cap + i]));
+            }
+            ed[qv * kBlkPad + jj] = (double)e;
+        }
+        __syncthreads();
+        double o[4][8];
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+            for (int y = 0; y < 8; ++y) o[x][y] = 0.0;
+        for (int jj = 0; jj < kAttnSplit; ++jj) {
+            double e4[4], v8[8];
+#pragma unroll
+            for (int x = 0; x < 4; ++x) e4[x] = ed[(qb + 16 * x) * kBlkPad + jj];
+#pragma unroll
+            for (int y = 0; y < 8; ++y) v8[y] = kd[jj * kBlkPad + kb + 16 * y];
+#pragma unroll
+            for (int x = 0; x < 4; ++x)
+#pragma unroll
+                for (int y = 0; y < 8; ++y) o[x][y] = fma(v8[y], e4[x], o[x][y]);
+        }
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+            const int qv = qb + 16 * x;
+            if (j0 >= lk[qv]) continue;  // beyond this query's keys
+            const double wi = (double)det_expf(__fsub_rn(mi[qv * nsp_cap + i], Mx[qv]));
+#pragma unroll
+            for (int y = 0; y < 8; ++y) acc[x][y] += o[x][y] * wi;
+            if (kb == 0) {
+                double si = 0.0;
+                for (int jj = 0; jj < kAttnSplit; ++jj) si += ed[qv * kBlkPad + jj];
+                ssum[x] += si * wi;
+            }
+        }
+    }
+    if (kb == 0)
+#pragma unroll
+        for (int x = 0; x < 4; ++x) ss[qb + 16 * x] = ssum[x];
+    __syncthreads();
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+        const int qv = qb + 16 * x, t = t0 + qv / G;
+        if (t >= a.T) continue;
+        const double S = ss[qv];
+#pragma unroll
+        for (int y = 0; y < 8; ++y)
+            a.out[(size_t)t * a.H * 128 + (size_t)(g * G + qv % G) * 128 + kb + 16 * y] = (float)(acc[x][y] / S);
+    }
+}
+
 cudaError_t attn_setup() {
     cudaError_t e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kAttnSmemMax);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attn_block_smem(kBlkMaxSplits));
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(attn_flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)attn_flash_smem(kMaxGroup, kFlMaxSplits));
@@ -522,6 +740,15 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st) {
             pdl_cfg(dim3(gx, a.Hkv, a.T), dim3(kFlThreads), attn_flash_smem(G, a.fl_nsp), st, attr);
         count_launch();
         return cudaLaunchKernelEx(&cfg, attn_flash_kernel, a);
+    }
+    if (!a.rows && a.T >= 16 && kBlkQV % G == 0 && nsp <= kBlkMaxSplits) {
+        // prompt prefill: 64 query vectors per CTA share the key tiles
+        cudaLaunchAttribute attr[1];
+        const int bq = kBlkQV / G;
+        cudaLaunchConfig_t cfg =
+            pdl_cfg(dim3(a.Hkv, (a.T + bq - 1) / bq), dim3(kBlkThreads), attn_block_smem(nsp), st, attr);
+        count_launch();
+        return cudaLaunchKernelEx(&cfg, attn_block_kernel, a);
     }
     const size_t smem = attn_split_smem(G, nsp);
     if (smem > kAttnSmemMax) return cudaErrorInvalidValue;
