@@ -25,7 +25,6 @@
 #include "s2k_model.h"
 
 #include <algorithm>
-#include <chrono>
 #include <cstring>
 #include <deque>
 #include <map>
