@@ -1158,6 +1158,9 @@ static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
     if (hp.num_codebooks > 16) ok = false;  // the persistent kernel's embedding sums at most 16 codebooks
     s->use_mega = ok;
     if (!ok) return S2K_OK;
+    s->mega_q8 = true;  // every GEMV Q8_0: the kernel variant with that consumer only
+    for (const MegaOp &o : ops)
+        if (o.kind == MK_GEMV && o.g.wtype != TW_Q8_0) s->mega_q8 = false;
     m->release(s->mega_ops);
     s->mega_ops = nullptr;
     CU(m->alloc(&s->mega_ops, ops.size()));
@@ -1177,14 +1180,14 @@ static cudaError_t enqueue_frame_mega(s2k_model *m, s2k_seq *s) {
     if ((e = cudaMemsetAsync(s->mega_ctl, 0, sizeof(MegaCtl) * nseg, st))) return e;
     for (int p = 0; p + 1 < hp.num_codebooks; ++p) {
         if ((e = launch_mega(s->mega_ops + s->seg_start[p], s->seg_len[p], s->seg_mt[p], s->mega_ctl + p, done,
-                             m->d_err, m->num_sms, st, m->d_epoch)))
+                             m->d_err, m->num_sms, st, m->d_epoch, s->mega_q8)))
             return e;
         if ((e = launch_sample_fast(m->flogits, s->dev, p + 1, m->d_err, st))) return e;
     }
     if ((e = launch_frame_commit(s->dev, st))) return e;
     const int last = nseg - 1;
     if ((e = launch_mega(s->mega_ops + s->seg_start[last], s->seg_len[last], s->seg_mt[last], s->mega_ctl + last, done,
-                         m->d_err, m->num_sms, st, m->d_epoch)))
+                         m->d_err, m->num_sms, st, m->d_epoch, s->mega_q8)))
         return e;
     return launch_sample_main(m->logits, s->dev, m->d_err, st);
 }
@@ -1456,13 +1459,13 @@ S2K_API s2k_status s2k_profile_frame(s2k_model *m, s2k_seq *s, int32_t reps, dou
         if ((err = cudaMemsetAsync(cf, 0, sizeof(MegaCtl), m->stream))) break;
         if ((err = cudaEventRecord(ev[4 * r], m->stream))) break;
         if ((err = launch_mega(s->mega_ops + s->seg_start[fseg], s->seg_len[fseg], s->seg_mt[fseg], cf, nullptr,
-                               m->d_err, m->num_sms, m->stream, m->d_epoch)))
+                               m->d_err, m->num_sms, m->stream, m->d_epoch, s->mega_q8)))
             break;
         if ((err = cudaEventRecord(ev[4 * r + 1], m->stream))) break;
         if ((err = cudaMemsetAsync(cs, 0, sizeof(MegaCtl), m->stream))) break;
         if ((err = cudaEventRecord(ev[4 * r + 2], m->stream))) break;
         if ((err = launch_mega(s->mega_ops + s->seg_start[sseg], slow_len, s->seg_mt[sseg], cs, nullptr, m->d_err,
-                               m->num_sms, m->stream, m->d_epoch)))
+                               m->num_sms, m->stream, m->d_epoch, s->mega_q8)))
             break;
         err = cudaEventRecord(ev[4 * r + 3], m->stream);
     }
@@ -1515,7 +1518,7 @@ static s2k_status trace_segment(s2k_model *m, s2k_seq *s, int segment, int reps,
     for (int r = 0; r < reps && err == cudaSuccess; ++r) {
         if ((err = cudaMemsetAsync(ctl, 0, sizeof(MegaCtl), m->stream))) break;
         err = launch_mega(s->mega_ops + s->seg_start[segment], len, s->seg_mt[segment], ctl, nullptr, m->d_err,
-                          m->num_sms, m->stream, m->d_epoch, d_tr + (size_t)r * per);
+                          m->num_sms, m->stream, m->d_epoch, s->mega_q8, d_tr + (size_t)r * per);
     }
     tr.assign((size_t)reps * per, 0ull);
     if (err == cudaSuccess)

@@ -251,7 +251,9 @@ __device__ void mega_kv_prefetch(const MegaOp *ops, int n_ops, MSmem &sm, int ct
 // ---------------------------------------------------------------------------
 // GEMV op (consumer side): activation prologue, then this CTA's tiles
 // ---------------------------------------------------------------------------
-template <int MT>
+// Q8: every GEMV of the launch is Q8_0 (the kernel then carries only that
+// consumer, which keeps its code compact).
+template <int MT, bool Q8>
 __device__ void mega_gemv(const MegaGemv &gref, const F8 (&nw)[kMPC], MSmem &sm, int cta, int G, int &slot,
                           uint32_t &phase, int *err, unsigned long long *tr, uint32_t ep8) {
     MegaGemv g = gref;  // op fields in registers; the op list holds producer op indices, the launch its epoch
@@ -266,8 +268,12 @@ __device__ void mega_gemv(const MegaGemv &gref, const F8 (&nw)[kMPC], MSmem &sm,
                                  tr != nullptr ? tr + 4 : nullptr, err);
     named_sync(1, kMNC);
     if (tr != nullptr && threadIdx.x == 0) tr[1] = globaltimer_ns();
-    tg_consume_any<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.u.g.xq, sm.u.g.xd, sm.u.g.xbs, cta, G, err,
-                   tr != nullptr ? tr + 6 : nullptr);
+    if constexpr (Q8)
+        tg_consume<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.u.g.xq, sm.u.g.xd, cta, G, err,
+                       tr != nullptr ? tr + 6 : nullptr);
+    else
+        tg_consume_any<MT>(g, &sm.ring[0][0], sm.full, sm.empty, kMStages, slot, phase, sm.u.g.xq, sm.u.g.xd,
+                           sm.u.g.xbs, cta, G, err, tr != nullptr ? tr + 6 : nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -747,7 +753,7 @@ __device__ void mega_embed_fast(const MegaEmbedFast &e, int cta, int G, int *err
 
 // 9 warps per CTA: one SM sub-partition holds three of them, so its 16K
 // registers cap a thread at 168 (the launch bound keeps the kernel there).
-template <int MT>
+template <int MT, bool Q8>
 __global__ void __launch_bounds__(kMThreads, 1)
     mega_kernel(const MegaOp *__restrict__ ops, int n_ops, MegaCtl *ctl, const int *done, int *err, int l2_ahead,
                 unsigned long long *trace, int flags, unsigned *epoch) {
@@ -801,7 +807,7 @@ __global__ void __launch_bounds__(kMThreads, 1)
         stamp(i, 1);
         switch (kind) {
         case MK_GEMV:
-            mega_gemv<MT>(ops[i].g, nw, sm, cta, G, cslot, cphase, err,
+            mega_gemv<MT, Q8>(ops[i].g, nw, sm, cta, G, cslot, cphase, err,
                           trace != nullptr ? trace + ((size_t)i * G + cta) * kTraceSlots : nullptr, ep8);
             break;
         case MK_ATTN:
@@ -854,13 +860,17 @@ int mega_l2_ahead() {
 
 cudaError_t mega_setup() {
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(mega_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MSmem))))
+    if ((e = cudaFuncSetAttribute(mega_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MSmem))))
         return e;
-    return cudaFuncSetAttribute(mega_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MSmem));
+    if ((e = cudaFuncSetAttribute(mega_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MSmem))))
+        return e;
+    if ((e = cudaFuncSetAttribute(mega_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MSmem))))
+        return e;
+    return cudaFuncSetAttribute(mega_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MSmem));
 }
 
 cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, const int *done, int *err, int num_sms,
-                        cudaStream_t st, unsigned *epoch, unsigned long long *trace) {
+                        cudaStream_t st, unsigned *epoch, bool q8, unsigned long long *trace) {
     if (mt < 1 || mt > kMaxT) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
@@ -876,8 +886,14 @@ cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, co
     const int ahead = mega_l2_ahead();
     const char *fe = getenv("S2K_MEGA_FLAGS");
     const int flags = fe ? atoi(fe) : 0;
-    if (mt == 1) return cudaLaunchKernelEx(&cfg, mega_kernel<1>, d_ops, n_ops, ctl, done, err, ahead, trace, flags, epoch);
-    return cudaLaunchKernelEx(&cfg, mega_kernel<2>, d_ops, n_ops, ctl, done, err, ahead, trace, flags, epoch);
+    if (q8) {
+        if (mt == 1)
+            return cudaLaunchKernelEx(&cfg, mega_kernel<1, true>, d_ops, n_ops, ctl, done, err, ahead, trace, flags, epoch);
+        return cudaLaunchKernelEx(&cfg, mega_kernel<2, true>, d_ops, n_ops, ctl, done, err, ahead, trace, flags, epoch);
+    }
+    if (mt == 1)
+        return cudaLaunchKernelEx(&cfg, mega_kernel<1, false>, d_ops, n_ops, ctl, done, err, ahead, trace, flags, epoch);
+    return cudaLaunchKernelEx(&cfg, mega_kernel<2, false>, d_ops, n_ops, ctl, done, err, ahead, trace, flags, epoch);
 }
 
 }  // namespace s2k

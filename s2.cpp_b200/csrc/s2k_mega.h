@@ -115,7 +115,7 @@ cudaError_t mega_setup();
 // grid barrier.  Slots a launch does not reach stay as they were.
 constexpr int kTraceSlots = 12;
 cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, const int *done, int *err, int num_sms,
-                        cudaStream_t st, unsigned *epoch, unsigned long long *trace = nullptr);
+                        cudaStream_t st, unsigned *epoch, bool q8, unsigned long long *trace = nullptr);
 // Tiles per CTA the producer keeps in flight into L2 beyond its ring.
 int mega_l2_ahead();
 // Host-side validation of a GEMV op for the persistent kernel.

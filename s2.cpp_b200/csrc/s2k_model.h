@@ -153,6 +153,7 @@ struct s2k_seq {
     MegaCtl *mega_ctl = nullptr;
     std::vector<int> seg_start, seg_len, seg_mt;
     bool use_mega = false;
+    bool mega_q8 = false;  // every GEMV op of the frame program is Q8_0
     KvPaged kv() const {
         KvPaged p;
         p.k = k;
