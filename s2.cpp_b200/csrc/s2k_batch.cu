@@ -529,10 +529,37 @@ static s2k_status sched_retire(s2k_sched *sc, int i) {
     return S2K_OK;
 }
 
+// Map request r's pages into sequence s, prefill its prompt and sample its
+// first main token.
+static s2k_status admit_one(s2k_sched *sc, Req &r, s2k_seq *s, const std::vector<int> &pages) {
+    s2k_model *m = sc->m;
+    const int need = (int)pages.size();
+    CU(cudaMemcpy(s->block_table, pages.data(), (size_t)need * sizeof(int), cudaMemcpyHostToDevice));
+    s->n_pages = need;
+    s->max_seq_len = need * kPage;
+    s2k_status rc = seq_publish(s);
+    if (rc) return rc;
+    rc = ensure_codes(m, s, r.gp.max_new_tokens);
+    if (rc) return rc;
+    const size_t ptoks = r.prompt_tm.size();
+    if (sc->prompt_cap < ptoks) {
+        m->release(sc->prompt_dev);
+        sc->prompt_dev = nullptr;
+        sc->prompt_cap = 0;
+        CU(m->alloc(&sc->prompt_dev, ptoks));
+        sc->prompt_cap = ptoks;
+    }
+    CU(cudaMemcpyAsync(sc->prompt_dev, r.prompt_tm.data(), ptoks * sizeof(int32_t), cudaMemcpyHostToDevice,
+                       m->stream));
+    rc = seq_begin_core(m, s, sc->prompt_dev, r.cols, &r.gp, s->codes, s->codes_cap);
+    if (rc) return rc;
+    CU(cudaStreamSynchronize(m->stream));
+    return check_err_word(m);
+}
+
 // Admit waiting requests (FIFO) while a slot and their pages are free:
 // map pages, prefill, sample the first main token.
 static s2k_status sched_admit(s2k_sched *sc) {
-    s2k_model *m = sc->m;
     while (!sc->waiting.empty()) {
         const int id = sc->waiting.front();
         Req &r = sc->reqs[id];
@@ -549,27 +576,14 @@ static s2k_status sched_admit(s2k_sched *sc) {
         s2k_seq *s = sl.seq;
         sl.pages.assign(sc->free_pages.end() - need, sc->free_pages.end());
         sc->free_pages.resize(sc->free_pages.size() - need);
-        CU(cudaMemcpy(s->block_table, sl.pages.data(), (size_t)need * sizeof(int), cudaMemcpyHostToDevice));
-        s->n_pages = need;
-        s->max_seq_len = need * kPage;
-        s2k_status rc = seq_publish(s);
-        if (rc) return rc;
-        rc = ensure_codes(m, s, r.gp.max_new_tokens);
-        if (rc) return rc;
-        const size_t ptoks = r.prompt_tm.size();
-        if (sc->prompt_cap < ptoks) {
-            m->release(sc->prompt_dev);
-            sc->prompt_dev = nullptr;
-            CU(m->alloc(&sc->prompt_dev, ptoks));
-            sc->prompt_cap = ptoks;
+        s2k_status rc = admit_one(sc, r, s, sl.pages);
+        if (rc) {
+            // the request goes back to the head of the queue, its pages to the pool
+            for (int pg : sl.pages) sc->free_pages.push_back(pg);
+            sl.pages.clear();
+            sc->waiting.push_front(id);
+            return rc;
         }
-        CU(cudaMemcpyAsync(sc->prompt_dev, r.prompt_tm.data(), ptoks * sizeof(int32_t), cudaMemcpyHostToDevice,
-                           m->stream));
-        rc = seq_begin_core(m, s, sc->prompt_dev, r.cols, &r.gp, s->codes, s->codes_cap);
-        if (rc) return rc;
-        CU(cudaStreamSynchronize(m->stream));
-        rc = check_err_word(m);
-        if (rc) return rc;
         sl.req = id;
         r.slot = si;
         r.state = S2K_REQ_LIVE;
