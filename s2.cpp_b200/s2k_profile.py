@@ -113,6 +113,53 @@ def _layer_table(tr: np.ndarray, kinds: np.ndarray) -> dict:
     return out
 
 
+def _gemv_shapes(hp, fast: bool) -> dict:
+    """(R, K) of the layer GEMVs of a segment, by op name."""
+    if fast:
+        d, H, Hkv, hd, ff = (hp.fast_embedding_length, hp.fast_head_count, hp.fast_head_count_kv, hp.fast_head_dim,
+                             hp.fast_feed_forward_length)
+    else:
+        d, H, Hkv, hd, ff = hp.embedding_length, hp.head_count, hp.head_count_kv, hp.head_dim, hp.feed_forward_length
+    return {"qkv": ((H + 2 * Hkv) * hd, d), "wo": (d, H * hd), "w13": (2 * ff, d), "w2": (d, ff)}
+
+
+def _critical_table(tr: np.ndarray, kinds: np.ndarray, shapes: dict) -> dict:
+    """Per op of a layer (mean over layers): `lat` = last CTA done of this op
+    minus last CTA done of the previous op (the op's share of the launch's
+    critical path).  For the GEMV ops, on the CTA that finished last:
+    `land` = its activation loads landed [4] after the previous op's last
+    done, `quant` = prologue end [1] after [4], `tile0` = first weight tile
+    ready [6] after [1], `tiles` = done [2] after [6], `n` = its weight tiles
+    in the op, `issued` = the producer's last tile of the op issued [3]
+    relative to [1] (negative: every tile was requested before the consumers
+    needed it); `us_per_tile` = median over CTAs with work of ([2] - [6]) / n."""
+    T = tr.astype(np.int64)
+    n = T.shape[0] - 1
+    G = T.shape[1]
+    dn = T[:, :, 2]
+    k = list(kinds)
+    first = k.index(2) - 1
+    nl = (n - first - 1) // 5
+    acc = {nm: [] for nm in OP_NAMES}
+    for l in range(nl):
+        for j, nm in enumerate(OP_NAMES):
+            i = first + 5 * l + j
+            prev = dn[i - 1].max()
+            c = int(dn[i].argmax())
+            row = dict(lat=(dn[i].max() - prev) / 1e3)
+            if nm in shapes:
+                R, K = shapes[nm]
+                RT, NKT = R // 32, K // 512
+                ntile = np.array([(RT * (cc + 1) // G - RT * cc // G) * NKT for cc in range(G)])
+                row.update(land=(T[i, c, 4] - prev) / 1e3, quant=(T[i, c, 1] - T[i, c, 4]) / 1e3,
+                           tile0=(T[i, c, 6] - T[i, c, 1]) / 1e3, tiles=(T[i, c, 2] - T[i, c, 6]) / 1e3,
+                           n=int(ntile[c]), issued=(T[i, c, 3] - T[i, c, 1]) / 1e3)
+                w = ntile > 0
+                row["us_per_tile"] = float(np.median((T[i, w, 2] - T[i, w, 6]) / ntile[w])) / 1e3
+            acc[nm].append(row)
+    return {nm: {key: round(float(np.mean([r[key] for r in rows])), 2) for key in rows[0]} for nm, rows in acc.items()}
+
+
 def cmd_ops(a) -> None:
     hp, m = _model(a.preset, a.quant)
     prompt = synthetic.text_prompt(hp, 64, seed=7)
@@ -124,6 +171,8 @@ def cmd_ops(a) -> None:
         tr = m.profile_trace(seg)
         _, kinds = m.profile_ops(seg, reps=1)
         print(json.dumps({label: _layer_table(tr, kinds)}), flush=True)
+        crit = _critical_table(tr, kinds, _gemv_shapes(hp, seg > 0))
+        print(json.dumps({label + "_critical_path": crit}), flush=True)
     m.close()
 
 
