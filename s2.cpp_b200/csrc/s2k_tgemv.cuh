@@ -119,6 +119,28 @@ __device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *q, int *sc, 
     }
 }
 
+// The 8 six-bit scales and mins of a Q4_K super-block header, one per byte,
+// from its 12 packed bytes in words w0 = bytes 0..3, w1 = 4..7, w2 = 8..11
+// (get_scale_min_k4 for all sub-blocks at once, in registers): scales of
+// sub-blocks 0..3 / 4..7, mins of 0..3 / 4..7.
+__device__ __forceinline__ void q4k_scales4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t &sc_lo, uint32_t &sc_hi,
+                                            uint32_t &mn_lo, uint32_t &mn_hi) {
+    sc_lo = w0 & 0x3f3f3f3fu;
+    mn_lo = w1 & 0x3f3f3f3fu;
+    sc_hi = (w2 & 0x0f0f0f0fu) | ((w0 >> 2) & 0x30303030u);
+    mn_hi = ((w2 >> 4) & 0x0f0f0f0fu) | ((w1 >> 2) & 0x30303030u);
+}
+
+// Shared-memory layout of a Q8_K activation row: byte o of the row is stored
+// at q8k_swz(o) (an XOR of 16-byte chunk bits inside each 512-byte block), so
+// that the eight lanes of a quarter-warp, which read 16-byte chunks 128 or 256
+// bytes apart in the K-quant consumers, hit all 32 banks.  Q4_K readers vary
+// chunk bits 2..4 of (o >> 4) at fixed bits 0..1, Q6_K readers bits 0, 3, 4 at
+// fixed bits 1..2; the swizzle maps either set onto bank-group bits 0..2.
+__device__ __forceinline__ int q8k_swz(int o, int wtype) {
+    return wtype == TW_Q6_K ? o ^ (((o >> 6) & 6) << 4) : o ^ (((o >> 7) & 3) << 4);
+}
+
 // Element (r, c) of a tiled matrix with K columns, dequantized as ggml's
 // dequantize_row_q8_0 / _q4_K / _q6_K do (float products in the same order).
 __device__ __forceinline__ float tq_elem(const uint8_t *w, int wtype, int K, long long r, int c) {
@@ -478,7 +500,8 @@ __device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC],
                 continue;
             }
             if (q8k) {
-                quant_q8k_warp(y.v, lane, valid, xq + 8 * (size_t)v, xd + (v >> 5), xbs + ((v >> 5) << 4));
+                quant_q8k_warp(y.v, lane, valid, xq + (size_t)mrow[j] * K + q8k_swz(8 * (v - mrow[j] * KC), g.wtype),
+                               xd + (v >> 5), xbs + ((v >> 5) << 4));
                 continue;
             }
             float amax = fabsf(y.v[0]);
@@ -639,13 +662,16 @@ __device__ __forceinline__ void tg_consume(const TGemv &g, const uint8_t *ring, 
 }
 
 // ---------------------------------------------------------------------------
-// K-quant consumers (Q8_K activation: xq int8 [M][K], xd [M][K/256] scales,
-// xbs [M][K/16] block sums).  Lane mapping per warp: row r = lane / 8 of the
-// warp's four rows (lane 8r holds row r after the reduction, as tg_emit
-// expects), s = lane % 8 picks super-block sb = s / 4 of the K-tile and a
-// quarter of its values.  Per super-block the integer sums are exact and the
-// block term is formed as ggml's vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K scale
-// it (d_w * d_x in float), then the terms are summed in double.
+// K-quant consumers (Q8_K activation: xq int8 [M][K] in the q8k_swz layout,
+// xd [M][K/256] scales, xbs [M][K/16] block sums).  Lane mapping per warp:
+// row r = lane / 8 of the warp's four rows (lane 8r holds row r after the
+// reduction, as tg_emit expects), s = lane % 8 picks super-block sb = s / 4 of
+// the K-tile and a quarter of its values.  Per super-block the integer sums
+// are exact and the block term is formed as ggml's vec_dot_q4_K_q8_K /
+// vec_dot_q6_K_q8_K scale it (d_w * d_x in float), then the terms are summed
+// in double.  Shared-memory reads are bank-conflict free: the activation by
+// its swizzle, the weight tile's two 16-byte halves of a lane by reading them
+// in an order that depends on sb.
 // ---------------------------------------------------------------------------
 template <int MT>
 __device__ __forceinline__ void tg_consume_q4k(const TGemv &g, const uint8_t *ring, uint64_t *full, uint64_t *empty,
@@ -658,6 +684,8 @@ __device__ __forceinline__ void tg_consume_q4k(const TGemv &g, const uint8_t *ri
     const int rt0 = (int)((long long)RT * cta / G), rt1 = (int)((long long)RT * (cta + 1) / G);
     const int r = lane >> 3, s = lane & 7, sb = s >> 2, c = s & 3;
     const int row_in_tile = warp * kTRW + r;
+    const int sh16 = (c & 1) * 16;  // sub-blocks 2c, 2c+1: bytes 2(c&1), 2(c&1)+1 of the lo (c < 2) / hi scale words
+    const int wo0 = sb * 16, wo1 = wo0 ^ 16;  // the two 16-byte quant halves, read in sb order (bank spread)
     for (int rt = rt0; rt < rt1; ++rt) {
         double acc[MT];
         float resv[MT];
@@ -682,17 +710,19 @@ __device__ __forceinline__ void tg_consume_q4k(const TGemv &g, const uint8_t *ri
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
                 const int mm = m < M ? m : 0;
-                const int8_t *xp = xq + (size_t)mm * K + sbg * 256 + 64 * c;
+                const int8_t *xr = xq + (size_t)mm * K;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) xa[m][i] = reinterpret_cast<const int4 *>(xp)[i];
+                for (int i = 0; i < 4; ++i)
+                    xa[m][i] = *reinterpret_cast<const int4 *>(xr + q8k_swz(sbg * 256 + 64 * c + 16 * i, TW_Q4_K));
                 bsv[m] = *reinterpret_cast<const uint2 *>(xbs + (size_t)mm * (K >> 4) + sbg * 16 + 4 * c);
                 dx[m] = xd[mm * NSB + sbg];
             }
             mbar_wait(&full[slot], phase, err, ERR_WAIT_FULL);
             if (t_first != nullptr && tid == 0 && rt == rt0 && kt == 0) *t_first = globaltimer_ns();
             const uint8_t *t = ring + (size_t)slot * kTileBytes;
-            const int4 q0 = *reinterpret_cast<const int4 *>(t + (row_in_tile * 2 + sb) * 128 + 32 * c);
-            const int4 q1 = *reinterpret_cast<const int4 *>(t + (row_in_tile * 2 + sb) * 128 + 32 * c + 16);
+            const uint8_t *qb = t + (row_in_tile * 2 + sb) * 128 + 32 * c;
+            const int4 qa = *reinterpret_cast<const int4 *>(qb + wo0);
+            const int4 qc = *reinterpret_cast<const int4 *>(qb + wo1);
             const int4 hd = *reinterpret_cast<const int4 *>(t + kQ4kHdr + (row_in_tile * 2 + sb) * 16);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -700,10 +730,11 @@ __device__ __forceinline__ void tg_consume_q4k(const TGemv &g, const uint8_t *ri
                 slot = 0;
                 phase ^= 1u;
             }
-            const uint8_t *scb = reinterpret_cast<const uint8_t *>(&hd) + 4;
-            int sc0, mn0, sc1, mn1;
-            q4k_scale_min(2 * c, scb, &sc0, &mn0);
-            q4k_scale_min(2 * c + 1, scb, &sc1, &mn1);
+            const int4 q0 = sb ? qc : qa, q1 = sb ? qa : qc;
+            uint32_t sc_lo, sc_hi, mn_lo, mn_hi;
+            q4k_scales4((uint32_t)hd.y, (uint32_t)hd.z, (uint32_t)hd.w, sc_lo, sc_hi, mn_lo, mn_hi);
+            const uint32_t scw = ((c & 2) ? sc_hi : sc_lo) >> sh16, mnw = ((c & 2) ? mn_hi : mn_lo) >> sh16;
+            const int sc0 = scw & 0xff, sc1 = (scw >> 8) & 0xff, mn0 = mnw & 0xff, mn1 = (mnw >> 8) & 0xff;
             const float dw = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff)));
             const float dmw = __half2float(__ushort_as_half((unsigned short)((unsigned)hd.x >> 16)));
             const int qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
@@ -752,6 +783,7 @@ __device__ __forceinline__ void tg_consume_q6k(const TGemv &g, const uint8_t *ri
     const int r = lane >> 3, s = lane & 7, sb = s >> 2, h = (s >> 1) & 1, is = s & 1;
     const int row_in_tile = warp * kTRW + r;
     const int rb = row_in_tile * 2 + sb;
+    const int ao0 = sb * 32, ao1 = ao0 ^ 32;  // ql halves A (+0) and B (+32), read in sb order (bank spread)
     for (int rt = rt0; rt < rt1; ++rt) {
         double acc[MT];
         float resv[MT];
@@ -775,16 +807,19 @@ __device__ __forceinline__ void tg_consume_q6k(const TGemv &g, const uint8_t *ri
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
                 const int mm = m < M ? m : 0;
-                const int8_t *xp = xq + (size_t)mm * K + sbg * 256 + 128 * h + 16 * is;
+                const int8_t *xr = xq + (size_t)mm * K;
+                const int o = sbg * 256 + 128 * h + 16 * is;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) xa[m][k] = *reinterpret_cast<const int4 *>(xp + 32 * k);
+                for (int k = 0; k < 4; ++k)
+                    xa[m][k] = *reinterpret_cast<const int4 *>(xr + q8k_swz(o + 32 * k, TW_Q6_K));
                 dx[m] = xd[mm * NSB + sbg];
             }
             mbar_wait(&full[slot], phase, err, ERR_WAIT_FULL);
             if (t_first != nullptr && tid == 0 && rt == rt0 && kt == 0) *t_first = globaltimer_ns();
             const uint8_t *t = ring + (size_t)slot * kTileBytes;
-            const int4 A = *reinterpret_cast<const int4 *>(t + rb * 128 + 64 * h + 16 * is);
-            const int4 B = *reinterpret_cast<const int4 *>(t + rb * 128 + 64 * h + 32 + 16 * is);
+            const uint8_t *qlb = t + rb * 128 + 64 * h + 16 * is;
+            const int4 P0 = *reinterpret_cast<const int4 *>(qlb + ao0);
+            const int4 P1 = *reinterpret_cast<const int4 *>(qlb + ao1);
             const int4 Q = *reinterpret_cast<const int4 *>(t + kQ6kQh + rb * 64 + 32 * h + 16 * is);
             const int8_t *scp = reinterpret_cast<const int8_t *>(t + kQ6kSc + rb * 16 + 8 * h + is);
             const int sc0 = scp[0], sc1 = scp[2], sc2 = scp[4], sc3 = scp[6];
@@ -795,6 +830,7 @@ __device__ __forceinline__ void tg_consume_q6k(const TGemv &g, const uint8_t *ri
                 slot = 0;
                 phase ^= 1u;
             }
+            const int4 A = sb ? P1 : P0, B = sb ? P0 : P1;
             const int aw[4] = {A.x, A.y, A.z, A.w}, bw[4] = {B.x, B.y, B.z, B.w}, qw[4] = {Q.x, Q.y, Q.z, Q.w};
 #pragma unroll
             for (int m = 0; m < MT; ++m)
