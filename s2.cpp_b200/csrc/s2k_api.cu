@@ -110,9 +110,10 @@ cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int 
     }
     if (prefill && T >= kPrefillMinT && m->prefill_mma) {
         const int kmax = std::max(std::max(dim, w.qs), ff);
-        if ((e = m->alloc(&w.pf_xq, tn * kmax))) return e;
+        // Q8_K rows of a Q6_K GEMM are twice as wide (zero-padded sub-blocks)
+        if ((e = m->alloc(&w.pf_xq, tn * kmax * 2))) return e;
         if ((e = m->alloc(&w.pf_xh, tn * kmax))) return e;
-        if ((e = m->alloc(&w.pf_dx, tn * kmax / 32))) return e;
+        if ((e = m->alloc(&w.pf_dx, tn * kmax * 2 / 32))) return e;
         // stream-K partials (one CTA per SM), and K-tile
         // counters for every (row block, token tile) of the largest GEMM
         w.pf_part_n = prefill_part_doubles(m->num_sms);
@@ -189,8 +190,12 @@ cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool prefill, b
                                        m->num_sms, m->d_err, m->stream);
     }
     if (prefill && m->prefill_mma && w.pf_xq && g.M >= kPrefillMinT && g.M <= w.T && prefill_ok(*g.w, g.M)) {
-        cudaError_t e = launch_quant_rows_q8(g.x, g.ldx, g.M, g.w->cols, g.in_mode == IN_RMSNORM ? g.norm_w : nullptr,
-                                             g.eps, w.pf_xq, w.pf_dx, g.act_out, m->stream);
+        const float *nw = g.in_mode == IN_RMSNORM ? g.norm_w : nullptr;
+        cudaError_t e = g.w->type == S2K_TYPE_Q8_0
+                            ? launch_quant_rows_q8(g.x, g.ldx, g.M, g.w->cols, nw, g.eps, w.pf_xq, w.pf_dx, g.act_out,
+                                                   m->stream)
+                            : launch_quant_rows_q8k(g.x, g.ldx, g.M, g.w->cols, nw, g.eps, g.w->type, w.pf_xq, w.pf_dx,
+                                                    g.act_out, m->stream);
         if (e != cudaSuccess) return e;
         PrefillArgs a;
         a.w = g.w;
@@ -723,6 +728,19 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     m->prefill_mma = prefill_setup() == cudaSuccess;
     m->prefill_f16 = m->prefill_mma && prefill_f16_setup() == cudaSuccess;
     cudaGetLastError();  // a device without the tensor-map entry point keeps the GEMV path
+    if (m->prefill_mma) {
+        // int8 copies of the Slow stack's K-quant matrices for the tensor-core prefill
+        for (Layer &L : m->layers)
+            for (DevMat *dm : {&L.wqkv, &L.wo, &L.w13, &L.w2}) {
+                size_t side = 0;
+                const size_t nb = kq_prefill_bytes(*dm, &side);
+                if (nb == 0 || dm->pf) continue;
+                CU(m->alloc(&dm->pf, nb));
+                CU(m->alloc(&dm->pf_side, side));
+                CU(launch_build_kq_prefill(*dm, m->stream));
+            }
+        CU(cudaStreamSynchronize(m->stream));
+    }
     if (m->staging) {
         m->release(m->staging);
         m->staging = nullptr;

@@ -30,6 +30,11 @@ struct DevMat {
     int type = -1;  // ggml type id
     int rows = 0, cols = 0;
     uint8_t *w = nullptr;
+    // Q4_K / Q6_K matrices of the Slow stack: the int8 copy the tensor-core
+    // prefill reads and its (d, dmin) side array (s2k_prefill.cu); null when
+    // absent
+    uint8_t *pf = nullptr;
+    uint8_t *pf_side = nullptr;
     size_t bytes() const;
 };
 
@@ -101,6 +106,16 @@ cudaError_t launch_rows_f16(const float *x, int ldx, int T, int K, const float *
                             float *act_out, cudaStream_t st);
 cudaError_t launch_prefill_f16_gemm(const uint8_t *wtiles, int R, int K, int T, const __half *xh, int epi, float *y,
                                     int ldy, const float *res, int ldres, int num_sms, int *err, cudaStream_t st);
+// K-quant prefill copy of a Q4_K / Q6_K matrix: bytes of its int8 tiles (0
+// when the matrix cannot have one) and of its side array; the launch fills
+// w.pf / w.pf_side (allocated by the caller) from the decode tiles w.w.
+size_t kq_prefill_bytes(const DevMat &w, size_t *side_bytes);
+cudaError_t launch_build_kq_prefill(const DevMat &w, cudaStream_t st);
+// x [T][ldx] (optional RMSNorm) -> Q8_K rows for the K-quant GEMM of a matrix
+// of ggml type ggml_type: xq [T][Ke] int8 and slots [T][Ke/32], Ke = K (Q4_K)
+// or 2K (Q6_K, each 16 values followed by 16 zeros).
+cudaError_t launch_quant_rows_q8k(const float *x, int ldx, int T, int K, const float *norm_w, float eps, int ggml_type,
+                                  int8_t *xq, double *slots, float *act_out, cudaStream_t st);
 // x [T][ldx] (optional RMSNorm with norm_w, eps) -> xq [T][K] int8, dx [T][K/32]
 cudaError_t launch_quant_rows_q8(const float *x, int ldx, int T, int K, const float *norm_w, float eps, int8_t *xq,
                                  double *dx, float *act_out, cudaStream_t st);

@@ -31,6 +31,18 @@
 // Partials of (row block, token tile) pairs split over CTAs go to global
 // scratch; the CTA that completes a pair adds them in K order and runs the
 // epilogue (residual or SwiGLU), like the GEMV kernels'.
+//
+// K-quant weights (Q4_K, Q6_K) take the same MMAs on an int8 prefill copy of
+// the matrix (built once at finalize, kq_build_kernel), with the exact
+// arithmetic of ggml's vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K kept in the
+// epilogue: the activation rows are quantized to Q8_K (quant_rows_q8k_kernel),
+// an MMA block of 32 columns gives one exact int32 sub-block sum s_j per
+// (row, token), the epilogue forms isum = sum_j sc_j * s_j (and for Q4_K
+// msum = sum_j m_j * bsum_j) in integers per 256-value super-block and adds
+// the super-block term (d_w*d_x) * isum - (dmin_w*d_x) * msum in double.
+// Q6_K's 16-value sub-blocks each get a 32-column MMA block of their own (16
+// quants and 16 zeros; the activation rows carry the same zero padding), so
+// the copy and the activation rows are twice as wide as the matrix.
 #include "s2k_common.cuh"
 #include "s2k_kernels.h"
 #include "s2k_tc.cuh"
@@ -63,6 +75,8 @@ struct PSmemT {
     alignas(1024) uint8_t b[kPStages][N * kPKC];
     alignas(128) __half dw[2][kPM][16];   // weight block scales of a 512-column K-tile
     alignas(128) double dx[2][N][16];     // activation block scales of the K-tile
+    // K-quant: (d, dmin) of the K-tile's super-blocks per row (N = 64 only)
+    alignas(16) __half2 ds[N == 64 ? 2 : 1][N == 64 ? kPM : 1][2];
     alignas(16) double red[kRed];
     uint64_t full[kPStages], empty[kPStages];
     uint64_t sfull[2], sempty[2];
@@ -84,8 +98,12 @@ struct PrefillParams {
     double *part;         // stream-K partials [gridDim.x][2][kPN][kPM]
     int *counters;        // K-tiles done per (row block, token tile) [R/128][token tiles], zero between launches
     const __half *wtiles; // weight tiles (scales read by bulk copies)
+    const __half2 *side;  // K-quant: (d, dmin) per (row block, K-tile, row, super-block)
     int *err;
 };
+
+// K-quant modes of the GEMM (template argument KQ)
+enum : int { KQ_NONE = 0, KQ_Q4K = 1, KQ_Q6K = 2 };
 
 // Instruction descriptor: kind::i8, D s32, A and B signed int8, both K-major,
 // N tokens, M = kPM.
@@ -150,10 +168,11 @@ __device__ __forceinline__ void store_rows8(const PrefillParams &p, const double
 
 // 18 warps: 5 of them share a sub-partition's 16K registers, so at most 96
 // registers per thread.
-template <int N>
+template <int N, int KQ>
 __global__ void __launch_bounds__(kPThreads, 1)
     prefill_q8_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                       const __grid_constant__ CUtensorMap dxmap, PrefillParams p) {
+    static_assert(KQ == KQ_NONE || N == 64, "K-quant epilogue: 64-token tiles (4 token groups, no block phases)");
     using Sm = PSmemT<N>;
     constexpr int NB = Sm::kNB;
     extern __shared__ uint8_t praw[];
@@ -206,12 +225,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const int kc = kt * 4 + (i & 3), st = i;
                 if ((i & 3) == 0) {
                     const int sb = (i >> 2) & 1;
-                    mbar_arrive_expect_tx(&sm.sfull[sb], 4 * 1024 + N * 16 * 8);
+                    mbar_arrive_expect_tx(&sm.sfull[sb], 4 * 1024 + N * 16 * 8 + (KQ != KQ_NONE ? kPM * 8 : 0));
                     for (int q = 0; q < 4; ++q) {
                         const uint8_t *tile = reinterpret_cast<const uint8_t *>(p.wtiles) +
                                               ((size_t)(rb * 4 + q) * NKT + kt) * kTileBytes + kTileQ;
                         bulk_g2s_plain(&sm.dw[sb][q * 32][0], tile, 1024, &sm.sfull[sb]);
                     }
+                    if constexpr (KQ != KQ_NONE)
+                        bulk_g2s_plain(&sm.ds[sb][0][0], p.side + ((size_t)rb * NKT + kt) * kPM * 2, kPM * 8,
+                                       &sm.sfull[sb]);
                 }
                 mbar_arrive_expect_tx(&sm.full[st], kPStageA + N * kPKC);
                 tma_load_4d(sm.a[st], &wmap, (kc * kPKC) % kTK, 0, (kc * kPKC) / kTK, rb * 4, &sm.full[st]);
@@ -232,12 +254,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     const int ti = i >> 2, sb = ti & 1;
                     if (ti >= 2) ok = mbar_wait(&sm.sempty[sb], ((ti >> 1) - 1) & 1, p.err, ERR_WAIT_EMPTY);
                     if (!ok) break;
-                    mbar_arrive_expect_tx(&sm.sfull[sb], 4 * 1024 + N * 16 * 8);
+                    mbar_arrive_expect_tx(&sm.sfull[sb], 4 * 1024 + N * 16 * 8 + (KQ != KQ_NONE ? kPM * 8 : 0));
                     for (int q = 0; q < 4; ++q) {
                         const uint8_t *tile = reinterpret_cast<const uint8_t *>(p.wtiles) +
                                               ((size_t)(rb * 4 + q) * NKT + kt) * kTileBytes + kTileQ;
                         bulk_g2s_plain(&sm.dw[sb][q * 32][0], tile, 1024, &sm.sfull[sb]);
                     }
+                    if constexpr (KQ != KQ_NONE)
+                        bulk_g2s_plain(&sm.ds[sb][0][0], p.side + ((size_t)rb * NKT + kt) * kPM * 2, kPM * 8,
+                                       &sm.sfull[sb]);
                     tma_load_2d(&sm.dx[sb][0][0], &dxmap, kt * 16, tt * N, &sm.sfull[sb]);
                 }
                 ok = mbar_wait(&sm.empty[st], ((i / kPStages) - 1) & 1, p.err, ERR_WAIT_EMPTY);
@@ -280,6 +305,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const int e = warp - 2, q = warp & 3, h4 = e >> 2;
         const int row_local = q * 32 + lane;
         double acc[16];
+        int isum[KQ != KQ_NONE ? 16 : 1];  // K-quant: sum_j sc_j * s_j of the current super-block
+#pragma unroll
+        for (int j = 0; j < (KQ != KQ_NONE ? 16 : 1); ++j) isum[j] = 0;
         int rb, tt, kt, seg_kt0 = 0, TQ = 1, BS = 4, tg = 0, bp = 0, nvalid = 0, nv_tile = 0;
         unit_of(u_lo, NKT, TT, rb, tt, kt);
         bool first_seg = true;
@@ -310,7 +338,51 @@ __global__ void __launch_bounds__(kPThreads, 1)
             if (ok) ok = mbar_wait(&sm.tfull[buf], (i / NB) & 1, p.err, ERR_WAIT_FULL);
             if (ok) {
                 tc_fence_after();
-                if (nvalid > 0) {
+                if constexpr (KQ != KQ_NONE) {
+                    // every block of the chunk (BS = 1): integer super-block sums
+                    if (nvalid > 0) {
+#pragma unroll
+                        for (int blk = 0; blk < 4; ++blk) {
+                            const int b = (i & 3) * 4 + blk;
+                            int s[16];
+                            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + buf * 4 * N + blk * N + 16 * tg, s);
+                            const uint32_t scm = __half_as_ushort(sm.dw[sb][row_local][b]);
+                            const int sc = KQ == KQ_Q4K ? (int)(scm & 0xff) : (int)(int8_t)(scm & 0xff);
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) isum[j] += sc * s[j];
+                        }
+                        const bool sb_end = KQ == KQ_Q4K ? (i & 1) == 1 : (i & 3) == 3;
+                        if (sb_end) {
+                            const int sbl = KQ == KQ_Q4K ? (i & 3) >> 1 : 0;  // super-block of the K-tile
+                            const float2 dd = __half22float2(sm.ds[sb][row_local][sbl]);
+                            int mn[8];
+                            if constexpr (KQ == KQ_Q4K) {
+                                const uint4 pr = *reinterpret_cast<const uint4 *>(&sm.dw[sb][row_local][8 * sbl]);
+                                const uint32_t pw[4] = {pr.x, pr.y, pr.z, pr.w};
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    mn[2 * k] = (int)((pw[k] >> 8) & 0xff);
+                                    mn[2 * k + 1] = (int)(pw[k] >> 24);
+                                }
+                            }
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                const int2 *slot = reinterpret_cast<const int2 *>(&sm.dx[sb][16 * tg + j][8 * sbl]);
+                                const float dxf = __int_as_float(slot[0].y);
+                                if constexpr (KQ == KQ_Q4K) {
+                                    int ms = 0;
+#pragma unroll
+                                    for (int k = 0; k < 8; ++k) ms += mn[k] * slot[k].x;
+                                    const double d = (double)__fmul_rn(dd.x, dxf), dmn = (double)__fmul_rn(dd.y, dxf);
+                                    acc[j] += fma(d, (double)isum[j], -(dmn * (double)ms));
+                                } else {
+                                    acc[j] += (double)__fmul_rn(dd.x, dxf) * (double)isum[j];
+                                }
+                                isum[j] = 0;
+                            }
+                        }
+                    }
+                } else if (nvalid > 0) {
                     for (int blk = bp; blk < 4; blk += BS) {
                         const int b = (i & 3) * 4 + blk;
                         int s[16];
@@ -470,38 +542,232 @@ __global__ void __launch_bounds__(256) quant_rows_q8_kernel(const float *x, int 
 }
 
 // ---------------------------------------------------------------------------
+// K-quant prefill copy: int8 tiles in the Q8_0 tile geometry (32 x 512 int8,
+// then 2 bytes per (row, 32-column block)) + side (d, dmin) per super-block
+// ---------------------------------------------------------------------------
+// One thread per (row, 32-column block of the copy).  Q4_K: block j of a
+// super-block holds sub-block j's 32 quants (0..15, the nibbles of ggml's qs
+// bytes 32*(j/2) .. +31, low nibble for even j) and the bytes (sc_j, m_j) of
+// get_scale_min_k4.  Q6_K: copy block j holds sub-block j's 16 quants
+// (q - 32, as dequantize_row_q6_K forms them) then 16 zeros, and the bytes
+// (sc_j, 0).  side[rb][kt][row % 128][slot] = (d, dmin) of the super-block
+// the K-tile's slot covers (Q4_K: two per K-tile; Q6_K: one, dmin 0).
+__global__ void kq_build_kernel(const uint8_t *__restrict__ src, int wtype, int R, int K, uint8_t *__restrict__ dst,
+                                __half2 *__restrict__ side) {
+    const int Ke = wtype == TW_Q6_K ? 2 * K : K;  // copy columns
+    const int NBe = Ke / 32, NKTs = K / kTK, NKTe = Ke / kTK;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)R * NBe) return;
+    const int row = (int)(idx / NBe), be = (int)(idx % NBe);
+    const int kte = be / 16, bl = be % 16;
+    const int rl = row % kTR;
+    uint8_t *tile = dst + ((size_t)(row / kTR) * NKTe + kte) * kTileBytes;
+    int8_t q[32];
+    uint16_t scm;
+    __half2 dd = __floats2half2_rn(0.f, 0.f);
+    bool first = false;
+    int slot = 0;
+    if (wtype == TW_Q4_K) {
+        const int sbg = be / 8, j = be % 8;  // super-block of the row, sub-block
+        const uint8_t *t = src + ((size_t)(row / kTR) * NKTs + sbg / 2) * kTileBytesQ4K;
+        const int rb2 = rl * 2 + (sbg & 1);
+        const uint8_t *qs = t + rb2 * 128 + 32 * (j >> 1);
+#pragma unroll
+        for (int l = 0; l < 32; ++l) q[l] = (int8_t)((j & 1) ? (qs[l] >> 4) : (qs[l] & 0xF));
+        const uint8_t *hd = t + kQ4kHdr + rb2 * 16;
+        int sc, mn;
+        q4k_scale_min(j, hd + 4, &sc, &mn);
+        scm = (uint16_t)(sc | (mn << 8));
+        first = j == 0;
+        slot = sbg & 1;
+        dd = __halves2half2(__ushort_as_half(*reinterpret_cast<const unsigned short *>(hd)),
+                            __ushort_as_half(*reinterpret_cast<const unsigned short *>(hd + 2)));
+    } else {
+        const int sbg = kte, j = bl;  // one super-block per copy K-tile, 16-value sub-block j
+        const uint8_t *t = src + ((size_t)(row / kTR) * NKTs + sbg / 2) * kTileBytesQ6K;
+        const int rb2 = rl * 2 + (sbg & 1);
+#pragma unroll
+        for (int l = 0; l < 16; ++l) {
+            const int cc = 16 * j + l, h = cc >> 7, k = (cc >> 5) & 3, ll = cc & 31;
+            const uint8_t ql = t[rb2 * 128 + 64 * h + ll + ((k & 1) << 5)];
+            const uint8_t qh = t[kQ6kQh + rb2 * 64 + 32 * h + ll];
+            q[l] = (int8_t)((((k & 2) ? (ql >> 4) : (ql & 0xF)) | (((qh >> (2 * k)) & 3) << 4)) - 32);
+        }
+#pragma unroll
+        for (int l = 16; l < 32; ++l) q[l] = 0;
+        scm = (uint16_t)t[kQ6kSc + rb2 * 16 + j];
+        first = j == 0;
+        slot = 0;
+        dd = __halves2half2(__ushort_as_half(*reinterpret_cast<const unsigned short *>(t + kQ6kD + rb2 * 2)),
+                            __float2half_rn(0.f));
+    }
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+        w[k] = (uint32_t)(uint8_t)q[4 * k] | ((uint32_t)(uint8_t)q[4 * k + 1] << 8) |
+               ((uint32_t)(uint8_t)q[4 * k + 2] << 16) | ((uint32_t)(uint8_t)q[4 * k + 3] << 24);
+    uint4 *qd = reinterpret_cast<uint4 *>(tile + rl * kTK + bl * 32);
+    qd[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    qd[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    reinterpret_cast<uint16_t *>(tile + kTileQ)[rl * 16 + bl] = scm;
+    if (first) {
+        side[(((size_t)(row / kPM) * NKTe + kte) * kPM + row % kPM) * 2 + slot] = dd;
+        if (wtype == TW_Q6_K) side[(((size_t)(row / kPM) * NKTe + kte) * kPM + row % kPM) * 2 + 1] = dd;
+    }
+}
+
+// Activation rows -> Q8_K for the K-quant GEMM: int8 rows [T][Ke] (Q6_K:
+// every 16 values followed by 16 zeros) and per 32-column copy block a slot
+// (low word: the block's value sum, high word: the super-block's d as float
+// bits).  The arithmetic of the GEMV prologue (RMSNorm, quant_q8k_warp).
+// Grid (token row, 8 super-blocks per CTA), one warp per super-block.
+__global__ void __launch_bounds__(256) quant_rows_q8k_kernel(const float *x, int ldx, int K, const float *norm_w,
+                                                            float eps, int wtype, int8_t *xq, double *slots,
+                                                            float *act_out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float *row = x + (size_t)t * ldx;
+    __shared__ double red[8];
+    __shared__ int16_t bs[8][16];
+    __shared__ float dsh[8];
+    float sc = 1.f;
+    if (norm_w != nullptr) {
+        double s = 0.0;
+        for (int i = tid * 4; i < K; i += 256 * 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(row + i));
+            s += (double)__fmul_rn(v.x, v.x) + (double)__fmul_rn(v.y, v.y);
+            s += (double)__fmul_rn(v.z, v.z) + (double)__fmul_rn(v.w, v.w);
+        }
+        s = warp_sum_d(s);
+        if (lane == 0) red[warp] = s;
+        __syncthreads();
+        double tot = 0.0;
+        for (int w = 0; w < 8; ++w) tot += red[w];
+        const float mean = (float)(tot / (double)K);
+        sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    }
+    const int sbi = blockIdx.y * 8 + warp;
+    if (sbi >= K / 256) return;
+    const int c0 = sbi * 256 + 8 * lane;
+    const float4 a = __ldcg(reinterpret_cast<const float4 *>(row + c0));
+    const float4 b = __ldcg(reinterpret_cast<const float4 *>(row + c0 + 4));
+    float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    if (norm_w != nullptr) {
+        const float4 wa = __ldg(reinterpret_cast<const float4 *>(norm_w + c0));
+        const float4 wb = __ldg(reinterpret_cast<const float4 *>(norm_w + c0 + 4));
+        const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = __fmul_rn(__fmul_rn(y[e], sc), wv[e]);
+    }
+    if (act_out != nullptr) {
+        float4 *dst = reinterpret_cast<float4 *>(act_out + (size_t)t * K + c0);
+        dst[0] = make_float4(y[0], y[1], y[2], y[3]);
+        dst[1] = make_float4(y[4], y[5], y[6], y[7]);
+    }
+    const bool q6 = wtype == TW_Q6_K;
+    const int Ke = q6 ? 2 * K : K;
+    int8_t *xr = xq + (size_t)t * Ke;
+    // Q4_K: values in place; Q6_K: 16-value group g = lane / 2 at copy column 32 g (+ 8 for odd lanes)
+    int8_t *dstq = q6 ? xr + (size_t)sbi * 512 + (lane >> 1) * 32 + (lane & 1) * 8 : xr + c0;
+    quant_q8k_warp(y, lane, true, dstq, &dsh[warp], &bs[warp][0]);
+    if (q6) *reinterpret_cast<uint2 *>(dstq + 16) = make_uint2(0u, 0u);
+    __syncwarp();
+    const float d = dsh[warp];
+    double *sl = slots + (size_t)t * (Ke / 32);
+    if (q6) {
+        if (lane < 16) sl[sbi * 16 + lane] = __hiloint2double(__float_as_int(d), 0);
+    } else if (lane < 8) {
+        sl[sbi * 8 + lane] = __hiloint2double(__float_as_int(d), (int)bs[warp][2 * lane] + (int)bs[warp][2 * lane + 1]);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 cudaError_t prefill_setup() {
     if (!encode_fn()) return cudaErrorNotSupported;
-    cudaError_t e = cudaFuncSetAttribute(prefill_q8_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(prefill_q8_kernel<16, KQ_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)(sizeof(PSmemT<16>) + 1024));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(prefill_q8_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(prefill_q8_kernel<32, KQ_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)(sizeof(PSmemT<32>) + 1024));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(prefill_q8_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(prefill_q8_kernel<64, KQ_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(sizeof(PSmemT<64>) + 1024));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_q8_kernel<64, KQ_Q4K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(sizeof(PSmemT<64>) + 1024));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_q8_kernel<64, KQ_Q6K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)(sizeof(PSmemT<64>) + 1024));
     return e;
 }
 
+static bool is_kq(int type) { return type == 12 || type == 14; }
+
 bool prefill_ok(const DevMat &w, int T) {
-    return w.type == 8 && w.rows % kPM == 0 && w.cols % kTK == 0 && T >= 1;
+    if (w.rows % kPM != 0 || w.cols % kTK != 0 || T < 1) return false;
+    if (w.type == 8) return true;
+    // K-quant: the int8 copy exists and the call fills 64-token tiles
+    return is_kq(w.type) && w.pf != nullptr && w.pf_side != nullptr && T >= kPN;
+}
+
+size_t kq_prefill_bytes(const DevMat &w, size_t *side_bytes) {
+    if (!is_kq(w.type) || w.rows % kPM != 0 || w.cols % kTK != 0) {
+        if (side_bytes) *side_bytes = 0;
+        return 0;
+    }
+    const size_t ke = (size_t)w.cols * (w.type == 14 ? 2 : 1);
+    if (side_bytes) *side_bytes = (size_t)w.rows * (ke / kTK) * 2 * sizeof(__half2);
+    return (size_t)(w.rows / kTR) * (ke / kTK) * kTileBytes;
+}
+
+cudaError_t launch_build_kq_prefill(const DevMat &w, cudaStream_t st) {
+    size_t sb = 0;
+    if (!w.w || !w.pf || !w.pf_side || kq_prefill_bytes(w, &sb) == 0) return cudaErrorInvalidValue;
+    const int wt = w.type == 12 ? TW_Q4_K : TW_Q6_K;
+    const long long n = (long long)w.rows * (w.cols * (wt == TW_Q6_K ? 2 : 1) / 32);
+    count_launch();
+    kq_build_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w.w, wt, w.rows, w.cols, w.pf,
+                                                                 reinterpret_cast<__half2 *>(w.pf_side));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quant_rows_q8k(const float *x, int ldx, int T, int K, const float *norm_w, float eps, int ggml_type,
+                                  int8_t *xq, double *slots, float *act_out, cudaStream_t st) {
+    if (!is_kq(ggml_type) || K % 256 != 0 || T < 1 || ldx % 4 != 0 || reinterpret_cast<uintptr_t>(x) % 16 != 0)
+        return cudaErrorInvalidValue;
+    count_launch();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(T, (K / 256 + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, quant_rows_q8k_kernel, x, ldx, K, norm_w, eps,
+                              ggml_type == 12 ? (int)TW_Q4_K : (int)TW_Q6_K, xq, slots, act_out);
 }
 
 cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st) {
     const DevMat &w = *a.w;
     EncodeTiledFn enc = encode_fn();
     if (!enc || !prefill_ok(w, a.T) || !a.xq || !a.dx || !a.counters) return cudaErrorInvalidValue;
-    const int R = w.rows, K = w.cols, NKT = K / kTK, RT = R / kTR;
+    const int kq = w.type == 12 ? KQ_Q4K : (w.type == 14 ? KQ_Q6K : KQ_NONE);
+    // K: columns of the operand tiles (the K-quant copy is twice as wide for Q6_K)
+    const int R = w.rows, K = w.cols * (kq == KQ_Q6K ? 2 : 1), NKT = K / kTK, RT = R / kTR;
     const int N = a.T <= 16 ? 16 : (a.T <= 32 ? 32 : 64);  // token tile
+    uint8_t *wt = kq != KQ_NONE ? w.pf : w.w;
     CUtensorMap wmap, xmap, dxmap;
     {
         const cuuint64_t dims[4] = {(cuuint64_t)kTK, (cuuint64_t)kTR, (cuuint64_t)NKT, (cuuint64_t)RT};
         const cuuint64_t strides[3] = {(cuuint64_t)kTK, (cuuint64_t)kTileBytes, (cuuint64_t)kTileBytes * NKT};
         const cuuint32_t box[4] = {(cuuint32_t)kPKC, (cuuint32_t)kTR, 1, 4};
         const cuuint32_t es[4] = {1, 1, 1, 1};
-        if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w.w, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+        if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, wt, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
@@ -542,7 +808,8 @@ cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st) {
     p.ldres = a.ldres;
     p.part = a.part;
     p.counters = a.counters;
-    p.wtiles = reinterpret_cast<const __half *>(w.w);
+    p.wtiles = reinterpret_cast<const __half *>(wt);
+    p.side = reinterpret_cast<const __half2 *>(w.pf_side);
     p.err = a.err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);
@@ -555,9 +822,11 @@ cudaError_t launch_prefill_gemm(const PrefillArgs &a, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     count_launch();
-    if (N == 16) return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<16>, wmap, xmap, dxmap, p);
-    if (N == 32) return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<32>, wmap, xmap, dxmap, p);
-    return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<64>, wmap, xmap, dxmap, p);
+    if (kq == KQ_Q4K) return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<64, KQ_Q4K>, wmap, xmap, dxmap, p);
+    if (kq == KQ_Q6K) return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<64, KQ_Q6K>, wmap, xmap, dxmap, p);
+    if (N == 16) return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<16, KQ_NONE>, wmap, xmap, dxmap, p);
+    if (N == 32) return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<32, KQ_NONE>, wmap, xmap, dxmap, p);
+    return cudaLaunchKernelEx(&cfg, prefill_q8_kernel<64, KQ_NONE>, wmap, xmap, dxmap, p);
 }
 
 size_t prefill_part_doubles(int ctas) { return (size_t)ctas * 2 * kPN * kPM; }

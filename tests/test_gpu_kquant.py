@@ -76,9 +76,10 @@ def test_kquant_weight_bytes(kq_pair):
 
 
 def test_kquant_prefill_long_prompt(kq_pair):
-    """A 96-token prompt (K-quant prefill stays on the exact tile GEMV:
-    a 16-bit-activation tensor-core path would leave the reference's Q8_K
-    arithmetic by ~8 % of the logits' std)."""
+    """A 96-token prompt: the Slow stack's GEMMs run on the int8 tensor cores
+    over the K-quant prefill copies (Q8_K rows, exact super-block terms in the
+    epilogue; a 16-bit-activation path would leave the reference's Q8_K
+    arithmetic by ~8 % of the logits' std), then decode steps."""
     hp, m, om = kq_pair
     p = synthetic.semantic_prompt(hp, 96, seed=4)
     m.init_kv_cache(128)
@@ -93,3 +94,51 @@ def test_kquant_prefill_long_prompt(kq_pair):
         hg, lg = m.step(tok)
         ho, lo = om.eval(tok, 1)
         assert_close(lg, lo, f"kquant step {i} after long prefill")
+
+
+@pytest.mark.parametrize("T", [64, 150])
+def test_kquant_tensor_core_prefill_tiles(kq_pair, T):
+    """The tensor-core K-quant prefill on one full 64-token tile and on three
+    tiles with a partial last one (150 tokens), against the oracle's prefill
+    of the same prompt (prefill semantics: every K/V row of the call in f32),
+    then a decode step reading the cached f16 rows."""
+    hp, m, om = kq_pair
+    p = synthetic.text_prompt(hp, T, seed=100 + T)
+    flat = p.T.reshape(-1)
+    m.init_kv_cache(T + 4)
+    om.init_kv_cache(T + 4)
+    hg, lg = m.prefill_fast(flat, T)
+    ho, lo = om.eval(flat, T)
+    assert_close(hg, ho, f"kquant tc prefill hidden T={T}")
+    assert_close(lg, lo, f"kquant tc prefill logits T={T}")
+    tok = np.zeros(hp.num_codebooks + 1, np.int32)
+    tok[0] = 9
+    _, lg = m.step(tok)
+    _, lo = om.eval(tok, 1)
+    assert_close(lg, lo, f"kquant step after tc prefill T={T}")
+
+
+def test_kquant_tensor_core_prefill_real_widths():
+    """S2 Pro widths (d 2560, GQA 32/8, ff 9728: Q4_K attention / FFN-up,
+    Q6_K FFN-down over K = 9728), 2 Slow layers: a 72-token prefill through
+    the tensor cores against the oracle, then a step."""
+    hp = synthetic.preset("mid")
+    tensors = list(synthetic.make_model(hp, seed=33, quant="q4_k_m", norm_std=0.1))
+    m = s2k.SlowARModel(hp)
+    m.load_tensors(tensors)
+    om = oracle.OracleModel(hp)
+    om.load_tensors(tensors)
+    p = synthetic.semantic_prompt(hp, 72, seed=5)
+    m.init_kv_cache(80)
+    om.init_kv_cache(80)
+    hg, lg = m.prefill_fast(p.T.reshape(-1), 72)
+    ho, lo = om.eval(p.T.reshape(-1), 72)
+    assert_close(hg, ho, "kquant mid prefill hidden")
+    assert_close(lg, lo, "kquant mid prefill logits")
+    tok = np.zeros(hp.num_codebooks + 1, np.int32)
+    tok[0] = 1000
+    _, lg = m.step(tok)
+    _, lo = om.eval(tok, 1)
+    assert_close(lg, lo, "kquant mid step logits")
+    m.close()
+    om.close()
