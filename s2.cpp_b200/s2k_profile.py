@@ -126,11 +126,13 @@ def _gemv_shapes(hp, fast: bool) -> dict:
 def _critical_table(tr: np.ndarray, kinds: np.ndarray, shapes: dict) -> dict:
     """Per op of a layer (mean over layers): `lat` = last CTA done of this op
     minus last CTA done of the previous op (the op's share of the launch's
-    critical path).  For the GEMV ops, on the CTA that finished last:
-    `land` = its activation loads landed [4] after the previous op's last
-    done, `quant` = prologue end [1] after [4], `tile0` = first weight tile
-    ready [6] after [1], `tiles` = done [2] after [6], `n` = its weight tiles
-    in the op, `issued` = the producer's last tile of the op issued [3]
+    critical path).  For the GEMV ops, on the CTA that finished last (times
+    after the previous op's last done): `quantized` = its activation
+    quantized [7] (also the median and slowest CTA with work), for RMSNorm'd
+    inputs `warp0` / `all_warps` = warp 0's squares summed [4] / every
+    warp's, the norm scale known [5]; then `tile0` = first weight tile
+    ready [6] after the prologue end [1], `tiles` = done [2] after [6], `n` =
+    its weight tiles in the op, `issued` = the producer's last tile of the op issued [3]
     relative to [1] (negative: every tile was requested before the consumers
     needed it); `us_per_tile` = median over CTAs with work of ([2] - [6]) / n."""
     T = tr.astype(np.int64)
@@ -151,10 +153,16 @@ def _critical_table(tr: np.ndarray, kinds: np.ndarray, shapes: dict) -> dict:
                 R, K = shapes[nm]
                 RT, NKT = R // 32, K // 512
                 ntile = np.array([(RT * (cc + 1) // G - RT * cc // G) * NKT for cc in range(G)])
-                row.update(land=(T[i, c, 4] - prev) / 1e3, quant=(T[i, c, 1] - T[i, c, 4]) / 1e3,
-                           tile0=(T[i, c, 6] - T[i, c, 1]) / 1e3, tiles=(T[i, c, 2] - T[i, c, 6]) / 1e3,
-                           n=int(ntile[c]), issued=(T[i, c, 3] - T[i, c, 1]) / 1e3)
                 w = ntile > 0
+                qz = T[i, :, 7] - prev
+                row.update(quantized=(T[i, c, 7] - prev) / 1e3, quantized_med=float(np.median(qz[w])) / 1e3,
+                           quantized_max=float(qz[w].max()) / 1e3, tile0=(T[i, c, 6] - T[i, c, 1]) / 1e3,
+                           tiles=(T[i, c, 2] - T[i, c, 6]) / 1e3, n=int(ntile[c]),
+                           issued=(T[i, c, 3] - T[i, c, 1]) / 1e3)
+                if nm in ("qkv", "w13"):  # RMSNorm'd input: [4] warp 0's squares summed, [5] scale known
+                    row.update(warp0=(T[i, c, 4] - prev) / 1e3, all_warps=(T[i, c, 5] - prev) / 1e3,
+                               warp0_med=float(np.median(T[i, w, 4] - prev)) / 1e3,
+                               all_warps_med=float(np.median(T[i, w, 5] - prev)) / 1e3)
                 row["us_per_tile"] = float(np.median((T[i, w, 2] - T[i, w, 6]) / ntile[w])) / 1e3
             acc[nm].append(row)
     return {nm: {key: round(float(np.mean([r[key] for r in rows])), 2) for key in rows[0]} for nm, rows in acc.items()}
