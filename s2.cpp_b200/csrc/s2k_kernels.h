@@ -73,9 +73,10 @@ cudaError_t launch_relayout(const uint8_t *src, int row0, int rows, int cols, De
 int tw_of(int ggml_type);
 
 // ---------------------------------------------------------------------------
-// Prefill GEMM on the tensor cores (s2k_prefill.cu), Q8_0 weights:
-// y[T][R] (+ res, or SwiGLU of interleaved rows) from activations already
-// quantized by launch_quant_rows_q8.
+// Prefill GEMM on the tensor cores (s2k_prefill.cu): y[T][R] (+ res, or
+// SwiGLU of interleaved rows) from activations already quantized by
+// launch_quant_rows_q8 (Q8_0 weights) or launch_quant_rows_q8k (Q4_K / Q6_K
+// weights through their prefill copy, 64+ tokens).
 // ---------------------------------------------------------------------------
 struct PrefillArgs {
     const DevMat *w = nullptr;

@@ -1,5 +1,6 @@
 // s2k_prefill.cu -- prompt prefill GEMMs on the 5th-generation tensor cores
-// (tcgen05, sm_100a): Y[T][R] = X[T][K] . W[R][K]^T for Q8_0 weights.
+// (tcgen05, sm_100a): Y[T][R] = X[T][K] . W[R][K]^T for Q8_0, Q4_K and Q6_K
+// weights.
 //
 // Arithmetic.  The reference's CPU mat-mul quantizes each activation row to
 // Q8_0 and sums, per output, the block terms (int32 sum of 32 int8 products)
