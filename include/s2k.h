@@ -130,7 +130,10 @@ S2K_API s2k_status s2k_model_upload_tensor(s2k_model *m, const char *name, int32
                                            const int64_t ne[4], const void *host, size_t nbytes);
 
 /* Checks every required tensor is bound (the req_t checks of
- * src/s2_model.cpp:366-428) and prepares the decode kernels. */
+ * src/s2_model.cpp:366-428) and prepares the decode kernels.  For Q4_K /
+ * Q6_K matrices of the Slow stack it also builds the int8 copies the
+ * tensor-core prefill reads: about one extra byte of device memory per
+ * weight (two per Q6_K weight); s2k_model_weight_bytes does not count them. */
 S2K_API s2k_status s2k_model_finalize(s2k_model *m);
 S2K_API void s2k_model_free(s2k_model *m);
 /* SlowARModel::hparams (include/s2_model.h:130) */
