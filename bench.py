@@ -43,6 +43,11 @@ PROMPT = 64
 FRAMES = 200
 SEED = 1234
 METRIC = "codec frames/s (dual-AR frame loop, Q8_0, bs=1 per GPU)"
+
+
+def frame_metric(quant: str) -> str:
+    """The frame-loop metric for a weight scheme (the headline one for Q8_0)."""
+    return METRIC if quant == "q8_0" else METRIC.replace("Q8_0", quant.upper())
 WORKLOAD = ("dual-AR frame loop, S2 Pro shape (36+4 layers, d2560, GQA 32/8, ff 9728, vocab 155648), "
             "Q8_0, bs=1: 64-token text prompt prefill + 200 greedy frames")
 
@@ -544,7 +549,8 @@ def main() -> None:
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+            "metric": frame_metric(args.quant), "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": args.quant, "data": "synthetic",
             "config": {"workload": workload(args.preset, args.quant, P, frames),

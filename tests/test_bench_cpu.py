@@ -40,3 +40,11 @@ def test_frame_bytes_match_survey():
     assert fast == 440074240
     one = bench.frame_bytes(hp, 64, 1)
     assert one == slow + 9 * fast + 147456 * 65
+
+
+def test_frame_metric_names_the_weight_scheme():
+    """The default (Q8_0) run reports the headline metric unchanged; other
+    weight schemes name themselves instead of claiming Q8_0."""
+    assert bench.frame_metric("q8_0") == bench.METRIC
+    assert "Q4_K_M" in bench.frame_metric("q4_k_m") and "Q8_0" not in bench.frame_metric("q4_k_m")
+    assert "F16" in bench.frame_metric("f16")
