@@ -142,3 +142,26 @@ def test_kquant_tensor_core_prefill_real_widths():
     assert_close(lg, lo, "kquant mid step logits")
     m.close()
     om.close()
+
+
+def test_kquant_batch_of_64_matches_single_sequence(kq_pair):
+    """64 live sequences: the batched Slow GEMMs take 64 rows, so they run on
+    the tensor-core K-quant path (the Fast-AR stack stays on the tile GEMV);
+    every request's codes equal its single-sequence frame loop's."""
+    hp, m, _ = kq_pair
+    rng = np.random.default_rng(64)
+    reqs = []
+    for i in range(64):
+        cols = int(rng.integers(4, 9))
+        p = synthetic.text_prompt(hp, cols, seed=500 + i) if i % 2 else synthetic.semantic_prompt(hp, cols, seed=500 + i)
+        kw = dict(temperature=0.0 if i % 3 == 0 else 0.7, top_p=0.9, top_k=30, seed=900 + i, seq_id=i, im_end_id=-1)
+        reqs.append((p, 3, kw))
+    sc = s2k.BatchScheduler(m, 64, 16)
+    ids = [sc.submit(p, f, **kw) for p, f, kw in reqs]
+    sc.run()
+    st = sc.stats()
+    got = [sc.result(i) for i in ids]
+    sc.close()
+    assert st["max_live"] == 64
+    for i, (p, f, kw) in enumerate(reqs):
+        assert np.array_equal(got[i], m.generate(p, f, **kw)), f"request {i}"
