@@ -169,31 +169,106 @@ def cpu_sample(hp, tensors, frames_sample: int, prompt_len: int = PROMPT, frames
             "prefill_s": pre_ms / 1e3, "s_per_frame": per_frame / 1e3}
 
 
-def run_reference(args, rank: int) -> None:
+def frame_config(hp, quant: str, preset: str, prompt: int, frames: int, world: int) -> dict:
+    """The `config` of the frame-loop workload, the same on both arms."""
+    return {"workload": workload(preset, quant, prompt, frames),
+            "prompt_tokens": prompt, "frames": frames, "batch_per_gpu": 1,
+            "weights": f"seeded N(0,0.02) -> {quant}",
+            "l2": f"inputs larger than L2 ({weight_stream_bytes(hp, quant)[0] / 1e9:.1f} GB of Slow weights per frame)",
+            "parallelism": f"request-level x{world}, no collectives"}
+
+
+def run_reference(args, rank: int, world: int) -> None:
     """--impl reference: the reference's CPU path on the host cores.  ggml is an
     un-vendored submodule of s2.cpp (absent), so the reference cannot be built;
-    its restatement in oracle/ is timed instead."""
+    its restatement in oracle/ is timed instead, with every host thread.
+
+    One step runs a bounded sample of the workload (the prompt prefill + a few
+    frames; a whole 200-frame step takes minutes on the CPU): steps and
+    ms_per_step are what ran.  value is the workload's rate from the measured
+    prefill time and time per frame (medians over the steps)."""
     if rank != 0:
         return
     hp = synthetic.preset("s2pro")
     tensors = build_weights(hp, os.cpu_count() or 1)
-    vals = []
+    walls, runs = [], []
     for i in range(args.warmup + args.steps):
+        t = time.perf_counter()
         r = cpu_sample(hp, tensors, args.cpu_frames)
         if i >= args.warmup:
-            vals.append(r)
-    v = float(np.mean([r["value"] for r in vals]))
-    ms = 1e3 * FRAMES / v
+            walls.append(time.perf_counter() - t)
+            runs.append(r)
+    pre_s = float(np.median([r["prefill_s"] for r in runs]))
+    frame_s = float(np.median([r["s_per_frame"] for r in runs]))
+    v = FRAMES / (pre_s + FRAMES * frame_s)
     line = {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "frames/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "q8_0", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "prompt_tokens": PROMPT, "frames": FRAMES},
-        "cpu_baseline": {k: vals[-1][k] for k in ("unit", "cores", "kind", "sample")} | {"value": v},
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "frames/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * float(np.mean(walls)),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q8_0", "data": "synthetic",
+        "config": frame_config(hp, "q8_0", "s2pro", PROMPT, FRAMES, world),
+        "step": {"frames_run": args.cpu_frames, "prompt_tokens": PROMPT,
+                 "note": (f"each step ran the {PROMPT}-token prefill + {args.cpu_frames} greedy frames; value = "
+                          f"{FRAMES} / (prefill_s + {FRAMES} x s_per_frame)"),
+                 "prefill_s": pre_s, "s_per_frame": frame_s},
+        "cpu_baseline": {k: runs[-1][k] for k in ("unit", "cores", "kind", "sample")} | {"value": v},
         "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "ggml (s2.cpp's compute backend) is an absent submodule; the C restatement in oracle/ is timed",
     }
     print(json.dumps(line), flush=True)
+
+
+def slow_step_at_512(m, hp, tensors, with_cpu: bool, reps: int = 20, warmup: int = 3) -> dict:
+    """The single-step workload: one Slow-AR step (s2k_eval, 1 text token, host
+    token in and host logits out) over an f16 cache of 512 N(0,1) positions.
+    Every rep restores the cache to exactly 512 positions first (untimed) and
+    times the step with CUDA events on the model stream; median of `reps`
+    after `warmup`.  Beside it the CPU oracle's step on the same cache."""
+    import torch
+    rng = np.random.default_rng(512)
+    shape = (hp.block_count, 512, hp.head_count_kv, hp.head_dim)
+    k = rng.standard_normal(shape, dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal(shape, dtype=np.float32).astype(np.float16)
+    tok = np.zeros(hp.num_codebooks + 1, np.int32)
+    tok[0] = int(rng.integers(0, hp.semantic_begin_id))
+    m.init_kv_cache(513)
+    dev = torch.device("cuda", m.device)
+    stream = torch.cuda.ExternalStream(m.stream(), device=dev)
+    times = []
+    for i in range(warmup + reps):
+        m.load_kv(k, v)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        _, logits = m.step(tok)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if i >= warmup:
+            times.append(e0.elapsed_time(e1))
+    slow_b, _ = weight_stream_bytes(hp, "q8_0")
+    kv_b = 512 * hp.block_count * 2 * hp.head_count_kv * hp.head_dim * 2
+    ms = float(np.median(times))
+    out = {"workload": "Slow-AR step, Q8_0, bs=1, 512 cached N(0,1) f16 positions, text token; host logits out",
+           "ms_per_step": ms, "reps": reps, "warmup": warmup, "bytes": slow_b + kv_b,
+           "achieved_gbs": (slow_b + kv_b) / (ms / 1e3) / 1e9}
+    out["frac"] = out["achieved_gbs"] / peaks()["hbm_gbs"]
+    if with_cpu and tensors is not None:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle  # noqa: E402  (cpu_baseline leg only)
+        oracle.set_threads(os.cpu_count() or 1)
+        om = oracle.OracleModel(hp)
+        om.load_tensors(tensors)
+        om.init_kv_cache(513)
+        cpu = []
+        for _ in range(3):
+            om.load_kv(k, v)
+            t = time.perf_counter()
+            _, lo = om.eval(tok, 1)
+            cpu.append(time.perf_counter() - t)
+        om.close()
+        out["cpu_oracle_ms_per_step"] = 1e3 * float(np.median(cpu))
+        out["cpu_cores"] = os.cpu_count() or 1
+        out["logits_equal_cpu"] = bool(np.array_equal(lo, logits))
+    return out
 
 
 RAGGED_UTTS = 64
@@ -430,6 +505,7 @@ def main() -> None:
                     help="weight quantization scheme (q4_k_m: the mixed Q4_K / Q6_K workload)")
     ap.add_argument("--cpu-frames", type=int, default=2, help="frames in the CPU oracle sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-slow-step", action="store_true", help="skip the Slow step at 512 cached positions")
     ap.add_argument("--preset", choices=["s2pro", "mid"], default="s2pro",
                     help="model shape; 'mid' (2+1 layers, real widths) is for small profiler captures only")
     ap.add_argument("--workload", choices=["frames", "ragged", "f16long"], default="frames",
@@ -447,7 +523,7 @@ def main() -> None:
     rank, world, local = shard.dist_env()
 
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         return
     if args.workload == "ragged":
         args.utterances = args.utterances or RAGGED_UTTS
@@ -515,6 +591,7 @@ def main() -> None:
     ms_per_step = ms / args.steps
     value = shard.aggregate_rate(world, args.steps, frames, ms)
 
+    timed_codes = d_codes.cpu().numpy()
     # end to end through the host API: host prompt in, host codes out
     e2e_times = []
     for _ in range(args.steps):
@@ -523,6 +600,9 @@ def main() -> None:
         out = m.generate(prompt, frames, **kw)
         e2e_times.append(time.perf_counter() - a)
         assert out.shape == (hp.num_codebooks, frames)
+    # the timed run decoded the request the host API decodes
+    codes_match = bool(np.array_equal(timed_codes, out))
+    assert codes_match, "timed frames differ from an untimed generate of the same request"
     e2e_s = shard.max_over_ranks(float(np.sum(e2e_times)), f"cuda:{local}")
     e2e_value = shard.aggregate_rate(world, args.steps, frames, e2e_s * 1e3)
 
@@ -546,6 +626,9 @@ def main() -> None:
             cpu = cpu_sample(hp, tensors, args.cpu_frames, P, frames)
         except Exception as e:  # reported, never fatal
             cpu = {"value": None, "error": str(e)}
+    step512 = None
+    if args.preset == "s2pro" and args.quant == "q8_0" and not args.no_slow_step:
+        step512 = slow_step_at_512(m, hp, tensors, with_cpu=cpu is not None and cpu.get("value") is not None)
 
     if rank == 0:
         line = {
@@ -553,11 +636,7 @@ def main() -> None:
             "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": args.quant, "data": "synthetic",
-            "config": {"workload": workload(args.preset, args.quant, P, frames),
-                       "prompt_tokens": P, "frames": frames, "batch_per_gpu": 1,
-                       "weights": f"seeded N(0,0.02) -> {args.quant}",
-                       "l2": f"inputs larger than L2 ({weight_stream_bytes(hp, args.quant)[0] / 1e9:.1f} GB of Slow weights per frame)",
-                       "parallelism": f"request-level x{world}, no collectives"},
+            "config": frame_config(hp, args.quant, args.preset, P, frames, world),
             "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": int(prompt.nbytes),
                     "d2h_bytes_per_step": int(hp.num_codebooks * frames * 4)},
             "roofline": {"bound": "hbm", "kernel": "mega_kernel (persistent decode kernel, 9 Fast-pass + 1 Slow-step "
@@ -575,6 +654,8 @@ def main() -> None:
             "frame_roofline": {"achieved": frame_achieved, "frac": frame_achieved / pk["hbm_gbs"], "unit": "GB/s",
                                "bytes_per_step": step_bytes},
             "cpu_baseline": cpu,
+            "slow_step_512": step512,
+            "timed_codes_match_generate": codes_match,
             "clocks": clk,
             "gpu_launches": int(launches),
             "setup_s": {"synth": t_synth},

@@ -129,6 +129,29 @@ S2K_API s2k_status s2k_model_create(int32_t device, const s2k_hparams *hp, s2k_m
 S2K_API s2k_status s2k_model_upload_tensor(s2k_model *m, const char *name, int32_t ggml_type,
                                            const int64_t ne[4], const void *host, size_t nbytes);
 
+/* ---- GGUF files without ggml.  The reference reads the hyper-parameters
+ * with gguf_get_val_* under the keys and defaults of SlowARModel::load_shared
+ * (src/s2_model.cpp:245-288: "<general.architecture>.*" and "fish_speech.*")
+ * and copies each model tensor's bytes from data_offset + offset
+ * (read_all_tensor_data, src/s2_pipeline.cpp:306-389).  These do the same
+ * with a reader of their own (GGUF v2 / v3). */
+
+/* The model hyper-parameters of a GGUF file (host only, no device needed).
+ * head_dim comes from layer 0's q_norm or wo shape (src/s2_model.cpp:879-884). */
+S2K_API s2k_status s2k_gguf_read_hparams(const char *path, s2k_hparams *out);
+/* Tensor `index` of a GGUF file: name (NUL-terminated, capacity name_cap),
+ * ggml type, ne (unused dimensions 1), absolute file offset of its data and
+ * its size in bytes (0 for a ggml type this path does not read).  Any output
+ * may be NULL; *n_tensors gets the file's tensor count (index -1: count only). */
+S2K_API s2k_status s2k_gguf_tensor_info(const char *path, int32_t index, char *name, size_t name_cap,
+                                        int32_t *type, int64_t ne[4], uint64_t *offset, uint64_t *nbytes,
+                                        int32_t *n_tensors);
+/* Creates the model on `device` from a GGUF file: hyper-parameters as
+ * s2k_gguf_read_hparams, every tensor the model binds uploaded (the codec's
+ * and other tensors are skipped, as the reference leaves them to the codec),
+ * then s2k_model_finalize. */
+S2K_API s2k_status s2k_model_load_gguf(int32_t device, const char *path, s2k_model **out);
+
 /* Checks every required tensor is bound (the req_t checks of
  * src/s2_model.cpp:366-428) and prepares the decode kernels.  For Q4_K /
  * Q6_K matrices of the Slow stack it also builds the int8 copies the
@@ -152,6 +175,14 @@ S2K_API s2k_status s2k_seq_reset(s2k_seq *s);
 S2K_API void s2k_seq_free(s2k_seq *s);
 S2K_API int32_t s2k_seq_n_past(const s2k_seq *s);
 
+/* Restores the sequence's KV cache from host memory: k and v hold n_pos
+ * positions in the reference's cache layout, f16 [layer][pos][kv_head][head_dim]
+ * (src/s2_model.cpp:746-747, with max_seq_len = n_pos), and n_past becomes
+ * n_pos, as if those positions had been prefilled (the state prefill_fast
+ * leaves, src/s2_model.cpp:788-791).  For a cached voice-clone prefix, and for
+ * a step over a given cache.  Not for sequences of a scheduler. */
+S2K_API s2k_status s2k_seq_load_kv(s2k_seq *s, const uint16_t *k, const uint16_t *v, int32_t n_pos);
+
 /* SlowARModel::eval_cached, reached through prefill_fast / step
  * (src/s2_model.cpp:788-791, 855-1097).  flat_tokens is [n_tokens][num_codebooks+1]
  * token-major.  hidden_out [embedding_length] and logits_out [vocab_size] are
@@ -171,7 +202,13 @@ S2K_API s2k_status s2k_fast_decode(s2k_model *m, const float *hidden, const int3
  * cb-major, compacted like src/s2_generate.cpp:201-213 (capacity
  * num_codebooks * max_new_tokens).  The sequence is reset first (the
  * clear/init_kv_cache the Pipeline does, src/s2_pipeline.cpp:838-851) and
- * must hold cols + max_new_tokens positions.  on_frame may be NULL. */
+ * must hold cols + max_new_tokens positions.
+ * on_frame (may be NULL) is called on the calling thread for each frame as
+ * soon as its codes reach host memory, while up to 3 later frames decode on
+ * the device (src/s2_generate.cpp:150-163).  Returning 0 stops generation:
+ * no further frame is launched, codes_out holds frames 0..frame_index, and
+ * n_past is cols + frame_index, as in the reference, which breaks before the
+ * aborted frame's step(). */
 S2K_API s2k_status s2k_generate(s2k_model *m, s2k_seq *s, const int32_t *prompt, int32_t cols,
                                 const s2k_gen_params *gp, int32_t *codes_out,
                                 int32_t *n_frames_out, s2k_frame_callback on_frame, void *user);
@@ -196,16 +233,47 @@ S2K_API s2k_status s2k_sample(s2k_model *m, const float *logits, int32_t n, floa
  * reference.  Same arguments, result and tie break as s2k_sample, but it
  * allocates no device memory: the logits staging row, the result slot and
  * the error word live in one fixed file-scope device array of
- * S2K_SAMPLE_NOALLOC_MAX_N floats + 256 bytes (32.25 KiB) per device.
+ * S2K_SAMPLE_NOALLOC_MAX_N floats + 256 bytes (32.25 KiB) per device, which
+ * every device that loads the library holds until exit.
  * n > S2K_SAMPLE_NOALLOC_MAX_N is rejected with S2K_ERR_ARG.
- * The first call on a device looks up that array's address (set-up); make
- * it before any stream capture on that device.  The error word is cleared
- * on the model stream at the start of every call.  The scratch is shared by
- * every model on the device: calls that overlap in time (other threads,
- * other models on the same device) race on it and must be serialised by the
- * caller. */
+ * The first call on a device (and the first after a device reset) looks up
+ * that array's address with that device current.  Every call copies the
+ * logits in, samples and synchronizes the model stream to read the token, so
+ * it cannot be called while a stream is being captured.  The error word is
+ * cleared on the model stream at the start of every call.  The scratch is
+ * shared by every model on the device: calls that overlap in time (other
+ * threads, other models on the same device) race on it and must be
+ * serialised by the caller. */
 S2K_API s2k_status s2k_sample_noalloc(s2k_model *m, const float *logits, int32_t n, float temperature,
                                       float top_p, int32_t top_k, double u, int32_t *token_out);
+
+/* ggml_get_rows of a weight table on the device (the embedding gathers of
+ * src/s2_model.cpp:941-962, 1150-1157): out [n][embedding_length] f32 gets
+ * rows ids[0..n) of `table` ("embeddings.weight", "codebook_embeddings.weight",
+ * "fast_embeddings.weight", "fast_output.weight") dequantized exactly as the
+ * decode kernels read them (ggml dequantize_row_* per block). */
+S2K_API s2k_status s2k_get_rows(s2k_model *m, const char *table, const int32_t *ids, int32_t n, float *out);
+
+/* ---- Failure detection (no reference counterpart: the reference's ggml
+ * waits have no bound).  Every wait of a kernel on data another CTA, copy
+ * engine or launch produces is bounded; when the bound passes, the kernel
+ * records the failure in the model's error word and returns, and the call
+ * returns S2K_ERR_TIMEOUT with the model still usable. */
+
+/* Bound of every device-side wait of this model's kernels, in SM clock cycles
+ * (0 = the default, 4e9, about 2 s).  Takes effect for launches after it. */
+S2K_API s2k_status s2k_model_set_wait_limit(s2k_model *m, int64_t cycles);
+/* Launches one warp that waits, with the persistent kernel's bounded wait, for
+ * an activation tag nobody writes.  Returns S2K_ERR_TIMEOUT once the wait
+ * limit has passed (the path every timed-out wait takes). */
+S2K_API s2k_status s2k_debug_wait_probe(s2k_model *m);
+/* Test hook: the device allocation `after` allocations from now fails once
+ * (as an out-of-memory error); a negative value disarms it. */
+S2K_API s2k_status s2k_debug_fail_alloc(s2k_model *m, int64_t after);
+/* Device bytes the model holds (weights, workspaces, sequences, schedulers). */
+S2K_API size_t s2k_model_device_bytes(const s2k_model *m);
+/* cudaMemGetInfo of a device. */
+S2K_API s2k_status s2k_device_mem_info(int32_t device, size_t *free_bytes, size_t *total_bytes);
 
 /* Profiling hook for the dominant kernel (no reference counterpart): launches
  * every Slow-step weight GEMV (per layer wqkv, wo, w1|w3, w2, then the LM head)
@@ -296,7 +364,11 @@ S2K_API s2k_status s2k_seq_frames(s2k_seq *s, int32_t *codes_out, int32_t cap_fr
  * prefilled, joins the next batched frame, and leaves the batch (its pages
  * back in the pool) when it stops (im_end or max_new_tokens). */
 typedef struct s2k_sched s2k_sched;
-enum { S2K_REQ_WAITING = 0, S2K_REQ_LIVE = 1, S2K_REQ_DONE = 2 };
+/* Request states.  FAILED: admission failed for this request alone (no
+ * memory for it, bad input; s2k_sched_poll_status gives the status) and the
+ * scheduler went on with the others.  CANCELLED: stopped by s2k_sched_cancel
+ * or by the frame callback; it keeps the frames it had. */
+enum { S2K_REQ_WAITING = 0, S2K_REQ_LIVE = 1, S2K_REQ_DONE = 2, S2K_REQ_FAILED = 3, S2K_REQ_CANCELLED = 4 };
 typedef struct {
     int64_t steps;           /* batched frames run */
     int64_t frames;          /* frames produced, all requests */
@@ -305,7 +377,14 @@ typedef struct {
     int64_t kv_positions;    /* cached positions the batched Slow steps attended over */
     int32_t max_live;        /* largest batch so far */
     int32_t free_pages, pool_pages;
+    int32_t pad_;
+    int64_t cancelled, failed;
 } s2k_sched_stats;
+/* Called after each batched frame for each frame a live request produced
+ * (the streaming hand-off of src/s2_generate.cpp:150-163 per request);
+ * returning 0 cancels that request. */
+typedef int32_t (*s2k_sched_frame_callback)(int32_t req_id, const int32_t *codes, int32_t frame_index,
+                                            int32_t num_codebooks, void *user);
 S2K_API s2k_status s2k_sched_create(s2k_model *m, int32_t max_batch, int32_t max_seq_len, int32_t pool_pages,
                                     s2k_sched **out);
 S2K_API void s2k_sched_free(s2k_sched *sc);
@@ -319,7 +398,17 @@ S2K_API s2k_status s2k_sched_step(s2k_sched *sc, int32_t *n_live, int32_t *n_wai
 /* s2k_sched_step until no request is live or waiting. */
 S2K_API s2k_status s2k_sched_run(s2k_sched *sc);
 S2K_API s2k_status s2k_sched_poll(s2k_sched *sc, int32_t req_id, int32_t *state, int32_t *n_frames);
-/* Codes of a finished request, cb-major [num_codebooks][*n_frames]. */
+/* s2k_sched_poll plus the status a FAILED request failed with (S2K_OK otherwise). */
+S2K_API s2k_status s2k_sched_poll_status(s2k_sched *sc, int32_t req_id, int32_t *state, int32_t *n_frames,
+                                         s2k_status *req_status);
+/* Stops a request between frames (the reference cancels through on_frame,
+ * src/s2_pipeline.cpp:1102-1105): a waiting one leaves the queue, a live one
+ * leaves the batch with the frames it has and its KV pages go back to the
+ * pool.  A finished request is left as it is. */
+S2K_API s2k_status s2k_sched_cancel(s2k_sched *sc, int32_t req_id);
+/* Per-frame hand-off for every request (cb may be NULL to turn it off). */
+S2K_API s2k_status s2k_sched_set_frame_callback(s2k_sched *sc, s2k_sched_frame_callback cb, void *user);
+/* Codes of a finished (or cancelled) request, cb-major [num_codebooks][*n_frames]. */
 S2K_API s2k_status s2k_sched_result(s2k_sched *sc, int32_t req_id, int32_t *codes_out, int32_t cap_frames,
                                     int32_t *n_frames);
 S2K_API s2k_status s2k_sched_get_stats(const s2k_sched *sc, s2k_sched_stats *out);

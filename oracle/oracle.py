@@ -74,6 +74,7 @@ def lib() -> ctypes.CDLL:
             "so_model_check": ([vp], ctypes.c_int),
             "so_kv_init": ([vp, i32], ctypes.c_int),
             "so_kv_clear": ([vp], None),
+            "so_kv_load": ([vp, vp, vp, i32], ctypes.c_int),
             "so_n_past": ([vp], i32),
             "so_eval": ([vp, vp, i32, vp, vp], ctypes.c_int),
             "so_fast_decode": ([vp, vp, vp, i32, vp], ctypes.c_int),
@@ -176,6 +177,12 @@ class OracleModel:
 
     def clear_kv_cache(self) -> None:
         lib().so_kv_clear(self._m)
+
+    def load_kv(self, k: np.ndarray, v: np.ndarray) -> None:
+        """Restore the cache: k, v f16 [layer][pos][kv_head][head_dim]; n_past = pos."""
+        k = np.ascontiguousarray(k, dtype=np.float16)
+        v = np.ascontiguousarray(v, dtype=np.float16)
+        assert lib().so_kv_load(self._m, k.ctypes.data, v.ctypes.data, int(k.shape[1])) == 0
 
     @property
     def n_past(self) -> int:

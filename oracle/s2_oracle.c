@@ -570,6 +570,20 @@ int so_kv_init(so_model *m, int32_t max_seq_len) {
     return (m->kv_k && m->kv_v) ? 0 : -1;
 }
 
+/* Positions 0..n_pos-1 of every layer's cache from k / v laid out
+ * [layer][pos][kv_head][head_dim] (the cache layout of src/s2_model.cpp:746-747
+ * with max_seq_len = n_pos); n_past = n_pos. */
+int so_kv_load(so_model *m, const uint16_t *k, const uint16_t *v, int32_t n_pos) {
+    if (!m->kv_k || n_pos < 0 || n_pos > m->max_seq_len) return -1;
+    const size_t kvs = (size_t)m->hp.head_count_kv * m->hp.head_dim;
+    for (int l = 0; l < m->hp.block_count; ++l) {
+        memcpy(m->kv_k + (size_t)l * m->max_seq_len * kvs, k + (size_t)l * n_pos * kvs, (size_t)n_pos * kvs * 2);
+        memcpy(m->kv_v + (size_t)l * m->max_seq_len * kvs, v + (size_t)l * n_pos * kvs, (size_t)n_pos * kvs * 2);
+    }
+    m->n_past = n_pos;
+    return 0;
+}
+
 void so_kv_clear(so_model *m) {
     free(m->kv_k);
     free(m->kv_v);

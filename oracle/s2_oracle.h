@@ -128,6 +128,8 @@ int so_model_set_tensor(so_model *m, const char *name, int type, const int64_t n
 int so_model_check(so_model *m);                 /* all required tensors bound? */
 int so_kv_init(so_model *m, int32_t max_seq_len); /* init_kv_cache */
 void so_kv_clear(so_model *m);                    /* clear_kv_cache */
+/* restore n_pos cached positions, f16 [layer][pos][kv_head][head_dim]; n_past = n_pos */
+int so_kv_load(so_model *m, const uint16_t *k, const uint16_t *v, int32_t n_pos);
 int32_t so_n_past(const so_model *m);
 /* eval_cached: flat_tokens is [n_tokens][num_codebooks+1] token-major */
 int so_eval(so_model *m, const int32_t *flat_tokens, int32_t n_tokens, float *hidden_out,

@@ -51,7 +51,8 @@ s2k_status check_err_word(s2k_model *m) {
     CU(cudaMemcpy(&h, m->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (h) {
         CU(cudaMemset(m->d_err, 0, sizeof(int)));
-        if (h & (ERR_WAIT_FULL | ERR_WAIT_EMPTY)) return fail(S2K_ERR_TIMEOUT, "device wait timed out (flags 0x%x)", h);
+        if (h & (ERR_WAIT_FULL | ERR_WAIT_EMPTY | ERR_GRID))
+            return fail(S2K_ERR_TIMEOUT, "device wait timed out (flags 0x%x)", h);
         return fail(S2K_ERR_ARG, "device reported invalid input (flags 0x%x)", h);
     }
     return S2K_OK;
@@ -145,8 +146,14 @@ s2k_status ensure_slow_work(s2k_model *m, int T, int L) {
     work_free(m, m->sw);
     m->ws_gen++;
     const s2k_hparams &hp = m->hp;
-    CU(work_alloc(m, m->sw, T, L, hp.embedding_length, hp.head_count, hp.head_count_kv, hp.head_dim,
-                  hp.feed_forward_length, hp.block_count, true, 1));
+    const cudaError_t e = work_alloc(m, m->sw, T, L, hp.embedding_length, hp.head_count, hp.head_count_kv, hp.head_dim,
+                                     hp.feed_forward_length, hp.block_count, true, 1);
+    if (e != cudaSuccess) {
+        // no half-built workspace stays behind: the next call allocates it again
+        work_free(m, m->sw);
+        return fail(e == cudaErrorMemoryAllocation ? S2K_ERR_OOM : S2K_ERR_CUDA,
+                    "Slow workspace for %d tokens x %d positions: %s", T, L, cudaGetErrorString(e));
+    }
     return S2K_OK;
 }
 
@@ -484,6 +491,15 @@ static Slot parse_name(const s2k_model *m, const char *name, bool *fast, int *il
     return SL_NONE;
 }
 
+bool s2k_model_binds(const s2k_model *m, const char *name) {
+    bool fast = false;
+    int il = -1;
+    const Slot sl = parse_name(m, name, &fast, &il);
+    if (sl == SL_NONE) return false;
+    const bool fast_slot = fast || sl == SL_FEMB || sl == SL_FNORM || sl == SL_FOUT;
+    return !fast_slot || m->hp.has_fast_decoder;
+}
+
 static s2k_status upload_vec(s2k_model *m, float **dst, int type, const int64_t ne[4], const void *host, size_t nbytes,
                              int64_t expect, const char *name) {
     if (type != S2K_TYPE_F32) return fail(S2K_ERR_UNSUPPORTED, "%s: norm weights must be F32 (type %d)", name, type);
@@ -595,7 +611,8 @@ S2K_API s2k_status s2k_model_create(int32_t device, const s2k_hparams *hp, s2k_m
     m->layers.resize(hp->block_count);
     m->fast_layers.resize(hp->has_fast_decoder ? hp->fast_block_count : 0);
     const unsigned epoch1 = 1;
-    if (m->alloc(&m->d_err, 1) != cudaSuccess || cudaMemset(m->d_err, 0, sizeof(int)) != cudaSuccess ||
+    if (m->alloc(&m->d_err, kErrBlockInts) != cudaSuccess ||
+        cudaMemset(m->d_err, 0, kErrBlockInts * sizeof(int)) != cudaSuccess ||
         m->alloc(&m->d_epoch, 1) != cudaSuccess ||
         cudaMemcpy(m->d_epoch, &epoch1, sizeof(unsigned), cudaMemcpyHostToDevice) != cudaSuccess) {
         s2k_model_free(m);
@@ -947,15 +964,42 @@ S2K_API s2k_status s2k_sample(s2k_model *m, const float *logits, int32_t n, floa
 
 // ---------------------------------------------------------------------------
 // allocation-free sampler entry: fixed per-device scratch in a static
-// __device__ array -- [0, 4*max) logits row, then the token slot and the
-// error word (the only part that must start at zero: cleared every call).
+// __device__ array -- [0, 4*max) logits row, then the token slot and, 16
+// bytes in, the error block (error word and wait limit, the part that must
+// start at zero: cleared every call).
 // ---------------------------------------------------------------------------
 static_assert(S2K_SAMPLE_NOALLOC_MAX_N <= 8192, "the sampler kernel takes at most 8192 logits");
 constexpr size_t kNoAllocTokOff = (size_t)S2K_SAMPLE_NOALLOC_MAX_N * sizeof(float);
+constexpr size_t kNoAllocErrOff = kNoAllocTokOff + 16;
 static __device__ __align__(256) unsigned char g_sample_scratch[kNoAllocTokOff + 256];
+static_assert(kNoAllocErrOff + kErrBlockInts * sizeof(int) <= sizeof(g_sample_scratch), "scratch layout");
 constexpr int kNoAllocMaxDevices = 64;
-static void *g_sample_scratch_ptr[kNoAllocMaxDevices];
+// Per device: the array's device address and the context it was looked up
+// in.  A device reset gives the device a new context, and the address is
+// looked up again there.
+struct NoAllocScratch {
+    void *ptr = nullptr;
+    void *ctx = nullptr;
+};
+static NoAllocScratch g_sample_scratch_at[kNoAllocMaxDevices];
 static std::mutex g_sample_scratch_mu;
+
+// The current context (cuCtxGetCurrent through the runtime's driver entry
+// point, so the library needs no link against libcuda), or null.
+static void *current_context() {
+    typedef int (*CtxGetCurrent)(void **);
+    static CtxGetCurrent fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<CtxGetCurrent>(p);
+    }();
+    void *ctx = nullptr;
+    if (!fn || fn(&ctx) != 0) return nullptr;
+    return ctx;
+}
 
 S2K_API s2k_status s2k_sample_noalloc(s2k_model *m, const float *logits, int32_t n, float temperature, float top_p,
                                       int32_t top_k, double u, int32_t *token_out) {
@@ -968,26 +1012,30 @@ S2K_API s2k_status s2k_sample_noalloc(s2k_model *m, const float *logits, int32_t
     void *base = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_sample_scratch_mu);
-        if (!g_sample_scratch_ptr[m->device]) {
+        NoAllocScratch &sc = g_sample_scratch_at[m->device];
+        void *ctx = current_context();
+        if (!sc.ptr || ctx != sc.ctx) {
             void *p = nullptr;
             cudaError_t e = cudaGetSymbolAddress(&p, g_sample_scratch);
             if (e != cudaSuccess || !p)
                 return fail(S2K_ERR_CUDA, "cudaGetSymbolAddress(sampler scratch) failed: %s", cudaGetErrorString(e));
-            g_sample_scratch_ptr[m->device] = p;
+            sc.ptr = p;
+            sc.ctx = ctx;
         }
-        base = g_sample_scratch_ptr[m->device];
+        base = sc.ptr;
     }
     float *d_logits = static_cast<float *>(base);
     int *d_tok = reinterpret_cast<int *>(static_cast<unsigned char *>(base) + kNoAllocTokOff);
-    int *d_err = d_tok + 1;
-    int h[2] = {0, 0};
-    CU(cudaMemsetAsync(d_err, 0, sizeof(int), m->stream));
+    int *d_err = reinterpret_cast<int *>(static_cast<unsigned char *>(base) + kNoAllocErrOff);
+    int h_tok = 0, h_err = 0;
+    CU(cudaMemsetAsync(d_err, 0, kErrBlockInts * sizeof(int), m->stream));
     CU(cudaMemcpyAsync(d_logits, logits, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, m->stream));
     CU(launch_sample_one(d_logits, n, temperature, top_p, top_k, u, d_tok, d_err, m->stream));
-    CU(cudaMemcpyAsync(h, d_tok, sizeof(h), cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaMemcpyAsync(&h_tok, d_tok, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaMemcpyAsync(&h_err, d_err, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
     CU(cudaStreamSynchronize(m->stream));
-    if (h[1]) return fail(S2K_ERR_ARG, "device reported invalid input (flags 0x%x)", h[1]);
-    *token_out = h[0];
+    if (h_err) return fail(S2K_ERR_ARG, "device reported invalid input (flags 0x%x)", h_err);
+    *token_out = h_tok;
     return S2K_OK;
 }
 
@@ -1266,8 +1314,17 @@ void fill_sample_cfg(const s2k_model *m, const s2k_gen_params *gp, int *d_codes,
     *out = c;
 }
 
+// The frame loop of generate() (src/s2_generate.cpp:57-183) on the device.
+// Each frame is one graph launch; up to kLookahead frames run ahead of the
+// host.  Frame f's codes reach the host ring (HostStatus::ring) when its
+// frame_commit kernel ends, and on_frame (if any) is called for it as soon
+// as the host sees them, while later frames run.  A zero return stops
+// launching frames: the frames already in flight finish on the device, the
+// result keeps frames 0..f, and n_past ends at cols + f, where the reference
+// model stands when it breaks before step() (src/s2_generate.cpp:150-163).
 static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_prompt_tm, int32_t cols,
-                                const s2k_gen_params *gp, int32_t *d_codes, int32_t codes_ld, int32_t *n_frames_out) {
+                                const s2k_gen_params *gp, int32_t *d_codes, int32_t codes_ld, int32_t *n_frames_out,
+                                s2k_frame_callback on_frame, void *user) {
     const s2k_hparams &hp = m->hp;
     if (cols <= 0 || gp->max_new_tokens < 0) return fail(S2K_ERR_ARG, "bad prompt length / max_new_tokens");
     if (cols + gp->max_new_tokens > s->max_seq_len)
@@ -1277,14 +1334,16 @@ static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_promp
     if (rc) return rc;
     SampleCfg c;
     fill_sample_cfg(m, gp, d_codes, codes_ld, &c);
+    const int ncb = c.ncb;
     // the Pipeline clears and re-inits the KV cache per synthesis (src/s2_pipeline.cpp:838-851)
     CU(cudaMemsetAsync(&s->dev->state, 0, sizeof(SeqState), m->stream));
     CU(cudaMemcpyAsync(&s->dev->cfg, &c, sizeof(SampleCfg), cudaMemcpyHostToDevice, m->stream));
-    HostStatus *hs = s->hstat_dev;
-    CU(cudaMemcpyAsync(&s->dev->host, &hs, sizeof(HostStatus *), cudaMemcpyHostToDevice, m->stream));
+    HostStatus *hs_dev = s->hstat_dev;
+    CU(cudaMemcpyAsync(&s->dev->host, &hs_dev, sizeof(HostStatus *), cudaMemcpyHostToDevice, m->stream));
     CU(cudaStreamSynchronize(m->stream));
-    s->hstat->n_frames = 0;
-    s->hstat->done = 0;
+    volatile HostStatus *hs = s->hstat;
+    hs->n_frames = 0;
+    hs->done = 0;
     s->n_past = 0;
     // prefill (generate(): prefill_fast of the whole prompt, src/s2_generate.cpp:51)
     CU(enqueue_slow(m, s, cols, d_prompt_tm, nullptr));
@@ -1292,25 +1351,60 @@ static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_promp
     rc = ensure_frame_graph(m, s);
     if (rc) return rc;
     constexpr int kLookahead = 4;
+    static_assert(kLookahead < kFrameRing, "frames in flight must not overwrite ring slots the host has not read");
     cudaEvent_t ev[kLookahead];
     for (int i = 0; i < kLookahead; ++i) CU(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
     s2k_status out_rc = S2K_OK;
-    for (int f = 0; f < gp->max_new_tokens; ++f) {
-        if (f >= kLookahead) {
-            cudaError_t e = cudaEventSynchronize(ev[f % kLookahead]);
-            if (e != cudaSuccess) {
-                out_rc = fail(S2K_ERR_CUDA, "frame %d: %s", f, cudaGetErrorString(e));
-                break;
+    int launched = 0, delivered = 0;
+    bool aborted = false;
+    // hand frames [delivered, upto) to on_frame; false once it asks to stop
+    auto deliver = [&](int upto) -> bool {
+        for (; delivered < upto; ++delivered) {
+            if (!on_frame) continue;
+            int codes[16];
+            for (int cb = 0; cb < ncb; ++cb) codes[cb] = hs->ring[delivered % kFrameRing][cb];
+            if (!on_frame(codes, delivered, delivered + 1, ncb, user)) {
+                ++delivered;
+                return false;
             }
         }
-        if (s->hstat->done) break;
-        cudaError_t e = cudaGraphLaunch(s->frame_exec, m->stream);
-        if (e == cudaSuccess) e = cudaEventRecord(ev[f % kLookahead], m->stream);
-        if (e != cudaSuccess) {
-            out_rc = fail(S2K_ERR_CUDA, "frame %d launch: %s", f, cudaGetErrorString(e));
+        return true;
+    };
+    for (;;) {
+        const int landed = hs->n_frames;
+        std::atomic_thread_fence(std::memory_order_acquire);
+        if (!deliver(landed)) {
+            aborted = true;
             break;
         }
-        count_launch((int)s->frame_nodes);
+        if (hs->done) {
+            // the stop was decided after the last frame landed: nothing more comes
+            std::atomic_thread_fence(std::memory_order_acquire);
+            if (!deliver(hs->n_frames)) aborted = true;
+            break;
+        }
+        if (launched < gp->max_new_tokens && launched - delivered < kLookahead) {
+            cudaError_t e = cudaGraphLaunch(s->frame_exec, m->stream);
+            if (e == cudaSuccess) e = cudaEventRecord(ev[launched % kLookahead], m->stream);
+            if (e != cudaSuccess) {
+                out_rc = fail(S2K_ERR_CUDA, "frame %d launch: %s", launched, cudaGetErrorString(e));
+                break;
+            }
+            count_launch((int)s->frame_nodes);
+            ++launched;
+            continue;
+        }
+        if (launched == delivered) break;  // every launched frame handed over, none left to launch
+        // wait for the graph of the oldest frame the host has not seen
+        cudaError_t e = cudaEventSynchronize(ev[delivered % kLookahead]);
+        if (e != cudaSuccess) {
+            out_rc = fail(S2K_ERR_CUDA, "frame %d: %s", delivered, cudaGetErrorString(e));
+            break;
+        }
+        if (hs->n_frames <= delivered && !hs->done) {
+            out_rc = fail(S2K_ERR_STATE, "frame %d ended without codes", delivered);
+            break;
+        }
     }
     cudaError_t e = cudaStreamSynchronize(m->stream);
     for (int i = 0; i < kLookahead; ++i) cudaEventDestroy(ev[i]);
@@ -1318,7 +1412,15 @@ static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_promp
     if (e != cudaSuccess) return fail(S2K_ERR_CUDA, "generate: %s", cudaGetErrorString(e));
     rc = check_err_word(m);
     if (rc) return rc;
-    *n_frames_out = s->hstat->n_frames;
+    if (aborted) {
+        // the reference breaks before step() of the aborted frame
+        const int n_past = cols + delivered - 1;
+        CU(cudaMemcpy(&s->dev->state.n_past, &n_past, sizeof(int), cudaMemcpyHostToDevice));
+        *n_frames_out = delivered;
+        s->n_past = n_past;
+        return S2K_OK;
+    }
+    *n_frames_out = hs->n_frames;
     s->n_past = cols + *n_frames_out;
     return S2K_OK;
 }
@@ -1329,7 +1431,8 @@ S2K_API s2k_status s2k_generate_device(s2k_model *m, s2k_seq *s, const int32_t *
     if (!m->finalized) return fail(S2K_ERR_STATE, "model not finalized");
     if (s->m != m) return fail(S2K_ERR_ARG, "sequence belongs to another model");
     if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
-    return generate_core(m, s, d_prompt_tm, cols, gp, d_codes_out, std::max(gp->max_new_tokens, 1), n_frames_out);
+    return generate_core(m, s, d_prompt_tm, cols, gp, d_codes_out, std::max(gp->max_new_tokens, 1), n_frames_out,
+                         nullptr, nullptr);
 }
 
 S2K_API s2k_status s2k_generate(s2k_model *m, s2k_seq *s, const int32_t *prompt, int32_t cols,
@@ -1363,22 +1466,13 @@ S2K_API s2k_status s2k_generate(s2k_model *m, s2k_seq *s, const int32_t *prompt,
     }
     CU(cudaMemcpyAsync(s->prompt, tm.data(), tm.size() * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
     int32_t nf = 0;
-    rc = generate_core(m, s, s->prompt, cols, gp, s->codes, ld, &nf);
+    rc = generate_core(m, s, s->prompt, cols, gp, s->codes, ld, &nf, on_frame, user);
     if (rc) return rc;
-    std::vector<int32_t> full((size_t)ncb * ld);
-    CU(cudaMemcpy(full.data(), s->codes, full.size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
-    if (on_frame) {
-        std::vector<int32_t> fr(ncb);
-        for (int f = 0; f < nf; ++f) {
-            for (int cb = 0; cb < ncb; ++cb) fr[cb] = full[(size_t)cb * ld + f];
-            if (!on_frame(fr.data(), f, f + 1, ncb, user)) {
-                nf = f + 1;
-                break;
-            }
-        }
-    }
-    for (int cb = 0; cb < ncb; ++cb)
-        for (int f = 0; f < nf; ++f) codes_out[(size_t)cb * nf + f] = full[(size_t)cb * ld + f];
+    // compaction (src/s2_generate.cpp:201-213)
+    for (int cb = 0; cb < ncb && nf > 0; ++cb)
+        CU(cudaMemcpyAsync(codes_out + (size_t)cb * nf, s->codes + (size_t)cb * ld, (size_t)nf * sizeof(int32_t),
+                           cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
     *n_frames_out = nf;
     return S2K_OK;
 }
@@ -1627,3 +1721,106 @@ S2K_API s2k_status s2k_debug_copy(s2k_model *m, s2k_seq *s, const char *name, vo
     return S2K_OK;
 }
 
+
+// ---------------------------------------------------------------------------
+// KV restore, get_rows, and the failure-injection / bounded-wait hooks
+// ---------------------------------------------------------------------------
+S2K_API s2k_status s2k_seq_load_kv(s2k_seq *s, const uint16_t *k, const uint16_t *v, int32_t n_pos) {
+    if (!s || !k || !v || n_pos < 0) return fail(S2K_ERR_ARG, "bad argument");
+    if (s->pooled) return fail(S2K_ERR_ARG, "sequence belongs to a scheduler's page pool");
+    if (n_pos > s->max_seq_len) return fail(S2K_ERR_KV_FULL, "%d positions, the sequence holds %d", n_pos, s->max_seq_len);
+    s2k_model *m = s->m;
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    const s2k_hparams &hp = m->hp;
+    const int L = hp.block_count, Hkv = hp.head_count_kv, hd = hp.head_dim;
+    const size_t kvs = (size_t)Hkv * hd;
+    const size_t page_elems = (size_t)L * Hkv * kPage * hd;
+    const int np = (n_pos + kPage - 1) / kPage;
+    if (np > 0) {
+        // [layer][pos][kv_head][hd] -> pages [page][layer][kv_head][slot][hd]; the
+        // sequence's own block table is the identity (s2k_seq_create)
+        std::vector<uint16_t> pk((size_t)np * page_elems, 0), pv((size_t)np * page_elems, 0);
+        for (int l = 0; l < L; ++l)
+            for (int pos = 0; pos < n_pos; ++pos) {
+                const int pg = pos / kPage, slot = pos % kPage;
+                for (int g = 0; g < Hkv; ++g) {
+                    const size_t src = ((size_t)l * n_pos + pos) * kvs + (size_t)g * hd;
+                    const size_t dst = ((((size_t)pg * L + l) * Hkv + g) * kPage + slot) * hd;
+                    memcpy(&pk[dst], k + src, (size_t)hd * 2);
+                    memcpy(&pv[dst], v + src, (size_t)hd * 2);
+                }
+            }
+        CU(cudaMemcpy(s->k, pk.data(), pk.size() * 2, cudaMemcpyHostToDevice));
+        CU(cudaMemcpy(s->v, pv.data(), pv.size() * 2, cudaMemcpyHostToDevice));
+    }
+    CU(cudaStreamSynchronize(m->stream));
+    CU(cudaMemsetAsync(&s->dev->state, 0, sizeof(SeqState), m->stream));
+    CU(cudaMemcpyAsync(&s->dev->state.n_past, &n_pos, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    s->n_past = n_pos;
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_get_rows(s2k_model *m, const char *table, const int32_t *ids, int32_t n, float *out) {
+    if (!m || !table || !ids || !out || n <= 0) return fail(S2K_ERR_ARG, "bad argument");
+    if (!m->finalized) return fail(S2K_ERR_STATE, "model not finalized");
+    const std::string t(table);
+    const DevMat *E = t == "embeddings.weight" ? &m->embed
+                      : t == "codebook_embeddings.weight" ? &m->cb_embed
+                      : t == "fast_embeddings.weight" ? &m->fast_embed
+                      : t == "fast_output.weight" ? &m->fast_out
+                                                   : nullptr;
+    if (!E || !E->w) return fail(S2K_ERR_ARG, "no table '%s'", table);
+    for (int i = 0; i < n; ++i)
+        if (ids[i] < 0 || ids[i] >= E->rows) return fail(S2K_ERR_ARG, "row %d out of range (%d rows)", ids[i], E->rows);
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    int *d_ids = nullptr;
+    float *d_out = nullptr;
+    CU(m->alloc(&d_ids, (size_t)n));
+    if (m->alloc(&d_out, (size_t)n * E->cols) != cudaSuccess) {
+        m->release(d_ids);
+        return fail(S2K_ERR_OOM, "get_rows output");
+    }
+    cudaError_t e = cudaMemcpyAsync(d_ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = launch_gather_rows(E, d_ids, n, d_out, m->d_err, m->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(out, d_out, (size_t)n * E->cols * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    m->release(d_ids);
+    m->release(d_out);
+    CU(e);
+    return check_err_word(m);
+}
+
+S2K_API s2k_status s2k_model_set_wait_limit(s2k_model *m, int64_t cycles) {
+    if (!m || cycles < 0) return fail(S2K_ERR_ARG, "bad argument");
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    const long long c = cycles;
+    CU(cudaStreamSynchronize(m->stream));
+    CU(cudaMemcpy(m->d_err + 2, &c, sizeof(c), cudaMemcpyHostToDevice));
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_debug_wait_probe(s2k_model *m) {
+    if (!m) return fail(S2K_ERR_ARG, "NULL model");
+    if (!m->finalized || !m->sw.lx) return fail(S2K_ERR_STATE, "model not finalized");
+    if (cuda_set(m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    CU(launch_wait_probe(m->sw.lx, m->d_err, m->stream));
+    CU(cudaStreamSynchronize(m->stream));
+    return check_err_word(m);
+}
+
+S2K_API s2k_status s2k_debug_fail_alloc(s2k_model *m, int64_t after) {
+    if (!m) return fail(S2K_ERR_ARG, "NULL model");
+    m->fail_alloc_at = after < 0 ? -1 : after;
+    return S2K_OK;
+}
+
+S2K_API size_t s2k_model_device_bytes(const s2k_model *m) { return m ? m->dev_bytes : 0; }
+
+S2K_API s2k_status s2k_device_mem_info(int32_t device, size_t *free_bytes, size_t *total_bytes) {
+    if (!free_bytes || !total_bytes) return fail(S2K_ERR_ARG, "NULL argument");
+    if (cuda_set(device)) return fail(S2K_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    CU(cudaMemGetInfo(free_bytes, total_bytes));
+    return S2K_OK;
+}

@@ -390,7 +390,9 @@ struct Req {
     int cols = 0;
     s2k_gen_params gp{};
     int state = S2K_REQ_WAITING;
+    s2k_status status = S2K_OK;  // why a failed request failed
     int slot = -1;
+    int delivered = 0;  // frames handed to the frame callback
     std::vector<int32_t> codes;  // [ncb][n_frames] once finished
     int n_frames = 0;
 };
@@ -414,6 +416,8 @@ struct s2k_sched {
     int32_t *prompt_dev = nullptr;
     size_t prompt_cap = 0;
     s2k_sched_stats stats{};
+    s2k_sched_frame_callback on_frame = nullptr;
+    void *on_frame_user = nullptr;
 };
 
 static void sched_release(s2k_sched *sc) {
@@ -509,7 +513,7 @@ S2K_API s2k_status s2k_sched_submit(s2k_sched *sc, const int32_t *prompt, int32_
 }
 
 // Retire the request in slot i: copy its codes out, return its pages.
-static s2k_status sched_retire(s2k_sched *sc, int i) {
+static s2k_status sched_retire(s2k_sched *sc, int i, int final_state = S2K_REQ_DONE) {
     s2k_model *m = sc->m;
     Slot &sl = sc->slots[i];
     Req &r = sc->reqs[sl.req];
@@ -520,9 +524,10 @@ static s2k_status sched_retire(s2k_sched *sc, int i) {
     s2k_status rc = seq_codes(m, sl.seq, r.codes.data(), (int)(r.codes.size() / std::max(ncb, 1)), &nf);
     if (rc) return rc;
     r.n_frames = nf;
-    r.state = S2K_REQ_DONE;
+    r.state = final_state;
     r.slot = -1;
-    sc->stats.finished++;
+    if (final_state == S2K_REQ_DONE) sc->stats.finished++;
+    else sc->stats.cancelled++;
     for (int p : sl.pages) sc->free_pages.push_back(p);
     sl.pages.clear();
     sl.req = -1;
@@ -578,11 +583,19 @@ static s2k_status sched_admit(s2k_sched *sc) {
         sc->free_pages.resize(sc->free_pages.size() - need);
         s2k_status rc = admit_one(sc, r, s, sl.pages);
         if (rc) {
-            // the request goes back to the head of the queue, its pages to the pool
             for (int pg : sl.pages) sc->free_pages.push_back(pg);
             sl.pages.clear();
-            sc->waiting.push_front(id);
-            return rc;
+            if (rc == S2K_ERR_CUDA || rc == S2K_ERR_TIMEOUT) {
+                // the device failed, not the request: it goes back to the head of the queue
+                sc->waiting.push_front(id);
+                return rc;
+            }
+            // this request cannot run (no memory for it, bad input): it fails
+            // alone and the others carry on
+            r.state = S2K_REQ_FAILED;
+            r.status = rc;
+            sc->stats.failed++;
+            continue;
         }
         sl.req = id;
         r.slot = si;
@@ -618,7 +631,22 @@ S2K_API s2k_status s2k_sched_step(s2k_sched *sc, int32_t *n_live, int32_t *n_wai
         sc->stats.max_live = std::max<int32_t>(sc->stats.max_live, (int32_t)live.size());
         for (size_t j = 0; j < live.size(); ++j) {
             s2k_seq *s = live[j];
-            if (s->hstat->done) {
+            Req &r = sc->reqs[sc->slots[live_slots[j]].req];
+            bool cancel = false;
+            if (sc->on_frame) {
+                // the frame this step produced, from the sequence's host ring
+                const int nf = s->hstat->n_frames;
+                const int ncb = std::max(m->hp.num_codebooks, 1);
+                int codes[16];
+                for (; r.delivered < nf && !cancel; ++r.delivered) {
+                    for (int cb = 0; cb < ncb; ++cb) codes[cb] = s->hstat->ring[r.delivered % kFrameRing][cb];
+                    cancel = !sc->on_frame(sc->slots[live_slots[j]].req, codes, r.delivered, ncb, sc->on_frame_user);
+                }
+            }
+            if (cancel) {
+                rc = sched_retire(sc, live_slots[j], S2K_REQ_CANCELLED);
+                if (rc) return rc;
+            } else if (s->hstat->done) {
                 rc = sched_retire(sc, live_slots[j]);
                 if (rc) return rc;
             }
@@ -626,7 +654,7 @@ S2K_API s2k_status s2k_sched_step(s2k_sched *sc, int32_t *n_live, int32_t *n_wai
         int64_t frames = 0;
         for (Req &r : sc->reqs)
             if (r.state == S2K_REQ_LIVE) frames += sc->slots[r.slot].seq->hstat->n_frames;
-            else if (r.state == S2K_REQ_DONE) frames += r.n_frames;
+            else if (r.state == S2K_REQ_DONE || r.state == S2K_REQ_CANCELLED) frames += r.n_frames;
         sc->stats.frames = frames;
     }
     int nl = 0;
@@ -648,9 +676,15 @@ S2K_API s2k_status s2k_sched_run(s2k_sched *sc) {
 }
 
 S2K_API s2k_status s2k_sched_poll(s2k_sched *sc, int32_t req_id, int32_t *state, int32_t *n_frames) {
+    return s2k_sched_poll_status(sc, req_id, state, n_frames, nullptr);
+}
+
+S2K_API s2k_status s2k_sched_poll_status(s2k_sched *sc, int32_t req_id, int32_t *state, int32_t *n_frames,
+                                         s2k_status *req_status) {
     if (!sc || req_id < 0 || req_id >= (int32_t)sc->reqs.size()) return fail(S2K_ERR_ARG, "bad request id");
     const Req &r = sc->reqs[req_id];
     if (state) *state = r.state;
+    if (req_status) *req_status = r.status;
     if (n_frames) *n_frames = r.state == S2K_REQ_LIVE ? sc->slots[r.slot].seq->hstat->n_frames : r.n_frames;
     return S2K_OK;
 }
@@ -659,7 +693,8 @@ S2K_API s2k_status s2k_sched_result(s2k_sched *sc, int32_t req_id, int32_t *code
                                     int32_t *n_frames) {
     if (!sc || req_id < 0 || req_id >= (int32_t)sc->reqs.size() || !n_frames) return fail(S2K_ERR_ARG, "bad argument");
     const Req &r = sc->reqs[req_id];
-    if (r.state != S2K_REQ_DONE) return fail(S2K_ERR_STATE, "request %d has not finished", req_id);
+    if (r.state != S2K_REQ_DONE && r.state != S2K_REQ_CANCELLED)
+        return fail(S2K_ERR_STATE, "request %d has no result (state %d)", req_id, r.state);
     *n_frames = r.n_frames;
     if (codes_out) {
         if (cap_frames < r.n_frames) return fail(S2K_ERR_ARG, "codes capacity %d < %d frames", cap_frames, r.n_frames);
@@ -673,5 +708,33 @@ S2K_API s2k_status s2k_sched_get_stats(const s2k_sched *sc, s2k_sched_stats *out
     *out = sc->stats;
     out->free_pages = (int32_t)sc->free_pages.size();
     out->pool_pages = sc->pool_pages;
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_sched_cancel(s2k_sched *sc, int32_t req_id) {
+    if (!sc || req_id < 0 || req_id >= (int32_t)sc->reqs.size()) return fail(S2K_ERR_ARG, "bad request id");
+    if (cuda_set(sc->m->device)) return fail(S2K_ERR_CUDA, "cudaSetDevice failed");
+    Req &r = sc->reqs[req_id];
+    if (r.state == S2K_REQ_WAITING) {
+        auto it = std::find(sc->waiting.begin(), sc->waiting.end(), req_id);
+        if (it != sc->waiting.end()) sc->waiting.erase(it);
+        r.state = S2K_REQ_CANCELLED;
+        r.n_frames = 0;
+        r.codes.clear();
+        sc->stats.cancelled++;
+        return S2K_OK;
+    }
+    if (r.state == S2K_REQ_LIVE) {
+        // between frames nothing of the scheduler runs on the device: the
+        // request keeps the frames it has, its pages go back to the pool
+        return sched_retire(sc, r.slot, S2K_REQ_CANCELLED);
+    }
+    return S2K_OK;  // finished, failed or cancelled already: nothing to stop
+}
+
+S2K_API s2k_status s2k_sched_set_frame_callback(s2k_sched *sc, s2k_sched_frame_callback cb, void *user) {
+    if (!sc) return fail(S2K_ERR_ARG, "NULL scheduler");
+    sc->on_frame = cb;
+    sc->on_frame_user = user;
     return S2K_OK;
 }

@@ -23,6 +23,17 @@ enum : int {
 // that a lost copy turns into an error status instead of a hang.
 constexpr long long kWaitLimitCycles = 4000000000LL;
 
+// The model's error block: int word 0 holds the error bits, the 8-byte word
+// at int offset 2 the wait limit in SM cycles (0 = kWaitLimitCycles).  Every
+// kernel gets a pointer to word 0; s2k_model_set_wait_limit writes the limit.
+constexpr int kErrBlockInts = 4;
+
+__device__ __forceinline__ long long wait_limit(const int *err) {
+    if (err == nullptr) return kWaitLimitCycles;
+    const long long v = *reinterpret_cast<const volatile long long *>(err + 2);
+    return v > 0 ? v : kWaitLimitCycles;
+}
+
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -72,9 +83,9 @@ constexpr unsigned kErrPollEvery = 64;
 // their next look at the error word instead of each spending the full limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     if (mbar_test(bar, parity)) return true;
-    const long long t0 = clock64();
+    const long long t0 = clock64(), lim = wait_limit(err);
     for (unsigned it = 1; !mbar_test(bar, parity); ++it) {
-        if (clock64() - t0 > kWaitLimitCycles) {
+        if (clock64() - t0 > lim) {
             if (err) atomicOr(err, code);
             return false;
         }

@@ -5,11 +5,19 @@
 
 namespace s2k {
 
-// Mapped pinned memory the host polls while frames run.
+// Frames of codes a sequence's host ring holds: the host reads frame f from
+// slot f % kFrameRing while later frames run (at most kFrameRing - 1 frames
+// may be in flight ahead of the oldest one the host has not read).
+constexpr int kFrameRing = 8;
+
+// Mapped pinned memory the host polls while frames run.  frame_commit writes
+// frame f's codes into ring[f % kFrameRing], then (after a system-scope
+// fence) n_frames = f + 1.
 struct HostStatus {
     volatile int n_frames;
     volatile int done;
     int pad[2];
+    volatile int ring[kFrameRing][16];
 };
 
 // Generation parameters as the kernels read them (device copy, so a captured

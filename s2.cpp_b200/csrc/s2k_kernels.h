@@ -235,6 +235,8 @@ cudaError_t launch_sample_fast_batch(const float *logits, size_t ld, SeqDev *con
                                      cudaStream_t st);
 cudaError_t launch_frame_commit_batch(SeqDev *const *seqs, int n, cudaStream_t st);
 cudaError_t launch_advance_batch(SeqDev *const *seqs, int n, int T, cudaStream_t st);
+// get_rows of a (tiled) weight matrix: out [n][E->cols] f32 (s2k_get_rows).
+cudaError_t launch_gather_rows(const DevMat *E, const int *ids, int n, float *out, int *err, cudaStream_t st);
 // Standalone sampler (s2k_sample)
 cudaError_t launch_sample_one(const float *logits, int n, float temperature, float top_p, int top_k,
                               double u, int *out, int *err, cudaStream_t st);

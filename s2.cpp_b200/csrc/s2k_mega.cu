@@ -137,9 +137,9 @@ __device__ __forceinline__ float4 ll_wait4(const void *base, size_t i, uint32_t 
                (uint32_t)(w3 >> 32) == tag;
     };
     if (!load()) {
-        const long long t0 = clock64();
+        const long long t0 = clock64(), lim = wait_limit(err);
         for (unsigned it = 1; !load(); ++it) {
-            if (clock64() - t0 > kWaitLimitCycles ||
+            if (clock64() - t0 > lim ||
                 (it % kErrPollEvery == 0 && (*reinterpret_cast<volatile int *>(err) & ERR_GRID))) {
                 atomicOr(err, ERR_GRID);
                 break;
@@ -186,9 +186,9 @@ __device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, 
         // at launch would queue ahead of each of them.  Start the stream once
         // the consumers have moved on to the first GEMV.
         const volatile int *cur = &sm.cur_op;
-        const long long t0 = clock64();
+        const long long t0 = clock64(), lim = wait_limit(err);
         while (*cur < 1) {
-            if (clock64() - t0 > kWaitLimitCycles) return;  // the consumers stopped (their error is reported)
+            if (clock64() - t0 > lim) return;  // the consumers stopped (their error is reported)
             __nanosleep(64);
         }
     }
@@ -221,13 +221,14 @@ __device__ void mega_producer(const MegaOp *ops, int n_ops, MSmem &sm, int cta, 
 // the op before a Slow attention op (its QKV GEMV), one lane pulls the pages
 // of this CTA's attention units into L2, so the unit's bulk copies do not
 // queue behind the weight stream in HBM.
-__device__ void mega_kv_prefetch(const MegaOp *ops, int n_ops, MSmem &sm, int cta, int G) {
+__device__ void mega_kv_prefetch(const MegaOp *ops, int n_ops, MSmem &sm, int cta, int G, const int *err) {
     volatile int *cur = &sm.cur_op;
+    const long long lim = wait_limit(err);
     for (int j = 1; j < n_ops; ++j) {
         if (ops[j].kind != MK_ATTN || ops[j].a.kv_k == nullptr) continue;
         const long long t0 = clock64();
         while (*cur < j - 1) {
-            if (clock64() - t0 > kWaitLimitCycles) return;  // the consumers stopped (their error is reported)
+            if (clock64() - t0 > lim) return;  // the consumers stopped (their error is reported)
             __nanosleep(256);
         }
         const MegaAttn &a = ops[j].a;
@@ -783,7 +784,7 @@ __global__ void __launch_bounds__(kMThreads, 1)
         return;
     }
     if (warp == kMW + 1) {
-        if (lane == 0) mega_kv_prefetch(ops, n_ops, sm, cta, G);
+        if (lane == 0) mega_kv_prefetch(ops, n_ops, sm, cta, G, err);
         return;
     }
     // trace: per op and CTA, [start, prologue done, work done, producer's last tile issued]
@@ -824,9 +825,9 @@ __global__ void __launch_bounds__(kMThreads, 1)
                 __threadfence();
                 atomicAdd(&ctl->pad[0], 1u);
                 if (cta == 0) {
-                    const long long t0 = clock64();
+                    const long long t0 = clock64(), lim = wait_limit(err);
                     while (ld_acquire_u32(&ctl->pad[0]) < (unsigned)G) {
-                        if (clock64() - t0 > kWaitLimitCycles) {
+                        if (clock64() - t0 > lim) {
                             atomicOr(err, ERR_GRID);
                             break;
                         }
@@ -894,6 +895,22 @@ cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, co
     if (mt == 1)
         return cudaLaunchKernelEx(&cfg, mega_kernel<1, false>, d_ops, n_ops, ctl, done, err, ahead, trace, flags, epoch);
     return cudaLaunchKernelEx(&cfg, mega_kernel<2, false>, d_ops, n_ops, ctl, done, err, ahead, trace, flags, epoch);
+}
+
+// Bounded-wait probe: one warp polls four tagged activation words for a tag
+// that no launch writes (epoch 2^24 - 1 is never reached), through the same
+// wait the persistent kernel's consumers use.  It returns once the model's
+// wait limit has passed, with ERR_GRID set in *err.  Only reads `words`.
+__global__ void wait_probe_kernel(const uint64_t *words, int *err) {
+    const float4 v = ll_wait4(words, 0, 0xFFFFFFFFu, err);
+    (void)v;
+}
+
+cudaError_t launch_wait_probe(const uint64_t *words, int *err, cudaStream_t st) {
+    if (words == nullptr || reinterpret_cast<uintptr_t>(words) % 32 != 0) return cudaErrorInvalidValue;
+    count_launch();
+    wait_probe_kernel<<<1, 32, 0, st>>>(words, err);
+    return cudaGetLastError();
 }
 
 }  // namespace s2k

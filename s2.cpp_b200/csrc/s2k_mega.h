@@ -120,6 +120,9 @@ cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, co
 int mega_l2_ahead();
 // Host-side validation of a GEMV op for the persistent kernel.
 bool mega_gemv_ok(const MegaGemv &g);
+// One warp waits (bounded by the model's wait limit) for a tag nobody writes
+// on the tagged words at `words` (32-byte aligned, read only); sets ERR_GRID.
+cudaError_t launch_wait_probe(const uint64_t *words, int *err, cudaStream_t st);
 // Host-side validation of an attention op; max_keys bounds any token's key range.
 bool mega_attn_ok(const MegaAttn &a, int max_keys);
 

@@ -472,16 +472,25 @@ __device__ void frame_commit_body(SeqDev *sd) {
     if (st.done) return;
     const int f = st.n_frames;
     const int i = threadIdx.x;
+    HostStatus *hs = (HostStatus *)__ldcg((const unsigned long long *)&sd->host);
     if (i < c.ncb) {
-        c.codes_out[(size_t)i * c.codes_ld + f] = st.codes[i];
-        st.step_in[1 + i] = st.codes[i];
+        const int code = st.codes[i];
+        c.codes_out[(size_t)i * c.codes_ld + f] = code;
+        st.step_in[1 + i] = code;
+        if (hs) {
+            // streaming hand-off: the frame's codes into the host ring before its count
+            hs->ring[f % kFrameRing][i] = code;
+            __threadfence_system();
+        }
     }
     __syncthreads();
     if (i == 0) {
         st.step_in[0] = st.main_token;
         st.n_frames = f + 1;
-        HostStatus *hs = (HostStatus *)__ldcg((const unsigned long long *)&sd->host);
-        if (hs) hs->n_frames = f + 1;
+        if (hs) {
+            __threadfence_system();
+            hs->n_frames = f + 1;
+        }
     }
 }
 
@@ -604,6 +613,24 @@ cudaError_t launch_advance(SeqDev *sd, int T, const int *done, cudaStream_t st) 
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(1), 0, st, attr);
     count_launch();
     return cudaLaunchKernelEx(&cfg, advance_kernel, sd, T, done);
+}
+
+// get_rows: out[r][c] = dequantized table row ids[r] (grid n, block 256).
+// Invalid ids set ERR_BAD_TOKEN and give a zero row.
+__global__ void gather_rows_kernel(DevMat E, const int *ids, int n, float *out, int *err) {
+    const int r = blockIdx.x;
+    const int id = __ldg(ids + r);
+    const bool ok = id >= 0 && id < E.rows;
+    if (!ok && threadIdx.x == 0) atomicOr(err, ERR_BAD_TOKEN);
+    for (int c = threadIdx.x; c < E.cols; c += blockDim.x)
+        out[(size_t)r * E.cols + c] = ok ? deq_elem(E, id, c) : 0.0f;
+}
+
+cudaError_t launch_gather_rows(const DevMat *E, const int *ids, int n, float *out, int *err, cudaStream_t st) {
+    if (n < 1 || tw_of(E->type) < 0) return cudaErrorInvalidValue;
+    count_launch();
+    gather_rows_kernel<<<n, 256, 0, st>>>(*E, ids, n, out, err);
+    return cudaGetLastError();
 }
 
 // standalone sampler (s2k_sample)

@@ -10,6 +10,7 @@
 #include "s2k_mega.h"
 
 #include <algorithm>
+#include <cstddef>
 #include <string>
 #include <vector>
 
@@ -82,6 +83,9 @@ struct s2k_model {
     float *norm = nullptr, *fast_norm = nullptr;
     std::vector<Layer> layers, fast_layers;
     std::vector<void *> allocs;
+    std::vector<size_t> alloc_bytes;  // size of allocs[i]
+    size_t dev_bytes = 0;             // device bytes this model holds
+    long long fail_alloc_at = -1;     // test hook: the allocation this many allocations ahead fails (once)
     bool finalized = false;
     bool prefill_mma = false;  // the tensor-core prefill path could be set up on this device
     bool prefill_f16 = false;  // the fp16 tensor-core prefill GEMM (F16 models) could be set up
@@ -114,10 +118,14 @@ struct s2k_model {
 
     template <class T>
     cudaError_t alloc(T **p, size_t n) {
+        if (fail_alloc_at >= 0 && fail_alloc_at-- == 0) return cudaErrorMemoryAllocation;
         void *v = nullptr;
-        cudaError_t e = cudaMalloc(&v, std::max<size_t>(n, 1) * sizeof(T));
+        const size_t bytes = std::max<size_t>(n, 1) * sizeof(T);
+        cudaError_t e = cudaMalloc(&v, bytes);
         if (e == cudaSuccess) {
             allocs.push_back(v);
+            alloc_bytes.push_back(bytes);
+            dev_bytes += bytes;
             *p = reinterpret_cast<T *>(v);
         }
         return e;
@@ -125,7 +133,12 @@ struct s2k_model {
     void release(void *p) {
         if (!p) return;
         auto it = std::find(allocs.begin(), allocs.end(), p);
-        if (it != allocs.end()) allocs.erase(it);
+        if (it != allocs.end()) {
+            const size_t i = (size_t)(it - allocs.begin());
+            dev_bytes -= alloc_bytes[i];
+            alloc_bytes.erase(alloc_bytes.begin() + (std::ptrdiff_t)i);
+            allocs.erase(it);
+        }
         cudaFree(p);
     }
 };
@@ -211,3 +224,6 @@ s2k_status check_tokens_host(const s2k_model *m, const int32_t *flat, int32_t T)
 void fill_sample_cfg(const s2k_model *m, const s2k_gen_params *gp, int *d_codes, int codes_ld, SampleCfg *c);
 void batch_free(s2k_model *m);
 s2k_status seq_publish(s2k_seq *s);
+// Whether `name` is a tensor the model binds (the GGUF names SlowARModel
+// reads, src/s2_model.cpp:374-423; Fast-AR tensors only with a fast decoder).
+bool s2k_model_binds(const s2k_model *m, const char *name);

@@ -251,9 +251,9 @@ __device__ __forceinline__ bool ll_load8(const void *p, uint32_t tag, F8 &out) {
 __device__ __forceinline__ F8 ll_wait8(const void *p, uint32_t tag, int *err) {
     F8 out;
     if (ll_load8(p, tag, out)) return out;
-    const long long t0 = clock64();
+    const long long t0 = clock64(), lim = wait_limit(err);
     for (unsigned it = 1; !ll_load8(p, tag, out); ++it) {
-        if (clock64() - t0 > kWaitLimitCycles ||
+        if (clock64() - t0 > lim ||
             (err && it % kErrPollEvery == 0 && (*reinterpret_cast<volatile int *>(err) & ERR_GRID))) {
             if (err) atomicOr(err, ERR_GRID);
             break;
@@ -266,10 +266,10 @@ __device__ __forceinline__ float ll_wait1(const void *p, size_t i, uint32_t tag,
     const uint64_t *q = reinterpret_cast<const uint64_t *>(p) + i;
     uint64_t w = __ldcg(reinterpret_cast<const unsigned long long *>(q));
     if ((uint32_t)(w >> 32) != tag) {
-        const long long t0 = clock64();
+        const long long t0 = clock64(), lim = wait_limit(err);
         unsigned it = 0;
         do {
-            if (clock64() - t0 > kWaitLimitCycles ||
+            if (clock64() - t0 > lim ||
                 (err && ++it % kErrPollEvery == 0 && (*reinterpret_cast<volatile int *>(err) & ERR_GRID))) {
                 if (err) atomicOr(err, ERR_GRID);
                 break;

@@ -37,10 +37,13 @@ EXPORTED = [
     "s2k_profile_frame", "s2k_profile_ops", "s2k_profile_trace",
     "s2k_seq_begin", "s2k_batch_frame", "s2k_seq_frames", "s2k_sched_create", "s2k_sched_free",
     "s2k_sched_submit", "s2k_sched_step", "s2k_sched_run", "s2k_sched_poll", "s2k_sched_result",
-    "s2k_sched_get_stats",
+    "s2k_sched_get_stats", "s2k_sched_poll_status", "s2k_sched_cancel", "s2k_sched_set_frame_callback",
+    "s2k_seq_load_kv", "s2k_get_rows", "s2k_model_set_wait_limit", "s2k_debug_wait_probe", "s2k_debug_fail_alloc",
+    "s2k_model_device_bytes", "s2k_device_mem_info", "s2k_gguf_read_hparams", "s2k_gguf_tensor_info",
+    "s2k_model_load_gguf",
 ]
 
-REQ_WAITING, REQ_LIVE, REQ_DONE = 0, 1, 2  # S2K_REQ_*
+REQ_WAITING, REQ_LIVE, REQ_DONE, REQ_FAILED, REQ_CANCELLED = 0, 1, 2, 3, 4  # S2K_REQ_*
 
 
 class S2KError(RuntimeError):
@@ -77,11 +80,14 @@ class _SchedStats(ctypes.Structure):
     _fields_ = [("steps", ctypes.c_int64), ("frames", ctypes.c_int64), ("prefill_tokens", ctypes.c_int64),
                 ("admitted", ctypes.c_int64), ("finished", ctypes.c_int64), ("kv_positions", ctypes.c_int64),
                 ("max_live", ctypes.c_int32),
-                ("free_pages", ctypes.c_int32), ("pool_pages", ctypes.c_int32)]
+                ("free_pages", ctypes.c_int32), ("pool_pages", ctypes.c_int32), ("pad_", ctypes.c_int32),
+                ("cancelled", ctypes.c_int64), ("failed", ctypes.c_int64)]
 
 
 FRAME_CB = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32,
                             ctypes.c_int32, ctypes.c_void_p)
+SCHED_FRAME_CB = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32,
+                                  ctypes.c_int32, ctypes.c_void_p)
 
 _lib = None
 
@@ -137,6 +143,21 @@ def lib() -> ctypes.CDLL:
         "s2k_sched_poll": ([vp, i32, ctypes.POINTER(i32), ctypes.POINTER(i32)], i32),
         "s2k_sched_result": ([vp, i32, vp, i32, ctypes.POINTER(i32)], i32),
         "s2k_sched_get_stats": ([vp, ctypes.POINTER(_SchedStats)], i32),
+        "s2k_sched_poll_status": ([vp, i32, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32)], i32),
+        "s2k_sched_cancel": ([vp, i32], i32),
+        "s2k_sched_set_frame_callback": ([vp, SCHED_FRAME_CB, vp], i32),
+        "s2k_seq_load_kv": ([vp, vp, vp, i32], i32),
+        "s2k_get_rows": ([vp, ctypes.c_char_p, vp, i32, vp], i32),
+        "s2k_model_set_wait_limit": ([vp, ctypes.c_int64], i32),
+        "s2k_debug_wait_probe": ([vp], i32),
+        "s2k_debug_fail_alloc": ([vp, ctypes.c_int64], i32),
+        "s2k_model_device_bytes": ([vp], ctypes.c_size_t),
+        "s2k_device_mem_info": ([i32, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)], i32),
+        "s2k_gguf_read_hparams": ([ctypes.c_char_p, ctypes.POINTER(_HParams)], i32),
+        "s2k_gguf_tensor_info": ([ctypes.c_char_p, i32, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(i32), i64p,
+                                  ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                                  ctypes.POINTER(i32)], i32),
+        "s2k_model_load_gguf": ([i32, ctypes.c_char_p, ctypes.POINTER(vp)], i32),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -155,6 +176,36 @@ def device_count() -> int:
     n = ctypes.c_int32(0)
     rc = lib().s2k_device_count(ctypes.byref(n))
     return n.value if rc == S2K_OK else 0
+
+
+def device_mem_info(device: int = 0):
+    """(free, total) bytes of a device (cudaMemGetInfo)."""
+    f, t = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    _check(lib().s2k_device_mem_info(device, ctypes.byref(f), ctypes.byref(t)))
+    return f.value, t.value
+
+
+def gguf_read_hparams(path: str) -> dict:
+    """Hyper-parameters of a GGUF file (s2k_gguf_read_hparams), by field name."""
+    h = _HParams()
+    _check(lib().s2k_gguf_read_hparams(os.fsencode(path), ctypes.byref(h)))
+    return {name: getattr(h, name) for name, _ in _HParams._fields_}
+
+
+def gguf_tensors(path: str) -> list:
+    """[(name, ggml type, ne[4], absolute data offset, nbytes)] of a GGUF file."""
+    n = ctypes.c_int32(0)
+    _check(lib().s2k_gguf_tensor_info(os.fsencode(path), -1, None, 0, None, None, None, None, ctypes.byref(n)))
+    out = []
+    for i in range(n.value):
+        name = ctypes.create_string_buffer(512)
+        t = ctypes.c_int32(0)
+        ne = (ctypes.c_int64 * 4)()
+        off, nb = ctypes.c_uint64(0), ctypes.c_uint64(0)
+        _check(lib().s2k_gguf_tensor_info(os.fsencode(path), i, name, 512, ctypes.byref(t), ne, ctypes.byref(off),
+                                          ctypes.byref(nb), None))
+        out.append((name.value.decode(), t.value, tuple(ne), off.value, nb.value))
+    return out
 
 
 def _hp_struct(hp) -> _HParams:
@@ -177,6 +228,20 @@ class SlowARModel:
         self._hp = hparams
         _check(lib().s2k_model_create(device, ctypes.byref(_hp_struct(hparams)), ctypes.byref(self._m)))
         self.device = device
+
+    @classmethod
+    def from_gguf(cls, path: str, device: int = 0) -> "SlowARModel":
+        """A finalized model read from a GGUF file (s2k_model_load_gguf)."""
+        import types
+        self = cls.__new__(cls)
+        self._m = ctypes.c_void_p()
+        self._seq = ctypes.c_void_p()
+        _check(lib().s2k_model_load_gguf(device, os.fsencode(path), ctypes.byref(self._m)))
+        h = _HParams()
+        _check(lib().s2k_model_get_hparams(self._m, ctypes.byref(h)))
+        self._hp = types.SimpleNamespace(**{name: getattr(h, name) for name, _ in _HParams._fields_})
+        self.device = device
+        return self
 
     # --- loading (SlowARModel::load_shared + read_tensor_data) ---
     def upload_tensor(self, name: str, ggml_type: int, ne, data: np.ndarray) -> None:
@@ -206,6 +271,37 @@ class SlowARModel:
 
     def weight_bytes(self) -> int:
         return int(lib().s2k_model_weight_bytes(self._m))
+
+    def device_bytes(self) -> int:
+        """Device bytes the model holds (s2k_model_device_bytes)."""
+        return int(lib().s2k_model_device_bytes(self._m))
+
+    def set_wait_limit(self, cycles: int) -> None:
+        """Bound of every device-side wait, in SM cycles (0 = default)."""
+        _check(lib().s2k_model_set_wait_limit(self._m, int(cycles)))
+
+    def wait_probe(self) -> None:
+        """A bounded wait on a tag nobody writes (raises S2KError ERR_TIMEOUT)."""
+        _check(lib().s2k_debug_wait_probe(self._m))
+
+    def fail_alloc(self, after: int) -> None:
+        """Test hook: the device allocation `after` allocations ahead fails once (-1 disarms)."""
+        _check(lib().s2k_debug_fail_alloc(self._m, int(after)))
+
+    def get_rows(self, table: str, ids) -> np.ndarray:
+        """Rows of a weight table dequantized on the device (s2k_get_rows)."""
+        i = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+        out = np.empty((i.size, self._hp.embedding_length), dtype=np.float32)
+        _check(lib().s2k_get_rows(self._m, table.encode(), _ptr(i), int(i.size), _ptr(out)))
+        return out
+
+    def load_kv(self, k: np.ndarray, v: np.ndarray) -> None:
+        """Restore the KV cache: k, v f16 [layer][pos][kv_head][head_dim]; n_past = pos."""
+        k = np.ascontiguousarray(k, dtype=np.float16)
+        v = np.ascontiguousarray(v, dtype=np.float16)
+        if k.shape != v.shape or k.ndim != 4:
+            raise S2KError(-1, "k and v must both be [layer][pos][kv_head][head_dim]")
+        _check(lib().s2k_seq_load_kv(self._seq, _ptr(k), _ptr(v), int(k.shape[1])))
 
     def stream(self) -> int:
         return int(lib().s2k_model_stream(self._m) or 0)
@@ -467,6 +563,28 @@ class BatchScheduler:
         st, nf = ctypes.c_int32(0), ctypes.c_int32(0)
         _check(lib().s2k_sched_poll(self._sc, req_id, ctypes.byref(st), ctypes.byref(nf)))
         return st.value, nf.value
+
+    def poll_status(self, req_id: int):
+        """(state, n_frames, status of a failed request)."""
+        st, nf, rs = ctypes.c_int32(0), ctypes.c_int32(0), ctypes.c_int32(0)
+        _check(lib().s2k_sched_poll_status(self._sc, req_id, ctypes.byref(st), ctypes.byref(nf), ctypes.byref(rs)))
+        return st.value, nf.value, rs.value
+
+    def cancel(self, req_id: int) -> None:
+        _check(lib().s2k_sched_cancel(self._sc, req_id))
+
+    def set_frame_callback(self, fn: Optional[Callable[[int, np.ndarray, int], bool]]) -> None:
+        """fn(req_id, codes [num_codebooks], frame_index) after each frame; False cancels the request."""
+        if fn is None:
+            self._cb = None
+            _check(lib().s2k_sched_set_frame_callback(self._sc, SCHED_FRAME_CB(), None))
+            return
+
+        def _cb(rid, codes_ptr, idx, ncb_, user):
+            arr = np.ctypeslib.as_array(codes_ptr, shape=(ncb_,)).copy()
+            return 1 if fn(rid, arr, idx) else 0
+        self._cb = SCHED_FRAME_CB(_cb)  # kept alive while the scheduler holds it
+        _check(lib().s2k_sched_set_frame_callback(self._sc, self._cb, None))
 
     def result(self, req_id: int) -> np.ndarray:
         nf = ctypes.c_int32(0)

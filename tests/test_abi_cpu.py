@@ -56,5 +56,5 @@ def test_sched_stats_struct_layout_matches_header():
         if decl:
             names += [n.strip() for n in decl.split(None, 1)[1].split(",")]
     assert names == [f for f, _ in s2k._SchedStats._fields_]
-    # 6 int64 + 3 int32, padded to 8-byte alignment
-    assert ctypes.sizeof(s2k._SchedStats) == 64
+    # 6 int64, 4 int32, 2 int64
+    assert ctypes.sizeof(s2k._SchedStats) == 80

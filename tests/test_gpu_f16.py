@@ -1,9 +1,10 @@
 """GPU parity for F16 (unquantized) weights against the CPU oracle, through
 the C ABI.  The F16 mat-vec rounds the activation to fp16 (ggml's vec_dot_type
 for F16 weights) and sums the exact fp16 x fp16 products in double, on both
-sides, so decode is held to the same bars as Q8_0: logits within
-1e-2 * std(logits), identical greedy codes, and batched frames equal to
-single-sequence frames."""
+sides, so decode is held to the same bars as Q8_0: bit-exact logits, identical
+greedy codes, and batched frames equal to single-sequence frames.  Prompts of
+8+ tokens prefill through the fp16 tensor-core GEMM (fp32 sums), which, and
+the steps reading the K/V it cached, are held to 1e-2 * std(logits)."""
 from __future__ import annotations
 
 import numpy as np
@@ -12,17 +13,10 @@ import pytest
 import oracle
 import s2k
 import synthetic
+from parity_util import assert_close, assert_exact
 
 pytestmark = pytest.mark.gpu
 
-LOGIT_TOL = 1e-2
-
-
-def assert_close(got: np.ndarray, want: np.ndarray, what: str) -> None:
-    assert np.isfinite(got).all(), f"{what}: non-finite values"
-    err = float(np.abs(got - want).max())
-    bound = LOGIT_TOL * float(want.std())
-    assert err <= bound, f"{what}: max|delta| {err:.3e} > {bound:.3e}"
 
 
 @pytest.fixture(scope="module")
@@ -46,8 +40,8 @@ def test_f16_steps_and_fast(f16_pair):
     om.init_kv_cache(64)
     hg, lg = m.prefill_fast(p.T.reshape(-1), 6)
     ho, lo = om.eval(p.T.reshape(-1), 6)
-    assert_close(hg, ho, "f16 prefill hidden")
-    assert_close(lg, lo, "f16 prefill logits")
+    assert_exact(hg, ho, "f16 prefill hidden")
+    assert_exact(lg, lo, "f16 prefill logits")
     rng = np.random.default_rng(3)
     for i in range(4):
         tok = np.zeros(hp.num_codebooks + 1, np.int32)
@@ -55,10 +49,10 @@ def test_f16_steps_and_fast(f16_pair):
         tok[0] = hp.semantic_begin_id + tok[1] if i % 2 == 0 else rng.integers(0, hp.semantic_begin_id)
         hg, lg = m.step(tok)
         ho, lo = om.eval(tok, 1)
-        assert_close(lg, lo, f"f16 step {i} logits")
+        assert_exact(lg, lo, f"f16 step {i} logits")
     for n in range(hp.num_codebooks):
         prefix = rng.integers(0, hp.codebook_size, n).astype(np.int32)
-        assert_close(m.fast_decode(ho, prefix), om.fast_decode(ho, prefix), f"f16 fast_decode {n}")
+        assert_exact(m.fast_decode(ho, prefix), om.fast_decode(ho, prefix), f"f16 fast_decode {n}")
 
 
 def test_f16_generate_greedy_64(f16_pair):
@@ -138,7 +132,7 @@ def test_f16_mid_real_widths():
     _, lg = m.step(tok)
     ho, lo = om.eval(tok, 1)
     assert_close(lg, lo, "f16 mid step logits")
-    assert_close(m.fast_decode(ho, np.array([5, 9], np.int32)), om.fast_decode(ho, np.array([5, 9], np.int32)),
+    assert_exact(m.fast_decode(ho, np.array([5, 9], np.int32)), om.fast_decode(ho, np.array([5, 9], np.int32)),
                  "f16 mid fast_decode")
     m.close()
     om.close()

@@ -10,17 +10,10 @@ import pytest
 import oracle
 import s2k
 import synthetic
+from parity_util import assert_exact
 
 pytestmark = pytest.mark.gpu
 
-LOGIT_TOL = 1e-2
-
-
-def assert_close(got: np.ndarray, want: np.ndarray, what: str) -> None:
-    assert np.isfinite(got).all(), f"{what}: non-finite values"
-    err = float(np.abs(got - want).max())
-    bound = LOGIT_TOL * float(want.std())
-    assert err <= bound, f"{what}: max|delta| {err:.3e} > {bound:.3e}"
 
 
 @pytest.fixture(scope="module")
@@ -44,8 +37,8 @@ def test_kquant_prefill_steps_fast(kq_pair):
     om.init_kv_cache(64)
     hg, lg = m.prefill_fast(p.T.reshape(-1), 16)
     ho, lo = om.eval(p.T.reshape(-1), 16)
-    assert_close(hg, ho, "kquant prefill hidden")
-    assert_close(lg, lo, "kquant prefill logits")
+    assert_exact(hg, ho, "kquant prefill hidden")
+    assert_exact(lg, lo, "kquant prefill logits")
     rng = np.random.default_rng(3)
     for i in range(4):
         tok = np.zeros(hp.num_codebooks + 1, np.int32)
@@ -53,10 +46,10 @@ def test_kquant_prefill_steps_fast(kq_pair):
         tok[0] = hp.semantic_begin_id + tok[1] if i % 2 == 0 else rng.integers(0, hp.semantic_begin_id)
         hg, lg = m.step(tok)
         ho, lo = om.eval(tok, 1)
-        assert_close(lg, lo, f"kquant step {i} logits")
+        assert_exact(lg, lo, f"kquant step {i} logits")
     for n in range(hp.num_codebooks):
         prefix = rng.integers(0, hp.codebook_size, n).astype(np.int32)
-        assert_close(m.fast_decode(ho, prefix), om.fast_decode(ho, prefix), f"kquant fast_decode {n}")
+        assert_exact(m.fast_decode(ho, prefix), om.fast_decode(ho, prefix), f"kquant fast_decode {n}")
 
 
 def test_kquant_generate_greedy_64(kq_pair):
@@ -86,14 +79,14 @@ def test_kquant_prefill_long_prompt(kq_pair):
     om.init_kv_cache(128)
     hg, lg = m.prefill_fast(p.T.reshape(-1), 96)
     ho, lo = om.eval(p.T.reshape(-1), 96)
-    assert_close(hg, ho, "kquant long prefill hidden")
-    assert_close(lg, lo, "kquant long prefill logits")
+    assert_exact(hg, ho, "kquant long prefill hidden")
+    assert_exact(lg, lo, "kquant long prefill logits")
     for i in range(3):
         tok = np.zeros(hp.num_codebooks + 1, np.int32)
         tok[0] = 17 + i
         hg, lg = m.step(tok)
         ho, lo = om.eval(tok, 1)
-        assert_close(lg, lo, f"kquant step {i} after long prefill")
+        assert_exact(lg, lo, f"kquant step {i} after long prefill")
 
 
 @pytest.mark.parametrize("T", [64, 150])
@@ -109,13 +102,13 @@ def test_kquant_tensor_core_prefill_tiles(kq_pair, T):
     om.init_kv_cache(T + 4)
     hg, lg = m.prefill_fast(flat, T)
     ho, lo = om.eval(flat, T)
-    assert_close(hg, ho, f"kquant tc prefill hidden T={T}")
-    assert_close(lg, lo, f"kquant tc prefill logits T={T}")
+    assert_exact(hg, ho, f"kquant tc prefill hidden T={T}")
+    assert_exact(lg, lo, f"kquant tc prefill logits T={T}")
     tok = np.zeros(hp.num_codebooks + 1, np.int32)
     tok[0] = 9
     _, lg = m.step(tok)
     _, lo = om.eval(tok, 1)
-    assert_close(lg, lo, f"kquant step after tc prefill T={T}")
+    assert_exact(lg, lo, f"kquant step after tc prefill T={T}")
 
 
 def test_kquant_tensor_core_prefill_real_widths():
@@ -133,13 +126,13 @@ def test_kquant_tensor_core_prefill_real_widths():
     om.init_kv_cache(80)
     hg, lg = m.prefill_fast(p.T.reshape(-1), 72)
     ho, lo = om.eval(p.T.reshape(-1), 72)
-    assert_close(hg, ho, "kquant mid prefill hidden")
-    assert_close(lg, lo, "kquant mid prefill logits")
+    assert_exact(hg, ho, "kquant mid prefill hidden")
+    assert_exact(lg, lo, "kquant mid prefill logits")
     tok = np.zeros(hp.num_codebooks + 1, np.int32)
     tok[0] = 1000
     _, lg = m.step(tok)
     _, lo = om.eval(tok, 1)
-    assert_close(lg, lo, "kquant mid step logits")
+    assert_exact(lg, lo, "kquant mid step logits")
     m.close()
     om.close()
 

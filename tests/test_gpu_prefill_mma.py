@@ -1,6 +1,8 @@
 """GPU: the tensor-core prefill GEMM (tcgen05 int8 MMAs with the double-
 precision block-scale epilogue) on prompts of one to three token tiles,
-ragged last tile and split-K partials included, against the CPU oracle."""
+ragged last tile and split-K partials included, against the CPU oracle.
+Each int8 MMA over a 32-column block is one exact Q8_0 block sum, so the
+prefill is bit-exact with the oracle."""
 from __future__ import annotations
 
 import numpy as np
@@ -8,6 +10,7 @@ import pytest
 
 import s2k
 import synthetic
+from parity_util import assert_exact
 
 pytestmark = pytest.mark.gpu
 
@@ -23,6 +26,5 @@ def test_prefill_mma_matches_oracle(small_model_data, small_oracle, n):
     hg, lg = m.prefill_fast(p.T.reshape(-1), n)
     ho, lo = small_oracle.eval(p.T.reshape(-1), n)
     m.close()
-    for got, want, what in ((hg, ho, "hidden"), (lg, lo, "logits")):
-        err = float(np.abs(got - want).max())
-        assert err <= 1e-2 * float(want.std()), f"{what}: {err}"
+    assert_exact(hg, ho, f"{n}-token tensor-core prefill hidden")
+    assert_exact(lg, lo, f"{n}-token tensor-core prefill logits")

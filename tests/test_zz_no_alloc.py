@@ -1,9 +1,12 @@
 """s2k_sample_noalloc: the allocation-free sampler entry (fixed static device
 scratch) against s2k_sample on the same logits and uniform draws.
 
-Collected last (file name) so it runs both alone and after every other GPU
-test on a device whose allocator has already been exercised.  Tokens are
-integers: the two entries must agree exactly, on two calls in a row.
+It exists for callers that may not allocate device memory, for instance a
+host that runs under a fixed device-memory budget set up front.  Collected
+last (file name) so it runs both alone and after every other GPU test on a
+device whose allocator has already been exercised.  Tokens are integers: the
+two entries must agree exactly, on two calls in a row.  The calls must leave
+the model's device bytes and the device's free memory unchanged.
 """
 from __future__ import annotations
 
@@ -60,3 +63,20 @@ def test_noalloc_rejects_oversize(model):
     y = np.zeros(16, np.float32)
     y[5] = 1.0
     assert model.sample_noalloc(y, 0.0, 1.0, 0) == 5
+
+
+def test_noalloc_allocates_nothing(model):
+    """After a first call (which looks up the scratch array's address), calls
+    of every size leave the model's device bytes and the device's free memory
+    unchanged."""
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal(s2k.SAMPLE_NOALLOC_MAX_N).astype(np.float32)
+    model.sample_noalloc(x, 0.8, 0.9, 30, 0.5)
+    held = model.device_bytes()
+    free0, _ = s2k.device_mem_info(model.device)
+    for n in (1, 777, 4096, s2k.SAMPLE_NOALLOC_MAX_N):
+        for _ in range(2):
+            model.sample_noalloc(x[:n], 0.8, 0.9, 30, float(rng.uniform()))
+    free1, _ = s2k.device_mem_info(model.device)
+    assert model.device_bytes() == held
+    assert free1 == free0
