@@ -220,6 +220,25 @@ S2K_API s2k_status s2k_generate_device(s2k_model *m, s2k_seq *s, const int32_t *
                                        int32_t cols, const s2k_gen_params *gp,
                                        int32_t *d_codes_out, int32_t *n_frames_out);
 
+/* Tokenizer callback for s2k_build_prompt: writes the token ids of `text`
+ * (at most cap of them; ids may be NULL with cap 0 to ask for the count) and
+ * returns how many the text encodes to, or a negative value on failure
+ * (the reference's Tokenizer::encode, src/s2_tokenizer.cpp). */
+typedef int32_t (*s2k_encode_fn)(const char *text, int32_t *ids, int32_t cap, void *user);
+
+/* s2::build_prompt (src/s2_prompt.cpp:5-103): the PromptTensor grid
+ * [num_codebooks+1][cols] row-major for a synthesis of `text`, voice-cloned
+ * from a reference clip when prompt_codes ([num_codebooks][T_prompt]
+ * cb-major), T_prompt > 0 and a non-empty prompt_text (its transcript) are
+ * given: the system / user / assistant turns encoded by `encode`, the
+ * reference codes under their semantic tokens (codebook 0 + semantic_begin_id)
+ * and code rows that are zero elsewhere.  *rows / *cols get the grid shape;
+ * with out NULL only the shape is computed (a size query). */
+S2K_API s2k_status s2k_build_prompt(s2k_encode_fn encode, void *user, const char *text, const char *prompt_text,
+                                    const int32_t *prompt_codes, int32_t num_codebooks, int32_t T_prompt,
+                                    int32_t im_end_id, int32_t voice_id, int32_t semantic_begin_id, int32_t *out,
+                                    size_t cap, int32_t *rows, int32_t *cols);
+
 /* Sampler on the device for one logits row already in device memory
  * (s2::sample_token, src/s2_sampler.cpp:42-99; tie break = lowest index).
  * u is the uniform draw used when temperature > 0.  Host logits in, token out. */

@@ -40,7 +40,7 @@ EXPORTED = [
     "s2k_sched_get_stats", "s2k_sched_poll_status", "s2k_sched_cancel", "s2k_sched_set_frame_callback",
     "s2k_seq_load_kv", "s2k_get_rows", "s2k_model_set_wait_limit", "s2k_debug_wait_probe", "s2k_debug_fail_alloc",
     "s2k_model_device_bytes", "s2k_device_mem_info", "s2k_gguf_read_hparams", "s2k_gguf_tensor_info",
-    "s2k_model_load_gguf",
+    "s2k_model_load_gguf", "s2k_build_prompt",
 ]
 
 REQ_WAITING, REQ_LIVE, REQ_DONE, REQ_FAILED, REQ_CANCELLED = 0, 1, 2, 3, 4  # S2K_REQ_*
@@ -86,6 +86,8 @@ class _SchedStats(ctypes.Structure):
 
 FRAME_CB = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32,
                             ctypes.c_int32, ctypes.c_void_p)
+ENCODE_FN = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32,
+                             ctypes.c_void_p)
 SCHED_FRAME_CB = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32,
                                   ctypes.c_int32, ctypes.c_void_p)
 
@@ -158,6 +160,8 @@ def lib() -> ctypes.CDLL:
                                   ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
                                   ctypes.POINTER(i32)], i32),
         "s2k_model_load_gguf": ([i32, ctypes.c_char_p, ctypes.POINTER(vp)], i32),
+        "s2k_build_prompt": ([ENCODE_FN, vp, ctypes.c_char_p, ctypes.c_char_p, vp, i32, i32, i32, i32, i32, vp,
+                              ctypes.c_size_t, ctypes.POINTER(i32), ctypes.POINTER(i32)], i32),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -183,6 +187,33 @@ def device_mem_info(device: int = 0):
     f, t = ctypes.c_size_t(0), ctypes.c_size_t(0)
     _check(lib().s2k_device_mem_info(device, ctypes.byref(f), ctypes.byref(t)))
     return f.value, t.value
+
+
+def build_prompt(encode: Callable[[str], list], text: str, prompt_text: str = "", prompt_codes=None,
+                 num_codebooks: int = 10, im_end_id: int = 151645, voice_id: int = 151673,
+                 semantic_begin_id: int = 151678) -> np.ndarray:
+    """s2::build_prompt through s2k_build_prompt: the PromptTensor grid
+    [num_codebooks+1][cols].  encode(text) -> token ids stands in for the
+    tokenizer; prompt_codes [num_codebooks][T_prompt] is the reference clip."""
+    def _enc(txt, ids, cap, user):
+        try:
+            toks = list(encode(txt.decode()))
+        except Exception:
+            return -1
+        for i in range(min(cap, len(toks))):
+            ids[i] = toks[i]
+        return len(toks)
+    cb = ENCODE_FN(_enc)
+    codes = None if prompt_codes is None else np.ascontiguousarray(prompt_codes, dtype=np.int32)
+    T = 0 if codes is None else int(codes.shape[1])
+    cptr = None if codes is None else _ptr(codes)
+    rows, cols = ctypes.c_int32(0), ctypes.c_int32(0)
+    args = (cb, None, text.encode(), prompt_text.encode(), cptr, num_codebooks, T, im_end_id, voice_id,
+            semantic_begin_id)
+    _check(lib().s2k_build_prompt(*args, None, 0, ctypes.byref(rows), ctypes.byref(cols)))
+    out = np.zeros((rows.value, cols.value), dtype=np.int32)
+    _check(lib().s2k_build_prompt(*args, _ptr(out), out.size, ctypes.byref(rows), ctypes.byref(cols)))
+    return out
 
 
 def gguf_read_hparams(path: str) -> dict:
