@@ -86,9 +86,10 @@ cudaError_t work_alloc(s2k_model *m, Work &w, int T, int L, int dim, int H, int 
     const size_t units = tm * Hkv * (size_t)w.n_split_max;
     if ((e = m->alloc(&w.part, units * (H / Hkv) * hd))) return e;
     if ((e = m->alloc(&w.part_ms, units * (H / Hkv) * 2))) return e;
-    // split arrival counters per (layer, token, kv head): no reuse within a launch
-    if ((e = m->alloc(&w.counters, (size_t)n_layers * tm * Hkv))) return e;
-    if ((e = cudaMemset(w.counters, 0, (size_t)n_layers * tm * Hkv * sizeof(int)))) return e;
+    // split arrival counters per (layer, token, kv head, head block): no reuse within a launch
+    const size_t n_counters = (size_t)n_layers * tm * Hkv * kAttnMaxGroup;
+    if ((e = m->alloc(&w.counters, n_counters))) return e;
+    if ((e = cudaMemset(w.counters, 0, n_counters * sizeof(int)))) return e;
     if ((e = m->alloc(&w.lx, tm * dim))) return e;
     if ((e = m->alloc(&w.lh, tm * dim))) return e;
     if ((e = m->alloc(&w.lqkv, tm * (w.qs + 2 * w.kvs)))) return e;
@@ -868,6 +869,9 @@ S2K_API void s2k_seq_free(s2k_seq *s) {
     m->release(s->prompt);
     m->release(s->mega_ops);
     m->release(s->mega_ctl);
+    m->release(s->eval_ops);
+    m->release(s->eval_ctl);
+    m->release(s->eval_tokens);
     if (s->hstat) cudaFreeHost((void *)s->hstat);
     delete s;
 }
@@ -889,6 +893,8 @@ s2k_status check_tokens_host(const s2k_model *m, const int32_t *flat, int32_t T)
     return S2K_OK;
 }
 
+static s2k_status ensure_eval_program(s2k_model *m, s2k_seq *s);
+
 S2K_API s2k_status s2k_eval(s2k_model *m, s2k_seq *s, const int32_t *flat, int32_t T, float *hidden_out,
                             float *logits_out) {
     if (!m || !s || !flat || T <= 0) return fail(S2K_ERR_ARG, "bad argument");
@@ -902,14 +908,28 @@ S2K_API s2k_status s2k_eval(s2k_model *m, s2k_seq *s, const int32_t *flat, int32
     rc = ensure_slow_work(m, T, s->max_seq_len);
     if (rc) return rc;
     const int stride = m->hp.num_codebooks + 1;
-    if (m->tokens_cap < T * stride) {
-        m->release(m->tokens);
-        m->tokens = nullptr;
-        CU(m->alloc(&m->tokens, (size_t)T * stride));
-        m->tokens_cap = T * stride;
+    bool on_mega = false;
+    if (T == 1 && !s->pooled) {
+        // one token: the whole step as one persistent-kernel launch
+        rc = ensure_eval_program(m, s);
+        if (rc) return rc;
+        on_mega = s->eval_ok;
     }
-    CU(cudaMemcpyAsync(m->tokens, flat, (size_t)T * stride * sizeof(int), cudaMemcpyHostToDevice, m->stream));
-    CU(enqueue_slow(m, s, T, m->tokens, nullptr));
+    if (on_mega) {
+        CU(cudaMemcpyAsync(s->eval_tokens, flat, (size_t)stride * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        CU(cudaMemsetAsync(s->eval_ctl, 0, sizeof(MegaCtl), m->stream));
+        CU(launch_mega(s->eval_ops, s->eval_len, 1, s->eval_ctl, nullptr, m->d_err, m->num_sms, m->stream, m->d_epoch,
+                       s->eval_q8));
+    } else {
+        if (m->tokens_cap < T * stride) {
+            m->release(m->tokens);
+            m->tokens = nullptr;
+            CU(m->alloc(&m->tokens, (size_t)T * stride));
+            m->tokens_cap = T * stride;
+        }
+        CU(cudaMemcpyAsync(m->tokens, flat, (size_t)T * stride * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        CU(enqueue_slow(m, s, T, m->tokens, nullptr));
+    }
     if (hidden_out)
         CU(cudaMemcpyAsync(hidden_out, m->hidden, (size_t)m->hp.embedding_length * 4, cudaMemcpyDeviceToHost, m->stream));
     if (logits_out)
@@ -1128,7 +1148,7 @@ static bool add_layers(s2k_model *m, s2k_seq *s, bool fast, int T, int pos_add, 
         a.a.layer = (int)il;
         a.a.part = w.part;
         a.a.part_ms = w.part_ms;
-        a.a.counters = w.counters + il * tn * Hkv;  // per layer: no counter is reused within a launch
+        a.a.counters = w.counters + il * tn * Hkv * kAttnMaxGroup;  // per layer: none is reused within a launch
         a.a.n_split_max = w.n_split_max;
         a.a.out = w.lattn;
         if (T * H > w.Tm * w.H || !mega_attn_ok(a.a, fast ? pos_add + T : s->max_seq_len)) return false;
@@ -1142,6 +1162,76 @@ static bool add_layers(s2k_model *m, s2k_seq *s, bool fast, int T, int pos_add, 
         x_op = d_op;
     }
     return true;
+}
+
+// The Slow-AR step over one token (eval_cached with n_tokens = 1,
+// src/s2_model.cpp:860-1097) as persistent-kernel ops appended to `ops`:
+// embedding of the token row at `tokens` ([num_codebooks+1] ints in device
+// memory), the layers, the final norm + tied LM head (logits, post-norm
+// hidden), then n_past += 1.  False when a shape falls outside the kernel's
+// limits.
+static bool push_slow_step(s2k_model *m, s2k_seq *s, const int *tokens, std::vector<MegaOp> &ops) {
+    const s2k_hparams &hp = m->hp;
+    const int start = (int)ops.size();
+    MegaOp e;
+    memset(&e, 0, sizeof(e));
+    e.kind = MK_EMBED_SLOW;
+    e.es.e = m->embed.w;
+    e.es.etype = tw_of(m->embed.type);
+    e.es.ctype = hp.num_codebooks > 0 ? tw_of(m->cb_embed.type) : 0;
+    e.es.e_rows = m->embed.rows;
+    e.es.dim = hp.embedding_length;
+    e.es.c = hp.num_codebooks > 0 ? m->cb_embed.w : nullptr;
+    e.es.c_rows = hp.num_codebooks > 0 ? m->cb_embed.rows : 0;
+    e.es.tokens = tokens;
+    e.es.T = 1;
+    e.es.ncb = hp.num_codebooks;
+    e.es.cb_size = hp.codebook_size;
+    e.es.sem_begin = hp.semantic_begin_id;
+    e.es.sem_end = hp.semantic_end_id;
+    e.es.scale_cb = hp.scale_codebook_embeddings;
+    e.es.sem_scale = 1.0f / sqrtf((float)(hp.num_codebooks + 1));
+    e.es.x = m->sw.lx;
+    e.es.tag = 0;
+    ops.push_back(e);
+    int x_op = 0;
+    if (!add_layers(m, s, false, 1, 0, ops, start, x_op)) return false;
+    ops.push_back(mk_gemv(m->embed, m->sw.lx, hp.embedding_length, 1, IN_RMSNORM, m->norm, hp.rms_norm_eps,
+                          EPI_STORE, m->logits, hp.vocab_size, nullptr, 0, m->hidden, LL_X, x_op));
+    MegaOp adv;
+    memset(&adv, 0, sizeof(adv));
+    adv.kind = MK_ADVANCE;
+    adv.adv.n_past = &s->dev->state.n_past;
+    adv.adv.T = 1;
+    ops.push_back(adv);
+    for (size_t i = (size_t)start; i < ops.size(); ++i)
+        if (ops[i].kind == MK_GEMV && !mega_gemv_ok(ops[i].g)) return false;
+    if ((int)ops.size() - start > 255) return false;  // op indices are the low 8 bits of the activation tags
+    return hp.num_codebooks <= 16;  // the persistent kernel's embedding sums at most 16 codebooks
+}
+
+// A single-token s2k_eval on the persistent kernel: the Slow step segment
+// reading its token row from the sequence's eval_tokens, built once per
+// sequence and workspace generation.
+static s2k_status ensure_eval_program(s2k_model *m, s2k_seq *s) {
+    if (s->eval_gen == m->ws_gen) return S2K_OK;
+    if (!s->eval_tokens) CU(m->alloc(&s->eval_tokens, 32));
+    if (!s->eval_ctl) CU(m->alloc(&s->eval_ctl, 1));
+    std::vector<MegaOp> ops;
+    s->eval_ok = push_slow_step(m, s, s->eval_tokens, ops);
+    s->eval_q8 = true;
+    for (const MegaOp &o : ops)
+        if (o.kind == MK_GEMV && o.g.wtype != TW_Q8_0) s->eval_q8 = false;
+    m->release(s->eval_ops);
+    s->eval_ops = nullptr;
+    s->eval_len = 0;
+    if (s->eval_ok) {
+        CU(m->alloc(&s->eval_ops, ops.size()));
+        CU(cudaMemcpy(s->eval_ops, ops.data(), ops.size() * sizeof(MegaOp), cudaMemcpyHostToDevice));
+        s->eval_len = (int)ops.size();
+    }
+    s->eval_gen = m->ws_gen;
+    return S2K_OK;
 }
 
 // Builds the segments of one frame: 9 Fast-AR passes and the Slow step.
@@ -1182,37 +1272,7 @@ static s2k_status build_mega(s2k_model *m, s2k_seq *s) {
     }
     {
         const int start = (int)ops.size();
-        MegaOp e;
-        memset(&e, 0, sizeof(e));
-        e.kind = MK_EMBED_SLOW;
-        e.es.e = m->embed.w;
-        e.es.etype = tw_of(m->embed.type);
-        e.es.ctype = hp.num_codebooks > 0 ? tw_of(m->cb_embed.type) : 0;
-        e.es.e_rows = m->embed.rows;
-        e.es.dim = hp.embedding_length;
-        e.es.c = hp.num_codebooks > 0 ? m->cb_embed.w : nullptr;
-        e.es.c_rows = hp.num_codebooks > 0 ? m->cb_embed.rows : 0;
-        e.es.tokens = s->dev->state.step_in;
-        e.es.T = 1;
-        e.es.ncb = hp.num_codebooks;
-        e.es.cb_size = hp.codebook_size;
-        e.es.sem_begin = hp.semantic_begin_id;
-        e.es.sem_end = hp.semantic_end_id;
-        e.es.scale_cb = hp.scale_codebook_embeddings;
-        e.es.sem_scale = 1.0f / sqrtf((float)(hp.num_codebooks + 1));
-        e.es.x = m->sw.lx;
-        e.es.tag = 0;
-        ops.push_back(e);
-        int x_op = 0;
-        ok = ok && add_layers(m, s, false, 1, 0, ops, start, x_op);
-        ops.push_back(mk_gemv(m->embed, m->sw.lx, hp.embedding_length, 1, IN_RMSNORM, m->norm, hp.rms_norm_eps,
-                              EPI_STORE, m->logits, hp.vocab_size, nullptr, 0, m->hidden, LL_X, x_op));
-        MegaOp adv;
-        memset(&adv, 0, sizeof(adv));
-        adv.kind = MK_ADVANCE;
-        adv.adv.n_past = &s->dev->state.n_past;
-        adv.adv.T = 1;
-        ops.push_back(adv);
+        ok = ok && push_slow_step(m, s, s->dev->state.step_in, ops);
         s->seg_start.push_back(start);
         s->seg_len.push_back((int)ops.size() - start);
         s->seg_mt.push_back(1);

@@ -48,7 +48,7 @@ bool mega_gemv_ok(const MegaGemv &g) {
     return true;
 }
 
-constexpr int kAG = 4;    // most query heads per kv head (one attention unit serves a whole group)
+constexpr int kAG = kAttnMaxGroup;  // most query heads per kv head (register arrays of a unit)
 constexpr int kAF32 = 32;  // most f32 key rows of a unit (Fast-AR context)
 constexpr int kCombineFast = 8;  // splits the combining unit reads in one round trip
 
@@ -124,6 +124,55 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+// Units of an attention op: one per (token, kv head, head block, split of
+// kAttnSplit keys).  A head block is nh query heads of the kv head's group:
+// the fewest heads per unit (1, 2 or the whole group) that still give every
+// unit a CTA of its own, so a short context spreads over more SMs and each
+// unit does less of the double-precision score and value work.  Every head's
+// arithmetic is the same whatever the block size (scores, split softmax and
+// split partials are per head).  All CTAs of a launch read the same n_past
+// (it advances only after every CTA has finished the segment's ops), so they
+// agree on the plan.
+struct AttnPlan {
+    int nc, pos0, nspl, nh, nhb, units;
+};
+
+__device__ __forceinline__ AttnPlan attn_plan(const MegaAttn &a, int G) {
+    AttnPlan p;
+    const int base = a.pos_base ? __ldcg(a.pos_base) : 0;
+    p.nc = a.n_cached_from_pos_base ? base : 0;
+    p.pos0 = base + a.pos_add;
+    p.nspl = (p.nc + a.cur_base + a.T + kAttnSplit - 1) / kAttnSplit;
+    const int grp = a.H / a.Hkv;
+    const int per = a.T * a.Hkv * p.nspl;  // units per head block
+    if (per * grp <= G) {
+        p.nh = 1;
+    } else if (grp % 2 == 0 && per * (grp / 2) <= G) {
+        p.nh = 2;
+    } else {
+        p.nh = grp;
+    }
+    p.nhb = grp / p.nh;
+    p.units = per * p.nhb;
+    return p;
+}
+
+struct AttnUnit {
+    int t, g, hb, i;
+};
+
+__device__ __forceinline__ AttnUnit attn_unit_of(const MegaAttn &a, const AttnPlan &p, int u) {
+    AttnUnit x;
+    const int per_t = a.Hkv * p.nhb * p.nspl, per_g = p.nhb * p.nspl;
+    x.t = u / per_t;
+    int r = u - x.t * per_t;
+    x.g = r / per_g;
+    r -= x.g * per_g;
+    x.hb = r / p.nspl;
+    x.i = r - x.hb * p.nspl;
+    return x;
 }
 
 // 4 tagged activation words at element i of base (32-byte aligned), polled
@@ -232,11 +281,11 @@ __device__ void mega_kv_prefetch(const MegaOp *ops, int n_ops, MSmem &sm, int ct
             __nanosleep(256);
         }
         const MegaAttn &a = ops[j].a;
-        const int nc = a.n_cached_from_pos_base && a.pos_base ? __ldcg(a.pos_base) : 0;
-        const int nspl = (nc + a.cur_base + a.T + kAttnSplit - 1) / kAttnSplit;
-        const int units = a.T * a.Hkv * nspl;
-        for (int u = cta; u < units; u += G) {
-            const int t = u / (a.Hkv * nspl), r = u - t * (a.Hkv * nspl), g = r / nspl, i = r - g * nspl;
+        const AttnPlan pl = attn_plan(a, G);
+        const int nc = pl.nc;
+        for (int u = cta; u < pl.units; u += G) {
+            const AttnUnit un = attn_unit_of(a, pl, u);
+            const int t = un.t, g = un.g, i = un.i;
             const int j0 = i * kAttnSplit, cnt = min(kAttnSplit, nc + a.cur_base + t + 1 - j0);
             const int ncp = max(0, min(cnt, nc - j0));
             for (int p = 0; p < (ncp + kPage - 1) / kPage; ++p) {
@@ -320,10 +369,10 @@ __device__ __forceinline__ float4 head_norm_rope_warp(float4 x, bool has_norm, f
 }
 
 // Norm weights and (cos, sin) pairs a consumer thread needs in its first
-// attention unit (unit = cta): warps 0..G-1 normalize query head `warp` of
-// the unit's group, warps 4 and 6 this call's keys of tokens 0 and 1.  None
-// of it depends on the previous op, so the loads are issued before the grid
-// barrier.
+// attention unit (unit = cta): warps 0..nh-1 normalize the unit's query
+// heads, warps 4 and 6 this call's keys of tokens 0 and 1.  None of it
+// depends on the previous op, so the loads are issued before the op's input
+// is polled.
 struct AttnPre {
     float4 nw, cs;
 };
@@ -332,24 +381,20 @@ __device__ __forceinline__ const float2 *rope_row(const MegaAttn &a, int pos) {
     return a.rope + (size_t)min(max(pos, 0), a.rope_positions - 1) * (kHD / 2);
 }
 
-__device__ __forceinline__ AttnPre attn_preload(const MegaAttn &a, int u) {
+__device__ __forceinline__ AttnPre attn_preload(const MegaAttn &a, int u, int G) {
     AttnPre p;
     p.nw = p.cs = make_float4(0.f, 0.f, 0.f, 0.f);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int grp = a.H / a.Hkv;
-    const int base = a.pos_base ? __ldcg(a.pos_base) : 0;
-    const int nc = a.n_cached_from_pos_base ? base : 0;
-    const int pos0 = base + a.pos_add;
-    const int nspl = (nc + a.cur_base + a.T + kAttnSplit - 1) / kAttnSplit;
-    if (u >= a.T * a.Hkv * nspl) return p;
-    const int t = u / (a.Hkv * nspl);
+    const AttnPlan pl = attn_plan(a, G);
+    if (u >= pl.units) return p;
+    const int t = attn_unit_of(a, pl, u).t;
     int pos = -1;
     const float *nw = nullptr;
-    if (warp < grp) {
-        pos = pos0 + t;
+    if (warp < pl.nh) {
+        pos = pl.pos0 + t;
         nw = a.q_norm;
     } else if (warp >= 4 && ((warp - 4) & 1) == 0 && ((warp - 4) >> 1) <= t) {
-        pos = pos0 + ((warp - 4) >> 1);
+        pos = pl.pos0 + ((warp - 4) >> 1);
         nw = a.k_norm;
     }
     if (nw != nullptr) p.nw = __ldg(reinterpret_cast<const float4 *>(nw) + lane);
@@ -357,336 +402,367 @@ __device__ __forceinline__ AttnPre attn_preload(const MegaAttn &a, int u) {
     return p;
 }
 
-__device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int cta, int G, int *err,
-                          unsigned long long *tr, uint32_t &apar, uint32_t ep8) {
-    const uint32_t in_tag = ep8 | a.in_tag, out_tag = ep8 | a.out_tag;
+// One attention unit (src/s2_model.cpp:979-1039 for query heads h0..h0+nh-1
+// of kv head g; GQA h -> h / (H / Hkv)): per-head qk-norm, RoPE mode 0, past
+// keys and values from the f16 cache, this call's keys and values un-rounded
+// f32, and softmax . V in the split convention the CPU oracle shares:
+//   s_j = float(sum_d double(k_j[d]) * double(q[d])) * scale
+//   split i: m_i = max s_j, e_j = det_expf(s_j - m_i),
+//            S_i = sum double(e_j), O_i[d] = sum double(v_j[d]) * double(e_j)
+//   out = float((sum_i O_i[d] * double(w_i)) / (sum_i S_i * double(w_i))),
+//         w_i = det_expf(m_i - max_i m_i)
+// A single-split unit writes out directly; otherwise each unit stores its
+// (O_i, m_i, S_i) and the last unit of the (token, kv head, head block) to
+// arrive combines the splits in order.  HPU bounds nh (register arrays).
+//
+// Latency plan: the split's cache pages are bulk-copied into shared memory at
+// the start of the unit, while warps 0..nh-1 normalize and rotate the queries
+// and warps 4..7 this call's keys and values.  Scores use four threads per
+// key (32 dims each), values two threads per output dim (even / odd keys).
+template <int HPU>
+__device__ void attn_unit(const MegaAttn &a, const AttnPlan &pl, const AttnUnit &un, const AttnPre &pre, bool first,
+                          MSmem &sm, int cta, int *err, unsigned long long *tr, uint32_t &apar, uint32_t in_tag,
+                          uint32_t out_tag) {
     AttnSm &as = sm.u.a;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int grp = a.H / a.Hkv;
+    const int nh = pl.nh;  // <= HPU
     const bool slow = a.kv_k != nullptr;
-    const int base = a.pos_base ? __ldcg(a.pos_base) : 0;
-    const int nc = a.n_cached_from_pos_base ? base : 0;  // positions in the paged cache
-    const int pos0 = base + a.pos_add;                    // position of this call's token 0
-    const int nspl = (nc + a.cur_base + a.T + kAttnSplit - 1) / kAttnSplit;
-    const int units = a.T * a.Hkv * nspl;
-    auto mark = [&](int u, int k) {
-        if (tr != nullptr && u == cta && tid == 0) tr[k] = globaltimer_ns();
+    const int nc = pl.nc, pos0 = pl.pos0;
+    const int t = un.t, g = un.g, hb = un.hb, i = un.i, h0 = hb * nh;
+    auto mark = [&](int k) {
+        if (tr != nullptr && first && tid == 0) tr[k] = globaltimer_ns();
     };
-    if (slow && cta < units && !sm.ptab_ready) {
+    const int Lk = nc + a.cur_base + t + 1;  // keys of token t
+    const int nsp = (Lk + kAttnSplit - 1) / kAttnSplit;
+    if (i >= nsp) return;  // CTA-uniform
+    const int j0 = i * kAttnSplit, cnt = min(kAttnSplit, Lk - j0);
+    const int ncp = slow ? max(0, min(cnt, nc - j0)) : 0;  // cached keys of the split
+    const int npg = (ncp + kPage - 1) / kPage;
+    // ---- A. the split's cache pages -> shared memory (bulk copies) ----
+    if (npg > 0 && tid == kMNC - 32) {  // warp 7 (this call's v of token 1: idle at T = 1) issues the copies
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&sm.abar, (uint32_t)(2 * npg * kPage * kHD * sizeof(__half)));
+        for (int p = 0; p < npg; ++p) {
+            const int pg = j0 / kPage + p;
+            const int page = pg < kPtab ? sm.ptab[pg] : __ldcg(a.block_table + pg);
+            const size_t off = (((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage * kHD;
+            bulk_g2s_plain(&as.k.h[p * kPage][0], a.kv_k + off, kPage * kHD * sizeof(__half), &sm.abar);
+            bulk_g2s_plain(&as.v.h[p * kPage][0], a.kv_v + off, kPage * kHD * sizeof(__half), &sm.abar);
+        }
+    }
+    // ---- B. queries (warps 0..nh-1), this call's keys / values (warps 4..7) ----
+    const bool has_cur = j0 + cnt > nc + a.cur_base;  // the split reaches this call's tokens
+    const bool own = (nc + a.cur_base + t) / kAttnSplit == i && hb == 0;  // this unit stores token t's K/V
+    if (warp < nh) {
+        const int h = g * grp + h0 + warp;
+        const int pos = pos0 + t;
+        if (pos >= a.rope_positions && lane == 0) atomicOr(err, ERR_BAD_POS);
+        const float4 x = ll_wait4(a.qkv, (size_t)t * a.ldqkv + (size_t)h * kHD + 4 * lane, in_tag, err);
+        const float4 y = head_norm_rope_warp(x, a.q_norm != nullptr, pre.nw, a.eps, pre.cs);
+        double *qd = &as.q[warp][lane >> 3][4 * (lane & 7)];  // 16-byte aligned: 34-double rows
+        qd[0] = (double)y.x;
+        qd[1] = (double)y.y;
+        qd[2] = (double)y.z;
+        qd[3] = (double)y.w;
+    } else if (warp >= 4 && has_cur) {
+        const int tt = (warp - 4) >> 1, isv = (warp - 4) & 1;
+        if (tt <= t) {
+            const int pos = pos0 + tt;
+            float4 x = ll_wait4(a.qkv, (size_t)tt * a.ldqkv + (size_t)(a.H + (isv ? a.Hkv : 0) + g) * kHD + 4 * lane,
+                                in_tag, err);
+            if (!isv) x = head_norm_rope_warp(x, a.k_norm != nullptr, pre.nw, a.eps, pre.cs);
+            float *dst = slow ? (isv ? as.vc[tt] : as.kc[tt]) : (isv ? as.v.f[a.cur_base + tt] : as.k.f[a.cur_base + tt]);
+            reinterpret_cast<float4 *>(dst)[lane] = x;
+            if (tt == t && own) {
+                // token t's K/V: f32 for the later calls of this frame, f16 into the cache (Slow)
+                float *cur = (isv ? a.vcur : a.kcur) + ((size_t)(a.cur_base + t) * a.Hkv + g) * kHD;
+                reinterpret_cast<float4 *>(cur)[lane] = x;
+                if (slow) {
+                    const int pg = pos / kPage, slot = pos - pg * kPage;
+                    if (pos >= 0 && pg < a.kv_pages) {
+                        const int page = __ldcg(a.block_table + pg);
+                        __half *c = (isv ? a.kv_v : a.kv_k) +
+                                    ((((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage + slot) * kHD;
+                        __half2 *c2 = reinterpret_cast<__half2 *>(c) + 2 * lane;
+                        c2[0] = __floats2half2_rn(x.x, x.y);
+                        c2[1] = __floats2half2_rn(x.z, x.w);
+                    } else if (lane == 0) {
+                        atomicOr(err, ERR_BAD_POS);
+                    }
+                }
+            }
+        }
+    }
+    mark(8);
+    if (!slow) {
+        // earlier Fast-AR positions of this frame: f32 rows written by the previous passes
+        for (int idx = tid; idx < a.cur_base * 64; idx += kMNC) {
+            const int row = idx >> 6, isv = (idx >> 5) & 1, c4 = idx & 31;
+            const float4 x = __ldcg(reinterpret_cast<const float4 *>((isv ? a.vcur : a.kcur) +
+                                                                     ((size_t)row * a.Hkv + g) * kHD) + c4);
+            reinterpret_cast<float4 *>(isv ? as.v.f[row] : as.k.f[row])[c4] = x;
+        }
+    }
+    named_sync(3, kMNC);
+    mark(9);
+    if (npg > 0) {
+        mbar_wait(&sm.abar, apar, err, ERR_WAIT_FULL);
+        apar ^= 1u;
+    }
+    mark(4);
+    // ---- C. scores: thread (key jj = tid / 4, quarter c = tid % 4) over 32 dims ----
+    {
+        const int jj = tid >> 2, c = tid & 3;
+        double acc[HPU];
+#pragma unroll
+        for (int h = 0; h < HPU; ++h) acc[h] = 0.0;
+        if (jj < cnt) {
+            const int j = j0 + jj;
+            if (j < nc) {
+                const uint4 *kp = reinterpret_cast<const uint4 *>(&as.k.h[jj][32 * c]);
+#pragma unroll
+                for (int qd = 0; qd < 4; ++qd) {
+                    const uint4 raw = kp[qd];
+                    const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) {
+                        const float2 f = __half22float2(hh[p]);
+                        const double k0 = (double)f.x, k1 = (double)f.y;
+#pragma unroll
+                        for (int h = 0; h < HPU; ++h) {
+                            const double2 qq = *reinterpret_cast<const double2 *>(&as.q[h][c][8 * qd + 2 * p]);
+                            acc[h] += k0 * qq.x + k1 * qq.y;
+                        }
+                    }
+                }
+            } else {
+                const float *kr = slow ? &as.kc[j - nc][32 * c] : &as.k.f[jj][32 * c];
+#pragma unroll
+                for (int d4 = 0; d4 < 8; ++d4) {
+                    const float4 f = reinterpret_cast<const float4 *>(kr)[d4];
+#pragma unroll
+                    for (int h = 0; h < HPU; ++h) {
+                        const double2 q0 = *reinterpret_cast<const double2 *>(&as.q[h][c][4 * d4]);
+                        const double2 q1 = *reinterpret_cast<const double2 *>(&as.q[h][c][4 * d4 + 2]);
+                        acc[h] += (double)f.x * q0.x + (double)f.y * q0.y + (double)f.z * q1.x + (double)f.w * q1.y;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < HPU; ++h) {
+            acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
+            acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 2);
+        }
+        if (c == 0 && jj < cnt)
+#pragma unroll
+            for (int h = 0; h < HPU; ++h)
+                if (h < nh) as.s[h][jj] = __fmul_rn((float)acc[h], a.scale);
+    }
+    named_sync(3, kMNC);
+    mark(5);
+    // ---- D. the split's softmax statistics: warp h for head h ----
+    if (warp < nh) {
+        const float s0 = lane < cnt ? as.s[warp][lane] : -INFINITY;
+        const float s1 = lane + 32 < cnt ? as.s[warp][lane + 32] : -INFINITY;
+        const float mx = warp_max(fmaxf(s0, s1));
+        const float e0 = lane < cnt ? det_expf(__fsub_rn(s0, mx)) : 0.f;
+        const float e1 = lane + 32 < cnt ? det_expf(__fsub_rn(s1, mx)) : 0.f;
+        as.e[lane][warp] = (double)e0;
+        as.e[lane + 32][warp] = (double)e1;
+        const double S = warp_sum_d((double)e0 + (double)e1);
+        if (lane == 0) {
+            as.m[warp] = mx;
+            as.S[warp] = S;
+        }
+    }
+    named_sync(3, kMNC);
+    mark(6);
+    // ---- E. values: thread (dim d = tid % 128, key parity kh = tid / 128) ----
+    const int d = tid & (kHD - 1), kh = tid >> 7;
+    double o[HPU];
+#pragma unroll
+    for (int h = 0; h < HPU; ++h) o[h] = 0.0;
+#pragma unroll 4
+    for (int jj = kh; jj < cnt; jj += 2) {
+        const int j = j0 + jj;
+        const double vd = j < nc ? (double)__half2float(as.v.h[jj][d])
+                                 : (double)(slow ? as.vc[j - nc][d] : as.v.f[jj][d]);
+        if constexpr (HPU == 1) {
+            o[0] += vd * as.e[jj][0];
+        } else {
+            const double2 e01 = *reinterpret_cast<const double2 *>(&as.e[jj][0]);
+            o[0] += vd * e01.x;
+            o[1] += vd * e01.y;
+            if constexpr (HPU == 4) {
+                const double2 e23 = *reinterpret_cast<const double2 *>(&as.e[jj][2]);
+                o[2] += vd * e23.x;
+                o[3] += vd * e23.y;
+            }
+        }
+    }
+    if (kh == 1)
+#pragma unroll
+        for (int h = 0; h < HPU; ++h) as.o[h][d] = o[h];
+    named_sync(3, kMNC);
+    mark(7);
+    if (kh == 0)
+#pragma unroll
+        for (int h = 0; h < HPU; ++h) o[h] += as.o[h][d];
+    const size_t out_row = (size_t)t * a.H * kHD + (size_t)(g * grp + h0) * kHD;
+    if (nsp == 1) {
+        if (kh == 0)
+#pragma unroll
+            for (int h = 0; h < HPU; ++h)
+                if (h < nh) ll_store(a.out, out_row + (size_t)h * kHD + d, (float)(o[h] / as.S[h]), out_tag);
+        named_sync(3, kMNC);  // the unit's shared buffers are free for the next unit
+        return;
+    }
+    const size_t pu = ((size_t)t * a.Hkv + g) * a.n_split_max;
+    if (kh == 0)
+#pragma unroll
+        for (int h = 0; h < HPU; ++h)
+            if (h < nh) a.part[((pu + i) * grp + h0 + h) * kHD + d] = o[h];
+    if (tid < nh) {
+        a.part_ms[((pu + i) * grp + h0 + tid) * 2] = (double)as.m[tid];
+        a.part_ms[((pu + i) * grp + h0 + tid) * 2 + 1] = as.S[tid];
+    }
+    named_sync(3, kMNC);
+    int *counter = a.counters + ((size_t)t * a.Hkv + g) * kAG + hb;
+    if (tid == 0) {
+        mark(10);
+        // release: the CTA's partials (ordered before this thread by the CTA
+        // barrier) become visible before the count; acquire: the other
+        // units' partials are visible to this CTA after the next barrier
+        unsigned old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+        as.last = (int)old == nsp - 1;
+        mark(3);
+    }
+    named_sync(3, kMNC);
+    if (as.last) {
+        // combine in split order; (m_k, S_k) staged in shared memory, weights
+        // w_k = det_expf(m_k - M); thread (d, kh) sums local heads kh, kh + 2
+        if (nsp <= kCombineFast) {
+            // one round trip: (m_k, S_k) staged by threads p < nh * nsp while every
+            // thread loads its own O_k[h][d] of heads kh, kh + 2 into registers
+            double ov[2][kCombineFast];
+#pragma unroll
+            for (int x = 0; x < 2; ++x)
+#pragma unroll
+                for (int k = 0; k < kCombineFast; ++k)
+                    ov[x][k] = (kh + 2 * x < nh && k < nsp)
+                                   ? __ldcg(a.part + ((pu + k) * grp + h0 + kh + 2 * x) * kHD + d)
+                                   : 0.0;
+            if (tid < nh * nsp) {
+                const int h = tid / nsp, k = tid - h * nsp;
+                const double2 ms = __ldcg(reinterpret_cast<const double2 *>(a.part_ms + ((pu + k) * grp + h0 + h) * 2));
+                as.s[h][k] = (float)ms.x;
+                as.e[k][h] = ms.y;
+            }
+            named_sync(3, kMNC);
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+                const int h = kh + 2 * x;
+                if (h < nh) {
+                    float M = as.s[h][0];
+                    for (int k = 1; k < nsp; ++k) M = fmaxf(M, as.s[h][k]);
+                    double acc = 0.0, S = 0.0;
+#pragma unroll
+                    for (int k = 0; k < kCombineFast; ++k)
+                        if (k < nsp) {
+                            const double w = (double)det_expf(__fsub_rn(as.s[h][k], M));
+                            acc += ov[x][k] * w;
+                            S += as.e[k][h] * w;
+                        }
+                    ll_store(a.out, out_row + (size_t)h * kHD + d, (float)(acc / S), out_tag);
+                }
+            }
+            if (tid == 0) *counter = 0;
+            named_sync(3, kMNC);
+            return;
+        }
+        const int nch = (nsp + kAttnSplit - 1) / kAttnSplit;
+        auto stage = [&](int kb, int kn) {
+            for (int p = tid; p < nh * kn; p += kMNC) {
+                const int h = p / kn, k = p - h * kn;
+                const double2 ms = __ldcg(reinterpret_cast<const double2 *>(a.part_ms + ((pu + kb + k) * grp + h0 + h) * 2));
+                as.s[h][k] = (float)ms.x;
+                as.e[k][h] = ms.y;
+            }
+            named_sync(3, kMNC);
+        };
+        for (int c = 0; c < nch; ++c) {
+            const int kb = c * kAttnSplit, kn = min(kAttnSplit, nsp - kb);
+            stage(kb, kn);
+            if (warp < nh) {
+                float mx = fmaxf(lane < kn ? as.s[warp][lane] : -INFINITY,
+                                 lane + 32 < kn ? as.s[warp][lane + 32] : -INFINITY);
+                mx = warp_max(mx);
+                if (lane == 0) as.m[warp] = c == 0 ? mx : fmaxf(as.m[warp], mx);
+            }
+            named_sync(3, kMNC);
+        }
+        double acc[2] = {0.0, 0.0}, S[2] = {0.0, 0.0};
+        for (int c = 0; c < nch; ++c) {
+            const int kb = c * kAttnSplit, kn = min(kAttnSplit, nsp - kb);
+            if (nch > 1) stage(kb, kn);  // one chunk: still staged from the max pass
+            for (int p = tid; p < nh * kn; p += kMNC) {
+                const int h = p / kn, k = p - h * kn;
+                as.o[h][k] = (double)det_expf(__fsub_rn(as.s[h][k], as.m[h]));
+            }
+            named_sync(3, kMNC);
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+                const int h = kh + 2 * x;
+                if (h < nh) {
+                    const double *src = a.part + ((pu + kb) * grp + h0 + h) * kHD + d;
+#pragma unroll 8
+                    for (int k = 0; k < kn; ++k) {
+                        acc[x] += __ldcg(src + (size_t)k * grp * kHD) * as.o[h][k];
+                        S[x] += as.e[k][h] * as.o[h][k];
+                    }
+                }
+            }
+            named_sync(3, kMNC);
+        }
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+            const int h = kh + 2 * x;
+            if (h < nh) ll_store(a.out, out_row + (size_t)h * kHD + d, (float)(acc[x] / S[x]), out_tag);
+        }
+        if (tid == 0) *counter = 0;
+    }
+    named_sync(3, kMNC);  // the unit's shared buffers are free for the next unit
+}
+
+__device__ void mega_attn(const MegaAttn &a, const AttnPre &pre, MSmem &sm, int cta, int G, int *err,
+                          unsigned long long *tr, uint32_t &apar, uint32_t ep8) {
+    const uint32_t in_tag = ep8 | a.in_tag, out_tag = ep8 | a.out_tag;
+    const int tid = threadIdx.x;
+    const bool slow = a.kv_k != nullptr;
+    const AttnPlan pl = attn_plan(a, G);
+    if (slow && cta < pl.units && !sm.ptab_ready) {
         // the block table and n_past do not change within a segment: stage the
         // page ids once, at the first attention op this CTA runs
-        const int npg = min((nc + kPage - 1) / kPage, kPtab);
+        const int npg = min((pl.nc + kPage - 1) / kPage, kPtab);
         for (int i = tid; i < npg; i += kMNC) sm.ptab[i] = __ldcg(a.block_table + i);
         named_sync(3, kMNC);
         if (tid == 0) sm.ptab_ready = 1;
     }
-    for (int u = cta; u < units; u += G) {
-        const int t = u / (a.Hkv * nspl), r = u - t * (a.Hkv * nspl), g = r / nspl, i = r - g * nspl;
-        const int Lk = nc + a.cur_base + t + 1;  // keys of token t
-        const int nsp = (Lk + kAttnSplit - 1) / kAttnSplit;
-        if (i >= nsp) continue;  // CTA-uniform
-        const int j0 = i * kAttnSplit, cnt = min(kAttnSplit, Lk - j0);
-        const int ncp = slow ? max(0, min(cnt, nc - j0)) : 0;  // cached keys of the split
-        const int npg = (ncp + kPage - 1) / kPage;
-        // ---- A. the split's cache pages -> shared memory (bulk copies) ----
-        if (npg > 0 && tid == kMNC - 32) {  // warp 7 (this call's v of token 1: idle at T = 1) issues the copies
-            fence_proxy_async_smem();
-            mbar_arrive_expect_tx(&sm.abar, (uint32_t)(2 * npg * kPage * kHD * sizeof(__half)));
-            for (int p = 0; p < npg; ++p) {
-                const int pg = j0 / kPage + p;
-                const int page = pg < kPtab ? sm.ptab[pg] : __ldcg(a.block_table + pg);
-                const size_t off = (((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage * kHD;
-                bulk_g2s_plain(&as.k.h[p * kPage][0], a.kv_k + off, kPage * kHD * sizeof(__half), &sm.abar);
-                bulk_g2s_plain(&as.v.h[p * kPage][0], a.kv_v + off, kPage * kHD * sizeof(__half), &sm.abar);
-            }
-        }
-        // ---- B. queries (warps 0..grp-1), this call's keys / values (warps 4..7) ----
-        const bool has_cur = j0 + cnt > nc + a.cur_base;  // the split reaches this call's tokens
-        const bool own = (nc + a.cur_base + t) / kAttnSplit == i;  // token t's own key lies in this split
-        if (warp < grp) {
-            const int h = g * grp + warp;
-            const int pos = pos0 + t;
-            if (pos >= a.rope_positions && lane == 0) atomicOr(err, ERR_BAD_POS);
-            const float4 x = ll_wait4(a.qkv, (size_t)t * a.ldqkv + (size_t)h * kHD + 4 * lane, in_tag, err);
-            const AttnPre pp = u == cta ? pre : attn_preload(a, u);
-            const float4 y = head_norm_rope_warp(x, a.q_norm != nullptr, pp.nw, a.eps, pp.cs);
-            double *qd = &as.q[warp][lane >> 3][4 * (lane & 7)];  // 16-byte aligned: 34-double rows
-            qd[0] = (double)y.x;
-            qd[1] = (double)y.y;
-            qd[2] = (double)y.z;
-            qd[3] = (double)y.w;
-        } else if (warp >= 4 && has_cur) {
-            const int tt = (warp - 4) >> 1, isv = (warp - 4) & 1;
-            if (tt <= t) {
-                const int pos = pos0 + tt;
-                float4 x = ll_wait4(a.qkv, (size_t)tt * a.ldqkv + (size_t)(a.H + (isv ? a.Hkv : 0) + g) * kHD + 4 * lane,
-                                    in_tag, err);
-                if (!isv) {
-                    const AttnPre pp = u == cta ? pre : attn_preload(a, u);
-                    x = head_norm_rope_warp(x, a.k_norm != nullptr, pp.nw, a.eps, pp.cs);
-                }
-                float *dst = slow ? (isv ? as.vc[tt] : as.kc[tt]) : (isv ? as.v.f[a.cur_base + tt] : as.k.f[a.cur_base + tt]);
-                reinterpret_cast<float4 *>(dst)[lane] = x;
-                if (tt == t && own) {
-                    // token t's K/V: f32 for the later calls of this frame, f16 into the cache (Slow)
-                    float *cur = (isv ? a.vcur : a.kcur) + ((size_t)(a.cur_base + t) * a.Hkv + g) * kHD;
-                    reinterpret_cast<float4 *>(cur)[lane] = x;
-                    if (slow) {
-                        const int pg = pos / kPage, slot = pos - pg * kPage;
-                        if (pos >= 0 && pg < a.kv_pages) {
-                            const int page = __ldcg(a.block_table + pg);
-                            __half *c = (isv ? a.kv_v : a.kv_k) +
-                                        ((((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage + slot) * kHD;
-                            __half2 *c2 = reinterpret_cast<__half2 *>(c) + 2 * lane;
-                            c2[0] = __floats2half2_rn(x.x, x.y);
-                            c2[1] = __floats2half2_rn(x.z, x.w);
-                        } else if (lane == 0) {
-                            atomicOr(err, ERR_BAD_POS);
-                        }
-                    }
-                }
-            }
-        }
-        mark(u, 8);
-        if (!slow) {
-            // earlier Fast-AR positions of this frame: f32 rows written by the previous passes
-            for (int idx = tid; idx < a.cur_base * 64; idx += kMNC) {
-                const int row = idx >> 6, isv = (idx >> 5) & 1, c4 = idx & 31;
-                const float4 x = __ldcg(reinterpret_cast<const float4 *>((isv ? a.vcur : a.kcur) +
-                                                                         ((size_t)row * a.Hkv + g) * kHD) + c4);
-                reinterpret_cast<float4 *>(isv ? as.v.f[row] : as.k.f[row])[c4] = x;
-            }
-        }
-        named_sync(3, kMNC);
-        mark(u, 9);
-        if (npg > 0) {
-            mbar_wait(&sm.abar, apar, err, ERR_WAIT_FULL);
-            apar ^= 1u;
-        }
-        mark(u, 4);
-        // ---- C. scores: thread (key jj = tid / 4, quarter c = tid % 4) over 32 dims ----
-        {
-            const int jj = tid >> 2, c = tid & 3;
-            double acc[kAG];
-#pragma unroll
-            for (int h = 0; h < kAG; ++h) acc[h] = 0.0;
-            if (jj < cnt) {
-                const int j = j0 + jj;
-                if (j < nc) {
-                    const uint4 *kp = reinterpret_cast<const uint4 *>(&as.k.h[jj][32 * c]);
-#pragma unroll
-                    for (int qd = 0; qd < 4; ++qd) {
-                        const uint4 raw = kp[qd];
-                        const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
-#pragma unroll
-                        for (int p = 0; p < 4; ++p) {
-                            const float2 f = __half22float2(hh[p]);
-                            const double k0 = (double)f.x, k1 = (double)f.y;
-#pragma unroll
-                            for (int h = 0; h < kAG; ++h) {
-                                const double2 qq = *reinterpret_cast<const double2 *>(&as.q[h][c][8 * qd + 2 * p]);
-                                acc[h] += k0 * qq.x + k1 * qq.y;
-                            }
-                        }
-                    }
-                } else {
-                    const float *kr = slow ? &as.kc[j - nc][32 * c] : &as.k.f[jj][32 * c];
-#pragma unroll
-                    for (int d4 = 0; d4 < 8; ++d4) {
-                        const float4 f = reinterpret_cast<const float4 *>(kr)[d4];
-#pragma unroll
-                        for (int h = 0; h < kAG; ++h) {
-                            const double2 q0 = *reinterpret_cast<const double2 *>(&as.q[h][c][4 * d4]);
-                            const double2 q1 = *reinterpret_cast<const double2 *>(&as.q[h][c][4 * d4 + 2]);
-                            acc[h] += (double)f.x * q0.x + (double)f.y * q0.y + (double)f.z * q1.x + (double)f.w * q1.y;
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int h = 0; h < kAG; ++h) {
-                acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
-                acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 2);
-            }
-            if (c == 0 && jj < cnt)
-#pragma unroll
-                for (int h = 0; h < kAG; ++h)
-                    if (h < grp) as.s[h][jj] = __fmul_rn((float)acc[h], a.scale);
-        }
-        named_sync(3, kMNC);
-        mark(u, 5);
-        // ---- D. the split's softmax statistics: warp h for head h ----
-        if (warp < grp) {
-            const float s0 = lane < cnt ? as.s[warp][lane] : -INFINITY;
-            const float s1 = lane + 32 < cnt ? as.s[warp][lane + 32] : -INFINITY;
-            const float mx = warp_max(fmaxf(s0, s1));
-            const float e0 = lane < cnt ? det_expf(__fsub_rn(s0, mx)) : 0.f;
-            const float e1 = lane + 32 < cnt ? det_expf(__fsub_rn(s1, mx)) : 0.f;
-            as.e[lane][warp] = (double)e0;
-            as.e[lane + 32][warp] = (double)e1;
-            const double S = warp_sum_d((double)e0 + (double)e1);
-            if (lane == 0) {
-                as.m[warp] = mx;
-                as.S[warp] = S;
-            }
-        }
-        named_sync(3, kMNC);
-        mark(u, 6);
-        // ---- E. values: thread (dim d = tid % 128, key parity kh = tid / 128) ----
-        const int d = tid & (kHD - 1), kh = tid >> 7;
-        double o[kAG];
-#pragma unroll
-        for (int h = 0; h < kAG; ++h) o[h] = 0.0;
-#pragma unroll 4
-        for (int jj = kh; jj < cnt; jj += 2) {
-            const int j = j0 + jj;
-            const double vd = j < nc ? (double)__half2float(as.v.h[jj][d])
-                                     : (double)(slow ? as.vc[j - nc][d] : as.v.f[jj][d]);
-            const double2 e01 = *reinterpret_cast<const double2 *>(&as.e[jj][0]);
-            const double2 e23 = *reinterpret_cast<const double2 *>(&as.e[jj][2]);
-            o[0] += vd * e01.x;
-            o[1] += vd * e01.y;
-            o[2] += vd * e23.x;
-            o[3] += vd * e23.y;
-        }
-        if (kh == 1)
-#pragma unroll
-            for (int h = 0; h < kAG; ++h) as.o[h][d] = o[h];
-        named_sync(3, kMNC);
-        mark(u, 7);
-        if (kh == 0)
-#pragma unroll
-            for (int h = 0; h < kAG; ++h) o[h] += as.o[h][d];
-        if (nsp == 1) {
-            if (kh == 0)
-#pragma unroll
-                for (int h = 0; h < kAG; ++h)
-                    if (h < grp)
-                        ll_store(a.out, (size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d, (float)(o[h] / as.S[h]),
-                                 out_tag);
-        } else {
-            const size_t pu = ((size_t)t * a.Hkv + g) * a.n_split_max;
-            if (kh == 0)
-#pragma unroll
-                for (int h = 0; h < kAG; ++h)
-                    if (h < grp) a.part[((pu + i) * grp + h) * kHD + d] = o[h];
-            if (tid < grp) {
-                a.part_ms[((pu + i) * grp + tid) * 2] = (double)as.m[tid];
-                a.part_ms[((pu + i) * grp + tid) * 2 + 1] = as.S[tid];
-            }
-            named_sync(3, kMNC);
-            if (tid == 0) {
-                mark(u, 10);
-                // release: the CTA's partials (ordered before this thread by the CTA
-                // barrier) become visible before the count; acquire: the other
-                // units' partials are visible to this CTA after the next barrier
-                unsigned old;
-                asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + t * a.Hkv + g) : "memory");
-                as.last = (int)old == nsp - 1;
-                mark(u, 3);
-            }
-            named_sync(3, kMNC);
-            if (as.last) {
-                // combine in split order; (m_k, S_k) staged in shared memory in chunks of
-                // kAttnSplit splits (one parallel load each), weights w_k = det_expf(m_k - M)
-                // kept as doubles in as.o; thread (d, kh) sums heads kh, kh + 2
-                if (nsp <= kCombineFast) {
-                    // one round trip: (m_k, S_k) staged by threads p < grp * nsp while every
-                    // thread loads its own O_k[h][d] of heads kh, kh + 2 into registers
-                    double ov[2][kCombineFast];
-#pragma unroll
-                    for (int x = 0; x < 2; ++x)
-#pragma unroll
-                        for (int k = 0; k < kCombineFast; ++k)
-                            ov[x][k] = (kh + 2 * x < grp && k < nsp)
-                                           ? __ldcg(a.part + ((pu + k) * grp + kh + 2 * x) * kHD + d)
-                                           : 0.0;
-                    if (tid < grp * nsp) {
-                        const int h = tid / nsp, k = tid - h * nsp;
-                        const double2 ms = __ldcg(reinterpret_cast<const double2 *>(a.part_ms + ((pu + k) * grp + h) * 2));
-                        as.s[h][k] = (float)ms.x;
-                        as.e[k][h] = ms.y;
-                    }
-                    named_sync(3, kMNC);
-#pragma unroll
-                    for (int x = 0; x < 2; ++x) {
-                        const int h = kh + 2 * x;
-                        if (h < grp) {
-                            float M = as.s[h][0];
-                            for (int k = 1; k < nsp; ++k) M = fmaxf(M, as.s[h][k]);
-                            double acc = 0.0, S = 0.0;
-#pragma unroll
-                            for (int k = 0; k < kCombineFast; ++k)
-                                if (k < nsp) {
-                                    const double w = (double)det_expf(__fsub_rn(as.s[h][k], M));
-                                    acc += ov[x][k] * w;
-                                    S += as.e[k][h] * w;
-                                }
-                            ll_store(a.out, (size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d, (float)(acc / S),
-                                     out_tag);
-                        }
-                    }
-                    if (tid == 0) a.counters[t * a.Hkv + g] = 0;
-                    named_sync(3, kMNC);
-                    continue;
-                }
-                const int nch = (nsp + kAttnSplit - 1) / kAttnSplit;
-                auto stage = [&](int kb, int kn) {
-                    for (int p = tid; p < grp * kn; p += kMNC) {
-                        const int h = p / kn, k = p - h * kn;
-                        const double2 ms = __ldcg(reinterpret_cast<const double2 *>(a.part_ms + ((pu + kb + k) * grp + h) * 2));
-                        as.s[h][k] = (float)ms.x;
-                        as.e[k][h] = ms.y;
-                    }
-                    named_sync(3, kMNC);
-                };
-                for (int c = 0; c < nch; ++c) {
-                    const int kb = c * kAttnSplit, kn = min(kAttnSplit, nsp - kb);
-                    stage(kb, kn);
-                    if (warp < grp) {
-                        float mx = fmaxf(lane < kn ? as.s[warp][lane] : -INFINITY,
-                                         lane + 32 < kn ? as.s[warp][lane + 32] : -INFINITY);
-                        mx = warp_max(mx);
-                        if (lane == 0) as.m[warp] = c == 0 ? mx : fmaxf(as.m[warp], mx);
-                    }
-                    named_sync(3, kMNC);
-                }
-                double acc[2] = {0.0, 0.0}, S[2] = {0.0, 0.0};
-                for (int c = 0; c < nch; ++c) {
-                    const int kb = c * kAttnSplit, kn = min(kAttnSplit, nsp - kb);
-                    if (nch > 1) stage(kb, kn);  // one chunk: still staged from the max pass
-                    for (int p = tid; p < grp * kn; p += kMNC) {
-                        const int h = p / kn, k = p - h * kn;
-                        as.o[h][k] = (double)det_expf(__fsub_rn(as.s[h][k], as.m[h]));
-                    }
-                    named_sync(3, kMNC);
-#pragma unroll
-                    for (int x = 0; x < 2; ++x) {
-                        const int h = kh + 2 * x;
-                        if (h < grp) {
-                            const double *src = a.part + ((pu + kb) * grp + h) * kHD + d;
-#pragma unroll 8
-                            for (int k = 0; k < kn; ++k) {
-                                acc[x] += __ldcg(src + (size_t)k * grp * kHD) * as.o[h][k];
-                                S[x] += as.e[k][h] * as.o[h][k];
-                            }
-                        }
-                    }
-                    named_sync(3, kMNC);
-                }
-#pragma unroll
-                for (int x = 0; x < 2; ++x) {
-                    const int h = kh + 2 * x;
-                    if (h < grp)
-                        ll_store(a.out, (size_t)t * a.H * kHD + (size_t)(g * grp + h) * kHD + d, (float)(acc[x] / S[x]),
-                                 out_tag);
-                }
-                if (tid == 0) a.counters[t * a.Hkv + g] = 0;
-            }
-        }
-        named_sync(3, kMNC);  // the unit's shared buffers are free for the next unit
+    for (int u = cta; u < pl.units; u += G) {
+        const AttnUnit un = attn_unit_of(a, pl, u);
+        const AttnPre pp = u == cta ? pre : attn_preload(a, u, G);
+        if (pl.nh == 1)
+            attn_unit<1>(a, pl, un, pp, u == cta, sm, cta, err, tr, apar, in_tag, out_tag);
+        else if (pl.nh == 2)
+            attn_unit<2>(a, pl, un, pp, u == cta, sm, cta, err, tr, apar, in_tag, out_tag);
+        else
+            attn_unit<kAG>(a, pl, un, pp, u == cta, sm, cta, err, tr, apar, in_tag, out_tag);
     }
 }
+
 
 // Every load a thread needs is issued before any is used (token id, the
 // codebook ids, then all rows' quants and scales), so the op costs about three
@@ -800,7 +876,7 @@ __global__ void __launch_bounds__(kMThreads, 1)
         F8 nw[kMPC];
         AttnPre ap;
         if (kind == MK_GEMV) tg_norm_preload<kMPC, kMNC>(ops[i].g, nw);
-        if (kind == MK_ATTN) ap = attn_preload(ops[i].a, cta);
+        if (kind == MK_ATTN) ap = attn_preload(ops[i].a, cta, G);
         // no grid barrier: each op's readers poll the tags of the words they read
         named_sync(1, kMNC);  // the previous op's shared buffers are free
         if (threadIdx.x == 0) *reinterpret_cast<volatile int *>(&sm.cur_op) = i;

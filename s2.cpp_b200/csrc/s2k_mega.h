@@ -25,6 +25,11 @@ enum MegaKind : int {
 
 using MegaGemv = TGemv;  // s2k_tgemv.cuh
 
+// Most query heads per kv head the persistent kernel's attention takes; its
+// split arrival counters are kept per (layer, token, kv head, head block of
+// up to this many blocks).
+constexpr int kAttnMaxGroup = 4;
+
 // Activations the persistent kernel passes between ops (x, h, qkv, attention
 // output, SwiGLU output) are tagged 8-byte words (s2k_tgemv.cuh ll_pack);
 // the *_tag fields hold the index, within the segment, of the op that writes

@@ -167,6 +167,12 @@ struct s2k_seq {
     std::vector<int> seg_start, seg_len, seg_mt;
     bool use_mega = false;
     bool mega_q8 = false;  // every GEMV op of the frame program is Q8_0
+    // single-token s2k_eval on the persistent kernel (its own token row and counters)
+    MegaOp *eval_ops = nullptr;
+    MegaCtl *eval_ctl = nullptr;
+    int *eval_tokens = nullptr;
+    int eval_len = 0, eval_gen = -1;
+    bool eval_ok = false, eval_q8 = false;
     KvPaged kv() const {
         KvPaged p;
         p.k = k;
