@@ -213,6 +213,18 @@ S2K_API s2k_status s2k_generate(s2k_model *m, s2k_seq *s, const int32_t *prompt,
                                 const s2k_gen_params *gp, int32_t *codes_out,
                                 int32_t *n_frames_out, s2k_frame_callback on_frame, void *user);
 
+/* The [Metrics] line generate() prints when verbose (src/s2_generate.cpp:185-199):
+ * device time of the last s2k_generate / s2k_generate_device call on this
+ * sequence (CUDA events on the model stream) -- prompt prefill, frame loop,
+ * their sum and the loop time per frame -- with its frame and prompt counts.
+ * The same calls also mark "s2k generate: prefill" and "s2k generate: frame
+ * loop" as NVTX ranges for a profiler's timeline. */
+typedef struct s2k_gen_metrics {
+    double prefill_ms, loop_ms, total_ms, ms_per_frame;
+    int32_t n_frames, prompt_tokens;
+} s2k_gen_metrics;
+S2K_API s2k_status s2k_seq_last_metrics(const s2k_seq *s, s2k_gen_metrics *out);
+
 /* Same as s2k_generate with device-resident buffers: d_prompt_tm is the
  * token-major [cols][num_codebooks+1] prompt and d_codes_out the
  * [num_codebooks][max_new_tokens] (uncompacted) codes, both device pointers. */

@@ -8,6 +8,8 @@
 #include "s2k_mega.h"
 #include "s2k_model.h"
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <algorithm>
 #include <atomic>
 #include <cmath>
@@ -1405,11 +1407,25 @@ static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_promp
     hs->n_frames = 0;
     hs->done = 0;
     s->n_past = 0;
+    // the reference's [Metrics] split (src/s2_generate.cpp:185-199), timed on the device
+    cudaEvent_t tev[3];
+    for (int i = 0; i < 3; ++i) CU(cudaEventCreate(&tev[i]));
+    struct EventGuard {
+        cudaEvent_t *e;
+        ~EventGuard() {
+            for (int i = 0; i < 3; ++i) cudaEventDestroy(e[i]);
+        }
+    } tev_guard{tev};
+    nvtxRangePushA("s2k generate: prefill");
     // prefill (generate(): prefill_fast of the whole prompt, src/s2_generate.cpp:51)
+    CU(cudaEventRecord(tev[0], m->stream));
     CU(enqueue_slow(m, s, cols, d_prompt_tm, nullptr));
     CU(launch_sample_main(m->logits, s->dev, m->d_err, m->stream));
+    CU(cudaEventRecord(tev[1], m->stream));
+    nvtxRangePop();
     rc = ensure_frame_graph(m, s);
     if (rc) return rc;
+    nvtxRangePushA("s2k generate: frame loop");
     constexpr int kLookahead = 4;
     static_assert(kLookahead < kFrameRing, "frames in flight must not overwrite ring slots the host has not read");
     cudaEvent_t ev[kLookahead];
@@ -1466,12 +1482,26 @@ static s2k_status generate_core(s2k_model *m, s2k_seq *s, const int32_t *d_promp
             break;
         }
     }
+    cudaEventRecord(tev[2], m->stream);
     cudaError_t e = cudaStreamSynchronize(m->stream);
+    nvtxRangePop();
     for (int i = 0; i < kLookahead; ++i) cudaEventDestroy(ev[i]);
     if (out_rc) return out_rc;
     if (e != cudaSuccess) return fail(S2K_ERR_CUDA, "generate: %s", cudaGetErrorString(e));
     rc = check_err_word(m);
     if (rc) return rc;
+    {
+        float pre = 0.f, loop = 0.f;
+        cudaEventElapsedTime(&pre, tev[0], tev[1]);
+        cudaEventElapsedTime(&loop, tev[1], tev[2]);
+        s2k_gen_metrics &gm = s->metrics;
+        gm.prefill_ms = pre;
+        gm.loop_ms = loop;
+        gm.total_ms = (double)pre + (double)loop;
+        gm.n_frames = aborted ? delivered : hs->n_frames;
+        gm.prompt_tokens = cols;
+        gm.ms_per_frame = gm.n_frames > 0 ? gm.loop_ms / gm.n_frames : 0.0;
+    }
     if (aborted) {
         // the reference breaks before step() of the aborted frame
         const int n_past = cols + delivered - 1;
@@ -1882,5 +1912,11 @@ S2K_API s2k_status s2k_device_mem_info(int32_t device, size_t *free_bytes, size_
     if (!free_bytes || !total_bytes) return fail(S2K_ERR_ARG, "NULL argument");
     if (cuda_set(device)) return fail(S2K_ERR_CUDA, "cudaSetDevice(%d) failed", device);
     CU(cudaMemGetInfo(free_bytes, total_bytes));
+    return S2K_OK;
+}
+
+S2K_API s2k_status s2k_seq_last_metrics(const s2k_seq *s, s2k_gen_metrics *out) {
+    if (!s || !out) return fail(S2K_ERR_ARG, "NULL argument");
+    *out = s->metrics;
     return S2K_OK;
 }

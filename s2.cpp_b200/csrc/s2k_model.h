@@ -173,6 +173,7 @@ struct s2k_seq {
     int *eval_tokens = nullptr;
     int eval_len = 0, eval_gen = -1;
     bool eval_ok = false, eval_q8 = false;
+    s2k_gen_metrics metrics{};  // of the last s2k_generate / s2k_generate_device
     KvPaged kv() const {
         KvPaged p;
         p.k = k;

@@ -40,7 +40,7 @@ EXPORTED = [
     "s2k_sched_get_stats", "s2k_sched_poll_status", "s2k_sched_cancel", "s2k_sched_set_frame_callback",
     "s2k_seq_load_kv", "s2k_get_rows", "s2k_model_set_wait_limit", "s2k_debug_wait_probe", "s2k_debug_fail_alloc",
     "s2k_model_device_bytes", "s2k_device_mem_info", "s2k_gguf_read_hparams", "s2k_gguf_tensor_info",
-    "s2k_model_load_gguf", "s2k_build_prompt",
+    "s2k_model_load_gguf", "s2k_build_prompt", "s2k_seq_last_metrics",
 ]
 
 REQ_WAITING, REQ_LIVE, REQ_DONE, REQ_FAILED, REQ_CANCELLED = 0, 1, 2, 3, 4  # S2K_REQ_*
@@ -82,6 +82,11 @@ class _SchedStats(ctypes.Structure):
                 ("max_live", ctypes.c_int32),
                 ("free_pages", ctypes.c_int32), ("pool_pages", ctypes.c_int32), ("pad_", ctypes.c_int32),
                 ("cancelled", ctypes.c_int64), ("failed", ctypes.c_int64)]
+
+
+class _GenMetrics(ctypes.Structure):
+    _fields_ = [("prefill_ms", ctypes.c_double), ("loop_ms", ctypes.c_double), ("total_ms", ctypes.c_double),
+                ("ms_per_frame", ctypes.c_double), ("n_frames", ctypes.c_int32), ("prompt_tokens", ctypes.c_int32)]
 
 
 FRAME_CB = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32,
@@ -160,6 +165,7 @@ def lib() -> ctypes.CDLL:
                                   ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
                                   ctypes.POINTER(i32)], i32),
         "s2k_model_load_gguf": ([i32, ctypes.c_char_p, ctypes.POINTER(vp)], i32),
+        "s2k_seq_last_metrics": ([vp, ctypes.POINTER(_GenMetrics)], i32),
         "s2k_build_prompt": ([ENCODE_FN, vp, ctypes.c_char_p, ctypes.c_char_p, vp, i32, i32, i32, i32, i32, vp,
                               ctypes.c_size_t, ctypes.POINTER(i32), ctypes.POINTER(i32)], i32),
     }
@@ -428,6 +434,12 @@ class SlowARModel:
                                   ctypes.byref(nf), cb, None))
         n = nf.value
         return codes[: ncb * n].reshape(ncb, n)
+
+    def last_metrics(self) -> dict:
+        """Device-timed prefill / frame-loop split of the last generate (s2k_seq_last_metrics)."""
+        gm = _GenMetrics()
+        _check(lib().s2k_seq_last_metrics(self._seq, ctypes.byref(gm)))
+        return {name: getattr(gm, name) for name, _ in _GenMetrics._fields_}
 
     def _max_seq(self) -> int:
         return getattr(self, "_max_seq_len", 0)

@@ -143,3 +143,17 @@ def test_sched_frame_callback_and_cancel(small_gpu, small_oracle, small_model_da
         for idx, c in got[rid]:
             assert np.array_equal(c, want[:, idx])
     sc.close()
+
+
+def test_generate_metrics(small_gpu, small_model_data):
+    """The [Metrics] split of generate (src/s2_generate.cpp:185-199), device-timed."""
+    hp, _ = small_model_data
+    p = synthetic.text_prompt(hp, 9, seed=9)
+    out = small_gpu.generate(p, 40, temperature=0.0, seed=1, im_end_id=-1)
+    gm = small_gpu.last_metrics()
+    assert gm["n_frames"] == out.shape[1] == 40 and gm["prompt_tokens"] == 9
+    assert gm["prefill_ms"] > 0 and gm["loop_ms"] > 0
+    assert abs(gm["total_ms"] - gm["prefill_ms"] - gm["loop_ms"]) < 1e-6
+    assert abs(gm["ms_per_frame"] * 40 - gm["loop_ms"]) < 1e-6
+    small_gpu.generate(p, 30, temperature=0.0, seed=1, im_end_id=-1, on_frame=lambda c, i, t: i < 2)
+    assert small_gpu.last_metrics()["n_frames"] == 3
