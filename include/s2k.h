@@ -153,10 +153,12 @@ S2K_API s2k_status s2k_gguf_tensor_info(const char *path, int32_t index, char *n
 S2K_API s2k_status s2k_model_load_gguf(int32_t device, const char *path, s2k_model **out);
 
 /* Checks every required tensor is bound (the req_t checks of
- * src/s2_model.cpp:366-428) and prepares the decode kernels.  For Q4_K /
- * Q6_K matrices of the Slow stack it also builds the int8 copies the
- * tensor-core prefill reads: about one extra byte of device memory per
- * weight (two per Q6_K weight); s2k_model_weight_bytes does not count them. */
+ * src/s2_model.cpp:366-428) and prepares the decode kernels.  For models with
+ * Q4_K / Q6_K matrices in the Slow stack it also reserves two layer slots for
+ * the int8 copies the tensor-core prefill reads (rebuilt one layer ahead
+ * during each prefill of 64+ tokens): about two layers' weights in extra
+ * device memory (twice that for Q6_K); s2k_model_weight_bytes does not count
+ * them. */
 S2K_API s2k_status s2k_model_finalize(s2k_model *m);
 S2K_API void s2k_model_free(s2k_model *m);
 /* SlowARModel::hparams (include/s2_model.h:130) */
@@ -268,9 +270,9 @@ S2K_API s2k_status s2k_sample(s2k_model *m, const float *logits, int32_t n, floa
  * every device that loads the library holds until exit.
  * n > S2K_SAMPLE_NOALLOC_MAX_N is rejected with S2K_ERR_ARG.
  * The first call on a device (and the first after a device reset) looks up
- * that array's address with that device current.  Every call copies the
- * logits in, samples and synchronizes the model stream to read the token, so
- * it cannot be called while a stream is being captured.  The error word is
+ * that array's address with that device current (set-up); make that first
+ * call before any stream capture.  Every call copies the logits in, samples
+ * and synchronizes the model stream to read the token.  The error word is
  * cleared on the model stream at the start of every call.  The scratch is
  * shared by every model on the device: calls that overlap in time (other
  * threads, other models on the same device) race on it and must be

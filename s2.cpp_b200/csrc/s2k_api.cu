@@ -228,6 +228,20 @@ cudaError_t stack_gemm(s2k_model *m, Work &w, const GemvArgs &g, bool prefill, b
     return launch_gemv(g, m->num_sms, m->stream);
 }
 
+// Builds layer il's int8 prefill copies (its K-quant matrices) into layer
+// slot il % 2.  A plain launch: it starts once every earlier kernel of the
+// stream has finished, so layer il - 2's GEMMs, the slot's last readers, are
+// done; layer il's GEMMs come a whole layer later.
+cudaError_t kq_layer_build(s2k_model *m, int il) {
+    Layer &L = m->layers[(size_t)il];
+    for (DevMat *dm : {&L.wqkv, &L.wo, &L.w13, &L.w2}) {
+        if (!dm->pf) continue;
+        cudaError_t e = launch_build_kq_prefill(*dm, m->stream);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 cudaError_t run_stack(s2k_model *m, const StackCall &c) {
     const s2k_hparams &hp = m->hp;
     Work &w = c.w ? *c.w : (c.fast ? m->fw : m->sw);
@@ -240,8 +254,13 @@ cudaError_t run_stack(s2k_model *m, const StackCall &c) {
     const int dim = w.dim;
     cudaStream_t st = m->stream;
     cudaError_t e;
+    // K-quant matrices on the tensor cores read int8 copies built here, one
+    // layer ahead, into two alternating layer slots (kq_layer_build)
+    const bool kq_build = !c.fast && c.mma && m->kq_slot_bytes > 0 && c.T >= kPrefillKqMinT;
+    if (kq_build && (e = kq_layer_build(m, 0))) return e;
     for (size_t il = 0; il < layers.size(); ++il) {
         const Layer &L = layers[il];
+        if (kq_build && il + 1 < layers.size() && (e = kq_layer_build(m, (int)il + 1))) return e;
         GemvArgs g;
         g.w = &L.wqkv;
         g.x = w.x;
@@ -749,17 +768,38 @@ S2K_API s2k_status s2k_model_finalize(s2k_model *m) {
     m->prefill_f16 = m->prefill_mma && prefill_f16_setup() == cudaSuccess;
     cudaGetLastError();  // a device without the tensor-map entry point keeps the GEMV path
     if (m->prefill_mma) {
-        // int8 copies of the Slow stack's K-quant matrices for the tensor-core prefill
-        for (Layer &L : m->layers)
+        // int8 copies of the Slow stack's K-quant matrices for the tensor-core
+        // prefill: two layer slots, layer il's copies in slot il % 2, built
+        // by run_stack one layer ahead of their GEMMs (kq_layer_build)
+        auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+        size_t slot = 0;
+        for (Layer &L : m->layers) {
+            size_t per = 0;
             for (DevMat *dm : {&L.wqkv, &L.wo, &L.w13, &L.w2}) {
                 size_t side = 0;
                 const size_t nb = kq_prefill_bytes(*dm, &side);
-                if (nb == 0 || dm->pf) continue;
-                CU(m->alloc(&dm->pf, nb));
-                CU(m->alloc(&dm->pf_side, side));
-                CU(launch_build_kq_prefill(*dm, m->stream));
+                if (nb) per += al(nb) + al(side);
             }
-        CU(cudaStreamSynchronize(m->stream));
+            slot = std::max(slot, per);
+        }
+        if (slot > 0) {
+            CU(m->alloc(&m->kq_slots[0], slot));
+            CU(m->alloc(&m->kq_slots[1], slot));
+            for (size_t il = 0; il < m->layers.size(); ++il) {
+                uint8_t *base = m->kq_slots[il % 2];
+                size_t off = 0;
+                for (DevMat *dm : {&m->layers[il].wqkv, &m->layers[il].wo, &m->layers[il].w13, &m->layers[il].w2}) {
+                    size_t side = 0;
+                    const size_t nb = kq_prefill_bytes(*dm, &side);
+                    if (nb == 0) continue;
+                    dm->pf = base + off;
+                    off += al(nb);
+                    dm->pf_side = base + off;
+                    off += al(side);
+                }
+            }
+            m->kq_slot_bytes = slot;
+        }
     }
     if (m->staging) {
         m->release(m->staging);

@@ -65,6 +65,9 @@ struct Work {
 #define S2K_PREFILL_MIN_T 8
 #endif
 constexpr int kPrefillMinT = S2K_PREFILL_MIN_T;
+// Tokens per call from which K-quant GEMMs run on the tensor cores (their
+// 64-token tiles; s2k_prefill.cu prefill_ok).
+constexpr int kPrefillKqMinT = 64;
 // Most tokens of one persistent-kernel call (the first Fast-AR pass: hidden + code 0).
 constexpr int kMegaTokens = 2;
 
@@ -89,6 +92,9 @@ struct s2k_model {
     bool finalized = false;
     bool prefill_mma = false;  // the tensor-core prefill path could be set up on this device
     bool prefill_f16 = false;  // the fp16 tensor-core prefill GEMM (F16 models) could be set up
+    // K-quant tensor-core prefill: two layer slots of int8 copies (layer il in slot il % 2)
+    uint8_t *kq_slots[2] = {nullptr, nullptr};
+    size_t kq_slot_bytes = 0;
     int *d_err = nullptr;
     unsigned *d_epoch = nullptr;  // tag epoch of the persistent kernel's activations (starts at 1)
     // staging for uploads

@@ -563,7 +563,9 @@ __global__ void kq_build_kernel(const uint8_t *__restrict__ src, int wtype, int 
     const int kte = be / 16, bl = be % 16;
     const int rl = row % kTR;
     uint8_t *tile = dst + ((size_t)(row / kTR) * NKTe + kte) * kTileBytes;
-    int8_t q[32];
+    // the sub-block's 32 (Q6_K: 16, then 16 zeros) int8 values, four per word,
+    // from 16-byte loads of the source planes
+    uint32_t w[8];
     uint16_t scm;
     __half2 dd = __floats2half2_rn(0.f, 0.f);
     bool first = false;
@@ -572,9 +574,12 @@ __global__ void kq_build_kernel(const uint8_t *__restrict__ src, int wtype, int 
         const int sbg = be / 8, j = be % 8;  // super-block of the row, sub-block
         const uint8_t *t = src + ((size_t)(row / kTR) * NKTs + sbg / 2) * kTileBytesQ4K;
         const int rb2 = rl * 2 + (sbg & 1);
-        const uint8_t *qs = t + rb2 * 128 + 32 * (j >> 1);
+        const uint4 *qs = reinterpret_cast<const uint4 *>(t + rb2 * 128 + 32 * (j >> 1));
+        const uint4 a0 = qs[0], a1 = qs[1];
+        const uint32_t src_w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const int sh = (j & 1) ? 4 : 0;  // odd sub-blocks: the high nibbles
 #pragma unroll
-        for (int l = 0; l < 32; ++l) q[l] = (int8_t)((j & 1) ? (qs[l] >> 4) : (qs[l] & 0xF));
+        for (int k = 0; k < 8; ++k) w[k] = (src_w[k] >> sh) & 0x0F0F0F0Fu;
         const uint8_t *hd = t + kQ4kHdr + rb2 * 16;
         int sc, mn;
         q4k_scale_min(j, hd + 4, &sc, &mn);
@@ -587,26 +592,25 @@ __global__ void kq_build_kernel(const uint8_t *__restrict__ src, int wtype, int 
         const int sbg = kte, j = bl;  // one super-block per copy K-tile, 16-value sub-block j
         const uint8_t *t = src + ((size_t)(row / kTR) * NKTs + sbg / 2) * kTileBytesQ6K;
         const int rb2 = rl * 2 + (sbg & 1);
+        // values 16j .. 16j+15 of the super-block: half h, quarter k, lanes l0 .. l0+15
+        const int h = j >> 3, k = (j >> 1) & 3, l0 = 16 * (j & 1);
+        const uint4 ql = *reinterpret_cast<const uint4 *>(t + rb2 * 128 + 64 * h + l0 + ((k & 1) << 5));
+        const uint4 qh = *reinterpret_cast<const uint4 *>(t + kQ6kQh + rb2 * 64 + 32 * h + l0);
+        const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w}, hw[4] = {qh.x, qh.y, qh.z, qh.w};
 #pragma unroll
-        for (int l = 0; l < 16; ++l) {
-            const int cc = 16 * j + l, h = cc >> 7, k = (cc >> 5) & 3, ll = cc & 31;
-            const uint8_t ql = t[rb2 * 128 + 64 * h + ll + ((k & 1) << 5)];
-            const uint8_t qh = t[kQ6kQh + rb2 * 64 + 32 * h + ll];
-            q[l] = (int8_t)((((k & 2) ? (ql >> 4) : (ql & 0xF)) | (((qh >> (2 * k)) & 3) << 4)) - 32);
+        for (int x = 0; x < 4; ++x) {
+            const uint32_t lo = ((k & 2) ? (lw[x] >> 4) : lw[x]) & 0x0F0F0F0Fu;
+            const uint32_t hi = ((hw[x] >> (2 * k)) & 0x03030303u) << 4;
+            w[x] = __vsub4(lo | hi, 0x20202020u);  // q - 32 per byte
         }
 #pragma unroll
-        for (int l = 16; l < 32; ++l) q[l] = 0;
+        for (int x = 4; x < 8; ++x) w[x] = 0;
         scm = (uint16_t)t[kQ6kSc + rb2 * 16 + j];
         first = j == 0;
         slot = 0;
         dd = __halves2half2(__ushort_as_half(*reinterpret_cast<const unsigned short *>(t + kQ6kD + rb2 * 2)),
                             __float2half_rn(0.f));
     }
-    uint32_t w[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-        w[k] = (uint32_t)(uint8_t)q[4 * k] | ((uint32_t)(uint8_t)q[4 * k + 1] << 8) |
-               ((uint32_t)(uint8_t)q[4 * k + 2] << 16) | ((uint32_t)(uint8_t)q[4 * k + 3] << 24);
     uint4 *qd = reinterpret_cast<uint4 *>(tile + rl * kTK + bl * 32);
     qd[0] = make_uint4(w[0], w[1], w[2], w[3]);
     qd[1] = make_uint4(w[4], w[5], w[6], w[7]);

@@ -71,7 +71,9 @@ def cmd_prefill(a) -> None:
             ms = e0.elapsed_time(e1)
             best = ms if best is None else min(best, ms)
         print(json.dumps(dict(preset=a.preset, quant=a.quant, tokens=T, ms=round(best, 3),
-                              gemm_tflops_equiv=round(2 * params * T / (best / 1e3) / 1e12, 1))), flush=True)
+                              gemm_tflops_equiv=round(2 * params * T / (best / 1e3) / 1e12, 1),
+                              weight_gb=round(m.weight_bytes() / 1e9, 3),
+                              device_gb=round(m.device_bytes() / 1e9, 3))), flush=True)
     m.close()
 
 

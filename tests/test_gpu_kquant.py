@@ -1,7 +1,7 @@
 """GPU parity for K-quant weights (the mixed Q4_K_M scheme: Q4_K attention /
 FFN-up / embedding tables, Q6_K FFN-down and output projections) against the
-CPU oracle, through the C ABI.  Same bars as the Q8_0 parity tests: logits
-within 1e-2 * std(logits), identical greedy codes."""
+CPU oracle, through the C ABI.  Same bars as the Q8_0 parity tests:
+bit-exact logits, identical greedy codes."""
 from __future__ import annotations
 
 import numpy as np
@@ -158,3 +158,46 @@ def test_kquant_batch_of_64_matches_single_sequence(kq_pair):
     assert st["max_live"] == 64
     for i, (p, f, kw) in enumerate(reqs):
         assert np.array_equal(got[i], m.generate(p, f, **kw)), f"request {i}"
+
+
+def test_kquant_prefill_layer_slots():
+    """The tensor-core K-quant prefill reads int8 copies that are built one
+    layer ahead into two alternating layer slots: a 6-layer model (every slot
+    rebuilt three times per pass) against the oracle at 64 and 150 tokens,
+    then a batched frame of 64 sequences; the copies take two layers of
+    device memory, not one per layer."""
+    import dataclasses
+    hp = dataclasses.replace(synthetic.preset("small"), block_count=6)
+    tensors = list(synthetic.make_model(hp, seed=61, quant="q4_k_m", norm_std=0.1))
+    m = s2k.SlowARModel(hp)
+    om = oracle.OracleModel(hp)
+    try:
+        m.load_tensors(tensors)
+        om.load_tensors(tensors)
+        layer_copy = sum(spec.ne0 * spec.ne1 * (2 if spec.type == synthetic.GGML_Q6_K else 1)
+                         for spec, _ in tensors if spec.name.startswith("layers.0.") and spec.ne1 > 1)
+        # weights + the two layer slots (plus workspaces), well under one copy per layer
+        assert m.device_bytes() - m.weight_bytes() < 4 * layer_copy + (64 << 20)
+        for T in (64, 150):
+            p = synthetic.text_prompt(hp, T, seed=T + 1)
+            m.init_kv_cache(T + 4)
+            om.init_kv_cache(T + 4)
+            hg, lg = m.prefill_fast(p.T.reshape(-1), T)
+            ho, lo = om.eval(p.T.reshape(-1), T)
+            assert_exact(lg, lo, f"6-layer kquant prefill logits T={T}")
+            tok = np.zeros(hp.num_codebooks + 1, np.int32)
+            tok[0] = 4
+            _, lg = m.step(tok)
+            _, lo = om.eval(tok, 1)
+            assert_exact(lg, lo, f"6-layer kquant step after T={T}")
+        sc = s2k.BatchScheduler(m, max_batch=64, max_seq_len=32)
+        prompts = [synthetic.text_prompt(hp, 6 + i % 5, seed=200 + i) for i in range(64)]
+        ids = [sc.submit(pp, 3, temperature=0.0, seed=1, seq_id=i, im_end_id=-1) for i, pp in enumerate(prompts)]
+        sc.run()
+        for i in (0, 17, 63):
+            want = om.generate(prompts[i], 3, temperature=0.0, seed=1, seq_id=i, im_end_id=-1)
+            assert np.array_equal(sc.result(ids[i]), want), i
+        sc.close()
+    finally:
+        m.close()
+        om.close()
