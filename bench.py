@@ -55,11 +55,11 @@ WORKLOAD = ("dual-AR frame loop, S2 Pro shape (36+4 layers, d2560, GQA 32/8, ff 
 # DRAM traffic / algorithmic bytes of the persistent kernel, measured with
 # ncu (dram__bytes_read.sum + dram__bytes_write.sum) on the same kernel with
 # 2 Slow + 1 Fast-AR layers at full widths (bench.py --preset mid, launches
-# 18 and 19): Slow segment 647.89 MB for 638.36 MB, Fast-AR segment 122.34 MB
+# 18 and 19): Slow segment 645.58 MB for 638.36 MB, Fast-AR segment 121.95 MB
 # for 118.37 MB.  Traffic grows with the bytes streamed, so full-size
 # launches are scaled by these ratios.
-TRAFFIC_RATIO_SLOW = 647.89 / 638.36
-TRAFFIC_RATIO_FAST = 122.34 / 118.37
+TRAFFIC_RATIO_SLOW = 645.58 / 638.36
+TRAFFIC_RATIO_FAST = 121.95 / 118.37
 
 
 def peaks() -> dict:
