@@ -61,3 +61,46 @@ def test_two_rank_sharding_gloo():
 def test_single_process_identity():
     assert shard.max_over_ranks(3.5) == 3.5
     assert shard.aggregate_rate(1, 5, 200, 1000.0) == pytest.approx(1000.0)
+
+
+def _leaver(rank: int, world: int, port: int, q) -> None:
+    """Rank 1 takes part in step 1 and then leaves between steps (exits
+    without joining step 2's barrier); rank 0 must learn of it from the
+    process group's short timeout instead of waiting for good."""
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    shard.init("gloo", rank, timeout_s=3)
+    dist.barrier()
+    shard.max_over_ranks(1.0, "cpu")  # step 1: both ranks
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()  # the message is out before the process goes
+        os._exit(0)  # no destroy_process_group: the rank is simply gone
+    t0 = time.monotonic()
+    try:
+        dist.barrier()  # step 2: its peer never comes
+        q.put((rank, "no error"))
+    except Exception as e:  # the timeout (or the peer's closed connection) ends the wait
+        q.put((rank, f"error after {time.monotonic() - t0:.1f} s: {type(e).__name__}"))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_rank_leaving_between_steps_is_detected():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    res = dict(q.get(timeout=10) for _ in range(world))
+    assert res[1] == "left"
+    assert res[0].startswith("error after"), res[0]
+    assert float(res[0].split()[2]) < 30.0
