@@ -449,6 +449,98 @@ S2K_API s2k_status s2k_sched_get_stats(const s2k_sched *sc, s2k_sched_stats *out
 /* Counts kernel launches issued by the library since the last reset. */
 S2K_API uint64_t s2k_launch_count(int32_t reset);
 
+/* ---- codec decode: codes -> audio (s2::AudioCodec, include/s2_codec.h) ----
+ *
+ * The DAC-style decoder the reference runs after generation: RVQ lookup and
+ * projection, the windowed post-module transformer, ConvTranspose + ConvNeXt
+ * upsampling, and the snake / residual-unit decoder
+ * (src/s2_codec.cpp:264-522, AudioCodec::decode :1297-1447).  Matrices are
+ * F16 as the reference's GGUF exports keep them; the arithmetic follows the
+ * reference's ggml graph (fp16-rounded operands for the F16 matrix products
+ * and the im2col convolutions, f32 for the transposed convolutions) with f32
+ * accumulation on the tensor cores, so audio agrees with the CPU oracle to a
+ * floating-point tolerance, not bit for bit. */
+
+/* The fish_speech.codec.* keys AudioCodec::load_shared reads
+ * (src/s2_codec.cpp:813-858); n_local_heads < 1 means n_head. */
+typedef struct s2k_codec_hparams {
+    int32_t sample_rate, hop_length;
+    int32_t latent_dim, decoder_dim;
+    int32_t n_decoder_rates, decoder_rates[8];
+    int32_t quantizer_input_dim, quantizer_codebook_dim;
+    int32_t quantizer_residual_codebooks, quantizer_residual_codebook_size, quantizer_semantic_codebook_size;
+    int32_t n_downsample, quantizer_downsample_factor[8];
+    int32_t rvq_window_size, rvq_block_size, rvq_n_layer, rvq_n_local_heads, rvq_head_dim, rvq_dim;
+    float rvq_rope_base, rvq_norm_eps;
+} s2k_codec_hparams;
+
+typedef struct s2k_codec s2k_codec;
+
+/* AudioCodec construction: s2k_codec_create + one upload per tensor (GGUF
+ * name, with or without the combined file's "c." prefix; F16 or F32; the
+ * bytes are copied) + s2k_codec_finalize, which builds the device layouts. */
+S2K_API s2k_status s2k_codec_create(int32_t device, const s2k_codec_hparams *hp, s2k_codec **out);
+S2K_API s2k_status s2k_codec_upload_tensor(s2k_codec *c, const char *name, int32_t ggml_type, const int64_t ne[4],
+                                           const void *data, size_t nbytes);
+S2K_API s2k_status s2k_codec_finalize(s2k_codec *c);
+/* AudioCodec::load (src/s2_codec.cpp:698-900): hyper-parameters and the
+ * codec tensors of a combined ("fish-speech", "c." names) or codec-only
+ * ("fish-speech-codec") GGUF. */
+S2K_API s2k_status s2k_codec_load_gguf(int32_t device, const char *path, s2k_codec **out);
+S2K_API void s2k_codec_free(s2k_codec *c);
+S2K_API s2k_status s2k_codec_get_hparams(const s2k_codec *c, s2k_codec_hparams *out);
+/* AudioCodec::samples_per_code_frame / streaming_history_frames / num_codebooks
+ * (include/s2_codec.h:40-45, src/s2_codec.cpp:858-874) */
+S2K_API int32_t s2k_codec_samples_per_frame(const s2k_codec *c);
+S2K_API int32_t s2k_codec_history_frames(const s2k_codec *c);
+S2K_API int32_t s2k_codec_num_codebooks(const s2k_codec *c);
+/* Frames before the first sample a window emits that the decoder stages
+ * (everything after the post-module transformer) must see for that sample to
+ * equal a decode of the whole window; derived from the kernel sizes,
+ * dilations and strides at finalize. */
+S2K_API int32_t s2k_codec_receptive_frames(const s2k_codec *c);
+
+/* AudioCodec::decode (src/s2_codec.cpp:1297-1447): codes [num_codebooks]
+ * [n_frames] cb-major (clamped into each codebook as sanitize_decode_codes
+ * does) -> n_frames * samples_per_frame samples in audio (capacity cap). */
+S2K_API s2k_status s2k_codec_decode(s2k_codec *c, const int32_t *codes, int32_t n_frames, float *audio, size_t cap,
+                                    int64_t *n_samples);
+/* One window of the windowed decode: the samples of frames
+ * [emit_begin, emit_end) of a decode of the n_frames-frame window, into
+ * audio.  Only what those samples depend on is computed: the transformer over
+ * frames [0, emit_end) (it is causal) and the decoder stages from
+ * emit_begin - receptive_frames on; the samples are those of the whole-window
+ * decode. */
+S2K_API s2k_status s2k_codec_decode_range(s2k_codec *c, const int32_t *codes, int32_t n_frames, int32_t emit_begin,
+                                          int32_t emit_end, float *audio, size_t cap, int64_t *n_samples);
+/* decode_codes_windowed (src/s2_pipeline.cpp:198-289), the offline
+ * synthesis decode: windows every stride_frames (<= 0: 16) frames with
+ * context_frames_override (< 0: s2k_codec_history_frames) frames of history;
+ * codes [num_codebooks][total_frames].  decode_ms: device time of the window
+ * decodes; decode_batches: windows decoded (either may be NULL). */
+S2K_API s2k_status s2k_codec_decode_windowed(s2k_codec *c, const int32_t *codes, int32_t total_frames,
+                                             int32_t num_codebooks, int32_t stride_frames,
+                                             int32_t context_frames_override, float *audio, size_t cap,
+                                             int64_t *n_samples, double *decode_ms, int32_t *decode_batches);
+
+/* Streaming decode (decode_window_and_emit and the on_frame trigger of
+ * Pipeline::synthesize_stream, src/s2_pipeline.cpp:1011-1115): frames are
+ * pushed one at a time as generation produces them; a window is decoded
+ * once stride_frames (<= 0: 4) frames arrived since the last decode, holding
+ * back holdback_frames (< 0: the context) frames, with context_frames
+ * (< 0: s2k_codec_history_frames) of history.  push / finish return the PCM
+ * the window released (possibly none). */
+typedef struct s2k_codec_stream s2k_codec_stream;
+S2K_API s2k_status s2k_codec_stream_create(s2k_codec *c, int32_t stride_frames, int32_t context_frames,
+                                           int32_t holdback_frames, s2k_codec_stream **out);
+S2K_API void s2k_codec_stream_free(s2k_codec_stream *s);
+/* frame_codes: [num_codebooks] codes of one frame (the on_frame payload) */
+S2K_API s2k_status s2k_codec_stream_push(s2k_codec_stream *s, const int32_t *frame_codes, float *pcm, size_t cap,
+                                         int64_t *n_pcm);
+S2K_API s2k_status s2k_codec_stream_finish(s2k_codec_stream *s, float *pcm, size_t cap, int64_t *n_pcm);
+/* PCM samples the next push / finish can release at most (capacity to give). */
+S2K_API int64_t s2k_codec_stream_max_release(const s2k_codec_stream *s);
+
 #ifdef __cplusplus
 }
 #endif

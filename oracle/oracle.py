@@ -20,7 +20,7 @@ _lib = None
 
 
 def build() -> str:
-    src = [os.path.join(HERE, f) for f in ("s2_oracle.c", "s2_oracle.h", "Makefile")]
+    src = [os.path.join(HERE, f) for f in ("s2_oracle.c", "s2_codec_oracle.c", "s2_oracle.h", "Makefile")]
     if not os.path.exists(LIB_PATH) or any(os.path.getmtime(s) > os.path.getmtime(LIB_PATH) for s in src):
         subprocess.run(["make", "-s", "-C", HERE], check=True)
     return LIB_PATH
@@ -49,6 +49,20 @@ class _GP(ctypes.Structure):
     _fields_ = [("max_new_tokens", ctypes.c_int32), ("temperature", ctypes.c_float), ("top_p", ctypes.c_float),
                 ("top_k", ctypes.c_int32), ("min_tokens_before_end", ctypes.c_int32), ("im_end_id", ctypes.c_int32),
                 ("seed", ctypes.c_uint64), ("seq_id", ctypes.c_uint32)]
+
+
+class _CodecHP(ctypes.Structure):
+    """so_codec_hparams (the same fields as s2k_codec_hparams)"""
+    _fields_ = [("sample_rate", ctypes.c_int32), ("hop_length", ctypes.c_int32), ("latent_dim", ctypes.c_int32),
+                ("decoder_dim", ctypes.c_int32), ("n_decoder_rates", ctypes.c_int32),
+                ("decoder_rates", ctypes.c_int32 * 8), ("quantizer_input_dim", ctypes.c_int32),
+                ("quantizer_codebook_dim", ctypes.c_int32), ("quantizer_residual_codebooks", ctypes.c_int32),
+                ("quantizer_residual_codebook_size", ctypes.c_int32),
+                ("quantizer_semantic_codebook_size", ctypes.c_int32), ("n_downsample", ctypes.c_int32),
+                ("quantizer_downsample_factor", ctypes.c_int32 * 8), ("rvq_window_size", ctypes.c_int32),
+                ("rvq_block_size", ctypes.c_int32), ("rvq_n_layer", ctypes.c_int32),
+                ("rvq_n_local_heads", ctypes.c_int32), ("rvq_head_dim", ctypes.c_int32), ("rvq_dim", ctypes.c_int32),
+                ("rvq_rope_base", ctypes.c_float), ("rvq_norm_eps", ctypes.c_float)]
 
 
 def lib() -> ctypes.CDLL:
@@ -83,6 +97,11 @@ def lib() -> ctypes.CDLL:
             "so_set_threads": ([ctypes.c_int], None),
             "so_generate_timed": ([vp, vp, i32, ctypes.POINTER(_GP), vp, ctypes.POINTER(i32),
                                    ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
+            "so_codec_create": ([ctypes.POINTER(_CodecHP)], vp),
+            "so_codec_free": ([vp], None),
+            "so_codec_set_tensor": ([vp, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(i64), vp], ctypes.c_int),
+            "so_codec_samples": ([vp, i32], i64),
+            "so_codec_decode": ([vp, vp, i32, vp, i64, ctypes.POINTER(i64)], ctypes.c_int),
         }
         for name, (a, r) in sig.items():
             f = getattr(L, name)
@@ -251,3 +270,142 @@ class OracleModel:
             self.close()
         except Exception:
             pass
+
+
+class CodecOracle:
+    """CPU restatement of s2::AudioCodec::decode (src/s2_codec.cpp:1297-1447)
+    and of its windowed callers (src/s2_pipeline.cpp:198-289, :1034-1115)."""
+
+    def __init__(self, ch):
+        h = _CodecHP()
+        for name, _ in _CodecHP._fields_:
+            if name in ("decoder_rates", "quantizer_downsample_factor"):
+                vals = list(getattr(ch, name))
+                arr = getattr(h, name)
+                for k, v in enumerate(vals):
+                    arr[k] = int(v)
+                setattr(h, "n_decoder_rates" if name == "decoder_rates" else "n_downsample", len(vals))
+            elif name not in ("n_decoder_rates", "n_downsample"):
+                setattr(h, name, getattr(ch, name))
+        self.ch = ch
+        self._c = lib().so_codec_create(ctypes.byref(h))
+
+    def set_tensor(self, name: str, arr: np.ndarray, ne) -> None:
+        arr = np.ascontiguousarray(arr)
+        t = 1 if arr.dtype == np.float16 else 0
+        ne4 = (ctypes.c_int64 * 4)(*[int(x) for x in (list(ne) + [1, 1, 1, 1])[:4]])
+        if lib().so_codec_set_tensor(self._c, name.encode(), t, ne4, arr.ctypes.data) != 0:
+            raise RuntimeError(f"codec oracle rejected {name}")
+
+    def load_tensors(self, tensors) -> None:
+        for spec, arr in tensors:
+            self.set_tensor(spec.name, arr, spec.ne)
+
+    def samples_per_frame(self) -> int:
+        return int(lib().so_codec_samples(self._c, 1))
+
+    def decode(self, codes: np.ndarray) -> np.ndarray:
+        codes = np.ascontiguousarray(codes, dtype=np.int32)
+        n = codes.shape[1]
+        cap = int(lib().so_codec_samples(self._c, n))
+        out = np.empty(cap, dtype=np.float32)
+        ns = ctypes.c_int64(0)
+        rc = lib().so_codec_decode(self._c, codes.ctypes.data, n, out.ctypes.data, cap, ctypes.byref(ns))
+        if rc != 0:
+            raise RuntimeError(f"codec oracle decode failed ({rc})")
+        return out[: ns.value]
+
+    def history_frames(self) -> int:
+        """streaming_history_frames (src/s2_codec.cpp:870-874)"""
+        h = ((max(0, self.ch.rvq_window_size - 1) + 16 + 7) // 8) * 8
+        return h if h > 0 else 160
+
+    def windows_offline(self, total: int, stride: int = 16, context: int = -1):
+        return codec_windows_offline(total, stride, context if context >= 0 else self.history_frames())
+
+    def decode_windowed(self, codes: np.ndarray, stride: int = 16, context: int = -1) -> np.ndarray:
+        spf = self.samples_per_frame()
+        parts = []
+        for start, wf, eb, ee in self.windows_offline(codes.shape[1], stride, context):
+            if ee > eb:
+                pcm = self.decode(codes[:, start:start + wf])
+                parts.append(pcm[eb * spf: ee * spf])
+        return np.concatenate(parts) if parts else np.zeros(0, np.float32)
+
+    def windows_stream(self, total: int, stride: int = 4, context: int = -1, holdback: int = -1):
+        ctx = context if context >= 0 else self.history_frames()
+        return codec_windows_stream(total, stride, ctx, holdback if holdback >= 0 else ctx)
+
+    def close(self) -> None:
+        if getattr(self, "_c", None):
+            lib().so_codec_free(self._c)
+            self._c = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def codec_windows_offline(total: int, stride: int, history: int):
+    """(start, frames, emit_begin, emit_end) of every window
+    decode_codes_windowed decodes (src/s2_pipeline.cpp:198-289)."""
+    stride = max(1, stride if stride > 0 else 16)
+    out, committed = [], 0
+
+    def window(avail, fin):
+        nonlocal committed
+        if avail <= 0 or avail <= committed:
+            return
+        stable = avail if fin else max(0, avail - history)
+        if stable <= committed and not fin:
+            return
+        start = max(0, committed - history)
+        wf = avail - start
+        if wf <= 0:
+            return
+        eb = max(0, committed - start)
+        ee = wf if fin else min(wf, max(0, stable - start))
+        out.append((start, wf, eb, ee))
+        committed = avail if fin else stable
+
+    avail = min(total, stride)
+    while avail < total:
+        window(avail, False)
+        avail += stride
+    window(total, True)
+    return out
+
+
+def codec_windows_stream(total: int, stride: int, context: int, holdback: int):
+    """Windows of the streaming path: on_frame after every frame, a window
+    once stride frames arrived since the last decode, then the final one
+    (src/s2_pipeline.cpp:1034-1115, :1136-1141); entries are
+    (frames seen, start, frames, emit_begin, emit_end)."""
+    stride = stride if stride > 0 else 4
+    out, committed, last = [], 0, 0
+
+    def window(tot, fin):
+        nonlocal committed, last
+        if tot <= 0 or tot <= committed:
+            return
+        stable = tot if fin else max(0, tot - holdback)
+        if stable <= committed and not fin:
+            return
+        start = max(0, committed - context)
+        wf = tot - start
+        if wf <= 0:
+            return
+        eb = max(0, committed - start)
+        ee = wf if fin else min(wf, max(0, stable - start))
+        out.append((tot, start, wf, eb, ee))
+        committed = tot if fin else stable
+        last = tot
+
+    for f in range(1, total + 1):
+        if f - last >= stride:
+            window(f, False)
+    if total > last or committed < total:
+        window(total, True)
+    return out

@@ -168,6 +168,27 @@ enum { SO_RNG_MAIN = 0, SO_RNG_RAS = 1, SO_RNG_FAST0 = 2 };
 
 void so_set_threads(int n);
 
+/* ---- codec decode (s2_codec_oracle.c): AudioCodec::decode, src/s2_codec.cpp:1297-1447 ---- */
+typedef struct so_codec_hparams {
+    int32_t sample_rate, hop_length;
+    int32_t latent_dim, decoder_dim;
+    int32_t n_decoder_rates, decoder_rates[8];
+    int32_t quantizer_input_dim, quantizer_codebook_dim;
+    int32_t quantizer_residual_codebooks, quantizer_residual_codebook_size, quantizer_semantic_codebook_size;
+    int32_t n_downsample, quantizer_downsample_factor[8];
+    int32_t rvq_window_size, rvq_block_size, rvq_n_layer, rvq_n_local_heads, rvq_head_dim, rvq_dim;
+    float rvq_rope_base, rvq_norm_eps;
+} so_codec_hparams;
+typedef struct so_codec so_codec;
+so_codec *so_codec_create(const so_codec_hparams *hp);
+void so_codec_free(so_codec *c);
+/* F32 or F16 tensor under its GGUF name (the "c." prefix is optional); copied */
+int so_codec_set_tensor(so_codec *c, const char *name, int type, const int64_t ne[4], const void *data);
+int64_t so_codec_samples(const so_codec *c, int32_t n_frames);
+/* codes [num_codebooks][n_frames] cb-major -> audio [*n_samples] (capacity cap) */
+int so_codec_decode(const so_codec *c, const int32_t *codes, int32_t n_frames, float *audio, int64_t cap,
+                    int64_t *n_samples);
+
 #ifdef __cplusplus
 }
 #endif

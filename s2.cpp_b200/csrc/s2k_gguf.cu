@@ -37,6 +37,8 @@ struct GgufValue {
     int64_t i = 0;
     double f = 0;
     std::string s;
+    std::vector<int64_t> arr;  // integer arrays (the codec's rate lists)
+    uint32_t arr_type = 0;
 };
 
 struct GgufTensor {
@@ -137,7 +139,17 @@ s2k_status parse(const char *path, GgufFile *g, std::FILE **keep) {
             } else {
                 const size_t es = scalar_size(et);
                 if (es == 0 || n > (1ull << 32)) return bad("array type");
-                if (std::fseek(f, (long)(es * n), SEEK_CUR) != 0) return bad("array data");
+                v.arr_type = et;
+                const bool keep = n <= 64 && (et == GT_U32 || et == GT_I32 || et == GT_U64 || et == GT_I64);
+                if (keep) {
+                    for (uint64_t i = 0; i < n; ++i) {
+                        uint64_t raw = 0;
+                        if (!r.read(&raw, es)) return bad("array data");
+                        v.arr.push_back(et == GT_I32 ? (int64_t)(int32_t)raw : (int64_t)raw);
+                    }
+                } else if (std::fseek(f, (long)(es * n), SEEK_CUR) != 0) {
+                    return bad("array data");
+                }
             }
         } else {
             const size_t es = scalar_size(v.type);
@@ -338,5 +350,129 @@ S2K_API s2k_status s2k_model_load_gguf(int32_t device, const char *path, s2k_mod
         return fail(rc, "%s", msg.c_str());
     }
     *out = m;
+    return S2K_OK;
+}
+
+// ---------------------------------------------------------------------------
+// codec: AudioCodec::load_shared's keys (src/s2_codec.cpp:765-874) and the
+// codec tensors ("c." names in the combined file, bare in a codec-only one)
+// ---------------------------------------------------------------------------
+namespace {
+
+s2k_status read_codec_hparams(const GgufFile &g, s2k_codec_hparams *hp, std::string *prefix) {
+    auto find = [&](const std::string &k) -> const GgufValue * {
+        auto it = g.kv.find(k);
+        return it == g.kv.end() ? nullptr : &it->second;
+    };
+    bool ok = true;
+    std::string missing;
+    auto req_int = [&](const std::string &k) -> int32_t {
+        const GgufValue *v = find(k);
+        if (!v || !(v->type == GT_U32 || v->type == GT_I32 || v->type == GT_U64 || v->type == GT_I64)) {
+            if (ok) missing = k;
+            ok = false;
+            return 0;
+        }
+        return (int32_t)v->i;
+    };
+    auto req_f32 = [&](const std::string &k) -> float {
+        const GgufValue *v = find(k);
+        if (!v || !(v->type == GT_F32 || v->type == GT_F64)) {
+            if (ok) missing = k;
+            ok = false;
+            return 0.f;
+        }
+        return (float)v->f;
+    };
+    auto req_arr = [&](const std::string &k, int32_t *dst, int32_t *n) {
+        const GgufValue *v = find(k);
+        if (!v || v->type != GT_ARRAY || v->arr.empty() || v->arr.size() > 8) {
+            if (ok) missing = k;
+            ok = false;
+            return;
+        }
+        *n = (int32_t)v->arr.size();
+        for (size_t i = 0; i < v->arr.size(); ++i) dst[i] = (int32_t)v->arr[i];
+    };
+    const GgufValue *a = find("general.architecture");
+    if (!a || a->type != GT_STRING) return fail(S2K_ERR_ARG, "codec GGUF: missing general.architecture");
+    if (a->s == "fish-speech") {
+        *prefix = "c.";
+    } else if (a->s == "fish-speech-codec") {
+        *prefix = "";
+    } else {
+        return fail(S2K_ERR_ARG, "codec GGUF: unexpected architecture %s", a->s.c_str());
+    }
+    std::memset(hp, 0, sizeof(*hp));
+    const std::string k = "fish_speech.codec.";
+    hp->sample_rate = req_int(k + "sample_rate");
+    hp->hop_length = req_int(k + "hop_length");
+    hp->latent_dim = req_int(k + "latent_dim");
+    hp->decoder_dim = req_int(k + "decoder_dim");
+    req_arr(k + "decoder_rates", hp->decoder_rates, &hp->n_decoder_rates);
+    hp->quantizer_input_dim = req_int(k + "quantizer_input_dim");
+    hp->quantizer_codebook_dim = req_int(k + "quantizer_codebook_dim");
+    hp->quantizer_residual_codebooks = req_int(k + "quantizer_residual_codebooks");
+    hp->quantizer_residual_codebook_size = req_int(k + "quantizer_residual_codebook_size");
+    hp->quantizer_semantic_codebook_size = req_int(k + "quantizer_semantic_codebook_size");
+    req_arr(k + "quantizer_downsample_factor", hp->quantizer_downsample_factor, &hp->n_downsample);
+    hp->rvq_window_size = req_int(k + "rvq_transformer.window_size");
+    hp->rvq_block_size = req_int(k + "rvq_transformer.block_size");
+    hp->rvq_n_layer = req_int(k + "rvq_transformer.n_layer");
+    hp->rvq_n_local_heads = req_int(k + "rvq_transformer.n_local_heads");
+    hp->rvq_head_dim = req_int(k + "rvq_transformer.head_dim");
+    hp->rvq_dim = req_int(k + "rvq_transformer.dim");
+    hp->rvq_rope_base = req_f32(k + "rvq_transformer.rope_freq_base");
+    hp->rvq_norm_eps = req_f32(k + "rvq_transformer.layer_norm_rms_eps");
+    if (!ok) return fail(S2K_ERR_ARG, "codec GGUF: missing key %s", missing.c_str());
+    return S2K_OK;
+}
+
+}  // namespace
+
+S2K_API s2k_status s2k_codec_load_gguf(int32_t device, const char *path, s2k_codec **out) {
+    if (!path || !out) return fail(S2K_ERR_ARG, "NULL argument");
+    *out = nullptr;
+    GgufFile g;
+    std::FILE *f = nullptr;
+    s2k_status rc = parse(path, &g, &f);
+    if (rc) return rc;
+    std::unique_ptr<std::FILE, int (*)(std::FILE *)> fh(f, &std::fclose);
+    s2k_codec_hparams hp;
+    std::string prefix;
+    if ((rc = read_codec_hparams(g, &hp, &prefix))) return rc;
+    s2k_codec *c = nullptr;
+    if ((rc = s2k_codec_create(device, &hp, &c))) return rc;
+    std::vector<uint8_t> buf;
+    for (const GgufTensor &t : g.tensors) {
+        if (t.name.compare(0, prefix.size(), prefix) != 0) continue;
+        // codec tensors only: the quantizer and decoder trees (the encoder's
+        // are left in the file, as decode does not read them)
+        const std::string bare = t.name.substr(prefix.size());
+        if (bare.compare(0, 10, "quantizer.") != 0 && bare.compare(0, 8, "decoder.") != 0) continue;
+        if (t.type != S2K_TYPE_F32 && t.type != S2K_TYPE_F16) {
+            s2k_codec_free(c);
+            return fail(S2K_ERR_UNSUPPORTED, "codec tensor '%s' has ggml type %u (F32 / F16)", t.name.c_str(), t.type);
+        }
+        buf.resize(t.nbytes);
+        if (fseeko(f, (off_t)(g.data_offset + t.offset), SEEK_SET) != 0 ||
+            std::fread(buf.data(), 1, t.nbytes, f) != t.nbytes) {
+            s2k_codec_free(c);
+            return fail(S2K_ERR_ARG, "failed to read tensor '%s'", t.name.c_str());
+        }
+        rc = s2k_codec_upload_tensor(c, t.name.c_str(), (int32_t)t.type, t.ne, buf.data(), t.nbytes);
+        if (rc) {
+            std::string msg = s2k_last_error();
+            s2k_codec_free(c);
+            return fail(rc, "%s", msg.c_str());
+        }
+    }
+    rc = s2k_codec_finalize(c);
+    if (rc) {
+        std::string msg = s2k_last_error();
+        s2k_codec_free(c);
+        return fail(rc, "%s", msg.c_str());
+    }
+    *out = c;
     return S2K_OK;
 }

@@ -41,6 +41,11 @@ EXPORTED = [
     "s2k_seq_load_kv", "s2k_get_rows", "s2k_model_set_wait_limit", "s2k_debug_wait_probe", "s2k_debug_fail_alloc",
     "s2k_model_device_bytes", "s2k_device_mem_info", "s2k_gguf_read_hparams", "s2k_gguf_tensor_info",
     "s2k_model_load_gguf", "s2k_build_prompt", "s2k_seq_last_metrics",
+    "s2k_codec_create", "s2k_codec_upload_tensor", "s2k_codec_finalize", "s2k_codec_load_gguf", "s2k_codec_free",
+    "s2k_codec_get_hparams", "s2k_codec_samples_per_frame", "s2k_codec_history_frames", "s2k_codec_num_codebooks",
+    "s2k_codec_receptive_frames", "s2k_codec_decode", "s2k_codec_decode_range", "s2k_codec_decode_windowed",
+    "s2k_codec_stream_create", "s2k_codec_stream_free", "s2k_codec_stream_push", "s2k_codec_stream_finish",
+    "s2k_codec_stream_max_release",
 ]
 
 REQ_WAITING, REQ_LIVE, REQ_DONE, REQ_FAILED, REQ_CANCELLED = 0, 1, 2, 3, 4  # S2K_REQ_*
@@ -87,6 +92,37 @@ class _SchedStats(ctypes.Structure):
 class _GenMetrics(ctypes.Structure):
     _fields_ = [("prefill_ms", ctypes.c_double), ("loop_ms", ctypes.c_double), ("total_ms", ctypes.c_double),
                 ("ms_per_frame", ctypes.c_double), ("n_frames", ctypes.c_int32), ("prompt_tokens", ctypes.c_int32)]
+
+
+class _CodecHParams(ctypes.Structure):
+    """s2k_codec_hparams"""
+    _fields_ = [("sample_rate", ctypes.c_int32), ("hop_length", ctypes.c_int32), ("latent_dim", ctypes.c_int32),
+                ("decoder_dim", ctypes.c_int32), ("n_decoder_rates", ctypes.c_int32),
+                ("decoder_rates", ctypes.c_int32 * 8), ("quantizer_input_dim", ctypes.c_int32),
+                ("quantizer_codebook_dim", ctypes.c_int32), ("quantizer_residual_codebooks", ctypes.c_int32),
+                ("quantizer_residual_codebook_size", ctypes.c_int32),
+                ("quantizer_semantic_codebook_size", ctypes.c_int32), ("n_downsample", ctypes.c_int32),
+                ("quantizer_downsample_factor", ctypes.c_int32 * 8), ("rvq_window_size", ctypes.c_int32),
+                ("rvq_block_size", ctypes.c_int32), ("rvq_n_layer", ctypes.c_int32),
+                ("rvq_n_local_heads", ctypes.c_int32), ("rvq_head_dim", ctypes.c_int32), ("rvq_dim", ctypes.c_int32),
+                ("rvq_rope_base", ctypes.c_float), ("rvq_norm_eps", ctypes.c_float)]
+
+
+def codec_hp_struct(ch, cls=_CodecHParams):
+    """A ctypes codec hyper-parameter struct from an object with the
+    CodecHParams attributes (decoder_rates / quantizer_downsample_factor as
+    sequences)."""
+    h = cls()
+    for name, _ in cls._fields_:
+        if name in ("decoder_rates", "quantizer_downsample_factor"):
+            vals = list(getattr(ch, name))
+            arr = getattr(h, name)
+            for k, v in enumerate(vals):
+                arr[k] = int(v)
+            setattr(h, "n_decoder_rates" if name == "decoder_rates" else "n_downsample", len(vals))
+        elif name not in ("n_decoder_rates", "n_downsample"):
+            setattr(h, name, getattr(ch, name))
+    return h
 
 
 FRAME_CB = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32,
@@ -168,6 +204,25 @@ def lib() -> ctypes.CDLL:
         "s2k_seq_last_metrics": ([vp, ctypes.POINTER(_GenMetrics)], i32),
         "s2k_build_prompt": ([ENCODE_FN, vp, ctypes.c_char_p, ctypes.c_char_p, vp, i32, i32, i32, i32, i32, vp,
                               ctypes.c_size_t, ctypes.POINTER(i32), ctypes.POINTER(i32)], i32),
+        "s2k_codec_create": ([i32, ctypes.POINTER(_CodecHParams), ctypes.POINTER(vp)], i32),
+        "s2k_codec_upload_tensor": ([vp, ctypes.c_char_p, i32, i64p, vp, ctypes.c_size_t], i32),
+        "s2k_codec_finalize": ([vp], i32),
+        "s2k_codec_load_gguf": ([i32, ctypes.c_char_p, ctypes.POINTER(vp)], i32),
+        "s2k_codec_free": ([vp], None),
+        "s2k_codec_get_hparams": ([vp, ctypes.POINTER(_CodecHParams)], i32),
+        "s2k_codec_samples_per_frame": ([vp], i32),
+        "s2k_codec_history_frames": ([vp], i32),
+        "s2k_codec_num_codebooks": ([vp], i32),
+        "s2k_codec_receptive_frames": ([vp], i32),
+        "s2k_codec_decode": ([vp, vp, i32, vp, ctypes.c_size_t, i64p], i32),
+        "s2k_codec_decode_range": ([vp, vp, i32, i32, i32, vp, ctypes.c_size_t, i64p], i32),
+        "s2k_codec_decode_windowed": ([vp, vp, i32, i32, i32, i32, vp, ctypes.c_size_t, i64p,
+                                       ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i32)], i32),
+        "s2k_codec_stream_create": ([vp, i32, i32, i32, ctypes.POINTER(vp)], i32),
+        "s2k_codec_stream_free": ([vp], None),
+        "s2k_codec_stream_push": ([vp, vp, vp, ctypes.c_size_t, i64p], i32),
+        "s2k_codec_stream_finish": ([vp, vp, ctypes.c_size_t, i64p], i32),
+        "s2k_codec_stream_max_release": ([vp], ctypes.c_int64),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -656,3 +711,127 @@ class BatchScheduler:
 
 def launch_count(reset: bool = False) -> int:
     return int(lib().s2k_launch_count(1 if reset else 0))
+
+
+class AudioCodec:
+    """Mirror of s2::AudioCodec's decode side (include/s2_codec.h:14-60):
+    decode (AudioCodec::decode), samples_per_code_frame,
+    streaming_history_frames, num_codebooks, plus the windowed decode of
+    offline synthesis (decode_codes_windowed) and a streaming decoder.
+    Codes are [num_codebooks][n_frames] int32, audio float32."""
+
+    def __init__(self, hparams, device: int = 0):
+        self._hp = hparams
+        self._c = ctypes.c_void_p()
+        h = codec_hp_struct(hparams)
+        _check(lib().s2k_codec_create(device, ctypes.byref(h), ctypes.byref(self._c)))
+
+    @classmethod
+    def from_gguf(cls, path: str, device: int = 0) -> "AudioCodec":
+        self = cls.__new__(cls)
+        self._hp = None
+        self._c = ctypes.c_void_p()
+        _check(lib().s2k_codec_load_gguf(device, path.encode(), ctypes.byref(self._c)))
+        return self
+
+    def upload_tensor(self, name: str, ggml_type: int, ne, data: np.ndarray) -> None:
+        data = np.ascontiguousarray(data)
+        ne4 = (ctypes.c_int64 * 4)(*[int(x) for x in (list(ne) + [1, 1, 1, 1])[:4]])
+        _check(lib().s2k_codec_upload_tensor(self._c, name.encode(), ggml_type, ne4, _ptr(data), data.nbytes))
+
+    def load_tensors(self, tensors) -> None:
+        """tensors: (spec, fp16 array) pairs as synthetic.make_codec yields"""
+        for spec, arr in tensors:
+            self.upload_tensor(spec.name, 1 if arr.dtype == np.float16 else 0, spec.ne, arr)
+        _check(lib().s2k_codec_finalize(self._c))
+
+    def samples_per_code_frame(self) -> int:
+        return int(lib().s2k_codec_samples_per_frame(self._c))
+
+    def streaming_history_frames(self) -> int:
+        return int(lib().s2k_codec_history_frames(self._c))
+
+    def num_codebooks(self) -> int:
+        return int(lib().s2k_codec_num_codebooks(self._c))
+
+    def receptive_frames(self) -> int:
+        return int(lib().s2k_codec_receptive_frames(self._c))
+
+    def decode(self, codes: np.ndarray) -> np.ndarray:
+        codes = np.ascontiguousarray(codes, dtype=np.int32)
+        n = codes.shape[1]
+        out = np.empty(n * self.samples_per_code_frame(), dtype=np.float32)
+        ns = ctypes.c_int64(0)
+        _check(lib().s2k_codec_decode(self._c, _ptr(codes), n, _ptr(out), out.size, ctypes.byref(ns)))
+        return out[: ns.value]
+
+    def decode_range(self, codes: np.ndarray, emit_begin: int, emit_end: int) -> np.ndarray:
+        codes = np.ascontiguousarray(codes, dtype=np.int32)
+        n = codes.shape[1]
+        out = np.empty(max(emit_end - emit_begin, 0) * self.samples_per_code_frame(), dtype=np.float32)
+        ns = ctypes.c_int64(0)
+        _check(lib().s2k_codec_decode_range(self._c, _ptr(codes), n, emit_begin, emit_end, _ptr(out), out.size,
+                                            ctypes.byref(ns)))
+        return out[: ns.value]
+
+    def decode_windowed(self, codes: np.ndarray, stride_frames: int = 16, context_frames: int = -1):
+        """(audio, device ms, windows) of decode_codes_windowed"""
+        codes = np.ascontiguousarray(codes, dtype=np.int32)
+        ncb, n = codes.shape
+        out = np.empty(n * self.samples_per_code_frame(), dtype=np.float32)
+        ns, ms, nb = ctypes.c_int64(0), ctypes.c_double(0), ctypes.c_int32(0)
+        _check(lib().s2k_codec_decode_windowed(self._c, _ptr(codes), n, ncb, stride_frames, context_frames, _ptr(out),
+                                               out.size, ctypes.byref(ns), ctypes.byref(ms), ctypes.byref(nb)))
+        return out[: ns.value], ms.value, nb.value
+
+    def stream(self, stride_frames: int = 4, context_frames: int = -1, holdback_frames: int = -1) -> "CodecStream":
+        return CodecStream(self, stride_frames, context_frames, holdback_frames)
+
+    def close(self) -> None:
+        if getattr(self, "_c", None):
+            lib().s2k_codec_free(self._c)
+            self._c = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CodecStream:
+    """Streaming decode: push one frame of codes at a time, get the PCM each
+    window releases (decode_window_and_emit, src/s2_pipeline.cpp:1034-1115)."""
+
+    def __init__(self, codec: AudioCodec, stride_frames: int, context_frames: int, holdback_frames: int):
+        self._codec = codec
+        self._s = ctypes.c_void_p()
+        _check(lib().s2k_codec_stream_create(codec._c, stride_frames, context_frames, holdback_frames,
+                                             ctypes.byref(self._s)))
+
+    def _buf(self) -> np.ndarray:
+        return np.empty(max(int(lib().s2k_codec_stream_max_release(self._s)), 1), dtype=np.float32)
+
+    def push(self, frame_codes) -> np.ndarray:
+        fc = np.ascontiguousarray(frame_codes, dtype=np.int32)
+        out = self._buf()
+        n = ctypes.c_int64(0)
+        _check(lib().s2k_codec_stream_push(self._s, _ptr(fc), _ptr(out), out.size, ctypes.byref(n)))
+        return out[: n.value]
+
+    def finish(self) -> np.ndarray:
+        out = self._buf()
+        n = ctypes.c_int64(0)
+        _check(lib().s2k_codec_stream_finish(self._s, _ptr(out), out.size, ctypes.byref(n)))
+        return out[: n.value]
+
+    def close(self) -> None:
+        if getattr(self, "_s", None):
+            lib().s2k_codec_stream_free(self._s)
+            self._s = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -62,3 +62,55 @@ def write_model_gguf(path: str, hp, tensors, extra_tensor: bool = True) -> None:
     w.write_kv_data_to_file()
     w.write_tensors_to_file()
     w.close()
+
+
+def write_codec_gguf(path: str, ch, tensors, combined: bool = True) -> None:
+    """A codec GGUF under the keys AudioCodec::load_shared reads
+    (src/s2_codec.cpp:813-858): the combined layout ("fish-speech", tensors
+    named "c.*", next to a model tensor the codec loader must skip) or a
+    codec-only file ("fish-speech-codec", bare names)."""
+    import gguf
+
+    w = gguf.GGUFWriter(path, arch="fish-speech" if combined else "fish-speech-codec")
+    k = "fish_speech.codec."
+    w.add_uint32(k + "sample_rate", ch.sample_rate)
+    w.add_uint32(k + "hop_length", ch.hop_length)
+    w.add_uint32(k + "frame_length", ch.hop_length)
+    w.add_uint32(k + "encoder_dim", 64)
+    w.add_uint32(k + "decoder_dim", ch.decoder_dim)
+    w.add_uint32(k + "latent_dim", ch.latent_dim)
+    w.add_array(k + "encoder_rates", list(reversed(ch.decoder_rates)))
+    w.add_array(k + "decoder_rates", list(ch.decoder_rates))
+    w.add_array(k + "encoder_transformer_layers", [0] * len(ch.decoder_rates))
+    w.add_array(k + "decoder_transformer_layers", [0] * len(ch.decoder_rates))
+    w.add_string(k + "quantizer_type", "downsample_residual_vector_quantize")
+    w.add_uint32(k + "quantizer_input_dim", ch.quantizer_input_dim)
+    w.add_uint32(k + "quantizer_codebook_dim", ch.quantizer_codebook_dim)
+    w.add_uint32(k + "quantizer_residual_codebooks", ch.quantizer_residual_codebooks)
+    w.add_uint32(k + "quantizer_residual_codebook_size", ch.quantizer_residual_codebook_size)
+    w.add_uint32(k + "quantizer_semantic_codebook_size", ch.quantizer_semantic_codebook_size)
+    w.add_array(k + "quantizer_downsample_factor", list(ch.quantizer_downsample_factor))
+    w.add_uint32(k + "transformer.block_size", 8192)
+    w.add_int32(k + "transformer.n_local_heads", -1)
+    w.add_uint32(k + "transformer.head_dim", 64)
+    w.add_float32(k + "transformer.rope_freq_base", 10000.0)
+    w.add_float32(k + "transformer.layer_norm_rms_eps", 1e-5)
+    w.add_uint32(k + "rvq_transformer.window_size", ch.rvq_window_size)
+    w.add_uint32(k + "rvq_transformer.block_size", ch.rvq_block_size)
+    w.add_uint32(k + "rvq_transformer.n_layer", ch.rvq_n_layer)
+    w.add_uint32(k + "rvq_transformer.n_head", ch.rvq_dim // ch.rvq_head_dim)
+    w.add_int32(k + "rvq_transformer.n_local_heads", ch.rvq_n_local_heads)
+    w.add_uint32(k + "rvq_transformer.head_dim", ch.rvq_head_dim)
+    w.add_uint32(k + "rvq_transformer.dim", ch.rvq_dim)
+    w.add_uint32(k + "rvq_transformer.feed_forward_length", ch.rvq_ff)
+    w.add_float32(k + "rvq_transformer.rope_freq_base", ch.rvq_rope_base)
+    w.add_float32(k + "rvq_transformer.layer_norm_rms_eps", ch.rvq_norm_eps)
+    pre = "c." if combined else ""
+    if combined:
+        w.add_tensor("norm.weight", np.ones(64, dtype=np.float32))  # a model tensor
+    for spec, arr in tensors:
+        w.add_tensor(pre + spec.name, np.asarray(arr).reshape(tuple(reversed(spec.ne))))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
