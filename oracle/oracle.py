@@ -102,6 +102,7 @@ def lib() -> ctypes.CDLL:
             "so_codec_set_tensor": ([vp, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(i64), vp], ctypes.c_int),
             "so_codec_samples": ([vp, i32], i64),
             "so_codec_decode": ([vp, vp, i32, vp, i64, ctypes.POINTER(i64)], ctypes.c_int),
+            "so_codec_set_f32_accum": ([ctypes.c_int], None),
         }
         for name, (a, r) in sig.items():
             f = getattr(L, name)
@@ -304,13 +305,19 @@ class CodecOracle:
     def samples_per_frame(self) -> int:
         return int(lib().so_codec_samples(self._c, 1))
 
-    def decode(self, codes: np.ndarray) -> np.ndarray:
+    def decode(self, codes: np.ndarray, f32_accum: bool = False) -> np.ndarray:
+        """f32_accum: sum the dot products in float, in sequence (a second
+        valid accumulation order) instead of double"""
         codes = np.ascontiguousarray(codes, dtype=np.int32)
         n = codes.shape[1]
         cap = int(lib().so_codec_samples(self._c, n))
         out = np.empty(cap, dtype=np.float32)
         ns = ctypes.c_int64(0)
-        rc = lib().so_codec_decode(self._c, codes.ctypes.data, n, out.ctypes.data, cap, ctypes.byref(ns))
+        lib().so_codec_set_f32_accum(1 if f32_accum else 0)
+        try:
+            rc = lib().so_codec_decode(self._c, codes.ctypes.data, n, out.ctypes.data, cap, ctypes.byref(ns))
+        finally:
+            lib().so_codec_set_f32_accum(0)
         if rc != 0:
             raise RuntimeError(f"codec oracle decode failed ({rc})")
         return out[: ns.value]
@@ -323,12 +330,13 @@ class CodecOracle:
     def windows_offline(self, total: int, stride: int = 16, context: int = -1):
         return codec_windows_offline(total, stride, context if context >= 0 else self.history_frames())
 
-    def decode_windowed(self, codes: np.ndarray, stride: int = 16, context: int = -1) -> np.ndarray:
+    def decode_windowed(self, codes: np.ndarray, stride: int = 16, context: int = -1,
+                        f32_accum: bool = False) -> np.ndarray:
         spf = self.samples_per_frame()
         parts = []
         for start, wf, eb, ee in self.windows_offline(codes.shape[1], stride, context):
             if ee > eb:
-                pcm = self.decode(codes[:, start:start + wf])
+                pcm = self.decode(codes[:, start:start + wf], f32_accum)
                 parts.append(pcm[eb * spf: ee * spf])
         return np.concatenate(parts) if parts else np.zeros(0, np.float32)
 

@@ -100,6 +100,16 @@ static int64_t numel(const sc_tensor *t) { return t->ne[0] * t->ne[1] * t->ne[2]
 
 /* ---- ops on [L][C] activations ---- */
 
+/* Accumulation order of the dot products: double (default), or float in
+ * sequence when set -- a second valid order, so tests can measure how far
+ * two correct evaluations of the fp16-rounded graph drift apart. */
+static int g_f32_accum = 0;
+void so_codec_set_f32_accum(int on) { g_f32_accum = on; }
+static inline void acc(double *s, double v) {
+    if (g_f32_accum) *s = (double)((float)*s + (float)v);
+    else *s += v;
+}
+
 /* fp32 -> fp16 -> fp32, round to nearest even (ggml's fp16 conversions) */
 static float r16(float x) { return so_fp16_to_fp32(so_fp32_to_fp16(x)); }
 
@@ -120,7 +130,7 @@ static void linear(const float *x, int L, int in, const sc_tensor *w, const sc_t
         for (int o = 0; o < out; ++o) {
             double s = 0.0;
             const float *wr = w->data + (size_t)o * in;
-            for (int i = 0; i < in; ++i) s += (double)wr[i] * (double)xs[(size_t)t * in + i];
+            for (int i = 0; i < in; ++i) acc(&s, (double)wr[i] * (double)xs[(size_t)t * in + i]);
             y[(size_t)t * out + o] = b ? (float)s + b->data[o] : (float)s;
         }
     free(xr);
@@ -154,7 +164,7 @@ static void conv1d(const float *x, int L, int Cin, const sc_tensor *w, const sc_
                 const int src = t - pad + k * dilation;
                 if (src < 0) continue;
                 const float *wr = wr16 + ((size_t)o * Cin) * K + k;
-                for (int i = 0; i < Cin; ++i) s += (double)wr[(size_t)i * K] * (double)xr[(size_t)src * Cin + i];
+                for (int i = 0; i < Cin; ++i) acc(&s, (double)wr[(size_t)i * K] * (double)xr[(size_t)src * Cin + i]);
             }
             y[(size_t)t * Cout + o] = (float)s + b->data[o];
         }
@@ -172,14 +182,14 @@ static int conv_t1d(const float *x, int L, int Cin, const sc_tensor *w, const sc
 #pragma omp parallel for schedule(static)
     for (int t = 0; t < Lo; ++t)
         for (int o = 0; o < Cout; ++o) {
-            double acc = 0.0;
+            double a = 0.0;
             for (int k = t % s; k < K; k += s) {
                 const int j = (t - k) / s;
                 if (j < 0 || j >= L) continue;
                 for (int i = 0; i < Cin; ++i)
-                    acc += (double)x[(size_t)j * Cin + i] * (double)w->data[((size_t)i * Cout + o) * K + k];
+                    acc(&a, (double)x[(size_t)j * Cin + i] * (double)w->data[((size_t)i * Cout + o) * K + k]);
             }
-            y[(size_t)t * Cout + o] = (float)acc + b->data[o];
+            y[(size_t)t * Cout + o] = (float)a + b->data[o];
         }
     return Lo;
 }
@@ -272,7 +282,7 @@ static int transformer(const so_codec *c, float *x, int L) {
                 for (int k = k0; k <= t; ++k) {
                     const float *kk = qkv + (size_t)k * qkvs + qs + kh * hd;
                     double s = 0.0;
-                    for (int d = 0; d < hd; ++d) s += (double)q[d] * (double)kk[d];
+                    for (int d = 0; d < hd; ++d) acc(&s, (double)q[d] * (double)kk[d]);
                     sc[k - k0] = (float)s * scale;
                     if (sc[k - k0] > mx) mx = sc[k - k0];
                 }
@@ -285,7 +295,7 @@ static int transformer(const so_codec *c, float *x, int L) {
                 for (int k = k0; k <= t; ++k) sc[k - k0] *= inv;
                 for (int d = 0; d < hd; ++d) {
                     double o = 0.0;
-                    for (int k = k0; k <= t; ++k) o += (double)sc[k - k0] * (double)qkv[(size_t)k * qkvs + qs + ks + kh * hd + d];
+                    for (int k = k0; k <= t; ++k) acc(&o, (double)sc[k - k0] * (double)qkv[(size_t)k * qkvs + qs + ks + kh * hd + d]);
                     att[(size_t)t * qs + hh * hd + d] = (float)o;
                 }
                 free(sc);
@@ -376,7 +386,7 @@ int so_codec_decode(const so_codec *c, const int32_t *codes, int32_t n_frames, f
             if (code >= cs) code = cs - 1;
             for (int o = 0; o < C0; ++o) {
                 double s = 0.0;
-                for (int d = 0; d < cd; ++d) s += (double)ow->data[(size_t)o * cd + d] * (double)cb->data[(size_t)code * cd + d];
+                for (int d = 0; d < cd; ++d) acc(&s, (double)ow->data[(size_t)o * cd + d] * (double)cb->data[(size_t)code * cd + d]);
                 const float v = (float)s + ob->data[o];
                 if (q == 0) a[(size_t)t * C0 + o] = v;
                 else a[(size_t)t * C0 + o] += v;
@@ -415,7 +425,7 @@ int so_codec_decode(const so_codec *c, const int32_t *codes, int32_t n_frames, f
                 double s = 0.0;
                 for (int k = 0; k < K; ++k) {
                     const int src = t - (K - 1) + k;
-                    if (src >= 0) s += (double)dwr[(size_t)ch2 * K + k] * (double)br[(size_t)src * C + ch2];
+                    if (src >= 0) acc(&s, (double)dwr[(size_t)ch2 * K + k] * (double)br[(size_t)src * C + ch2]);
                 }
                 r[(size_t)t * C + ch2] = (float)s + db->data[ch2];
             }

@@ -188,6 +188,9 @@ int64_t so_codec_samples(const so_codec *c, int32_t n_frames);
 /* codes [num_codebooks][n_frames] cb-major -> audio [*n_samples] (capacity cap) */
 int so_codec_decode(const so_codec *c, const int32_t *codes, int32_t n_frames, float *audio, int64_t cap,
                     int64_t *n_samples);
+/* 1: the decode's dot products accumulate in float, in sequence, instead of
+ * double (a second accumulation order, for measuring the graph's own drift) */
+void so_codec_set_f32_accum(int on);
 
 #ifdef __cplusplus
 }

@@ -1,14 +1,17 @@
 """GPU parity of the codec decode (s2k_codec_*, AudioCodec::decode,
 src/s2_codec.cpp:1297-1447) against the CPU oracle, through the C ABI.
 
-Bars.  Against the oracle: max |audio delta| <= 2e-3 (audio is in (-1, 1),
-std ~0.25-0.45 for these weights) and RMS delta <= 2e-4 -- floating-point
-tolerance: the reference graph rounds operands to fp16 at every matrix
-product and convolution, as the tensor-core GEMMs do, but accumulation order
-differs, so a rounding to fp16 can land on the other side now and then.
-Between GPU paths (a window decoded whole vs. the truncated decode of the
-emitted range, the windowed / streaming drivers vs. their windows decoded
-one by one): bit-exact."""
+Bars.  Against the oracle: the reference graph rounds operands to fp16 at
+every matrix product and convolution, as the tensor-core GEMMs do, but a
+different accumulation order lands some roundings on the other side, and
+those flips compound through the decoder stack.  The oracle itself drifts by
+that much between two valid accumulation orders (double vs. float in
+sequence: rms ~2e-4 on the small codec, ~1e-3 at S2 Pro widths, audio std
+0.25-0.45).  So the bar is relative to that drift, measured on the same
+input: max and rms |GPU - oracle| <= 3x the oracle's own max / rms drift
+(+1e-5 / 1e-6).  Between GPU paths (a window decoded whole vs. the
+truncated decode of the emitted range, the windowed / streaming drivers vs.
+their windows decoded one by one): bit-exact."""
 from __future__ import annotations
 
 import os
@@ -22,16 +25,20 @@ import synthetic
 
 pytestmark = pytest.mark.gpu
 
-MAX_ABS = 2e-3
-RMS = 2e-4
+def _dev(a: np.ndarray, b: np.ndarray):
+    d = np.abs(a.astype(np.float64) - b.astype(np.float64))
+    return float(d.max(initial=0.0)), float(np.sqrt(np.mean(d * d))) if d.size else 0.0
 
 
-def assert_audio_close(got: np.ndarray, want: np.ndarray, what: str) -> None:
-    assert got.shape == want.shape, (what, got.shape, want.shape)
+def assert_audio_close(got: np.ndarray, want: np.ndarray, want_f32acc: np.ndarray, what: str) -> None:
+    """got vs the oracle (want), bounded by the oracle's own drift between
+    its two accumulation orders (want vs want_f32acc)"""
+    assert got.shape == want.shape == want_f32acc.shape, (what, got.shape, want.shape)
     assert np.isfinite(got).all(), what
-    d = np.abs(got.astype(np.float64) - want.astype(np.float64))
-    rms = float(np.sqrt(np.mean(d * d))) if d.size else 0.0
-    assert d.max(initial=0.0) <= MAX_ABS and rms <= RMS, f"{what}: max |d| {d.max():.3g}, rms {rms:.3g}"
+    fmax, frms = _dev(want, want_f32acc)
+    gmax, grms = _dev(got, want)
+    assert gmax <= 3 * fmax + 1e-5 and grms <= 3 * frms + 1e-6, (
+        f"{what}: |gpu - oracle| max {gmax:.3g} rms {grms:.3g}; oracle drift max {fmax:.3g} rms {frms:.3g}")
 
 
 @pytest.fixture(scope="module")
@@ -54,7 +61,7 @@ def test_small_decode_matches_oracle(small):
     assert c.streaming_history_frames() == co.history_frames()
     for n, seed in ((1, 1), (7, 2), (40, 3), (130, 4)):
         codes = synthetic.codec_codes(ch, n, seed=seed)
-        assert_audio_close(c.decode(codes), co.decode(codes), f"small decode n={n}")
+        assert_audio_close(c.decode(codes), co.decode(codes), co.decode(codes, True), f"small decode n={n}")
 
 
 def test_small_codes_clamped(small):
@@ -69,7 +76,7 @@ def test_small_codes_clamped(small):
     clamped[0] = np.clip(clamped[0], 0, ch.quantizer_semantic_codebook_size - 1)
     clamped[1:] = np.clip(clamped[1:], 0, ch.quantizer_residual_codebook_size - 1)
     assert np.array_equal(got, c.decode(clamped))
-    assert_audio_close(got, co.decode(wild), "clamped codes")
+    assert_audio_close(got, co.decode(wild), co.decode(wild, True), "clamped codes")
 
 
 def test_small_range_is_exact_slice(small):
@@ -99,7 +106,8 @@ def test_small_windowed_matches_windows(small):
         assert nb == len(wins) and ms > 0
         parts = [c.decode(codes[:, s:s + wf])[eb * spf: ee * spf] for s, wf, eb, ee in wins]
         assert np.array_equal(got, np.concatenate(parts)), (total, stride, ctx)
-        assert_audio_close(got, co.decode_windowed(codes, stride, ctx), f"windowed {total}/{stride}/{ctx}")
+        assert_audio_close(got, co.decode_windowed(codes, stride, ctx), co.decode_windowed(codes, stride, ctx, True),
+                           f"windowed {total}/{stride}/{ctx}")
 
 
 @pytest.mark.parametrize("stride,ctx,hold", [(4, -1, -1), (4, 8, 2), (1, 6, 0), (5, 0, 3)])
@@ -168,7 +176,7 @@ def test_s2pro_decode_matches_oracle(s2pro):
     try:
         co.load_tensors(tensors)
         codes = synthetic.codec_codes(ch, 6, seed=21)
-        assert_audio_close(c.decode(codes), co.decode(codes), "s2pro decode")
+        assert_audio_close(c.decode(codes), co.decode(codes), co.decode(codes, True), "s2pro decode")
     finally:
         co.close()
 
