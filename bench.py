@@ -66,8 +66,88 @@ def peaks() -> dict:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
-    return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "tflops": float(d.get("bf16_tflops", 1590.0)), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "src": "fallback"}
+
+
+def codec_flops(ch, n_tr: int, n_dec: int) -> float:
+    """Algorithmic FLOPs (2 per multiply-add) of a codec decode over n_tr
+    transformer frames and n_dec decoder frames: the matrix products and
+    convolutions of the reference graph (each transposed convolution once, as
+    the reference computes it)."""
+    d, hd, ff = ch.rvq_dim, ch.rvq_head_dim, ch.rvq_ff
+    H = d // hd
+    Hk = ch.rvq_n_local_heads if ch.rvq_n_local_heads > 0 else H
+    keys = min(ch.rvq_window_size, n_tr) if ch.rvq_window_size > 0 else n_tr
+    f = ch.rvq_n_layer * 2.0 * n_tr * (d * (H + 2 * Hk) * hd + H * hd * d + 3 * d * ff + 2 * H * hd * keys)
+    L, C = n_dec, d
+    for fac in reversed(ch.quantizer_downsample_factor):
+        f += 2.0 * L * fac * C * C
+        L *= fac
+        f += 2.0 * L * C * (ch.dw_kernel + 2 * ch.convnext_hidden)
+    f += 2.0 * L * ch.decoder_dim * C * 7
+    C = ch.decoder_dim
+    for r in ch.decoder_rates:
+        co = C // 2
+        f += 2.0 * L * (r * co) * (2 * C)
+        L *= r
+        f += 3 * 2.0 * L * co * co * 8
+        C = co
+    return f + 2.0 * L * C * 7
+
+
+def codec_decode(with_cpu: bool, reps: int = 10, warmup: int = 3) -> dict:
+    """The codec decode after the frame loop (AudioCodec::decode,
+    src/s2_codec.cpp:1297-1447) on the S2 Pro codec shapes with seeded F16
+    weights: one decode of a 160-frame window (the offline windowed decode's
+    transformer span at stride 16 / history 144) timed with the library's CUDA
+    events, the tensor-core FLOP rate against the measured dense bf16/f16
+    peak, and the windowed decode of a 215-frame (10 s) utterance.  Beside
+    it the CPU oracle on a 2-frame sample."""
+    ch = synthetic.codec_preset("s2pro")
+    tensors = list(synthetic.make_codec(ch, seed=6))
+    c = s2k.AudioCodec(ch)
+    c.load_tensors(tensors)
+    out = {"workload": "codec decode, S2 Pro codec shapes (8-layer 1024-wide windowed transformer, 1536->96 "
+                       "channel decoder, 2048 samples/frame), F16 weights"}
+    n = 160
+    codes = synthetic.codec_codes(ch, n, seed=160)
+    dev = []
+    for i in range(warmup + reps):
+        _, ms, _ = c.decode_windowed(codes, n, 0)  # one window: the whole 160 frames
+        if i >= warmup:
+            dev.append(ms)
+    ms = float(np.median(dev))
+    fl = codec_flops(ch, n, n)
+    pk = peaks()
+    out["window_160"] = {"ms": ms, "flops": fl, "achieved_tflops": fl / (ms / 1e3) / 1e12,
+                         "peak_tflops": pk["tflops"], "frac": fl / (ms / 1e3) / 1e12 / pk["tflops"],
+                         "peak_src": pk["src"], "audio_s": n * ch.samples_per_frame / ch.sample_rate}
+    utt = synthetic.codec_codes(ch, 215, seed=215)
+    c.decode_windowed(utt, 16)
+    t = time.perf_counter()
+    audio, wms, nb = c.decode_windowed(utt, 16)
+    wall = (time.perf_counter() - t) * 1e3
+    out["windowed_215"] = {"device_ms": wms, "wall_ms": wall, "windows": nb, "audio_s": audio.size / ch.sample_rate,
+                           "rtf": wall / 1e3 / (audio.size / ch.sample_rate),
+                           "receptive_frames": c.receptive_frames()}
+    if with_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle  # noqa: E402  (cpu_baseline leg only)
+        oracle.set_threads(os.cpu_count() or 1)
+        co = oracle.CodecOracle(ch)
+        co.load_tensors(tensors)
+        sample = synthetic.codec_codes(ch, 2, seed=2)
+        t = time.perf_counter()
+        want = co.decode(sample)
+        cpu_s = time.perf_counter() - t
+        got = c.decode(sample)
+        d = np.abs(got.astype(np.float64) - want)
+        out["cpu_oracle"] = {"ms_per_frame": cpu_s * 1e3 / 2, "cores": os.cpu_count() or 1, "sample": "2 frames",
+                             "gpu_max_abs_diff": float(d.max()), "gpu_rms_diff": float(np.sqrt(np.mean(d * d)))}
+        co.close()
+    c.close()
+    return out
 
 
 def workload(preset: str, quant: str, prompt: int, frames: int) -> str:
@@ -506,6 +586,7 @@ def main() -> None:
     ap.add_argument("--cpu-frames", type=int, default=2, help="frames in the CPU oracle sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-slow-step", action="store_true", help="skip the Slow step at 512 cached positions")
+    ap.add_argument("--no-codec", action="store_true", help="skip the codec decode measurement")
     ap.add_argument("--preset", choices=["s2pro", "mid"], default="s2pro",
                     help="model shape; 'mid' (2+1 layers, real widths) is for small profiler captures only")
     ap.add_argument("--workload", choices=["frames", "ragged", "f16long"], default="frames",
@@ -629,6 +710,12 @@ def main() -> None:
     step512 = None
     if args.preset == "s2pro" and args.quant == "q8_0" and not args.no_slow_step:
         step512 = slow_step_at_512(m, hp, tensors, with_cpu=cpu is not None and cpu.get("value") is not None)
+    codec = None
+    if rank == 0 and world == 1 and not args.no_codec:
+        try:
+            codec = codec_decode(with_cpu=cpu is not None and cpu.get("value") is not None)
+        except Exception as e:  # reported, never fatal
+            codec = {"error": str(e)}
 
     if rank == 0:
         line = {
@@ -655,6 +742,7 @@ def main() -> None:
                                "bytes_per_step": step_bytes},
             "cpu_baseline": cpu,
             "slow_step_512": step512,
+            "codec_decode": codec,
             "timed_codes_match_generate": codes_match,
             "clocks": clk,
             "gpu_launches": int(launches),

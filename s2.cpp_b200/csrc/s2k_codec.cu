@@ -60,7 +60,7 @@ namespace codec {
 // ---------------------------------------------------------------------------
 constexpr int kCM = 128;  // A rows (time) per tile = MMA M
 constexpr int kCK = 64;   // fp16 columns per stage (one 128-byte swizzle row)
-constexpr int kCEpiWarps = 8;
+constexpr int kCEpiWarps = 16;  // 4 per TMEM lane quarter: enough warps in flight to hide L2 latency
 constexpr int kCThreads = (2 + kCEpiWarps) * 32;
 constexpr uint32_t kCStageA = kCM * kCK * 2;  // 16 KB
 
@@ -143,8 +143,16 @@ __device__ __forceinline__ void store_h16(__half *dst, const float (&z)[16]) {
     reinterpret_cast<uint4 *>(dst)[1] = s[1];
 }
 
+// the residual of 16 columns (loaded ahead of the accumulator)
+__device__ __forceinline__ void load_res16(const CGemm &p, int t, int n0, float4 (&r)[4]) {
+    if (!p.res || t >= p.M || n0 >= p.N) return;
+    const float4 *r4 = reinterpret_cast<const float4 *>(p.res + (size_t)t * p.ldres + n0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[j] = __ldcg(r4 + j);
+}
+
 // 16 accumulator columns n0..n0+15 of output row t
-__device__ __forceinline__ void epilogue16(const CGemm &p, int t, int n0, const int (&v)[16]) {
+__device__ __forceinline__ void epilogue16(const CGemm &p, int t, int n0, const int (&v)[16], const float4 (&r)[4]) {
     if (p.act == ACT_SWIGLU) {  // columns: 8 gates then the 8 matching ups
         __half2 h[4];
 #pragma unroll
@@ -173,14 +181,12 @@ __device__ __forceinline__ void epilogue16(const CGemm &p, int t, int n0, const 
         for (int j = 0; j < 16; ++j) y[j] = __fmul_rn(y[j], __ldg(p.gamma + ch + j));
     }
     if (p.res) {
-        const float4 *r4 = reinterpret_cast<const float4 *>(p.res + (size_t)t * p.ldres + n0);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const float4 r = __ldcg(r4 + j);
-            y[4 * j] = __fadd_rn(r.x, y[4 * j]);
-            y[4 * j + 1] = __fadd_rn(r.y, y[4 * j + 1]);
-            y[4 * j + 2] = __fadd_rn(r.z, y[4 * j + 2]);
-            y[4 * j + 3] = __fadd_rn(r.w, y[4 * j + 3]);
+            y[4 * j] = __fadd_rn(r[j].x, y[4 * j]);
+            y[4 * j + 1] = __fadd_rn(r[j].y, y[4 * j + 1]);
+            y[4 * j + 2] = __fadd_rn(r[j].z, y[4 * j + 2]);
+            y[4 * j + 3] = __fadd_rn(r[j].w, y[4 * j + 3]);
         }
     }
     if (p.y32) {
@@ -309,22 +315,48 @@ __global__ void __launch_bounds__(kCThreads, 1)
         }
     } else {
         // ---------------- epilogue ----------------
+        // warp quarter q = warp % 4 reads TMEM lanes 32q..32q+31 (rows);
+        // the 4 warps of a quarter take the 16-column chunks round-robin.
+        // Each chunk's residual is loaded before the accumulator is waited
+        // for / read, one chunk ahead.
         pdl_wait();
-        const int e = warp - 2, q = warp & 3, half = e >> 2;
-        const int cbeg = half * (BN / 2);
+        const int e = warp - 2, q = warp & 3, grp = e >> 2;
+        constexpr int kChunks = BN / 16;
         int ti = 0;
+        float4 rnext[4];
+        auto first_chunk_row = [&](int t, int &row, int &n0) {
+            const int mb = t / NT, nb = t - mb * NT;
+            row = mb * kCM + q * 32 + lane;
+            n0 = nb * BN + grp * 16;
+        };
+        if (c < n_tiles && grp < kChunks) {
+            int row, n0;
+            first_chunk_row(c, row, n0);
+            load_res16(p, row, n0, rnext);
+        }
         for (int t = c; t < n_tiles && ok; t += G, ++ti) {
             const int buf = ti & 1, mb = t / NT, nb = t - mb * NT;
             ok = mbar_wait(&sm.tfull[buf], (ti >> 1) & 1, p.err, ERR_WAIT_FULL);
             if (!ok) break;
             tc_fence_after();
             const int row = mb * kCM + q * 32 + lane;
-            for (int cc = 0; cc < BN / 2; cc += 16) {
-                const int n0 = nb * BN + cbeg + cc;
-                if (n0 >= p.N) break;  // warp-uniform
+            for (int cc = grp; cc < kChunks; cc += 4) {
+                const int n0 = nb * BN + cc * 16;
+                float4 rcur[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) rcur[j] = rnext[j];
+                // next chunk: this tile's, or the first of this CTA's next tile
+                if (cc + 4 < kChunks) {
+                    load_res16(p, row, n0 + 64, rnext);
+                } else if (t + G < n_tiles) {
+                    int r2, n2;
+                    first_chunk_row(t + G, r2, n2);
+                    load_res16(p, r2, n2, rnext);
+                }
+                if (n0 >= p.N) continue;  // warp-uniform; the chain of loads ahead goes on
                 int v[16];
-                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + cbeg + cc), v);
-                if (row < p.M) epilogue16(p, row, n0, v);
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + cc * 16), v);
+                if (row < p.M) epilogue16(p, row, n0, v, rcur);
             }
             tc_fence_before();
             __syncwarp();
@@ -420,66 +452,116 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float *x, int C
     }
 }
 
-// ggml_rope_ext mode 0 (adjacent pairs, theta_i = pos * ts^i by recurrence)
-// on every q and k head of the fused qkv rows, in place
-__global__ void __launch_bounds__(128) rope_kernel(float *qkv, int L, int ld, int H, int Hk, int hd, int qs, float ts) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= L * (H + Hk)) return;
-    const int t = idx / (H + Hk), h = idx % (H + Hk);
-    float *v = qkv + (size_t)t * ld + (h < H ? h * hd : qs + (h - H) * hd);
-    float theta = (float)t;
-    for (int i = 0; i < hd; i += 2) {
-        const float c = cosf(theta), s = sinf(theta), x0 = v[i], x1 = v[i + 1];
-        v[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        v[i + 1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-        theta = __fmul_rn(theta, ts);
+// Attention of the post-module transformer for a tile of kAQ query rows of
+// one head: RoPE (ggml_rope_ext mode 0: adjacent pairs, angle pos * ts^i with
+// the angles and their cos / sin taken from a table built on the host by the
+// same float recurrence) on q and k as they are staged in shared memory, then
+// softmax(q.k / sqrt(hd)) over keys [max(0, t-W+1), t] (the window mask, or
+// the causal mask when W <= 0) in the reference's order (all scores, their
+// max, exp, the sum, the normalised weights), times V; fp16 out (the wo
+// product's rounding).  GQA: head h reads kv head h / (H / Hk)
+// (repeat_interleave_heads).  Dot products accumulate in f32.
+constexpr int kAQ = 16;       // query rows per block
+constexpr int kAKC = 64;      // key rows per staged chunk
+constexpr int kAThreads = 128;
+constexpr int kAMaxHd = 128;
+
+// rows [r0, r0 + n) of one head of the fused qkv rows (column offset col),
+// rotated pair by pair, into dst rows of stride hp; threads over (row, pair)
+__device__ __forceinline__ void stage_rope(const float *qkv, int ld, int col, int r0, int n, const float2 *rope,
+                                           int hd, float *dst, int hp) {
+    const int half = hd / 2;
+    for (int e = threadIdx.x; e < n * half; e += blockDim.x) {
+        const int r = e / half, i = e - r * half;
+        const float2 x = *reinterpret_cast<const float2 *>(qkv + (size_t)(r0 + r) * ld + col + 2 * i);
+        const float2 cs = rope[(size_t)(r0 + r) * half + i];
+        dst[r * hp + 2 * i] = __fsub_rn(__fmul_rn(x.x, cs.x), __fmul_rn(x.y, cs.y));
+        dst[r * hp + 2 * i + 1] = __fadd_rn(__fmul_rn(x.x, cs.y), __fmul_rn(x.y, cs.x));
     }
 }
 
-// one (query row, head): softmax(q.k / sqrt(hd)) over keys [max(0, t-W+1), t]
-// (the window mask, or the causal mask when W <= 0), times V; fp16 out (the
-// wo product's rounding).  GQA: head h reads kv head h / (H / Hk)
-// (repeat_interleave_heads).
-__global__ void __launch_bounds__(128) codec_attn_kernel(const float *qkv, int ld, int H, int Hk, int hd, int qs,
-                                                         int W, float scale, __half *out, int ldo) {
+__global__ void __launch_bounds__(kAThreads) codec_attn_kernel(const float *qkv, int ld, int L, int H, int Hk, int hd,
+                                                               int qs, int W, float scale, const float2 *rope,
+                                                               __half *out, int ldo, int span) {
     pdl_launch_dependents();
     pdl_wait();
-    extern __shared__ float sh[];  // q [hd], p [keys]
-    __shared__ double redd[4];
-    __shared__ float redf[4];
-    const int t = blockIdx.x, h = blockIdx.y, kh = h / (H / Hk), tid = threadIdx.x;
-    const int k0 = W > 0 ? max(0, t - W + 1) : 0, nk = t - k0 + 1;
+    extern __shared__ float sh[];
+    const int hp = hd + 1;               // padded rows: conflict-free column reads
+    float *q = sh;                       // [kAQ][hp]
+    float *kv = q + kAQ * hp;            // [kAKC][hp] (K, then V)
+    float *sc = kv + kAKC * hp;          // [kAQ][span] scores / weights
+    const int q0 = blockIdx.x * kAQ, h = blockIdx.y, kh = h / (H / Hk), tid = threadIdx.x;
+    const int nq = min(kAQ, L - q0);
+    const int kbeg = W > 0 ? max(0, q0 - W + 1) : 0, kend = q0 + nq;  // keys [kbeg, kend)
     const int ks = Hk * hd;
-    float *q = sh, *p = sh + hd;
-    for (int d = tid; d < hd; d += blockDim.x) q[d] = qkv[(size_t)t * ld + h * hd + d];
-    __syncthreads();
-    float mx = -INFINITY;
-    for (int j = tid; j < nk; j += blockDim.x) {
-        const float *kr = qkv + (size_t)(k0 + j) * ld + qs + kh * hd;
-        double s = 0.0;
-        for (int d = 0; d < hd; ++d) s += (double)q[d] * (double)kr[d];
-        const float v = __fmul_rn((float)s, scale);
-        p[j] = v;
-        mx = fmaxf(mx, v);
+    stage_rope(qkv, ld, h * hd, q0, nq, rope, hd, q, hp);
+    // scores
+    for (int c0 = kbeg; c0 < kend; c0 += kAKC) {
+        const int nk = min(kAKC, kend - c0);
+        __syncthreads();
+        stage_rope(qkv, ld, qs + kh * hd, c0, nk, rope, hd, kv, hp);
+        __syncthreads();
+        for (int e = tid; e < kAQ * kAKC; e += kAThreads) {
+            const int qi = e / kAKC, kj = e % kAKC;
+            if (qi >= nq || kj >= nk) continue;
+            const int t = q0 + qi, key = c0 + kj;
+            const int lo = W > 0 ? max(0, t - W + 1) : 0;
+            float v = -INFINITY;
+            if (key >= lo && key <= t) {
+                float s = 0.f;
+                for (int d = 0; d < hd; ++d) s = fmaf(q[qi * hp + d], kv[kj * hp + d], s);
+                v = __fmul_rn(s, scale);
+            }
+            sc[qi * span + (key - kbeg)] = v;
+        }
     }
-    mx = block_max_f(mx, redf);
-    double sum = 0.0;
-    for (int j = tid; j < nk; j += blockDim.x) {
-        const float e = det_expf(__fsub_rn(p[j], mx));
-        p[j] = e;
-        sum += (double)e;
-    }
-    sum = block_sum_d(sum, redd);
-    const float inv = (float)(1.0 / sum);
-    for (int j = tid; j < nk; j += blockDim.x) p[j] = __fmul_rn(p[j], inv);
     __syncthreads();
-    for (int d = tid; d < hd; d += blockDim.x) {
-        const float *vc = qkv + (size_t)k0 * ld + qs + ks + kh * hd + d;
-        double o = 0.0;
-        for (int j = 0; j < nk; ++j) o += (double)p[j] * (double)vc[(size_t)j * ld];
-        out[(size_t)t * ldo + h * hd + d] = __float2half_rn((float)o);
+    // softmax per query row: one warp per row
+    const int warp = tid >> 5, lane = tid & 31, nkeys = kend - kbeg;
+    for (int qi = warp; qi < nq; qi += kAThreads / 32) {
+        float *row = sc + qi * span;
+        float mx = -INFINITY;
+        for (int j = lane; j < nkeys; j += 32) mx = fmaxf(mx, row[j]);
+        mx = warp_max(mx);
+        double sum = 0.0;
+        for (int j = lane; j < nkeys; j += 32) {
+            const float e = row[j] == -INFINITY ? 0.f : det_expf(__fsub_rn(row[j], mx));
+            row[j] = e;
+            sum += (double)e;
+        }
+        sum = warp_sum_d(sum);
+        const float inv = (float)(1.0 / sum);
+        for (int j = lane; j < nkeys; j += 32) row[j] = __fmul_rn(row[j], inv);
+    }
+    // weights x V
+    float acc[kAQ * kAMaxHd / kAThreads];
+    const int per = (kAQ * hd + kAThreads - 1) / kAThreads;
+#pragma unroll
+    for (int i = 0; i < kAQ * kAMaxHd / kAThreads; ++i) acc[i] = 0.f;
+    for (int c0 = kbeg; c0 < kend; c0 += kAKC) {
+        const int nk = min(kAKC, kend - c0);
+        __syncthreads();
+        for (int e = tid; e < nk * hd; e += kAThreads) {
+            const int r = e / hd, d = e % hd;
+            kv[r * hp + d] = qkv[(size_t)(c0 + r) * ld + qs + ks + kh * hd + d];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < kAQ * kAMaxHd / kAThreads; ++i) {
+            if (i >= per) break;
+            const int e = tid + i * kAThreads, qi = e / hd, d = e % hd;
+            if (qi >= nq) continue;
+            const float *w = sc + qi * span + (c0 - kbeg);
+            float a = acc[i];
+            for (int j = 0; j < nk; ++j) a = fmaf(w[j], kv[j * hp + d], a);
+            acc[i] = a;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kAQ * kAMaxHd / kAThreads; ++i) {
+        if (i >= per) break;
+        const int e = tid + i * kAThreads, qi = e / hd, d = e % hd;
+        if (qi < nq) out[(size_t)(q0 + qi) * ldo + h * hd + d] = __float2half_rn(acc[i]);
     }
 }
 
@@ -522,26 +604,42 @@ __global__ void __launch_bounds__(256) dwconv_ln_kernel(const float *x, int C, c
             __float2half_rn(__fadd_rn(__fmul_rn(__fmul_rn(yrow[c], sc), __ldg(lw + c)), __ldg(lb + c)));
 }
 
-// output conv (one channel out, K taps, input already snake'd and fp16) + tanh
+// output conv (one channel out, K taps, input already snake'd and fp16) + tanh:
+// the input rows of a block's samples staged in shared memory with an odd
+// word stride (conflict-free half2 reads), the weights alongside
 constexpr int kOutRows = 256;
 
 __global__ void __launch_bounds__(kOutRows) codec_out_kernel(const __half *x, int L, int C, const float *w, int K,
                                                              float bias, float *audio) {
     pdl_launch_dependents();
     pdl_wait();
-    extern __shared__ __half tile[];  // (kOutRows + K - 1) x C
+    extern __shared__ float osm[];
+    const int cs = C + 2;                           // halves per staged row (C % 2 == 0: odd word count)
+    float *ws = osm;                                // [K][C]
+    __half *tile = reinterpret_cast<__half *>(osm + K * C);  // (kOutRows + K - 1) x cs
     const int t0 = blockIdx.x * kOutRows, rows = kOutRows + K - 1;
-    for (int e = threadIdx.x; e < rows * C; e += blockDim.x) {
-        const int r = e / C, ch = e - r * C, src = t0 - (K - 1) + r;
-        tile[e] = (src >= 0 && src < L) ? x[(size_t)src * C + ch] : __float2half_rn(0.f);
+    for (int e = threadIdx.x; e < K * C; e += blockDim.x) {
+        const int k = e / C, i = e % C;
+        ws[e] = w[(size_t)i * K + k];
+    }
+    for (int e = threadIdx.x; e < rows * (C / 2); e += blockDim.x) {
+        const int r = e / (C / 2), i2 = e % (C / 2), src = t0 - (K - 1) + r;
+        const __half2 v = (src >= 0 && src < L) ? reinterpret_cast<const __half2 *>(x + (size_t)src * C)[i2]
+                                                : __floats2half2_rn(0.f, 0.f);
+        reinterpret_cast<__half2 *>(tile + (size_t)r * cs)[i2] = v;
     }
     __syncthreads();
     const int t = t0 + threadIdx.x;
     if (t >= L) return;
     float acc = 0.f;
     for (int k = 0; k < K; ++k) {
-        const __half *xr = tile + (size_t)(threadIdx.x + k) * C;
-        for (int i = 0; i < C; ++i) acc = fmaf(__ldg(w + (size_t)i * K + k), __half2float(xr[i]), acc);
+        const __half2 *xr = reinterpret_cast<const __half2 *>(tile + (size_t)(threadIdx.x + k) * cs);
+        const float *wk = ws + k * C;
+        for (int i2 = 0; i2 < C / 2; ++i2) {
+            const float2 v = __half22float2(xr[i2]);
+            acc = fmaf(wk[2 * i2], v.x, acc);
+            acc = fmaf(wk[2 * i2 + 1], v.y, acc);
+        }
     }
     audio[t] = tanhf(__fadd_rn(acc, bias));
 }
@@ -637,6 +735,7 @@ struct s2k_codec {
     size_t ws_tr = 0, ws_dec = 0;
     int *d_codes = nullptr;
     float *X = nullptr, *QKV = nullptr, *P = nullptr, *audio = nullptr;
+    float *rope = nullptr;  // [position][head_dim / 2] (cos, sin)
     __half *N16 = nullptr, *G16 = nullptr, *S16 = nullptr, *T16 = nullptr, *HLa = nullptr, *HLb = nullptr;
     std::vector<void *> ws_allocs;
 };
@@ -868,18 +967,21 @@ cudaError_t setup() {
     return e;
 }
 
-// Tile width: the fewest waves of BN-proportional tiles over the SMs, then
-// the wider tile (fewer A re-reads).
-int pick_bn(int M, int N, int sms) {
+// Tile width from a per-SM cost model: a tile takes the longest of its MMA
+// time (128 x BN x K MACs at ~4096 per cycle), its operand traffic
+// ((128 + BN) x K fp16 from L2 at ~64 bytes per cycle) and its epilogue
+// (~0.3 cycle per output), and the tiles run in waves over the SMs.
+int pick_bn(int M, int N, int K, int sms) {
     static const int cands[] = {256, 192, 128, 96, 64, 32};
-    const int MT = (M + kCM - 1) / kCM;
+    const long long MT = (M + kCM - 1) / kCM;
     int best = 256;
-    long long best_cost = -1;
+    double best_cost = -1;
     for (int bn : cands) {
         if ((bn == 32 && N > 32) || (bn > N && bn != 32)) continue;
-        const long long tiles = (long long)MT * ((N + bn - 1) / bn);
-        const long long cost = (tiles + sms - 1) / sms * bn;
-        if (best_cost < 0 || cost < best_cost) {
+        const long long tiles = MT * ((N + bn - 1) / bn);
+        const double mma = 128.0 * bn * K / 4096.0, load = (128.0 + bn) * K * 2.0 / 64.0, epi = 128.0 * bn * 0.3;
+        const double cost = (double)((tiles + sms - 1) / sms) * std::max(mma, std::max(load, epi));
+        if (best_cost < 0 || cost < best_cost * 0.999) {
             best_cost = cost;
             best = bn;
         }
@@ -917,7 +1019,7 @@ s2k_status gemm(s2k_codec *c, const ARef &a, const GW &g, int M, const Epi &e) {
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return fail(S2K_ERR_CUDA, "codec: activation tensor map (%d x %d, ld %d)", a.rows, a.width, a.ld);
     }
-    const int BN = pick_bn(M, g.N, c->num_sms);
+    const int BN = pick_bn(M, g.N, g.taps * g.kp, c->num_sms);
     {
         const cuuint64_t dims[2] = {(cuuint64_t)g.taps * g.kp, (cuuint64_t)g.N};
         const cuuint64_t strides[1] = {(cuuint64_t)g.taps * g.kp * 2};
@@ -1018,10 +1120,26 @@ s2k_status ensure_ws(s2k_codec *c, int n_tr, int n_dec) {
         (rc = dev_alloc(c, &c->G16, tr * (size_t)c->ff, c->ws_allocs)) ||
         (rc = dev_alloc(c, &c->P, p32, c->ws_allocs)) || (rc = dev_alloc(c, &c->S16, s16, c->ws_allocs)) ||
         (rc = dev_alloc(c, &c->T16, t16, c->ws_allocs)) || (rc = dev_alloc(c, &c->HLa, hl, c->ws_allocs)) ||
-        (rc = dev_alloc(c, &c->HLb, hl, c->ws_allocs)) || (rc = dev_alloc(c, &c->audio, L, c->ws_allocs))) {
+        (rc = dev_alloc(c, &c->HLb, hl, c->ws_allocs)) || (rc = dev_alloc(c, &c->audio, L, c->ws_allocs)) ||
+        (rc = dev_alloc(c, &c->rope, tr * (size_t)c->hd, c->ws_allocs))) {
         for (void *p : c->ws_allocs) cudaFree(p);
         c->ws_allocs.clear();
         return rc;
+    }
+    // RoPE angles of every position by ggml's float recurrence theta_{i+1} =
+    // theta_i * base^(-2/hd) from theta_0 = pos, and their cos / sin
+    {
+        const int half = c->hd / 2;
+        std::vector<float> tab(tr * (size_t)c->hd);
+        for (size_t pos = 0; pos < tr; ++pos) {
+            float theta = (float)pos;
+            for (int i = 0; i < half; ++i) {
+                tab[(pos * half + i) * 2] = ::cosf(theta);
+                tab[(pos * half + i) * 2 + 1] = ::sinf(theta);
+                theta *= c->rope_ts;
+            }
+        }
+        CU(cudaMemcpy(c->rope, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice));
     }
     c->ws_tr = tr;
     c->ws_dec = dec;
@@ -1060,15 +1178,12 @@ s2k_status run_window(s2k_codec *c, int n_tr, int f0) {
         e.y32 = c->QKV;
         e.ldy32 = qkvs;
         if ((rc = gemm(c, {c->N16, n_tr, c->dim, c->dim}, ly.wqkv, n_tr, e))) return rc;
-        const int nrope = n_tr * (c->H + c->Hk);
-        if ((rc = launch(c, rope_kernel, dim3((nrope + 127) / 128), dim3(128), 0, c->QKV, n_tr, qkvs, c->H, c->Hk,
-                         c->hd, c->qs, c->rope_ts)))
-            return rc;
-        const int keys = c->W > 0 ? std::min(c->W, n_tr) : n_tr;
-        if ((size_t)(c->hd + keys) * sizeof(float) > (size_t)kSmallSmemMax)
-            return fail(S2K_ERR_UNSUPPORTED, "codec: attention over %d keys", keys);
-        if ((rc = launch(c, codec_attn_kernel, dim3(n_tr, c->H), dim3(128), (size_t)(c->hd + keys) * sizeof(float),
-                         (const float *)c->QKV, qkvs, c->H, c->Hk, c->hd, c->qs, c->W, scale, c->N16, c->qs)))
+        const int span = (c->W > 0 ? std::min(c->W, n_tr) : n_tr) + kAQ - 1;
+        const size_t asmem = ((size_t)(kAQ + kAKC) * (c->hd + 1) + (size_t)kAQ * span) * sizeof(float);
+        if (asmem > (size_t)kSmallSmemMax) return fail(S2K_ERR_UNSUPPORTED, "codec: attention over %d keys", span);
+        if ((rc = launch(c, codec_attn_kernel, dim3((n_tr + kAQ - 1) / kAQ, c->H), dim3(kAThreads), asmem,
+                         (const float *)c->QKV, qkvs, n_tr, c->H, c->Hk, c->hd, c->qs, c->W, scale,
+                         (const float2 *)c->rope, c->N16, c->qs, span)))
             return rc;
         Epi eo;
         eo.gamma = ly.attn_gamma;
@@ -1190,10 +1305,11 @@ s2k_status run_window(s2k_codec *c, int n_tr, int f0) {
         }
         std::swap(hl_in, hl_out);
     }
-    if ((size_t)(kOutRows + c->out_K - 1) * c->out_C * sizeof(__half) > (size_t)kSmallSmemMax)
+    const size_t osmem = (size_t)c->out_K * c->out_C * sizeof(float) +
+                         (size_t)(kOutRows + c->out_K - 1) * (c->out_C + 2) * sizeof(__half);
+    if (osmem > (size_t)kSmallSmemMax)
         return fail(S2K_ERR_UNSUPPORTED, "codec: output conv of %d taps over %d channels", c->out_K, c->out_C);
-    return launch(c, codec_out_kernel, dim3((L + kOutRows - 1) / kOutRows), dim3(kOutRows),
-                  (size_t)(kOutRows + c->out_K - 1) * c->out_C * sizeof(__half), (const __half *)c->S16, L, c->out_C,
+    return launch(c, codec_out_kernel, dim3((L + kOutRows - 1) / kOutRows), dim3(kOutRows), osmem, (const __half *)c->S16, L, c->out_C,
                   (const float *)c->out_w, c->out_K, c->out_b, c->audio);
 }
 
@@ -1268,7 +1384,7 @@ s2k_status finalize(s2k_codec *c) {
     // transformer (as many layers as the file holds, src/s2_codec.cpp:300-303)
     c->dim = hp.rvq_dim;
     c->hd = hp.rvq_head_dim;
-    if (c->dim != c->C0 || c->hd < 2 || c->hd % 2 || c->dim % c->hd)
+    if (c->dim != c->C0 || c->hd < 2 || c->hd % 2 || c->hd > kAMaxHd || c->dim % c->hd)
         return fail(S2K_ERR_UNSUPPORTED, "codec: transformer dim %d / head_dim %d", c->dim, c->hd);
     c->H = c->dim / c->hd;
     c->Hk = hp.rvq_n_local_heads > 0 ? hp.rvq_n_local_heads : c->H;
@@ -1277,7 +1393,7 @@ s2k_status finalize(s2k_codec *c) {
     c->kvs = c->Hk * c->hd;
     c->W = hp.rvq_window_size;
     c->eps = hp.rvq_norm_eps;
-    c->rope_ts = std::pow(hp.rvq_rope_base, -2.0f / (float)c->hd);
+    c->rope_ts = ::powf(hp.rvq_rope_base, -2.0f / (float)c->hd);
     for (int l = 0;; ++l) {
         const std::string p = "quantizer.post_module.layers." + std::to_string(l) + ".";
         if (!find(c, p + "attention.wqkv.weight")) break;
