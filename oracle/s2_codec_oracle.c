@@ -21,7 +21,7 @@
  * f32 operands after the reference's casts), mul_mat with F16 weights (the
  * activation rounded to fp16, ggml's vec_dot_type), norm / rms_norm,
  * gelu_erf, rope mode 0 with the theta *= base^(-2/n_dims) recurrence,
- * soft_max.  exp is so_det_expf, as in the CUDA kernels.  Arithmetic is float
+ * soft_max.  exp and sin are so_det_expf / so_det_sinf, as in the CUDA kernels.  Arithmetic is float
  * with every dot product and reduction accumulated in double; parity with the
  * CUDA path is to a tolerance (audio samples), not bit for bit.
  *
@@ -136,12 +136,13 @@ static void linear(const float *x, int L, int in, const sc_tensor *w, const sc_t
     free(xr);
 }
 
-/* snake: x + sin(a x)^2 / a, per channel (src/s2_codec.cpp:197-204) */
+/* snake: x + sin(a x)^2 / a, per channel (src/s2_codec.cpp:197-204); sin is
+ * so_det_sinf, as in the CUDA kernels */
 static void snake(float *x, int L, int C, const sc_tensor *alpha) {
     for (int t = 0; t < L; ++t)
         for (int c = 0; c < C; ++c) {
             const float a = alpha->data[c], v = x[(size_t)t * C + c];
-            const float s = sinf(a * v);
+            const float s = so_det_sinf(a * v);
             x[(size_t)t * C + c] = v + (s * s) / a;
         }
 }

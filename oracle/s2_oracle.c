@@ -141,6 +141,28 @@ float so_det_expf(float x) {
     return ldexpf(p, (int)k);
 }
 
+/* sin with the same float steps as the CUDA det_sinf (s2k_common.cuh):
+ * Cody-Waite reduction by pi in three parts, the Taylor series of sin to
+ * degree 13 on |r| <= pi/2, negated for odd multiples; the library sinf
+ * beyond |x| = 6400.  (The reference's ggml_sin calls sinf; the two agree to
+ * an ulp or two.) */
+float so_det_sinf(float x) {
+    if (!(fabsf(x) <= 6400.0f)) return sinf(x);
+    const float k = rintf(x * 0.318309873342514038f);
+    float r = x - k * 3.140625f;
+    r = r - k * 9.6750259399414062e-4f;
+    r = r - k * 1.5099580252808664e-7f;
+    const float r2 = r * r;
+    float p = 1.60590443720742825917e-10f;
+    p = p * r2 + -2.50521079436794025241e-8f;
+    p = p * r2 + 2.75573188446287531406e-6f;
+    p = p * r2 + -1.98412701138295233250e-4f;
+    p = p * r2 + 8.33333376795053482056e-3f;
+    p = p * r2 + -1.66666671633720397949e-1f;
+    const float v = r + (r * r2) * p;
+    return ((int)k & 1) ? -v : v;
+}
+
 /* ------------------------------------------------------------------------ */
 /* block formats                                                             */
 /* ------------------------------------------------------------------------ */

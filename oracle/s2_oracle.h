@@ -114,6 +114,7 @@ void so_matvec(int type, const void *w, int64_t rows, int64_t n, const float *x,
 uint16_t so_fp32_to_fp16(float f);
 /* exp(x) by a fixed float operation sequence shared with the CUDA kernels */
 float so_det_expf(float x);
+float so_det_sinf(float x);
 float so_fp16_to_fp32(uint16_t h);
 void so_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);
 double so_philox_uniform(uint64_t seed, uint32_t frame, uint32_t purpose, uint32_t seq);

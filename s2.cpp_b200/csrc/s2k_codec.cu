@@ -63,11 +63,12 @@ constexpr int kCK = 64;   // fp16 columns per stage (one 128-byte swizzle row)
 constexpr int kCEpiWarps = 16;  // 4 per TMEM lane quarter: enough warps in flight to hide L2 latency
 constexpr int kCThreads = (2 + kCEpiWarps) * 32;
 constexpr uint32_t kCStageA = kCM * kCK * 2;  // 16 KB
+constexpr int kScr = 17;  // floats per scratch row (odd: conflict-free row-per-lane reads)
 
 template <int BN>
 struct CCfg {
     static constexpr uint32_t kStageB = BN * kCK * 2;
-    static constexpr int kFit = (int)((200u * 1024u) / (kCStageA + kStageB));
+    static constexpr int kFit = (int)((184u * 1024u) / (kCStageA + kStageB));
     static constexpr int kStages = kFit < 8 ? kFit : 8;
     static constexpr uint32_t kAlloc = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
 };
@@ -77,6 +78,7 @@ struct CSmem {
     alignas(1024) uint8_t a[CCfg<BN>::kStages][kCStageA];
     alignas(1024) uint8_t b[CCfg<BN>::kStages][CCfg<BN>::kStageB];
     uint64_t full[CCfg<BN>::kStages], empty[CCfg<BN>::kStages];
+    float scratch[kCEpiWarps][32 * kScr];  // per epilogue warp: row <-> coalesced transposes
     uint64_t tfull[2], tempty[2], mdone;
     uint32_t tmem_base;
 };
@@ -85,6 +87,19 @@ enum : int { ACT_NONE = 0, ACT_GELU = 1, ACT_SWIGLU = 2 };
 // 16-bit output of the epilogue: none, fp16(y), fp16(snake(y)), the exact
 // pair (hi, lo) of y, or of snake(y)
 enum : int { O16_NONE = 0, O16_PLAIN = 1, O16_SNAKE = 2, O16_HILO = 3, O16_SNAKE_HILO = 4 };
+
+// The epilogue of a launch as compile-time features (one kernel per
+// combination the decode uses: a small, branch-free epilogue per launch)
+enum : int { F_BIAS = 1, F_GAMMA = 2, F_RES = 4, F_Y32 = 8, F_GELU = 16, F_SWIGLU = 32 };
+constexpr int f_o16(int o16) { return o16 << 6; }
+template <int F>
+struct EpiF {
+    static constexpr bool bias = (F & F_BIAS) != 0, gamma = (F & F_GAMMA) != 0, res = (F & F_RES) != 0,
+                          y32 = (F & F_Y32) != 0, gelu = (F & F_GELU) != 0, swiglu = (F & F_SWIGLU) != 0;
+    static constexpr int o16 = (F >> 6) & 7;
+    static constexpr bool snake = o16 == O16_SNAKE || o16 == O16_SNAKE_HILO;
+    static constexpr bool hilo = o16 == O16_HILO || o16 == O16_SNAKE_HILO;
+};
 
 struct CGemm {
     int M, N;            // output rows (time), columns
@@ -125,7 +140,7 @@ __device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity, const
 
 // snake (src/s2_codec.cpp:197-204): x + sin(alpha x)^2 / alpha
 __device__ __forceinline__ float snake_f(float x, float a) {
-    const float s = sinf(__fmul_rn(a, x));
+    const float s = det_sinf(__fmul_rn(a, x));
     return __fadd_rn(x, __fdiv_rn(__fmul_rn(s, s), a));
 }
 
@@ -143,17 +158,109 @@ __device__ __forceinline__ void store_h16(__half *dst, const float (&z)[16]) {
     reinterpret_cast<uint4 *>(dst)[1] = s[1];
 }
 
-// the residual of 16 columns (loaded ahead of the accumulator)
-__device__ __forceinline__ void load_res16(const CGemm &p, int t, int n0, float4 (&r)[4]) {
-    if (!p.res || t >= p.M || n0 >= p.N) return;
-    const float4 *r4 = reinterpret_cast<const float4 *>(p.res + (size_t)t * p.ldres + n0);
+// The epilogue works on chunks of 32 rows (one per lane: the TMEM lane
+// quarter of the warp) x 16 columns.  Global loads and stores of a chunk go
+// through the warp's scratch so that they are coalesced: lane l moves row
+// l/4 + 8i, 16-byte piece l%4 (fp32), or row l/2 + 16i, piece l%2 (fp16).
+
+// residual of a chunk, coalesced layout (issued one chunk ahead)
+__device__ __forceinline__ void load_res_chunk(const CGemm &p, int row0, int n0, float4 (&r)[4]) {
+    if (!p.res || n0 >= p.N) return;
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) r[j] = __ldcg(r4 + j);
+    for (int i = 0; i < 4; ++i) {
+        const int rr = row0 + lane / 4 + 8 * i;
+        if (rr < p.M) r[i] = __ldcg(reinterpret_cast<const float4 *>(p.res + (size_t)rr * p.ldres + n0) + (lane & 3));
+    }
 }
 
-// 16 accumulator columns n0..n0+15 of output row t
-__device__ __forceinline__ void epilogue16(const CGemm &p, int t, int n0, const int (&v)[16], const float4 (&r)[4]) {
-    if (p.act == ACT_SWIGLU) {  // columns: 8 gates then the 8 matching ups
+// coalesced layout -> this lane's row
+__device__ __forceinline__ void rows_from_coal(const float4 (&r)[4], float *scr, float (&out)[16]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float *d = scr + (lane / 4 + 8 * i) * kScr + 4 * (lane & 3);
+        d[0] = r[i].x;
+        d[1] = r[i].y;
+        d[2] = r[i].z;
+        d[3] = r[i].w;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) out[j] = scr[lane * kScr + j];
+    __syncwarp();
+}
+
+// this lane's row of fp32 -> coalesced stores
+__device__ __forceinline__ void store_chunk32(const float (&y)[16], float *scr, float *dst, int ld, int row0, int M,
+                                              int n0) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) scr[lane * kScr + j] = y[j];
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int rr = lane / 4 + 8 * i;
+        const float *sr = scr + rr * kScr + 4 * (lane & 3);
+        if (row0 + rr < M)
+            reinterpret_cast<float4 *>(dst + (size_t)(row0 + rr) * ld + n0)[lane & 3] = make_float4(sr[0], sr[1], sr[2], sr[3]);
+    }
+    __syncwarp();
+}
+
+// this lane's row rounded to fp16 -> coalesced stores (two lanes per row)
+__device__ __forceinline__ void store_chunk16(const float (&z)[16], float *scr, __half *dst, int ld, int row0, int M,
+                                              int n0) {
+    const int lane = threadIdx.x & 31;
+    uint32_t *s32 = reinterpret_cast<uint32_t *>(scr);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const __half2 h = __floats2half2_rn(z[2 * i], z[2 * i + 1]);
+        s32[lane * kScr + i] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int rr = lane / 2 + 16 * i, part = lane & 1;
+        const uint32_t *sr = s32 + rr * kScr + 4 * part;
+        if (row0 + rr < M)
+            reinterpret_cast<uint4 *>(dst + (size_t)(row0 + rr) * ld + n0)[part] = make_uint4(sr[0], sr[1], sr[2], sr[3]);
+    }
+    __syncwarp();
+}
+
+// per-channel vectors of a chunk (loaded before the accumulator is read)
+template <int F>
+struct ChunkVecs {
+    float bias[EpiF<F>::bias ? 16 : 1], gamma[EpiF<F>::gamma ? 16 : 1], alpha[EpiF<F>::snake ? 16 : 1];
+};
+
+template <int F>
+__device__ __forceinline__ void load_vecs(const CGemm &p, int ch, ChunkVecs<F> &cv) {
+    using E = EpiF<F>;
+    if constexpr (E::bias) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) cv.bias[j] = __ldg(p.bias + ch + j);
+    }
+    if constexpr (E::gamma) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) cv.gamma[j] = __ldg(p.gamma + ch + j);
+    }
+    if constexpr (E::snake) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) cv.alpha[j] = __ldg(p.alpha + ch + j);
+    }
+}
+
+// 16 accumulator columns n0..n0+15 of the warp's 32 rows from row0 (this
+// lane: row0 + lane); r: the chunk's residual in the coalesced layout
+template <int F>
+__device__ __forceinline__ void epilogue16(const CGemm &p, int row0, int n0, const int (&v)[16], const float4 (&r)[4],
+                                           const ChunkVecs<F> &cv, float *scr) {
+    using E = EpiF<F>;
+    const int lane = threadIdx.x & 31, t = row0 + lane;
+    if constexpr (E::swiglu) {  // columns: 8 gates then the 8 matching ups
+        if (t >= p.M) return;
         __half2 h[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -162,55 +269,45 @@ __device__ __forceinline__ void epilogue16(const CGemm &p, int t, int n0, const 
             h[i] = __floats2half2_rn(o0, o1);
         }
         *reinterpret_cast<uint4 *>(p.y16 + (size_t)t * p.ldy16 + n0 / 2) = *reinterpret_cast<const uint4 *>(h);
-        return;
-    }
-    const int ch = n0 % p.cout;  // cout % 16 == 0: no wrap inside the chunk
-    float y[16];
+    } else {
+        float y[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) y[j] = __int_as_float(v[j]);
-    if (p.bias) {
+        for (int j = 0; j < 16; ++j) y[j] = __int_as_float(v[j]);
+        if constexpr (E::bias) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) y[j] = __fadd_rn(y[j], __ldg(p.bias + ch + j));
-    }
-    if (p.act == ACT_GELU) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) y[j] = gelu_erf_f(y[j]);
-    }
-    if (p.gamma) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) y[j] = __fmul_rn(y[j], __ldg(p.gamma + ch + j));
-    }
-    if (p.res) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            y[4 * j] = __fadd_rn(r[j].x, y[4 * j]);
-            y[4 * j + 1] = __fadd_rn(r[j].y, y[4 * j + 1]);
-            y[4 * j + 2] = __fadd_rn(r[j].z, y[4 * j + 2]);
-            y[4 * j + 3] = __fadd_rn(r[j].w, y[4 * j + 3]);
+            for (int j = 0; j < 16; ++j) y[j] = __fadd_rn(y[j], cv.bias[j]);
         }
-    }
-    if (p.y32) {
-        float4 *d4 = reinterpret_cast<float4 *>(p.y32 + (size_t)t * p.ldy32 + n0);
+        if constexpr (E::gelu) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) d4[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-    }
-    if (p.o16 != O16_NONE) {
-        if (p.o16 == O16_SNAKE || p.o16 == O16_SNAKE_HILO) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) y[j] = snake_f(y[j], __ldg(p.alpha + ch + j));
+            for (int j = 0; j < 16; ++j) y[j] = gelu_erf_f(y[j]);
         }
-        __half *dst = p.y16 + (size_t)t * p.ldy16 + n0;
-        store_h16(dst, y);
-        if (p.o16 == O16_HILO || p.o16 == O16_SNAKE_HILO) {
-            float lo[16];
+        if constexpr (E::gamma) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) lo[j] = __fsub_rn(y[j], __half2float(__float2half_rn(y[j])));
-            store_h16(dst + p.lo_off, lo);
+            for (int j = 0; j < 16; ++j) y[j] = __fmul_rn(y[j], cv.gamma[j]);
+        }
+        if constexpr (E::res) {
+            float rr[16];
+            rows_from_coal(r, scr, rr);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) y[j] = __fadd_rn(rr[j], y[j]);
+        }
+        if constexpr (E::y32) store_chunk32(y, scr, p.y32, p.ldy32, row0, p.M, n0);
+        if constexpr (E::o16 != O16_NONE) {
+            if constexpr (E::snake) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) y[j] = snake_f(y[j], cv.alpha[j]);
+            }
+            store_chunk16(y, scr, p.y16, p.ldy16, row0, p.M, n0);
+            if constexpr (E::hilo) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) y[j] = __fsub_rn(y[j], __half2float(__float2half_rn(y[j])));
+                store_chunk16(y, scr, p.y16 + p.lo_off, p.ldy16, row0, p.M, n0);
+            }
         }
     }
 }
 
-template <int BN>
+template <int BN, int F>
 __global__ void __launch_bounds__(kCThreads, 1)
     codec_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, CGemm p) {
     constexpr int S = CCfg<BN>::kStages;
@@ -324,22 +421,23 @@ __global__ void __launch_bounds__(kCThreads, 1)
         constexpr int kChunks = BN / 16;
         int ti = 0;
         float4 rnext[4];
-        auto first_chunk_row = [&](int t, int &row, int &n0) {
+        float *scr = sm.scratch[e];
+        auto first_chunk = [&](int t, int &row0, int &n0) {
             const int mb = t / NT, nb = t - mb * NT;
-            row = mb * kCM + q * 32 + lane;
+            row0 = mb * kCM + q * 32;
             n0 = nb * BN + grp * 16;
         };
         if (c < n_tiles && grp < kChunks) {
-            int row, n0;
-            first_chunk_row(c, row, n0);
-            load_res16(p, row, n0, rnext);
+            int r0, n0;
+            first_chunk(c, r0, n0);
+            load_res_chunk(p, r0, n0, rnext);
         }
         for (int t = c; t < n_tiles && ok; t += G, ++ti) {
             const int buf = ti & 1, mb = t / NT, nb = t - mb * NT;
             ok = mbar_wait(&sm.tfull[buf], (ti >> 1) & 1, p.err, ERR_WAIT_FULL);
             if (!ok) break;
             tc_fence_after();
-            const int row = mb * kCM + q * 32 + lane;
+            const int row0 = mb * kCM + q * 32;
             for (int cc = grp; cc < kChunks; cc += 4) {
                 const int n0 = nb * BN + cc * 16;
                 float4 rcur[4];
@@ -347,16 +445,18 @@ __global__ void __launch_bounds__(kCThreads, 1)
                 for (int j = 0; j < 4; ++j) rcur[j] = rnext[j];
                 // next chunk: this tile's, or the first of this CTA's next tile
                 if (cc + 4 < kChunks) {
-                    load_res16(p, row, n0 + 64, rnext);
+                    load_res_chunk(p, row0, n0 + 64, rnext);
                 } else if (t + G < n_tiles) {
                     int r2, n2;
-                    first_chunk_row(t + G, r2, n2);
-                    load_res16(p, r2, n2, rnext);
+                    first_chunk(t + G, r2, n2);
+                    load_res_chunk(p, r2, n2, rnext);
                 }
                 if (n0 >= p.N) continue;  // warp-uniform; the chain of loads ahead goes on
+                ChunkVecs<F> cv;
+                load_vecs<F>(p, n0 % p.cout, cv);  // cout % 16 == 0: no wrap inside the chunk
                 int v[16];
                 tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + cc * 16), v);
-                if (row < p.M) epilogue16(p, row, n0, v, rcur);
+                if (row0 < p.M) epilogue16<F>(p, row0, n0, v, rcur, cv, scr);  // warp-uniform
             }
             tc_fence_before();
             __syncwarp();
@@ -461,9 +561,9 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float *x, int C
 // max, exp, the sum, the normalised weights), times V; fp16 out (the wo
 // product's rounding).  GQA: head h reads kv head h / (H / Hk)
 // (repeat_interleave_heads).  Dot products accumulate in f32.
-constexpr int kAQ = 16;       // query rows per block
+constexpr int kAQ = 8;        // query rows per block
 constexpr int kAKC = 64;      // key rows per staged chunk
-constexpr int kAThreads = 128;
+constexpr int kAThreads = 256;
 constexpr int kAMaxHd = 128;
 
 // rows [r0, r0 + n) of one head of the fused qkv rows (column offset col),
@@ -942,23 +1042,10 @@ cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st, 
 bool g_setup_done = false;
 constexpr int kSmallSmemMax = 200 * 1024;  // dynamic shared memory of the non-GEMM kernels
 
-template <int BN>
-cudaError_t setup_one() {
-    return cudaFuncSetAttribute(codec_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)(sizeof(CSmem<BN>) + 1024));
-}
-
 cudaError_t setup() {
     if (g_setup_done) return cudaSuccess;
     if (!encode_fn()) return cudaErrorNotSupported;
-    cudaError_t e = setup_one<32>();
-    if (e == cudaSuccess) e = setup_one<64>();
-    if (e == cudaSuccess) e = setup_one<96>();
-    if (e == cudaSuccess) e = setup_one<128>();
-    if (e == cudaSuccess) e = setup_one<192>();
-    if (e == cudaSuccess) e = setup_one<256>();
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(codec_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmallSmemMax);
+    cudaError_t e = cudaFuncSetAttribute(codec_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmallSmemMax);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(codec_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmallSmemMax);
     if (e == cudaSuccess)
@@ -971,13 +1058,16 @@ cudaError_t setup() {
 // time (128 x BN x K MACs at ~4096 per cycle), its operand traffic
 // ((128 + BN) x K fp16 from L2 at ~64 bytes per cycle) and its epilogue
 // (~0.3 cycle per output), and the tiles run in waves over the SMs.
-int pick_bn(int M, int N, int K, int sms) {
-    static const int cands[] = {256, 192, 128, 96, 64, 32};
+int pick_bn(int M, int N, int K, int sms, bool narrow_set) {
+    static const int all[] = {256, 192, 128, 96, 64}, narrow[] = {256, 128, 64};
+    const int *cands = narrow_set ? narrow : all;
+    const int nc = narrow_set ? 3 : 5;
     const long long MT = (M + kCM - 1) / kCM;
-    int best = 256;
+    int best = cands[nc - 1];
     double best_cost = -1;
-    for (int bn : cands) {
-        if ((bn == 32 && N > 32) || (bn > N && bn != 32)) continue;
+    for (int i = 0; i < nc; ++i) {
+        const int bn = cands[i];
+        if (bn > N && bn != cands[nc - 1]) continue;
         const long long tiles = MT * ((N + bn - 1) / bn);
         const double mma = 128.0 * bn * K / 4096.0, load = (128.0 + bn) * K * 2.0 / 64.0, epi = 128.0 * bn * 0.3;
         const double cost = (double)((tiles + sms - 1) / sms) * std::max(mma, std::max(load, epi));
@@ -1004,6 +1094,80 @@ struct Epi {
     int ldy16 = 0, o16 = O16_NONE, lo_off = 0;
 };
 
+template <int BN, int F>
+cudaError_t launch_gemm_t(const CUtensorMap &amap, const CUtensorMap &bmap, const CGemm &p, int grid, cudaStream_t st) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        const cudaError_t e = cudaFuncSetAttribute(codec_gemm_kernel<BN, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)(sizeof(CSmem<BN>) + 1024));
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(grid), dim3(kCThreads), sizeof(CSmem<BN>) + 1024, st, attr);
+    return cudaLaunchKernelEx(&cfg, codec_gemm_kernel<BN, F>, amap, bmap, p);
+}
+
+// tile widths compiled for an epilogue: {64, 128, 256} for the transformer's
+// products, {64, 96, 128, 192, 256} for the convolutions
+template <int F, bool Narrow>
+cudaError_t launch_gemm_f(int BN, const CUtensorMap &amap, const CUtensorMap &bmap, const CGemm &p, int grid,
+                          cudaStream_t st) {
+    switch (BN) {
+    case 64: return launch_gemm_t<64, F>(amap, bmap, p, grid, st);
+    case 128: return launch_gemm_t<128, F>(amap, bmap, p, grid, st);
+    case 256: return launch_gemm_t<256, F>(amap, bmap, p, grid, st);
+    default: break;
+    }
+    if constexpr (!Narrow) {
+        if (BN == 96) return launch_gemm_t<96, F>(amap, bmap, p, grid, st);
+        if (BN == 192) return launch_gemm_t<192, F>(amap, bmap, p, grid, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+// the feature set of an epilogue
+int epi_features(const CGemm &p) {
+    return (p.bias ? F_BIAS : 0) | (p.gamma ? F_GAMMA : 0) | (p.res ? F_RES : 0) | (p.y32 ? F_Y32 : 0) |
+           (p.act == ACT_GELU ? F_GELU : 0) | (p.act == ACT_SWIGLU ? F_SWIGLU : 0) | f_o16(p.o16);
+}
+
+constexpr int kEpiQKV = F_Y32;                                          // wqkv
+constexpr int kEpiResGamma = F_GAMMA | F_RES | F_Y32;                   // wo, w2
+constexpr int kEpiSwiglu = F_SWIGLU;                                    // w1 | w3
+constexpr int kEpiBias32 = F_BIAS | F_Y32;                              // upsample transposed conv
+constexpr int kEpiGelu = F_BIAS | F_GELU | (O16_PLAIN << 6);            // pwconv1
+constexpr int kEpiCnxHilo = F_BIAS | F_GAMMA | F_RES | (O16_HILO << 6);  // pwconv2 -> next transposed conv
+constexpr int kEpiCnxPlain = F_BIAS | F_GAMMA | F_RES | (O16_PLAIN << 6);  // pwconv2 -> decoder conv
+constexpr int kEpiSnakeHilo = F_BIAS | (O16_SNAKE_HILO << 6);           // decoder conv
+constexpr int kEpiConvT = F_BIAS | F_Y32 | (O16_SNAKE << 6);             // block transposed conv
+constexpr int kEpiSnake = F_BIAS | (O16_SNAKE << 6);                     // residual unit conv 1
+constexpr int kEpiResSnake = F_BIAS | F_RES | F_Y32 | (O16_SNAKE << 6);  // residual unit conv 2
+constexpr int kEpiResSnakeHilo = F_BIAS | F_RES | (O16_SNAKE_HILO << 6);  // last unit -> next block
+constexpr int kEpiResSnakeOut = F_BIAS | F_RES | (O16_SNAKE << 6);       // last unit -> output conv
+
+bool narrow_epilogue(int F) { return F == kEpiQKV || F == kEpiResGamma || F == kEpiSwiglu; }
+
+cudaError_t launch_gemm(int F, int BN, const CUtensorMap &amap, const CUtensorMap &bmap, const CGemm &p, int grid,
+                        cudaStream_t st) {
+    switch (F) {
+    case kEpiQKV: return launch_gemm_f<kEpiQKV, true>(BN, amap, bmap, p, grid, st);
+    case kEpiResGamma: return launch_gemm_f<kEpiResGamma, true>(BN, amap, bmap, p, grid, st);
+    case kEpiSwiglu: return launch_gemm_f<kEpiSwiglu, true>(BN, amap, bmap, p, grid, st);
+    case kEpiBias32: return launch_gemm_f<kEpiBias32, false>(BN, amap, bmap, p, grid, st);
+    case kEpiGelu: return launch_gemm_f<kEpiGelu, false>(BN, amap, bmap, p, grid, st);
+    case kEpiCnxHilo: return launch_gemm_f<kEpiCnxHilo, false>(BN, amap, bmap, p, grid, st);
+    case kEpiCnxPlain: return launch_gemm_f<kEpiCnxPlain, false>(BN, amap, bmap, p, grid, st);
+    case kEpiSnakeHilo: return launch_gemm_f<kEpiSnakeHilo, false>(BN, amap, bmap, p, grid, st);
+    case kEpiConvT: return launch_gemm_f<kEpiConvT, false>(BN, amap, bmap, p, grid, st);
+    case kEpiSnake: return launch_gemm_f<kEpiSnake, false>(BN, amap, bmap, p, grid, st);
+    case kEpiResSnake: return launch_gemm_f<kEpiResSnake, false>(BN, amap, bmap, p, grid, st);
+    case kEpiResSnakeHilo: return launch_gemm_f<kEpiResSnakeHilo, false>(BN, amap, bmap, p, grid, st);
+    case kEpiResSnakeOut: return launch_gemm_f<kEpiResSnakeOut, false>(BN, amap, bmap, p, grid, st);
+    default: return cudaErrorNotSupported;
+    }
+}
+
 s2k_status gemm(s2k_codec *c, const ARef &a, const GW &g, int M, const Epi &e) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(S2K_ERR_UNSUPPORTED, "codec: cuTensorMapEncodeTiled unavailable");
@@ -1018,17 +1182,6 @@ s2k_status gemm(s2k_codec *c, const ARef &a, const GW &g, int M, const Epi &e) {
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return fail(S2K_ERR_CUDA, "codec: activation tensor map (%d x %d, ld %d)", a.rows, a.width, a.ld);
-    }
-    const int BN = pick_bn(M, g.N, g.taps * g.kp, c->num_sms);
-    {
-        const cuuint64_t dims[2] = {(cuuint64_t)g.taps * g.kp, (cuuint64_t)g.N};
-        const cuuint64_t strides[1] = {(cuuint64_t)g.taps * g.kp * 2};
-        const cuuint32_t box[2] = {(cuuint32_t)kCK, (cuuint32_t)BN};
-        const cuuint32_t es[2] = {1, 1};
-        if (enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.w, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return fail(S2K_ERR_CUDA, "codec: weight tensor map (%d x %d)", g.N, g.taps * g.kp);
     }
     CGemm p;
     p.M = M;
@@ -1052,27 +1205,23 @@ s2k_status gemm(s2k_codec *c, const ARef &a, const GW &g, int M, const Epi &e) {
     p.o16 = e.o16;
     p.lo_off = e.lo_off;
     p.err = c->d_err;
+    const int F = epi_features(p);
+    const int BN = pick_bn(M, g.N, g.taps * g.kp, c->num_sms, narrow_epilogue(F));
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)g.taps * g.kp, (cuuint64_t)g.N};
+        const cuuint64_t strides[1] = {(cuuint64_t)g.taps * g.kp * 2};
+        const cuuint32_t box[2] = {(cuuint32_t)kCK, (cuuint32_t)BN};
+        const cuuint32_t es[2] = {1, 1};
+        if (enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.w, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return fail(S2K_ERR_CUDA, "codec: weight tensor map (%d x %d)", g.N, g.taps * g.kp);
+    }
     const int MT = (M + kCM - 1) / kCM, NT = (g.N + BN - 1) / BN;
     const int grid = std::min(MT * NT, c->num_sms);
-    cudaLaunchAttribute attr[1];
-    cudaError_t err;
     count_launch();
-#define CODEC_GEMM_CASE(bn)                                                                                    \
-    case bn: {                                                                                                 \
-        cudaLaunchConfig_t cfg = pdl_cfg(dim3(grid), dim3(kCThreads), sizeof(CSmem<bn>) + 1024, c->st, attr); \
-        err = cudaLaunchKernelEx(&cfg, codec_gemm_kernel<bn>, amap, bmap, p);                                   \
-        break;                                                                                                 \
-    }
-    switch (BN) {
-        CODEC_GEMM_CASE(32)
-        CODEC_GEMM_CASE(64)
-        CODEC_GEMM_CASE(96)
-        CODEC_GEMM_CASE(128)
-        CODEC_GEMM_CASE(192)
-        CODEC_GEMM_CASE(256)
-    default: err = cudaErrorInvalidValue;
-    }
-#undef CODEC_GEMM_CASE
+    const cudaError_t err = launch_gemm(F, BN, amap, bmap, p, grid, c->st);
+    if (err == cudaErrorNotSupported) return fail(S2K_ERR_UNSUPPORTED, "codec: no GEMM epilogue for features 0x%x", F);
     CU(err);
     return S2K_OK;
 }

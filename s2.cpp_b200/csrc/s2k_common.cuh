@@ -198,6 +198,29 @@ __device__ __forceinline__ float det_expf(float x) {
     return ldexpf(p, (int)k);
 }
 
+// sin(x) for float x with a fixed sequence of IEEE float operations, so the
+// CUDA kernels and the CPU oracle (oracle/s2_oracle.c, so_det_sinf) return the
+// same bits: Cody-Waite reduction x = k*pi + r (pi split in three parts, k*P1
+// and k*P2 exact for |k| <= 2048), sin(r) by its Taylor series to degree 13
+// (|r| <= pi/2: truncation < 7e-10), negated for odd k.  Beyond |x| = 6400
+// (outside the reduction's exact range) it is the library sinf.
+__device__ __forceinline__ float det_sinf(float x) {
+    if (!(fabsf(x) <= 6400.0f)) return sinf(x);
+    const float k = rintf(__fmul_rn(x, 0.318309873342514038f));
+    float r = __fsub_rn(x, __fmul_rn(k, 3.140625f));
+    r = __fsub_rn(r, __fmul_rn(k, 9.6750259399414062e-4f));
+    r = __fsub_rn(r, __fmul_rn(k, 1.5099580252808664e-7f));
+    const float r2 = __fmul_rn(r, r);
+    float p = 1.60590443720742825917e-10f;                    // 1/13!
+    p = __fadd_rn(__fmul_rn(p, r2), -2.50521079436794025241e-8f);  // -1/11!
+    p = __fadd_rn(__fmul_rn(p, r2), 2.75573188446287531406e-6f);   // 1/9!
+    p = __fadd_rn(__fmul_rn(p, r2), -1.98412701138295233250e-4f);  // -1/7!
+    p = __fadd_rn(__fmul_rn(p, r2), 8.33333376795053482056e-3f);   // 1/5!
+    p = __fadd_rn(__fmul_rn(p, r2), -1.66666671633720397949e-1f);  // -1/3!
+    const float v = __fadd_rn(r, __fmul_rn(__fmul_rn(r, r2), p));
+    return ((int)k & 1) ? -v : v;
+}
+
 // x / (1 + exp(-x)), ggml_silu_f32
 __device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, det_expf(-x))); }
 
