@@ -20,6 +20,13 @@ with the repository.
       frame of the last size runs between cudaProfilerStart / Stop (for
       `ncu --profile-from-start off`).
 
+  python s2.cpp_b200/s2k_profile.py codec [--frames 160] [--reps 2]
+      The codec decode (s2k_codec_decode) of `frames` code frames on the S2
+      Pro codec shapes, `reps` times: kernel launches per decode, host wall
+      time per decode and the library's device time of one decode.  With
+      --reps 2 the second decode is the one to capture (skip the first
+      decode's launches).
+
 Seeded synthetic weights (no checkpoints offline).
 """
 from __future__ import annotations
@@ -222,6 +229,23 @@ def cmd_batch(a) -> None:
     m.close()
 
 
+def cmd_codec(a) -> None:
+    import time
+    ch = synthetic.codec_preset("s2pro")
+    c = s2k.AudioCodec(ch)
+    c.load_tensors(synthetic.make_codec(ch, seed=6))
+    codes = synthetic.codec_codes(ch, a.frames, seed=a.frames)
+    for i in range(a.reps):
+        s2k.launch_count(True)
+        t = time.perf_counter()
+        c.decode(codes)
+        wall = (time.perf_counter() - t) * 1e3
+        print(json.dumps({"decode": i, "frames": a.frames, "launches": s2k.launch_count(True), "wall_ms": wall}))
+    _, ms, _ = c.decode_windowed(codes, a.frames, 0)
+    print(json.dumps({"device_ms": ms, "receptive_frames": c.receptive_frames()}))
+    c.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -240,8 +264,11 @@ def main() -> None:
     b.add_argument("--context", type=int, default=512)
     b.add_argument("--frames", type=int, default=20)
     b.add_argument("--profile-one", action="store_true")
+    k = sub.add_parser("codec")
+    k.add_argument("--frames", type=int, default=160)
+    k.add_argument("--reps", type=int, default=2)
     a = ap.parse_args()
-    {"prefill": cmd_prefill, "ops": cmd_ops, "batch": cmd_batch}[a.cmd](a)
+    {"prefill": cmd_prefill, "ops": cmd_ops, "batch": cmd_batch, "codec": cmd_codec}[a.cmd](a)
 
 
 if __name__ == "__main__":
