@@ -104,6 +104,7 @@ def codec_decode(with_cpu: bool, reps: int = 10, warmup: int = 3) -> dict:
     events, the tensor-core FLOP rate against the measured dense bf16/f16
     peak, and the windowed decode of a 215-frame (10 s) utterance.  Beside
     it the CPU oracle on a 2-frame sample."""
+    import s2k  # noqa: E402
     ch = synthetic.codec_preset("s2pro")
     tensors = list(synthetic.make_codec(ch, seed=6))
     c = s2k.AudioCodec(ch)
