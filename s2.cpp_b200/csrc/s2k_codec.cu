@@ -486,11 +486,13 @@ struct VqParams {
 
 // x[t][o] = sum over quantizers q (in order) of out_proj_q(codebook_q[code]) + b_q
 // (build_vq_decode_stage and the adds of build_decode_codes_stage_backend)
-__global__ void __launch_bounds__(256) vq_decode_kernel(VqParams p, float *x) {
+__global__ void __launch_bounds__(128) vq_decode_kernel(VqParams p, float *x) {
     pdl_launch_dependents();
     pdl_wait();
     const int t = blockIdx.x;
-    for (int o = threadIdx.x; o < p.C; o += blockDim.x) {
+    {
+        const int o = blockIdx.y * blockDim.x + threadIdx.x;
+        if (o >= p.C) return;
         float acc = 0.f;
         for (int q = 0; q < p.nq; ++q) {
             int code = p.codes[(size_t)q * p.L + t];
@@ -1315,7 +1317,7 @@ s2k_status run_window(s2k_codec *c, int n_tr, int f0) {
         vp.ow[q] = c->vq_ow[q];
         vp.ob[q] = c->vq_ob[q];
     }
-    if ((rc = launch(c, vq_decode_kernel, dim3(n_tr), dim3(256), 0, vp, c->X))) return rc;
+    if ((rc = launch(c, vq_decode_kernel, dim3(n_tr, (c->C0 + 127) / 128), dim3(128), 0, vp, c->X))) return rc;
     // post-module transformer
     const int qkvs = c->qs + 2 * c->kvs;
     const float scale = 1.0f / std::sqrt((float)c->hd);
