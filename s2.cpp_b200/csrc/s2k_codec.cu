@@ -104,6 +104,7 @@ struct EpiF {
 struct CGemm {
     int M, N;            // output rows (time), columns
     int kchunks, kp;     // 64-column chunks of A per tap; B columns per tap
+    int ksteps_last;     // 16-column MMA steps with data in a tap's last chunk
     int taps, shift0, dshift;
     int cout;            // period of the per-channel vectors (bias, gamma, alpha)
     const float *bias, *gamma, *alpha;
@@ -397,10 +398,13 @@ __global__ void __launch_bounds__(kCThreads, 1)
                     ok = mbar_wait(&sm.full[st], (it / S) & 1, p.err, ERR_WAIT_FULL);
                     if (!ok) break;
                     tc_fence_after();
+                    // a tap's last chunk may be part-filled (zero columns past the input width)
+                    const int nsteps = (kk % p.kchunks) == p.kchunks - 1 ? p.ksteps_last : 4;
 #pragma unroll
                     for (int k4 = 0; k4 < 4; ++k4)
-                        mma_f16(tmem + buf * BN, sw128_desc(sm.a[st] + 32 * k4), sw128_desc(sm.b[st] + 32 * k4),
-                                idesc_f16<BN>(), (kk | k4) != 0);
+                        if (k4 < nsteps)
+                            mma_f16(tmem + buf * BN, sw128_desc(sm.a[st] + 32 * k4), sw128_desc(sm.b[st] + 32 * k4),
+                                    idesc_f16<BN>(), (kk | k4) != 0);
                     mma_commit(&sm.empty[st]);
                 }
                 if (ok) mma_commit(&sm.tfull[buf]);
@@ -884,14 +888,15 @@ s2k_status vec(s2k_codec *c, const std::string &name, int64_t n, float **out) {
     return S2K_OK;
 }
 
+// B columns per tap: whole 64-column chunks (128-byte aligned TMA rows)
+int round64(int x) { return (x + 63) / 64 * 64; }
+
 s2k_status upload_b(s2k_codec *c, GW &g, const std::vector<__half> &h) {
     s2k_status rc = dev_alloc(c, &g.w, h.size(), c->allocs);
     if (rc) return rc;
     CU(cudaMemcpy(g.w, h.data(), h.size() * sizeof(__half), cudaMemcpyHostToDevice));
     return S2K_OK;
 }
-
-int round64(int x) { return (x + 63) / 64 * 64; }
 
 // the matrices of F16-weight products must be F16 (the reference rounds the
 // activation to fp16 only for those); convolution weights may be F32 (their
@@ -1190,6 +1195,7 @@ s2k_status gemm(s2k_codec *c, const ARef &a, const GW &g, int M, const Epi &e) {
     p.N = g.N;
     p.kchunks = (a.width + kCK - 1) / kCK;
     p.kp = g.kp;
+    p.ksteps_last = (a.width - kCK * (p.kchunks - 1) + 15) / 16;
     p.taps = g.taps;
     p.shift0 = g.shift0;
     p.dshift = g.dshift;
