@@ -48,3 +48,32 @@ def test_frame_metric_names_the_weight_scheme():
     assert bench.frame_metric("q8_0") == bench.METRIC
     assert "Q4_K_M" in bench.frame_metric("q4_k_m") and "Q8_0" not in bench.frame_metric("q4_k_m")
     assert "F16" in bench.frame_metric("f16")
+
+
+def test_codec_flops_counts_the_graph():
+    """bench.codec_flops: linear in frames, and on the small codec equal to a
+    hand count of its products (transformer, upsample, decoder)."""
+    import synthetic
+    ch = synthetic.codec_preset("small")
+    f1, f2 = bench.codec_flops(ch, 10, 10), bench.codec_flops(ch, 20, 20)
+    assert abs(f2 - 2 * f1) < 1e-6 * f2
+    d, hd, ff = 128, 32, 256
+    H, Hk = 4, 2
+    keys = 8
+    n = 10
+    want = 2 * 2.0 * n * (d * (H + 2 * Hk) * hd + H * hd * d + 3 * d * ff + 2 * H * hd * keys)
+    L, C = n, d
+    for fac in (2, 3):
+        want += 2.0 * L * fac * C * C
+        L *= fac
+        want += 2.0 * L * C * (7 + 2 * 512)
+    want += 2.0 * L * 256 * C * 7
+    C = 256
+    for r in (4, 2):
+        co = C // 2
+        want += 2.0 * L * (r * co) * (2 * C)
+        L *= r
+        want += 3 * 2.0 * L * co * co * 8
+        C = co
+    want += 2.0 * L * C * 7
+    assert abs(f1 - want) < 1e-9 * want
