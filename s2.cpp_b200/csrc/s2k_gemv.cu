@@ -37,6 +37,7 @@ struct GemvCfg {
 };
 
 constexpr int kPC = 5;  // 8-value activation chunks per consumer thread per prologue pass
+constexpr int kGemvPL = 4;  // tiles the producer warp issues per group (one per lane)
 constexpr int kMaxMTF16 = 4;  // tokens per launch on F16 weights (their activation takes 2 B per value)
 
 template <int MT>
@@ -83,16 +84,32 @@ __global__ void __launch_bounds__(kThreads, 1) tgemv_kernel(TGemv g, const int *
     pdl_launch_dependents();
 
     if (warp == kTW) {  // ---------------- producer ----------------
-        if (lane == 0 && sm.abort_flag == 0) {
+        // Tiles go out in groups of up to kGemvPL, one bulk copy per lane in
+        // the same instruction (one lane issuing every copy bounds a CTA's
+        // tile rate).  Lane 0 checks the ring once per group: tile t reuses
+        // the slot of tile t - NS, and the consumers release tiles in order,
+        // so waiting for the group's last such tile covers the others.  The
+        // first NS tiles, which an aborting consumer drains, are issued
+        // without a check, so no group straddles tile NS.
+        if (__shfl_sync(0xffffffffu, sm.abort_flag, 0) == 0) {
             const uint64_t pol = policy_evict_first();
-            for (int t = 0; t < ntiles; ++t) {
-                const int slot = t % NS;
-                if (t >= NS) {
-                    if (!mbar_wait(&sm.empty[slot], ((t / NS) - 1) & 1, err, ERR_WAIT_EMPTY)) break;
-                    if (*reinterpret_cast<volatile int *>(&sm.abort_flag)) break;
+            for (int t = 0; t < ntiles;) {
+                const int n = min(min(kGemvPL, ntiles - t), t < NS ? NS - t : kGemvPL);
+                if (t + n - 1 >= NS) {
+                    int stop = 0;
+                    if (lane == 0) {
+                        const int q = t + n - 1 - NS;
+                        stop = !mbar_wait(&sm.empty[q % NS], (q / NS) & 1, err, ERR_WAIT_EMPTY) ||
+                               *reinterpret_cast<volatile int *>(&sm.abort_flag) != 0;
+                    }
+                    if (__shfl_sync(0xffffffffu, stop, 0)) break;
                 }
-                mbar_arrive_expect_tx(&sm.full[slot], tb);
-                bulk_g2s(sm.ring[slot], g.w + (size_t)(u0 + t) * tb, tb, &sm.full[slot], pol);
+                if (lane < n) {
+                    const int slot = (t + lane) % NS;
+                    mbar_arrive_expect_tx(&sm.full[slot], tb);
+                    bulk_g2s(sm.ring[slot], g.w + (size_t)(u0 + t + lane) * tb, tb, &sm.full[slot], pol);
+                }
+                t += n;
             }
         }
         return;
