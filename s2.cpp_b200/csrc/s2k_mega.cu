@@ -372,7 +372,7 @@ __device__ void mega_gemv(const MegaGemv &gref, const F8 (&nw)[kMPC], MSmem &sm,
     tg_range(g.R, g.K, g.wtype, cta, G, &u0, &u1);
     if (u0 == u1) return;  // no row tile of this op here (R / 32 < G)
     // the CTA owning row tile 0 stores act_out
-    tg_prologue8<MT, kMNC, kMPC>(g, nw, sm.u.g.xq, sm.u.g.xd, sm.u.g.xbs, &sm.tok[0][0], kMaxT, u0 == 0, 1,
+    tg_prologue8<MT, kMNC, kMPC, Q8>(g, nw, sm.u.g.xq, sm.u.g.xd, sm.u.g.xbs, &sm.tok[0][0], kMaxT, u0 == 0, 1,
                                  tr != nullptr ? tr + 4 : nullptr, err);
     named_sync(1, kMNC);
     if (tr != nullptr && threadIdx.x == 0) tr[1] = globaltimer_ns();
@@ -704,7 +704,10 @@ __device__ void attn_unit(const MegaAttn &a, const AttnPlan &pl, const AttnUnit 
         // w_k = det_expf(m_k - M); thread (d, kh) sums local heads kh, kh + 2
         if (nsp <= kCombineFast) {
             // one round trip: (m_k, S_k) staged by threads p < nh * nsp while every
-            // thread loads its own O_k[h][d] of heads kh, kh + 2 into registers
+            // thread loads its own O_k[h][d] of heads kh, kh + 2 into registers;
+            // then the same threads form each split's weight w_k once (one
+            // det_expf per (head, split), not one per output dim: the unit's
+            // code stays small, which the instruction cache rewards)
             double ov[2][kCombineFast];
 #pragma unroll
             for (int x = 0; x < 2; ++x)
@@ -720,17 +723,22 @@ __device__ void attn_unit(const MegaAttn &a, const AttnPlan &pl, const AttnUnit 
                 as.e[k][h] = ms.y;
             }
             named_sync(3, kMNC);
+            if (tid < nh * nsp) {
+                const int h = tid / nsp, k = tid - h * nsp;
+                float M = as.s[h][0];
+                for (int k2 = 1; k2 < nsp; ++k2) M = fmaxf(M, as.s[h][k2]);
+                as.o[h][k] = (double)det_expf(__fsub_rn(as.s[h][k], M));
+            }
+            named_sync(3, kMNC);
 #pragma unroll
             for (int x = 0; x < 2; ++x) {
                 const int h = kh + 2 * x;
                 if (h < nh) {
-                    float M = as.s[h][0];
-                    for (int k = 1; k < nsp; ++k) M = fmaxf(M, as.s[h][k]);
                     double acc = 0.0, S = 0.0;
 #pragma unroll
                     for (int k = 0; k < kCombineFast; ++k)
                         if (k < nsp) {
-                            const double w = (double)det_expf(__fsub_rn(as.s[h][k], M));
+                            const double w = as.o[h][k];
                             acc += ov[x][k] * w;
                             S += as.e[k][h] * w;
                         }

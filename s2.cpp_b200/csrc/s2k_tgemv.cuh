@@ -371,15 +371,17 @@ __device__ __forceinline__ void quant_q8k_warp(const float (&y)[8], int lane, bo
 // scales, xbs [M][K/16] block sums).  nw holds the norm weights of the
 // thread's pass-0 chunks when the activation fits one pass (tg_norm_preload);
 // otherwise they are loaded here.  tok [NT/32][tok_ld] is shared scratch.
-template <int MT, int NT, int PC>
+// Q8ONLY: every weight of the caller is Q8_0, so only that quantizer is
+// compiled in (a smaller prologue for the persistent kernel's Q8_0 build).
+template <int MT, int NT, int PC, bool Q8ONLY = false>
 __device__ __forceinline__ void tg_prologue8(const TGemv &g, const F8 (&nw)[PC], int8_t *xq, float *xd, int16_t *xbs,
                                              double *tok, int tok_ld, bool write_act, int bar_id,
                                              unsigned long long *ts = nullptr, int *err = nullptr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = g.K, KC = K >> 3, M = g.M, nv = M * KC;
     const bool rms = g.in_mode == IN_RMSNORM;
-    const bool f16 = g.wtype == TW_F16;
-    const bool q8k = g.wtype != TW_Q8_0 && !f16;
+    const bool f16 = !Q8ONLY && g.wtype == TW_F16;
+    const bool q8k = !Q8ONLY && g.wtype != TW_Q8_0 && !f16;
     const bool one_pass = nv <= PC * NT;
     float sc[MT];
 #pragma unroll
