@@ -300,6 +300,10 @@ S2K_API s2k_status s2k_model_set_wait_limit(s2k_model *m, int64_t cycles);
  * an activation tag nobody writes.  Returns S2K_ERR_TIMEOUT once the wait
  * limit has passed (the path every timed-out wait takes). */
 S2K_API s2k_status s2k_debug_wait_probe(s2k_model *m);
+/* Test hook: y[i] = the device exp (det_expf, the exp of every softmax, SiLU
+ * and sampler kernel) of x[i], i < n, on `device`; host arrays.  The CPU
+ * oracle's so_det_expf returns the same bits. */
+S2K_API s2k_status s2k_debug_det_expf(int32_t device, const float *x, float *y, int64_t n);
 /* Test hook: the device allocation `after` allocations from now fails once
  * (as an out-of-memory error); a negative value disarms it. */
 S2K_API s2k_status s2k_debug_fail_alloc(s2k_model *m, int64_t after);

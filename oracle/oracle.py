@@ -103,6 +103,9 @@ def lib() -> ctypes.CDLL:
             "so_codec_samples": ([vp, i32], i64),
             "so_codec_decode": ([vp, vp, i32, vp, i64, ctypes.POINTER(i64)], ctypes.c_int),
             "so_codec_set_f32_accum": ([ctypes.c_int], None),
+            "so_det_expf": ([ctypes.c_float], ctypes.c_float),
+            "so_det_expf_array": ([vp, vp, i64], None),
+            "so_check_pow2_scale": ([i64, ctypes.c_uint32], i64),
         }
         for name, (a, r) in sig.items():
             f = getattr(L, name)
@@ -110,6 +113,19 @@ def lib() -> ctypes.CDLL:
             f.restype = r
         _lib = L
     return _lib
+
+
+def det_expf(x: np.ndarray) -> np.ndarray:
+    """so_det_expf of every element (float32)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().so_det_expf_array(x.ctypes.data, y.ctypes.data, x.size)
+    return y
+
+
+def check_pow2_scale(n: int, seed: int = 1) -> int:
+    """Mismatches of the oracle's power-of-two scaling against ldexpf."""
+    return int(lib().so_check_pow2_scale(n, seed))
 
 
 def set_threads(n: int) -> None:

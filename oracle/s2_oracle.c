@@ -122,7 +122,22 @@ double so_philox_uniform(uint64_t seed, uint32_t frame, uint32_t purpose, uint32
 /* the same steps (s2k_common.cuh det_expf), so both return identical bits.  */
 /* Cody-Waite reduction x = k ln2 + r, Taylor series of exp(r) to degree 7,  */
 /* scaling by 2^k.  Accuracy ~1-2 ulp, like libm expf.                       */
+/* The scaling is two products by powers of two: p * 2^(k-h) is exact and   */
+/* normal for every k in [-150, 128], the product by 2^h rounds once (into   */
+/* the subnormals when k < -126), so the result is ldexpf(p, k).             */
 /* ------------------------------------------------------------------------ */
+
+static inline float pow2f_bits(int e) {
+    const uint32_t u = (uint32_t)(e + 127) << 23;
+    float f;
+    memcpy(&f, &u, sizeof f);
+    return f;
+}
+
+float so_pow2_scale(float p, int k) {
+    const int h = k < -100 ? -64 : (k > 100 ? 64 : 0);
+    return (p * pow2f_bits(k - h)) * pow2f_bits(h);
+}
 
 float so_det_expf(float x) {
     if (x != x) return x;
@@ -138,7 +153,38 @@ float so_det_expf(float x) {
     p = p * r + 0.5f;
     p = p * r + 1.0f;
     p = p * r + 1.0f;
-    return ldexpf(p, (int)k);
+    return so_pow2_scale(p, (int)k);
+}
+
+void so_det_expf_array(const float *x, float *y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = so_det_expf(x[i]);
+}
+
+/* Checker of the scaling step: so_pow2_scale(p, k) against the C library's
+ * ldexpf(p, k) for every k in [-150, 128] and n values of p (the reachable
+ * [0.70, 1.42], then random bit patterns in [0.5, 2)); returns the number of
+ * differing results. */
+int64_t so_check_pow2_scale(int64_t n, uint32_t seed) {
+    int64_t bad = 0;
+    uint32_t st = seed ? seed : 1u;
+    for (int k = -150; k <= 128; ++k) {
+        for (int64_t j = 0; j < n; ++j) {
+            float p;
+            if (j < n / 2) {
+                p = 0.70f + 0.72f * (float)j / (float)(n / 2);
+            } else {
+                st = st * 1664525u + 1013904223u;
+                const uint32_t u = 0x3f000000u + (st >> 8) % 0x01000000u;  /* [0.5, 2) */
+                memcpy(&p, &u, sizeof p);
+            }
+            const float a = so_pow2_scale(p, k), b = ldexpf(p, k);
+            uint32_t ua, ub;
+            memcpy(&ua, &a, 4);
+            memcpy(&ub, &b, 4);
+            bad += ua != ub;
+        }
+    }
+    return bad;
 }
 
 /* sin with the same float steps as the CUDA det_sinf (s2k_common.cuh):

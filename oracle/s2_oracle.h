@@ -114,6 +114,9 @@ void so_matvec(int type, const void *w, int64_t rows, int64_t n, const float *x,
 uint16_t so_fp32_to_fp16(float f);
 /* exp(x) by a fixed float operation sequence shared with the CUDA kernels */
 float so_det_expf(float x);
+float so_pow2_scale(float p, int k);
+void so_det_expf_array(const float *x, float *y, int64_t n);
+int64_t so_check_pow2_scale(int64_t n, uint32_t seed);
 float so_det_sinf(float x);
 float so_fp16_to_fp32(uint16_t h);
 void so_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);

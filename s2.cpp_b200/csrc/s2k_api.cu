@@ -1940,6 +1940,20 @@ S2K_API s2k_status s2k_debug_wait_probe(s2k_model *m) {
     return check_err_word(m);
 }
 
+S2K_API s2k_status s2k_debug_det_expf(int32_t device, const float *x, float *y, int64_t n) {
+    if (n < 0 || (n > 0 && (!x || !y))) return fail(S2K_ERR_ARG, "bad argument");
+    if (n == 0) return S2K_OK;
+    if (cuda_set(device)) return fail(S2K_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    float *d = nullptr;
+    CU(cudaMalloc(&d, (size_t)n * 2 * sizeof(float)));
+    cudaError_t e = cudaMemcpy(d, x, (size_t)n * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = launch_det_expf(d, d + n, n, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(y, d + n, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    CU(e);
+    return S2K_OK;
+}
+
 S2K_API s2k_status s2k_debug_fail_alloc(s2k_model *m, int64_t after) {
     if (!m) return fail(S2K_ERR_ARG, "NULL model");
     m->fail_alloc_at = after < 0 ? -1 : after;

@@ -180,7 +180,15 @@ __device__ __forceinline__ int quant_q8_0_lane(float v, float *d_out) {
 // CUDA kernels and the CPU oracle (oracle/s2_oracle.c, det_expf) return the
 // same bits: Cody-Waite reduction x = k*ln2 + r (ln2 split so k*LN2_HI is
 // exact), exp(r) by its Taylor series to degree 7 (|r| <= ln2/2, truncation
-// < 1e-8 relative), then scaling by 2^k.
+// < 1e-8 relative), then scaling by 2^k as two products by powers of two
+// (p * 2^(k-h) is exact and normal for every k in [-150, 128], the product
+// by 2^h rounds once, into the subnormals when k < -126): the correctly
+// rounded p * 2^k, i.e. ldexpf's result, at a fraction of its cost.
+__device__ __forceinline__ float pow2_scale(float p, int k) {
+    const int h = k < -100 ? -64 : (k > 100 ? 64 : 0);
+    return __fmul_rn(__fmul_rn(p, __int_as_float((k - h + 127) << 23)), __int_as_float((h + 127) << 23));
+}
+
 __device__ __forceinline__ float det_expf(float x) {
     if (x != x) return x;
     if (x > 88.72283935546875f) return INFINITY;
@@ -195,7 +203,7 @@ __device__ __forceinline__ float det_expf(float x) {
     p = __fadd_rn(__fmul_rn(p, r), 0.5f);
     p = __fadd_rn(__fmul_rn(p, r), 1.0f);
     p = __fadd_rn(__fmul_rn(p, r), 1.0f);
-    return ldexpf(p, (int)k);
+    return pow2_scale(p, (int)k);
 }
 
 // sin(x) for float x with a fixed sequence of IEEE float operations, so the

@@ -240,6 +240,8 @@ cudaError_t launch_gather_rows(const DevMat *E, const int *ids, int n, float *ou
 // Standalone sampler (s2k_sample)
 cudaError_t launch_sample_one(const float *logits, int n, float temperature, float top_p, int top_k,
                               double u, int *out, int *err, cudaStream_t st);
+// det_expf of n floats (s2k_debug_det_expf)
+cudaError_t launch_det_expf(const float *x, float *y, long long n, cudaStream_t st);
 
 // launch accounting
 void count_launch(int n = 1);

@@ -25,7 +25,7 @@
 
 namespace s2k {
 
-// 8 consumer warps (the tile engine's mapping, s2k_tgemv.cuh) + 1 producer.
+// 8 consumer warps (the tile engine's mapping, s2k_tgemv.cuh) + the producer warp + a helper warp.
 constexpr int kMW = kTW;                   // consumer warps
 constexpr int kMNC = kMW * 32;             // consumer threads
 constexpr int kMThreads = kMNC + 64;       // + producer warp + helper warp (attention K/V prefetch)
@@ -894,8 +894,9 @@ __device__ void mega_embed_fast(const MegaEmbedFast &e, int cta, int G, int *err
     }
 }
 
-// 9 warps per CTA: one SM sub-partition holds three of them, so its 16K
-// registers cap a thread at 168 (the launch bound keeps the kernel there).
+// 10 warps per CTA, dealt to the SM's four sub-partitions round robin: two
+// of them hold three warps, so their 16K registers cap a thread at 168 (the
+// launch bound keeps the kernel there; 200 registers would not launch).
 template <int MT, bool Q8>
 __global__ void __launch_bounds__(kMThreads, 1)
     mega_kernel(const MegaOp *__restrict__ ops, int n_ops, MegaCtl *ctl, const int *done, int *err, int l2_ahead,

@@ -17,6 +17,7 @@
 #include "s2k_kernels.h"
 #include "s2k_device.h"
 
+#include <algorithm>
 #include <climits>
 
 namespace s2k {
@@ -652,6 +653,19 @@ cudaError_t launch_sample_one(const float *logits, int n, float temperature, flo
     if (e != cudaSuccess) return e;
     count_launch();
     sample_one_kernel<<<1, kSampThreads, sizeof(SampSmem), st>>>(logits, n, temperature, top_p, top_k, u, out, err);
+    return cudaGetLastError();
+}
+
+// det_expf over an array (the exp every kernel shares with the CPU oracle).
+__global__ void det_expf_kernel(const float *x, float *y, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        y[i] = det_expf(x[i]);
+}
+
+cudaError_t launch_det_expf(const float *x, float *y, long long n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148 * 8);
+    det_expf_kernel<<<blocks, 256, 0, st>>>(x, y, n);
     return cudaGetLastError();
 }
 

@@ -38,7 +38,7 @@ EXPORTED = [
     "s2k_seq_begin", "s2k_batch_frame", "s2k_seq_frames", "s2k_sched_create", "s2k_sched_free",
     "s2k_sched_submit", "s2k_sched_step", "s2k_sched_run", "s2k_sched_poll", "s2k_sched_result",
     "s2k_sched_get_stats", "s2k_sched_poll_status", "s2k_sched_cancel", "s2k_sched_set_frame_callback",
-    "s2k_seq_load_kv", "s2k_get_rows", "s2k_model_set_wait_limit", "s2k_debug_wait_probe", "s2k_debug_fail_alloc",
+    "s2k_seq_load_kv", "s2k_get_rows", "s2k_model_set_wait_limit", "s2k_debug_wait_probe", "s2k_debug_fail_alloc", "s2k_debug_det_expf",
     "s2k_model_device_bytes", "s2k_device_mem_info", "s2k_gguf_read_hparams", "s2k_gguf_tensor_info",
     "s2k_model_load_gguf", "s2k_build_prompt", "s2k_seq_last_metrics",
     "s2k_codec_create", "s2k_codec_upload_tensor", "s2k_codec_finalize", "s2k_codec_load_gguf", "s2k_codec_free",
@@ -194,6 +194,7 @@ def lib() -> ctypes.CDLL:
         "s2k_model_set_wait_limit": ([vp, ctypes.c_int64], i32),
         "s2k_debug_wait_probe": ([vp], i32),
         "s2k_debug_fail_alloc": ([vp, ctypes.c_int64], i32),
+        "s2k_debug_det_expf": ([i32, vp, vp, ctypes.c_int64], i32),
         "s2k_model_device_bytes": ([vp], ctypes.c_size_t),
         "s2k_device_mem_info": ([i32, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)], i32),
         "s2k_gguf_read_hparams": ([ctypes.c_char_p, ctypes.POINTER(_HParams)], i32),
@@ -708,6 +709,15 @@ class BatchScheduler:
         except Exception:
             pass
 
+
+
+def det_expf(x: np.ndarray, device: int = 0) -> np.ndarray:
+    """The device exp every softmax / SiLU / sampler kernel uses, over x
+    (float32), through s2k_debug_det_expf."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    _check(lib().s2k_debug_det_expf(device, x.ctypes.data, y.ctypes.data, x.size))
+    return y
 
 def launch_count(reset: bool = False) -> int:
     return int(lib().s2k_launch_count(1 if reset else 0))

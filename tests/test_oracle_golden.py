@@ -105,3 +105,30 @@ def test_philox_uniform_properties():
     assert oracle.philox_uniform(42, 3, 2, 0) == oracle.philox_uniform(42, 3, 2, 0)
     assert oracle.philox_uniform(42, 3, 2, 0) != oracle.philox_uniform(43, 3, 2, 0)
     assert oracle.philox_uniform(42, 3, 2, 0) != oracle.philox_uniform(42, 3, 2, 1)
+
+
+def _expf_inputs(seed: int = 3) -> np.ndarray:
+    """Every regime of the exp: random x over its whole finite range, a dense
+    sweep where results turn subnormal (k < -126) and where they overflow,
+    reductions that land on k = 0, and the special values."""
+    rng = np.random.default_rng(seed)
+    parts = [rng.uniform(-110.0, 95.0, 200_000), np.linspace(-104.5, -86.0, 100_001),
+             np.linspace(87.0, 89.0, 20_001), rng.uniform(-0.4, 0.4, 20_000),
+             np.array([0.0, -0.0, 1.0, -1.0, 88.72283935546875, 88.7228394, -103.972084045410156, -103.9721,
+                       np.inf, -np.inf, np.nan])]
+    return np.concatenate(parts).astype(np.float32)
+
+
+def test_det_expf_scaling_equals_ldexpf():
+    """The oracle's exp scales by 2^k with two IEEE products (so_pow2_scale),
+    as the CUDA det_expf does: it must equal the C library's ldexpf (exact,
+    or correctly rounded into the subnormals) for every reachable k."""
+    assert oracle.check_pow2_scale(4000) == 0
+    x = _expf_inputs()
+    y = oracle.det_expf(x)
+    fin = np.isfinite(x) & (x > -103.972084045410156) & (x < 88.72283935546875)
+    ref = np.exp(x[fin].astype(np.float64))
+    rel = np.abs(y[fin].astype(np.float64) - ref) / np.maximum(ref, np.finfo(np.float32).tiny)
+    normal = ref >= np.finfo(np.float32).tiny
+    assert rel[normal].max() < 4e-7  # ~2 ulp
+    assert np.isnan(y[np.isnan(x)]).all() and y[x == np.inf][0] == np.inf and y[x == -np.inf][0] == 0.0
