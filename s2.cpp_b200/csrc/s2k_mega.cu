@@ -1029,6 +1029,9 @@ cudaError_t launch_mega(const MegaOp *d_ops, int n_ops, int mt, MegaCtl *ctl, co
     cfg.numAttrs = 1;
     count_launch();
     const int ahead = mega_l2_ahead();
+    // S2K_MEGA_FLAGS (tuning and measurement; 0 = defaults): bits 8-15 the
+    // most tiles in flight per CTA (1..kMStages), bits 16-19 the producer
+    // lanes per group of tiles (1..kMaxPL)
     const char *fe = getenv("S2K_MEGA_FLAGS");
     const int flags = fe ? atoi(fe) : 0;
     if (q8) {
