@@ -498,15 +498,22 @@ __device__ void attn_unit(const MegaAttn &a, const AttnPlan &pl, const AttnUnit 
     const int ncp = slow ? max(0, min(cnt, nc - j0)) : 0;  // cached keys of the split
     const int npg = (ncp + kPage - 1) / kPage;
     // ---- A. the split's cache pages -> shared memory (bulk copies) ----
-    if (npg > 0 && tid == kMNC - 32) {  // warp 7 (this call's v of token 1: idle at T = 1) issues the copies
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&sm.abar, (uint32_t)(2 * npg * kPage * kHD * sizeof(__half)));
-        for (int p = 0; p < npg; ++p) {
-            const int pg = j0 / kPage + p;
+    // Warp 7 (this call's v of token 1: idle at T = 1) issues them, one page's
+    // keys or values per lane in the same instruction (one lane issuing them
+    // one after another serializes the issue, as in the weight producer).
+    static_assert(2 * (kAttnSplit / kPage) <= 32, "a lane per page copy");
+    if (npg > 0 && warp == kMW - 1) {
+        if (lane == 0) mbar_arrive_expect_tx(&sm.abar, (uint32_t)(2 * npg * kPage * kHD * sizeof(__half)));
+        __syncwarp();
+        if (lane < 2 * npg) {
+            const int p = lane >> 1, pg = j0 / kPage + p;
             const int page = pg < kPtab ? sm.ptab[pg] : __ldcg(a.block_table + pg);
             const size_t off = (((size_t)page * a.kv_layers + a.layer) * a.Hkv + g) * kPage * kHD;
-            bulk_g2s_plain(&as.k.h[p * kPage][0], a.kv_k + off, kPage * kHD * sizeof(__half), &sm.abar);
-            bulk_g2s_plain(&as.v.h[p * kPage][0], a.kv_v + off, kPage * kHD * sizeof(__half), &sm.abar);
+            fence_proxy_async_smem();
+            if (lane & 1)
+                bulk_g2s_plain(&as.v.h[p * kPage][0], a.kv_v + off, kPage * kHD * sizeof(__half), &sm.abar);
+            else
+                bulk_g2s_plain(&as.k.h[p * kPage][0], a.kv_k + off, kPage * kHD * sizeof(__half), &sm.abar);
         }
     }
     // ---- B. queries (warps 0..nh-1), this call's keys / values (warps 4..7) ----
