@@ -1001,9 +1001,10 @@ __global__ void __launch_bounds__(kMThreads, 1)
     }
 }
 
-// Tiles per CTA the producer prefetches into L2 beyond its ring: 148 CTAs x
-// 24 tiles x 17 KB = 62 MB of the 126 MB L2.  S2K_L2_AHEAD (read at each
-// launch or graph capture) overrides it; 0 turns the run-ahead off.
+// Tiles per CTA the producer prefetches into L2 beyond its ring (148 CTAs x
+// 24 tiles x 17 KB would be 62 MB of the 126 MB L2).  Off by default: a
+// run-ahead of 8-64 tiles measured no faster.  S2K_L2_AHEAD (read at each
+// launch or graph capture) sets it, up to 64.
 int mega_l2_ahead() {
     const char *e = getenv("S2K_L2_AHEAD");
     const int d = e ? atoi(e) : 0;
